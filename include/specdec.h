@@ -1,0 +1,156 @@
+/*
+ * specdec.h — C ABI of the B200 (sm_100a) speculative-decoding backend for
+ * islhkafaa/neural-network.
+ *
+ * The reference runs speculative decoding as one C++ method,
+ * TransformerDecoder::generate_speculative (src/nn/layer.cpp:1382-1661,
+ * declared include/nn/layer.hpp:318-323), on two TransformerDecoder objects
+ * (target and draft) whose weights live behind the ExecutionBackend interface
+ * (include/backend/backend.hpp:20-221).  Most of that path bypasses the
+ * backend (RoPE, KV append/truncate, attention, sampling are host loops), so
+ * this library replaces the whole method rather than individual backend
+ * virtuals.  The entry points below are what the reference-side glue binds;
+ * see INTEGRATION.md for the C++ call site.
+ *
+ * Conventions: plain pointers and sizes only; every function returns a
+ * specdec_status (0 = success).  On failure specdec_last_error(handle) holds
+ * a one-line message.  The reference reports the same conditions as
+ * std::runtime_error; the C++ glue rethrows them as such.  A handle is bound
+ * to one device and must be used from one host thread at a time (the
+ * reference is not thread-safe either: its AMPContext is thread-local and its
+ * ThreadPool a process singleton, src/optim/grad_scaler.cpp:4-5,
+ * src/backend/thread_pool.cpp:4-7).
+ */
+#ifndef SPECDEC_H
+#define SPECDEC_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum specdec_status {
+  SPECDEC_OK = 0,
+  SPECDEC_ERR_INVALID = 1,     /* bad argument or shape (reference: shape checks throw, src/core/tensor.cpp:393-402) */
+  SPECDEC_ERR_CUDA = 2,        /* a CUDA runtime call failed */
+  SPECDEC_ERR_OOM = 3,         /* device allocation failed */
+  SPECDEC_ERR_SEQ_LEN = 4,     /* a cache would exceed its capacity (reference: src/nn/layer.cpp:1176-1179) */
+  SPECDEC_ERR_UNSUPPORTED = 5, /* a mode this build does not implement */
+  SPECDEC_ERR_STATE = 6,       /* call order (e.g. generate before both models are loaded) */
+  SPECDEC_ERR_RNG = 7          /* the host uniform table has too few rounds */
+} specdec_status;
+
+enum { SPECDEC_ARCH_REF = 0,   /* the reference TransformerDecoder: post-LN, SwiGLU, RoPE (src/nn/layer.cpp:1097-1114) */
+       SPECDEC_ARCH_CFG = 1 }; /* pre-LN, GELU FFN, learned positions, final LN (no reference counterpart) */
+
+enum { SPECDEC_F32 = 0, SPECDEC_BF16 = 1, SPECDEC_INT8 = 2 };
+
+enum { SPECDEC_TARGET = 0, SPECDEC_DRAFT = 1 };
+
+enum { SPECDEC_RNG_MT19937 = 0,      /* the reference's std::mt19937(seed) stream, per request seed + b */
+       SPECDEC_RNG_HOST_UNIFORM = 1 }; /* caller table u[b][round][2k+1] */
+
+enum { SPECDEC_CATCHUP_REF = 0,      /* the reference's draft catch-up (src/nn/layer.cpp:1632-1655) */
+       SPECDEC_CATCHUP_CORRECT = 1 };/* consistent draft rollback */
+
+/* Constructor arguments of TransformerDecoder (include/nn/layer.hpp:301-303)
+ * plus the number of KV heads of MultiHeadAttention (layer.hpp:238-240). */
+typedef struct specdec_model_config {
+  int32_t vocab_size;
+  int32_t d_model;
+  int32_t n_heads;
+  int32_t n_kv_heads;  /* 0 -> n_heads */
+  int32_t d_ff;
+  int32_t n_layers;
+  int32_t max_seq_len; /* per-request KV capacity in positions */
+  int32_t arch;        /* SPECDEC_ARCH_* */
+} specdec_model_config;
+
+typedef struct specdec_config {
+  specdec_model_config target;
+  specdec_model_config draft;      /* when draft_shares_target, only draft.n_layers is read */
+  int32_t draft_shares_target;     /* 1: draft = target's first draft.n_layers layers + its lm_head, same device memory */
+  int32_t weight_dtype;            /* SPECDEC_F32 or SPECDEC_INT8 (QuantizedDense, src/nn/quantization.cpp:7-66) */
+  int32_t act_dtype;               /* SPECDEC_F32 or SPECDEC_BF16 */
+  int32_t kv_dtype;                /* SPECDEC_F32, SPECDEC_BF16 or SPECDEC_INT8 (quantize_kv, src/nn/layer.cpp:635-665) */
+  int32_t max_batch;               /* concurrent requests per generate call */
+  int32_t max_lookahead;           /* largest k */
+  int32_t max_prompt_len;          /* longest prompt */
+} specdec_config;
+
+/* The arguments of generate_speculative (include/nn/layer.hpp:318-323) plus
+ * the switches the batched B200 path adds. */
+typedef struct specdec_gen_params {
+  int32_t max_new_tokens;          /* as the reference: at least one token is always emitted */
+  int32_t lookahead;               /* k */
+  float temperature;               /* <= 0: greedy */
+  int32_t top_k;                   /* 0: off */
+  float top_p;                     /* >= 1: off */
+  int32_t rng_mode;                /* SPECDEC_RNG_* */
+  uint32_t seed;                   /* mt19937 mode: request b uses seed + b */
+  const float *uniforms;           /* host-uniform mode: [B][uniform_rounds][2k+1] in [0,1) */
+  int32_t uniform_rounds;
+  int32_t draft_catchup;           /* SPECDEC_CATCHUP_* */
+} specdec_gen_params;
+
+typedef struct specdec_handle specdec_handle;
+
+/* Replaces constructing the two TransformerDecoder objects on a backend
+ * (include/nn/layer.hpp:301-303). Allocates all device memory up front. */
+int specdec_create(const specdec_config *cfg, int device, specdec_handle **out);
+
+int specdec_destroy(specdec_handle *h);
+
+/* Last error message of this handle (or of the last failed create if h is NULL). */
+const char *specdec_last_error(const specdec_handle *h);
+
+/* Replaces injecting weights through TransformerDecoder::parameters() +
+ * Tensor::copy_from_host (include/nn/layer.hpp:306, tests/nn/gqa_test.cpp:56-62).
+ * params[i] is a host fp32 array of numels[i] elements, in parameters() order;
+ * Dense weights are [in, out] row-major (src/nn/layer.cpp:153).  With
+ * weight_dtype INT8 every Dense weight (attention, FFN, lm_head) is quantised
+ * on load exactly as QuantizedDense does.  role = SPECDEC_DRAFT is rejected
+ * when draft_shares_target. */
+int specdec_load_params(specdec_handle *h, int role, int n_params,
+                        const float *const *params, const int64_t *numels);
+
+/* Replaces TransformerDecoder::generate_speculative (src/nn/layer.cpp:1382-1661)
+ * for B independent requests with equal prompt length S.  prompts [B][S] and
+ * out_tokens [B][S + max(1, max_new_tokens)] are HOST buffers (the tokens are
+ * the reference's return value: prompt followed by the new tokens).
+ * out_stats (optional) [B][4] = rounds, drafted tokens, accepted drafts,
+ * rejections. */
+int specdec_generate(specdec_handle *h, const specdec_gen_params *p,
+                     const int32_t *prompts, int B, int S,
+                     int32_t *out_tokens, int64_t *out_stats);
+
+/* The same with DEVICE buffers (no host copies, nothing synchronised): the
+ * caller times it on specdec_stream(h).  out_stats is a device int64 [B][4]. */
+int specdec_generate_device(specdec_handle *h, const specdec_gen_params *p,
+                            const int32_t *d_prompts, int B, int S,
+                            int32_t *d_out_tokens, int64_t *d_out_stats);
+
+/* The CUDA stream (cudaStream_t) every kernel of this handle runs on. */
+void *specdec_stream(specdec_handle *h);
+
+/* TransformerDecoder::forward without a cache (src/nn/layer.cpp:1161-1193) of
+ * one model on one host token sequence; logits [S][vocab] fp32, host. */
+int specdec_forward_logits(specdec_handle *h, int role, const int32_t *tokens,
+                           int S, float *logits);
+
+/* Philox4x32-10 uniform table u[b][round][slot] for SPECDEC_RNG_HOST_UNIFORM:
+ * key (seed lo, seed hi), counter (slot/4, round, b, 0x53504543), lane slot%4,
+ * value (x >> 8) * 2^-24. */
+int specdec_philox_uniforms(uint64_t seed, int B, int rounds, int slots,
+                            float *out);
+
+/* Number of kernel launches the last generate call issued on the device. */
+int64_t specdec_last_launch_count(const specdec_handle *h);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPECDEC_H */

@@ -1,0 +1,1105 @@
+// Host engine and C ABI of the B200 speculative-decoding backend.
+//
+// One specdec_handle = one device, two decoder models (target, draft), their
+// KV caches, the per-request speculative state and the activation buffers,
+// all allocated once in specdec_create.  specdec_generate runs the
+// reference's TransformerDecoder::generate_speculative
+// (src/nn/layer.cpp:1382-1661) for B requests at once:
+//
+//   prefill target + draft  ->  first token  ->  WHILE(any request active) {
+//     draft step 0 (catch-up + last token), draft steps 1..k-1 (+ sample),
+//     verify (k+1 rows per request), accept/reject/rollback }
+//
+// The whole sequence is captured once per (B, S, sampling mode) into a CUDA
+// graph whose round loop is a device-driven conditional WHILE node, so one
+// generate call is one graph launch with no host round trips.  The same
+// kernels can be launched directly (SPECDEC_NO_GRAPH=1) for debugging.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <thread>
+#include <tuple>
+#include <vector>
+
+#include "../../include/specdec.h"
+#include "forward.cuh"
+#include "sample.cuh"
+
+using namespace specdec;
+
+namespace {
+
+thread_local std::string g_create_err;
+
+struct SpecErr {
+  int code;
+  std::string msg;
+};
+
+#define CK(x)                                                                                   \
+  do {                                                                                          \
+    cudaError_t e_ = (x);                                                                       \
+    if (e_ != cudaSuccess)                                                                      \
+      throw SpecErr{e_ == cudaErrorMemoryAllocation ? SPECDEC_ERR_OOM : SPECDEC_ERR_CUDA,       \
+                    std::string(#x) + ": " + cudaGetErrorString(e_)};                         \
+  } while (0)
+
+[[noreturn]] void fail(int code, const std::string &m) { throw SpecErr{code, m}; }
+
+struct Dims {
+  int V, d, H, Hkv, D, F, L, max_seq, arch, kvd;
+};
+
+struct LayerW {
+  void *wqkv = nullptr; float *sqkv = nullptr, *bqkv = nullptr;
+  void *wo = nullptr; float *so = nullptr, *bo = nullptr;
+  void *wgu = nullptr; float *sgu = nullptr, *bgu = nullptr;  // ref: gate/up interleaved; cfg: fc1
+  void *wd = nullptr; float *sd = nullptr, *bd = nullptr;     // ref: down; cfg: fc2
+  float *g1 = nullptr, *b1 = nullptr, *g2 = nullptr, *b2 = nullptr;
+};
+
+struct ModelW {
+  Dims dm{};
+  float *emb = nullptr, *pos = nullptr, *gf = nullptr, *bfin = nullptr;
+  void *whead = nullptr; float *shead = nullptr, *bhead = nullptr;
+  std::vector<LayerW> layers;
+  bool loaded = false;
+};
+
+struct GraphKey {
+  int B, S, k, greedy, rng_mode, catchup, max_new, u_rounds;
+  float T;
+  uint32_t seed;
+  bool operator<(const GraphKey &o) const {
+    return std::tie(B, S, k, greedy, rng_mode, catchup, max_new, u_rounds, T, seed) <
+           std::tie(o.B, o.S, o.k, o.greedy, o.rng_mode, o.catchup, o.max_new, o.u_rounds, o.T, o.seed);
+  }
+};
+
+struct GraphEntry {
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  int64_t fixed_kernels = 0;   // kernels outside the loop
+  int64_t body_kernels = 0;    // kernels per loop iteration
+};
+
+__global__ void mt_seed_kernel(uint32_t *mt, int *mt_idx, uint32_t seed, int B) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  // std::mersenne_twister_engine::seed: x0 = seed, xi = f * (x_{i-1} ^ (x_{i-1} >> 30)) + i
+  uint32_t *g = mt + static_cast<size_t>(b) * kMtN;
+  uint32_t x = seed + static_cast<uint32_t>(b);
+  g[0] = x;
+  for (int i = 1; i < kMtN; ++i) {
+    x = 1812433253u * (x ^ (x >> 30)) + static_cast<uint32_t>(i);
+    g[i] = x;
+  }
+  mt_idx[b] = kMtN;
+}
+
+// Last kernel of a round: decides whether the WHILE node runs again.
+__global__ void round_cond_kernel(cudaGraphConditionalHandle hnd, const int *active_count, int *iters,
+                                  int max_iters, int *err) {
+  const int it = *iters + 1;
+  *iters = it;
+  unsigned int more = (*active_count > 0) ? 1u : 0u;
+  if (more && it >= max_iters) {
+    atomicOr(err, kErrSeqLen);
+    more = 0u;
+  }
+  cudaGraphSetConditional(hnd, more);
+}
+
+__global__ void count_iter_kernel(int *iters) { *iters = *iters + 1; }
+
+// Before the WHILE node: enter the loop only if a request is still active.
+__global__ void prime_cond_kernel(cudaGraphConditionalHandle hnd, const int *active, int B) {
+  int any = 0;
+  for (int b = threadIdx.x; b < B; b += blockDim.x) any |= active[b];
+  any = __any_sync(0xffffffffu, any);
+  if (threadIdx.x == 0) cudaGraphSetConditional(hnd, any ? 1u : 0u);
+}
+
+}  // namespace
+
+struct specdec_handle {
+  specdec_config cfg{};
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  std::string err;
+  ModelW tgt, dft;
+  std::vector<void *> allocs;
+  std::vector<void *> weight_allocs[2];
+
+  // caches
+  void *tk = nullptr, *tv = nullptr, *dk = nullptr, *dv = nullptr;
+  size_t t_layer_stride = 0, d_layer_stride = 0, t_req_stride = 0, d_req_stride = 0;
+  int t_cap = 0, d_cap = 0;
+  float2 *rope = nullptr;
+  int rope_max = 0, rope_D = 0;
+
+  // activations
+  int R_max = 0, R_part = 0, max_split = 1;
+  size_t act_elt = 4;
+  void *x = nullptr, *x1 = nullptr, *hb = nullptr, *qb = nullptr, *att = nullptr, *ffa = nullptr;
+  float *logits = nullptr, *part = nullptr;
+  int *rtok = nullptr, *rpos = nullptr, *rreq = nullptr, *sel = nullptr;
+
+  // speculative state
+  SpecState st{};
+  int *d_prompts = nullptr, *d_out = nullptr;
+  long long *d_stats = nullptr;
+  float *d_uniforms = nullptr;
+  size_t uniforms_cap = 0;
+  int *d_iters = nullptr;
+  int *h_pinned = nullptr;
+
+  std::map<GraphKey, GraphEntry> graphs;
+  int64_t launches = 0;        // direct mode: kernels enqueued by the last call
+  int64_t graph_fixed = 0, graph_body = 0, extra_launches = 0;
+  bool use_graph = true;
+
+  void *dalloc(size_t bytes, std::vector<void *> *owner = nullptr) {
+    void *p = nullptr;
+    CK(cudaMalloc(&p, bytes ? bytes : 16));
+    (owner ? *owner : allocs).push_back(p);
+    return p;
+  }
+};
+
+namespace {
+
+bool act_bf16(const specdec_handle *h) { return h->cfg.act_dtype == SPECDEC_BF16; }
+bool w_int8(const specdec_handle *h) { return h->cfg.weight_dtype == SPECDEC_INT8; }
+
+Dims make_dims(const specdec_model_config &m) {
+  Dims d{};
+  d.V = m.vocab_size;
+  d.d = m.d_model;
+  d.H = m.n_heads;
+  d.Hkv = m.n_kv_heads ? m.n_kv_heads : m.n_heads;
+  d.D = m.n_heads ? m.d_model / m.n_heads : 0;
+  d.F = m.d_ff;
+  d.L = m.n_layers;
+  d.max_seq = m.max_seq_len;
+  d.arch = m.arch;
+  d.kvd = d.Hkv * d.D;
+  return d;
+}
+
+void check_dims(const Dims &d, const char *who) {
+  auto bad = [&](const char *m) { fail(SPECDEC_ERR_INVALID, std::string(who) + ": " + m); };
+  if (d.V < 1 || d.d < 2 || d.H < 1 || d.F < 1 || d.L < 0 || d.max_seq < 1) bad("non-positive dimension");
+  if (d.d % d.H) bad("embed_dim must be divisible by num_heads");
+  if (d.H % d.Hkv) bad("num_heads must be divisible by num_kv_heads");
+  if (d.D % 2) bad("rope: head dimension D must be even");
+  if (d.D > kAttnThreads) bad("head dimension above 128 is not supported");
+  if (d.d > 32 * 128) bad("d_model above 4096 is not supported");
+  if (d.arch != SPECDEC_ARCH_REF && d.arch != SPECDEC_ARCH_CFG) bad("unknown arch");
+}
+
+// --- weights ---------------------------------------------------------------
+// QuantizedDense (src/nn/quantization.cpp:40-66): per-output-column scale
+// max|W[:, c]| / 127 (0 -> 1), q = clamp(round(W / s), -127, 127).
+void quantize_columns(const float *w, int K, int N, std::vector<int8_t> &q, std::vector<float> &s) {
+  s.assign(N, 1.f);
+  q.assign(static_cast<size_t>(K) * N, 0);
+  for (int c = 0; c < N; ++c) {
+    float mx = 0.f;
+    for (int r = 0; r < K; ++r) mx = std::max(mx, std::abs(w[static_cast<size_t>(r) * N + c]));
+    const float sc = mx / 127.0f;
+    s[c] = (sc == 0.0f) ? 1.0f : sc;
+  }
+  for (int r = 0; r < K; ++r)
+    for (int c = 0; c < N; ++c) {
+      float v = std::round(w[static_cast<size_t>(r) * N + c] / s[c]);
+      v = std::max(-127.0f, std::min(127.0f, v));
+      q[static_cast<size_t>(r) * N + c] = static_cast<int8_t>(v);
+    }
+}
+
+// A set of reference Dense weights [K][N_i] (+ bias [N_i]) stacked into one
+// output-major device matrix [sum N_i][K]; `interleave` stacks two equally
+// wide matrices column by column (SwiGLU gate/up).
+struct DenseSrc {
+  const float *w;
+  const float *b;
+  int N;
+};
+
+void upload_stacked(specdec_handle *h, int role, const std::vector<DenseSrc> &src, int K, bool interleave,
+                    void **wout, float **sout, float **bout) {
+  int Ntot = 0;
+  for (auto &s : src) Ntot += s.N;
+  std::vector<float> bias(Ntot);
+  std::vector<float> scale(Ntot, 1.f);
+  const bool i8 = w_int8(h);
+  std::vector<float> wf;
+  std::vector<int8_t> wq;
+  if (i8) wq.assign(static_cast<size_t>(Ntot) * K, 0);
+  else wf.assign(static_cast<size_t>(Ntot) * K, 0.f);
+  int base = 0;
+  for (size_t m = 0; m < src.size(); ++m) {
+    const DenseSrc &s = src[m];
+    std::vector<int8_t> q;
+    std::vector<float> sc;
+    if (i8) quantize_columns(s.w, K, s.N, q, sc);
+    for (int c = 0; c < s.N; ++c) {
+      const int row = interleave ? (2 * c + static_cast<int>(m)) : (base + c);
+      bias[row] = s.b[c];
+      if (i8) scale[row] = sc[c];
+      for (int k = 0; k < K; ++k) {
+        const size_t si = static_cast<size_t>(k) * s.N + c;
+        if (i8) wq[static_cast<size_t>(row) * K + k] = q[si];
+        else wf[static_cast<size_t>(row) * K + k] = s.w[si];
+      }
+    }
+    base += s.N;
+  }
+  auto &own = h->weight_allocs[role];
+  const size_t wbytes = static_cast<size_t>(Ntot) * K * (i8 ? 1 : 4);
+  void *dw = h->dalloc(wbytes, &own);
+  CK(cudaMemcpy(dw, i8 ? static_cast<const void *>(wq.data()) : static_cast<const void *>(wf.data()), wbytes,
+                cudaMemcpyHostToDevice));
+  float *db = static_cast<float *>(h->dalloc(Ntot * sizeof(float), &own));
+  CK(cudaMemcpy(db, bias.data(), Ntot * sizeof(float), cudaMemcpyHostToDevice));
+  float *ds = nullptr;
+  if (i8) {
+    ds = static_cast<float *>(h->dalloc(Ntot * sizeof(float), &own));
+    CK(cudaMemcpy(ds, scale.data(), Ntot * sizeof(float), cudaMemcpyHostToDevice));
+  }
+  *wout = dw;
+  *sout = ds;
+  *bout = db;
+}
+
+float *upload_vec(specdec_handle *h, int role, const float *p, size_t n) {
+  float *d = static_cast<float *>(h->dalloc(n * sizeof(float), &h->weight_allocs[role]));
+  CK(cudaMemcpy(d, p, n * sizeof(float), cudaMemcpyHostToDevice));
+  return d;
+}
+
+void load_model(specdec_handle *h, int role, ModelW &m, int n, const float *const *P, const int64_t *numel) {
+  const Dims &dm = m.dm;
+  const int d = dm.d, F = dm.F, V = dm.V, kvd = dm.kvd;
+  const bool ref = dm.arch == SPECDEC_ARCH_REF;
+  const int per = ref ? 18 : 16;
+  const int lead = ref ? 1 : 2, tail = ref ? 2 : 4;
+  const int expect = lead + per * dm.L + tail;
+  if (n != expect) fail(SPECDEC_ERR_INVALID, "expected " + std::to_string(expect) + " parameters, got " + std::to_string(n));
+  // shape checks (element counts) in parameters() order
+  std::vector<int64_t> want;
+  want.push_back(static_cast<int64_t>(V) * d);
+  if (!ref) want.push_back(static_cast<int64_t>(dm.max_seq) * d);
+  for (int l = 0; l < dm.L; ++l) {
+    std::vector<int64_t> attn = {int64_t(d) * d, d, int64_t(d) * kvd, kvd, int64_t(d) * kvd, kvd, int64_t(d) * d, d};
+    if (ref) {
+      want.insert(want.end(), attn.begin(), attn.end());
+      for (int64_t x : {int64_t(d) * F, int64_t(F), int64_t(d) * F, int64_t(F), int64_t(F) * d, int64_t(d)}) want.push_back(x);
+      for (int i = 0; i < 4; ++i) want.push_back(d);
+    } else {
+      want.push_back(d); want.push_back(d);
+      want.insert(want.end(), attn.begin(), attn.end());
+      want.push_back(d); want.push_back(d);
+      for (int64_t x : {int64_t(d) * F, int64_t(F), int64_t(F) * d, int64_t(d)}) want.push_back(x);
+    }
+  }
+  if (!ref) { want.push_back(d); want.push_back(d); }
+  want.push_back(static_cast<int64_t>(d) * V);
+  want.push_back(V);
+  for (int i = 0; i < n; ++i) {
+    if (!P[i]) fail(SPECDEC_ERR_INVALID, "parameter " + std::to_string(i) + " is null");
+    if (numel[i] != want[i])
+      fail(SPECDEC_ERR_INVALID, "parameter " + std::to_string(i) + " has " + std::to_string(numel[i]) +
+                                    " elements, expected " + std::to_string(want[i]));
+  }
+  for (void *p : h->weight_allocs[role]) cudaFree(p);
+  h->weight_allocs[role].clear();
+
+  int i = 0;
+  m.emb = upload_vec(h, role, P[i++], static_cast<size_t>(V) * d);
+  if (!ref) m.pos = upload_vec(h, role, P[i++], static_cast<size_t>(dm.max_seq) * d);
+  m.layers.assign(dm.L, LayerW{});
+  for (int l = 0; l < dm.L; ++l) {
+    LayerW &L = m.layers[l];
+    if (!ref) { L.g1 = upload_vec(h, role, P[i], d); L.b1 = upload_vec(h, role, P[i + 1], d); i += 2; }
+    const float *qw = P[i], *qb = P[i + 1], *kw = P[i + 2], *kb = P[i + 3], *vw = P[i + 4], *vb = P[i + 5];
+    const float *ow = P[i + 6], *ob = P[i + 7];
+    i += 8;
+    upload_stacked(h, role, {{qw, qb, d}, {kw, kb, kvd}, {vw, vb, kvd}}, d, false, &L.wqkv, &L.sqkv, &L.bqkv);
+    upload_stacked(h, role, {{ow, ob, d}}, d, false, &L.wo, &L.so, &L.bo);
+    if (ref) {
+      const float *gw = P[i], *gb = P[i + 1], *uw = P[i + 2], *ub = P[i + 3], *dw = P[i + 4], *db = P[i + 5];
+      i += 6;
+      upload_stacked(h, role, {{gw, gb, F}, {uw, ub, F}}, d, true, &L.wgu, &L.sgu, &L.bgu);
+      upload_stacked(h, role, {{dw, db, d}}, F, false, &L.wd, &L.sd, &L.bd);
+      L.g1 = upload_vec(h, role, P[i], d); L.b1 = upload_vec(h, role, P[i + 1], d);
+      L.g2 = upload_vec(h, role, P[i + 2], d); L.b2 = upload_vec(h, role, P[i + 3], d);
+      i += 4;
+    } else {
+      L.g2 = upload_vec(h, role, P[i], d); L.b2 = upload_vec(h, role, P[i + 1], d);
+      i += 2;
+      const float *f1w = P[i], *f1b = P[i + 1], *f2w = P[i + 2], *f2b = P[i + 3];
+      i += 4;
+      upload_stacked(h, role, {{f1w, f1b, F}}, d, false, &L.wgu, &L.sgu, &L.bgu);
+      upload_stacked(h, role, {{f2w, f2b, d}}, F, false, &L.wd, &L.sd, &L.bd);
+    }
+  }
+  if (!ref) { m.gf = upload_vec(h, role, P[i], d); m.bfin = upload_vec(h, role, P[i + 1], d); i += 2; }
+  upload_stacked(h, role, {{P[i], P[i + 1], V}}, d, false, &m.whead, &m.shead, &m.bhead);
+  m.loaded = true;
+}
+
+// --- kernel launch helpers ---------------------------------------------------
+template <int EPI>
+void launch_linear(specdec_handle *h, const LinearArgs &a) {
+  if (a.R <= 0) return;
+  dim3 grid((a.N + 2 * kLinWarps - 1) / (2 * kLinWarps), (a.R + kRowTile - 1) / kRowTile);
+  dim3 block(32 * kLinWarps);
+  const bool bf = act_bf16(h), i8 = w_int8(h);
+  if (i8 && bf) linear_kernel<int8_t, __nv_bfloat16, EPI><<<grid, block, 0, h->stream>>>(a);
+  else if (i8) linear_kernel<int8_t, float, EPI><<<grid, block, 0, h->stream>>>(a);
+  else if (bf) linear_kernel<float, __nv_bfloat16, EPI><<<grid, block, 0, h->stream>>>(a);
+  else linear_kernel<float, float, EPI><<<grid, block, 0, h->stream>>>(a);
+  ++h->launches;
+}
+
+// Logits always fp32: the head writes through a float view regardless of the
+// activation type (kEpiStore with AT = fp32 output needs its own instantiation).
+template <typename WT, typename AT>
+__global__ void head_kernel(LinearArgs a);
+
+void layernorm(specdec_handle *h, const void *in, int R, int d, const float *g, const float *b, void *out) {
+  if (R <= 0) return;
+  if (act_bf16(h))
+    layernorm_kernel<__nv_bfloat16><<<R, 128, 0, h->stream>>>(static_cast<const __nv_bfloat16 *>(in), d, R, d, g, b,
+                                                              static_cast<__nv_bfloat16 *>(out), d);
+  else
+    layernorm_kernel<float><<<R, 128, 0, h->stream>>>(static_cast<const float *>(in), d, R, d, g, b,
+                                                      static_cast<float *>(out), d);
+  ++h->launches;
+}
+
+void attention(specdec_handle *h, const Dims &dm, int R, const void *kc, const void *vc, size_t req_stride, int S_cap) {
+  if (R <= 0) return;
+  RowsView rows{h->rtok, h->rpos, h->rreq};
+  int nsplit = 1;
+  if (R <= h->R_part) nsplit = std::max(1, std::min(h->max_split, (S_cap + 255) / 256));
+  const int chunk = (S_cap + nsplit - 1) / nsplit;
+  dim3 grid(R, dm.H, nsplit);
+  const size_t smem = (dm.D + 2 * kAttnThreads) * sizeof(float);
+  const bool bf = act_bf16(h);
+  const bool kvbf = h->cfg.kv_dtype == SPECDEC_BF16;
+#define ATTN(AT, KT)                                                                                          \
+  attention_kernel<AT, KT><<<grid, kAttnThreads, smem, h->stream>>>(                                        \
+      static_cast<const AT *>(h->qb), dm.d, rows, R, static_cast<const KT *>(kc), static_cast<const KT *>(vc), \
+      req_stride, S_cap, dm.H, dm.Hkv, dm.D, chunk, static_cast<AT *>(h->att), dm.d, h->part)
+  if (bf && kvbf) ATTN(__nv_bfloat16, __nv_bfloat16);
+  else if (bf) ATTN(__nv_bfloat16, float);
+  else if (kvbf) ATTN(float, __nv_bfloat16);
+  else ATTN(float, float);
+#undef ATTN
+  ++h->launches;
+  if (nsplit > 1) {
+    dim3 g2(R, dm.H);
+    if (bf) attn_combine_kernel<__nv_bfloat16><<<g2, 128, 0, h->stream>>>(h->part, rows, R, dm.H, dm.D, nsplit,
+                                                                          static_cast<__nv_bfloat16 *>(h->att), dm.d);
+    else attn_combine_kernel<float><<<g2, 128, 0, h->stream>>>(h->part, rows, R, dm.H, dm.D, nsplit,
+                                                               static_cast<float *>(h->att), dm.d);
+    ++h->launches;
+  }
+}
+
+// One forward pass of model m over the current row batch (R rows).  When
+// `logits` is set, the lm_head runs over the rows listed in `sel` (n_sel of
+// them, or all R rows when sel is null).
+void forward_rows(specdec_handle *h, bool target, int R, const int *sel, int n_sel, float *logits) {
+  ModelW &m = target ? h->tgt : h->dft;
+  const Dims &dm = m.dm;
+  const int d = dm.d;
+  RowsView rows{h->rtok, h->rpos, h->rreq};
+  void *kc = target ? h->tk : h->dk;
+  void *vc = target ? h->tv : h->dv;
+  const size_t lstride = target ? h->t_layer_stride : h->d_layer_stride;
+  const size_t rstride = target ? h->t_req_stride : h->d_req_stride;
+  const int S_cap = target ? h->t_cap : h->d_cap;
+  const size_t kv_elt = h->cfg.kv_dtype == SPECDEC_BF16 ? 2 : 4;
+
+  if (act_bf16(h))
+    embed_kernel<__nv_bfloat16><<<R, 128, 0, h->stream>>>(rows, R, m.emb, m.pos, dm.V, d, dm.max_seq,
+                                                          static_cast<__nv_bfloat16 *>(h->x));
+  else
+    embed_kernel<float><<<R, 128, 0, h->stream>>>(rows, R, m.emb, m.pos, dm.V, d, dm.max_seq, static_cast<float *>(h->x));
+  ++h->launches;
+
+  const bool ref = dm.arch == SPECDEC_ARCH_REF;
+  for (int l = 0; l < dm.L; ++l) {
+    const LayerW &L = m.layers[l];
+    void *kcl = static_cast<char *>(kc) + l * lstride * kv_elt;
+    void *vcl = static_cast<char *>(vc) + l * lstride * kv_elt;
+    const void *ain = h->x;
+    if (!ref) {
+      layernorm(h, h->x, R, d, L.g1, L.b1, h->x1);
+      ain = h->x1;
+    }
+    // QKV + RoPE + KV append
+    LinearArgs a{};
+    a.x = ain; a.ldx = d; a.R = R; a.W = L.wqkv; a.scale = L.sqkv; a.bias = L.bqkv;
+    a.N = d + 2 * dm.kvd; a.K = d; a.out = h->qb; a.ldo = d; a.rows = rows;
+    a.qkv = QKVArgs{d, dm.kvd, dm.D, h->rope, h->rope_max, kcl, vcl, rstride, S_cap,
+                    h->cfg.kv_dtype == SPECDEC_BF16 ? 1 : 0, h->st.err};
+    launch_linear<kEpiQKV>(h, a);
+    attention(h, dm, R, kcl, vcl, rstride, S_cap);
+    // out projection + residual
+    LinearArgs o{};
+    o.x = h->att; o.ldx = d; o.R = R; o.W = L.wo; o.scale = L.so; o.bias = L.bo; o.N = d; o.K = d;
+    o.out = h->hb; o.ldo = d; o.resid = h->x; o.ldr = d;
+    launch_linear<kEpiResid>(h, o);
+    if (ref) {
+      // x1 = norm1(x + attn); x = norm2(x1 + ffn(x1))  (src/nn/layer.cpp:1097-1114)
+      layernorm(h, h->hb, R, d, L.g1, L.b1, h->x1);
+      LinearArgs g{};
+      g.x = h->x1; g.ldx = d; g.R = R; g.W = L.wgu; g.scale = L.sgu; g.bias = L.bgu; g.N = 2 * dm.F; g.K = d;
+      g.out = h->ffa; g.ldo = dm.F;
+      launch_linear<kEpiSwiGLU>(h, g);
+      LinearArgs dn{};
+      dn.x = h->ffa; dn.ldx = dm.F; dn.R = R; dn.W = L.wd; dn.scale = L.sd; dn.bias = L.bd; dn.N = d; dn.K = dm.F;
+      dn.out = h->hb; dn.ldo = d; dn.resid = h->x1; dn.ldr = d;
+      launch_linear<kEpiResid>(h, dn);
+      layernorm(h, h->hb, R, d, L.g2, L.b2, h->x);
+    } else {
+      // pre-LN: x = x + attn; x = x + fc2(gelu(fc1(LN2(x))))
+      std::swap(h->x, h->hb);
+      layernorm(h, h->x, R, d, L.g2, L.b2, h->x1);
+      LinearArgs f1{};
+      f1.x = h->x1; f1.ldx = d; f1.R = R; f1.W = L.wgu; f1.scale = L.sgu; f1.bias = L.bgu; f1.N = dm.F; f1.K = d;
+      f1.out = h->ffa; f1.ldo = dm.F;
+      launch_linear<kEpiGelu>(h, f1);
+      LinearArgs f2{};
+      f2.x = h->ffa; f2.ldx = dm.F; f2.R = R; f2.W = L.wd; f2.scale = L.sd; f2.bias = L.bd; f2.N = d; f2.K = dm.F;
+      f2.out = h->hb; f2.ldo = d; f2.resid = h->x; f2.ldr = d;
+      launch_linear<kEpiResid>(h, f2);
+      std::swap(h->x, h->hb);
+    }
+  }
+  if (!logits) return;
+  const void *hin = h->x;
+  if (!ref) {
+    layernorm(h, h->x, R, d, m.gf, m.bfin, h->x1);
+    hin = h->x1;
+  }
+  LinearArgs hd{};
+  hd.x = hin; hd.ldx = d; hd.in_rows = sel; hd.R = sel ? n_sel : R; hd.W = m.whead; hd.scale = m.shead; hd.bias = m.bhead;
+  hd.N = dm.V; hd.K = d; hd.out = logits; hd.ldo = dm.V;
+  {
+    dim3 grid((hd.N + 2 * kLinWarps - 1) / (2 * kLinWarps), (hd.R + kRowTile - 1) / kRowTile);
+    dim3 block(32 * kLinWarps);
+    const bool bf = act_bf16(h), i8 = w_int8(h);
+    if (i8 && bf) head_kernel<int8_t, __nv_bfloat16><<<grid, block, 0, h->stream>>>(hd);
+    else if (i8) head_kernel<int8_t, float><<<grid, block, 0, h->stream>>>(hd);
+    else if (bf) head_kernel<float, __nv_bfloat16><<<grid, block, 0, h->stream>>>(hd);
+    else head_kernel<float, float><<<grid, block, 0, h->stream>>>(hd);
+    ++h->launches;
+  }
+}
+
+}  // namespace
+
+// The lm_head reads activations of type AT but always writes fp32 logits.
+namespace {
+template <typename WT, typename AT>
+__global__ void __launch_bounds__(32 * kLinWarps) head_kernel(LinearArgs a) {
+  constexpr int E = WVec<WT>::E;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int n0 = (blockIdx.x * kLinWarps + warp) * 2;
+  const int r0 = blockIdx.y * kRowTile;
+  if (n0 >= a.N) return;
+  const bool has1 = (n0 + 1) < a.N;
+  const int nrows = min(kRowTile, a.R - r0);
+  const WT *w0 = static_cast<const WT *>(a.W) + static_cast<size_t>(n0) * a.K;
+  const WT *w1 = has1 ? w0 + a.K : w0;
+  const AT *xrow[kRowTile];
+#pragma unroll
+  for (int i = 0; i < kRowTile; ++i) {
+    int lr = r0 + (i < nrows ? i : 0);
+    int pr = a.in_rows ? a.in_rows[lr] : lr;
+    xrow[i] = static_cast<const AT *>(a.x) + static_cast<size_t>(pr) * a.ldx;
+  }
+  float acc0[kRowTile], acc1[kRowTile];
+#pragma unroll
+  for (int i = 0; i < kRowTile; ++i) acc0[i] = acc1[i] = 0.f;
+  const bool vec_ok = ((a.K * static_cast<int>(sizeof(WT))) % 16 == 0) && ((a.ldx * static_cast<int>(sizeof(AT))) % 16 == 0);
+  const int kvec = vec_ok ? a.K / E : 0;
+  for (int v = lane; v < kvec; v += 32) {
+    float wa[E], wb[E];
+    if constexpr (sizeof(WT) == 4) {
+      unpack_w(__ldg(reinterpret_cast<const float4 *>(w0) + v), wa);
+      unpack_w(__ldg(reinterpret_cast<const float4 *>(w1) + v), wb);
+    } else {
+      unpack_w(__ldg(reinterpret_cast<const int4 *>(w0) + v), wa);
+      unpack_w(__ldg(reinterpret_cast<const int4 *>(w1) + v), wb);
+    }
+#pragma unroll
+    for (int i = 0; i < kRowTile; ++i) {
+      if (i < nrows) {
+        float xv[E];
+        load_x<AT, E>(xrow[i] + v * E, xv);
+        float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          s0 = fmaf(xv[e], wa[e], s0);
+          s1 = fmaf(xv[e], wb[e], s1);
+        }
+        acc0[i] += s0;
+        acc1[i] += s1;
+      }
+    }
+  }
+  for (int k = kvec * E + lane; k < a.K; k += 32) {
+    const float wa = static_cast<float>(w0[k]), wb = static_cast<float>(w1[k]);
+#pragma unroll
+    for (int i = 0; i < kRowTile; ++i)
+      if (i < nrows) {
+        const float xv = to_f32(xrow[i][k]);
+        acc0[i] = fmaf(xv, wa, acc0[i]);
+        acc1[i] = fmaf(xv, wb, acc1[i]);
+      }
+  }
+#pragma unroll
+  for (int i = 0; i < kRowTile; ++i) {
+    acc0[i] = warp_sum(acc0[i]);
+    acc1[i] = warp_sum(acc1[i]);
+  }
+#pragma unroll
+  for (int i = 0; i < kRowTile; ++i) {
+    if (lane == i && i < nrows) {
+      float v0 = acc0[i], v1 = acc1[i];
+      if (a.scale) { v0 *= a.scale[n0]; if (has1) v1 *= a.scale[n0 + 1]; }
+      float *o = static_cast<float *>(a.out) + static_cast<size_t>(r0 + i) * a.ldo;
+      o[n0] = v0 + a.bias[n0];
+      if (has1) o[n0 + 1] = v1 + a.bias[n0 + 1];
+    }
+  }
+}
+}  // namespace
+
+namespace {
+
+void sync_check(specdec_handle *h) { CK(cudaStreamSynchronize(h->stream)); }
+
+void validate_gen(specdec_handle *h, const specdec_gen_params *p, int B, int S) {
+  if (!p) fail(SPECDEC_ERR_INVALID, "null params");
+  if (!h->tgt.loaded || !h->dft.loaded) fail(SPECDEC_ERR_STATE, "target and draft weights must be loaded first");
+  if (B < 1 || B > h->cfg.max_batch) fail(SPECDEC_ERR_INVALID, "batch out of range");
+  if (S < 1 || S > h->cfg.max_prompt_len) fail(SPECDEC_ERR_INVALID, "prompt length out of range");
+  if (p->lookahead < 1 || p->lookahead > h->cfg.max_lookahead) fail(SPECDEC_ERR_INVALID, "lookahead out of range");
+  if (p->max_new_tokens < 0) fail(SPECDEC_ERR_INVALID, "max_new_tokens < 0");
+  // The target cache ends at S + max_new positions (every round verifies
+  // M = min(k, remaining) drafts); the reference throws when that exceeds
+  // max_seq_len (src/nn/layer.cpp:1176-1179).
+  if (S + (p->max_new_tokens > 1 ? p->max_new_tokens : 0) > h->t_cap)
+    fail(SPECDEC_ERR_SEQ_LEN, "Sequence length S plus past cached length exceeds max_seq_len");
+  const int V = h->tgt.dm.V;
+  if ((p->top_k > 0 && p->top_k < V) || (p->top_p > 0.f && p->top_p < 1.f))
+    fail(SPECDEC_ERR_UNSUPPORTED, "top-k / top-p filtering is not implemented on the device path");
+  if (p->rng_mode == SPECDEC_RNG_HOST_UNIFORM && p->temperature > 0.f) {
+    if (!p->uniforms || p->uniform_rounds < 1) fail(SPECDEC_ERR_INVALID, "host-uniform mode needs a uniform table");
+  } else if (p->rng_mode != SPECDEC_RNG_MT19937 && p->rng_mode != SPECDEC_RNG_HOST_UNIFORM) {
+    fail(SPECDEC_ERR_INVALID, "unknown rng_mode");
+  }
+  if (p->draft_catchup != SPECDEC_CATCHUP_REF && p->draft_catchup != SPECDEC_CATCHUP_CORRECT)
+    fail(SPECDEC_ERR_INVALID, "unknown draft_catchup");
+}
+
+// Enqueues one full round (everything between two accept kernels).
+void enqueue_round(specdec_handle *h) {
+  SpecState &st = h->st;
+  const int B = st.B, k = st.k;
+  const int tpb = 256;
+  const int nb = (B + tpb - 1) / tpb;
+  // draft step 0: [catch-up, last] per request
+  plan_draft0_kernel<<<nb, tpb, 0, h->stream>>>(st, h->rtok, h->rpos, h->rreq, h->sel);
+  ++h->launches;
+  forward_rows(h, false, 2 * B, h->sel, B, h->logits);
+  draft_sample_kernel<<<B, kSampThreads, 0, h->stream>>>(st, 0, h->logits);
+  ++h->launches;
+  for (int j = 1; j < k; ++j) {
+    plan_draft_kernel<<<nb, tpb, 0, h->stream>>>(st, j, h->rtok, h->rpos, h->rreq, h->sel);
+    ++h->launches;
+    forward_rows(h, false, B, nullptr, B, h->logits);
+    draft_sample_kernel<<<B, kSampThreads, 0, h->stream>>>(st, j, h->logits);
+    ++h->launches;
+  }
+  plan_verify_kernel<<<nb, tpb, 0, h->stream>>>(st, h->rtok, h->rpos, h->rreq);
+  ++h->launches;
+  forward_rows(h, true, B * (k + 1), nullptr, B * (k + 1), h->logits);
+  accept_kernel<<<B, kSampThreads, 0, h->stream>>>(st, h->logits);
+  ++h->launches;
+}
+
+void setup_state(specdec_handle *h, const specdec_gen_params *p, int B, int S, int *d_out_tokens) {
+  SpecState &st = h->st;
+  st.B = B;
+  st.k = p->lookahead;
+  st.kmax = h->cfg.max_lookahead;
+  st.V = h->tgt.dm.V;
+  st.max_new = p->max_new_tokens;
+  st.prompt_len = S;
+  st.out_len = S + std::max(1, p->max_new_tokens);
+  st.T = p->temperature;
+  st.greedy = p->temperature <= 0.f ? 1 : 0;
+  st.rng_mode = p->rng_mode;
+  st.catchup = p->draft_catchup;
+  st.t_cap = h->t_cap;
+  st.d_cap = h->d_cap;
+  st.u_slots = 2 * p->lookahead + 1;
+  st.u_rounds = p->uniform_rounds;
+  st.uniforms = h->d_uniforms;
+  (void)d_out_tokens;
+}
+
+}  // namespace
+
+// Everything up to and including the first token (src/nn/layer.cpp:1396-1512).
+static void enqueue_prologue(specdec_handle *h, int B, int S, uint32_t seed) {
+  SpecState &st = h->st;
+  init_state_kernel<<<B, 128, 0, h->stream>>>(st, h->d_prompts, S);
+  ++h->launches;
+  if (!st.greedy && st.rng_mode == 0) {
+    mt_seed_kernel<<<(B + 127) / 128, 128, 0, h->stream>>>(st.mt, st.mt_idx, seed, B);
+    ++h->launches;
+  }
+  const int chunk = std::max(1, std::min(S, h->R_max / B));
+  for (int pass = 0; pass < 2; ++pass) {
+    const bool target = pass == 0;
+    for (int c0 = 0; c0 < S; c0 += chunk) {
+      const int clen = std::min(chunk, S - c0);
+      const int R = B * clen;
+      plan_prefill_kernel<<<(R + 255) / 256, 256, 0, h->stream>>>(h->d_prompts, B, S, c0, clen, h->rtok, h->rpos,
+                                                                 h->rreq, h->sel);
+      ++h->launches;
+      const bool last = c0 + clen >= S;
+      // the draft's prefill logits are discarded (src/nn/layer.cpp:1408)
+      forward_rows(h, target, R, h->sel, B, (target && last) ? h->logits : nullptr);
+    }
+  }
+  first_token_kernel<<<B, kSampThreads, 0, h->stream>>>(st, h->logits);
+  ++h->launches;
+}
+
+static void destroy_graphs(specdec_handle *h) {
+  for (auto &kv : h->graphs) {
+    if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    if (kv.second.graph) cudaGraphDestroy(kv.second.graph);
+  }
+  h->graphs.clear();
+}
+
+// Builds prologue -> WHILE(active) { round } as one executable graph.
+static GraphEntry build_graph(specdec_handle *h, int B, int S, uint32_t seed, int max_iters) {
+  GraphEntry ge;
+  CK(cudaGraphCreate(&ge.graph, 0));
+  cudaGraphConditionalHandle hnd;
+  CK(cudaGraphConditionalHandleCreate(&hnd, ge.graph, 0, cudaGraphCondAssignDefault));
+  CK(cudaStreamBeginCaptureToGraph(h->stream, ge.graph, nullptr, nullptr, 0, cudaStreamCaptureModeThreadLocal));
+  h->launches = 0;
+  enqueue_prologue(h, B, S, seed);
+  prime_cond_kernel<<<1, 32, 0, h->stream>>>(hnd, h->st.active, B);
+  ++h->launches;
+  ge.fixed_kernels = h->launches;
+  CK(cudaStreamEndCapture(h->stream, &ge.graph));
+  size_t nn = 0;
+  CK(cudaGraphGetNodes(ge.graph, nullptr, &nn));
+  std::vector<cudaGraphNode_t> nodes(nn);
+  CK(cudaGraphGetNodes(ge.graph, nodes.data(), &nn));
+  std::vector<cudaGraphNode_t> sinks;
+  for (auto n : nodes) {
+    size_t nd = 0;
+    CK(cudaGraphNodeGetDependentNodes(n, nullptr, &nd));
+    if (nd == 0) sinks.push_back(n);
+  }
+  cudaGraphNodeParams cp{};
+  cp.type = cudaGraphNodeTypeConditional;
+  cp.conditional.handle = hnd;
+  cp.conditional.type = cudaGraphCondTypeWhile;
+  cp.conditional.size = 1;
+  cudaGraphNode_t wnode;
+  CK(cudaGraphAddNode(&wnode, ge.graph, sinks.data(), sinks.size(), &cp));
+  cudaGraph_t body = cp.conditional.phGraph_out[0];
+  CK(cudaStreamBeginCaptureToGraph(h->stream, body, nullptr, nullptr, 0, cudaStreamCaptureModeThreadLocal));
+  h->launches = 0;
+  enqueue_round(h);
+  round_cond_kernel<<<1, 1, 0, h->stream>>>(hnd, h->st.active_count, h->d_iters, max_iters, h->st.err);
+  ++h->launches;
+  ge.body_kernels = h->launches;
+  CK(cudaStreamEndCapture(h->stream, &body));
+  CK(cudaGraphInstantiate(&ge.exec, ge.graph, 0));
+  return ge;
+}
+
+// d_prompts may be any device buffer; it is staged into the handle's prompt
+// buffer so captured graphs stay valid across calls.
+static int generate_impl(specdec_handle *h, const specdec_gen_params *p, const int32_t *d_prompts, int B, int S,
+                         int32_t *d_out, int64_t *d_stats_out, bool uniforms_on_host) {
+  validate_gen(h, p, B, S);
+  SpecState &st = h->st;
+  setup_state(h, p, B, S, d_out);
+  if (d_prompts != h->d_prompts)
+    CK(cudaMemcpyAsync(h->d_prompts, d_prompts, static_cast<size_t>(B) * S * sizeof(int), cudaMemcpyDeviceToDevice,
+                       h->stream));
+  const bool table = p->rng_mode == SPECDEC_RNG_HOST_UNIFORM && p->temperature > 0.f;
+  if (table) {
+    const size_t n = static_cast<size_t>(B) * p->uniform_rounds * (2 * p->lookahead + 1);
+    if (n > h->uniforms_cap) {
+      destroy_graphs(h);
+      if (h->d_uniforms) cudaFree(h->d_uniforms);
+      h->d_uniforms = nullptr;
+      h->uniforms_cap = 0;
+      CK(cudaMalloc(&h->d_uniforms, n * sizeof(float)));
+      h->uniforms_cap = n;
+    }
+    st.uniforms = h->d_uniforms;
+    CK(cudaMemcpyAsync(h->d_uniforms, p->uniforms, n * sizeof(float),
+                       cudaMemcpyDefault, h->stream));
+  }
+  CK(cudaMemsetAsync(st.err, 0, sizeof(int), h->stream));
+  CK(cudaMemsetAsync(h->d_iters, 0, sizeof(int), h->stream));
+  // every active request emits at least one token per round
+  const int max_iters = std::max(2, p->max_new_tokens + 2);
+
+  if (h->use_graph) {
+    GraphKey key{B, S, p->lookahead, st.greedy, table ? 1 : 0, p->draft_catchup, p->max_new_tokens,
+                 table ? p->uniform_rounds : 0, p->temperature, (!st.greedy && !table) ? p->seed : 0u};
+    auto it = h->graphs.find(key);
+    if (it == h->graphs.end()) it = h->graphs.emplace(key, build_graph(h, B, S, p->seed, max_iters)).first;
+    CK(cudaGraphLaunch(it->second.exec, h->stream));
+    h->graph_fixed = it->second.fixed_kernels;
+    h->graph_body = it->second.body_kernels;
+    h->launches = -1;  // resolved from the iteration count when read
+  } else {
+    h->launches = 0;
+    enqueue_prologue(h, B, S, p->seed);
+    std::vector<int> act(B);
+    for (int it = 0; it < max_iters; ++it) {
+      CK(cudaMemcpyAsync(act.data(), st.active, B * sizeof(int), cudaMemcpyDeviceToHost, h->stream));
+      sync_check(h);
+      int n_act = 0;
+      for (int v : act) n_act += v;
+      if (n_act == 0) break;
+      enqueue_round(h);
+      count_iter_kernel<<<1, 1, 0, h->stream>>>(h->d_iters);
+      ++h->launches;
+    }
+  }
+  finalize_kernel<<<B, 128, 0, h->stream>>>(st, d_out, reinterpret_cast<long long *>(d_stats_out));
+  h->extra_launches = 1;
+  if (h->launches >= 0) h->launches += 1;
+  return SPECDEC_OK;
+}
+
+// ---------------------------------------------------------------------------
+extern "C" {
+
+const char *specdec_last_error(const specdec_handle *h) { return h ? h->err.c_str() : g_create_err.c_str(); }
+
+int specdec_create(const specdec_config *cfg, int device, specdec_handle **out) {
+  if (!out) return SPECDEC_ERR_INVALID;
+  *out = nullptr;
+  auto h = std::make_unique<specdec_handle>();
+  try {
+    if (!cfg) fail(SPECDEC_ERR_INVALID, "null config");
+    h->cfg = *cfg;
+    h->device = device;
+    CK(cudaSetDevice(device));
+    Dims td = make_dims(cfg->target);
+    check_dims(td, "target");
+    specdec_model_config dcfg = cfg->draft;
+    if (cfg->draft_shares_target) {
+      const int nl = cfg->draft.n_layers;
+      dcfg = cfg->target;
+      dcfg.n_layers = nl;
+      if (nl < 0 || nl > cfg->target.n_layers) fail(SPECDEC_ERR_INVALID, "draft layers exceed target layers");
+    }
+    Dims dd = make_dims(dcfg);
+    check_dims(dd, "draft");
+    if (dd.V != td.V) fail(SPECDEC_ERR_INVALID, "target and draft vocab differ");
+    if (dd.arch != td.arch) fail(SPECDEC_ERR_INVALID, "target and draft arch differ");
+    if (cfg->weight_dtype != SPECDEC_F32 && cfg->weight_dtype != SPECDEC_INT8)
+      fail(SPECDEC_ERR_INVALID, "weight_dtype must be F32 or INT8");
+    if (cfg->act_dtype != SPECDEC_F32 && cfg->act_dtype != SPECDEC_BF16) fail(SPECDEC_ERR_INVALID, "bad act_dtype");
+    if (cfg->kv_dtype == SPECDEC_INT8) fail(SPECDEC_ERR_UNSUPPORTED, "int8 KV cache is not implemented on the device path");
+    if (cfg->kv_dtype != SPECDEC_F32 && cfg->kv_dtype != SPECDEC_BF16) fail(SPECDEC_ERR_INVALID, "bad kv_dtype");
+    if (cfg->max_batch < 1 || cfg->max_lookahead < 1 || cfg->max_lookahead > 32 || cfg->max_prompt_len < 1)
+      fail(SPECDEC_ERR_INVALID, "max_batch / max_lookahead / max_prompt_len out of range");
+    h->tgt.dm = td;
+    h->dft.dm = dd;
+    CK(cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking));
+    h->use_graph = std::getenv("SPECDEC_NO_GRAPH") == nullptr;
+
+    const int B = cfg->max_batch, k = cfg->max_lookahead;
+    const size_t kv_elt = cfg->kv_dtype == SPECDEC_BF16 ? 2 : 4;
+    // KV caches: [layer][B][Hkv][cap][D]
+    h->t_cap = td.max_seq;
+    h->d_cap = dd.max_seq;
+    h->t_req_stride = static_cast<size_t>(td.Hkv) * h->t_cap * td.D;
+    h->d_req_stride = static_cast<size_t>(dd.Hkv) * h->d_cap * dd.D;
+    h->t_layer_stride = h->t_req_stride * B;
+    h->d_layer_stride = h->d_req_stride * B;
+    h->tk = h->dalloc(h->t_layer_stride * std::max(1, td.L) * kv_elt);
+    h->tv = h->dalloc(h->t_layer_stride * std::max(1, td.L) * kv_elt);
+    h->dk = h->dalloc(h->d_layer_stride * std::max(1, dd.L) * kv_elt);
+    h->dv = h->dalloc(h->d_layer_stride * std::max(1, dd.L) * kv_elt);
+    // RoPE table, computed with the reference's float formula
+    // (src/core/tensor.cpp:1147-1152): theta = pow(10000, -2j/D), omega = m*theta.
+    h->rope_max = std::max(td.max_seq, dd.max_seq);
+    h->rope_D = td.D;
+    {
+      const int D = td.D;
+      std::vector<float2> tab(static_cast<size_t>(h->rope_max) * (D / 2));
+      for (int m = 0; m < h->rope_max; ++m)
+        for (int j = 0; j < D / 2; ++j) {
+          const float theta = std::pow(10000.0f, -2.0f * static_cast<float>(j) / static_cast<float>(D));
+          const float omega = static_cast<float>(m) * theta;
+          tab[static_cast<size_t>(m) * (D / 2) + j] = make_float2(std::cos(omega), std::sin(omega));
+        }
+      h->rope = static_cast<float2 *>(h->dalloc(tab.size() * sizeof(float2)));
+      CK(cudaMemcpy(h->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    }
+    // activations
+    const int R_round = std::max(B * (k + 1), 2 * B);
+    h->R_max = std::max(R_round, std::min(B * cfg->max_prompt_len, std::max(8192, R_round)));
+    h->R_part = R_round;
+    h->max_split = 16;
+    h->act_elt = act_bf16(h.get()) ? 2 : 4;
+    const int dmax = std::max(td.d, dd.d), Fmax = std::max(td.F, dd.F);
+    const size_t rowb = static_cast<size_t>(h->R_max) * dmax * h->act_elt;
+    h->x = h->dalloc(rowb);
+    h->x1 = h->dalloc(rowb);
+    h->hb = h->dalloc(rowb);
+    h->qb = h->dalloc(rowb);
+    h->att = h->dalloc(rowb);
+    h->ffa = h->dalloc(static_cast<size_t>(h->R_max) * Fmax * h->act_elt);
+    h->logits = static_cast<float *>(h->dalloc(static_cast<size_t>(R_round) * td.V * sizeof(float)));
+    h->part = static_cast<float *>(
+        h->dalloc(static_cast<size_t>(h->R_part) * std::max(td.H, dd.H) * h->max_split * (std::max(td.D, dd.D) + 2) * sizeof(float)));
+    h->rtok = static_cast<int *>(h->dalloc(h->R_max * sizeof(int)));
+    h->rpos = static_cast<int *>(h->dalloc(h->R_max * sizeof(int)));
+    h->rreq = static_cast<int *>(h->dalloc(h->R_max * sizeof(int)));
+    h->sel = static_cast<int *>(h->dalloc(h->R_max * sizeof(int)));
+    // speculative state
+    SpecState &st = h->st;
+    const int out_len_max = cfg->max_prompt_len + std::max(td.max_seq, 1) + 1;
+    st.tokens_out = static_cast<int *>(h->dalloc(static_cast<size_t>(B) * out_len_max * sizeof(int)));
+    auto ib = [&](int n) { return static_cast<int *>(h->dalloc(static_cast<size_t>(n) * sizeof(int))); };
+    st.n_new = ib(B); st.t_len = ib(B); st.d_len = ib(B); st.t_start = ib(B); st.d_start = ib(B);
+    st.last_tok = ib(B); st.catch_tok = ib(B); st.active = ib(B); st.M = ib(B); st.round = ib(B);
+    st.cand = ib(B * k);
+    st.q = static_cast<float *>(h->dalloc(static_cast<size_t>(B) * k * td.V * sizeof(float)));
+    st.pbuf = static_cast<float *>(h->dalloc(static_cast<size_t>(B) * td.V * sizeof(float)));
+    st.stats = static_cast<long long *>(h->dalloc(static_cast<size_t>(B) * 4 * sizeof(long long)));
+    st.mt = static_cast<uint32_t *>(h->dalloc(static_cast<size_t>(B) * kMtN * sizeof(uint32_t)));
+    st.mt_idx = ib(B);
+    st.active_count = ib(1);
+    st.err = ib(1);
+    CK(cudaMemset(st.err, 0, sizeof(int)));
+    h->d_iters = ib(1);
+    h->d_prompts = ib(B * cfg->max_prompt_len);
+    h->d_out = static_cast<int *>(h->dalloc(static_cast<size_t>(B) * out_len_max * sizeof(int)));
+    h->d_stats = static_cast<long long *>(h->dalloc(static_cast<size_t>(B) * 4 * sizeof(long long)));
+    CK(cudaMallocHost(&h->h_pinned, 64));
+    CK(cudaDeviceSynchronize());
+  } catch (const SpecErr &e) {
+    g_create_err = e.msg;
+    specdec_destroy(h.release());
+    return e.code;
+  }
+  *out = h.release();
+  return SPECDEC_OK;
+}
+
+int specdec_destroy(specdec_handle *h) {
+  if (!h) return SPECDEC_OK;
+  cudaSetDevice(h->device);
+  if (h->stream) cudaStreamSynchronize(h->stream);
+  for (auto &kv : h->graphs) {
+    if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    if (kv.second.graph) cudaGraphDestroy(kv.second.graph);
+  }
+  for (int r = 0; r < 2; ++r)
+    for (void *p : h->weight_allocs[r]) cudaFree(p);
+  for (void *p : h->allocs) cudaFree(p);
+  if (h->d_uniforms) cudaFree(h->d_uniforms);
+  if (h->h_pinned) cudaFreeHost(h->h_pinned);
+  if (h->stream) cudaStreamDestroy(h->stream);
+  delete h;
+  return SPECDEC_OK;
+}
+
+void *specdec_stream(specdec_handle *h) { return h ? static_cast<void *>(h->stream) : nullptr; }
+
+int64_t specdec_last_launch_count(const specdec_handle *h) {
+  if (!h) return 0;
+  if (h->launches >= 0) return h->launches;
+  if (cudaMemcpyAsync(h->h_pinned + 1, h->d_iters, sizeof(int), cudaMemcpyDeviceToHost, h->stream) != cudaSuccess ||
+      cudaStreamSynchronize(h->stream) != cudaSuccess)
+    return -1;
+  return h->graph_fixed + h->graph_body * h->h_pinned[1] + h->extra_launches;
+}
+
+int specdec_load_params(specdec_handle *h, int role, int n_params, const float *const *params, const int64_t *numels) {
+  if (!h) return SPECDEC_ERR_INVALID;
+  try {
+    CK(cudaSetDevice(h->device));
+    if (!params || !numels) fail(SPECDEC_ERR_INVALID, "null parameter list");
+    if (role == SPECDEC_TARGET) {
+      load_model(h, 0, h->tgt, n_params, params, numels);
+      if (h->cfg.draft_shares_target) {
+        // draft = first n layers + shared embedding / lm_head, same device memory
+        ModelW &d = h->dft;
+        const ModelW &t = h->tgt;
+        d.emb = t.emb; d.pos = t.pos; d.gf = t.gf; d.bfin = t.bfin;
+        d.whead = t.whead; d.shead = t.shead; d.bhead = t.bhead;
+        d.layers.assign(t.layers.begin(), t.layers.begin() + d.dm.L);
+        d.loaded = true;
+      }
+    } else if (role == SPECDEC_DRAFT) {
+      if (h->cfg.draft_shares_target) fail(SPECDEC_ERR_STATE, "the draft shares the target's weights");
+      load_model(h, 1, h->dft, n_params, params, numels);
+    } else {
+      fail(SPECDEC_ERR_INVALID, "unknown role");
+    }
+    destroy_graphs(h);
+    CK(cudaDeviceSynchronize());
+  } catch (const SpecErr &e) {
+    h->err = e.msg;
+    return e.code;
+  }
+  return SPECDEC_OK;
+}
+
+int specdec_generate_device(specdec_handle *h, const specdec_gen_params *p, const int32_t *d_prompts, int B, int S,
+                            int32_t *d_out_tokens, int64_t *d_out_stats) {
+  if (!h) return SPECDEC_ERR_INVALID;
+  try {
+    CK(cudaSetDevice(h->device));
+    return generate_impl(h, p, d_prompts, B, S, d_out_tokens, d_out_stats, false);
+  } catch (const SpecErr &e) {
+    h->err = e.msg;
+    return e.code;
+  }
+}
+
+int specdec_generate(specdec_handle *h, const specdec_gen_params *p, const int32_t *prompts, int B, int S,
+                     int32_t *out_tokens, int64_t *out_stats) {
+  if (!h) return SPECDEC_ERR_INVALID;
+  try {
+    CK(cudaSetDevice(h->device));
+    if (!prompts || !out_tokens) fail(SPECDEC_ERR_INVALID, "null buffer");
+    if (!p) fail(SPECDEC_ERR_INVALID, "null params");
+    if (B < 1 || B > h->cfg.max_batch || S < 1 || S > h->cfg.max_prompt_len) fail(SPECDEC_ERR_INVALID, "batch or prompt length out of range");
+    CK(cudaMemcpyAsync(h->d_prompts, prompts, static_cast<size_t>(B) * S * sizeof(int), cudaMemcpyHostToDevice, h->stream));
+    int rc = generate_impl(h, p, h->d_prompts, B, S, h->d_out, reinterpret_cast<int64_t *>(h->d_stats), true);
+    if (rc != SPECDEC_OK) return rc;
+    const int n = S + std::max(1, p->max_new_tokens);
+    CK(cudaMemcpyAsync(out_tokens, h->d_out, static_cast<size_t>(B) * n * sizeof(int), cudaMemcpyDeviceToHost, h->stream));
+    if (out_stats)
+      CK(cudaMemcpyAsync(out_stats, h->d_stats, static_cast<size_t>(B) * 4 * sizeof(int64_t), cudaMemcpyDeviceToHost, h->stream));
+    int err = 0;
+    CK(cudaMemcpyAsync(h->h_pinned, h->st.err, sizeof(int), cudaMemcpyDeviceToHost, h->stream));
+    sync_check(h);
+    err = h->h_pinned[0];
+    if (err & kErrSeqLen) fail(SPECDEC_ERR_SEQ_LEN, "Sequence length S plus past cached length exceeds max_seq_len");
+    if (err & kErrRngTable) fail(SPECDEC_ERR_RNG, "the host uniform table has too few rounds");
+  } catch (const SpecErr &e) {
+    h->err = e.msg;
+    return e.code;
+  }
+  return SPECDEC_OK;
+}
+
+int specdec_forward_logits(specdec_handle *h, int role, const int32_t *tokens, int S, float *logits) {
+  if (!h) return SPECDEC_ERR_INVALID;
+  try {
+    CK(cudaSetDevice(h->device));
+    const bool target = role == SPECDEC_TARGET;
+    ModelW &m = target ? h->tgt : h->dft;
+    if (!m.loaded) fail(SPECDEC_ERR_STATE, "weights not loaded");
+    if (S < 1 || S > (target ? h->t_cap : h->d_cap) || S > h->R_max || S > h->cfg.max_prompt_len)
+      fail(SPECDEC_ERR_INVALID, "sequence length out of range");
+    CK(cudaMemsetAsync(h->st.err, 0, sizeof(int), h->stream));
+    CK(cudaMemcpyAsync(h->d_prompts, tokens, S * sizeof(int), cudaMemcpyHostToDevice, h->stream));
+    plan_prefill_kernel<<<(S + 255) / 256, 256, 0, h->stream>>>(h->d_prompts, 1, S, 0, S, h->rtok, h->rpos, h->rreq, h->sel);
+    // logits for every row: identity selection, in chunks that fit the logits buffer
+    const int R_round = std::max(h->cfg.max_batch * (h->cfg.max_lookahead + 1), 2 * h->cfg.max_batch);
+    forward_rows(h, target, S, nullptr, 0, nullptr);
+    // head over row chunks
+    std::vector<int> idx(S);
+    for (int i = 0; i < S; ++i) idx[i] = i;
+    for (int c0 = 0; c0 < S; c0 += R_round) {
+      const int n = std::min(R_round, S - c0);
+      CK(cudaMemcpyAsync(h->sel, idx.data() + c0, n * sizeof(int), cudaMemcpyHostToDevice, h->stream));
+      const void *hin = h->x;
+      const Dims &dm = m.dm;
+      if (dm.arch != SPECDEC_ARCH_REF) {
+        layernorm(h, h->x, S, dm.d, m.gf, m.bfin, h->x1);
+        hin = h->x1;
+      }
+      LinearArgs hd{};
+      hd.x = hin; hd.ldx = dm.d; hd.in_rows = h->sel; hd.R = n; hd.W = m.whead; hd.scale = m.shead; hd.bias = m.bhead;
+      hd.N = dm.V; hd.K = dm.d; hd.out = h->logits; hd.ldo = dm.V;
+      dim3 grid((hd.N + 2 * kLinWarps - 1) / (2 * kLinWarps), (hd.R + kRowTile - 1) / kRowTile);
+      const bool bf = act_bf16(h), i8 = w_int8(h);
+      if (i8 && bf) head_kernel<int8_t, __nv_bfloat16><<<grid, 32 * kLinWarps, 0, h->stream>>>(hd);
+      else if (i8) head_kernel<int8_t, float><<<grid, 32 * kLinWarps, 0, h->stream>>>(hd);
+      else if (bf) head_kernel<float, __nv_bfloat16><<<grid, 32 * kLinWarps, 0, h->stream>>>(hd);
+      else head_kernel<float, float><<<grid, 32 * kLinWarps, 0, h->stream>>>(hd);
+      CK(cudaGetLastError());
+      CK(cudaMemcpyAsync(logits + static_cast<size_t>(c0) * dm.V, h->logits, static_cast<size_t>(n) * dm.V * sizeof(float),
+                         cudaMemcpyDeviceToHost, h->stream));
+    }
+    int err = 0;
+    CK(cudaMemcpyAsync(h->h_pinned, h->st.err, sizeof(int), cudaMemcpyDeviceToHost, h->stream));
+    sync_check(h);
+    err = h->h_pinned[0];
+    if (err) fail(SPECDEC_ERR_SEQ_LEN, "cache capacity exceeded");
+  } catch (const SpecErr &e) {
+    h->err = e.msg;
+    return e.code;
+  }
+  return SPECDEC_OK;
+}
+
+int specdec_philox_uniforms(uint64_t seed, int B, int rounds, int slots, float *out) {
+  if (!out || B < 0 || rounds < 0 || slots < 0) return SPECDEC_ERR_INVALID;
+  const uint32_t M0 = 0xD2511F53u, M1 = 0xCD9E8D57u, W0 = 0x9E3779B9u, W1 = 0xBB67AE85u;
+  const int nblk = (slots + 3) / 4;
+  for (int b = 0; b < B; ++b)
+    for (int r = 0; r < rounds; ++r)
+      for (int blk = 0; blk < nblk; ++blk) {
+        uint32_t c[4] = {static_cast<uint32_t>(blk), static_cast<uint32_t>(r), static_cast<uint32_t>(b), 0x53504543u};
+        uint32_t k0 = static_cast<uint32_t>(seed), k1 = static_cast<uint32_t>(seed >> 32);
+        for (int i = 0; i < 10; ++i) {
+          const uint64_t p0 = static_cast<uint64_t>(M0) * c[0], p1 = static_cast<uint64_t>(M1) * c[2];
+          const uint32_t hi0 = static_cast<uint32_t>(p0 >> 32), lo0 = static_cast<uint32_t>(p0);
+          const uint32_t hi1 = static_cast<uint32_t>(p1 >> 32), lo1 = static_cast<uint32_t>(p1);
+          const uint32_t n0 = hi1 ^ c[1] ^ k0, n2 = hi0 ^ c[3] ^ k1;
+          c[0] = n0; c[1] = lo1; c[2] = n2; c[3] = lo0;
+          k0 += W0;
+          k1 += W1;
+        }
+        for (int l = 0; l < 4; ++l) {
+          const int s = blk * 4 + l;
+          if (s < slots) out[(static_cast<size_t>(b) * rounds + r) * slots + s] = static_cast<float>(c[l] >> 8) * (1.0f / 16777216.0f);
+        }
+      }
+  return SPECDEC_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,195 @@
+"""Python binding of the B200 speculative-decoding backend (libspecdec_b200.so).
+
+Mirrors the reference's entry point
+``TransformerDecoder::generate_speculative(draft, prompt, max_new_tokens,
+lookahead, temperature, top_k, top_p, seed, quantized_cache)``
+(include/nn/layer.hpp:318-323, src/nn/layer.cpp:1382-1661) over the C ABI of
+include/specdec.h, batched over B requests.  Failures raise ``SpecDecError``
+(a RuntimeError, as the reference throws std::runtime_error).
+
+There is no CPU fallback: if the shared library is missing or cannot be
+loaded, importing the engine raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from typing import Optional, Sequence, Tuple
+
+import numpy as np
+
+from .synth import ARCH_CFG, ARCH_REF, ModelShape  # noqa: F401
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libspecdec_b200.so")
+
+F32, BF16, INT8 = 0, 1, 2
+TARGET, DRAFT = 0, 1
+RNG_MT19937, RNG_HOST_UNIFORM = 0, 1
+CATCHUP_REF, CATCHUP_CORRECT = 0, 1
+
+STATUS = {0: "OK", 1: "ERR_INVALID", 2: "ERR_CUDA", 3: "ERR_OOM", 4: "ERR_SEQ_LEN", 5: "ERR_UNSUPPORTED",
+          6: "ERR_STATE", 7: "ERR_RNG"}
+
+# Every symbol include/specdec.h declares.
+EXPORTS = ("specdec_create", "specdec_destroy", "specdec_last_error", "specdec_load_params",
+           "specdec_generate", "specdec_generate_device", "specdec_stream", "specdec_forward_logits",
+           "specdec_philox_uniforms", "specdec_last_launch_count")
+
+
+class SpecDecError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{STATUS.get(code, code)}: {msg}")
+        self.code = code
+
+
+class _ModelConfig(C.Structure):
+    _fields_ = [("vocab_size", C.c_int32), ("d_model", C.c_int32), ("n_heads", C.c_int32),
+                ("n_kv_heads", C.c_int32), ("d_ff", C.c_int32), ("n_layers", C.c_int32),
+                ("max_seq_len", C.c_int32), ("arch", C.c_int32)]
+
+
+class _Config(C.Structure):
+    _fields_ = [("target", _ModelConfig), ("draft", _ModelConfig), ("draft_shares_target", C.c_int32),
+                ("weight_dtype", C.c_int32), ("act_dtype", C.c_int32), ("kv_dtype", C.c_int32),
+                ("max_batch", C.c_int32), ("max_lookahead", C.c_int32), ("max_prompt_len", C.c_int32)]
+
+
+class _GenParams(C.Structure):
+    _fields_ = [("max_new_tokens", C.c_int32), ("lookahead", C.c_int32), ("temperature", C.c_float),
+                ("top_k", C.c_int32), ("top_p", C.c_float), ("rng_mode", C.c_int32), ("seed", C.c_uint32),
+                ("uniforms", C.c_void_p), ("uniform_rounds", C.c_int32), ("draft_catchup", C.c_int32)]
+
+
+_lib = None
+
+
+def load_library(path: str = LIB_PATH):
+    """Loads the shared library (raises if it is absent: no fallback path)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise ImportError(f"{path} is missing; build it with neural-network_b200/build.py")
+    lib = C.CDLL(path)
+    lib.specdec_create.argtypes = [C.POINTER(_Config), C.c_int, C.POINTER(C.c_void_p)]
+    lib.specdec_destroy.argtypes = [C.c_void_p]
+    lib.specdec_last_error.restype = C.c_char_p
+    lib.specdec_last_error.argtypes = [C.c_void_p]
+    lib.specdec_load_params.argtypes = [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_void_p),
+                                        C.POINTER(C.c_int64)]
+    lib.specdec_generate.argtypes = [C.c_void_p, C.POINTER(_GenParams), C.c_void_p, C.c_int, C.c_int,
+                                     C.c_void_p, C.c_void_p]
+    lib.specdec_generate_device.argtypes = [C.c_void_p, C.POINTER(_GenParams), C.c_void_p, C.c_int, C.c_int,
+                                            C.c_void_p, C.c_void_p]
+    lib.specdec_stream.restype = C.c_void_p
+    lib.specdec_stream.argtypes = [C.c_void_p]
+    lib.specdec_forward_logits.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p]
+    lib.specdec_philox_uniforms.argtypes = [C.c_uint64, C.c_int, C.c_int, C.c_int, C.c_void_p]
+    lib.specdec_last_launch_count.restype = C.c_int64
+    lib.specdec_last_launch_count.argtypes = [C.c_void_p]
+    _lib = lib
+    return lib
+
+
+def _mcfg(m: ModelShape) -> _ModelConfig:
+    return _ModelConfig(m.vocab, m.d_model, m.n_heads, m.n_kv_heads, m.d_ff, m.n_layers, m.max_seq_len, m.arch)
+
+
+def philox_uniforms(seed: int, B: int, rounds: int, slots: int) -> np.ndarray:
+    lib = load_library()
+    out = np.zeros((B, rounds, slots), np.float32)
+    rc = lib.specdec_philox_uniforms(seed, B, rounds, slots, out.ctypes.data)
+    if rc:
+        raise SpecDecError(rc, "philox")
+    return out
+
+
+class Engine:
+    """A target/draft pair on one B200 (one handle of the C ABI)."""
+
+    def __init__(self, target: ModelShape, draft_layers: Optional[int] = None, draft: Optional[ModelShape] = None,
+                 weight_dtype: int = F32, act_dtype: int = F32, kv_dtype: int = F32, max_batch: int = 1,
+                 max_lookahead: int = 4, max_prompt_len: int = 128, device: int = 0):
+        lib = load_library()
+        shares = draft is None
+        if shares and draft_layers is None:
+            raise ValueError("give draft_layers (shared draft) or a draft shape")
+        dshape = target.with_layers(draft_layers) if shares else draft
+        cfg = _Config(_mcfg(target), _mcfg(dshape), 1 if shares else 0, weight_dtype, act_dtype, kv_dtype,
+                      max_batch, max_lookahead, max_prompt_len)
+        h = C.c_void_p()
+        rc = lib.specdec_create(C.byref(cfg), device, C.byref(h))
+        if rc:
+            raise SpecDecError(rc, lib.specdec_last_error(None).decode())
+        self._lib = lib
+        self.h = h
+        self.target = target
+        self.draft = dshape
+        self.shares = shares
+        self.max_batch = max_batch
+        self.max_lookahead = max_lookahead
+
+    def close(self):
+        if getattr(self, "h", None):
+            self._lib.specdec_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def _check(self, rc: int):
+        if rc:
+            raise SpecDecError(rc, self._lib.specdec_last_error(self.h).decode())
+
+    def load_params(self, role: int, params: Sequence[np.ndarray]) -> None:
+        arrs = [np.ascontiguousarray(p, np.float32) for p in params]
+        ptrs = (C.c_void_p * len(arrs))(*[a.ctypes.data for a in arrs])
+        nums = (C.c_int64 * len(arrs))(*[a.size for a in arrs])
+        self._check(self._lib.specdec_load_params(self.h, role, len(arrs), ptrs, nums))
+
+    def _params(self, max_new, lookahead, temperature, top_k, top_p, seed, uniforms, draft_catchup):
+        if uniforms is not None:
+            u = np.ascontiguousarray(uniforms, np.float32)
+            return _GenParams(max_new, lookahead, temperature, top_k, top_p, RNG_HOST_UNIFORM, seed & 0xFFFFFFFF,
+                              u.ctypes.data, u.shape[1], draft_catchup), u
+        return _GenParams(max_new, lookahead, temperature, top_k, top_p, RNG_MT19937, seed & 0xFFFFFFFF, None, 0,
+                          draft_catchup), None
+
+    def generate_speculative(self, prompts, max_new_tokens: int, lookahead: int = 4, temperature: float = 1.0,
+                             top_k: int = 0, top_p: float = 1.0, seed: int = 42,
+                             uniforms: Optional[np.ndarray] = None,
+                             draft_catchup: int = CATCHUP_REF) -> Tuple[np.ndarray, np.ndarray]:
+        """prompts [B, S] -> (tokens [B, S + max(1, max_new)], stats [B, 4])."""
+        p = np.ascontiguousarray(np.atleast_2d(prompts), np.int32)
+        B, S = p.shape
+        prm, keep = self._params(max_new_tokens, lookahead, temperature, top_k, top_p, seed, uniforms, draft_catchup)
+        out = np.zeros((B, S + max(1, max_new_tokens)), np.int32)
+        stats = np.zeros((B, 4), np.int64)
+        self._check(self._lib.specdec_generate(self.h, C.byref(prm), p.ctypes.data, B, S, out.ctypes.data,
+                                               stats.ctypes.data))
+        del keep
+        return out.astype(np.int64), stats
+
+    def generate_device(self, d_prompts: int, B: int, S: int, d_out: int, d_stats: int, max_new_tokens: int,
+                        lookahead: int = 4, temperature: float = 1.0, seed: int = 42, uniforms=None,
+                        draft_catchup: int = CATCHUP_REF) -> None:
+        """Device-pointer variant (ints are raw CUDA pointers); enqueued on `stream`."""
+        prm, keep = self._params(max_new_tokens, lookahead, temperature, 0, 1.0, seed, uniforms, draft_catchup)
+        self._check(self._lib.specdec_generate_device(self.h, C.byref(prm), C.c_void_p(d_prompts), B, S,
+                                                      C.c_void_p(d_out), C.c_void_p(d_stats)))
+        del keep
+
+    def forward_logits(self, role: int, tokens) -> np.ndarray:
+        t = np.ascontiguousarray(tokens, np.int32).ravel()
+        V = self.target.vocab
+        out = np.zeros((t.size, V), np.float32)
+        self._check(self._lib.specdec_forward_logits(self.h, role, t.ctypes.data, t.size, out.ctypes.data))
+        return out
+
+    @property
+    def stream(self) -> int:
+        return int(self._lib.specdec_stream(self.h) or 0)
+
+    def last_launch_count(self) -> int:
+        return int(self._lib.specdec_last_launch_count(self.h))

@@ -1,0 +1,96 @@
+"""Parity of the B200 path (through the C ABI) against the CPU restatement
+oracle on identical seeded weights, prompts and uniforms.
+
+Tolerances (the ones the parity contract states): logits within 1e-3
+relative in fp32 and 2e-2 relative with bf16 activations; tokens bit-exact
+except at logged near-ties (helpers.compare_tokens)."""
+import numpy as np
+import pytest
+
+import specdec_b200 as sd
+from helpers import compare_tokens, make_pair, run_both
+from specdec_b200.synth import ARCH_CFG, ModelShape, make_prompts
+
+pytestmark = pytest.mark.gpu
+
+FP32_REL = 1e-3
+BF16_REL = 2e-2
+
+SHAPES = {
+    "tiny8": (ModelShape(vocab=8, d_model=8, n_heads=2, d_ff=16, n_layers=2, max_seq_len=96), 1),
+    "small": (ModelShape(vocab=97, d_model=32, n_heads=4, d_ff=64, n_layers=2, max_seq_len=160), 1),
+    "cfg1": (ModelShape(vocab=2048, d_model=256, n_heads=4, d_ff=1024, n_layers=4, max_seq_len=200), 1),
+}
+
+
+def rel_err(a, b):
+    return float(np.max(np.abs(a - b)) / max(1e-30, float(np.max(np.abs(b)))))
+
+
+@pytest.mark.parametrize("name", list(SHAPES))
+@pytest.mark.parametrize("int8", [False, True])
+def test_forward_logits(gpu_lib, oracle_built, name, int8):
+    shape, dl = SHAPES[name]
+    pair = make_pair(shape, dl, seed=3, int8=int8, max_prompt_len=40)
+    toks = make_prompts(1, 33, shape.vocab, seed=9)[0]
+    for role, om in ((sd.TARGET, pair.target), (sd.DRAFT, pair.draft)):
+        g = pair.engine.forward_logits(role, toks)
+        o = om.forward(toks)
+        assert rel_err(g, o) < FP32_REL, (name, role, rel_err(g, o))
+
+
+def test_forward_logits_bf16(gpu_lib, oracle_built):
+    shape, dl = SHAPES["cfg1"]
+    pair = make_pair(shape, dl, seed=4, int8=True, act_bf16=True, kv_mode=1, max_prompt_len=40)
+    toks = make_prompts(1, 24, shape.vocab, seed=10)[0]
+    g = pair.engine.forward_logits(sd.TARGET, toks)
+    o = pair.target.forward(toks, act_bf16=True, kv_mode=1)
+    assert rel_err(g, o) < BF16_REL
+
+
+def test_forward_logits_cfg_arch(gpu_lib, oracle_built):
+    shape = ModelShape(vocab=300, d_model=64, n_heads=4, d_ff=128, n_layers=3, max_seq_len=64, arch=ARCH_CFG)
+    pair = make_pair(shape, 1, seed=5, max_prompt_len=40)
+    toks = make_prompts(1, 20, shape.vocab, seed=11)[0]
+    for role, om in ((sd.TARGET, pair.target), (sd.DRAFT, pair.draft)):
+        assert rel_err(pair.engine.forward_logits(role, toks), om.forward(toks)) < FP32_REL
+
+
+@pytest.mark.parametrize("name", list(SHAPES))
+@pytest.mark.parametrize("B", [1, 3])
+def test_greedy_spec(gpu_lib, oracle_built, name, B):
+    shape, dl = SHAPES[name]
+    pair = make_pair(shape, dl, seed=6, max_batch=4, max_prompt_len=40)
+    _, tg, sg, to, so, mg = run_both(pair, B, 12, 40, 4, 0.0)
+    exact, ties = compare_tokens(tg, to, mg, 12, greedy=True)
+    assert exact + ties == B and ties <= max(1, B // 3)
+    if ties == 0:
+        assert np.array_equal(sg, so)
+
+
+@pytest.mark.parametrize("name", ["tiny8", "small", "cfg1"])
+@pytest.mark.parametrize("T", [1.0, 0.7])
+def test_sampled_mt19937(gpu_lib, oracle_built, name, T):
+    shape, dl = SHAPES[name]
+    pair = make_pair(shape, dl, seed=7, max_batch=4, max_prompt_len=40)
+    _, tg, sg, to, so, mg = run_both(pair, 3, 10, 48, 3, T, seed=123)
+    exact, ties = compare_tokens(tg, to, mg, 10, greedy=False)
+    assert exact + ties == 3 and ties <= 1
+
+
+@pytest.mark.parametrize("int8", [False, True])
+def test_sampled_host_uniforms(gpu_lib, oracle_built, int8):
+    shape, dl = SHAPES["cfg1"]
+    pair = make_pair(shape, dl, seed=8, int8=int8, max_batch=4, max_prompt_len=40)
+    _, tg, sg, to, so, mg = run_both(pair, 4, 16, 48, 4, 1.0, seed=2024, use_uniforms=True)
+    exact, ties = compare_tokens(tg, to, mg, 16, greedy=False)
+    assert exact + ties == 4 and ties <= 1
+
+
+@pytest.mark.parametrize("T", [0.0, 1.0])
+def test_catchup_correct(gpu_lib, oracle_built, T):
+    shape, dl = SHAPES["small"]
+    pair = make_pair(shape, dl, seed=9, max_batch=4, max_prompt_len=40)
+    _, tg, sg, to, so, mg = run_both(pair, 2, 8, 40, 3, T, seed=5, use_uniforms=T > 0, catchup=1)
+    exact, ties = compare_tokens(tg, to, mg, 8, greedy=T <= 0)
+    assert exact + ties == 2

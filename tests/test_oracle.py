@@ -1,0 +1,165 @@
+"""The CPU restatement (oracle/specdec_oracle.cpp) pinned against the
+reference: committed golden fixtures made by the unmodified reference
+(tests/golden/make_golden.py), the reference's own unit-test known answers,
+and -- where the reference library is built here -- live comparisons."""
+import numpy as np
+import pytest
+
+import oracle
+from specdec_b200.synth import ModelShape, draft_params, make_params, make_prompts, philox4x32_10, philox_uniforms
+
+GOLDEN_MODELS = {
+    "tiny8": (ModelShape(vocab=8, d_model=8, n_heads=2, d_ff=16, n_layers=2, max_seq_len=64), 1, 11, 0.05),
+    "tiny6": (ModelShape(vocab=6, d_model=8, n_heads=2, d_ff=16, n_layers=2, max_seq_len=64), 1, 12, 0.05),
+    "small": (ModelShape(vocab=97, d_model=32, n_heads=4, d_ff=64, n_layers=2, max_seq_len=160), 1, 13, 0.02),
+    "cfg1cut": (ModelShape(vocab=2048, d_model=256, n_heads=4, d_ff=1024, n_layers=2, max_seq_len=96), 1, 0, 0.0),
+}
+
+
+def _models(name):
+    shape, dl, seed, jit = GOLDEN_MODELS[name]
+    P = make_params(shape, seed=seed, bias_std=jit, ln_jitter=jit)
+    return shape, oracle.Oracle(shape, P), oracle.Oracle(shape.with_layers(dl), draft_params(shape, P, dl))
+
+
+@pytest.mark.parametrize("name", list(GOLDEN_MODELS))
+def test_oracle_logits_match_reference_fixture(oracle_built, golden, name):
+    shape, t, d = _models(name)
+    prompt = golden[f"{name}/prompt"]
+    for key, m in (("logits_target", t), ("logits_draft", d)):
+        ref = golden[f"{name}/{key}"]
+        got = m.forward(prompt)
+        assert np.max(np.abs(got - ref)) <= 1e-5 * max(1.0, np.max(np.abs(ref))), key
+    # the reference's fused and unfused attention agree (gqa_test.cpp:115-211 asserts 1e-4)
+    assert np.max(np.abs(golden[f"{name}/logits_target_unfused"] - golden[f"{name}/logits_target"])) < 1e-4
+
+
+@pytest.mark.parametrize("name", list(GOLDEN_MODELS))
+def test_oracle_spec_tokens_match_reference_fixture(oracle_built, golden, name):
+    shape, t, d = _models(name)
+    prompt = golden[f"{name}/prompt"]
+    n = 0
+    for key in golden:
+        if not key.startswith(f"{name}/spec/") or key.endswith("/args"):
+            continue
+        mn, k, T, tk, tp, seed, qc = golden[key + "/args"]
+        out, stats, _ = oracle.oracle_generate_speculative(t, d, prompt[None], int(mn), int(k), float(T), int(tk),
+                                                           float(tp), int(seed), kv_mode=2 if qc else 0)
+        assert np.array_equal(out[0], golden[key]), key
+        n += 1
+    assert n >= 2
+
+
+@pytest.mark.parametrize("name", list(GOLDEN_MODELS))
+def test_oracle_ar_matches_reference_fixture(oracle_built, golden, name):
+    shape, t, d = _models(name)
+    prompt = golden[f"{name}/prompt"]
+    assert np.array_equal(t.generate_advanced(prompt, 12, 0.0, 0, 1.0, 42), golden[f"{name}/ar_greedy"])
+    assert np.array_equal(t.generate_advanced(prompt, 12, 0.9, 5, 0.8, 7), golden[f"{name}/ar_t09"])
+    # KVCachingCorrectness (transformer_test.cpp:250-273): cache == no cache
+    assert np.array_equal(golden[f"{name}/ar_greedy"], golden[f"{name}/ar_greedy_nocache"])
+
+
+def test_greedy_spec_equals_greedy_ar(oracle_built, golden):
+    # SpeculativeDecodingParity (transformer_test.cpp:307-335)
+    for name in GOLDEN_MODELS:
+        g = golden[f"{name}/spec/greedy"]
+        ar = golden[f"{name}/ar_greedy"]
+        assert np.array_equal(g, ar), name
+
+
+def test_rope_known_answer(oracle_built, golden):
+    # RopeAutogradVerification (rope_swiglu_test.cpp:34-35): D=4, m=1, (5,6) -> (-2.34731, 7.44917)
+    x = golden["rope/in"].reshape(2, 4)
+    out = oracle.oracle_rope(x, np.array([0, 1], np.int32))
+    assert np.allclose(out[0], [1, 2, 3, 4], atol=1e-5)
+    assert abs(out[1, 0] - (-2.34731)) < 1e-4 and abs(out[1, 1] - 7.44917) < 1e-4
+    assert np.array_equal(out.reshape(golden["rope/out"].shape), golden["rope/out"])
+
+
+def test_int8_known_answer(oracle_built, golden):
+    # SymmetricInt8 (quantization_test.cpp:15-25): scales 0.1 / 0.05
+    s = golden["int8/scales"]
+    assert abs(s[0] - 0.1) < 1e-5 and abs(s[1] - 0.05) < 1e-5
+    shape = ModelShape(vocab=2, d_model=2, n_heads=1, d_ff=2, n_layers=0, max_seq_len=4)
+    P = make_params(shape, seed=0)
+    P[-2] = golden["int8/w"].copy()
+    m = oracle.Oracle(shape, P, int8=True)
+    assert np.array_equal(m.param(len(P) - 2).reshape(2, 2), golden["int8/dequant"])
+
+
+def test_mt19937_standard_value(oracle_built):
+    # [rand.predef]: the 10000th output of a default-constructed mt19937 is 4123659995
+    assert int(oracle.mt19937(5489, 10000)[-1]) == 4123659995
+
+
+def test_philox_known_answers():
+    # Random123 published known-answer vectors for philox4x32-10
+    kat = [((0, 0, 0, 0), (0, 0), (0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8)),
+           ((0xFFFFFFFF,) * 4, (0xFFFFFFFF, 0xFFFFFFFF), (0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD)),
+           ((0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344), (0xA4093822, 0x299F31D0),
+            (0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1))]
+    for ctr, key, want in kat:
+        got = philox4x32_10(np.array([ctr], np.uint32), key)[0]
+        assert tuple(int(x) for x in got) == want
+    u = philox_uniforms(5, 2, 3, 9)
+    assert u.shape == (2, 3, 9) and u.min() >= 0.0 and u.max() < 1.0
+
+
+def test_host_uniform_mode_is_a_valid_sampler(oracle_built):
+    """Rejection sampling with table uniforms keeps the target distribution:
+    the first new token after one round, over many seeds, follows the target's
+    own next-token distribution (chi-square at V=8)."""
+    shape = ModelShape(vocab=8, d_model=8, n_heads=2, d_ff=16, n_layers=2, max_seq_len=32)
+    P = make_params(shape, seed=21, bias_std=0.3, ln_jitter=0.2, head_std=0.6)
+    t = oracle.Oracle(shape, P)
+    d = oracle.Oracle(shape.with_layers(1), draft_params(shape, P, 1))
+    prompt = np.array([[1, 2, 3]], np.int64)
+    N = 4000
+    prompts = np.repeat(prompt, N, axis=0)
+    uni = philox_uniforms(99, N, 4, 2 * 2 + 1)
+    out, _, _ = oracle.oracle_generate_speculative(t, d, prompts, 3, 2, 1.0, uniforms=uni, n_threads=8)
+    # position S+1: produced by the speculative round (draft + acceptance)
+    first = out[:, 3]
+    second = out[:, 4]
+    # exact target conditional for the second token given the first
+    counts = np.zeros(8)
+    expect = np.zeros(8)
+    for a in range(8):
+        sel = first == a
+        if sel.sum() < 50:
+            continue
+        lg = t.forward(np.array([1, 2, 3, a]))[-1]
+        p = oracle.oracle_get_probs(lg, 1.0)
+        counts += np.bincount(second[sel], minlength=8)
+        expect += p * sel.sum()
+    mask = expect > 5
+    chi2 = float(np.sum((counts[mask] - expect[mask]) ** 2 / expect[mask]))
+    assert chi2 < 40.0, (chi2, counts, expect)
+
+
+@pytest.mark.skipif(not oracle.reference_available(), reason="reference library not built here")
+@pytest.mark.parametrize("T,seed,k", [(0.0, 1, 4), (1.0, 3, 4), (0.8, 5, 2), (1.0, 9, 1)])
+def test_oracle_matches_live_reference(oracle_built, T, seed, k):
+    shape = ModelShape(vocab=211, d_model=48, n_heads=6, d_ff=96, n_layers=3, max_seq_len=200)
+    P = make_params(shape, seed=seed, bias_std=0.02, ln_jitter=0.05)
+    DP = draft_params(shape, P, 1)
+    rt = oracle.Reference(shape, P, requires_grad=False)
+    rd = oracle.Reference(shape.with_layers(1), DP, requires_grad=False)
+    t, d = oracle.Oracle(shape, P), oracle.Oracle(shape.with_layers(1), DP)
+    prompt = make_prompts(1, 17, shape.vocab, seed=seed)[0]
+    ref = rt.generate_speculative(rd, prompt, 40, k, T, 0, 1.0, seed)
+    got, _, _ = oracle.oracle_generate_speculative(t, d, prompt[None], 40, k, T, seed=seed)
+    assert np.array_equal(ref, got[0])
+
+
+@pytest.mark.skipif(not oracle.reference_available(), reason="reference library not built here")
+def test_oracle_int8_matches_reference_quantizer(oracle_built):
+    rng = np.random.default_rng(0)
+    w = rng.standard_normal((64, 48)).astype(np.float32)
+    s, q, dq = oracle.ref_quantize_int8(w)
+    shape = ModelShape(vocab=48, d_model=64, n_heads=1, d_ff=2, n_layers=0, max_seq_len=4)
+    P = make_params(shape, seed=0)
+    P[-2] = w
+    m = oracle.Oracle(shape, P, int8=True)
+    assert np.array_equal(m.param(len(P) - 2).reshape(64, 48), dq)
