@@ -146,6 +146,24 @@ int specdec_forward_logits(specdec_handle *h, int role, const int32_t *tokens,
 int specdec_philox_uniforms(uint64_t seed, int B, int rounds, int slots,
                             float *out);
 
+/* No counterpart in the reference.  The forward of specdec_forward_logits for
+ * callers that cannot allocate device memory when they need it: code running
+ * inside another runtime's memory pool, latency-critical loops where an
+ * allocation may stall the device, or a shared context that must not grow.
+ * d_tokens [S] int32 and d_logits [S][vocab] fp32 are DEVICE buffers the caller
+ * owns; the call is asynchronous on `stream` (a cudaStream_t; NULL selects
+ * specdec_stream(h)).  Every byte of working memory (activations, row tables,
+ * the sequence's KV cache, attention partials) comes from one fixed 8 MiB
+ * device array inside the library; work that needs more is rejected with
+ * SPECDEC_ERR_INVALID.  No cudaMalloc, cudaFree or other allocating call is
+ * made.  The array is shared by all calls on a device and keeps the last
+ * call's contents: calls that overlap on the GPU race and must be serialised
+ * by the caller.  The first call on each device looks the array's address up
+ * (that device current); make it before any stream capture begins. */
+int specdec_forward_logits_noalloc(specdec_handle *h, int role,
+                                   const int32_t *d_tokens, int S,
+                                   float *d_logits, void *stream);
+
 /* Number of kernel launches the last generate call issued on the device. */
 int64_t specdec_last_launch_count(const specdec_handle *h);
 

@@ -22,6 +22,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <memory>
 #include <string>
 #include <thread>
@@ -1103,3 +1104,152 @@ int specdec_philox_uniforms(uint64_t seed, int B, int rounds, int slots, float *
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Forward logits without any device allocation.
+//
+// Some callers cannot call cudaMalloc at the moment they need a forward pass:
+// code that runs inside another runtime's memory pool (which owns every
+// device byte and forbids allocations behind its back), real-time serving
+// loops where an allocation can stall the device, and callers whose CUDA
+// context is shared and must not grow.  For them this entry point takes the
+// tokens and the logits as device buffers they already own and keeps all of
+// its own working memory (activations, the row tables, the per-sequence KV
+// cache and the split-K attention partials) in one file-scope device array of
+// fixed size, SPECDEC_NOALLOC_SCRATCH_BYTES, which every GPU that loads this
+// library holds until the process exits.  It calls no cudaMalloc, cudaFree or
+// allocating library routine.
+//
+// The array is shared by every call on a device and keeps the last call's
+// contents; the error word is cleared at the start of each call.  Calls whose
+// work overlaps on the GPU (different streams, or different handles on the
+// same device) race on the array and must be serialised by the caller.  The
+// first call on each device looks up the array's device address
+// (cudaGetSymbolAddress) with that device current; make that first call
+// before starting any stream capture.
+#define SPECDEC_NOALLOC_SCRATCH_BYTES (8u << 20)
+static __device__ __align__(256) unsigned char g_noalloc_scratch[SPECDEC_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_noalloc_mu;
+std::map<int, unsigned char *> g_noalloc_base;  // device ordinal -> device address of the array
+
+// The device address of the scratch array on the current device (set-up once
+// per device).  The host-side name of the array is not a device address.
+cudaError_t noalloc_base(int device, unsigned char **out) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  auto it = g_noalloc_base.find(device);
+  if (it != g_noalloc_base.end()) {
+    *out = it->second;
+    return cudaSuccess;
+  }
+  void *ptr = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+  if (e != cudaSuccess) return e;
+  g_noalloc_base[device] = static_cast<unsigned char *>(ptr);
+  *out = static_cast<unsigned char *>(ptr);
+  return cudaSuccess;
+}
+
+struct ArenaCarver {
+  unsigned char *base;
+  size_t used = 0;
+  void *take(size_t bytes) {
+    void *p = base ? base + used : nullptr;
+    used += (bytes + 255) & ~size_t(255);
+    return p;
+  }
+};
+}  // namespace
+
+extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const int32_t *d_tokens, int S,
+                                              float *d_logits, void *stream) {
+  if (!h) return SPECDEC_ERR_INVALID;
+  // The handle's buffers are pointed at the scratch array for the duration of
+  // the call and restored on every exit path.
+  struct Saved {
+    void *x, *x1, *hb, *qb, *att, *ffa, *tk, *tv, *dk, *dv;
+    float *part;
+    int *rtok, *rpos, *rreq, *sel, *err;
+    size_t tls, dls, trs, drs;
+    int tcap, dcap, R_part, max_split, R_max;
+    cudaStream_t stream;
+  };
+  Saved sv{h->x, h->x1, h->hb, h->qb, h->att, h->ffa, h->tk, h->tv, h->dk, h->dv, h->part,
+           h->rtok, h->rpos, h->rreq, h->sel, h->st.err, h->t_layer_stride, h->d_layer_stride,
+           h->t_req_stride, h->d_req_stride, h->t_cap, h->d_cap, h->R_part, h->max_split, h->R_max, h->stream};
+  auto restore = [&] {
+    h->x = sv.x; h->x1 = sv.x1; h->hb = sv.hb; h->qb = sv.qb; h->att = sv.att; h->ffa = sv.ffa;
+    h->tk = sv.tk; h->tv = sv.tv; h->dk = sv.dk; h->dv = sv.dv; h->part = sv.part;
+    h->rtok = sv.rtok; h->rpos = sv.rpos; h->rreq = sv.rreq; h->sel = sv.sel; h->st.err = sv.err;
+    h->t_layer_stride = sv.tls; h->d_layer_stride = sv.dls; h->t_req_stride = sv.trs; h->d_req_stride = sv.drs;
+    h->t_cap = sv.tcap; h->d_cap = sv.dcap; h->R_part = sv.R_part; h->max_split = sv.max_split;
+    h->R_max = sv.R_max; h->stream = sv.stream;
+  };
+  try {
+    CK(cudaSetDevice(h->device));
+    const bool target = role == SPECDEC_TARGET;
+    if (role != SPECDEC_TARGET && role != SPECDEC_DRAFT) fail(SPECDEC_ERR_INVALID, "unknown role");
+    ModelW &m = target ? h->tgt : h->dft;
+    if (!m.loaded) fail(SPECDEC_ERR_STATE, "weights not loaded");
+    if (!d_tokens || !d_logits) fail(SPECDEC_ERR_INVALID, "null device buffer");
+    const Dims &dm = m.dm;
+    if (S < 1 || S > h->rope_max) fail(SPECDEC_ERR_INVALID, "sequence length out of range");
+    // carve the layout first with a null base to size it
+    const size_t act = h->act_elt;
+    const size_t kv_elt = h->cfg.kv_dtype == SPECDEC_BF16 ? 2 : 4;
+    const int nsplit = std::max(1, std::min(16, (S + 255) / 256));
+    auto layout = [&](ArenaCarver &c, void **ptrs) {
+      ptrs[0] = c.take(static_cast<size_t>(S) * dm.d * act);   // x
+      ptrs[1] = c.take(static_cast<size_t>(S) * dm.d * act);   // x1
+      ptrs[2] = c.take(static_cast<size_t>(S) * dm.d * act);   // hb
+      ptrs[3] = c.take(static_cast<size_t>(S) * dm.d * act);   // qb
+      ptrs[4] = c.take(static_cast<size_t>(S) * dm.d * act);   // att
+      ptrs[5] = c.take(static_cast<size_t>(S) * dm.F * act);   // ffa
+      const size_t kv = static_cast<size_t>(std::max(1, dm.L)) * dm.Hkv * S * dm.D * kv_elt;
+      ptrs[6] = c.take(kv);                                    // K cache
+      ptrs[7] = c.take(kv);                                    // V cache
+      ptrs[8] = c.take(static_cast<size_t>(S) * dm.H * nsplit * (dm.D + 2) * sizeof(float));  // partials
+      ptrs[9] = c.take(S * sizeof(int));                       // row tokens
+      ptrs[10] = c.take(S * sizeof(int));                      // row positions
+      ptrs[11] = c.take(S * sizeof(int));                      // row requests
+      ptrs[12] = c.take(S * sizeof(int));                      // selection
+      ptrs[13] = c.take(sizeof(int));                          // error word
+    };
+    void *ptrs[14];
+    ArenaCarver sizing{nullptr};
+    layout(sizing, ptrs);
+    if (sizing.used > SPECDEC_NOALLOC_SCRATCH_BYTES)
+      fail(SPECDEC_ERR_INVALID, "this forward needs " + std::to_string(sizing.used) +
+                                    " bytes of scratch; the no-allocation path holds at most " +
+                                    std::to_string(static_cast<size_t>(SPECDEC_NOALLOC_SCRATCH_BYTES)));
+    unsigned char *base = nullptr;
+    CK(noalloc_base(h->device, &base));
+    ArenaCarver arena{base};
+    layout(arena, ptrs);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+    h->x = ptrs[0]; h->x1 = ptrs[1]; h->hb = ptrs[2]; h->qb = ptrs[3]; h->att = ptrs[4]; h->ffa = ptrs[5];
+    if (target) { h->tk = ptrs[6]; h->tv = ptrs[7]; } else { h->dk = ptrs[6]; h->dv = ptrs[7]; }
+    h->part = static_cast<float *>(ptrs[8]);
+    h->rtok = static_cast<int *>(ptrs[9]); h->rpos = static_cast<int *>(ptrs[10]);
+    h->rreq = static_cast<int *>(ptrs[11]); h->sel = static_cast<int *>(ptrs[12]);
+    h->st.err = static_cast<int *>(ptrs[13]);
+    const size_t req_stride = static_cast<size_t>(dm.Hkv) * S * dm.D;
+    if (target) { h->t_req_stride = req_stride; h->t_layer_stride = req_stride; h->t_cap = S; }
+    else { h->d_req_stride = req_stride; h->d_layer_stride = req_stride; h->d_cap = S; }
+    h->R_part = S;
+    h->R_max = S;
+    h->max_split = nsplit;
+    h->stream = st;
+    CK(cudaMemsetAsync(h->st.err, 0, sizeof(int), st));
+    plan_prefill_kernel<<<(S + 255) / 256, 256, 0, st>>>(d_tokens, 1, S, 0, S, h->rtok, h->rpos, h->rreq, h->sel);
+    forward_rows(h, target, S, nullptr, S, d_logits);
+    CK(cudaGetLastError());
+    restore();
+  } catch (const SpecErr &e) {
+    restore();
+    h->err = e.msg;
+    return e.code;
+  }
+  return SPECDEC_OK;
+}

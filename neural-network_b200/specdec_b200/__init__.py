@@ -34,7 +34,7 @@ STATUS = {0: "OK", 1: "ERR_INVALID", 2: "ERR_CUDA", 3: "ERR_OOM", 4: "ERR_SEQ_LE
 # Every symbol include/specdec.h declares.
 EXPORTS = ("specdec_create", "specdec_destroy", "specdec_last_error", "specdec_load_params",
            "specdec_generate", "specdec_generate_device", "specdec_stream", "specdec_forward_logits",
-           "specdec_philox_uniforms", "specdec_last_launch_count")
+           "specdec_philox_uniforms", "specdec_last_launch_count", "specdec_forward_logits_noalloc")
 
 
 class SpecDecError(RuntimeError):
@@ -86,6 +86,8 @@ def load_library(path: str = LIB_PATH):
     lib.specdec_stream.argtypes = [C.c_void_p]
     lib.specdec_forward_logits.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p]
     lib.specdec_philox_uniforms.argtypes = [C.c_uint64, C.c_int, C.c_int, C.c_int, C.c_void_p]
+    lib.specdec_forward_logits_noalloc.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p,
+                                                   C.c_void_p]
     lib.specdec_last_launch_count.restype = C.c_int64
     lib.specdec_last_launch_count.argtypes = [C.c_void_p]
     _lib = lib
@@ -186,6 +188,15 @@ class Engine:
         out = np.zeros((t.size, V), np.float32)
         self._check(self._lib.specdec_forward_logits(self.h, role, t.ctypes.data, t.size, out.ctypes.data))
         return out
+
+    def forward_logits_noalloc(self, role: int, d_tokens: int, S: int, d_logits: int, stream: int = 0) -> None:
+        """Device-buffer forward that allocates nothing (see include/specdec.h).
+
+        For callers that may not allocate device memory at call time; all
+        working memory comes from the library's fixed 8 MiB device array, so
+        overlapping calls on one device must be serialised by the caller."""
+        self._check(self._lib.specdec_forward_logits_noalloc(self.h, role, C.c_void_p(d_tokens), S,
+                                                             C.c_void_p(d_logits), C.c_void_p(stream or None)))
 
     @property
     def stream(self) -> int:
