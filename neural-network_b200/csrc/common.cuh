@@ -14,6 +14,7 @@ constexpr int kWarp = 32;
 enum : int {
   kErrSeqLen = 1,     // a cache position reached its capacity
   kErrRngTable = 2,   // the host uniform table ran out of rounds
+  kErrTimeout = 4,    // a bounded wait on an asynchronous copy gave up
 };
 
 __device__ __forceinline__ float to_f32(float v) { return v; }

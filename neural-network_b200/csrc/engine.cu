@@ -13,7 +13,8 @@
 // The whole sequence is captured once per (B, S, sampling mode) into a CUDA
 // graph whose round loop is a device-driven conditional WHILE node, so one
 // generate call is one graph launch with no host round trips.  The same
-// kernels can be launched directly (SPECDEC_NO_GRAPH=1) for debugging.
+// kernels can be launched directly (SPECDEC_NO_GRAPH=1), e.g. for per-kernel
+// profiling (ncu cannot profile kernel nodes of graphs with conditional nodes).
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -22,8 +23,8 @@
 #include <cstdlib>
 #include <cstring>
 #include <map>
-#include <mutex>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <thread>
 #include <tuple>
@@ -105,12 +106,15 @@ __global__ void mt_seed_kernel(uint32_t *mt, int *mt_idx, uint32_t seed, int B) 
   mt_idx[b] = kMtN;
 }
 
-// Last kernel of a round: decides whether the WHILE node runs again.
-__global__ void round_cond_kernel(cudaGraphConditionalHandle hnd, const int *active_count, int *iters,
-                                  int max_iters, int *err) {
+// Last kernel of a round: decides whether the WHILE node runs again and
+// resets the per-round active counter.  The loop is bounded: every active
+// request emits at least one token per round.
+__global__ void round_cond_kernel(cudaGraphConditionalHandle hnd, int *active_count, int *iters, int max_iters,
+                                  int *err) {
   const int it = *iters + 1;
   *iters = it;
   unsigned int more = (*active_count > 0) ? 1u : 0u;
+  *active_count = 0;
   if (more && it >= max_iters) {
     atomicOr(err, kErrSeqLen);
     more = 0u;
@@ -118,7 +122,10 @@ __global__ void round_cond_kernel(cudaGraphConditionalHandle hnd, const int *act
   cudaGraphSetConditional(hnd, more);
 }
 
-__global__ void count_iter_kernel(int *iters) { *iters = *iters + 1; }
+__global__ void count_iter_kernel(int *iters, int *active_count) {
+  *iters = *iters + 1;
+  *active_count = 0;
+}
 
 // Before the WHILE node: enter the loop only if a request is still active.
 __global__ void prime_cond_kernel(cudaGraphConditionalHandle hnd, const int *active, int B) {
@@ -126,6 +133,12 @@ __global__ void prime_cond_kernel(cudaGraphConditionalHandle hnd, const int *act
   for (int b = threadIdx.x; b < B; b += blockDim.x) any |= active[b];
   any = __any_sync(0xffffffffu, any);
   if (threadIdx.x == 0) cudaGraphSetConditional(hnd, any ? 1u : 0u);
+}
+
+// Head-row selection that never changes: row 2b+1 of draft step 0.
+__global__ void fill_odd_kernel(int *sel, int B) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < B) sel[b] = 2 * b + 1;
 }
 
 }  // namespace
@@ -146,12 +159,15 @@ struct specdec_handle {
   float2 *rope = nullptr;
   int rope_max = 0, rope_D = 0;
 
-  // activations
+  // activations: X layer input / residual stream, H projection outputs,
+  // X1 normed rows, A FFN hidden, Q queries, ATT attention out
   int R_max = 0, R_part = 0, max_split = 1;
   size_t act_elt = 4;
-  void *x = nullptr, *x1 = nullptr, *hb = nullptr, *qb = nullptr, *att = nullptr, *ffa = nullptr;
+  void *X = nullptr, *H = nullptr, *X1 = nullptr, *A = nullptr, *Q = nullptr, *ATT = nullptr;
   float *logits = nullptr, *part = nullptr;
-  int *rtok = nullptr, *rpos = nullptr, *rreq = nullptr, *sel = nullptr;
+  int *counters = nullptr, *tile_counters = nullptr;
+  RowPool pool{};
+  int *sel_odd = nullptr, *sel_prefill = nullptr;
 
   // speculative state
   SpecState st{};
@@ -163,7 +179,7 @@ struct specdec_handle {
   int *h_pinned = nullptr;
 
   std::map<GraphKey, GraphEntry> graphs;
-  int64_t launches = 0;        // direct mode: kernels enqueued by the last call
+  int64_t launches = 0;        // direct mode: kernels enqueued by the last call; -1 in graph mode
   int64_t graph_fixed = 0, graph_body = 0, extra_launches = 0;
   bool use_graph = true;
 
@@ -359,236 +375,175 @@ void load_model(specdec_handle *h, int role, ModelW &m, int n, const float *cons
 }
 
 // --- kernel launch helpers ---------------------------------------------------
+template <typename... KArgs, typename... Args>
+void launch(specdec_handle *h, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, Args... args) {
+  kern<<<grid, block, smem, h->stream>>>(static_cast<KArgs>(args)...);
+  CK(cudaGetLastError());
+  ++h->launches;
+}
+
+// K-split: enough warps per column pair that each lane streams one or two
+// weight vectors, while the grid stays within about two waves.
+int pick_ksplit(int N, int R, int K, int E) {
+  const int row_tiles = (R + kRowTile - 1) / kRowTile;
+  int ks = 1;
+  while (ks < 8) {
+    const int pairs = kLinWarps / (2 * ks);
+    const long blocks = static_cast<long>((N + 2 * pairs - 1) / (2 * pairs)) * row_tiles;
+    if (K / E <= 64 * ks || blocks > 2 * 148) break;
+    ks *= 2;
+  }
+  return ks;
+}
+
 template <int EPI>
-void launch_linear(specdec_handle *h, const LinearArgs &a) {
+void launch_linear(specdec_handle *h, LinearArgs a) {
   if (a.R <= 0) return;
-  dim3 grid((a.N + 2 * kLinWarps - 1) / (2 * kLinWarps), (a.R + kRowTile - 1) / kRowTile);
-  dim3 block(32 * kLinWarps);
   const bool bf = act_bf16(h), i8 = w_int8(h);
-  if (i8 && bf) linear_kernel<int8_t, __nv_bfloat16, EPI><<<grid, block, 0, h->stream>>>(a);
-  else if (i8) linear_kernel<int8_t, float, EPI><<<grid, block, 0, h->stream>>>(a);
-  else if (bf) linear_kernel<float, __nv_bfloat16, EPI><<<grid, block, 0, h->stream>>>(a);
-  else linear_kernel<float, float, EPI><<<grid, block, 0, h->stream>>>(a);
-  ++h->launches;
+  a.ksplit = pick_ksplit(a.N, a.R, a.K, i8 ? WVec<int8_t>::E : WVec<float>::E);
+  const int pairs = kLinWarps / a.ksplit;
+  dim3 grid((a.N + 2 * pairs - 1) / (2 * pairs), (a.R + kRowTile - 1) / kRowTile);
+  dim3 block(32 * kLinWarps);
+  if (a.ln_out) {
+    if (a.N > 32 * kLnMaxPerLane) fail(SPECDEC_ERR_UNSUPPORTED, "fused LayerNorm supports rows up to 1024 wide");
+    a.tile_counters = h->tile_counters;
+  }
+  if (i8 && bf) launch(h, linear_kernel<int8_t, __nv_bfloat16, EPI>, grid, block, 0, a);
+  else if (i8) launch(h, linear_kernel<int8_t, float, EPI>, grid, block, 0, a);
+  else if (bf) launch(h, linear_kernel<float, __nv_bfloat16, EPI>, grid, block, 0, a);
+  else launch(h, linear_kernel<float, float, EPI>, grid, block, 0, a);
 }
 
-// Logits always fp32: the head writes through a float view regardless of the
-// activation type (kEpiStore with AT = fp32 output needs its own instantiation).
-template <typename WT, typename AT>
-__global__ void head_kernel(LinearArgs a);
-
-void layernorm(specdec_handle *h, const void *in, int R, int d, const float *g, const float *b, void *out) {
-  if (R <= 0) return;
-  if (act_bf16(h))
-    layernorm_kernel<__nv_bfloat16><<<R, 128, 0, h->stream>>>(static_cast<const __nv_bfloat16 *>(in), d, R, d, g, b,
-                                                              static_cast<__nv_bfloat16 *>(out), d);
-  else
-    layernorm_kernel<float><<<R, 128, 0, h->stream>>>(static_cast<const float *>(in), d, R, d, g, b,
-                                                      static_cast<float *>(out), d);
-  ++h->launches;
+template <typename AT, typename KT, int D>
+void set_attn_attr() {
+  CK(cudaFuncSetAttribute(attention_kernel<AT, KT, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          attn_smem_bytes<KT, D>()));
+}
+template <typename AT, typename KT>
+void set_attn_attrs() {
+  set_attn_attr<AT, KT, 4>();
+  set_attn_attr<AT, KT, 8>();
+  set_attn_attr<AT, KT, 16>();
+  set_attn_attr<AT, KT, 32>();
+  set_attn_attr<AT, KT, 64>();
+  set_attn_attr<AT, KT, 128>();
 }
 
-void attention(specdec_handle *h, const Dims &dm, int R, const void *kc, const void *vc, size_t req_stride, int S_cap) {
+template <typename AT, typename KT>
+void launch_attention_t(specdec_handle *h, const AttnArgs &a, int D, int ngroups) {
+  dim3 grid(ngroups * ((a.Q + kAttnQT - 1) / kAttnQT), a.H, a.nsplit);
+  dim3 block(kAttnThreads);
+#define ATTN_CASE(DD) \
+  case DD: launch(h, attention_kernel<AT, KT, DD>, grid, block, static_cast<size_t>(attn_smem_bytes<KT, DD>()), a); break;
+  switch (D) {
+    ATTN_CASE(4)
+    ATTN_CASE(8)
+    ATTN_CASE(16)
+    ATTN_CASE(32)
+    ATTN_CASE(64)
+    ATTN_CASE(128)
+    default: fail(SPECDEC_ERR_UNSUPPORTED, "head dimension must be 4, 8, 16, 32, 64 or 128");
+  }
+#undef ATTN_CASE
+}
+
+// Attention over a row batch whose rows form groups of Q consecutive rows of
+// one request each.  Contexts are split over blocks only when they are long.
+void attention(specdec_handle *h, const Dims &dm, RowsView rows, int R, int Q, const void *kc, const void *vc,
+               size_t req_stride, int S_cap) {
   if (R <= 0) return;
-  RowsView rows{h->rtok, h->rpos, h->rreq};
-  int nsplit = 1;
-  if (R <= h->R_part) nsplit = std::max(1, std::min(h->max_split, (S_cap + 255) / 256));
-  const int chunk = (S_cap + nsplit - 1) / nsplit;
-  dim3 grid(R, dm.H, nsplit);
-  const size_t smem = (dm.D + 2 * kAttnThreads) * sizeof(float);
+  AttnArgs a{};
+  a.q = h->Q; a.ldq = dm.d; a.rows = rows; a.R = R; a.Q = Q;
+  a.kc = kc; a.vc = vc; a.kv_req_stride = req_stride; a.S_cap = S_cap; a.H = dm.H; a.Hkv = dm.Hkv;
+  a.nsplit = 1;
+  if (R <= h->R_part) a.nsplit = std::max(1, std::min(h->max_split, (S_cap + 1023) / 1024));
+  a.chunk = (S_cap + a.nsplit - 1) / a.nsplit;
+  a.out = h->ATT; a.ldo = dm.d; a.part = h->part; a.counters = h->counters; a.err = h->st.err;
+  const int ngroups = (R + Q - 1) / Q;
   const bool bf = act_bf16(h);
   const bool kvbf = h->cfg.kv_dtype == SPECDEC_BF16;
-#define ATTN(AT, KT)                                                                                          \
-  attention_kernel<AT, KT><<<grid, kAttnThreads, smem, h->stream>>>(                                        \
-      static_cast<const AT *>(h->qb), dm.d, rows, R, static_cast<const KT *>(kc), static_cast<const KT *>(vc), \
-      req_stride, S_cap, dm.H, dm.Hkv, dm.D, chunk, static_cast<AT *>(h->att), dm.d, h->part)
-  if (bf && kvbf) ATTN(__nv_bfloat16, __nv_bfloat16);
-  else if (bf) ATTN(__nv_bfloat16, float);
-  else if (kvbf) ATTN(float, __nv_bfloat16);
-  else ATTN(float, float);
-#undef ATTN
-  ++h->launches;
-  if (nsplit > 1) {
-    dim3 g2(R, dm.H);
-    if (bf) attn_combine_kernel<__nv_bfloat16><<<g2, 128, 0, h->stream>>>(h->part, rows, R, dm.H, dm.D, nsplit,
-                                                                          static_cast<__nv_bfloat16 *>(h->att), dm.d);
-    else attn_combine_kernel<float><<<g2, 128, 0, h->stream>>>(h->part, rows, R, dm.H, dm.D, nsplit,
-                                                               static_cast<float *>(h->att), dm.d);
-    ++h->launches;
-  }
+  if (bf && kvbf) launch_attention_t<__nv_bfloat16, __nv_bfloat16>(h, a, dm.D, ngroups);
+  else if (bf) launch_attention_t<__nv_bfloat16, float>(h, a, dm.D, ngroups);
+  else if (kvbf) launch_attention_t<float, __nv_bfloat16>(h, a, dm.D, ngroups);
+  else launch_attention_t<float, float>(h, a, dm.D, ngroups);
 }
 
-// One forward pass of model m over the current row batch (R rows).  When
-// `logits` is set, the lm_head runs over the rows listed in `sel` (n_sel of
-// them, or all R rows when sel is null).
-void forward_rows(specdec_handle *h, bool target, int R, const int *sel, int n_sel, float *logits) {
+// One forward pass of model m over the row batch at pool offset `off`
+// (R rows in groups of Q rows per request).  When `logits` is set, the
+// lm_head runs over the rows listed in `sel` (n_sel of them; all R rows when
+// sel is null) and writes fp32 logits.
+//
+// Reference arch, per layer (src/nn/layer.cpp:1097-1114, post-LN):
+//   QKV    X -> Q, K/V cache (RoPE, append)
+//   ATT    attention -> ATT
+//   OPROJ  ATT.Wo + bo + X -> H, then X1 = LN1(H) by the tile's last block
+//   GATEUP silu(X1.Wg + bg) * (X1.Wu + bu) -> A
+//   DOWN   A.Wd + bd + X1 -> H, then X = LN2(H)
+// cfg arch (pre-LN): the embedding writes X and X1 = LN1(X); QKV reads X1;
+// OPROJ -> H = X + attn, X1 = LN2(H); FC1 GELU -> A; FC2 -> X = H + ffn,
+// X1 = the next layer's LN1(X) or the final LN; the head reads X1.
+void forward_rows(specdec_handle *h, bool target, int off, int R, int Q, const int *sel, int n_sel, float *logits) {
   ModelW &m = target ? h->tgt : h->dft;
   const Dims &dm = m.dm;
   const int d = dm.d;
-  RowsView rows{h->rtok, h->rpos, h->rreq};
+  RowsView rows{h->pool.tok + off, h->pool.pos + off, h->pool.req + off};
   void *kc = target ? h->tk : h->dk;
   void *vc = target ? h->tv : h->dv;
   const size_t lstride = target ? h->t_layer_stride : h->d_layer_stride;
   const size_t rstride = target ? h->t_req_stride : h->d_req_stride;
   const int S_cap = target ? h->t_cap : h->d_cap;
   const size_t kv_elt = h->cfg.kv_dtype == SPECDEC_BF16 ? 2 : 4;
-
-  if (act_bf16(h))
-    embed_kernel<__nv_bfloat16><<<R, 128, 0, h->stream>>>(rows, R, m.emb, m.pos, dm.V, d, dm.max_seq,
-                                                          static_cast<__nv_bfloat16 *>(h->x));
-  else
-    embed_kernel<float><<<R, 128, 0, h->stream>>>(rows, R, m.emb, m.pos, dm.V, d, dm.max_seq, static_cast<float *>(h->x));
-  ++h->launches;
-
   const bool ref = dm.arch == SPECDEC_ARCH_REF;
+
+  const float *lg0 = ref ? nullptr : m.layers[0].g1, *lb0 = ref ? nullptr : m.layers[0].b1;
+  if (act_bf16(h))
+    launch(h, embed_kernel<__nv_bfloat16>, dim3(R), dim3(128), 0, rows, R, m.emb, m.pos, d, dm.max_seq,
+           static_cast<__nv_bfloat16 *>(h->X), lg0, lb0, static_cast<__nv_bfloat16 *>(h->X1));
+  else
+    launch(h, embed_kernel<float>, dim3(R), dim3(128), 0, rows, R, m.emb, m.pos, d, dm.max_seq,
+           static_cast<float *>(h->X), lg0, lb0, static_cast<float *>(h->X1));
+
   for (int l = 0; l < dm.L; ++l) {
     const LayerW &L = m.layers[l];
     void *kcl = static_cast<char *>(kc) + l * lstride * kv_elt;
     void *vcl = static_cast<char *>(vc) + l * lstride * kv_elt;
-    const void *ain = h->x;
-    if (!ref) {
-      layernorm(h, h->x, R, d, L.g1, L.b1, h->x1);
-      ain = h->x1;
-    }
-    // QKV + RoPE + KV append
     LinearArgs a{};
-    a.x = ain; a.ldx = d; a.R = R; a.W = L.wqkv; a.scale = L.sqkv; a.bias = L.bqkv;
-    a.N = d + 2 * dm.kvd; a.K = d; a.out = h->qb; a.ldo = d; a.rows = rows;
+    a.x = ref ? h->X : h->X1; a.ldx = d; a.R = R; a.W = L.wqkv; a.scale = L.sqkv; a.bias = L.bqkv;
+    a.N = d + 2 * dm.kvd; a.K = d; a.out = h->Q; a.ldo = d; a.rows = rows;
     a.qkv = QKVArgs{d, dm.kvd, dm.D, h->rope, h->rope_max, kcl, vcl, rstride, S_cap,
                     h->cfg.kv_dtype == SPECDEC_BF16 ? 1 : 0, h->st.err};
     launch_linear<kEpiQKV>(h, a);
-    attention(h, dm, R, kcl, vcl, rstride, S_cap);
-    // out projection + residual
+    attention(h, dm, rows, R, Q, kcl, vcl, rstride, S_cap);
     LinearArgs o{};
-    o.x = h->att; o.ldx = d; o.R = R; o.W = L.wo; o.scale = L.so; o.bias = L.bo; o.N = d; o.K = d;
-    o.out = h->hb; o.ldo = d; o.resid = h->x; o.ldr = d;
+    o.x = h->ATT; o.ldx = d; o.R = R; o.W = L.wo; o.scale = L.so; o.bias = L.bo; o.N = d; o.K = d;
+    o.out = h->H; o.ldo = d; o.resid = h->X; o.ldr = d; o.rows = rows;
+    o.ln_g = ref ? L.g1 : L.g2; o.ln_b = ref ? L.b1 : L.b2; o.ln_out = h->X1;
     launch_linear<kEpiResid>(h, o);
+    LinearArgs g{};
+    g.x = h->X1; g.ldx = d; g.R = R; g.W = L.wgu; g.scale = L.sgu; g.bias = L.bgu; g.K = d; g.rows = rows;
+    g.out = h->A; g.ldo = dm.F; g.N = ref ? 2 * dm.F : dm.F;
+    if (ref) launch_linear<kEpiSwiGLU>(h, g);
+    else launch_linear<kEpiGelu>(h, g);
+    LinearArgs dn{};
+    dn.x = h->A; dn.ldx = dm.F; dn.R = R; dn.W = L.wd; dn.scale = L.sd; dn.bias = L.bd; dn.N = d; dn.K = dm.F;
+    dn.rows = rows; dn.ldo = d; dn.ldr = d;
     if (ref) {
-      // x1 = norm1(x + attn); x = norm2(x1 + ffn(x1))  (src/nn/layer.cpp:1097-1114)
-      layernorm(h, h->hb, R, d, L.g1, L.b1, h->x1);
-      LinearArgs g{};
-      g.x = h->x1; g.ldx = d; g.R = R; g.W = L.wgu; g.scale = L.sgu; g.bias = L.bgu; g.N = 2 * dm.F; g.K = d;
-      g.out = h->ffa; g.ldo = dm.F;
-      launch_linear<kEpiSwiGLU>(h, g);
-      LinearArgs dn{};
-      dn.x = h->ffa; dn.ldx = dm.F; dn.R = R; dn.W = L.wd; dn.scale = L.sd; dn.bias = L.bd; dn.N = d; dn.K = dm.F;
-      dn.out = h->hb; dn.ldo = d; dn.resid = h->x1; dn.ldr = d;
-      launch_linear<kEpiResid>(h, dn);
-      layernorm(h, h->hb, R, d, L.g2, L.b2, h->x);
+      dn.out = h->H; dn.resid = h->X1; dn.ln_g = L.g2; dn.ln_b = L.b2; dn.ln_out = h->X;
     } else {
-      // pre-LN: x = x + attn; x = x + fc2(gelu(fc1(LN2(x))))
-      std::swap(h->x, h->hb);
-      layernorm(h, h->x, R, d, L.g2, L.b2, h->x1);
-      LinearArgs f1{};
-      f1.x = h->x1; f1.ldx = d; f1.R = R; f1.W = L.wgu; f1.scale = L.sgu; f1.bias = L.bgu; f1.N = dm.F; f1.K = d;
-      f1.out = h->ffa; f1.ldo = dm.F;
-      launch_linear<kEpiGelu>(h, f1);
-      LinearArgs f2{};
-      f2.x = h->ffa; f2.ldx = dm.F; f2.R = R; f2.W = L.wd; f2.scale = L.sd; f2.bias = L.bd; f2.N = d; f2.K = dm.F;
-      f2.out = h->hb; f2.ldo = d; f2.resid = h->x; f2.ldr = d;
-      launch_linear<kEpiResid>(h, f2);
-      std::swap(h->x, h->hb);
+      dn.out = h->X; dn.resid = h->H; dn.ln_out = h->X1;
+      if (l + 1 < dm.L) { dn.ln_g = m.layers[l + 1].g1; dn.ln_b = m.layers[l + 1].b1; }
+      else { dn.ln_g = m.gf; dn.ln_b = m.bfin; }
     }
+    launch_linear<kEpiResid>(h, dn);
   }
   if (!logits) return;
-  const void *hin = h->x;
-  if (!ref) {
-    layernorm(h, h->x, R, d, m.gf, m.bfin, h->x1);
-    hin = h->x1;
-  }
   LinearArgs hd{};
-  hd.x = hin; hd.ldx = d; hd.in_rows = sel; hd.R = sel ? n_sel : R; hd.W = m.whead; hd.scale = m.shead; hd.bias = m.bhead;
-  hd.N = dm.V; hd.K = d; hd.out = logits; hd.ldo = dm.V;
-  {
-    dim3 grid((hd.N + 2 * kLinWarps - 1) / (2 * kLinWarps), (hd.R + kRowTile - 1) / kRowTile);
-    dim3 block(32 * kLinWarps);
-    const bool bf = act_bf16(h), i8 = w_int8(h);
-    if (i8 && bf) head_kernel<int8_t, __nv_bfloat16><<<grid, block, 0, h->stream>>>(hd);
-    else if (i8) head_kernel<int8_t, float><<<grid, block, 0, h->stream>>>(hd);
-    else if (bf) head_kernel<float, __nv_bfloat16><<<grid, block, 0, h->stream>>>(hd);
-    else head_kernel<float, float><<<grid, block, 0, h->stream>>>(hd);
-    ++h->launches;
-  }
+  hd.x = ref ? h->X : h->X1; hd.ldx = d; hd.in_rows = sel; hd.R = sel ? n_sel : R;
+  hd.W = m.whead; hd.scale = m.shead; hd.bias = m.bhead;
+  hd.N = dm.V; hd.K = d; hd.out = logits; hd.ldo = dm.V; hd.out_f32 = 1; hd.rows = rows;
+  launch_linear<kEpiStore>(h, hd);
 }
 
-}  // namespace
-
-// The lm_head reads activations of type AT but always writes fp32 logits.
-namespace {
-template <typename WT, typename AT>
-__global__ void __launch_bounds__(32 * kLinWarps) head_kernel(LinearArgs a) {
-  constexpr int E = WVec<WT>::E;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int n0 = (blockIdx.x * kLinWarps + warp) * 2;
-  const int r0 = blockIdx.y * kRowTile;
-  if (n0 >= a.N) return;
-  const bool has1 = (n0 + 1) < a.N;
-  const int nrows = min(kRowTile, a.R - r0);
-  const WT *w0 = static_cast<const WT *>(a.W) + static_cast<size_t>(n0) * a.K;
-  const WT *w1 = has1 ? w0 + a.K : w0;
-  const AT *xrow[kRowTile];
-#pragma unroll
-  for (int i = 0; i < kRowTile; ++i) {
-    int lr = r0 + (i < nrows ? i : 0);
-    int pr = a.in_rows ? a.in_rows[lr] : lr;
-    xrow[i] = static_cast<const AT *>(a.x) + static_cast<size_t>(pr) * a.ldx;
-  }
-  float acc0[kRowTile], acc1[kRowTile];
-#pragma unroll
-  for (int i = 0; i < kRowTile; ++i) acc0[i] = acc1[i] = 0.f;
-  const bool vec_ok = ((a.K * static_cast<int>(sizeof(WT))) % 16 == 0) && ((a.ldx * static_cast<int>(sizeof(AT))) % 16 == 0);
-  const int kvec = vec_ok ? a.K / E : 0;
-  for (int v = lane; v < kvec; v += 32) {
-    float wa[E], wb[E];
-    if constexpr (sizeof(WT) == 4) {
-      unpack_w(__ldg(reinterpret_cast<const float4 *>(w0) + v), wa);
-      unpack_w(__ldg(reinterpret_cast<const float4 *>(w1) + v), wb);
-    } else {
-      unpack_w(__ldg(reinterpret_cast<const int4 *>(w0) + v), wa);
-      unpack_w(__ldg(reinterpret_cast<const int4 *>(w1) + v), wb);
-    }
-#pragma unroll
-    for (int i = 0; i < kRowTile; ++i) {
-      if (i < nrows) {
-        float xv[E];
-        load_x<AT, E>(xrow[i] + v * E, xv);
-        float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-        for (int e = 0; e < E; ++e) {
-          s0 = fmaf(xv[e], wa[e], s0);
-          s1 = fmaf(xv[e], wb[e], s1);
-        }
-        acc0[i] += s0;
-        acc1[i] += s1;
-      }
-    }
-  }
-  for (int k = kvec * E + lane; k < a.K; k += 32) {
-    const float wa = static_cast<float>(w0[k]), wb = static_cast<float>(w1[k]);
-#pragma unroll
-    for (int i = 0; i < kRowTile; ++i)
-      if (i < nrows) {
-        const float xv = to_f32(xrow[i][k]);
-        acc0[i] = fmaf(xv, wa, acc0[i]);
-        acc1[i] = fmaf(xv, wb, acc1[i]);
-      }
-  }
-#pragma unroll
-  for (int i = 0; i < kRowTile; ++i) {
-    acc0[i] = warp_sum(acc0[i]);
-    acc1[i] = warp_sum(acc1[i]);
-  }
-#pragma unroll
-  for (int i = 0; i < kRowTile; ++i) {
-    if (lane == i && i < nrows) {
-      float v0 = acc0[i], v1 = acc1[i];
-      if (a.scale) { v0 *= a.scale[n0]; if (has1) v1 *= a.scale[n0 + 1]; }
-      float *o = static_cast<float *>(a.out) + static_cast<size_t>(r0 + i) * a.ldo;
-      o[n0] = v0 + a.bias[n0];
-      if (has1) o[n0 + 1] = v1 + a.bias[n0 + 1];
-    }
-  }
-}
 }  // namespace
 
 namespace {
@@ -619,33 +574,25 @@ void validate_gen(specdec_handle *h, const specdec_gen_params *p, int B, int S) 
     fail(SPECDEC_ERR_INVALID, "unknown draft_catchup");
 }
 
+int samp_threads(const specdec_handle *h) { return h->tgt.dm.V <= 4096 ? 512 : kSampThreads; }
+size_t samp_smem(const specdec_handle *h) { return static_cast<size_t>(h->tgt.dm.V) * sizeof(float); }
+
 // Enqueues one full round (everything between two accept kernels).
 void enqueue_round(specdec_handle *h) {
   SpecState &st = h->st;
   const int B = st.B, k = st.k;
-  const int tpb = 256;
-  const int nb = (B + tpb - 1) / tpb;
-  // draft step 0: [catch-up, last] per request
-  plan_draft0_kernel<<<nb, tpb, 0, h->stream>>>(st, h->rtok, h->rpos, h->rreq, h->sel);
-  ++h->launches;
-  forward_rows(h, false, 2 * B, h->sel, B, h->logits);
-  draft_sample_kernel<<<B, kSampThreads, 0, h->stream>>>(st, 0, h->logits);
-  ++h->launches;
+  const dim3 sb(samp_threads(h));
+  forward_rows(h, false, st.rows.off_step0, 2 * B, 2, h->sel_odd, B, h->logits);
+  launch(h, draft_sample_kernel, dim3(B), sb, samp_smem(h), st, 0, static_cast<const float *>(h->logits));
   for (int j = 1; j < k; ++j) {
-    plan_draft_kernel<<<nb, tpb, 0, h->stream>>>(st, j, h->rtok, h->rpos, h->rreq, h->sel);
-    ++h->launches;
-    forward_rows(h, false, B, nullptr, B, h->logits);
-    draft_sample_kernel<<<B, kSampThreads, 0, h->stream>>>(st, j, h->logits);
-    ++h->launches;
+    forward_rows(h, false, st.rows.off_step1 + (j - 1) * B, B, 1, nullptr, B, h->logits);
+    launch(h, draft_sample_kernel, dim3(B), sb, samp_smem(h), st, j, static_cast<const float *>(h->logits));
   }
-  plan_verify_kernel<<<nb, tpb, 0, h->stream>>>(st, h->rtok, h->rpos, h->rreq);
-  ++h->launches;
-  forward_rows(h, true, B * (k + 1), nullptr, B * (k + 1), h->logits);
-  accept_kernel<<<B, kSampThreads, 0, h->stream>>>(st, h->logits);
-  ++h->launches;
+  forward_rows(h, true, st.rows.off_verify, B * (k + 1), k + 1, nullptr, B * (k + 1), h->logits);
+  launch(h, accept_kernel, dim3(B), sb, samp_smem(h), st, static_cast<const float *>(h->logits));
 }
 
-void setup_state(specdec_handle *h, const specdec_gen_params *p, int B, int S, int *d_out_tokens) {
+void setup_state(specdec_handle *h, const specdec_gen_params *p, int B, int S) {
   SpecState &st = h->st;
   st.B = B;
   st.k = p->lookahead;
@@ -663,39 +610,35 @@ void setup_state(specdec_handle *h, const specdec_gen_params *p, int B, int S, i
   st.u_slots = 2 * p->lookahead + 1;
   st.u_rounds = p->uniform_rounds;
   st.uniforms = h->d_uniforms;
-  (void)d_out_tokens;
+  // row regions: [prefill R_max][step0 2B][steps 1..k-1: B each][verify B(k+1)]
+  st.rows = h->pool;
+  st.rows.off_step0 = h->R_max;
+  st.rows.off_step1 = h->R_max + 2 * B;
+  st.rows.off_verify = h->R_max + 2 * B + (st.kmax - 1) * B;
 }
 
-}  // namespace
-
 // Everything up to and including the first token (src/nn/layer.cpp:1396-1512).
-static void enqueue_prologue(specdec_handle *h, int B, int S, uint32_t seed) {
+void enqueue_prologue(specdec_handle *h, int B, int S, uint32_t seed) {
   SpecState &st = h->st;
-  init_state_kernel<<<B, 128, 0, h->stream>>>(st, h->d_prompts, S);
-  ++h->launches;
-  if (!st.greedy && st.rng_mode == 0) {
-    mt_seed_kernel<<<(B + 127) / 128, 128, 0, h->stream>>>(st.mt, st.mt_idx, seed, B);
-    ++h->launches;
-  }
+  launch(h, init_state_kernel, dim3(B), dim3(128), 0, st, static_cast<const int *>(h->d_prompts), S);
+  if (!st.greedy && st.rng_mode == 0) launch(h, mt_seed_kernel, dim3((B + 127) / 128), dim3(128), 0, st.mt, st.mt_idx, seed, B);
   const int chunk = std::max(1, std::min(S, h->R_max / B));
   for (int pass = 0; pass < 2; ++pass) {
     const bool target = pass == 0;
     for (int c0 = 0; c0 < S; c0 += chunk) {
       const int clen = std::min(chunk, S - c0);
       const int R = B * clen;
-      plan_prefill_kernel<<<(R + 255) / 256, 256, 0, h->stream>>>(h->d_prompts, B, S, c0, clen, h->rtok, h->rpos,
-                                                                 h->rreq, h->sel);
-      ++h->launches;
       const bool last = c0 + clen >= S;
+      launch(h, plan_prefill_kernel, dim3((R + 255) / 256), dim3(256), 0, static_cast<const int *>(h->d_prompts), B, S,
+             c0, clen, h->tgt.dm.V, h->pool.tok, h->pool.pos, h->pool.req, (target && last) ? h->sel_prefill : nullptr);
       // the draft's prefill logits are discarded (src/nn/layer.cpp:1408)
-      forward_rows(h, target, R, h->sel, B, (target && last) ? h->logits : nullptr);
+      forward_rows(h, target, 0, R, clen, h->sel_prefill, B, (target && last) ? h->logits : nullptr);
     }
   }
-  first_token_kernel<<<B, kSampThreads, 0, h->stream>>>(st, h->logits);
-  ++h->launches;
+  launch(h, first_token_kernel, dim3(B), dim3(samp_threads(h)), samp_smem(h), st, static_cast<const float *>(h->logits));
 }
 
-static void destroy_graphs(specdec_handle *h) {
+void destroy_graphs(specdec_handle *h) {
   for (auto &kv : h->graphs) {
     if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
     if (kv.second.graph) cudaGraphDestroy(kv.second.graph);
@@ -704,16 +647,21 @@ static void destroy_graphs(specdec_handle *h) {
 }
 
 // Builds prologue -> WHILE(active) { round } as one executable graph.
-static GraphEntry build_graph(specdec_handle *h, int B, int S, uint32_t seed, int max_iters) {
+GraphEntry build_graph(specdec_handle *h, int B, int S, uint32_t seed, int max_iters) {
   GraphEntry ge;
   CK(cudaGraphCreate(&ge.graph, 0));
   cudaGraphConditionalHandle hnd;
   CK(cudaGraphConditionalHandleCreate(&hnd, ge.graph, 0, cudaGraphCondAssignDefault));
   CK(cudaStreamBeginCaptureToGraph(h->stream, ge.graph, nullptr, nullptr, 0, cudaStreamCaptureModeThreadLocal));
   h->launches = 0;
-  enqueue_prologue(h, B, S, seed);
-  prime_cond_kernel<<<1, 32, 0, h->stream>>>(hnd, h->st.active, B);
-  ++h->launches;
+  try {
+    enqueue_prologue(h, B, S, seed);
+    launch(h, prime_cond_kernel, dim3(1), dim3(32), 0, hnd, static_cast<const int *>(h->st.active), B);
+  } catch (...) {
+    cudaGraph_t g;
+    cudaStreamEndCapture(h->stream, &g);
+    throw;
+  }
   ge.fixed_kernels = h->launches;
   CK(cudaStreamEndCapture(h->stream, &ge.graph));
   size_t nn = 0;
@@ -736,9 +684,14 @@ static GraphEntry build_graph(specdec_handle *h, int B, int S, uint32_t seed, in
   cudaGraph_t body = cp.conditional.phGraph_out[0];
   CK(cudaStreamBeginCaptureToGraph(h->stream, body, nullptr, nullptr, 0, cudaStreamCaptureModeThreadLocal));
   h->launches = 0;
-  enqueue_round(h);
-  round_cond_kernel<<<1, 1, 0, h->stream>>>(hnd, h->st.active_count, h->d_iters, max_iters, h->st.err);
-  ++h->launches;
+  try {
+    enqueue_round(h);
+    launch(h, round_cond_kernel, dim3(1), dim3(1), 0, hnd, h->st.active_count, h->d_iters, max_iters, h->st.err);
+  } catch (...) {
+    cudaGraph_t g;
+    cudaStreamEndCapture(h->stream, &g);
+    throw;
+  }
   ge.body_kernels = h->launches;
   CK(cudaStreamEndCapture(h->stream, &body));
   CK(cudaGraphInstantiate(&ge.exec, ge.graph, 0));
@@ -747,11 +700,11 @@ static GraphEntry build_graph(specdec_handle *h, int B, int S, uint32_t seed, in
 
 // d_prompts may be any device buffer; it is staged into the handle's prompt
 // buffer so captured graphs stay valid across calls.
-static int generate_impl(specdec_handle *h, const specdec_gen_params *p, const int32_t *d_prompts, int B, int S,
-                         int32_t *d_out, int64_t *d_stats_out, bool uniforms_on_host) {
+int generate_impl(specdec_handle *h, const specdec_gen_params *p, const int32_t *d_prompts, int B, int S, int32_t *d_out,
+                  int64_t *d_stats_out) {
   validate_gen(h, p, B, S);
   SpecState &st = h->st;
-  setup_state(h, p, B, S, d_out);
+  setup_state(h, p, B, S);
   if (d_prompts != h->d_prompts)
     CK(cudaMemcpyAsync(h->d_prompts, d_prompts, static_cast<size_t>(B) * S * sizeof(int), cudaMemcpyDeviceToDevice,
                        h->stream));
@@ -767,12 +720,11 @@ static int generate_impl(specdec_handle *h, const specdec_gen_params *p, const i
       h->uniforms_cap = n;
     }
     st.uniforms = h->d_uniforms;
-    CK(cudaMemcpyAsync(h->d_uniforms, p->uniforms, n * sizeof(float),
-                       cudaMemcpyDefault, h->stream));
+    CK(cudaMemcpyAsync(h->d_uniforms, p->uniforms, n * sizeof(float), cudaMemcpyDefault, h->stream));
   }
   CK(cudaMemsetAsync(st.err, 0, sizeof(int), h->stream));
   CK(cudaMemsetAsync(h->d_iters, 0, sizeof(int), h->stream));
-  // every active request emits at least one token per round
+  CK(cudaMemsetAsync(st.active_count, 0, sizeof(int), h->stream));
   const int max_iters = std::max(2, p->max_new_tokens + 2);
 
   if (h->use_graph) {
@@ -783,7 +735,6 @@ static int generate_impl(specdec_handle *h, const specdec_gen_params *p, const i
     CK(cudaGraphLaunch(it->second.exec, h->stream));
     h->graph_fixed = it->second.fixed_kernels;
     h->graph_body = it->second.body_kernels;
-    h->launches = -1;  // resolved from the iteration count when read
   } else {
     h->launches = 0;
     enqueue_prologue(h, B, S, p->seed);
@@ -795,15 +746,18 @@ static int generate_impl(specdec_handle *h, const specdec_gen_params *p, const i
       for (int v : act) n_act += v;
       if (n_act == 0) break;
       enqueue_round(h);
-      count_iter_kernel<<<1, 1, 0, h->stream>>>(h->d_iters);
-      ++h->launches;
+      launch(h, count_iter_kernel, dim3(1), dim3(1), 0, h->d_iters, st.active_count);
     }
   }
-  finalize_kernel<<<B, 128, 0, h->stream>>>(st, d_out, reinterpret_cast<long long *>(d_stats_out));
+  const int64_t direct = h->launches;
+  launch(h, finalize_kernel, dim3(B), dim3(128), 0, st, static_cast<int *>(d_out),
+         reinterpret_cast<long long *>(d_stats_out));
   h->extra_launches = 1;
-  if (h->launches >= 0) h->launches += 1;
+  h->launches = h->use_graph ? -1 : direct + 1;
   return SPECDEC_OK;
 }
+
+}  // namespace
 
 // ---------------------------------------------------------------------------
 extern "C" {
@@ -826,12 +780,13 @@ int specdec_create(const specdec_config *cfg, int device, specdec_handle **out) 
       const int nl = cfg->draft.n_layers;
       dcfg = cfg->target;
       dcfg.n_layers = nl;
-      if (nl < 0 || nl > cfg->target.n_layers) fail(SPECDEC_ERR_INVALID, "draft layers exceed target layers");
+      if (nl < 1 || nl > cfg->target.n_layers) fail(SPECDEC_ERR_INVALID, "draft layers must be in [1, target layers]");
     }
     Dims dd = make_dims(dcfg);
     check_dims(dd, "draft");
     if (dd.V != td.V) fail(SPECDEC_ERR_INVALID, "target and draft vocab differ");
     if (dd.arch != td.arch) fail(SPECDEC_ERR_INVALID, "target and draft arch differ");
+    if (td.L < 1 || dd.L < 1) fail(SPECDEC_ERR_INVALID, "models need at least one layer");
     if (cfg->weight_dtype != SPECDEC_F32 && cfg->weight_dtype != SPECDEC_INT8)
       fail(SPECDEC_ERR_INVALID, "weight_dtype must be F32 or INT8");
     if (cfg->act_dtype != SPECDEC_F32 && cfg->act_dtype != SPECDEC_BF16) fail(SPECDEC_ERR_INVALID, "bad act_dtype");
@@ -839,10 +794,21 @@ int specdec_create(const specdec_config *cfg, int device, specdec_handle **out) 
     if (cfg->kv_dtype != SPECDEC_F32 && cfg->kv_dtype != SPECDEC_BF16) fail(SPECDEC_ERR_INVALID, "bad kv_dtype");
     if (cfg->max_batch < 1 || cfg->max_lookahead < 1 || cfg->max_lookahead > 32 || cfg->max_prompt_len < 1)
       fail(SPECDEC_ERR_INVALID, "max_batch / max_lookahead / max_prompt_len out of range");
+    if (td.V > 51200) fail(SPECDEC_ERR_UNSUPPORTED, "vocabularies above 51200 entries are not supported");
     h->tgt.dm = td;
     h->dft.dm = dd;
     CK(cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking));
     h->use_graph = std::getenv("SPECDEC_NO_GRAPH") == nullptr;
+    set_attn_attrs<float, float>();
+    set_attn_attrs<float, __nv_bfloat16>();
+    set_attn_attrs<__nv_bfloat16, float>();
+    set_attn_attrs<__nv_bfloat16, __nv_bfloat16>();
+    {
+      const int vs = td.V * static_cast<int>(sizeof(float));
+      CK(cudaFuncSetAttribute(first_token_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, vs));
+      CK(cudaFuncSetAttribute(draft_sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, vs));
+      CK(cudaFuncSetAttribute(accept_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, vs));
+    }
 
     const int B = cfg->max_batch, k = cfg->max_lookahead;
     const size_t kv_elt = cfg->kv_dtype == SPECDEC_BF16 ? 2 : 4;
@@ -853,10 +819,10 @@ int specdec_create(const specdec_config *cfg, int device, specdec_handle **out) 
     h->d_req_stride = static_cast<size_t>(dd.Hkv) * h->d_cap * dd.D;
     h->t_layer_stride = h->t_req_stride * B;
     h->d_layer_stride = h->d_req_stride * B;
-    h->tk = h->dalloc(h->t_layer_stride * std::max(1, td.L) * kv_elt);
-    h->tv = h->dalloc(h->t_layer_stride * std::max(1, td.L) * kv_elt);
-    h->dk = h->dalloc(h->d_layer_stride * std::max(1, dd.L) * kv_elt);
-    h->dv = h->dalloc(h->d_layer_stride * std::max(1, dd.L) * kv_elt);
+    h->tk = h->dalloc(h->t_layer_stride * td.L * kv_elt);
+    h->tv = h->dalloc(h->t_layer_stride * td.L * kv_elt);
+    h->dk = h->dalloc(h->d_layer_stride * dd.L * kv_elt);
+    h->dv = h->dalloc(h->d_layer_stride * dd.L * kv_elt);
     // RoPE table, computed with the reference's float formula
     // (src/core/tensor.cpp:1147-1152): theta = pow(10000, -2j/D), omega = m*theta.
     h->rope_max = std::max(td.max_seq, dd.max_seq);
@@ -879,40 +845,53 @@ int specdec_create(const specdec_config *cfg, int device, specdec_handle **out) 
     h->R_part = R_round;
     h->max_split = 16;
     h->act_elt = act_bf16(h.get()) ? 2 : 4;
-    const int dmax = std::max(td.d, dd.d), Fmax = std::max(td.F, dd.F);
+    const int dmax = std::max(td.d, dd.d), Fmax = std::max(td.F, dd.F), Hmax = std::max(td.H, dd.H);
     const size_t rowb = static_cast<size_t>(h->R_max) * dmax * h->act_elt;
-    h->x = h->dalloc(rowb);
-    h->x1 = h->dalloc(rowb);
-    h->hb = h->dalloc(rowb);
-    h->qb = h->dalloc(rowb);
-    h->att = h->dalloc(rowb);
-    h->ffa = h->dalloc(static_cast<size_t>(h->R_max) * Fmax * h->act_elt);
+    h->X = h->dalloc(rowb);
+    h->H = h->dalloc(rowb);
+    h->X1 = h->dalloc(rowb);
+    h->Q = h->dalloc(rowb);
+    h->ATT = h->dalloc(rowb);
+    h->A = h->dalloc(static_cast<size_t>(h->R_max) * Fmax * h->act_elt);
     h->logits = static_cast<float *>(h->dalloc(static_cast<size_t>(R_round) * td.V * sizeof(float)));
     h->part = static_cast<float *>(
-        h->dalloc(static_cast<size_t>(h->R_part) * std::max(td.H, dd.H) * h->max_split * (std::max(td.D, dd.D) + 2) * sizeof(float)));
-    h->rtok = static_cast<int *>(h->dalloc(h->R_max * sizeof(int)));
-    h->rpos = static_cast<int *>(h->dalloc(h->R_max * sizeof(int)));
-    h->rreq = static_cast<int *>(h->dalloc(h->R_max * sizeof(int)));
-    h->sel = static_cast<int *>(h->dalloc(h->R_max * sizeof(int)));
+        h->dalloc(static_cast<size_t>(h->R_part) * Hmax * h->max_split * (std::max(td.D, dd.D) + 2) * sizeof(float)));
+    h->counters = static_cast<int *>(h->dalloc(static_cast<size_t>(h->R_part) * Hmax * sizeof(int)));
+    CK(cudaMemset(h->counters, 0, static_cast<size_t>(h->R_part) * Hmax * sizeof(int)));
+    const size_t n_tiles = static_cast<size_t>(h->R_max) / kRowTile + 2;
+    h->tile_counters = static_cast<int *>(h->dalloc(n_tiles * sizeof(int)));
+    CK(cudaMemset(h->tile_counters, 0, n_tiles * sizeof(int)));
+    const size_t pool_rows =
+        static_cast<size_t>(h->R_max) + 2 * B + static_cast<size_t>(k - 1) * B + static_cast<size_t>(B) * (k + 1);
+    auto ib = [&](size_t n) { return static_cast<int *>(h->dalloc(n * sizeof(int))); };
+    h->pool.tok = ib(pool_rows);
+    h->pool.pos = ib(pool_rows);
+    h->pool.req = ib(pool_rows);
+    CK(cudaMemset(h->pool.tok, 0, pool_rows * sizeof(int)));
+    CK(cudaMemset(h->pool.pos, 0, pool_rows * sizeof(int)));
+    CK(cudaMemset(h->pool.req, 0xff, pool_rows * sizeof(int)));
+    h->sel_odd = ib(B);
+    h->sel_prefill = ib(B);
+    fill_odd_kernel<<<(B + 127) / 128, 128, 0, h->stream>>>(h->sel_odd, B);
+    CK(cudaGetLastError());
     // speculative state
     SpecState &st = h->st;
     const int out_len_max = cfg->max_prompt_len + std::max(td.max_seq, 1) + 1;
-    st.tokens_out = static_cast<int *>(h->dalloc(static_cast<size_t>(B) * out_len_max * sizeof(int)));
-    auto ib = [&](int n) { return static_cast<int *>(h->dalloc(static_cast<size_t>(n) * sizeof(int))); };
+    st.tokens_out = ib(static_cast<size_t>(B) * out_len_max);
     st.n_new = ib(B); st.t_len = ib(B); st.d_len = ib(B); st.t_start = ib(B); st.d_start = ib(B);
-    st.last_tok = ib(B); st.catch_tok = ib(B); st.active = ib(B); st.M = ib(B); st.round = ib(B);
-    st.cand = ib(B * k);
+    st.last_tok = ib(B); st.active = ib(B); st.M = ib(B); st.round = ib(B);
+    st.cand = ib(static_cast<size_t>(B) * k);
     st.q = static_cast<float *>(h->dalloc(static_cast<size_t>(B) * k * td.V * sizeof(float)));
-    st.pbuf = static_cast<float *>(h->dalloc(static_cast<size_t>(B) * td.V * sizeof(float)));
     st.stats = static_cast<long long *>(h->dalloc(static_cast<size_t>(B) * 4 * sizeof(long long)));
     st.mt = static_cast<uint32_t *>(h->dalloc(static_cast<size_t>(B) * kMtN * sizeof(uint32_t)));
     st.mt_idx = ib(B);
     st.active_count = ib(1);
     st.err = ib(1);
     CK(cudaMemset(st.err, 0, sizeof(int)));
+    CK(cudaMemset(st.active_count, 0, sizeof(int)));
     h->d_iters = ib(1);
-    h->d_prompts = ib(B * cfg->max_prompt_len);
-    h->d_out = static_cast<int *>(h->dalloc(static_cast<size_t>(B) * out_len_max * sizeof(int)));
+    h->d_prompts = ib(static_cast<size_t>(B) * cfg->max_prompt_len);
+    h->d_out = ib(static_cast<size_t>(B) * out_len_max);
     h->d_stats = static_cast<long long *>(h->dalloc(static_cast<size_t>(B) * 4 * sizeof(long long)));
     CK(cudaMallocHost(&h->h_pinned, 64));
     CK(cudaDeviceSynchronize());
@@ -929,10 +908,7 @@ int specdec_destroy(specdec_handle *h) {
   if (!h) return SPECDEC_OK;
   cudaSetDevice(h->device);
   if (h->stream) cudaStreamSynchronize(h->stream);
-  for (auto &kv : h->graphs) {
-    if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
-    if (kv.second.graph) cudaGraphDestroy(kv.second.graph);
-  }
+  destroy_graphs(h);
   for (int r = 0; r < 2; ++r)
     for (void *p : h->weight_allocs[r]) cudaFree(p);
   for (void *p : h->allocs) cudaFree(p);
@@ -990,7 +966,8 @@ int specdec_generate_device(specdec_handle *h, const specdec_gen_params *p, cons
   if (!h) return SPECDEC_ERR_INVALID;
   try {
     CK(cudaSetDevice(h->device));
-    return generate_impl(h, p, d_prompts, B, S, d_out_tokens, d_out_stats, false);
+    if (!d_prompts || !d_out_tokens) fail(SPECDEC_ERR_INVALID, "null buffer");
+    return generate_impl(h, p, d_prompts, B, S, d_out_tokens, d_out_stats);
   } catch (const SpecErr &e) {
     h->err = e.msg;
     return e.code;
@@ -1004,20 +981,22 @@ int specdec_generate(specdec_handle *h, const specdec_gen_params *p, const int32
     CK(cudaSetDevice(h->device));
     if (!prompts || !out_tokens) fail(SPECDEC_ERR_INVALID, "null buffer");
     if (!p) fail(SPECDEC_ERR_INVALID, "null params");
-    if (B < 1 || B > h->cfg.max_batch || S < 1 || S > h->cfg.max_prompt_len) fail(SPECDEC_ERR_INVALID, "batch or prompt length out of range");
+    if (B < 1 || B > h->cfg.max_batch || S < 1 || S > h->cfg.max_prompt_len)
+      fail(SPECDEC_ERR_INVALID, "batch or prompt length out of range");
     CK(cudaMemcpyAsync(h->d_prompts, prompts, static_cast<size_t>(B) * S * sizeof(int), cudaMemcpyHostToDevice, h->stream));
-    int rc = generate_impl(h, p, h->d_prompts, B, S, h->d_out, reinterpret_cast<int64_t *>(h->d_stats), true);
+    int rc = generate_impl(h, p, h->d_prompts, B, S, h->d_out, reinterpret_cast<int64_t *>(h->d_stats));
     if (rc != SPECDEC_OK) return rc;
     const int n = S + std::max(1, p->max_new_tokens);
     CK(cudaMemcpyAsync(out_tokens, h->d_out, static_cast<size_t>(B) * n * sizeof(int), cudaMemcpyDeviceToHost, h->stream));
     if (out_stats)
-      CK(cudaMemcpyAsync(out_stats, h->d_stats, static_cast<size_t>(B) * 4 * sizeof(int64_t), cudaMemcpyDeviceToHost, h->stream));
-    int err = 0;
+      CK(cudaMemcpyAsync(out_stats, h->d_stats, static_cast<size_t>(B) * 4 * sizeof(int64_t), cudaMemcpyDeviceToHost,
+                         h->stream));
     CK(cudaMemcpyAsync(h->h_pinned, h->st.err, sizeof(int), cudaMemcpyDeviceToHost, h->stream));
     sync_check(h);
-    err = h->h_pinned[0];
+    const int err = h->h_pinned[0];
     if (err & kErrSeqLen) fail(SPECDEC_ERR_SEQ_LEN, "Sequence length S plus past cached length exceeds max_seq_len");
     if (err & kErrRngTable) fail(SPECDEC_ERR_RNG, "the host uniform table has too few rounds");
+    if (err & kErrTimeout) fail(SPECDEC_ERR_CUDA, "an asynchronous copy did not complete within its wait limit");
   } catch (const SpecErr &e) {
     h->err = e.msg;
     return e.code;
@@ -1030,46 +1009,37 @@ int specdec_forward_logits(specdec_handle *h, int role, const int32_t *tokens, i
   try {
     CK(cudaSetDevice(h->device));
     const bool target = role == SPECDEC_TARGET;
+    if (role != SPECDEC_TARGET && role != SPECDEC_DRAFT) fail(SPECDEC_ERR_INVALID, "unknown role");
     ModelW &m = target ? h->tgt : h->dft;
     if (!m.loaded) fail(SPECDEC_ERR_STATE, "weights not loaded");
-    if (S < 1 || S > (target ? h->t_cap : h->d_cap) || S > h->R_max || S > h->cfg.max_prompt_len)
+    if (!tokens || !logits) fail(SPECDEC_ERR_INVALID, "null buffer");
+    if (S < 1 || S > (target ? h->t_cap : h->d_cap) || S > h->R_max || S > h->cfg.max_prompt_len * h->cfg.max_batch)
       fail(SPECDEC_ERR_INVALID, "sequence length out of range");
+    const Dims &dm = m.dm;
+    h->launches = 0;
     CK(cudaMemsetAsync(h->st.err, 0, sizeof(int), h->stream));
     CK(cudaMemcpyAsync(h->d_prompts, tokens, S * sizeof(int), cudaMemcpyHostToDevice, h->stream));
-    plan_prefill_kernel<<<(S + 255) / 256, 256, 0, h->stream>>>(h->d_prompts, 1, S, 0, S, h->rtok, h->rpos, h->rreq, h->sel);
-    // logits for every row: identity selection, in chunks that fit the logits buffer
+    launch(h, plan_prefill_kernel, dim3((S + 255) / 256), dim3(256), 0, static_cast<const int *>(h->d_prompts), 1, S, 0,
+           S, dm.V, h->pool.tok, h->pool.pos, h->pool.req, static_cast<int *>(nullptr));
+    forward_rows(h, target, 0, S, S, nullptr, 0, nullptr);
+    // the lm_head over row chunks that fit the logits buffer
     const int R_round = std::max(h->cfg.max_batch * (h->cfg.max_lookahead + 1), 2 * h->cfg.max_batch);
-    forward_rows(h, target, S, nullptr, 0, nullptr);
-    // head over row chunks
-    std::vector<int> idx(S);
-    for (int i = 0; i < S; ++i) idx[i] = i;
+    RowsView rows{h->pool.tok, h->pool.pos, h->pool.req};
+    const bool ref = dm.arch == SPECDEC_ARCH_REF;
     for (int c0 = 0; c0 < S; c0 += R_round) {
       const int n = std::min(R_round, S - c0);
-      CK(cudaMemcpyAsync(h->sel, idx.data() + c0, n * sizeof(int), cudaMemcpyHostToDevice, h->stream));
-      const void *hin = h->x;
-      const Dims &dm = m.dm;
-      if (dm.arch != SPECDEC_ARCH_REF) {
-        layernorm(h, h->x, S, dm.d, m.gf, m.bfin, h->x1);
-        hin = h->x1;
-      }
       LinearArgs hd{};
-      hd.x = hin; hd.ldx = dm.d; hd.in_rows = h->sel; hd.R = n; hd.W = m.whead; hd.scale = m.shead; hd.bias = m.bhead;
-      hd.N = dm.V; hd.K = dm.d; hd.out = h->logits; hd.ldo = dm.V;
-      dim3 grid((hd.N + 2 * kLinWarps - 1) / (2 * kLinWarps), (hd.R + kRowTile - 1) / kRowTile);
-      const bool bf = act_bf16(h), i8 = w_int8(h);
-      if (i8 && bf) head_kernel<int8_t, __nv_bfloat16><<<grid, 32 * kLinWarps, 0, h->stream>>>(hd);
-      else if (i8) head_kernel<int8_t, float><<<grid, 32 * kLinWarps, 0, h->stream>>>(hd);
-      else if (bf) head_kernel<float, __nv_bfloat16><<<grid, 32 * kLinWarps, 0, h->stream>>>(hd);
-      else head_kernel<float, float><<<grid, 32 * kLinWarps, 0, h->stream>>>(hd);
-      CK(cudaGetLastError());
+      hd.R = n; hd.W = m.whead; hd.scale = m.shead; hd.bias = m.bhead; hd.N = dm.V; hd.K = dm.d;
+      hd.out = h->logits; hd.ldo = dm.V; hd.out_f32 = 1; hd.rows = rows;
+      hd.x = static_cast<char *>(ref ? h->X : h->X1) + static_cast<size_t>(c0) * dm.d * h->act_elt;
+      hd.ldx = dm.d;
+      launch_linear<kEpiStore>(h, hd);
       CK(cudaMemcpyAsync(logits + static_cast<size_t>(c0) * dm.V, h->logits, static_cast<size_t>(n) * dm.V * sizeof(float),
                          cudaMemcpyDeviceToHost, h->stream));
     }
-    int err = 0;
     CK(cudaMemcpyAsync(h->h_pinned, h->st.err, sizeof(int), cudaMemcpyDeviceToHost, h->stream));
     sync_check(h);
-    err = h->h_pinned[0];
-    if (err) fail(SPECDEC_ERR_SEQ_LEN, "cache capacity exceeded");
+    if (h->h_pinned[0]) fail(SPECDEC_ERR_SEQ_LEN, "cache capacity exceeded");
   } catch (const SpecErr &e) {
     h->err = e.msg;
     return e.code;
@@ -1121,7 +1091,8 @@ int specdec_philox_uniforms(uint64_t seed, int B, int rounds, int slots, float *
 // allocating library routine.
 //
 // The array is shared by every call on a device and keeps the last call's
-// contents; the error word is cleared at the start of each call.  Calls whose
+// contents; the error word and the arrival counters are cleared at the start of
+// each call.  Calls whose
 // work overlaps on the GPU (different streams, or different handles on the
 // same device) race on the array and must be serialised by the caller.  The
 // first call on each device looks up the array's device address
@@ -1165,23 +1136,24 @@ struct ArenaCarver {
 extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const int32_t *d_tokens, int S,
                                               float *d_logits, void *stream) {
   if (!h) return SPECDEC_ERR_INVALID;
-  // The handle's buffers are pointed at the scratch array for the duration of
-  // the call and restored on every exit path.
+  // The handle's working buffers are pointed at the scratch array for the
+  // duration of the call and restored on every exit path.
   struct Saved {
-    void *x, *x1, *hb, *qb, *att, *ffa, *tk, *tv, *dk, *dv;
+    void *X, *H, *X1, *A, *Q, *ATT, *tk, *tv, *dk, *dv;
     float *part;
-    int *rtok, *rpos, *rreq, *sel, *err;
+    int *counters, *tile_counters, *err;
+    RowPool pool;
     size_t tls, dls, trs, drs;
     int tcap, dcap, R_part, max_split, R_max;
     cudaStream_t stream;
   };
-  Saved sv{h->x, h->x1, h->hb, h->qb, h->att, h->ffa, h->tk, h->tv, h->dk, h->dv, h->part,
-           h->rtok, h->rpos, h->rreq, h->sel, h->st.err, h->t_layer_stride, h->d_layer_stride,
-           h->t_req_stride, h->d_req_stride, h->t_cap, h->d_cap, h->R_part, h->max_split, h->R_max, h->stream};
+  Saved sv{h->X, h->H, h->X1, h->A, h->Q, h->ATT, h->tk, h->tv, h->dk, h->dv, h->part, h->counters, h->tile_counters,
+           h->st.err, h->pool, h->t_layer_stride, h->d_layer_stride, h->t_req_stride, h->d_req_stride, h->t_cap,
+           h->d_cap, h->R_part, h->max_split, h->R_max, h->stream};
   auto restore = [&] {
-    h->x = sv.x; h->x1 = sv.x1; h->hb = sv.hb; h->qb = sv.qb; h->att = sv.att; h->ffa = sv.ffa;
+    h->X = sv.X; h->H = sv.H; h->X1 = sv.X1; h->A = sv.A; h->Q = sv.Q; h->ATT = sv.ATT;
     h->tk = sv.tk; h->tv = sv.tv; h->dk = sv.dk; h->dv = sv.dv; h->part = sv.part;
-    h->rtok = sv.rtok; h->rpos = sv.rpos; h->rreq = sv.rreq; h->sel = sv.sel; h->st.err = sv.err;
+    h->counters = sv.counters; h->tile_counters = sv.tile_counters; h->st.err = sv.err; h->pool = sv.pool;
     h->t_layer_stride = sv.tls; h->d_layer_stride = sv.dls; h->t_req_stride = sv.trs; h->d_req_stride = sv.drs;
     h->t_cap = sv.tcap; h->d_cap = sv.dcap; h->R_part = sv.R_part; h->max_split = sv.max_split;
     h->R_max = sv.R_max; h->stream = sv.stream;
@@ -1195,28 +1167,30 @@ extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const
     if (!d_tokens || !d_logits) fail(SPECDEC_ERR_INVALID, "null device buffer");
     const Dims &dm = m.dm;
     if (S < 1 || S > h->rope_max) fail(SPECDEC_ERR_INVALID, "sequence length out of range");
-    // carve the layout first with a null base to size it
     const size_t act = h->act_elt;
     const size_t kv_elt = h->cfg.kv_dtype == SPECDEC_BF16 ? 2 : 4;
-    const int nsplit = std::max(1, std::min(16, (S + 255) / 256));
+    const int nsplit = std::max(1, std::min(16, (S + 1023) / 1024));
+    const size_t n_tiles = static_cast<size_t>(S) / kRowTile + 2;
     auto layout = [&](ArenaCarver &c, void **ptrs) {
-      ptrs[0] = c.take(static_cast<size_t>(S) * dm.d * act);   // x
-      ptrs[1] = c.take(static_cast<size_t>(S) * dm.d * act);   // x1
-      ptrs[2] = c.take(static_cast<size_t>(S) * dm.d * act);   // hb
-      ptrs[3] = c.take(static_cast<size_t>(S) * dm.d * act);   // qb
-      ptrs[4] = c.take(static_cast<size_t>(S) * dm.d * act);   // att
-      ptrs[5] = c.take(static_cast<size_t>(S) * dm.F * act);   // ffa
+      const size_t rows_d = static_cast<size_t>(S) * dm.d * act;
+      ptrs[0] = c.take(rows_d);                                // X
+      ptrs[1] = c.take(rows_d);                                // H
+      ptrs[2] = c.take(rows_d);                                // X1
+      ptrs[3] = c.take(static_cast<size_t>(S) * dm.F * act);   // A
+      ptrs[4] = c.take(rows_d);                                // Q
+      ptrs[5] = c.take(rows_d);                                // ATT
       const size_t kv = static_cast<size_t>(std::max(1, dm.L)) * dm.Hkv * S * dm.D * kv_elt;
       ptrs[6] = c.take(kv);                                    // K cache
       ptrs[7] = c.take(kv);                                    // V cache
-      ptrs[8] = c.take(static_cast<size_t>(S) * dm.H * nsplit * (dm.D + 2) * sizeof(float));  // partials
-      ptrs[9] = c.take(S * sizeof(int));                       // row tokens
-      ptrs[10] = c.take(S * sizeof(int));                      // row positions
-      ptrs[11] = c.take(S * sizeof(int));                      // row requests
-      ptrs[12] = c.take(S * sizeof(int));                      // selection
-      ptrs[13] = c.take(sizeof(int));                          // error word
+      ptrs[8] = c.take(static_cast<size_t>(S) * dm.H * nsplit * (dm.D + 2) * sizeof(float));  // attention partials
+      ptrs[9] = c.take(static_cast<size_t>(S) * dm.H * sizeof(int));                          // split counters
+      ptrs[10] = c.take(n_tiles * sizeof(int));                                              // row-tile counters
+      ptrs[11] = c.take(S * sizeof(int));                      // row tokens
+      ptrs[12] = c.take(S * sizeof(int));                      // row positions
+      ptrs[13] = c.take(S * sizeof(int));                      // row requests
+      ptrs[14] = c.take(sizeof(int));                          // error word
     };
-    void *ptrs[14];
+    void *ptrs[15];
     ArenaCarver sizing{nullptr};
     layout(sizing, ptrs);
     if (sizing.used > SPECDEC_NOALLOC_SCRATCH_BYTES)
@@ -1228,12 +1202,15 @@ extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const
     ArenaCarver arena{base};
     layout(arena, ptrs);
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : h->stream;
-    h->x = ptrs[0]; h->x1 = ptrs[1]; h->hb = ptrs[2]; h->qb = ptrs[3]; h->att = ptrs[4]; h->ffa = ptrs[5];
+    h->X = ptrs[0]; h->H = ptrs[1]; h->X1 = ptrs[2]; h->A = ptrs[3]; h->Q = ptrs[4]; h->ATT = ptrs[5];
     if (target) { h->tk = ptrs[6]; h->tv = ptrs[7]; } else { h->dk = ptrs[6]; h->dv = ptrs[7]; }
     h->part = static_cast<float *>(ptrs[8]);
-    h->rtok = static_cast<int *>(ptrs[9]); h->rpos = static_cast<int *>(ptrs[10]);
-    h->rreq = static_cast<int *>(ptrs[11]); h->sel = static_cast<int *>(ptrs[12]);
-    h->st.err = static_cast<int *>(ptrs[13]);
+    h->counters = static_cast<int *>(ptrs[9]);
+    h->tile_counters = static_cast<int *>(ptrs[10]);
+    h->pool.tok = static_cast<int *>(ptrs[11]);
+    h->pool.pos = static_cast<int *>(ptrs[12]);
+    h->pool.req = static_cast<int *>(ptrs[13]);
+    h->st.err = static_cast<int *>(ptrs[14]);
     const size_t req_stride = static_cast<size_t>(dm.Hkv) * S * dm.D;
     if (target) { h->t_req_stride = req_stride; h->t_layer_stride = req_stride; h->t_cap = S; }
     else { h->d_req_stride = req_stride; h->d_layer_stride = req_stride; h->d_cap = S; }
@@ -1242,9 +1219,11 @@ extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const
     h->max_split = nsplit;
     h->stream = st;
     CK(cudaMemsetAsync(h->st.err, 0, sizeof(int), st));
-    plan_prefill_kernel<<<(S + 255) / 256, 256, 0, st>>>(d_tokens, 1, S, 0, S, h->rtok, h->rpos, h->rreq, h->sel);
-    forward_rows(h, target, S, nullptr, S, d_logits);
-    CK(cudaGetLastError());
+    CK(cudaMemsetAsync(h->counters, 0, static_cast<size_t>(S) * dm.H * sizeof(int), st));
+    CK(cudaMemsetAsync(h->tile_counters, 0, n_tiles * sizeof(int), st));
+    launch(h, plan_prefill_kernel, dim3((S + 255) / 256), dim3(256), 0, d_tokens, 1, S, 0, S, dm.V, h->pool.tok,
+           h->pool.pos, h->pool.req, static_cast<int *>(nullptr));
+    forward_rows(h, target, 0, S, S, nullptr, S, d_logits);
     restore();
   } catch (const SpecErr &e) {
     restore();

@@ -1,15 +1,14 @@
 // Forward-pass kernels of the decoder stack (target and draft share them).
 //
 // A forward pass runs over a batch of "rows": one row is one token of one
-// request, at one cache position.  Prefill, a draft step, the (k+1)-token
+// request at one cache position.  Prefill, a draft step, the (k+1)-token
 // verify block and the draft catch-up are all row batches; row r carries
 // (token, position, request) and request < 0 marks an unused row.  Every row
-// writes its K/V at its own position before the attention kernel reads the
-// cache, so causal attention over the cache is exactly the reference's
-// masked attention over past + new tokens (src/nn/layer.cpp:842-952, mask
-// j > S_past + i).
+// writes its K/V at its own position before attention reads the cache, so
+// causal attention over the cache is the reference's masked attention over
+// past + new tokens (src/nn/layer.cpp:842-952, mask j > S_past + i).
 //
-// Device layouts (all chosen for coalesced 16-byte streaming on B200):
+// Device layouts (chosen for coalesced streaming on B200):
 //   weights     W^T [N][K] row-major (output-major), fp32 or int8 + fp32
 //               per-output scale; the reference keeps W [K][N]
 //               (src/nn/layer.cpp:153) and the loader transposes.
@@ -17,6 +16,10 @@
 //   SwiGLU      gate/up interleaved: row 2c = gate_c, row 2c+1 = up_c.
 //   activations [R][d] in the activation dtype (fp32 or bf16).
 //   KV cache    [layer][request slot][kv head][position][D].
+//
+// The small configurations are latency-bound: every kernel here is built to
+// issue its global loads together (one or two L2 round trips per kernel)
+// rather than in dependent chains.
 #pragma once
 
 #include "common.cuh"
@@ -24,7 +27,7 @@
 namespace specdec {
 
 struct RowsView {
-  const int *tok;
+  const int *tok;  // embedding row (clamped to [0, V) by whoever wrote the row)
   const int *pos;
   const int *req;
 };
@@ -32,30 +35,66 @@ struct RowsView {
 // ---------------------------------------------------------------------------
 // Embedding gather (Embedding::forward -> CpuBackend::embedding,
 // src/backend/cpu_backend.cpp:998-1033: an out-of-range id reads row 0).  The
-// cfg architecture adds the learned position row.
+// cfg architecture adds the learned position row and also writes LN1(x) for
+// the first layer.  One block per row; d <= 32 * blockDim.
 template <typename AT>
-__global__ void embed_kernel(RowsView rows, int R, const float *__restrict__ emb,
-                             const float *__restrict__ pos_emb, int V, int d, int max_pos,
-                             AT *__restrict__ x) {
+__global__ void embed_kernel(RowsView rows, int R, const float *__restrict__ emb, const float *__restrict__ pos_emb,
+                             int d, int max_pos, AT *__restrict__ x, const float *__restrict__ ln_g,
+                             const float *__restrict__ ln_b, AT *__restrict__ x_ln) {
+  __shared__ float red[32];
   const int r = blockIdx.x;
   if (r >= R) return;
-  int id = rows.tok[r];
-  if (id < 0 || id >= V) id = 0;
-  int p = rows.pos[r];
-  p = p < 0 ? 0 : (p >= max_pos ? max_pos - 1 : p);
-  const float *e = emb + static_cast<size_t>(id) * d;
-  for (int i = threadIdx.x; i < d; i += blockDim.x) {
-    float v = e[i];
-    if (pos_emb) v += pos_emb[static_cast<size_t>(p) * d + i];
-    x[static_cast<size_t>(r) * d + i] = from_f32<AT>(v);
+  const int id = rows.tok[r];
+  const int p = min(max(rows.pos[r], 0), max_pos - 1);
+  constexpr int kMax = 32;
+  float v[kMax];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMax; ++i) {
+    const int c = threadIdx.x + i * blockDim.x;
+    float t = 0.f;
+    if (c < d) {
+      t = emb[static_cast<size_t>(id) * d + c];
+      if (pos_emb) t += pos_emb[static_cast<size_t>(p) * d + c];
+      t = to_f32(from_f32<AT>(t));
+      x[static_cast<size_t>(r) * d + c] = from_f32<AT>(t);
+    }
+    v[i] = t;
+    s += t;
+  }
+  if (!ln_g) return;
+  const float mean = __fdiv_rn(block_sum(s, red), static_cast<float>(d));
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMax; ++i) {
+    const int c = threadIdx.x + i * blockDim.x;
+    if (c < d) {
+      const float df = v[i] - mean;
+      q = fmaf(df, df, q);
+    }
+  }
+  const float sd = sqrtf(__fdiv_rn(block_sum(q, red), static_cast<float>(d)) + 1e-5f);
+#pragma unroll
+  for (int i = 0; i < kMax; ++i) {
+    const int c = threadIdx.x + i * blockDim.x;
+    if (c < d)
+      x_ln[static_cast<size_t>(r) * d + c] =
+          from_f32<AT>(__fadd_rn(__fmul_rn(__fdiv_rn(v[i] - mean, sd), ln_g[c]), ln_b[c]));
   }
 }
 
 // ---------------------------------------------------------------------------
-// Linear layer y = x . W + b on CUDA cores, for the small row counts of
-// draft steps and verify blocks.  Each warp owns a PAIR of adjacent output
-// columns (so RoPE pairs and SwiGLU gate/up pairs land in one lane) for a tile
-// of kRowTile rows; lanes split K in 16-byte weight vectors.
+// Linear layer y = x . W + b on CUDA cores for the small row counts of draft
+// steps and verify blocks (a GEMV per tile of kRowTile rows).
+//
+// A warp owns a PAIR of adjacent output columns (so RoPE pairs and SwiGLU
+// gate/up pairs land in one lane); `ksplit` warps of a block share one pair
+// and split K, so each lane issues its weight and input vectors in one go.
+// Everything the epilogue needs (scale, bias, residual, row position, RoPE
+// factors) is loaded before the dot products.  With `ln_out` set, the last
+// block to finish a row tile applies the following LayerNorm
+// (LayerNorm::forward, src/nn/layer.cpp:242-261) to the complete rows, so no
+// separate norm kernel runs.
 enum Epi : int {
   kEpiStore = 0,   // out = acc*s + b
   kEpiResid = 1,   // out = acc*s + b + resid
@@ -76,94 +115,129 @@ struct QKVArgs {
 };
 
 struct LinearArgs {
-  const void *x;       // activations
+  const void *x;          // input rows (activation dtype)
   int ldx;
-  const int *in_rows;  // optional: logical row r reads x row in_rows[r]
+  const int *in_rows;     // optional row map: logical row r reads x row in_rows[r]
   int R;
-  const void *W;       // [N][K]
-  const float *scale;  // [N] or null
-  const float *bias;   // [N] (interleaved like W for SwiGLU)
+  const void *W;          // [N][K]
+  const float *scale;     // [N] or null
+  const float *bias;      // [N] (interleaved like W for SwiGLU)
   int N, K;
   void *out;
   int ldo;
+  int out_f32;            // 1: fp32 output (logits); 0: activation dtype
   const void *resid;
   int ldr;
-  RowsView rows;       // for kEpiQKV
+  RowsView rows;          // row metadata (QKV epilogue)
   QKVArgs qkv;
+  const float *ln_g, *ln_b;  // optional LayerNorm of the finished output rows ...
+  void *ln_out;              // ... written here (activation dtype, leading dim ldo)
+  int *tile_counters;        // [row tiles] arrival counters (left at 0)
+  int ksplit;                // warps per column pair: 1, 2, 4 or 8
 };
 
 constexpr int kLinWarps = 8;
 constexpr int kRowTile = 8;
+constexpr int kLnMaxPerLane = 32;  // LayerNorm rows held in registers: N <= 1024 per warp
 
 template <typename WT> struct WVec;
 template <> struct WVec<float> { static constexpr int E = 4; };
-template <> struct WVec<int8_t> { static constexpr int E = 16; };
-template <> struct WVec<__nv_bfloat16> { static constexpr int E = 8; };
+template <> struct WVec<int8_t> { static constexpr int E = 8; };
 
-__device__ __forceinline__ void unpack_w(const float4 &raw, float (&w)[4]) {
-  w[0] = raw.x; w[1] = raw.y; w[2] = raw.z; w[3] = raw.w;
+__device__ __forceinline__ void load_wvec(const float *p, float (&w)[4]) {
+  const float4 t = __ldg(reinterpret_cast<const float4 *>(p));
+  w[0] = t.x; w[1] = t.y; w[2] = t.z; w[3] = t.w;
 }
-__device__ __forceinline__ void unpack_w(const int4 &raw, float (&w)[16]) {
-  const int v[4] = {raw.x, raw.y, raw.z, raw.w};
+__device__ __forceinline__ void load_wvec(const int8_t *p, float (&w)[8]) {
+  const uint2 t = __ldg(reinterpret_cast<const uint2 *>(p));
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-#pragma unroll
-    for (int b = 0; b < 4; ++b) w[4 * i + b] = static_cast<float>(static_cast<int8_t>((v[i] >> (8 * b)) & 0xff));
+  for (int b = 0; b < 4; ++b) {
+    w[b] = static_cast<float>(static_cast<int8_t>((t.x >> (8 * b)) & 0xff));
+    w[4 + b] = static_cast<float>(static_cast<int8_t>((t.y >> (8 * b)) & 0xff));
   }
 }
 
-template <typename AT>
-__device__ __forceinline__ float load_act(const AT *p) { return to_f32(*p); }
-
+// E consecutive input elements as fp32.
 template <typename AT, int E>
-__device__ __forceinline__ void load_x(const AT *p, float (&xv)[E]) {
+__device__ __forceinline__ void load_xvec(const AT *p, float (&xv)[E]) {
   if constexpr (sizeof(AT) == 4) {
 #pragma unroll
     for (int i = 0; i < E; i += 4) {
-      float4 t = __ldg(reinterpret_cast<const float4 *>(p + i));
+      const float4 t = __ldg(reinterpret_cast<const float4 *>(p + i));
       xv[i] = t.x; xv[i + 1] = t.y; xv[i + 2] = t.z; xv[i + 3] = t.w;
     }
-  } else if constexpr (E == 4) {
-    uint2 t = __ldg(reinterpret_cast<const uint2 *>(p));
-    const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&t);
-    float2 f0 = __bfloat1622float2(h[0]), f1 = __bfloat1622float2(h[1]);
-    xv[0] = f0.x; xv[1] = f0.y; xv[2] = f1.x; xv[3] = f1.y;
   } else {
 #pragma unroll
-    for (int i = 0; i < E; i += 8) {
-      int4 t = __ldg(reinterpret_cast<const int4 *>(p + i));
-      const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&t);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float2 f = __bfloat1622float2(h[j]);
-        xv[i + 2 * j] = f.x; xv[i + 2 * j + 1] = f.y;
-      }
+    for (int i = 0; i < E; i += 4) {
+      const uint2 t = __ldg(reinterpret_cast<const uint2 *>(p + i));
+      const __nv_bfloat162 *hh = reinterpret_cast<const __nv_bfloat162 *>(&t);
+      const float2 f0 = __bfloat1622float2(hh[0]), f1 = __bfloat1622float2(hh[1]);
+      xv[i] = f0.x; xv[i + 1] = f0.y; xv[i + 2] = f1.x; xv[i + 3] = f1.y;
+    }
+  }
+}
+
+// Operands of one lane's epilogue (row r, columns n and n+1), loaded early.
+struct EpiPre {
+  float s0, s1, b0, b1;  // scale and bias
+  float r0, r1;          // residual
+  float c, sn;           // RoPE (cos, sin)
+  int req, pos;
+};
+
+template <typename AT, int EPI>
+__device__ __forceinline__ void epilogue_prefetch(const LinearArgs &a, int r, int n, EpiPre &p) {
+  const bool has1 = (n + 1) < a.N;
+  p.s0 = a.scale ? __ldg(a.scale + n) : 1.f;
+  p.s1 = (a.scale && has1) ? __ldg(a.scale + n + 1) : 1.f;
+  p.b0 = __ldg(a.bias + n);
+  p.b1 = has1 ? __ldg(a.bias + n + 1) : 0.f;
+  p.r0 = p.r1 = 0.f;
+  p.c = 1.f;
+  p.sn = 0.f;
+  p.req = 0;
+  p.pos = 0;
+  if constexpr (EPI == kEpiResid) {
+    const AT *rs = static_cast<const AT *>(a.resid) + static_cast<size_t>(r) * a.ldr;
+    p.r0 = to_f32(rs[n]);
+    p.r1 = has1 ? to_f32(rs[n + 1]) : 0.f;
+  }
+  if constexpr (EPI == kEpiQKV) {
+    const QKVArgs &q = a.qkv;
+    p.req = a.rows.req[r];
+    p.pos = a.rows.pos[r];
+    if (p.req >= 0 && p.pos >= 0 && p.pos < q.rope_max_pos && n < q.d + q.kvd) {
+      const int e = (n < q.d ? n : n - q.d) % q.D;
+      const float2 cs = q.rope[static_cast<size_t>(p.pos) * (q.D / 2) + (e >> 1)];
+      p.c = cs.x;
+      p.sn = cs.y;
     }
   }
 }
 
 template <typename AT, int EPI>
-__device__ __forceinline__ void linear_epilogue(const LinearArgs &a, int r, int n, float v0, float v1) {
+__device__ __forceinline__ void linear_epilogue(const LinearArgs &a, int r, int n, float v0, float v1, const EpiPre &p) {
   const bool has1 = (n + 1) < a.N;
-  if (a.scale) {
-    v0 *= a.scale[n];
-    if (has1) v1 *= a.scale[n + 1];
-  }
-  v0 += a.bias[n];
-  if (has1) v1 += a.bias[n + 1];
+  v0 = v0 * p.s0 + p.b0;
+  v1 = v1 * p.s1 + p.b1;
   if constexpr (EPI == kEpiStore || EPI == kEpiResid || EPI == kEpiGelu) {
     if constexpr (EPI == kEpiResid) {
-      const AT *rs = static_cast<const AT *>(a.resid) + static_cast<size_t>(r) * a.ldr;
-      v0 = v0 + to_f32(rs[n]);
-      if (has1) v1 = v1 + to_f32(rs[n + 1]);
+      v0 = v0 + p.r0;
+      v1 = v1 + p.r1;
     }
     if constexpr (EPI == kEpiGelu) {
       v0 = 0.5f * v0 * (1.0f + erff(v0 * 0.70710678118654752f));
       v1 = 0.5f * v1 * (1.0f + erff(v1 * 0.70710678118654752f));
     }
-    AT *o = static_cast<AT *>(a.out) + static_cast<size_t>(r) * a.ldo;
-    o[n] = from_f32<AT>(v0);
-    if (has1) o[n + 1] = from_f32<AT>(v1);
+    if (a.out_f32) {
+      float *o = static_cast<float *>(a.out) + static_cast<size_t>(r) * a.ldo;
+      o[n] = v0;
+      if (has1) o[n + 1] = v1;
+    } else {
+      AT *o = static_cast<AT *>(a.out) + static_cast<size_t>(r) * a.ldo;
+      o[n] = from_f32<AT>(v0);
+      if (has1) o[n + 1] = from_f32<AT>(v1);
+    }
   } else if constexpr (EPI == kEpiSwiGLU) {
     // SwiGLU::forward (src/nn/layer.cpp:1704-1710): (g * sigmoid(g)) * up,
     // sigmoid = 1 / (1 + exp(-g)) (src/backend/cpu_backend.cpp:487-488).
@@ -172,10 +246,9 @@ __device__ __forceinline__ void linear_epilogue(const LinearArgs &a, int r, int 
     AT *o = static_cast<AT *>(a.out) + static_cast<size_t>(r) * a.ldo;
     o[n >> 1] = from_f32<AT>(__fmul_rn(__fmul_rn(g, sg), u));
   } else if constexpr (EPI == kEpiQKV) {
-    const int req = a.rows.req[r];
-    if (req < 0) return;
-    const int pos = a.rows.pos[r];
+    if (p.req < 0) return;
     const QKVArgs &q = a.qkv;
+    const int pos = p.pos;
     if (pos < 0 || pos >= q.S_cap || pos >= q.rope_max_pos) {
       if (q.err) atomicOr(q.err, kErrSeqLen);
       return;
@@ -184,12 +257,10 @@ __device__ __forceinline__ void linear_epilogue(const LinearArgs &a, int r, int 
       // Tensor::rope (src/core/tensor.cpp:1144-1163): pair (2j, 2j+1) of each
       // head rotated by pos * 10000^(-2j/D); the (cos, sin) table is computed
       // on the host with the reference's float formula.
-      const int e = (n < q.d ? n : n - q.d) % q.D;
-      const float2 cs = q.rope[static_cast<size_t>(pos) * (q.D / 2) + (e >> 1)];
-      const float r0 = __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y));
-      const float r1 = __fadd_rn(__fmul_rn(v0, cs.y), __fmul_rn(v1, cs.x));
-      v0 = r0;
-      v1 = r1;
+      const float x0 = __fsub_rn(__fmul_rn(v0, p.c), __fmul_rn(v1, p.sn));
+      const float x1 = __fadd_rn(__fmul_rn(v0, p.sn), __fmul_rn(v1, p.c));
+      v0 = x0;
+      v1 = x1;
     }
     if (n < q.d) {
       AT *o = static_cast<AT *>(a.out) + static_cast<size_t>(r) * a.ldo;
@@ -199,8 +270,7 @@ __device__ __forceinline__ void linear_epilogue(const LinearArgs &a, int r, int 
       const bool is_k = n < q.d + q.kvd;
       const int nn = is_k ? n - q.d : n - q.d - q.kvd;
       const int h = nn / q.D, e = nn % q.D;
-      const size_t off = static_cast<size_t>(req) * q.kv_req_stride +
-                         (static_cast<size_t>(h) * q.S_cap + pos) * q.D + e;
+      const size_t off = static_cast<size_t>(p.req) * q.kv_req_stride + (static_cast<size_t>(h) * q.S_cap + pos) * q.D + e;
       if (q.kv_bf16) {
         __nv_bfloat16 *c = static_cast<__nv_bfloat16 *>(is_k ? q.kc : q.vc);
         c[off] = __float2bfloat16_rn(v0);
@@ -214,230 +284,453 @@ __device__ __forceinline__ void linear_epilogue(const LinearArgs &a, int r, int 
   }
 }
 
-// grid: (ceil(N / (2*kLinWarps)), ceil(R / kRowTile)); block: 32*kLinWarps.
+// LayerNorm of rows [r0, r0 + nrows) of `in` (N columns, fp32 statistics),
+// one warp per row with the row in registers; the rows were written by other
+// blocks of this grid, so they are read through L2 (ld.global.cg).
+template <typename AT>
+__device__ void rows_layernorm(const AT *in, int ld, int r0, int nrows, int N, const float *g, const float *b, AT *out) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int i = warp; i < nrows; i += blockDim.x >> 5) {
+    const AT *x = in + static_cast<size_t>(r0 + i) * ld;
+    float v[kLnMaxPerLane];
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < kLnMaxPerLane; ++j) {
+      const int c = lane + 32 * j;
+      v[j] = (c < N) ? to_f32(__ldcg(x + c)) : 0.f;
+      s += v[j];
+    }
+    const float mean = __fdiv_rn(warp_sum(s), static_cast<float>(N));
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < kLnMaxPerLane; ++j) {
+      const int c = lane + 32 * j;
+      if (c < N) {
+        const float df = v[j] - mean;
+        q = fmaf(df, df, q);
+      }
+    }
+    const float sd = sqrtf(__fdiv_rn(warp_sum(q), static_cast<float>(N)) + 1e-5f);
+    AT *y = out + static_cast<size_t>(r0 + i) * ld;
+#pragma unroll
+    for (int j = 0; j < kLnMaxPerLane; ++j) {
+      const int c = lane + 32 * j;
+      if (c < N) y[c] = from_f32<AT>(__fadd_rn(__fmul_rn(__fdiv_rn(v[j] - mean, sd), __ldg(g + c)), __ldg(b + c)));
+    }
+  }
+}
+
+// grid: (ceil(N / (2 * kLinWarps / ksplit)), ceil(R / kRowTile)); block: 32 * kLinWarps.
 template <typename WT, typename AT, int EPI>
 __global__ void __launch_bounds__(32 * kLinWarps) linear_kernel(LinearArgs a) {
   constexpr int E = WVec<WT>::E;
+  __shared__ float s_red[kLinWarps][2 * kRowTile];
+  __shared__ int s_last;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int n0 = (blockIdx.x * kLinWarps + warp) * 2;
+  const int ks = a.ksplit;
+  const int pairs = kLinWarps / ks;
+  const int pair = warp / ks, kidx = warp % ks;
+  const int n0 = (blockIdx.x * pairs + pair) * 2;
   const int r0 = blockIdx.y * kRowTile;
-  if (n0 >= a.N) return;
-  const bool has1 = (n0 + 1) < a.N;
   const int nrows = min(kRowTile, a.R - r0);
-
-  const WT *w0 = static_cast<const WT *>(a.W) + static_cast<size_t>(n0) * a.K;
-  const WT *w1 = has1 ? w0 + a.K : w0;
-  const AT *xrow[kRowTile];
-#pragma unroll
-  for (int i = 0; i < kRowTile; ++i) {
-    int lr = r0 + (i < nrows ? i : 0);
-    int pr = a.in_rows ? a.in_rows[lr] : lr;
-    xrow[i] = static_cast<const AT *>(a.x) + static_cast<size_t>(pr) * a.ldx;
-  }
+  const bool col_ok = n0 < a.N;
+  const bool has1 = (n0 + 1) < a.N;
 
   float acc0[kRowTile], acc1[kRowTile];
 #pragma unroll
   for (int i = 0; i < kRowTile; ++i) acc0[i] = acc1[i] = 0.f;
-
-  // 16-byte vector path when rows of W and x are 16-byte aligned.
-  const bool vec_ok = ((a.K * static_cast<int>(sizeof(WT))) % 16 == 0) &&
-                      ((a.ldx * static_cast<int>(sizeof(AT))) % 16 == 0) &&
-                      ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0);
-  const int kvec = vec_ok ? a.K / E : 0;
-  for (int v = lane; v < kvec; v += 32) {
-    float wa[E], wb[E];
-    if constexpr (sizeof(WT) == 4) {
-      unpack_w(__ldg(reinterpret_cast<const float4 *>(w0) + v), wa);
-      unpack_w(__ldg(reinterpret_cast<const float4 *>(w1) + v), wb);
-    } else if constexpr (sizeof(WT) == 1) {
-      unpack_w(__ldg(reinterpret_cast<const int4 *>(w0) + v), wa);
-      unpack_w(__ldg(reinterpret_cast<const int4 *>(w1) + v), wb);
-    }
+  EpiPre pre{};
+  if (col_ok) {
+    // lane i finishes row i: fetch its epilogue operands now
+    if (kidx == 0 && lane < nrows) epilogue_prefetch<AT, EPI>(a, r0 + lane, n0, pre);
+    const WT *w0 = static_cast<const WT *>(a.W) + static_cast<size_t>(n0) * a.K;
+    const WT *w1 = has1 ? w0 + a.K : w0;
+    const AT *xrow[kRowTile];
 #pragma unroll
     for (int i = 0; i < kRowTile; ++i) {
-      if (i < nrows) {
-        float xv[E];
-        load_x<AT, E>(xrow[i] + v * E, xv);
-        float s0 = 0.f, s1 = 0.f;
+      const int lr = r0 + (i < nrows ? i : 0);
+      const int pr = a.in_rows ? a.in_rows[lr] : lr;
+      xrow[i] = static_cast<const AT *>(a.x) + static_cast<size_t>(pr) * a.ldx;
+    }
+    const bool vec_ok = (a.K % E == 0) && (a.ldx % 4 == 0);
+    const int kvec = vec_ok ? a.K / E : 0;
+#pragma unroll 2
+    for (int v = kidx * 32 + lane; v < kvec; v += 32 * ks) {
+      float wa[E], wb[E];
+      load_wvec(w0 + v * E, wa);
+      load_wvec(w1 + v * E, wb);
+      float xv[kRowTile][E];
 #pragma unroll
-        for (int e = 0; e < E; ++e) {
-          s0 = fmaf(xv[e], wa[e], s0);
-          s1 = fmaf(xv[e], wb[e], s1);
+      for (int i = 0; i < kRowTile; ++i)
+        if (i < nrows) load_xvec<AT, E>(xrow[i] + v * E, xv[i]);
+#pragma unroll
+      for (int i = 0; i < kRowTile; ++i) {
+        if (i < nrows) {
+          float t0 = 0.f, t1 = 0.f;
+#pragma unroll
+          for (int e = 0; e < E; ++e) {
+            t0 = fmaf(xv[i][e], wa[e], t0);
+            t1 = fmaf(xv[i][e], wb[e], t1);
+          }
+          acc0[i] += t0;
+          acc1[i] += t1;
         }
-        acc0[i] += s0;
-        acc1[i] += s1;
       }
     }
-  }
-  // scalar tail (and the whole K when rows are not 16-byte aligned)
-  for (int k = kvec * E + lane; k < a.K; k += 32) {
-    const float wa = static_cast<float>(w0[k]);
-    const float wb = static_cast<float>(w1[k]);
+    for (int k = kvec * E + kidx * 32 + lane; k < a.K; k += 32 * ks) {  // scalar tail / unaligned rows
+      const float wa = static_cast<float>(w0[k]), wb = static_cast<float>(w1[k]);
+#pragma unroll
+      for (int i = 0; i < kRowTile; ++i)
+        if (i < nrows) {
+          const float xv = to_f32(xrow[i][k]);
+          acc0[i] = fmaf(xv, wa, acc0[i]);
+          acc1[i] = fmaf(xv, wb, acc1[i]);
+        }
+    }
 #pragma unroll
     for (int i = 0; i < kRowTile; ++i) {
-      if (i < nrows) {
-        const float xv = load_act(xrow[i] + k);
-        acc0[i] = fmaf(xv, wa, acc0[i]);
-        acc1[i] = fmaf(xv, wb, acc1[i]);
+      acc0[i] = warp_sum(acc0[i]);
+      acc1[i] = warp_sum(acc1[i]);
+    }
+  }
+  if (ks > 1) {
+    if (lane == 0) {
+#pragma unroll
+      for (int i = 0; i < kRowTile; ++i) {
+        s_red[warp][2 * i] = acc0[i];
+        s_red[warp][2 * i + 1] = acc1[i];
       }
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < kRowTile; ++i) {
-    acc0[i] = warp_sum(acc0[i]);
-    acc1[i] = warp_sum(acc1[i]);
-  }
-  // lane i finishes row i
-#pragma unroll
-  for (int i = 0; i < kRowTile; ++i) {
-    if (lane == i && i < nrows) linear_epilogue<AT, EPI>(a, r0 + i, n0, acc0[i], acc1[i]);
-  }
-}
-
-// ---------------------------------------------------------------------------
-// Residual LayerNorm (LayerNorm::forward, src/nn/layer.cpp:242-261):
-// mean = sum/N, var = sum((x-mean)^2)/N, y = ((x-mean)/sqrt(var+eps))*g + b.
-// One block per row; the row is held in registers (d <= 32 * blockDim).
-template <typename AT>
-__global__ void layernorm_kernel(const AT *__restrict__ in, int ldi, int R, int d,
-                                 const float *__restrict__ g, const float *__restrict__ b,
-                                 AT *__restrict__ out, int ldo) {
-  __shared__ float red[32];
-  const int r = blockIdx.x;
-  if (r >= R) return;
-  constexpr int kMax = 32;
-  float v[kMax];
-  const AT *x = in + static_cast<size_t>(r) * ldi;
-  float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < kMax; ++i) {
-    int c = threadIdx.x + i * blockDim.x;
-    v[i] = (c < d) ? to_f32(x[c]) : 0.f;
-    s += v[i];
-  }
-  const float N = static_cast<float>(d);
-  const float mean = __fdiv_rn(block_sum(s, red), N);
-  float q = 0.f;
-#pragma unroll
-  for (int i = 0; i < kMax; ++i) {
-    int c = threadIdx.x + i * blockDim.x;
-    if (c < d) {
-      float df = v[i] - mean;
-      q = fmaf(df, df, q);
-    }
-  }
-  const float var = __fdiv_rn(block_sum(q, red), N);
-  const float sd = sqrtf(var + 1e-5f);
-  AT *y = out + static_cast<size_t>(r) * ldo;
-#pragma unroll
-  for (int i = 0; i < kMax; ++i) {
-    int c = threadIdx.x + i * blockDim.x;
-    if (c < d) y[c] = from_f32<AT>(__fadd_rn(__fmul_rn(__fdiv_rn(v[i] - mean, sd), g[c]), b[c]));
-  }
-}
-
-// ---------------------------------------------------------------------------
-// Causal attention of each row over its request's cache, positions
-// [0, pos] (split into chunks of `chunk` positions across blockIdx.z).
-// score = (q . k) / sqrt(D) (src/nn/layer.cpp:870, 891-897), softmax, P.V.
-// With one split the block writes the normalised output; otherwise it writes
-// (max, sum, unnormalised acc[D]) to `part` and attn_combine_kernel merges.
-constexpr int kAttnThreads = 128;
-
-template <typename AT, typename KT>
-__global__ void __launch_bounds__(kAttnThreads)
-attention_kernel(const AT *__restrict__ q, int ldq, RowsView rows, int R, const KT *__restrict__ kc,
-                 const KT *__restrict__ vc, size_t kv_req_stride, int S_cap, int H, int Hkv, int D,
-                 int chunk, AT *__restrict__ out, int ldo, float *__restrict__ part) {
-  extern __shared__ float sm[];
-  float *qs = sm;                    // [D]
-  float *sc = qs + D;                // [kAttnThreads]
-  float *accs = sc + kAttnThreads;   // [kAttnThreads] partial accumulators
-  __shared__ float red[32];
-
-  const int r = blockIdx.x, h = blockIdx.y, split = blockIdx.z, nsplit = gridDim.z;
-  const int req = rows.req[r];
-  const int pos = rows.pos[r];
-  const int tid = threadIdx.x;
-  const bool valid = req >= 0 && pos >= 0 && pos < S_cap;
-  const int ctx = valid ? pos + 1 : 0;
-  const int j0 = split * chunk;
-  const int j1 = min(ctx, j0 + chunk);
-
-  const int hk = h / (H / Hkv);
-  const KT *kbase = kc + (valid ? static_cast<size_t>(req) * kv_req_stride : 0) + static_cast<size_t>(hk) * S_cap * D;
-  const KT *vbase = vc + (valid ? static_cast<size_t>(req) * kv_req_stride : 0) + static_cast<size_t>(hk) * S_cap * D;
-
-  for (int e = tid; e < D; e += blockDim.x) qs[e] = valid ? to_f32(q[static_cast<size_t>(r) * ldq + h * D + e]) : 0.f;
-  __syncthreads();
-
-  const float scale = sqrtf(static_cast<float>(D));
-  float m = -INFINITY, l = 0.f;
-  // PV layout: G = blockDim / D groups of D threads; thread (grp, e).
-  const int G = blockDim.x / D;
-  const int grp = tid / D, e = tid % D;
-  float acc = 0.f;
-
-  for (int t0 = j0; t0 < j1; t0 += blockDim.x) {
-    const int j = t0 + tid;
-    float s = -INFINITY;
-    if (j < j1) {
-      const KT *kr = kbase + static_cast<size_t>(j) * D;
-      float dot = 0.f;
-      for (int c = 0; c < D; ++c) dot = fmaf(qs[c], to_f32(kr[c]), dot);
-      s = __fdiv_rn(dot, scale);
-    }
-    const float tmax = block_max(s, red);
-    const float mnew = fmaxf(m, tmax);
-    const float p = (j < j1) ? expf(s - mnew) : 0.f;
-    sc[tid] = p;
-    const float psum = block_sum(p, red);  // includes a __syncthreads after sc writes
-    const float alpha = (m == -INFINITY) ? 0.f : expf(m - mnew);
-    l = l * alpha + psum;
-    m = mnew;
-    acc *= alpha;
-    const int nt = min(static_cast<int>(blockDim.x), j1 - t0);
-    if (grp < G) {
-      for (int t = grp; t < nt; t += G) acc = fmaf(sc[t], to_f32(vbase[static_cast<size_t>(t0 + t) * D + e]), acc);
     }
     __syncthreads();
-  }
-  // merge the G groups
-  accs[tid] = acc;
-  __syncthreads();
-  if (tid < D) {
-    float a = 0.f;
-    for (int g2 = 0; g2 < G; ++g2) a += accs[g2 * D + tid];
-    if (nsplit == 1) {
-      if (valid) out[static_cast<size_t>(r) * ldo + h * D + tid] = from_f32<AT>(l > 0.f ? a / l : 0.f);
-    } else {
-      float *pp = part + ((static_cast<size_t>(r) * H + h) * nsplit + split) * (D + 2);
-      pp[2 + tid] = a;
-      if (tid == 0) { pp[0] = m; pp[1] = l; }
-    }
-  }
-}
-
-template <typename AT>
-__global__ void attn_combine_kernel(const float *__restrict__ part, RowsView rows, int R, int H, int D,
-                                    int nsplit, AT *__restrict__ out, int ldo) {
-  const int r = blockIdx.x, h = blockIdx.y;
-  if (rows.req[r] < 0) return;
-  const float *pp = part + (static_cast<size_t>(r) * H + h) * nsplit * (D + 2);
-  float M = -INFINITY;
-  for (int s = 0; s < nsplit; ++s)
-    if (pp[s * (D + 2) + 1] > 0.f) M = fmaxf(M, pp[s * (D + 2)]);
-  for (int e = threadIdx.x; e < D; e += blockDim.x) {
-    float L = 0.f, A = 0.f;
-    for (int s = 0; s < nsplit; ++s) {
-      const float *ps = pp + s * (D + 2);
-      if (ps[1] > 0.f) {
-        const float w = expf(ps[0] - M);
-        L += ps[1] * w;
-        A += ps[2 + e] * w;
+    if (kidx == 0) {
+#pragma unroll
+      for (int i = 0; i < kRowTile; ++i) {
+        float t0 = 0.f, t1 = 0.f;
+        for (int j = 0; j < ks; ++j) {
+          t0 += s_red[warp + j][2 * i];
+          t1 += s_red[warp + j][2 * i + 1];
+        }
+        acc0[i] = t0;
+        acc1[i] = t1;
       }
     }
-    out[static_cast<size_t>(r) * ldo + h * D + e] = from_f32<AT>(L > 0.f ? A / L : 0.f);
+  }
+  if (col_ok && kidx == 0) {
+#pragma unroll
+    for (int i = 0; i < kRowTile; ++i)
+      if (lane == i && i < nrows) linear_epilogue<AT, EPI>(a, r0 + i, n0, acc0[i], acc1[i], pre);
+  }
+  if (!a.ln_out) return;
+  // the last block of this row tile normalises the finished rows
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int *cnt = a.tile_counters + blockIdx.y;
+    const int prev = atomicAdd(cnt, 1);
+    s_last = (prev == static_cast<int>(gridDim.x) - 1) ? 1 : 0;
+    if (s_last) *cnt = 0;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  rows_layernorm<AT>(static_cast<const AT *>(a.out), a.ldo, r0, nrows, a.N, a.ln_g, a.ln_b, static_cast<AT *>(a.ln_out));
+}
+
+// ---------------------------------------------------------------------------
+// Causal attention (src/nn/layer.cpp:859-948): score = (q . k) / sqrt(D)
+// (layer.cpp:870, 891-897), softmax over positions j <= pos, then P.V.
+//
+// The rows of one request in one forward pass are consecutive and form a
+// "group" of Q queries (the k+1 verify rows, the catch-up + last draft rows,
+// a prefill chunk); a block handles up to QT queries of one group for one head
+// and one split of the context, so the request's K/V are read once for all of
+// them.  K/V arrive in tiles of kAttnTile positions that one thread copies
+// into shared memory with TMA bulk copies (cp.async.bulk, completion on an
+// mbarrier; a (request, head) tile is contiguous in the cache), double
+// buffered so the next tile streams in while the current one is used.  Warp w
+// owns tile positions w*32 .. w*32+31 (one per lane) and keeps an online
+// softmax per query; P.V is accumulated with lanes owning head dimensions.
+// Warps are merged through shared memory.  With several splits each block
+// writes (max, sum, acc[D]) partials and the last block of a (query tile,
+// head) merges them (log-sum-exp), so no separate combine kernel runs.
+constexpr int kAttnThreads = 128;
+constexpr int kAttnWarps = kAttnThreads / 32;
+constexpr int kAttnQT = 8;  // queries per block
+
+// Positions per shared-memory tile: 128 (one per thread), or 64 when a K/V
+// row is wider than 256 bytes so two stages of K and V stay within 128 KiB.
+template <typename KT, int D>
+constexpr int attn_tile() { return (D * sizeof(KT) > 256) ? 64 : 128; }
+
+struct AttnArgs {
+  const void *q;
+  int ldq;
+  RowsView rows;
+  int R, Q;                 // rows, queries per group
+  const void *kc, *vc;
+  size_t kv_req_stride;
+  int S_cap, H, Hkv;
+  int chunk, nsplit;
+  void *out;
+  int ldo;
+  float *part;              // [R][H][nsplit][D + 2]
+  int *counters;            // [R][H] split arrival counters (left at 0)
+  int *err;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Polls an mbarrier phase a bounded number of times; false = gave up.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t phase) {
+  const uint32_t addr = smem_u32(bar);
+  for (int it = 0; it < (1 << 22); ++it) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(addr), "r"(phase)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+// One bulk copy global -> this CTA's shared memory (no multicast), completing
+// `bytes` (multiple of 16, both addresses 16-byte aligned) on `bar`.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+template <typename KT, int D>
+constexpr int attn_smem_bytes() {
+  return 2 /*stages*/ * 2 /*K,V*/ * attn_tile<KT, D>() * D * static_cast<int>(sizeof(KT));
+}
+
+template <typename AT, typename KT, int D>
+__global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a) {
+  constexpr int QT = kAttnQT;
+  constexpr int DC = (D + 31) / 32;  // dims per lane in P.V
+  constexpr bool kBulk = (D * sizeof(KT)) % 16 == 0;
+  constexpr int kAttnTile = attn_tile<KT, D>();
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  KT *tiles = reinterpret_cast<KT *>(smem_raw);  // [stage][K|V][kAttnTile][D]
+  __shared__ float qs[QT][D];
+  __shared__ float s_m[kAttnWarps][QT], s_l[kAttnWarps][QT];
+  __shared__ float s_acc[kAttnWarps][QT][D];
+  __shared__ int s_pos[QT], s_req[QT], s_last;
+  __shared__ __align__(8) uint64_t bars[2];
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int ngt = (a.Q + QT - 1) / QT;
+  const int g = blockIdx.x / ngt, qt = blockIdx.x % ngt;
+  const int h = blockIdx.y, split = blockIdx.z;
+  const int rq0 = g * a.Q + qt * QT;
+  const int nq = max(0, min(QT, min(a.Q - qt * QT, a.R - rq0)));
+
+  // query metadata and vectors, all loads in parallel
+  if (threadIdx.x < QT) {
+    const int i = threadIdx.x;
+    const int rr = (i < nq) ? a.rows.req[rq0 + i] : -1;
+    s_req[i] = rr;
+    s_pos[i] = (rr >= 0) ? a.rows.pos[rq0 + i] : -1;
+  }
+  for (int idx = threadIdx.x; idx < QT * D; idx += blockDim.x) {
+    const int i = idx / D, e = idx % D;
+    qs[i][e] = (i < nq) ? to_f32(static_cast<const AT *>(a.q)[static_cast<size_t>(rq0 + i) * a.ldq + h * D + e]) : 0.f;
+  }
+  if (kBulk && threadIdx.x == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&bars[0])) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&bars[1])) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  int req = -1, maxpos = -1;
+#pragma unroll
+  for (int i = 0; i < QT; ++i)
+    if (s_req[i] >= 0) {
+      req = s_req[i];
+      maxpos = max(maxpos, s_pos[i]);
+    }
+  if (req < 0 || maxpos >= a.S_cap) return;  // uniform over the block
+
+  const int ctx = maxpos + 1;
+  const int j0 = split * a.chunk, j1 = min(ctx, j0 + a.chunk);
+  const int hk = h / (a.H / a.Hkv);
+  const KT *kb = static_cast<const KT *>(a.kc) + static_cast<size_t>(req) * a.kv_req_stride + static_cast<size_t>(hk) * a.S_cap * D;
+  const KT *vb = static_cast<const KT *>(a.vc) + static_cast<size_t>(req) * a.kv_req_stride + static_cast<size_t>(hk) * a.S_cap * D;
+  const float scale = sqrtf(static_cast<float>(D));
+
+  float m[QT], l[QT], acc[QT][DC];
+  int qpos[QT];
+#pragma unroll
+  for (int i = 0; i < QT; ++i) {
+    m[i] = -INFINITY;
+    l[i] = 0.f;
+    qpos[i] = s_pos[i];
+#pragma unroll
+    for (int c = 0; c < DC; ++c) acc[i][c] = 0.f;
+  }
+
+  const int ntiles = (j1 > j0) ? (j1 - j0 + kAttnTile - 1) / kAttnTile : 0;
+  auto issue = [&](int t) {  // thread 0 only
+    const int t0 = j0 + t * kAttnTile;
+    const int nt = min(kAttnTile, j1 - t0);
+    KT *kt = tiles + (t & 1) * 2 * kAttnTile * D;
+    const uint32_t bytes = static_cast<uint32_t>(nt * D * sizeof(KT));
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&bars[t & 1])), "r"(2 * bytes)
+                 : "memory");
+    bulk_g2s(kt, kb + static_cast<size_t>(t0) * D, bytes, &bars[t & 1]);
+    bulk_g2s(kt + kAttnTile * D, vb + static_cast<size_t>(t0) * D, bytes, &bars[t & 1]);
+  };
+  if (kBulk && threadIdx.x == 0 && ntiles > 0) issue(0);
+  bool ok = true;
+  for (int t = 0; t < ntiles; ++t) {
+    const int t0 = j0 + t * kAttnTile;
+    const int nt = min(kAttnTile, j1 - t0);
+    KT *ktile = tiles + (t & 1) * 2 * kAttnTile * D;
+    KT *vtile = ktile + kAttnTile * D;
+    if constexpr (kBulk) {
+      if (threadIdx.x == 0 && t + 1 < ntiles) issue(t + 1);  // the other stage was released at the end of t-1
+      ok = __syncthreads_and(mbar_wait(&bars[t & 1], (t >> 1) & 1) ? 1 : 0) != 0;
+      if (!ok) break;
+    } else {
+      for (int idx = threadIdx.x; idx < nt * D; idx += blockDim.x) {
+        ktile[idx] = kb[static_cast<size_t>(t0) * D + idx];
+        vtile[idx] = vb[static_cast<size_t>(t0) * D + idx];
+      }
+      __syncthreads();
+    }
+    // scores: lane = position; the dot product walks the head dimension
+    // rotated by the lane so the 32 lanes read 32 different banks
+    const int tp = warp * 32 + lane;
+    const int pos = t0 + tp;
+    float p[QT];
+    {
+      float kr[D];
+      if (tp < nt) {
+#pragma unroll
+        for (int c = 0; c < D; ++c) kr[c] = to_f32(ktile[tp * D + ((c + lane) % D)]);
+      }
+#pragma unroll
+      for (int i = 0; i < QT; ++i) {
+        float s = -INFINITY;
+        if (i < nq && tp < nt && pos <= qpos[i]) {
+          float dot = 0.f;
+#pragma unroll
+          for (int c = 0; c < D; ++c) dot = fmaf(qs[i][(c + lane) % D], kr[c], dot);
+          s = __fdiv_rn(dot, scale);
+        }
+        const float tmax = warp_max(s);
+        const float mnew = fmaxf(m[i], tmax);
+        p[i] = (s == -INFINITY) ? 0.f : expf(s - mnew);
+        const float alpha = (m[i] == -INFINITY) ? 0.f : expf(m[i] - mnew);
+        l[i] = l[i] * alpha + warp_sum(p[i]);
+#pragma unroll
+        for (int c = 0; c < DC; ++c) acc[i][c] *= alpha;
+        m[i] = mnew;
+      }
+    }
+    const int nvalid = max(0, min(32, nt - warp * 32));
+    for (int pp = 0; pp < nvalid; ++pp) {
+      float vv[DC];
+#pragma unroll
+      for (int c = 0; c < DC; ++c) {
+        const int e = lane + 32 * c;
+        vv[c] = (e < D) ? to_f32(vtile[(warp * 32 + pp) * D + e]) : 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < QT; ++i) {
+        const float pb = __shfl_sync(0xffffffffu, p[i], pp);
+#pragma unroll
+        for (int c = 0; c < DC; ++c) acc[i][c] = fmaf(pb, vv[c], acc[i][c]);
+      }
+    }
+    __syncthreads();  // this stage is refilled two tiles later
+  }
+  if (!ok) {
+    if (threadIdx.x == 0 && a.err) atomicOr(a.err, kErrTimeout);
+    return;  // uniform: decided by the block vote
+  }
+  // merge the block's warps
+  if (lane == 0) {
+#pragma unroll
+    for (int i = 0; i < QT; ++i) {
+      s_m[warp][i] = m[i];
+      s_l[warp][i] = l[i];
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < QT; ++i)
+#pragma unroll
+    for (int c = 0; c < DC; ++c) {
+      const int e = lane + 32 * c;
+      if (e < D) s_acc[warp][i][e] = acc[i][c];
+    }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < nq * D; idx += blockDim.x) {
+    const int i = idx / D, e = idx % D;
+    if (s_pos[i] < 0) continue;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, s_m[w][i]);
+    float L = 0.f, A = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) {
+      if (s_m[w][i] == -INFINITY) continue;
+      const float f = expf(s_m[w][i] - M);
+      L += s_l[w][i] * f;
+      A += s_acc[w][i][e] * f;
+    }
+    const int r = rq0 + i;
+    if (a.nsplit == 1) {
+      static_cast<AT *>(a.out)[static_cast<size_t>(r) * a.ldo + h * D + e] = from_f32<AT>(L > 0.f ? A / L : 0.f);
+    } else {
+      float *pp = a.part + ((static_cast<size_t>(r) * a.H + h) * a.nsplit + split) * (D + 2);
+      pp[2 + e] = A;
+      if (e == 0) {
+        pp[0] = M;
+        pp[1] = L;
+      }
+    }
+  }
+  if (a.nsplit == 1) return;
+  // the last block of this (query tile, head) to arrive merges the splits
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int *cnt = a.counters + static_cast<size_t>(rq0) * a.H + h;
+    const int prev = atomicAdd(cnt, 1);
+    s_last = (prev == a.nsplit - 1) ? 1 : 0;
+    if (s_last) *cnt = 0;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int idx = threadIdx.x; idx < nq * D; idx += blockDim.x) {
+    const int i = idx / D, e = idx % D;
+    if (s_pos[i] < 0) continue;
+    const int r = rq0 + i;
+    const float *pp = a.part + (static_cast<size_t>(r) * a.H + h) * a.nsplit * (D + 2);
+    float M = -INFINITY;
+    for (int s = 0; s < a.nsplit; ++s)
+      if (__ldcg(pp + s * (D + 2) + 1) > 0.f) M = fmaxf(M, __ldcg(pp + s * (D + 2)));
+    float L = 0.f, A = 0.f;
+    for (int s = 0; s < a.nsplit; ++s) {
+      const float *ps = pp + s * (D + 2);
+      const float ls = __ldcg(ps + 1);
+      if (ls > 0.f) {
+        const float w = expf(__ldcg(ps) - M);
+        L += ls * w;
+        A += __ldcg(ps + 2 + e) * w;
+      }
+    }
+    static_cast<AT *>(a.out)[static_cast<size_t>(r) * a.ldo + h * D + e] = from_f32<AT>(L > 0.f ? A / L : 0.f);
   }
 }
 

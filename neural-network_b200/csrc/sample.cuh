@@ -64,6 +64,17 @@ __device__ __forceinline__ float canon_f32(uint32_t g) {
 }
 
 // ---------------------------------------------------------------------------
+// Row tables: one pool of (token, position, request) triples with fixed
+// regions for the prefill chunk, draft step 0 (two rows per request: the
+// catch-up token and the last token), draft steps 1..k-1 (one row per
+// request) and the verify block (k+1 rows per request).  The sampling kernels
+// write the rows of the next forward pass directly, so no planning kernel
+// runs between them.
+struct RowPool {
+  int *tok, *pos, *req;
+  int off_step0, off_step1, off_verify;  // region offsets (the prefill region is at 0)
+};
+
 struct SpecState {
   int *tokens_out;     // [B][out_len]
   int out_len;
@@ -71,16 +82,16 @@ struct SpecState {
   int *n_new;          // [B]
   int *t_len, *d_len;  // cache lengths
   int *t_start, *d_start;
-  int *last_tok, *catch_tok, *active, *M;
+  int *last_tok, *active, *M;
   int *cand;           // [B][kmax]
-  float *q;            // [B][kmax][V]
-  float *pbuf;         // [B][V]
+  float *q;            // [B][kmax][V] draft probabilities
   long long *stats;    // [B][4]
   int *round;          // [B]
   uint32_t *mt;        // [B][624]
   int *mt_idx;         // [B]
   int *active_count;
   int *err;
+  RowPool rows;
   int B, kmax, V;
   int max_new, k;
   float T;
@@ -91,6 +102,51 @@ struct SpecState {
   int catchup;         // 0 reference, 1 consistent
   int t_cap, d_cap;
 };
+
+__device__ __forceinline__ void set_row(const SpecState &st, int idx, int tok, int pos, int req) {
+  st.rows.tok[idx] = (tok >= 0 && tok < st.V) ? tok : 0;  // an out-of-range id embeds as row 0
+  st.rows.pos[idx] = pos;
+  st.rows.req[idx] = req;
+}
+__device__ __forceinline__ void clear_row(const SpecState &st, int idx) { set_row(st, idx, 0, 0, -1); }
+__device__ __forceinline__ int step_row(const SpecState &st, int j, int b) {
+  return j == 0 ? st.rows.off_step0 + 2 * b + 1 : st.rows.off_step1 + (j - 1) * st.B + b;
+}
+__device__ __forceinline__ int verify_row(const SpecState &st, int b, int i) {
+  return st.rows.off_verify + b * (st.k + 1) + i;
+}
+
+// Every row of request b unused (the request finished or failed).
+__device__ void clear_request_rows(const SpecState &st, int b) {
+  clear_row(st, st.rows.off_step0 + 2 * b);
+  clear_row(st, st.rows.off_step0 + 2 * b + 1);
+  for (int j = 1; j < st.k; ++j) clear_row(st, step_row(st, j, b));
+  for (int i = 0; i <= st.k; ++i) clear_row(st, verify_row(st, b, i));
+}
+
+// Draft step 0 rows of the coming round: [catch-up (if any), last token].
+// Folding the reference's post-round draft catch-up forward
+// (src/nn/layer.cpp:1639-1642, 1649-1653) into the next round's first draft
+// step computes the same cache and the same logits for the last row.  Returns
+// false (and flags the error) when the round would overflow a cache.
+__device__ bool start_round(const SpecState &st, int b, int catch_tok) {
+  const int M = min(st.k, st.max_new - st.n_new[b]);
+  int d = st.d_len[b];
+  const int has_c = catch_tok >= 0 ? 1 : 0;
+  if (d + has_c + M > st.d_cap || st.t_len[b] + M + 1 > st.t_cap) {
+    atomicOr(st.err, kErrSeqLen);
+    st.active[b] = 0;
+    clear_request_rows(st, b);
+    return false;
+  }
+  if (has_c) set_row(st, st.rows.off_step0 + 2 * b, catch_tok, d++, b);
+  else clear_row(st, st.rows.off_step0 + 2 * b);
+  st.d_start[b] = d;
+  set_row(st, st.rows.off_step0 + 2 * b + 1, st.last_tok[b], d, b);
+  st.d_len[b] = d + 1;
+  st.M[b] = M;
+  return true;
+}
 
 struct RngCtx {
   uint32_t *old_s, *new_s;  // shared [624] each
@@ -157,35 +213,63 @@ __device__ __forceinline__ float draw_accept_u(const SpecState &st, int b, int r
 }
 
 // ---------------------------------------------------------------------------
-// get_probs for T > 0 without top-k/top-p (src/nn/layer.cpp:1426-1489):
-// l/T, subtract the max, exp, divide by the sum, then divide by the sum of the
-// normalised values (the reference's second normalisation, taken there in
-// sorted order).  Writes out[V]; block-cooperative.
-__device__ void probs_row(const float *__restrict__ lg, int V, float T, float *__restrict__ out, float *red) {
-  float mx = -INFINITY;
-  for (int v = threadIdx.x; v < V; v += blockDim.x) mx = fmaxf(mx, __fdiv_rn(lg[v], T));
-  mx = block_max(mx, red);
-  float s = 0.f;
-  for (int v = threadIdx.x; v < V; v += blockDim.x) {
-    const float e = expf(__fsub_rn(__fdiv_rn(lg[v], T), mx));
-    out[v] = e;
-    s += e;
+// The sampling kernels keep the vocabulary row they work on in dynamic shared
+// memory (V floats): one coalesced load, then every pass is on-chip.
+__device__ void load_row(const float *__restrict__ g, int V, float *srow) {
+  if ((V & 3) == 0 && (reinterpret_cast<uintptr_t>(g) & 15) == 0) {
+    const float4 *g4 = reinterpret_cast<const float4 *>(g);
+    float4 *s4 = reinterpret_cast<float4 *>(srow);
+#pragma unroll 4
+    for (int v = threadIdx.x; v < V / 4; v += blockDim.x) s4[v] = __ldg(g4 + v);
+  } else {
+    for (int v = threadIdx.x; v < V; v += blockDim.x) srow[v] = g[v];
   }
-  s = block_sum(s, red);
-  float fs = 0.f;
-  for (int v = threadIdx.x; v < V; v += blockDim.x) {
-    const float p = __fdiv_rn(out[v], s);
-    out[v] = p;
-    fs += p;
-  }
-  fs = block_sum(fs, red);
-  for (int v = threadIdx.x; v < V; v += blockDim.x) out[v] = __fdiv_rn(out[v], fs);
   __syncthreads();
 }
 
-__device__ int argmax_row(const float *__restrict__ lg, int V, float *redv, int *redi) {
+__device__ void store_row(const float *srow, int V, float *__restrict__ g) {
+  if ((V & 3) == 0 && (reinterpret_cast<uintptr_t>(g) & 15) == 0) {
+    const float4 *s4 = reinterpret_cast<const float4 *>(srow);
+    float4 *g4 = reinterpret_cast<float4 *>(g);
+    for (int v = threadIdx.x; v < V / 4; v += blockDim.x) g4[v] = s4[v];
+  } else {
+    for (int v = threadIdx.x; v < V; v += blockDim.x) g[v] = srow[v];
+  }
+}
+
+// get_probs for T > 0 without top-k/top-p (src/nn/layer.cpp:1426-1489), in
+// place on a shared-memory row: l/T, subtract the max, exp, divide by the
+// sum, then divide by the sum of the normalised values (the reference's
+// second normalisation, taken there in sorted order).  Max and exp-sum come
+// from one pass with a per-thread running maximum.
+__device__ void probs_smem(float *srow, int V, float T, float *red) {
+  float mx = -INFINITY, se = 0.f;
+  for (int v = threadIdx.x; v < V; v += blockDim.x) {
+    const float x = __fdiv_rn(srow[v], T);
+    srow[v] = x;
+    if (x > mx) {
+      se = se * expf(mx - x) + 1.f;
+      mx = x;
+    } else {
+      se += expf(x - mx);
+    }
+  }
+  const float M = block_max(mx, red);
+  const float s = block_sum(mx == -INFINITY ? 0.f : se * expf(mx - M), red);
+  float fs = 0.f;
+  for (int v = threadIdx.x; v < V; v += blockDim.x) {
+    const float p = __fdiv_rn(expf(__fsub_rn(srow[v], M)), s);
+    srow[v] = p;
+    fs += p;
+  }
+  fs = block_sum(fs, red);
+  for (int v = threadIdx.x; v < V; v += blockDim.x) srow[v] = __fdiv_rn(srow[v], fs);
+  __syncthreads();
+}
+
+__device__ int argmax_smem(const float *srow, int V, float *redv, int *redi) {
   ArgMax a{-INFINITY, 0x7fffffff};
-  for (int v = threadIdx.x; v < V; v += blockDim.x) a = argmax_merge(a, ArgMax{lg[v], v});
+  for (int v = threadIdx.x; v < V; v += blockDim.x) a = argmax_merge(a, ArgMax{srow[v], v});
   a = block_argmax(a, redv, redi);
   return a.i == 0x7fffffff ? 0 : a.i;
 }
@@ -195,7 +279,7 @@ __device__ int argmax_row(const float *__restrict__ lg, int V, float *redv, int 
 //    normalised weights, the last forced to 1, first index with cum >= u;
 //  mode 1 (host table): first index whose fp64 running sum exceeds u * total.
 // `u` must be the same value in every thread.
-__device__ int sample_row(const float *__restrict__ p, int V, double u, int mode, double *redd, int *redi) {
+__device__ int sample_smem(const float *p, int V, double u, int mode, double *redd, int *redi) {
   const int C = (V + blockDim.x - 1) / blockDim.x;
   const int lo = min(V, static_cast<int>(threadIdx.x) * C), hi = min(V, lo + C);
   double loc = 0.0;
@@ -211,9 +295,11 @@ __device__ int sample_row(const float *__restrict__ p, int V, double u, int mode
   for (int v = lo; v < hi; ++v) {
     cum += static_cast<double>(p[v]);
     const bool hit = (mode == 0) ? (v == V - 1 || cum / total >= u) : (cum > thr);
-    if (hit) { pick = v; break; }
+    if (hit) {
+      pick = v;
+      break;
+    }
   }
-  // block min of pick, block max of last_nz
   __syncthreads();
   int m = pick;
 #pragma unroll
@@ -222,7 +308,10 @@ __device__ int sample_row(const float *__restrict__ p, int V, double u, int mode
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) lz = max(lz, __shfl_xor_sync(0xffffffffu, lz, o));
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
-  if (lane == 0) { redi[wid] = m; redi[32 + wid] = lz; }
+  if (lane == 0) {
+    redi[wid] = m;
+    redi[32 + wid] = lz;
+  }
   __syncthreads();
   m = (lane < nw) ? redi[lane] : 0x7fffffff;
   lz = (lane < nw) ? redi[32 + lane] : -1;
@@ -249,7 +338,6 @@ struct SampShared {
   int used;
   double u;
   int flag;
-  int tok;
 };
 
 __device__ __forceinline__ RngCtx make_rng(SampShared &s) { return RngCtx{s.old_s, s.new_s, s.win, &s.used}; }
@@ -261,7 +349,7 @@ __device__ __forceinline__ void emit(const SpecState &st, int b, int tok) {
 }
 
 // ---------------------------------------------------------------------------
-// Request setup: prompt copy and fresh counters (one thread per request).
+// Request setup: prompt copy, fresh counters, all rows unused.
 __global__ void init_state_kernel(SpecState st, const int *__restrict__ prompts, int S) {
   const int b = blockIdx.x;
   if (b >= st.B) return;
@@ -274,150 +362,115 @@ __global__ void init_state_kernel(SpecState st, const int *__restrict__ prompts,
     st.t_start[b] = S;
     st.d_start[b] = S;
     st.last_tok[b] = 0;
-    st.catch_tok[b] = -1;
     st.active[b] = 1;
     st.M[b] = 0;
     st.round[b] = 0;
     for (int i = 0; i < 4; ++i) st.stats[4 * b + i] = 0;
     if (S > st.t_cap || S > st.d_cap) atomicOr(st.err, kErrSeqLen);
+    clear_request_rows(st, b);
   }
 }
 
-// Prefill rows of one chunk [c0, c0 + clen) of every prompt; row b*clen + i.
-__global__ void plan_prefill_kernel(const int *__restrict__ prompts, int B, int S, int c0, int clen, int *rtok,
+// Prefill rows of one chunk [c0, c0 + clen) of every prompt (row b*clen + i)
+// and the head's row selection (the last row of each request).
+__global__ void plan_prefill_kernel(const int *__restrict__ prompts, int B, int S, int c0, int clen, int V, int *rtok,
                                     int *rpos, int *rreq, int *sel) {
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= B * clen) return;
   const int b = r / clen, i = r % clen;
-  rtok[r] = prompts[static_cast<size_t>(b) * S + c0 + i];
+  const int t = prompts[static_cast<size_t>(b) * S + c0 + i];
+  rtok[r] = (t >= 0 && t < V) ? t : 0;
   rpos[r] = c0 + i;
   rreq[r] = b;
-  if (i == clen - 1) sel[b] = r;
+  if (sel && i == clen - 1) sel[b] = r;
 }
 
-// First new token from the target's prefill logits (src/nn/layer.cpp:1500-1510).
+// First new token from the target's prefill logits (src/nn/layer.cpp:1500-1510),
+// then the rows of the first round's draft step 0.
 __global__ void __launch_bounds__(kSampThreads) first_token_kernel(SpecState st, const float *__restrict__ logits) {
   __shared__ SampShared sh;
+  extern __shared__ float srow[];  // [V]
   const int b = blockIdx.x;
   RngCtx rc = make_rng(sh);
-  const float *lg = logits + static_cast<size_t>(b) * st.V;
+  load_row(logits + static_cast<size_t>(b) * st.V, st.V, srow);
   int tok;
   if (st.greedy) {
-    tok = argmax_row(lg, st.V, sh.redv, sh.redi);
+    tok = argmax_smem(srow, st.V, sh.redv, sh.redi);
   } else {
     rng_prepare(st, b, 2, rc);
-    float *p = st.pbuf + static_cast<size_t>(b) * st.V;
-    probs_row(lg, st.V, st.T, p, sh.red);
+    probs_smem(srow, st.V, st.T, sh.red);
     if (threadIdx.x == 0) sh.u = draw_sample_u(st, b, 0, 2 * st.k, rc);
     __syncthreads();
-    tok = sample_row(p, st.V, sh.u, st.rng_mode, sh.redd, sh.redi);
+    tok = sample_smem(srow, st.V, sh.u, st.rng_mode, sh.redd, sh.redi);
     rng_commit(st, b, rc);
   }
   if (threadIdx.x == 0) {
     emit(st, b, tok);
     st.last_tok[b] = tok;
-    st.active[b] = st.n_new[b] < st.max_new ? 1 : 0;
     st.round[b] = 1;
-  }
-}
-
-// Draft step 0 rows: [catch-up token (if any), last token] per request at rows
-// 2b, 2b+1.  Folding the reference's post-round draft catch-up forward
-// (src/nn/layer.cpp:1639-1642, 1649-1653) into the next round's first draft
-// step computes the same cache and the same logits for the last row.
-__global__ void plan_draft0_kernel(SpecState st, int *rtok, int *rpos, int *rreq, int *sel) {
-  const int b = blockIdx.x * blockDim.x + threadIdx.x;
-  if (b == 0) *st.active_count = 0;
-  if (b >= st.B) return;
-  int r0 = 2 * b, r1 = 2 * b + 1;
-  sel[b] = r1;
-  rreq[r0] = -1; rtok[r0] = 0; rpos[r0] = 0;
-  rreq[r1] = -1; rtok[r1] = 0; rpos[r1] = 0;
-  if (!st.active[b]) { st.M[b] = 0; return; }
-  const int M = min(st.k, st.max_new - st.n_new[b]);
-  st.M[b] = M;
-  const int c = st.catch_tok[b];
-  int d = st.d_len[b];
-  if (d + (c >= 0 ? 1 : 0) + M > st.d_cap) {
-    atomicOr(st.err, kErrSeqLen);
-    st.active[b] = 0;
-    st.M[b] = 0;
-    return;
-  }
-  if (c >= 0) { rtok[r0] = c; rpos[r0] = d; rreq[r0] = b; ++d; }
-  st.d_start[b] = d;
-  rtok[r1] = st.last_tok[b]; rpos[r1] = d; rreq[r1] = b;
-  st.d_len[b] = d + 1;
-  st.catch_tok[b] = -1;
-}
-
-// Draft step j >= 1: row b feeds candidate j-1.
-__global__ void plan_draft_kernel(SpecState st, int j, int *rtok, int *rpos, int *rreq, int *sel) {
-  const int b = blockIdx.x * blockDim.x + threadIdx.x;
-  if (b >= st.B) return;
-  sel[b] = b;
-  if (!st.active[b] || j >= st.M[b]) { rreq[b] = -1; rtok[b] = 0; rpos[b] = 0; return; }
-  const int d = st.d_len[b];
-  rtok[b] = st.cand[b * st.kmax + j - 1];
-  rpos[b] = d;
-  rreq[b] = b;
-  st.d_len[b] = d + 1;
-}
-
-// Verify rows b*(k+1) + i: [last, c_0 .. c_{M-1}] at t_len + i
-// (src/nn/layer.cpp:1560-1567).  One thread per request.
-__global__ void plan_verify_kernel(SpecState st, int *rtok, int *rpos, int *rreq) {
-  const int b = blockIdx.x * blockDim.x + threadIdx.x;
-  if (b >= st.B) return;
-  const int W = st.k + 1;
-  const int M = st.M[b];
-  bool on = st.active[b] != 0;
-  const int t = st.t_len[b];
-  if (on && t + M + 1 > st.t_cap) {
-    atomicOr(st.err, kErrSeqLen);
-    on = false;
-  }
-  for (int i = 0; i < W; ++i) {
-    const int r = b * W + i;
-    const bool ri = on && i <= M;
-    rreq[r] = ri ? b : -1;
-    rtok[r] = ri ? (i == 0 ? st.last_tok[b] : st.cand[b * st.kmax + i - 1]) : 0;
-    rpos[r] = ri ? t + i : 0;
-  }
-  if (on) {
-    st.t_start[b] = t;
-    st.t_len[b] = t + M + 1;
+    const bool more = st.n_new[b] < st.max_new;
+    st.active[b] = more ? 1 : 0;
+    if (more) start_round(st, b, -1);
   }
 }
 
 // Draft sample after draft step j (src/nn/layer.cpp:1541-1558): q_j =
-// get_probs(draft logits), candidate j = sample_token(q_j).
+// get_probs(draft logits), candidate j = sample_token(q_j).  Writes the rows
+// of draft step j+1, and after the last draft step the verify rows
+// [last, c_0 .. c_{M-1}] at t_len + i (src/nn/layer.cpp:1560-1567).
 __global__ void __launch_bounds__(kSampThreads) draft_sample_kernel(SpecState st, int j, const float *__restrict__ logits) {
   __shared__ SampShared sh;
+  extern __shared__ float srow[];  // [V]
   const int b = blockIdx.x;
-  if (!st.active[b] || j >= st.M[b]) return;
+  if (!st.active[b]) return;
+  const int M = st.M[b];
+  if (j >= M) {
+    if (threadIdx.x == 0 && j + 1 < st.k) clear_row(st, step_row(st, j + 1, b));
+    return;
+  }
   RngCtx rc = make_rng(sh);
-  const float *lg = logits + static_cast<size_t>(b) * st.V;
+  load_row(logits + static_cast<size_t>(b) * st.V, st.V, srow);
   int tok;
   if (st.greedy) {
-    tok = argmax_row(lg, st.V, sh.redv, sh.redi);
+    tok = argmax_smem(srow, st.V, sh.redv, sh.redi);
   } else {
     rng_prepare(st, b, 2, rc);
-    float *q = st.q + (static_cast<size_t>(b) * st.kmax + j) * st.V;
-    probs_row(lg, st.V, st.T, q, sh.red);
+    probs_smem(srow, st.V, st.T, sh.red);
+    store_row(srow, st.V, st.q + (static_cast<size_t>(b) * st.kmax + j) * st.V);  // q_j, read by accept
     if (threadIdx.x == 0) sh.u = draw_sample_u(st, b, st.round[b], j, rc);
     __syncthreads();
-    tok = sample_row(q, st.V, sh.u, st.rng_mode, sh.redd, sh.redi);
+    tok = sample_smem(srow, st.V, sh.u, st.rng_mode, sh.redd, sh.redi);
     rng_commit(st, b, rc);
   }
-  if (threadIdx.x == 0) st.cand[b * st.kmax + j] = tok;
+  if (threadIdx.x == 0) {
+    int *cand = st.cand + b * st.kmax;
+    cand[j] = tok;
+    if (j + 1 < M) {
+      const int d = st.d_len[b];
+      set_row(st, step_row(st, j + 1, b), tok, d, b);
+      st.d_len[b] = d + 1;
+    } else if (j + 1 < st.k) {
+      clear_row(st, step_row(st, j + 1, b));
+    }
+    if (j == M - 1) {
+      const int t = st.t_len[b];
+      for (int i = 0; i <= st.k; ++i) {
+        if (i <= M) set_row(st, verify_row(st, b, i), i == 0 ? st.last_tok[b] : cand[i - 1], t + i, b);
+        else clear_row(st, verify_row(st, b, i));
+      }
+      st.t_start[b] = t;
+      st.t_len[b] = t + M + 1;
+    }
+  }
 }
 
 // Acceptance, residual / bonus sample and rollback for one request
 // (src/nn/layer.cpp:1581-1655).  Rollback is a length reset: the cache slots
-// past the new length are simply overwritten by later rows.
+// past the new length are simply overwritten by later rows.  Ends by writing
+// the next round's draft step 0 rows.
 __global__ void __launch_bounds__(kSampThreads) accept_kernel(SpecState st, const float *__restrict__ logits) {
   __shared__ SampShared sh;
+  extern __shared__ float srow[];  // [V]
   const int b = blockIdx.x;
   if (!st.active[b]) return;
   RngCtx rc = make_rng(sh);
@@ -425,7 +478,6 @@ __global__ void __launch_bounds__(kSampThreads) accept_kernel(SpecState st, cons
   const int W = st.k + 1;
   const int round = st.round[b];
   const float *lg0 = logits + static_cast<size_t>(b) * W * st.V;
-  float *p = st.pbuf + static_cast<size_t>(b) * st.V;
   const int *cand = st.cand + b * st.kmax;
   if (!st.greedy) rng_prepare(st, b, st.k + 2, rc);
 
@@ -433,17 +485,17 @@ __global__ void __launch_bounds__(kSampThreads) accept_kernel(SpecState st, cons
   int rj = -1, am_rj = 0, naccept = 0;
   for (int j = 0; j < M; ++j) {
     const int c = cand[j];
-    const float *lg = lg0 + static_cast<size_t>(j) * st.V;
+    load_row(lg0 + static_cast<size_t>(j) * st.V, st.V, srow);
     bool acc;
     if (st.greedy) {
-      const int am = argmax_row(lg, st.V, sh.redv, sh.redi);
+      const int am = argmax_smem(srow, st.V, sh.redv, sh.redi);
       acc = (c == am);
       am_rj = am;
     } else {
-      probs_row(lg, st.V, st.T, p, sh.red);
+      probs_smem(srow, st.V, st.T, sh.red);
       if (threadIdx.x == 0) {
         const float qv = st.q[(static_cast<size_t>(b) * st.kmax + j) * st.V + c];
-        const float pv = p[c];
+        const float pv = srow[c];
         const float r = draw_accept_u(st, b, round, st.k + j, rc);
         sh.flag = (__fmul_rn(r, qv) < pv) ? 1 : 0;
       }
@@ -451,7 +503,10 @@ __global__ void __launch_bounds__(kSampThreads) accept_kernel(SpecState st, cons
       acc = sh.flag != 0;
       __syncthreads();
     }
-    if (!acc) { rj = j; break; }
+    if (!acc) {
+      rj = j;
+      break;
+    }
     ++naccept;
   }
 
@@ -464,44 +519,46 @@ __global__ void __launch_bounds__(kSampThreads) accept_kernel(SpecState st, cons
       const float *q = st.q + (static_cast<size_t>(b) * st.kmax + rj) * st.V;
       float s = 0.f;
       for (int v = threadIdx.x; v < st.V; v += blockDim.x) {
-        const float rv = fmaxf(0.0f, __fsub_rn(p[v], q[v]));
-        p[v] = rv;
+        const float rv = fmaxf(0.0f, __fsub_rn(srow[v], q[v]));
+        srow[v] = rv;
         s += rv;
       }
       s = block_sum(s, sh.red);
       if (s <= 0.0f) {
-        probs_row(lg0 + static_cast<size_t>(rj) * st.V, st.V, st.T, p, sh.red);
+        load_row(lg0 + static_cast<size_t>(rj) * st.V, st.V, srow);
+        probs_smem(srow, st.V, st.T, sh.red);
       } else {
-        for (int v = threadIdx.x; v < st.V; v += blockDim.x) p[v] = __fdiv_rn(p[v], s);
+        for (int v = threadIdx.x; v < st.V; v += blockDim.x) srow[v] = __fdiv_rn(srow[v], s);
         __syncthreads();
       }
       if (threadIdx.x == 0) sh.u = draw_sample_u(st, b, round, 2 * st.k, rc);
       __syncthreads();
-      out_tok = sample_row(p, st.V, sh.u, st.rng_mode, sh.redd, sh.redi);
+      out_tok = sample_smem(srow, st.V, sh.u, st.rng_mode, sh.redd, sh.redi);
     }
   } else if (n0 + naccept < st.max_new) {
-    const float *lg = lg0 + static_cast<size_t>(M) * st.V;
+    load_row(lg0 + static_cast<size_t>(M) * st.V, st.V, srow);
     if (st.greedy) {
-      out_tok = argmax_row(lg, st.V, sh.redv, sh.redi);
+      out_tok = argmax_smem(srow, st.V, sh.redv, sh.redi);
     } else {
-      probs_row(lg, st.V, st.T, p, sh.red);
+      probs_smem(srow, st.V, st.T, sh.red);
       if (threadIdx.x == 0) sh.u = draw_sample_u(st, b, round, 2 * st.k, rc);
       __syncthreads();
-      out_tok = sample_row(p, st.V, sh.u, st.rng_mode, sh.redd, sh.redi);
+      out_tok = sample_smem(srow, st.V, sh.u, st.rng_mode, sh.redd, sh.redi);
     }
   }
   if (!st.greedy) rng_commit(st, b, rc);
   if (threadIdx.x == 0) {
     for (int j = 0; j < naccept; ++j) emit(st, b, cand[j]);
+    int catch_tok = -1;
     if (rj >= 0) {
       emit(st, b, out_tok);
       st.t_len[b] = st.t_start[b] + rj + 1;
       st.d_len[b] = min(st.d_len[b], st.d_start[b] + rj + 1);
-      st.catch_tok[b] = (st.catchup == 0) ? out_tok : -1;
+      catch_tok = (st.catchup == 0) ? out_tok : -1;
       st.last_tok[b] = out_tok;
     } else if (out_tok >= 0) {
       emit(st, b, out_tok);
-      st.catch_tok[b] = cand[M - 1];
+      catch_tok = cand[M - 1];
       st.last_tok[b] = out_tok;
     } else {
       st.last_tok[b] = M > 0 ? cand[M - 1] : st.last_tok[b];
@@ -512,8 +569,10 @@ __global__ void __launch_bounds__(kSampThreads) accept_kernel(SpecState st, cons
     sx[2] += naccept;
     sx[3] += (rj >= 0) ? 1 : 0;
     st.round[b] = round + 1;
-    const int still = st.n_new[b] < st.max_new ? 1 : 0;
-    st.active[b] = still;
+    bool still = st.n_new[b] < st.max_new;
+    if (still) still = start_round(st, b, catch_tok);
+    else clear_request_rows(st, b);
+    st.active[b] = still ? 1 : 0;
     if (still) atomicAdd(st.active_count, 1);
   }
 }
