@@ -416,8 +416,11 @@ void launch_linear(specdec_handle *h, LinearArgs a) {
 
 template <typename AT, typename KT, int D>
 void set_attn_attr() {
-  CK(cudaFuncSetAttribute(attention_kernel<AT, KT, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                          attn_smem_bytes<KT, D>()));
+  const int bytes = attn_smem_bytes<KT, D>();
+  CK(cudaFuncSetAttribute(attention_kernel<AT, KT, D, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  CK(cudaFuncSetAttribute(attention_kernel<AT, KT, D, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  CK(cudaFuncSetAttribute(attention_kernel<AT, KT, D, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  CK(cudaFuncSetAttribute(attention_kernel<AT, KT, D, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
 }
 template <typename AT, typename KT>
 void set_attn_attrs() {
@@ -429,22 +432,31 @@ void set_attn_attrs() {
   set_attn_attr<AT, KT, 128>();
 }
 
+template <typename AT, typename KT, int D>
+void launch_attention_d(specdec_handle *h, const AttnArgs &a, int ngroups) {
+  const int qt = a.Q <= 1 ? 1 : a.Q <= 2 ? 2 : a.Q <= 4 ? 4 : kAttnQT;
+  dim3 grid(ngroups * ((a.Q + qt - 1) / qt), a.H, a.nsplit);
+  dim3 block(kAttnThreads);
+  const size_t smem = static_cast<size_t>(attn_smem_bytes<KT, D>());
+  switch (qt) {
+    case 1: launch(h, attention_kernel<AT, KT, D, 1>, grid, block, smem, a); break;
+    case 2: launch(h, attention_kernel<AT, KT, D, 2>, grid, block, smem, a); break;
+    case 4: launch(h, attention_kernel<AT, KT, D, 4>, grid, block, smem, a); break;
+    default: launch(h, attention_kernel<AT, KT, D, 8>, grid, block, smem, a); break;
+  }
+}
+
 template <typename AT, typename KT>
 void launch_attention_t(specdec_handle *h, const AttnArgs &a, int D, int ngroups) {
-  dim3 grid(ngroups * ((a.Q + kAttnQT - 1) / kAttnQT), a.H, a.nsplit);
-  dim3 block(kAttnThreads);
-#define ATTN_CASE(DD) \
-  case DD: launch(h, attention_kernel<AT, KT, DD>, grid, block, static_cast<size_t>(attn_smem_bytes<KT, DD>()), a); break;
   switch (D) {
-    ATTN_CASE(4)
-    ATTN_CASE(8)
-    ATTN_CASE(16)
-    ATTN_CASE(32)
-    ATTN_CASE(64)
-    ATTN_CASE(128)
+    case 4: launch_attention_d<AT, KT, 4>(h, a, ngroups); break;
+    case 8: launch_attention_d<AT, KT, 8>(h, a, ngroups); break;
+    case 16: launch_attention_d<AT, KT, 16>(h, a, ngroups); break;
+    case 32: launch_attention_d<AT, KT, 32>(h, a, ngroups); break;
+    case 64: launch_attention_d<AT, KT, 64>(h, a, ngroups); break;
+    case 128: launch_attention_d<AT, KT, 128>(h, a, ngroups); break;
     default: fail(SPECDEC_ERR_UNSUPPORTED, "head dimension must be 4, 8, 16, 32, 64 or 128");
   }
-#undef ATTN_CASE
 }
 
 // Attention over a row batch whose rows form groups of Q consecutive rows of
@@ -456,7 +468,7 @@ void attention(specdec_handle *h, const Dims &dm, RowsView rows, int R, int Q, c
   a.q = h->Q; a.ldq = dm.d; a.rows = rows; a.R = R; a.Q = Q;
   a.kc = kc; a.vc = vc; a.kv_req_stride = req_stride; a.S_cap = S_cap; a.H = dm.H; a.Hkv = dm.Hkv;
   a.nsplit = 1;
-  if (R <= h->R_part) a.nsplit = std::max(1, std::min(h->max_split, (S_cap + 1023) / 1024));
+  if (R <= h->R_part) a.nsplit = std::max(1, std::min(h->max_split, (S_cap + 255) / 256));
   a.chunk = (S_cap + a.nsplit - 1) / a.nsplit;
   a.out = h->ATT; a.ldo = dm.d; a.part = h->part; a.counters = h->counters; a.err = h->st.err;
   const int ngroups = (R + Q - 1) / Q;

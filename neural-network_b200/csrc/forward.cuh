@@ -148,13 +148,60 @@ __device__ __forceinline__ void load_wvec(const float *p, float (&w)[4]) {
   const float4 t = __ldg(reinterpret_cast<const float4 *>(p));
   w[0] = t.x; w[1] = t.y; w[2] = t.z; w[3] = t.w;
 }
+// int8 -> fp32 without the conversion unit: with u = q + 128 placed in the
+// low byte of 0x4B000000 the float is exactly 2^23 + u, so subtracting
+// 2^23 + 128 gives q exactly.
+__device__ __forceinline__ void i8x4_to_f32(uint32_t word, float *w) {
+  const uint32_t u = word ^ 0x80808080u;
+  w[0] = __int_as_float(__byte_perm(u, 0x4B000000u, 0x7540)) - 8388736.0f;
+  w[1] = __int_as_float(__byte_perm(u, 0x4B000000u, 0x7541)) - 8388736.0f;
+  w[2] = __int_as_float(__byte_perm(u, 0x4B000000u, 0x7542)) - 8388736.0f;
+  w[3] = __int_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - 8388736.0f;
+}
 __device__ __forceinline__ void load_wvec(const int8_t *p, float (&w)[8]) {
   const uint2 t = __ldg(reinterpret_cast<const uint2 *>(p));
+  i8x4_to_f32(t.x, w);
+  i8x4_to_f32(t.y, w + 4);
+}
+
+// Reduce-scatter of 2*kRowTile per-lane partial sums over the warp in 16
+// shuffles: afterwards lane l holds the full sum of value (column
+// (l >> 4) & 1, row ((l >> 1) & 7)); lanes differing only in bit 0 agree.
+__device__ __forceinline__ float warp_reduce16(const float (&a0)[kRowTile], const float (&a1)[kRowTile]) {
+  const int lane = threadIdx.x & 31;
+  float v8[8];
+  {
+    const bool hi = lane & 16;
 #pragma unroll
-  for (int b = 0; b < 4; ++b) {
-    w[b] = static_cast<float>(static_cast<int8_t>((t.x >> (8 * b)) & 0xff));
-    w[4 + b] = static_cast<float>(static_cast<int8_t>((t.y >> (8 * b)) & 0xff));
+    for (int i = 0; i < 8; ++i) {
+      const float send = hi ? a0[i] : a1[i];
+      const float keep = hi ? a1[i] : a0[i];
+      v8[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
   }
+  float v4[4];
+  {
+    const bool hi = lane & 8;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float send = hi ? v8[i] : v8[i + 4];
+      const float keep = hi ? v8[i + 4] : v8[i];
+      v4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+  }
+  float v2[2];
+  {
+    const bool hi = lane & 4;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float send = hi ? v4[i] : v4[i + 2];
+      const float keep = hi ? v4[i + 2] : v4[i];
+      v2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+  }
+  const bool hi = lane & 2;
+  float v = (hi ? v2[1] : v2[0]) + __shfl_xor_sync(0xffffffffu, hi ? v2[0] : v2[1], 2);
+  return v + __shfl_xor_sync(0xffffffffu, v, 1);
 }
 
 // E consecutive input elements as fp32.
@@ -341,8 +388,9 @@ __global__ void __launch_bounds__(32 * kLinWarps) linear_kernel(LinearArgs a) {
   for (int i = 0; i < kRowTile; ++i) acc0[i] = acc1[i] = 0.f;
   EpiPre pre{};
   if (col_ok) {
-    // lane i finishes row i: fetch its epilogue operands now
-    if (kidx == 0 && lane < nrows) epilogue_prefetch<AT, EPI>(a, r0 + lane, n0, pre);
+    // lane 2i finishes row i: fetch its epilogue operands now
+    if (kidx == 0 && lane < 16 && !(lane & 1) && (lane >> 1) < nrows)
+      epilogue_prefetch<AT, EPI>(a, r0 + (lane >> 1), n0, pre);
     const WT *w0 = static_cast<const WT *>(a.W) + static_cast<size_t>(n0) * a.K;
     const WT *w1 = has1 ? w0 + a.K : w0;
     const AT *xrow[kRowTile];
@@ -387,39 +435,22 @@ __global__ void __launch_bounds__(32 * kLinWarps) linear_kernel(LinearArgs a) {
           acc1[i] = fmaf(xv, wb, acc1[i]);
         }
     }
-#pragma unroll
-    for (int i = 0; i < kRowTile; ++i) {
-      acc0[i] = warp_sum(acc0[i]);
-      acc1[i] = warp_sum(acc1[i]);
-    }
   }
+  // warp totals: lane l holds (column (l >> 4) & 1, row (l >> 1) & 7)
+  float tot = warp_reduce16(acc0, acc1);
+  const int vidx = ((lane >> 4) & 1) * kRowTile + ((lane >> 1) & 7);
   if (ks > 1) {
-    if (lane == 0) {
-#pragma unroll
-      for (int i = 0; i < kRowTile; ++i) {
-        s_red[warp][2 * i] = acc0[i];
-        s_red[warp][2 * i + 1] = acc1[i];
-      }
-    }
+    if (!(lane & 1)) s_red[warp][vidx] = tot;
     __syncthreads();
     if (kidx == 0) {
-#pragma unroll
-      for (int i = 0; i < kRowTile; ++i) {
-        float t0 = 0.f, t1 = 0.f;
-        for (int j = 0; j < ks; ++j) {
-          t0 += s_red[warp + j][2 * i];
-          t1 += s_red[warp + j][2 * i + 1];
-        }
-        acc0[i] = t0;
-        acc1[i] = t1;
-      }
+      float t = 0.f;
+      for (int j = 0; j < ks; ++j) t += s_red[warp + j][vidx];
+      tot = t;
     }
   }
-  if (col_ok && kidx == 0) {
-#pragma unroll
-    for (int i = 0; i < kRowTile; ++i)
-      if (lane == i && i < nrows) linear_epilogue<AT, EPI>(a, r0 + i, n0, acc0[i], acc1[i], pre);
-  }
+  const float tot1 = __shfl_xor_sync(0xffffffffu, tot, 16);
+  if (col_ok && kidx == 0 && lane < 16 && !(lane & 1) && (lane >> 1) < nrows)
+    linear_epilogue<AT, EPI>(a, r0 + (lane >> 1), n0, tot, tot1, pre);
   if (!a.ln_out) return;
   // the last block of this row tile normalises the finished rows
   __threadfence();
@@ -455,7 +486,7 @@ __global__ void __launch_bounds__(32 * kLinWarps) linear_kernel(LinearArgs a) {
 // head) merges them (log-sum-exp), so no separate combine kernel runs.
 constexpr int kAttnThreads = 128;
 constexpr int kAttnWarps = kAttnThreads / 32;
-constexpr int kAttnQT = 8;  // queries per block
+constexpr int kAttnQT = 8;  // most queries per block (the group size rounds up to 1, 2, 4 or 8)
 
 // Positions per shared-memory tile: 128 (one per thread), or 64 when a K/V
 // row is wider than 256 bytes so two stages of K and V stay within 128 KiB.
@@ -511,9 +542,8 @@ constexpr int attn_smem_bytes() {
   return 2 /*stages*/ * 2 /*K,V*/ * attn_tile<KT, D>() * D * static_cast<int>(sizeof(KT));
 }
 
-template <typename AT, typename KT, int D>
+template <typename AT, typename KT, int D, int QT>
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a) {
-  constexpr int QT = kAttnQT;
   constexpr int DC = (D + 31) / 32;  // dims per lane in P.V
   constexpr bool kBulk = (D * sizeof(KT)) % 16 == 0;
   constexpr int kAttnTile = attn_tile<KT, D>();
@@ -617,23 +647,43 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a) {
 #pragma unroll
         for (int c = 0; c < D; ++c) kr[c] = to_f32(ktile[tp * D + ((c + lane) % D)]);
       }
+      float sc[QT];
 #pragma unroll
       for (int i = 0; i < QT; ++i) {
-        float s = -INFINITY;
+        sc[i] = -INFINITY;
         if (i < nq && tp < nt && pos <= qpos[i]) {
           float dot = 0.f;
 #pragma unroll
           for (int c = 0; c < D; ++c) dot = fmaf(qs[i][(c + lane) % D], kr[c], dot);
-          s = __fdiv_rn(dot, scale);
+          sc[i] = __fdiv_rn(dot, scale);
         }
-        const float tmax = warp_max(s);
-        const float mnew = fmaxf(m[i], tmax);
-        p[i] = (s == -INFINITY) ? 0.f : expf(s - mnew);
-        const float alpha = (m[i] == -INFINITY) ? 0.f : expf(m[i] - mnew);
-        l[i] = l[i] * alpha + warp_sum(p[i]);
+      }
+      // tile maxima and sums of all queries, butterflies interleaved
+      float tm[QT];
 #pragma unroll
-        for (int c = 0; c < DC; ++c) acc[i][c] *= alpha;
+      for (int i = 0; i < QT; ++i) tm[i] = sc[i];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int i = 0; i < QT; ++i) tm[i] = fmaxf(tm[i], __shfl_xor_sync(0xffffffffu, tm[i], o));
+      float ps[QT], alpha[QT];
+#pragma unroll
+      for (int i = 0; i < QT; ++i) {
+        const float mnew = fmaxf(m[i], tm[i]);
+        p[i] = (sc[i] == -INFINITY) ? 0.f : expf(sc[i] - mnew);
+        alpha[i] = (m[i] == -INFINITY) ? 0.f : expf(m[i] - mnew);
         m[i] = mnew;
+        ps[i] = p[i];
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int i = 0; i < QT; ++i) ps[i] += __shfl_xor_sync(0xffffffffu, ps[i], o);
+#pragma unroll
+      for (int i = 0; i < QT; ++i) {
+        l[i] = l[i] * alpha[i] + ps[i];
+#pragma unroll
+        for (int c = 0; c < DC; ++c) acc[i][c] *= alpha[i];
       }
     }
     const int nvalid = max(0, min(32, nt - warp * 32));
