@@ -15,6 +15,8 @@
 // generate call is one graph launch with no host round trips.  The same
 // kernels can be launched directly (SPECDEC_NO_GRAPH=1), e.g. for per-kernel
 // profiling (ncu cannot profile kernel nodes of graphs with conditional nodes).
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -161,11 +163,11 @@ struct specdec_handle {
 
   // activations: X layer input / residual stream, H projection outputs,
   // X1 normed rows, A FFN hidden, Q queries, ATT attention out
-  int R_max = 0, R_part = 0, max_split = 1;
+  int R_max = 0;
+  int num_sms = 148;
   size_t act_elt = 4;
   void *X = nullptr, *H = nullptr, *X1 = nullptr, *A = nullptr, *Q = nullptr, *ATT = nullptr;
-  float *logits = nullptr, *part = nullptr;
-  int *counters = nullptr, *tile_counters = nullptr;
+  float *logits = nullptr;
   RowPool pool{};
   int *sel_odd = nullptr, *sel_prefill = nullptr;
 
@@ -382,6 +384,62 @@ void launch(specdec_handle *h, void (*kern)(KArgs...), dim3 grid, dim3 block, si
   ++h->launches;
 }
 
+// A launch whose CTAs form thread-block clusters of `cluster` CTAs.
+template <typename... KArgs, typename... Args>
+void launch_cluster(specdec_handle *h, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, dim3 cluster,
+                    Args... args) {
+  cudaLaunchConfig_t lc{};
+  lc.gridDim = grid;
+  lc.blockDim = block;
+  lc.dynamicSmemBytes = smem;
+  lc.stream = h->stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = cluster.x;
+  at[0].val.clusterDim.y = cluster.y;
+  at[0].val.clusterDim.z = cluster.z;
+  lc.attrs = at;
+  lc.numAttrs = 1;
+  CK(cudaLaunchKernelEx(&lc, kern, static_cast<KArgs>(args)...));
+  ++h->launches;
+}
+
+// cuTensorMapEncodeTiled, looked up from the driver once (no link-time
+// dependency on libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  if (!fn) fail(SPECDEC_ERR_CUDA, "the driver does not provide cuTensorMapEncodeTiled");
+  return fn;
+}
+
+// 2-D TMA view [rows][D] of one layer's K or V cache (row = slot * Hkv * S_cap
+// + kv head * S_cap + position), box = box_cols x box_rows elements, with the
+// 128-byte swizzle when a row is a multiple of 128 bytes.  Rows past the end
+// read as zeros.
+CUtensorMap kv_tensor_map(const void *base, bool bf16, int D, size_t rows, int box_cols, int box_rows) {
+  const size_t elt = bf16 ? 2 : 4;
+  if (rows >= (size_t(1) << 31)) fail(SPECDEC_ERR_UNSUPPORTED, "KV cache too large for 32-bit TMA row coordinates");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(D * elt)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  const bool swz = (D * elt) % 128 == 0;
+  const CUresult r = tensor_map_encoder()(
+      &m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base), dims,
+      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+      CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) fail(SPECDEC_ERR_CUDA, "cuTensorMapEncodeTiled failed with " + std::to_string(static_cast<int>(r)));
+  return m;
+}
+
 // K-split: enough warps per column pair that each lane streams one or two
 // weight vectors, while the grid stays within about two waves.
 int pick_ksplit(int N, int R, int K, int E) {
@@ -396,6 +454,8 @@ int pick_ksplit(int N, int R, int K, int E) {
   return ks;
 }
 
+constexpr size_t kLinLnSmemMax = 128 * 1024;
+
 template <int EPI>
 void launch_linear(specdec_handle *h, LinearArgs a) {
   if (a.R <= 0) return;
@@ -404,19 +464,42 @@ void launch_linear(specdec_handle *h, LinearArgs a) {
   const int pairs = kLinWarps / a.ksplit;
   dim3 grid((a.N + 2 * pairs - 1) / (2 * pairs), (a.R + kRowTile - 1) / kRowTile);
   dim3 block(32 * kLinWarps);
-  if (a.ln_out) {
-    if (a.N > 32 * kLnMaxPerLane) fail(SPECDEC_ERR_UNSUPPORTED, "fused LayerNorm supports rows up to 1024 wide");
-    a.tile_counters = h->tile_counters;
+  if (a.in_g) {
+    const size_t smem = static_cast<size_t>(kRowTile) * a.K * h->act_elt;
+    if (smem > kLinLnSmemMax) fail(SPECDEC_ERR_UNSUPPORTED, "input rows too wide for the fused LayerNorm");
+    if (i8 && bf) launch(h, linear_kernel<int8_t, __nv_bfloat16, EPI, true>, grid, block, smem, a);
+    else if (i8) launch(h, linear_kernel<int8_t, float, EPI, true>, grid, block, smem, a);
+    else if (bf) launch(h, linear_kernel<float, __nv_bfloat16, EPI, true>, grid, block, smem, a);
+    else launch(h, linear_kernel<float, float, EPI, true>, grid, block, smem, a);
+  } else {
+    if (i8 && bf) launch(h, linear_kernel<int8_t, __nv_bfloat16, EPI, false>, grid, block, 0, a);
+    else if (i8) launch(h, linear_kernel<int8_t, float, EPI, false>, grid, block, 0, a);
+    else if (bf) launch(h, linear_kernel<float, __nv_bfloat16, EPI, false>, grid, block, 0, a);
+    else launch(h, linear_kernel<float, float, EPI, false>, grid, block, 0, a);
   }
-  if (i8 && bf) launch(h, linear_kernel<int8_t, __nv_bfloat16, EPI>, grid, block, 0, a);
-  else if (i8) launch(h, linear_kernel<int8_t, float, EPI>, grid, block, 0, a);
-  else if (bf) launch(h, linear_kernel<float, __nv_bfloat16, EPI>, grid, block, 0, a);
-  else launch(h, linear_kernel<float, float, EPI>, grid, block, 0, a);
+}
+
+// Dynamic shared memory of the input-LayerNorm linear kernels: kLinLnSmemMax
+// holds kRowTile rows of up to 4096 fp32 or 8192 bf16 elements.
+template <int EPI>
+void set_linear_attr_epi() {
+  const int b = static_cast<int>(kLinLnSmemMax);
+  CK(cudaFuncSetAttribute(linear_kernel<int8_t, __nv_bfloat16, EPI, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
+  CK(cudaFuncSetAttribute(linear_kernel<int8_t, float, EPI, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
+  CK(cudaFuncSetAttribute(linear_kernel<float, __nv_bfloat16, EPI, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
+  CK(cudaFuncSetAttribute(linear_kernel<float, float, EPI, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
+}
+void set_linear_attrs() {
+  set_linear_attr_epi<kEpiStore>();
+  set_linear_attr_epi<kEpiResid>();
+  set_linear_attr_epi<kEpiQKV>();
+  set_linear_attr_epi<kEpiSwiGLU>();
+  set_linear_attr_epi<kEpiGelu>();
 }
 
 template <typename AT, typename KT, int D>
 void set_attn_attr() {
-  const int bytes = attn_smem_bytes<KT, D>();
+  const int bytes = AttnGeom<KT, D>::smem_bytes(2);
   CK(cudaFuncSetAttribute(attention_kernel<AT, KT, D, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
   CK(cudaFuncSetAttribute(attention_kernel<AT, KT, D, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
   CK(cudaFuncSetAttribute(attention_kernel<AT, KT, D, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
@@ -432,68 +515,104 @@ void set_attn_attrs() {
   set_attn_attr<AT, KT, 128>();
 }
 
+// Splits: one tile of positions per split where the cache is long, at most a
+// portable cluster (8) of them, and about two CTAs per SM over the grid.
 template <typename AT, typename KT, int D>
-void launch_attention_d(specdec_handle *h, const AttnArgs &a, int ngroups) {
+void launch_attention_d(specdec_handle *h, AttnArgs &a, int ngroups, const void *kc, const void *vc, size_t rows) {
+  using G = AttnGeom<KT, D>;
+  if (!G::kTma) fail(SPECDEC_ERR_UNSUPPORTED, "a K/V cache row (head_dim x element size) must be a multiple of 16 bytes");
+  constexpr bool kbf = std::is_same<KT, __nv_bfloat16>::value;
+  a.tmk = kv_tensor_map(kc, kbf, D, rows, G::kBoxCols, G::kTile);
+  a.tmv = kv_tensor_map(vc, kbf, D, rows, G::kBoxCols, G::kTile);
   const int qt = a.Q <= 1 ? 1 : a.Q <= 2 ? 2 : a.Q <= 4 ? 4 : kAttnQT;
-  dim3 grid(ngroups * ((a.Q + qt - 1) / qt), a.H, a.nsplit);
+  const int ngt = (a.Q + qt - 1) / qt;
+  const int base = ngroups * ngt * a.H;
+  int ns = 1;
+  if (a.S_cap > G::kTile) {
+    const int want = (a.S_cap + G::kTile - 1) / G::kTile;
+    const int fit = std::max(1, 2 * h->num_sms / base);
+    ns = std::min(std::min(kAttnMaxSplit, want), fit);
+  }
+  a.nsplit = ns;
+  a.chunk = (a.S_cap + ns - 1) / ns;
+  const size_t smem = static_cast<size_t>(G::smem_bytes(a.chunk > G::kTile ? 2 : 1));
+  dim3 grid(ngroups * ngt, a.H, ns);
   dim3 block(kAttnThreads);
-  const size_t smem = static_cast<size_t>(attn_smem_bytes<KT, D>());
+  auto go = [&](auto kern) {
+    if (ns == 1) launch(h, kern, grid, block, smem, a);
+    else launch_cluster(h, kern, grid, block, smem, dim3(1, 1, ns), a);
+  };
   switch (qt) {
-    case 1: launch(h, attention_kernel<AT, KT, D, 1>, grid, block, smem, a); break;
-    case 2: launch(h, attention_kernel<AT, KT, D, 2>, grid, block, smem, a); break;
-    case 4: launch(h, attention_kernel<AT, KT, D, 4>, grid, block, smem, a); break;
-    default: launch(h, attention_kernel<AT, KT, D, 8>, grid, block, smem, a); break;
+    case 1: go(attention_kernel<AT, KT, D, 1>); break;
+    case 2: go(attention_kernel<AT, KT, D, 2>); break;
+    case 4: go(attention_kernel<AT, KT, D, 4>); break;
+    default: go(attention_kernel<AT, KT, D, 8>); break;
   }
 }
 
 template <typename AT, typename KT>
-void launch_attention_t(specdec_handle *h, const AttnArgs &a, int D, int ngroups) {
+void launch_attention_t(specdec_handle *h, AttnArgs &a, int D, int ngroups, const void *kc, const void *vc,
+                        size_t rows) {
   switch (D) {
-    case 4: launch_attention_d<AT, KT, 4>(h, a, ngroups); break;
-    case 8: launch_attention_d<AT, KT, 8>(h, a, ngroups); break;
-    case 16: launch_attention_d<AT, KT, 16>(h, a, ngroups); break;
-    case 32: launch_attention_d<AT, KT, 32>(h, a, ngroups); break;
-    case 64: launch_attention_d<AT, KT, 64>(h, a, ngroups); break;
-    case 128: launch_attention_d<AT, KT, 128>(h, a, ngroups); break;
+    case 4: launch_attention_d<AT, KT, 4>(h, a, ngroups, kc, vc, rows); break;
+    case 8: launch_attention_d<AT, KT, 8>(h, a, ngroups, kc, vc, rows); break;
+    case 16: launch_attention_d<AT, KT, 16>(h, a, ngroups, kc, vc, rows); break;
+    case 32: launch_attention_d<AT, KT, 32>(h, a, ngroups, kc, vc, rows); break;
+    case 64: launch_attention_d<AT, KT, 64>(h, a, ngroups, kc, vc, rows); break;
+    case 128: launch_attention_d<AT, KT, 128>(h, a, ngroups, kc, vc, rows); break;
     default: fail(SPECDEC_ERR_UNSUPPORTED, "head dimension must be 4, 8, 16, 32, 64 or 128");
   }
 }
 
 // Attention over a row batch whose rows form groups of Q consecutive rows of
-// one request each.  Contexts are split over blocks only when they are long.
+// one request each.  kc/vc are one layer's caches of `layer_elems` elements
+// ([slot][kv head][S_cap][D]).
 void attention(specdec_handle *h, const Dims &dm, RowsView rows, int R, int Q, const void *kc, const void *vc,
-               size_t req_stride, int S_cap) {
+               size_t layer_elems, int S_cap) {
   if (R <= 0) return;
   AttnArgs a{};
   a.q = h->Q; a.ldq = dm.d; a.rows = rows; a.R = R; a.Q = Q;
-  a.kc = kc; a.vc = vc; a.kv_req_stride = req_stride; a.S_cap = S_cap; a.H = dm.H; a.Hkv = dm.Hkv;
-  a.nsplit = 1;
-  if (R <= h->R_part) a.nsplit = std::max(1, std::min(h->max_split, (S_cap + 255) / 256));
-  a.chunk = (S_cap + a.nsplit - 1) / a.nsplit;
-  a.out = h->ATT; a.ldo = dm.d; a.part = h->part; a.counters = h->counters; a.err = h->st.err;
+  a.S_cap = S_cap; a.H = dm.H; a.Hkv = dm.Hkv;
+  a.out = h->ATT; a.ldo = dm.d; a.err = h->st.err;
   const int ngroups = (R + Q - 1) / Q;
+  const size_t nrows = layer_elems / dm.D;
   const bool bf = act_bf16(h);
   const bool kvbf = h->cfg.kv_dtype == SPECDEC_BF16;
-  if (bf && kvbf) launch_attention_t<__nv_bfloat16, __nv_bfloat16>(h, a, dm.D, ngroups);
-  else if (bf) launch_attention_t<__nv_bfloat16, float>(h, a, dm.D, ngroups);
-  else if (kvbf) launch_attention_t<float, __nv_bfloat16>(h, a, dm.D, ngroups);
-  else launch_attention_t<float, float>(h, a, dm.D, ngroups);
+  if (bf && kvbf) launch_attention_t<__nv_bfloat16, __nv_bfloat16>(h, a, dm.D, ngroups, kc, vc, nrows);
+  else if (bf) launch_attention_t<__nv_bfloat16, float>(h, a, dm.D, ngroups, kc, vc, nrows);
+  else if (kvbf) launch_attention_t<float, __nv_bfloat16>(h, a, dm.D, ngroups, kc, vc, nrows);
+  else launch_attention_t<float, float>(h, a, dm.D, ngroups, kc, vc, nrows);
+}
+
+// Where the lm_head reads the last hidden rows, and the LayerNorm it applies
+// to them first.
+struct HeadInput {
+  const void *x;
+  const float *g, *b;
+};
+HeadInput head_input(specdec_handle *h, const ModelW &m) {
+  if (m.dm.arch == SPECDEC_ARCH_REF)
+    return m.dm.L > 0 ? HeadInput{h->H, m.layers[m.dm.L - 1].g2, m.layers[m.dm.L - 1].b2} : HeadInput{h->X, nullptr, nullptr};
+  return HeadInput{h->X, m.gf, m.bfin};
 }
 
 // One forward pass of model m over the row batch at pool offset `off`
 // (R rows in groups of Q rows per request).  When `logits` is set, the
 // lm_head runs over the rows listed in `sel` (n_sel of them; all R rows when
-// sel is null) and writes fp32 logits.
+// sel is null) and writes fp32 logits.  Every LayerNorm runs in the prologue
+// of the linear kernel that consumes its output.
 //
-// Reference arch, per layer (src/nn/layer.cpp:1097-1114, post-LN):
-//   QKV    X -> Q, K/V cache (RoPE, append)
+// Reference arch, per layer (src/nn/layer.cpp:1097-1114, post-LN); the
+// embedding writes X:
+//   QKV    LN2_prev(H) (layer 0: X) -> Q, K/V cache (RoPE, append); stores
+//          the normalised rows in X
 //   ATT    attention -> ATT
-//   OPROJ  ATT.Wo + bo + X -> H, then X1 = LN1(H) by the tile's last block
-//   GATEUP silu(X1.Wg + bg) * (X1.Wu + bu) -> A
-//   DOWN   A.Wd + bd + X1 -> H, then X = LN2(H)
-// cfg arch (pre-LN): the embedding writes X and X1 = LN1(X); QKV reads X1;
-// OPROJ -> H = X + attn, X1 = LN2(H); FC1 GELU -> A; FC2 -> X = H + ffn,
-// X1 = the next layer's LN1(X) or the final LN; the head reads X1.
+//   OPROJ  ATT.Wo + bo + X -> H
+//   GATEUP silu(LN1(H).Wg + bg) * (LN1(H).Wu + bu) -> A; stores LN1(H) in X1
+//   DOWN   A.Wd + bd + X1 -> H
+//   head   LN2_last(H) -> logits
+// cfg arch (pre-LN): QKV reads LN1(X); OPROJ H = X + attn; FC1 GELU over
+// LN2(H) -> A; FC2 X = H + ffn; the head reads LN_final(X).
 void forward_rows(specdec_handle *h, bool target, int off, int R, int Q, const int *sel, int n_sel, float *logits) {
   ModelW &m = target ? h->tgt : h->dft;
   const Dims &dm = m.dm;
@@ -507,50 +626,55 @@ void forward_rows(specdec_handle *h, bool target, int off, int R, int Q, const i
   const size_t kv_elt = h->cfg.kv_dtype == SPECDEC_BF16 ? 2 : 4;
   const bool ref = dm.arch == SPECDEC_ARCH_REF;
 
-  const float *lg0 = ref ? nullptr : m.layers[0].g1, *lb0 = ref ? nullptr : m.layers[0].b1;
   if (act_bf16(h))
     launch(h, embed_kernel<__nv_bfloat16>, dim3(R), dim3(128), 0, rows, R, m.emb, m.pos, d, dm.max_seq,
-           static_cast<__nv_bfloat16 *>(h->X), lg0, lb0, static_cast<__nv_bfloat16 *>(h->X1));
+           static_cast<__nv_bfloat16 *>(h->X));
   else
     launch(h, embed_kernel<float>, dim3(R), dim3(128), 0, rows, R, m.emb, m.pos, d, dm.max_seq,
-           static_cast<float *>(h->X), lg0, lb0, static_cast<float *>(h->X1));
+           static_cast<float *>(h->X));
 
   for (int l = 0; l < dm.L; ++l) {
     const LayerW &L = m.layers[l];
     void *kcl = static_cast<char *>(kc) + l * lstride * kv_elt;
     void *vcl = static_cast<char *>(vc) + l * lstride * kv_elt;
     LinearArgs a{};
-    a.x = ref ? h->X : h->X1; a.ldx = d; a.R = R; a.W = L.wqkv; a.scale = L.sqkv; a.bias = L.bqkv;
+    a.ldx = d; a.R = R; a.W = L.wqkv; a.scale = L.sqkv; a.bias = L.bqkv;
     a.N = d + 2 * dm.kvd; a.K = d; a.out = h->Q; a.ldo = d; a.rows = rows;
+    if (ref) {
+      a.x = l == 0 ? h->X : h->H;
+      if (l > 0) { a.in_g = m.layers[l - 1].g2; a.in_b = m.layers[l - 1].b2; a.norm_out = h->X; }
+    } else {
+      a.x = h->X; a.in_g = L.g1; a.in_b = L.b1;
+    }
     a.qkv = QKVArgs{d, dm.kvd, dm.D, h->rope, h->rope_max, kcl, vcl, rstride, S_cap,
                     h->cfg.kv_dtype == SPECDEC_BF16 ? 1 : 0, h->st.err};
     launch_linear<kEpiQKV>(h, a);
-    attention(h, dm, rows, R, Q, kcl, vcl, rstride, S_cap);
+    attention(h, dm, rows, R, Q, kcl, vcl, lstride, S_cap);
     LinearArgs o{};
     o.x = h->ATT; o.ldx = d; o.R = R; o.W = L.wo; o.scale = L.so; o.bias = L.bo; o.N = d; o.K = d;
     o.out = h->H; o.ldo = d; o.resid = h->X; o.ldr = d; o.rows = rows;
-    o.ln_g = ref ? L.g1 : L.g2; o.ln_b = ref ? L.b1 : L.b2; o.ln_out = h->X1;
     launch_linear<kEpiResid>(h, o);
     LinearArgs g{};
-    g.x = h->X1; g.ldx = d; g.R = R; g.W = L.wgu; g.scale = L.sgu; g.bias = L.bgu; g.K = d; g.rows = rows;
+    g.x = h->H; g.ldx = d; g.R = R; g.W = L.wgu; g.scale = L.sgu; g.bias = L.bgu; g.K = d; g.rows = rows;
     g.out = h->A; g.ldo = dm.F; g.N = ref ? 2 * dm.F : dm.F;
-    if (ref) launch_linear<kEpiSwiGLU>(h, g);
-    else launch_linear<kEpiGelu>(h, g);
+    g.in_g = ref ? L.g1 : L.g2; g.in_b = ref ? L.b1 : L.b2;
+    if (ref) {
+      g.norm_out = h->X1;
+      launch_linear<kEpiSwiGLU>(h, g);
+    } else {
+      launch_linear<kEpiGelu>(h, g);
+    }
     LinearArgs dn{};
     dn.x = h->A; dn.ldx = dm.F; dn.R = R; dn.W = L.wd; dn.scale = L.sd; dn.bias = L.bd; dn.N = d; dn.K = dm.F;
     dn.rows = rows; dn.ldo = d; dn.ldr = d;
-    if (ref) {
-      dn.out = h->H; dn.resid = h->X1; dn.ln_g = L.g2; dn.ln_b = L.b2; dn.ln_out = h->X;
-    } else {
-      dn.out = h->X; dn.resid = h->H; dn.ln_out = h->X1;
-      if (l + 1 < dm.L) { dn.ln_g = m.layers[l + 1].g1; dn.ln_b = m.layers[l + 1].b1; }
-      else { dn.ln_g = m.gf; dn.ln_b = m.bfin; }
-    }
+    if (ref) { dn.out = h->H; dn.resid = h->X1; }
+    else { dn.out = h->X; dn.resid = h->H; }
     launch_linear<kEpiResid>(h, dn);
   }
   if (!logits) return;
+  const HeadInput hi = head_input(h, m);
   LinearArgs hd{};
-  hd.x = ref ? h->X : h->X1; hd.ldx = d; hd.in_rows = sel; hd.R = sel ? n_sel : R;
+  hd.x = hi.x; hd.in_g = hi.g; hd.in_b = hi.b; hd.ldx = d; hd.in_rows = sel; hd.R = sel ? n_sel : R;
   hd.W = m.whead; hd.scale = m.shead; hd.bias = m.bhead;
   hd.N = dm.V; hd.K = d; hd.out = logits; hd.ldo = dm.V; hd.out_f32 = 1; hd.rows = rows;
   launch_linear<kEpiStore>(h, hd);
@@ -785,6 +909,7 @@ int specdec_create(const specdec_config *cfg, int device, specdec_handle **out) 
     h->cfg = *cfg;
     h->device = device;
     CK(cudaSetDevice(device));
+    CK(cudaDeviceGetAttribute(&h->num_sms, cudaDevAttrMultiProcessorCount, device));
     Dims td = make_dims(cfg->target);
     check_dims(td, "target");
     specdec_model_config dcfg = cfg->draft;
@@ -815,6 +940,7 @@ int specdec_create(const specdec_config *cfg, int device, specdec_handle **out) 
     set_attn_attrs<float, __nv_bfloat16>();
     set_attn_attrs<__nv_bfloat16, float>();
     set_attn_attrs<__nv_bfloat16, __nv_bfloat16>();
+    set_linear_attrs();
     {
       const int vs = td.V * static_cast<int>(sizeof(float));
       CK(cudaFuncSetAttribute(first_token_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, vs));
@@ -854,10 +980,8 @@ int specdec_create(const specdec_config *cfg, int device, specdec_handle **out) 
     // activations
     const int R_round = std::max(B * (k + 1), 2 * B);
     h->R_max = std::max(R_round, std::min(B * cfg->max_prompt_len, std::max(8192, R_round)));
-    h->R_part = R_round;
-    h->max_split = 16;
     h->act_elt = act_bf16(h.get()) ? 2 : 4;
-    const int dmax = std::max(td.d, dd.d), Fmax = std::max(td.F, dd.F), Hmax = std::max(td.H, dd.H);
+    const int dmax = std::max(td.d, dd.d), Fmax = std::max(td.F, dd.F);
     const size_t rowb = static_cast<size_t>(h->R_max) * dmax * h->act_elt;
     h->X = h->dalloc(rowb);
     h->H = h->dalloc(rowb);
@@ -866,13 +990,6 @@ int specdec_create(const specdec_config *cfg, int device, specdec_handle **out) 
     h->ATT = h->dalloc(rowb);
     h->A = h->dalloc(static_cast<size_t>(h->R_max) * Fmax * h->act_elt);
     h->logits = static_cast<float *>(h->dalloc(static_cast<size_t>(R_round) * td.V * sizeof(float)));
-    h->part = static_cast<float *>(
-        h->dalloc(static_cast<size_t>(h->R_part) * Hmax * h->max_split * (std::max(td.D, dd.D) + 2) * sizeof(float)));
-    h->counters = static_cast<int *>(h->dalloc(static_cast<size_t>(h->R_part) * Hmax * sizeof(int)));
-    CK(cudaMemset(h->counters, 0, static_cast<size_t>(h->R_part) * Hmax * sizeof(int)));
-    const size_t n_tiles = static_cast<size_t>(h->R_max) / kRowTile + 2;
-    h->tile_counters = static_cast<int *>(h->dalloc(n_tiles * sizeof(int)));
-    CK(cudaMemset(h->tile_counters, 0, n_tiles * sizeof(int)));
     const size_t pool_rows =
         static_cast<size_t>(h->R_max) + 2 * B + static_cast<size_t>(k - 1) * B + static_cast<size_t>(B) * (k + 1);
     auto ib = [&](size_t n) { return static_cast<int *>(h->dalloc(n * sizeof(int))); };
@@ -1037,13 +1154,14 @@ int specdec_forward_logits(specdec_handle *h, int role, const int32_t *tokens, i
     // the lm_head over row chunks that fit the logits buffer
     const int R_round = std::max(h->cfg.max_batch * (h->cfg.max_lookahead + 1), 2 * h->cfg.max_batch);
     RowsView rows{h->pool.tok, h->pool.pos, h->pool.req};
-    const bool ref = dm.arch == SPECDEC_ARCH_REF;
+    const HeadInput hi = head_input(h, m);
     for (int c0 = 0; c0 < S; c0 += R_round) {
       const int n = std::min(R_round, S - c0);
       LinearArgs hd{};
       hd.R = n; hd.W = m.whead; hd.scale = m.shead; hd.bias = m.bhead; hd.N = dm.V; hd.K = dm.d;
       hd.out = h->logits; hd.ldo = dm.V; hd.out_f32 = 1; hd.rows = rows;
-      hd.x = static_cast<char *>(ref ? h->X : h->X1) + static_cast<size_t>(c0) * dm.d * h->act_elt;
+      hd.in_g = hi.g; hd.in_b = hi.b;
+      hd.x = static_cast<const char *>(hi.x) + static_cast<size_t>(c0) * dm.d * h->act_elt;
       hd.ldx = dm.d;
       launch_linear<kEpiStore>(h, hd);
       CK(cudaMemcpyAsync(logits + static_cast<size_t>(c0) * dm.V, h->logits, static_cast<size_t>(n) * dm.V * sizeof(float),
@@ -1096,15 +1214,14 @@ int specdec_philox_uniforms(uint64_t seed, int B, int rounds, int slots, float *
 // loops where an allocation can stall the device, and callers whose CUDA
 // context is shared and must not grow.  For them this entry point takes the
 // tokens and the logits as device buffers they already own and keeps all of
-// its own working memory (activations, the row tables, the per-sequence KV
-// cache and the split-K attention partials) in one file-scope device array of
+// its own working memory (activations, the row tables and the per-sequence KV
+// cache) in one file-scope device array of
 // fixed size, SPECDEC_NOALLOC_SCRATCH_BYTES, which every GPU that loads this
 // library holds until the process exits.  It calls no cudaMalloc, cudaFree or
 // allocating library routine.
 //
 // The array is shared by every call on a device and keeps the last call's
-// contents; the error word and the arrival counters are cleared at the start of
-// each call.  Calls whose
+// contents; the error word is cleared at the start of each call.  Calls whose
 // work overlaps on the GPU (different streams, or different handles on the
 // same device) race on the array and must be serialised by the caller.  The
 // first call on each device looks up the array's device address
@@ -1152,23 +1269,21 @@ extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const
   // duration of the call and restored on every exit path.
   struct Saved {
     void *X, *H, *X1, *A, *Q, *ATT, *tk, *tv, *dk, *dv;
-    float *part;
-    int *counters, *tile_counters, *err;
+    int *err;
     RowPool pool;
     size_t tls, dls, trs, drs;
-    int tcap, dcap, R_part, max_split, R_max;
+    int tcap, dcap, R_max;
     cudaStream_t stream;
   };
-  Saved sv{h->X, h->H, h->X1, h->A, h->Q, h->ATT, h->tk, h->tv, h->dk, h->dv, h->part, h->counters, h->tile_counters,
-           h->st.err, h->pool, h->t_layer_stride, h->d_layer_stride, h->t_req_stride, h->d_req_stride, h->t_cap,
-           h->d_cap, h->R_part, h->max_split, h->R_max, h->stream};
+  Saved sv{h->X, h->H, h->X1, h->A, h->Q, h->ATT, h->tk, h->tv, h->dk, h->dv, h->st.err, h->pool,
+           h->t_layer_stride, h->d_layer_stride, h->t_req_stride, h->d_req_stride, h->t_cap, h->d_cap, h->R_max,
+           h->stream};
   auto restore = [&] {
     h->X = sv.X; h->H = sv.H; h->X1 = sv.X1; h->A = sv.A; h->Q = sv.Q; h->ATT = sv.ATT;
-    h->tk = sv.tk; h->tv = sv.tv; h->dk = sv.dk; h->dv = sv.dv; h->part = sv.part;
-    h->counters = sv.counters; h->tile_counters = sv.tile_counters; h->st.err = sv.err; h->pool = sv.pool;
+    h->tk = sv.tk; h->tv = sv.tv; h->dk = sv.dk; h->dv = sv.dv;
+    h->st.err = sv.err; h->pool = sv.pool;
     h->t_layer_stride = sv.tls; h->d_layer_stride = sv.dls; h->t_req_stride = sv.trs; h->d_req_stride = sv.drs;
-    h->t_cap = sv.tcap; h->d_cap = sv.dcap; h->R_part = sv.R_part; h->max_split = sv.max_split;
-    h->R_max = sv.R_max; h->stream = sv.stream;
+    h->t_cap = sv.tcap; h->d_cap = sv.dcap; h->R_max = sv.R_max; h->stream = sv.stream;
   };
   try {
     CK(cudaSetDevice(h->device));
@@ -1181,8 +1296,6 @@ extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const
     if (S < 1 || S > h->rope_max) fail(SPECDEC_ERR_INVALID, "sequence length out of range");
     const size_t act = h->act_elt;
     const size_t kv_elt = h->cfg.kv_dtype == SPECDEC_BF16 ? 2 : 4;
-    const int nsplit = std::max(1, std::min(16, (S + 1023) / 1024));
-    const size_t n_tiles = static_cast<size_t>(S) / kRowTile + 2;
     auto layout = [&](ArenaCarver &c, void **ptrs) {
       const size_t rows_d = static_cast<size_t>(S) * dm.d * act;
       ptrs[0] = c.take(rows_d);                                // X
@@ -1194,15 +1307,12 @@ extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const
       const size_t kv = static_cast<size_t>(std::max(1, dm.L)) * dm.Hkv * S * dm.D * kv_elt;
       ptrs[6] = c.take(kv);                                    // K cache
       ptrs[7] = c.take(kv);                                    // V cache
-      ptrs[8] = c.take(static_cast<size_t>(S) * dm.H * nsplit * (dm.D + 2) * sizeof(float));  // attention partials
-      ptrs[9] = c.take(static_cast<size_t>(S) * dm.H * sizeof(int));                          // split counters
-      ptrs[10] = c.take(n_tiles * sizeof(int));                                              // row-tile counters
-      ptrs[11] = c.take(S * sizeof(int));                      // row tokens
-      ptrs[12] = c.take(S * sizeof(int));                      // row positions
-      ptrs[13] = c.take(S * sizeof(int));                      // row requests
-      ptrs[14] = c.take(sizeof(int));                          // error word
+      ptrs[8] = c.take(S * sizeof(int));                       // row tokens
+      ptrs[9] = c.take(S * sizeof(int));                       // row positions
+      ptrs[10] = c.take(S * sizeof(int));                      // row requests
+      ptrs[11] = c.take(sizeof(int));                          // error word
     };
-    void *ptrs[15];
+    void *ptrs[12];
     ArenaCarver sizing{nullptr};
     layout(sizing, ptrs);
     if (sizing.used > SPECDEC_NOALLOC_SCRATCH_BYTES)
@@ -1216,23 +1326,16 @@ extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : h->stream;
     h->X = ptrs[0]; h->H = ptrs[1]; h->X1 = ptrs[2]; h->A = ptrs[3]; h->Q = ptrs[4]; h->ATT = ptrs[5];
     if (target) { h->tk = ptrs[6]; h->tv = ptrs[7]; } else { h->dk = ptrs[6]; h->dv = ptrs[7]; }
-    h->part = static_cast<float *>(ptrs[8]);
-    h->counters = static_cast<int *>(ptrs[9]);
-    h->tile_counters = static_cast<int *>(ptrs[10]);
-    h->pool.tok = static_cast<int *>(ptrs[11]);
-    h->pool.pos = static_cast<int *>(ptrs[12]);
-    h->pool.req = static_cast<int *>(ptrs[13]);
-    h->st.err = static_cast<int *>(ptrs[14]);
+    h->pool.tok = static_cast<int *>(ptrs[8]);
+    h->pool.pos = static_cast<int *>(ptrs[9]);
+    h->pool.req = static_cast<int *>(ptrs[10]);
+    h->st.err = static_cast<int *>(ptrs[11]);
     const size_t req_stride = static_cast<size_t>(dm.Hkv) * S * dm.D;
     if (target) { h->t_req_stride = req_stride; h->t_layer_stride = req_stride; h->t_cap = S; }
     else { h->d_req_stride = req_stride; h->d_layer_stride = req_stride; h->d_cap = S; }
-    h->R_part = S;
     h->R_max = S;
-    h->max_split = nsplit;
     h->stream = st;
     CK(cudaMemsetAsync(h->st.err, 0, sizeof(int), st));
-    CK(cudaMemsetAsync(h->counters, 0, static_cast<size_t>(S) * dm.H * sizeof(int), st));
-    CK(cudaMemsetAsync(h->tile_counters, 0, n_tiles * sizeof(int), st));
     launch(h, plan_prefill_kernel, dim3((S + 255) / 256), dim3(256), 0, d_tokens, 1, S, 0, S, dm.V, h->pool.tok,
            h->pool.pos, h->pool.req, static_cast<int *>(nullptr));
     forward_rows(h, target, 0, S, S, nullptr, S, d_logits);

@@ -22,6 +22,11 @@
 // rather than in dependent chains.
 #pragma once
 
+#include <cooperative_groups.h>
+#include <cuda.h>
+
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace specdec {
@@ -35,51 +40,18 @@ struct RowsView {
 // ---------------------------------------------------------------------------
 // Embedding gather (Embedding::forward -> CpuBackend::embedding,
 // src/backend/cpu_backend.cpp:998-1033: an out-of-range id reads row 0).  The
-// cfg architecture adds the learned position row and also writes LN1(x) for
-// the first layer.  One block per row; d <= 32 * blockDim.
+// cfg architecture adds the learned position row.  One block per row.
 template <typename AT>
 __global__ void embed_kernel(RowsView rows, int R, const float *__restrict__ emb, const float *__restrict__ pos_emb,
-                             int d, int max_pos, AT *__restrict__ x, const float *__restrict__ ln_g,
-                             const float *__restrict__ ln_b, AT *__restrict__ x_ln) {
-  __shared__ float red[32];
+                             int d, int max_pos, AT *__restrict__ x) {
   const int r = blockIdx.x;
   if (r >= R) return;
   const int id = rows.tok[r];
   const int p = min(max(rows.pos[r], 0), max_pos - 1);
-  constexpr int kMax = 32;
-  float v[kMax];
-  float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < kMax; ++i) {
-    const int c = threadIdx.x + i * blockDim.x;
-    float t = 0.f;
-    if (c < d) {
-      t = emb[static_cast<size_t>(id) * d + c];
-      if (pos_emb) t += pos_emb[static_cast<size_t>(p) * d + c];
-      t = to_f32(from_f32<AT>(t));
-      x[static_cast<size_t>(r) * d + c] = from_f32<AT>(t);
-    }
-    v[i] = t;
-    s += t;
-  }
-  if (!ln_g) return;
-  const float mean = __fdiv_rn(block_sum(s, red), static_cast<float>(d));
-  float q = 0.f;
-#pragma unroll
-  for (int i = 0; i < kMax; ++i) {
-    const int c = threadIdx.x + i * blockDim.x;
-    if (c < d) {
-      const float df = v[i] - mean;
-      q = fmaf(df, df, q);
-    }
-  }
-  const float sd = sqrtf(__fdiv_rn(block_sum(q, red), static_cast<float>(d)) + 1e-5f);
-#pragma unroll
-  for (int i = 0; i < kMax; ++i) {
-    const int c = threadIdx.x + i * blockDim.x;
-    if (c < d)
-      x_ln[static_cast<size_t>(r) * d + c] =
-          from_f32<AT>(__fadd_rn(__fmul_rn(__fdiv_rn(v[i] - mean, sd), ln_g[c]), ln_b[c]));
+  for (int c = threadIdx.x; c < d; c += blockDim.x) {
+    float t = emb[static_cast<size_t>(id) * d + c];
+    if (pos_emb) t += pos_emb[static_cast<size_t>(p) * d + c];
+    x[static_cast<size_t>(r) * d + c] = from_f32<AT>(t);
   }
 }
 
@@ -91,10 +63,14 @@ __global__ void embed_kernel(RowsView rows, int R, const float *__restrict__ emb
 // gate/up pairs land in one lane); `ksplit` warps of a block share one pair
 // and split K, so each lane issues its weight and input vectors in one go.
 // Everything the epilogue needs (scale, bias, residual, row position, RoPE
-// factors) is loaded before the dot products.  With `ln_out` set, the last
-// block to finish a row tile applies the following LayerNorm
-// (LayerNorm::forward, src/nn/layer.cpp:242-261) to the complete rows, so no
-// separate norm kernel runs.
+// factors) is loaded before the dot products.
+//
+// LayerNorm is applied by the consumer: with `in_g` set, each block first
+// normalises its kRowTile input rows into shared memory (every block holds
+// the full rows it multiplies, so a row's statistics never cross blocks),
+// and the blocks of column 0 store the normalised rows for the residual
+// that follows.  No kernel waits on another block's output and no separate
+// norm kernel runs.
 enum Epi : int {
   kEpiStore = 0,   // out = acc*s + b
   kEpiResid = 1,   // out = acc*s + b + resid
@@ -130,15 +106,13 @@ struct LinearArgs {
   int ldr;
   RowsView rows;          // row metadata (QKV epilogue)
   QKVArgs qkv;
-  const float *ln_g, *ln_b;  // optional LayerNorm of the finished output rows ...
-  void *ln_out;              // ... written here (activation dtype, leading dim ldo)
-  int *tile_counters;        // [row tiles] arrival counters (left at 0)
+  const float *in_g, *in_b;  // optional LayerNorm of the input rows (over K) before the product ...
+  void *norm_out;            // ... whose normalised rows the blocks of column 0 also store here (leading dim K)
   int ksplit;                // warps per column pair: 1, 2, 4 or 8
 };
 
 constexpr int kLinWarps = 8;
 constexpr int kRowTile = 8;
-constexpr int kLnMaxPerLane = 32;  // LayerNorm rows held in registers: N <= 1024 per warp
 
 template <typename WT> struct WVec;
 template <> struct WVec<float> { static constexpr int E = 4; };
@@ -204,19 +178,19 @@ __device__ __forceinline__ float warp_reduce16(const float (&a0)[kRowTile], cons
   return v + __shfl_xor_sync(0xffffffffu, v, 1);
 }
 
-// E consecutive input elements as fp32.
-template <typename AT, int E>
+// E consecutive input elements as fp32 (kShared: p points into shared memory).
+template <typename AT, int E, bool kShared>
 __device__ __forceinline__ void load_xvec(const AT *p, float (&xv)[E]) {
   if constexpr (sizeof(AT) == 4) {
 #pragma unroll
     for (int i = 0; i < E; i += 4) {
-      const float4 t = __ldg(reinterpret_cast<const float4 *>(p + i));
+      const float4 t = kShared ? *reinterpret_cast<const float4 *>(p + i) : __ldg(reinterpret_cast<const float4 *>(p + i));
       xv[i] = t.x; xv[i + 1] = t.y; xv[i + 2] = t.z; xv[i + 3] = t.w;
     }
   } else {
 #pragma unroll
     for (int i = 0; i < E; i += 4) {
-      const uint2 t = __ldg(reinterpret_cast<const uint2 *>(p + i));
+      const uint2 t = kShared ? *reinterpret_cast<const uint2 *>(p + i) : __ldg(reinterpret_cast<const uint2 *>(p + i));
       const __nv_bfloat162 *hh = reinterpret_cast<const __nv_bfloat162 *>(&t);
       const float2 f0 = __bfloat1622float2(hh[0]), f1 = __bfloat1622float2(hh[1]);
       xv[i] = f0.x; xv[i + 1] = f0.y; xv[i + 2] = f1.x; xv[i + 3] = f1.y;
@@ -331,48 +305,14 @@ __device__ __forceinline__ void linear_epilogue(const LinearArgs &a, int r, int 
   }
 }
 
-// LayerNorm of rows [r0, r0 + nrows) of `in` (N columns, fp32 statistics),
-// one warp per row with the row in registers; the rows were written by other
-// blocks of this grid, so they are read through L2 (ld.global.cg).
-template <typename AT>
-__device__ void rows_layernorm(const AT *in, int ld, int r0, int nrows, int N, const float *g, const float *b, AT *out) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int i = warp; i < nrows; i += blockDim.x >> 5) {
-    const AT *x = in + static_cast<size_t>(r0 + i) * ld;
-    float v[kLnMaxPerLane];
-    float s = 0.f;
-#pragma unroll
-    for (int j = 0; j < kLnMaxPerLane; ++j) {
-      const int c = lane + 32 * j;
-      v[j] = (c < N) ? to_f32(__ldcg(x + c)) : 0.f;
-      s += v[j];
-    }
-    const float mean = __fdiv_rn(warp_sum(s), static_cast<float>(N));
-    float q = 0.f;
-#pragma unroll
-    for (int j = 0; j < kLnMaxPerLane; ++j) {
-      const int c = lane + 32 * j;
-      if (c < N) {
-        const float df = v[j] - mean;
-        q = fmaf(df, df, q);
-      }
-    }
-    const float sd = sqrtf(__fdiv_rn(warp_sum(q), static_cast<float>(N)) + 1e-5f);
-    AT *y = out + static_cast<size_t>(r0 + i) * ld;
-#pragma unroll
-    for (int j = 0; j < kLnMaxPerLane; ++j) {
-      const int c = lane + 32 * j;
-      if (c < N) y[c] = from_f32<AT>(__fadd_rn(__fmul_rn(__fdiv_rn(v[j] - mean, sd), __ldg(g + c)), __ldg(b + c)));
-    }
-  }
-}
-
 // grid: (ceil(N / (2 * kLinWarps / ksplit)), ceil(R / kRowTile)); block: 32 * kLinWarps.
-template <typename WT, typename AT, int EPI>
-__global__ void __launch_bounds__(32 * kLinWarps) linear_kernel(LinearArgs a) {
+// IN_LN: dynamic shared memory of kRowTile * K activation elements holds the
+// block's normalised input rows.
+template <typename WT, typename AT, int EPI, bool IN_LN>
+__global__ void __launch_bounds__(32 * kLinWarps, 2) linear_kernel(LinearArgs a) {
   constexpr int E = WVec<WT>::E;
   __shared__ float s_red[kLinWarps][2 * kRowTile];
-  __shared__ int s_last;
+  extern __shared__ __align__(16) unsigned char lin_smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int ks = a.ksplit;
   const int pairs = kLinWarps / ks;
@@ -383,47 +323,130 @@ __global__ void __launch_bounds__(32 * kLinWarps) linear_kernel(LinearArgs a) {
   const bool col_ok = n0 < a.N;
   const bool has1 = (n0 + 1) < a.N;
 
-  float acc0[kRowTile], acc1[kRowTile];
-#pragma unroll
-  for (int i = 0; i < kRowTile; ++i) acc0[i] = acc1[i] = 0.f;
   EpiPre pre{};
-  if (col_ok) {
-    // lane 2i finishes row i: fetch its epilogue operands now
-    if (kidx == 0 && lane < 16 && !(lane & 1) && (lane >> 1) < nrows)
-      epilogue_prefetch<AT, EPI>(a, r0 + (lane >> 1), n0, pre);
-    const WT *w0 = static_cast<const WT *>(a.W) + static_cast<size_t>(n0) * a.K;
-    const WT *w1 = has1 ? w0 + a.K : w0;
-    const AT *xrow[kRowTile];
+  // lane 2i finishes row i: fetch its epilogue operands early
+  if (col_ok && kidx == 0 && lane < 16 && !(lane & 1) && (lane >> 1) < nrows)
+    epilogue_prefetch<AT, EPI>(a, r0 + (lane >> 1), n0, pre);
+
+  const WT *w0 = static_cast<const WT *>(a.W) + static_cast<size_t>(n0) * a.K;
+  const WT *w1 = has1 ? w0 + a.K : w0;
+  const int ldx = IN_LN ? a.K : a.ldx;
+  const bool vec_ok = (a.K % E == 0) && (ldx % 4 == 0);
+  const int kvec = vec_ok ? a.K / E : 0;
+  const int vstart = kidx * 32 + lane;
+  // the first K step's weights are requested before anything else, so their
+  // latency overlaps the input rows (and their LayerNorm)
+  float wa0[E], wb0[E];
+  const bool first = col_ok && vstart < kvec;
+  if (first) {
+    load_wvec(w0 + vstart * E, wa0);
+    load_wvec(w1 + vstart * E, wb0);
+  }
+
+  const AT *xrow[kRowTile];
+  if constexpr (IN_LN) {
+    // LayerNorm::forward (src/nn/layer.cpp:242-261; eps 1e-5, biased
+    // variance) of the input rows, warp i normalising row i with fp32
+    // statistics; the normalised row is rounded to the activation type.
+    // Columns c = lane + 32 j; the first kLnChunk of them per lane (all of a
+    // 256-wide row) keep x, gamma and beta in registers, loaded together.
+    constexpr int kLnChunk = 8;
+    AT *s_x = reinterpret_cast<AT *>(lin_smem);
+    if (warp < nrows) {
+      const int lr = r0 + warp;
+      const int pr = a.in_rows ? a.in_rows[lr] : lr;
+      const AT *x = static_cast<const AT *>(a.x) + static_cast<size_t>(pr) * a.ldx;
+      AT *y = s_x + warp * a.K;
+      float xv[kLnChunk], gv[kLnChunk], bv[kLnChunk];
+#pragma unroll
+      for (int j = 0; j < kLnChunk; ++j) {
+        const int c = lane + 32 * j;
+        const bool in = c < a.K;
+        xv[j] = in ? to_f32(x[c]) : 0.f;
+        gv[j] = in ? __ldg(a.in_g + c) : 0.f;
+        bv[j] = in ? __ldg(a.in_b + c) : 0.f;
+      }
+      float s = 0.f;
+#pragma unroll
+      for (int j = 0; j < kLnChunk; ++j) s += xv[j];
+      for (int c = lane + 32 * kLnChunk; c < a.K; c += 32) {
+        const AT v = x[c];
+        y[c] = v;
+        s += to_f32(v);
+      }
+      const float mean = __fdiv_rn(warp_sum(s), static_cast<float>(a.K));
+      float q = 0.f;
+#pragma unroll
+      for (int j = 0; j < kLnChunk; ++j) {
+        if (lane + 32 * j < a.K) {
+          const float df = xv[j] - mean;
+          q = fmaf(df, df, q);
+        }
+      }
+      for (int c = lane + 32 * kLnChunk; c < a.K; c += 32) {
+        const float df = to_f32(y[c]) - mean;
+        q = fmaf(df, df, q);
+      }
+      const float sd = sqrtf(__fdiv_rn(warp_sum(q), static_cast<float>(a.K)) + 1e-5f);
+      AT *no = (a.norm_out && blockIdx.x == 0) ? static_cast<AT *>(a.norm_out) + static_cast<size_t>(lr) * a.K : nullptr;
+#pragma unroll
+      for (int j = 0; j < kLnChunk; ++j) {
+        const int c = lane + 32 * j;
+        if (c < a.K) {
+          const AT v = from_f32<AT>(__fadd_rn(__fmul_rn(__fdiv_rn(xv[j] - mean, sd), gv[j]), bv[j]));
+          y[c] = v;
+          if (no) no[c] = v;
+        }
+      }
+      for (int c = lane + 32 * kLnChunk; c < a.K; c += 32) {
+        const AT v = from_f32<AT>(
+            __fadd_rn(__fmul_rn(__fdiv_rn(to_f32(y[c]) - mean, sd), __ldg(a.in_g + c)), __ldg(a.in_b + c)));
+        y[c] = v;
+        if (no) no[c] = v;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kRowTile; ++i) xrow[i] = s_x + (i < nrows ? i : 0) * a.K;
+  } else {
 #pragma unroll
     for (int i = 0; i < kRowTile; ++i) {
       const int lr = r0 + (i < nrows ? i : 0);
       const int pr = a.in_rows ? a.in_rows[lr] : lr;
       xrow[i] = static_cast<const AT *>(a.x) + static_cast<size_t>(pr) * a.ldx;
     }
-    const bool vec_ok = (a.K % E == 0) && (a.ldx % 4 == 0);
-    const int kvec = vec_ok ? a.K / E : 0;
+  }
+
+  float acc0[kRowTile], acc1[kRowTile];
+#pragma unroll
+  for (int i = 0; i < kRowTile; ++i) acc0[i] = acc1[i] = 0.f;
+  auto step = [&](int v, const float (&wa)[E], const float (&wb)[E]) {
+    float xv[kRowTile][E];
+#pragma unroll
+    for (int i = 0; i < kRowTile; ++i)
+      if (i < nrows) load_xvec<AT, E, IN_LN>(xrow[i] + v * E, xv[i]);
+#pragma unroll
+    for (int i = 0; i < kRowTile; ++i) {
+      if (i < nrows) {
+        float t0 = 0.f, t1 = 0.f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          t0 = fmaf(xv[i][e], wa[e], t0);
+          t1 = fmaf(xv[i][e], wb[e], t1);
+        }
+        acc0[i] += t0;
+        acc1[i] += t1;
+      }
+    }
+  };
+  if (col_ok) {
+    if (first) step(vstart, wa0, wb0);
 #pragma unroll 2
-    for (int v = kidx * 32 + lane; v < kvec; v += 32 * ks) {
+    for (int v = vstart + 32 * ks; v < kvec; v += 32 * ks) {
       float wa[E], wb[E];
       load_wvec(w0 + v * E, wa);
       load_wvec(w1 + v * E, wb);
-      float xv[kRowTile][E];
-#pragma unroll
-      for (int i = 0; i < kRowTile; ++i)
-        if (i < nrows) load_xvec<AT, E>(xrow[i] + v * E, xv[i]);
-#pragma unroll
-      for (int i = 0; i < kRowTile; ++i) {
-        if (i < nrows) {
-          float t0 = 0.f, t1 = 0.f;
-#pragma unroll
-          for (int e = 0; e < E; ++e) {
-            t0 = fmaf(xv[i][e], wa[e], t0);
-            t1 = fmaf(xv[i][e], wb[e], t1);
-          }
-          acc0[i] += t0;
-          acc1[i] += t1;
-        }
-      }
+      step(v, wa, wb);
     }
     for (int k = kvec * E + kidx * 32 + lane; k < a.K; k += 32 * ks) {  // scalar tail / unaligned rows
       const float wa = static_cast<float>(w0[k]), wb = static_cast<float>(w1[k]);
@@ -451,61 +474,67 @@ __global__ void __launch_bounds__(32 * kLinWarps) linear_kernel(LinearArgs a) {
   const float tot1 = __shfl_xor_sync(0xffffffffu, tot, 16);
   if (col_ok && kidx == 0 && lane < 16 && !(lane & 1) && (lane >> 1) < nrows)
     linear_epilogue<AT, EPI>(a, r0 + (lane >> 1), n0, tot, tot1, pre);
-  if (!a.ln_out) return;
-  // the last block of this row tile normalises the finished rows
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int *cnt = a.tile_counters + blockIdx.y;
-    const int prev = atomicAdd(cnt, 1);
-    s_last = (prev == static_cast<int>(gridDim.x) - 1) ? 1 : 0;
-    if (s_last) *cnt = 0;
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  rows_layernorm<AT>(static_cast<const AT *>(a.out), a.ldo, r0, nrows, a.N, a.ln_g, a.ln_b, static_cast<AT *>(a.ln_out));
 }
 
 // ---------------------------------------------------------------------------
 // Causal attention (src/nn/layer.cpp:859-948): score = (q . k) / sqrt(D)
 // (layer.cpp:870, 891-897), softmax over positions j <= pos, then P.V.
 //
-// The rows of one request in one forward pass are consecutive and form a
-// "group" of Q queries (the k+1 verify rows, the catch-up + last draft rows,
-// a prefill chunk); a block handles up to QT queries of one group for one head
-// and one split of the context, so the request's K/V are read once for all of
-// them.  K/V arrive in tiles of kAttnTile positions that one thread copies
-// into shared memory with TMA bulk copies (cp.async.bulk, completion on an
-// mbarrier; a (request, head) tile is contiguous in the cache), double
-// buffered so the next tile streams in while the current one is used.  Warp w
-// owns tile positions w*32 .. w*32+31 (one per lane) and keeps an online
-// softmax per query; P.V is accumulated with lanes owning head dimensions.
-// Warps are merged through shared memory.  With several splits each block
-// writes (max, sum, acc[D]) partials and the last block of a (query tile,
-// head) merges them (log-sum-exp), so no separate combine kernel runs.
+// Work split.  The rows of one request in one forward pass are consecutive
+// and form a "group" of Q queries (the k+1 verify rows, the catch-up + last
+// draft rows, a prefill chunk).  A CTA handles up to QT queries of one group
+// for one head and one split (a contiguous chunk of positions) of the
+// context, so the request's K/V are read once for all of its queries.  The
+// splits of one (query tile, head) are one thread-block cluster along z:
+// each CTA leaves its (max, sum, unnormalised P.V) in its own shared memory
+// and, after a cluster barrier, every CTA merges a share of the outputs
+// (log-sum-exp) by reading its peers' shared memory, so the split merge costs
+// no global-memory round trip.
+//
+// Staging.  Thread 0 issues TMA tensor copies (cp.async.bulk.tensor.2d, no
+// multicast, completion on an mbarrier) of kTile cache rows of K and of V;
+// with several tiles per chunk the two stages alternate.  Rows that are a
+// multiple of 128 bytes wide arrive with the 128-byte swizzle (16-byte unit
+// j of row r lands in unit j ^ (r & 7) of its 128-byte line), so the score
+// loop -- thread = position, walking the head dimension -- reads K without
+// bank conflicts while all threads read the same q words (broadcast).  P.V
+// has lanes over head dimensions and reads the warp's probabilities from
+// shared memory as broadcasts.
 constexpr int kAttnThreads = 128;
 constexpr int kAttnWarps = kAttnThreads / 32;
-constexpr int kAttnQT = 8;  // most queries per block (the group size rounds up to 1, 2, 4 or 8)
+constexpr int kAttnQT = 8;        // most queries per CTA (a group rounds up to 1, 2, 4 or 8)
+constexpr int kAttnMaxSplit = 8;  // portable cluster size
 
-// Positions per shared-memory tile: 128 (one per thread), or 64 when a K/V
-// row is wider than 256 bytes so two stages of K and V stay within 128 KiB.
 template <typename KT, int D>
-constexpr int attn_tile() { return (D * sizeof(KT) > 256) ? 64 : 128; }
+struct AttnGeom {
+  static constexpr int kRowBytes = D * static_cast<int>(sizeof(KT));
+  static constexpr bool kTma = kRowBytes % 16 == 0;  // else the host rejects the shape
+  static constexpr bool kSwz = kRowBytes % 128 == 0;
+  static constexpr int kTile = kRowBytes > 256 ? 64 : 128;  // rows per stage
+  static constexpr int kE = 16 / static_cast<int>(sizeof(KT));  // elements per 16-byte unit
+  static constexpr int kNC = kRowBytes / 16;                      // 16-byte units per row
+  static constexpr int kStageBytes = 2 * kTile * kRowBytes;       // K tile + V tile
+  static constexpr int kEPL = D >= 32 ? D / 32 : 1;               // P.V: head dims per lane
+  static constexpr int kLanesPV = D / kEPL;
+  static constexpr int kBoxCols = kSwz ? 128 / static_cast<int>(sizeof(KT)) : D;  // TMA box width
+  static constexpr int smem_bytes(int stages) { return stages * kStageBytes + 1024; }
+  // byte offset of 16-byte unit c of tile row r within a K or V tile
+  __device__ static __forceinline__ int unit(int r, int c) {
+    if constexpr (kSwz) return (c >> 3) * (kTile * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4);
+    else return r * kRowBytes + c * 16;
+  }
+};
 
-struct AttnArgs {
+struct alignas(64) AttnArgs {
+  CUtensorMap tmk, tmv;  // 2-D views [slot * Hkv * S_cap + position][D] of this layer's K and V cache
   const void *q;
   int ldq;
   RowsView rows;
-  int R, Q;                 // rows, queries per group
-  const void *kc, *vc;
-  size_t kv_req_stride;
+  int R, Q;      // rows, queries per group
   int S_cap, H, Hkv;
   int chunk, nsplit;
   void *out;
   int ldo;
-  float *part;              // [R][H][nsplit][D + 2]
-  int *counters;            // [R][H] split arrival counters (left at 0)
   int *err;
 };
 
@@ -513,10 +542,17 @@ __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-// Polls an mbarrier phase a bounded number of times; false = gave up.
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Polls an mbarrier phase for at most about a second; false = gave up.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t phase) {
   const uint32_t addr = smem_u32(bar);
-  for (int it = 0; it < (1 << 22); ++it) {
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; ++it) {
     uint32_t done;
     asm volatile(
         "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
@@ -524,35 +560,86 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t phase) {
         : "r"(addr), "r"(phase)
         : "memory");
     if (done) return true;
+    if ((it & 63) == 0) {
+      const uint64_t now = global_ns();
+      if (it == 0) t0 = now;
+      else if (now - t0 > 1000000000ull) return false;
+    }
   }
-  return false;
 }
 
-// One bulk copy global -> this CTA's shared memory (no multicast), completing
-// `bytes` (multiple of 16, both addresses 16-byte aligned) on `bar`.
-__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
-                   smem_u32(dst)),
-               "l"(src), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
+// One tiled TMA load of box (x, y) of `map` into this CTA's shared memory,
+// completing on `bar`.  x * sizeof(element) is a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
 }
 
-template <typename KT, int D>
-constexpr int attn_smem_bytes() {
-  return 2 /*stages*/ * 2 /*K,V*/ * attn_tile<KT, D>() * D * static_cast<int>(sizeof(KT));
+// 16 bytes of cache elements -> fp32
+__device__ __forceinline__ void unpack16(uint4 u, float *f, float) {
+  f[0] = __uint_as_float(u.x); f[1] = __uint_as_float(u.y);
+  f[2] = __uint_as_float(u.z); f[3] = __uint_as_float(u.w);
+}
+__device__ __forceinline__ void unpack16(uint4 u, float *f, __nv_bfloat16) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
+// N consecutive cache elements at shared address p -> fp32
+template <typename KT, int N>
+__device__ __forceinline__ void lds_elems(const unsigned char *p, float *f) {
+  constexpr int bytes = N * static_cast<int>(sizeof(KT));
+  if constexpr (std::is_same<KT, float>::value) {
+    if constexpr (bytes == 16) {
+      const float4 v = *reinterpret_cast<const float4 *>(p);
+      f[0] = v.x; f[1] = v.y; f[2] = v.z; f[3] = v.w;
+    } else if constexpr (bytes == 8) {
+      const float2 v = *reinterpret_cast<const float2 *>(p);
+      f[0] = v.x; f[1] = v.y;
+    } else {
+      f[0] = *reinterpret_cast<const float *>(p);
+    }
+  } else {
+    if constexpr (bytes == 8) {
+      const uint2 v = *reinterpret_cast<const uint2 *>(p);
+      f[0] = __uint_as_float(v.x << 16); f[1] = __uint_as_float(v.x & 0xffff0000u);
+      f[2] = __uint_as_float(v.y << 16); f[3] = __uint_as_float(v.y & 0xffff0000u);
+    } else if constexpr (bytes == 4) {
+      const uint32_t v = *reinterpret_cast<const uint32_t *>(p);
+      f[0] = __uint_as_float(v << 16); f[1] = __uint_as_float(v & 0xffff0000u);
+    } else {
+      f[0] = __uint_as_float(static_cast<uint32_t>(*reinterpret_cast<const unsigned short *>(p)) << 16);
+    }
+  }
 }
 
 template <typename AT, typename KT, int D, int QT>
-__global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a) {
-  constexpr int DC = (D + 31) / 32;  // dims per lane in P.V
-  constexpr bool kBulk = (D * sizeof(KT)) % 16 == 0;
-  constexpr int kAttnTile = attn_tile<KT, D>();
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  KT *tiles = reinterpret_cast<KT *>(smem_raw);  // [stage][K|V][kAttnTile][D]
-  __shared__ float qs[QT][D];
+__global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_constant__ AttnArgs a) {
+  using G = AttnGeom<KT, D>;
+  if constexpr (!G::kTma) {
+    return;  // unreachable: the host rejects rows that are not a multiple of 16 bytes
+  } else {
+  constexpr int kTile = G::kTile;
+  constexpr int EPL = G::kEPL;
+  constexpr int NACC = QT == 1 ? 4 : (QT == 2 ? 2 : 1);  // independent partial dots per query
+  constexpr bool kSqrtPow2 = D == 4 || D == 16 || D == 64;
+  constexpr float kInvSqrt = D == 4 ? 0.5f : D == 16 ? 0.25f : 0.125f;
+  extern __shared__ unsigned char attn_smem_raw[];
+  unsigned char *tiles =
+      reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(attn_smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(16) float qs[QT][D];
+  __shared__ __align__(16) float s_p[kAttnWarps][QT][32];
+  __shared__ __align__(16) float s_acc[kAttnWarps][QT][D];  // [0] holds the CTA's merged P.V
   __shared__ float s_m[kAttnWarps][QT], s_l[kAttnWarps][QT];
-  __shared__ float s_acc[kAttnWarps][QT][D];
-  __shared__ int s_pos[QT], s_req[QT], s_last;
+  __shared__ float c_m[QT], c_l[QT];  // the CTA's merged max and sum
+  __shared__ int s_pos[QT], s_req[QT];
   __shared__ __align__(8) uint64_t bars[2];
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -562,40 +649,77 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a) {
   const int rq0 = g * a.Q + qt * QT;
   const int nq = max(0, min(QT, min(a.Q - qt * QT, a.R - rq0)));
 
-  // query metadata and vectors, all loads in parallel
-  if (threadIdx.x < QT) {
-    const int i = threadIdx.x;
-    const int rr = (i < nq) ? a.rows.req[rq0 + i] : -1;
-    s_req[i] = rr;
-    s_pos[i] = (rr >= 0) ? a.rows.pos[rq0 + i] : -1;
-  }
-  for (int idx = threadIdx.x; idx < QT * D; idx += blockDim.x) {
-    const int i = idx / D, e = idx % D;
-    qs[i][e] = (i < nq) ? to_f32(static_cast<const AT *>(a.q)[static_cast<size_t>(rq0 + i) * a.ldq + h * D + e]) : 0.f;
-  }
-  if (kBulk && threadIdx.x == 0) {
+  const int hk = h / (a.H / a.Hkv);
+  const float scale = sqrtf(static_cast<float>(D));
+  __shared__ int s_meta[2];
+  // Thread 0 reads the queries' rows, then issues the first tile while the
+  // other threads fetch the query vectors.
+  auto span = [&](int maxpos, int &j0, int &j1) {
+    j0 = split * a.chunk;
+    j1 = min(maxpos + 1, j0 + a.chunk);
+    return (j1 > j0) ? (j1 - j0 + kTile - 1) / kTile : 0;
+  };
+  auto issue = [&](int t, int row0, int j0) {  // thread 0 only
+    const int s = t & 1;
+    unsigned char *kdst = tiles + s * G::kStageBytes;
+    unsigned char *vdst = kdst + kTile * G::kRowBytes;
+    const int y = row0 + j0 + t * kTile;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&bars[s])),
+                 "r"(G::kStageBytes)
+                 : "memory");
+#pragma unroll
+    for (int cb = 0; cb < D / G::kBoxCols; ++cb) {
+      tma_load_2d(kdst + cb * kTile * 128, &a.tmk, cb * G::kBoxCols, y, &bars[s]);
+      tma_load_2d(vdst + cb * kTile * 128, &a.tmv, cb * G::kBoxCols, y, &bars[s]);
+    }
+  };
+  if (threadIdx.x == 0) {
+    int rr[QT], pr[QT];
+#pragma unroll
+    for (int i = 0; i < QT; ++i) {
+      rr[i] = (i < nq) ? a.rows.req[rq0 + i] : -1;
+      pr[i] = (i < nq) ? a.rows.pos[rq0 + i] : -1;
+    }
+    int req = -1, maxpos = -1;
+#pragma unroll
+    for (int i = 0; i < QT; ++i) {
+      s_req[i] = rr[i];
+      s_pos[i] = (rr[i] >= 0) ? pr[i] : -1;
+      if (rr[i] >= 0) {
+        req = rr[i];
+        maxpos = max(maxpos, pr[i]);
+      }
+    }
+    s_meta[0] = req;
+    s_meta[1] = maxpos;
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&bars[0])) : "memory");
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&bars[1])) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    if (req >= 0 && maxpos < a.S_cap) {
+      int j0, j1;
+      if (span(maxpos, j0, j1) > 0) issue(0, (req * a.Hkv + hk) * a.S_cap, j0);
+    }
+  }
+  constexpr int kQIter = (QT * D + kAttnThreads - 1) / kAttnThreads;
+#pragma unroll
+  for (int k = 0; k < kQIter; ++k) {
+    const int idx = threadIdx.x + k * kAttnThreads;
+    if (idx < QT * D) {
+      const int i = idx / D, e = idx % D;
+      qs[i][e] =
+          (i < nq) ? to_f32(static_cast<const AT *>(a.q)[static_cast<size_t>(rq0 + i) * a.ldq + h * D + e]) : 0.f;
+    }
   }
   __syncthreads();
-  int req = -1, maxpos = -1;
-#pragma unroll
-  for (int i = 0; i < QT; ++i)
-    if (s_req[i] >= 0) {
-      req = s_req[i];
-      maxpos = max(maxpos, s_pos[i]);
-    }
-  if (req < 0 || maxpos >= a.S_cap) return;  // uniform over the block
+  const int req = s_meta[0], maxpos = s_meta[1];
+  // uniform over the cluster: all its CTAs share (query tile, head)
+  if (req < 0 || maxpos >= a.S_cap) return;
+  int j0, j1;
+  const int ntiles = span(maxpos, j0, j1);
+  const int row0 = (req * a.Hkv + hk) * a.S_cap;
 
-  const int ctx = maxpos + 1;
-  const int j0 = split * a.chunk, j1 = min(ctx, j0 + a.chunk);
-  const int hk = h / (a.H / a.Hkv);
-  const KT *kb = static_cast<const KT *>(a.kc) + static_cast<size_t>(req) * a.kv_req_stride + static_cast<size_t>(hk) * a.S_cap * D;
-  const KT *vb = static_cast<const KT *>(a.vc) + static_cast<size_t>(req) * a.kv_req_stride + static_cast<size_t>(hk) * a.S_cap * D;
-  const float scale = sqrtf(static_cast<float>(D));
-
-  float m[QT], l[QT], acc[QT][DC];
+  float m[QT], l[QT], acc[QT][EPL];
   int qpos[QT];
 #pragma unroll
   for (int i = 0; i < QT; ++i) {
@@ -603,111 +727,130 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a) {
     l[i] = 0.f;
     qpos[i] = s_pos[i];
 #pragma unroll
-    for (int c = 0; c < DC; ++c) acc[i][c] = 0.f;
+    for (int e = 0; e < EPL; ++e) acc[i][e] = 0.f;
   }
+  // P.V: this lane's head dimensions [lane*EPL, lane*EPL + EPL) in unit pv_c at byte pv_b
+  const int pv_c = (lane * EPL) / G::kE;
+  const int pv_b = ((lane * EPL) % G::kE) * static_cast<int>(sizeof(KT));
 
-  const int ntiles = (j1 > j0) ? (j1 - j0 + kAttnTile - 1) / kAttnTile : 0;
-  auto issue = [&](int t) {  // thread 0 only
-    const int t0 = j0 + t * kAttnTile;
-    const int nt = min(kAttnTile, j1 - t0);
-    KT *kt = tiles + (t & 1) * 2 * kAttnTile * D;
-    const uint32_t bytes = static_cast<uint32_t>(nt * D * sizeof(KT));
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&bars[t & 1])), "r"(2 * bytes)
-                 : "memory");
-    bulk_g2s(kt, kb + static_cast<size_t>(t0) * D, bytes, &bars[t & 1]);
-    bulk_g2s(kt + kAttnTile * D, vb + static_cast<size_t>(t0) * D, bytes, &bars[t & 1]);
-  };
-  if (kBulk && threadIdx.x == 0 && ntiles > 0) issue(0);
   bool ok = true;
-  for (int t = 0; t < ntiles; ++t) {
-    const int t0 = j0 + t * kAttnTile;
-    const int nt = min(kAttnTile, j1 - t0);
-    KT *ktile = tiles + (t & 1) * 2 * kAttnTile * D;
-    KT *vtile = ktile + kAttnTile * D;
-    if constexpr (kBulk) {
-      if (threadIdx.x == 0 && t + 1 < ntiles) issue(t + 1);  // the other stage was released at the end of t-1
-      ok = __syncthreads_and(mbar_wait(&bars[t & 1], (t >> 1) & 1) ? 1 : 0) != 0;
-      if (!ok) break;
-    } else {
-      for (int idx = threadIdx.x; idx < nt * D; idx += blockDim.x) {
-        ktile[idx] = kb[static_cast<size_t>(t0) * D + idx];
-        vtile[idx] = vb[static_cast<size_t>(t0) * D + idx];
-      }
-      __syncthreads();
-    }
-    // scores: lane = position; the dot product walks the head dimension
-    // rotated by the lane so the 32 lanes read 32 different banks
-    const int tp = warp * 32 + lane;
-    const int pos = t0 + tp;
-    float p[QT];
+  int t = 0;
+  for (; t < ntiles; ++t) {
+    const int t0 = j0 + t * kTile;
+    const int nt = min(kTile, j1 - t0);
+    if (threadIdx.x == 0 && t + 1 < ntiles) issue(t + 1, row0, j0);  // the other stage was released at the end of t-1
+    ok = __syncthreads_and(mbar_wait(&bars[t & 1], (t >> 1) & 1) ? 1 : 0) != 0;
+    if (!ok) break;
+    const unsigned char *kt = tiles + (t & 1) * G::kStageBytes;
+    const unsigned char *vt = kt + kTile * G::kRowBytes;
+
+    // scores: thread = tile row
+    const int r = threadIdx.x;
+    const int pos = t0 + r;
+    float sc[QT];
     {
-      float kr[D];
-      if (tp < nt) {
+      float dot[QT][NACC];
 #pragma unroll
-        for (int c = 0; c < D; ++c) kr[c] = to_f32(ktile[tp * D + ((c + lane) % D)]);
-      }
-      float sc[QT];
+      for (int i = 0; i < QT; ++i)
 #pragma unroll
-      for (int i = 0; i < QT; ++i) {
-        sc[i] = -INFINITY;
-        if (i < nq && tp < nt && pos <= qpos[i]) {
-          float dot = 0.f;
+        for (int u = 0; u < NACC; ++u) dot[i][u] = 0.f;
+      // Branch-free: all QT queries (rows past nq hold zeros) and all
+      // threads (with 64-row tiles the upper threads read in-bounds rows of
+      // the stage and are masked below).
 #pragma unroll
-          for (int c = 0; c < D; ++c) dot = fmaf(qs[i][(c + lane) % D], kr[c], dot);
-          sc[i] = __fdiv_rn(dot, scale);
+      for (int c = 0; c < G::kNC; ++c) {
+        float kf[G::kE];
+        unpack16(*reinterpret_cast<const uint4 *>(kt + G::unit(r, c)), kf, KT{});
+#pragma unroll
+        for (int i = 0; i < QT; ++i) {
+#pragma unroll
+          for (int e = 0; e < G::kE; e += 4) {
+            const float4 q4 = *reinterpret_cast<const float4 *>(&qs[i][c * G::kE + e]);
+            const int u = ((c * G::kE + e) / 4) % NACC;
+            dot[i][u] = fmaf(q4.x, kf[e], dot[i][u]);
+            dot[i][u] = fmaf(q4.y, kf[e + 1], dot[i][u]);
+            dot[i][u] = fmaf(q4.z, kf[e + 2], dot[i][u]);
+            dot[i][u] = fmaf(q4.w, kf[e + 3], dot[i][u]);
+          }
         }
       }
-      // tile maxima and sums of all queries, butterflies interleaved
-      float tm[QT];
-#pragma unroll
-      for (int i = 0; i < QT; ++i) tm[i] = sc[i];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int i = 0; i < QT; ++i) tm[i] = fmaxf(tm[i], __shfl_xor_sync(0xffffffffu, tm[i], o));
-      float ps[QT], alpha[QT];
 #pragma unroll
       for (int i = 0; i < QT; ++i) {
-        const float mnew = fmaxf(m[i], tm[i]);
-        p[i] = (sc[i] == -INFINITY) ? 0.f : expf(sc[i] - mnew);
-        alpha[i] = (m[i] == -INFINITY) ? 0.f : expf(m[i] - mnew);
-        m[i] = mnew;
-        ps[i] = p[i];
-      }
+        float dd = dot[i][0];
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int i = 0; i < QT; ++i) ps[i] += __shfl_xor_sync(0xffffffffu, ps[i], o);
-#pragma unroll
-      for (int i = 0; i < QT; ++i) {
-        l[i] = l[i] * alpha[i] + ps[i];
-#pragma unroll
-        for (int c = 0; c < DC; ++c) acc[i][c] *= alpha[i];
+        for (int u = 1; u < NACC; ++u) dd += dot[i][u];
+        // sqrt(D) is a power of two for D = 4, 16, 64: the product by its
+        // reciprocal is then the correctly rounded quotient
+        const float sv = kSqrtPow2 ? dd * kInvSqrt : __fdiv_rn(dd, scale);
+        sc[i] = (i < nq && r < nt && pos <= qpos[i]) ? sv : -INFINITY;
       }
     }
-    const int nvalid = max(0, min(32, nt - warp * 32));
-    for (int pp = 0; pp < nvalid; ++pp) {
-      float vv[DC];
+    // online softmax per warp: the warp's running max is shared by its lanes
+    float tm[QT];
 #pragma unroll
-      for (int c = 0; c < DC; ++c) {
-        const int e = lane + 32 * c;
-        vv[c] = (e < D) ? to_f32(vtile[(warp * 32 + pp) * D + e]) : 0.f;
-      }
+    for (int i = 0; i < QT; ++i) tm[i] = sc[i];
 #pragma unroll
-      for (int i = 0; i < QT; ++i) {
-        const float pb = __shfl_sync(0xffffffffu, p[i], pp);
+    for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-        for (int c = 0; c < DC; ++c) acc[i][c] = fmaf(pb, vv[c], acc[i][c]);
+      for (int i = 0; i < QT; ++i) tm[i] = fmaxf(tm[i], __shfl_xor_sync(0xffffffffu, tm[i], o));
+#pragma unroll
+    for (int i = 0; i < QT; ++i) {
+      const float mnew = fmaxf(m[i], tm[i]);
+      const float p = (sc[i] == -INFINITY) ? 0.f : expf(sc[i] - mnew);
+      const float alpha = (m[i] == -INFINITY) ? 0.f : expf(m[i] - mnew);
+      m[i] = mnew;
+      l[i] = l[i] * alpha + p;  // per-lane partial sum, reduced after the loop
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) acc[i][e] *= alpha;
+      s_p[warp][i][lane] = p;
+    }
+    __syncwarp();
+    // P.V over the warp's 32 rows; rows past the tile's end re-read its last
+    // row (finite) with probability 0
+    const int nvalid = min(32, nt - warp * 32);
+    if (lane < G::kLanesPV && nvalid > 0) {
+#pragma unroll
+      for (int pp = 0; pp < 32; pp += 4) {
+        float v[4][EPL];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          lds_elems<KT, EPL>(vt + G::unit(warp * 32 + min(pp + u, nvalid - 1), pv_c) + pv_b, v[u]);
+#pragma unroll
+        for (int i = 0; i < QT; ++i) {
+          const float4 p4 = *reinterpret_cast<const float4 *>(&s_p[warp][i][pp]);
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) {
+            acc[i][e] = fmaf(p4.x, v[0][e], acc[i][e]);
+            acc[i][e] = fmaf(p4.y, v[1][e], acc[i][e]);
+            acc[i][e] = fmaf(p4.z, v[2][e], acc[i][e]);
+            acc[i][e] = fmaf(p4.w, v[3][e], acc[i][e]);
+          }
+        }
       }
     }
-    __syncthreads();  // this stage is refilled two tiles later
+    __syncthreads();  // this stage is refilled two tiles later; s_p is rewritten next tile
   }
   if (!ok) {
-    if (threadIdx.x == 0 && a.err) atomicOr(a.err, kErrTimeout);
-    return;  // uniform: decided by the block vote
+    // give the copies in flight a bounded time to land before the CTA moves on
+    if (threadIdx.x == 0) {
+      mbar_wait(&bars[t & 1], (t >> 1) & 1);
+      if (t + 1 < ntiles) mbar_wait(&bars[(t + 1) & 1], ((t + 1) >> 1) & 1);
+      if (a.err) atomicOr(a.err, kErrTimeout);
+    }
+#pragma unroll
+    for (int i = 0; i < QT; ++i) {
+      m[i] = -INFINITY;
+      l[i] = 0.f;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) acc[i][e] = 0.f;
+    }
   }
-  // merge the block's warps
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int i = 0; i < QT; ++i) l[i] += __shfl_xor_sync(0xffffffffu, l[i], o);
+
+  // merge the CTA's warps
   if (lane == 0) {
 #pragma unroll
     for (int i = 0; i < QT; ++i) {
@@ -715,17 +858,18 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a) {
       s_l[warp][i] = l[i];
     }
   }
+  if (lane < G::kLanesPV) {
 #pragma unroll
-  for (int i = 0; i < QT; ++i)
+    for (int i = 0; i < QT; ++i)
 #pragma unroll
-    for (int c = 0; c < DC; ++c) {
-      const int e = lane + 32 * c;
-      if (e < D) s_acc[warp][i][e] = acc[i][c];
-    }
+      for (int e = 0; e < EPL; ++e) s_acc[warp][i][lane * EPL + e] = acc[i][e];
+  }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < nq * D; idx += blockDim.x) {
+#pragma unroll
+  for (int k = 0; k < kQIter; ++k) {
+    const int idx = threadIdx.x + k * kAttnThreads;
+    if (idx >= QT * D) break;
     const int i = idx / D, e = idx % D;
-    if (s_pos[i] < 0) continue;
     float M = -INFINITY;
 #pragma unroll
     for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, s_m[w][i]);
@@ -737,50 +881,53 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a) {
       L += s_l[w][i] * f;
       A += s_acc[w][i][e] * f;
     }
-    const int r = rq0 + i;
     if (a.nsplit == 1) {
-      static_cast<AT *>(a.out)[static_cast<size_t>(r) * a.ldo + h * D + e] = from_f32<AT>(L > 0.f ? A / L : 0.f);
+      if (i < nq && s_pos[i] >= 0)
+        static_cast<AT *>(a.out)[static_cast<size_t>(rq0 + i) * a.ldo + h * D + e] = from_f32<AT>(L > 0.f ? A / L : 0.f);
     } else {
-      float *pp = a.part + ((static_cast<size_t>(r) * a.H + h) * a.nsplit + split) * (D + 2);
-      pp[2 + e] = A;
+      s_acc[0][i][e] = A;  // only this thread reads or writes (i, e) here
       if (e == 0) {
-        pp[0] = M;
-        pp[1] = L;
+        c_m[i] = M;
+        c_l[i] = L;
       }
     }
   }
   if (a.nsplit == 1) return;
-  // the last block of this (query tile, head) to arrive merges the splits
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int *cnt = a.counters + static_cast<size_t>(rq0) * a.H + h;
-    const int prev = atomicAdd(cnt, 1);
-    s_last = (prev == a.nsplit - 1) ? 1 : 0;
-    if (s_last) *cnt = 0;
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  for (int idx = threadIdx.x; idx < nq * D; idx += blockDim.x) {
+
+  // merge the splits through distributed shared memory
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
+  cl.sync();
+  const int rank = static_cast<int>(cl.block_rank());
+  for (int idx = rank * blockDim.x + threadIdx.x; idx < nq * D; idx += a.nsplit * blockDim.x) {
     const int i = idx / D, e = idx % D;
     if (s_pos[i] < 0) continue;
-    const int r = rq0 + i;
-    const float *pp = a.part + (static_cast<size_t>(r) * a.H + h) * a.nsplit * (D + 2);
-    float M = -INFINITY;
-    for (int s = 0; s < a.nsplit; ++s)
-      if (__ldcg(pp + s * (D + 2) + 1) > 0.f) M = fmaxf(M, __ldcg(pp + s * (D + 2)));
-    float L = 0.f, A = 0.f;
-    for (int s = 0; s < a.nsplit; ++s) {
-      const float *ps = pp + s * (D + 2);
-      const float ls = __ldcg(ps + 1);
-      if (ls > 0.f) {
-        const float w = expf(__ldcg(ps) - M);
-        L += ls * w;
-        A += __ldcg(ps + 2 + e) * w;
+    float Ms[kAttnMaxSplit], Ls[kAttnMaxSplit], As[kAttnMaxSplit];
+#pragma unroll
+    for (int s = 0; s < kAttnMaxSplit; ++s) {
+      Ls[s] = 0.f;
+      if (s < a.nsplit) {
+        Ms[s] = *cl.map_shared_rank(&c_m[i], s);
+        Ls[s] = *cl.map_shared_rank(&c_l[i], s);
+        As[s] = *cl.map_shared_rank(&s_acc[0][i][e], s);
       }
     }
-    static_cast<AT *>(a.out)[static_cast<size_t>(r) * a.ldo + h * D + e] = from_f32<AT>(L > 0.f ? A / L : 0.f);
+    float M = -INFINITY;
+#pragma unroll
+    for (int s = 0; s < kAttnMaxSplit; ++s)
+      if (Ls[s] > 0.f) M = fmaxf(M, Ms[s]);
+    float L = 0.f, A = 0.f;
+#pragma unroll
+    for (int s = 0; s < kAttnMaxSplit; ++s) {
+      if (Ls[s] > 0.f) {
+        const float w = expf(Ms[s] - M);
+        L += Ls[s] * w;
+        A += As[s] * w;
+      }
+    }
+    static_cast<AT *>(a.out)[static_cast<size_t>(rq0 + i) * a.ldo + h * D + e] = from_f32<AT>(L > 0.f ? A / L : 0.f);
+  }
+  cl.sync();  // every CTA's shared memory stays in place until its peers have read it
   }
 }
 
