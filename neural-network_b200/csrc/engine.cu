@@ -81,9 +81,12 @@ struct GraphKey {
   int B, S, k, greedy, rng_mode, catchup, max_new, u_rounds;
   float T;
   uint32_t seed;
+  int top_k;
+  float top_p;
   bool operator<(const GraphKey &o) const {
-    return std::tie(B, S, k, greedy, rng_mode, catchup, max_new, u_rounds, T, seed) <
-           std::tie(o.B, o.S, o.k, o.greedy, o.rng_mode, o.catchup, o.max_new, o.u_rounds, o.T, o.seed);
+    return std::tie(B, S, k, greedy, rng_mode, catchup, max_new, u_rounds, T, seed, top_k, top_p) <
+           std::tie(o.B, o.S, o.k, o.greedy, o.rng_mode, o.catchup, o.max_new, o.u_rounds, o.T, o.seed, o.top_k,
+                    o.top_p);
   }
 };
 
@@ -698,9 +701,7 @@ void validate_gen(specdec_handle *h, const specdec_gen_params *p, int B, int S) 
   // max_seq_len (src/nn/layer.cpp:1176-1179).
   if (S + (p->max_new_tokens > 1 ? p->max_new_tokens : 0) > h->t_cap)
     fail(SPECDEC_ERR_SEQ_LEN, "Sequence length S plus past cached length exceeds max_seq_len");
-  const int V = h->tgt.dm.V;
-  if ((p->top_k > 0 && p->top_k < V) || (p->top_p > 0.f && p->top_p < 1.f))
-    fail(SPECDEC_ERR_UNSUPPORTED, "top-k / top-p filtering is not implemented on the device path");
+  if (!(p->top_p == p->top_p)) fail(SPECDEC_ERR_INVALID, "top_p is NaN");
   if (p->rng_mode == SPECDEC_RNG_HOST_UNIFORM && p->temperature > 0.f) {
     if (!p->uniforms || p->uniform_rounds < 1) fail(SPECDEC_ERR_INVALID, "host-uniform mode needs a uniform table");
   } else if (p->rng_mode != SPECDEC_RNG_MT19937 && p->rng_mode != SPECDEC_RNG_HOST_UNIFORM) {
@@ -739,6 +740,8 @@ void setup_state(specdec_handle *h, const specdec_gen_params *p, int B, int S) {
   st.out_len = S + std::max(1, p->max_new_tokens);
   st.T = p->temperature;
   st.greedy = p->temperature <= 0.f ? 1 : 0;
+  st.top_k = p->top_k;
+  st.top_p = p->top_p;
   st.rng_mode = p->rng_mode;
   st.catchup = p->draft_catchup;
   st.t_cap = h->t_cap;
@@ -865,7 +868,8 @@ int generate_impl(specdec_handle *h, const specdec_gen_params *p, const int32_t 
 
   if (h->use_graph) {
     GraphKey key{B, S, p->lookahead, st.greedy, table ? 1 : 0, p->draft_catchup, p->max_new_tokens,
-                 table ? p->uniform_rounds : 0, p->temperature, (!st.greedy && !table) ? p->seed : 0u};
+                 table ? p->uniform_rounds : 0, p->temperature, (!st.greedy && !table) ? p->seed : 0u,
+                 st.greedy ? 0 : p->top_k, st.greedy ? 1.f : p->top_p};
     auto it = h->graphs.find(key);
     if (it == h->graphs.end()) it = h->graphs.emplace(key, build_graph(h, B, S, p->seed, max_iters)).first;
     CK(cudaGraphLaunch(it->second.exec, h->stream));

@@ -491,8 +491,9 @@ __global__ void __launch_bounds__(32 * kLinWarps, 2) linear_kernel(LinearArgs a)
 // (log-sum-exp) by reading its peers' shared memory, so the split merge costs
 // no global-memory round trip.
 //
-// Staging.  Thread 0 issues TMA tensor copies (cp.async.bulk.tensor.2d, no
-// multicast, completion on an mbarrier) of kTile cache rows of K and of V;
+// Staging.  Thread 0 issues TMA tensor copies (cp.async.bulk.tensor.2d into
+// this CTA's own shared memory, completion on an mbarrier) of kTile cache
+// rows of K and of V;
 // with several tiles per chunk the two stages alternate.  Rows that are a
 // multiple of 128 bytes wide arrive with the 128-byte swizzle (16-byte unit
 // j of row r lands in unit j ^ (r & 7) of its 128-byte line), so the score

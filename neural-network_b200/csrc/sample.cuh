@@ -96,6 +96,8 @@ struct SpecState {
   int max_new, k;
   float T;
   int greedy;
+  int top_k;           // > 0 and < V: keep the k most probable tokens
+  float top_p;         // in (0, 1): keep the smallest descending prefix of mass >= top_p
   int rng_mode;        // 0 mt19937, 1 host table
   const float *uniforms;
   int u_rounds, u_slots;
@@ -242,7 +244,105 @@ __device__ void store_row(const float *srow, int V, float *__restrict__ g) {
 // sum, then divide by the sum of the normalised values (the reference's
 // second normalisation, taken there in sorted order).  Max and exp-sum come
 // from one pass with a per-thread running maximum.
-__device__ void probs_smem(float *srow, int V, float T, float *red) {
+// Scratch of the top-k / top-p cut.
+struct CutShared {
+  unsigned int cnt[256];
+  unsigned long long mass[256];  // probability mass in units of 2^-40 (exact integer sums)
+  unsigned int pfx, above_cnt, eq_cnt;
+  unsigned long long above_mass;
+  int hit;
+};
+constexpr double kMassUnit = 1099511627776.0;  // 2^40
+
+__device__ __forceinline__ unsigned long long mass_fixed(float p) {
+  return static_cast<unsigned long long>(__double2ull_rn(static_cast<double>(p) * kMassUnit));
+}
+
+// Position of the cut in the descending order of the probabilities in srow
+// (all >= 0, so their bit patterns order like their values), found by a
+// radix descent over the float bits, 8 bits per pass: by count (the target-th
+// largest element) or by mass (the element at which the descending running
+// sum reaches the target).  On return c.pfx holds the cut value's bits,
+// c.above_cnt / c.above_mass the count / mass strictly above it, c.eq_cnt the
+// number of elements equal to it; c.hit = 0 when the target is never reached.
+__device__ void radix_cut(const float *srow, int V, bool by_mass, unsigned long long target, CutShared &c) {
+  if (threadIdx.x == 0) {
+    c.pfx = 0;
+    c.above_cnt = 0;
+    c.above_mass = 0;
+    c.hit = 1;
+  }
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+      c.cnt[i] = 0;
+      c.mass[i] = 0;
+    }
+    __syncthreads();
+    const unsigned int pfx = c.pfx;
+    const unsigned int hmask = shift == 24 ? 0u : (0xffffffffu << (shift + 8));
+    for (int v = threadIdx.x; v < V; v += blockDim.x) {
+      const unsigned int bits = __float_as_uint(srow[v]);
+      if ((bits & hmask) == pfx) {
+        const unsigned int bkt = (bits >> shift) & 255u;
+        atomicAdd(&c.cnt[bkt], 1u);
+        if (by_mass) atomicAdd(&c.mass[bkt], mass_fixed(srow[v]));
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      // lane l covers buckets 255 - 8l down to 248 - 8l
+      const int lane = threadIdx.x;
+      unsigned long long lc = 0, lm = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        lc += c.cnt[255 - 8 * lane - j];
+        lm += c.mass[255 - 8 * lane - j];
+      }
+      unsigned long long ic = lc, im = lm;  // inclusive scans in descending bucket order
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long yc = __shfl_up_sync(0xffffffffu, ic, o);
+        const unsigned long long ym = __shfl_up_sync(0xffffffffu, im, o);
+        if (lane >= o) {
+          ic += yc;
+          im += ym;
+        }
+      }
+      const unsigned long long bc = c.above_cnt, bm = c.above_mass;
+      const bool hit = (by_mass ? bm + im : bc + ic) >= target;
+      const unsigned int ballot = __ballot_sync(0xffffffffu, hit);
+      const int L = ballot ? __ffs(ballot) - 1 : 31;
+      if (lane == L) {
+        unsigned long long rc = bc + ic - lc, rm = bm + im - lm;  // above this lane's buckets
+        int chosen = 255 - 8 * lane - 7;
+        for (int j = 0; j < 8; ++j) {
+          const int bkt = 255 - 8 * lane - j;
+          if ((by_mass ? rm + c.mass[bkt] : rc + c.cnt[bkt]) >= target) {
+            chosen = bkt;
+            break;
+          }
+          rc += c.cnt[bkt];
+          rm += c.mass[bkt];
+        }
+        if (!ballot) c.hit = 0;
+        c.pfx = pfx | (static_cast<unsigned int>(chosen) << shift);
+        c.above_cnt = static_cast<unsigned int>(rc);
+        c.above_mass = rm;
+        c.eq_cnt = c.cnt[chosen];
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// get_probs (src/nn/layer.cpp:1410-1491) for T > 0 on a logits row in
+// shared memory: softmax of l / T, then -- when top-k or top-p is active --
+// keep the first min(k, m_p) entries of the descending order (m_p = the
+// shortest prefix whose running sum reaches top_p) and renormalise by their
+// sum; without a filter the second normalisation divides by the total.  Ties
+// at the cut keep the lowest token ids (std::sort leaves their order
+// unspecified).
+__device__ void probs_smem(float *srow, int V, float T, int top_k, float top_p, float *red, CutShared &cut) {
   float mx = -INFINITY, se = 0.f;
   for (int v = threadIdx.x; v < V; v += blockDim.x) {
     const float x = __fdiv_rn(srow[v], T);
@@ -256,10 +356,54 @@ __device__ void probs_smem(float *srow, int V, float T, float *red) {
   }
   const float M = block_max(mx, red);
   const float s = block_sum(mx == -INFINITY ? 0.f : se * expf(mx - M), red);
+  for (int v = threadIdx.x; v < V; v += blockDim.x) srow[v] = __fdiv_rn(expf(__fsub_rn(srow[v], M)), s);
+  __syncthreads();
+  const bool use_k = top_k > 0 && top_k < V;
+  const bool use_p = top_p > 0.f && top_p < 1.f;
+  unsigned int t_bits = 0, keep_eq = 0, eq_cnt = 0;
+  bool filter = false;
+  if (use_p) {
+    radix_cut(srow, V, true, mass_fixed(top_p), cut);
+    if (cut.hit) {
+      const unsigned long long need = mass_fixed(top_p) - min(mass_fixed(top_p), cut.above_mass);
+      const unsigned long long unit = mass_fixed(__uint_as_float(cut.pfx));
+      unsigned long long e = unit ? (need + unit - 1) / unit : 1ull;
+      e = max(1ull, min(e, static_cast<unsigned long long>(cut.eq_cnt)));
+      const unsigned int m_p = cut.above_cnt + static_cast<unsigned int>(e);
+      if (!use_k || m_p <= static_cast<unsigned int>(top_k)) {
+        filter = true;
+        t_bits = cut.pfx;
+        keep_eq = static_cast<unsigned int>(e);
+        eq_cnt = cut.eq_cnt;
+      }
+    }
+    __syncthreads();
+  }
+  if (use_k && !filter) {
+    radix_cut(srow, V, false, static_cast<unsigned long long>(top_k), cut);
+    filter = true;
+    t_bits = cut.pfx;
+    keep_eq = static_cast<unsigned int>(top_k) - cut.above_cnt;
+    eq_cnt = cut.eq_cnt;
+    __syncthreads();
+  }
+  if (filter && keep_eq < eq_cnt && threadIdx.x == 0) {
+    // drop the tied entries past the first keep_eq token ids
+    unsigned int taken = 0;
+    for (int v = 0; v < V; ++v)
+      if (__float_as_uint(srow[v]) == t_bits) {
+        if (taken < keep_eq) ++taken;
+        else srow[v] = 0.f;
+      }
+  }
+  __syncthreads();
   float fs = 0.f;
   for (int v = threadIdx.x; v < V; v += blockDim.x) {
-    const float p = __fdiv_rn(expf(__fsub_rn(srow[v], M)), s);
-    srow[v] = p;
+    float p = srow[v];
+    if (filter && __float_as_uint(p) < t_bits) {
+      p = 0.f;
+      srow[v] = 0.f;
+    }
     fs += p;
   }
   fs = block_sum(fs, red);
@@ -338,6 +482,7 @@ struct SampShared {
   int used;
   double u;
   int flag;
+  CutShared cut;
 };
 
 __device__ __forceinline__ RngCtx make_rng(SampShared &s) { return RngCtx{s.old_s, s.new_s, s.win, &s.used}; }
@@ -398,7 +543,7 @@ __global__ void __launch_bounds__(kSampThreads) first_token_kernel(SpecState st,
     tok = argmax_smem(srow, st.V, sh.redv, sh.redi);
   } else {
     rng_prepare(st, b, 2, rc);
-    probs_smem(srow, st.V, st.T, sh.red);
+    probs_smem(srow, st.V, st.T, st.top_k, st.top_p, sh.red, sh.cut);
     if (threadIdx.x == 0) sh.u = draw_sample_u(st, b, 0, 2 * st.k, rc);
     __syncthreads();
     tok = sample_smem(srow, st.V, sh.u, st.rng_mode, sh.redd, sh.redi);
@@ -435,7 +580,7 @@ __global__ void __launch_bounds__(kSampThreads) draft_sample_kernel(SpecState st
     tok = argmax_smem(srow, st.V, sh.redv, sh.redi);
   } else {
     rng_prepare(st, b, 2, rc);
-    probs_smem(srow, st.V, st.T, sh.red);
+    probs_smem(srow, st.V, st.T, st.top_k, st.top_p, sh.red, sh.cut);
     store_row(srow, st.V, st.q + (static_cast<size_t>(b) * st.kmax + j) * st.V);  // q_j, read by accept
     if (threadIdx.x == 0) sh.u = draw_sample_u(st, b, st.round[b], j, rc);
     __syncthreads();
@@ -492,7 +637,7 @@ __global__ void __launch_bounds__(kSampThreads) accept_kernel(SpecState st, cons
       acc = (c == am);
       am_rj = am;
     } else {
-      probs_smem(srow, st.V, st.T, sh.red);
+      probs_smem(srow, st.V, st.T, st.top_k, st.top_p, sh.red, sh.cut);
       if (threadIdx.x == 0) {
         const float qv = st.q[(static_cast<size_t>(b) * st.kmax + j) * st.V + c];
         const float pv = srow[c];
@@ -526,7 +671,7 @@ __global__ void __launch_bounds__(kSampThreads) accept_kernel(SpecState st, cons
       s = block_sum(s, sh.red);
       if (s <= 0.0f) {
         load_row(lg0 + static_cast<size_t>(rj) * st.V, st.V, srow);
-        probs_smem(srow, st.V, st.T, sh.red);
+        probs_smem(srow, st.V, st.T, st.top_k, st.top_p, sh.red, sh.cut);
       } else {
         for (int v = threadIdx.x; v < st.V; v += blockDim.x) srow[v] = __fdiv_rn(srow[v], s);
         __syncthreads();
@@ -540,7 +685,7 @@ __global__ void __launch_bounds__(kSampThreads) accept_kernel(SpecState st, cons
     if (st.greedy) {
       out_tok = argmax_smem(srow, st.V, sh.redv, sh.redi);
     } else {
-      probs_smem(srow, st.V, st.T, sh.red);
+      probs_smem(srow, st.V, st.T, st.top_k, st.top_p, sh.red, sh.cut);
       if (threadIdx.x == 0) sh.u = draw_sample_u(st, b, round, 2 * st.k, rc);
       __syncthreads();
       out_tok = sample_smem(srow, st.V, sh.u, st.rng_mode, sh.redd, sh.redi);

@@ -70,14 +70,14 @@ def compare_tokens(gpu: np.ndarray, ref: np.ndarray, margins: np.ndarray, prompt
 
 
 def run_both(pair: Pair, B: int, S: int, max_new: int, k: int, T: float, seed: int = 42, use_uniforms: bool = False,
-             catchup: int = 0, prompt_seed: int = 1):
+             catchup: int = 0, prompt_seed: int = 1, top_k: int = 0, top_p: float = 1.0):
     prompts = make_prompts(B, S, pair.shape.vocab, seed=prompt_seed)
     uni = None
     if use_uniforms:
         uni = sd.philox_uniforms(seed, B, max_new + 2, 2 * k + 1)
-    tok_g, st_g = pair.engine.generate_speculative(prompts, max_new, k, T, 0, 1.0, seed, uniforms=uni,
+    tok_g, st_g = pair.engine.generate_speculative(prompts, max_new, k, T, top_k, top_p, seed, uniforms=uni,
                                                    draft_catchup=catchup)
     tok_o, st_o, mg = oracle.oracle_generate_speculative(
-        pair.target, pair.draft, prompts, max_new, k, T, 0, 1.0, seed, uniforms=uni, catchup=catchup,
+        pair.target, pair.draft, prompts, max_new, k, T, top_k, top_p, seed, uniforms=uni, catchup=catchup,
         act_bf16=pair.act_bf16, kv_mode=pair.kv_mode, cache_cap=pair.shape.max_seq_len)
     return prompts, tok_g, st_g, tok_o, st_o, mg

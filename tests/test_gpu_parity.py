@@ -94,3 +94,17 @@ def test_catchup_correct(gpu_lib, oracle_built, T):
     _, tg, sg, to, so, mg = run_both(pair, 2, 8, 40, 3, T, seed=5, use_uniforms=T > 0, catchup=1)
     exact, ties = compare_tokens(tg, to, mg, 8, greedy=T <= 0)
     assert exact + ties == 2
+
+
+# get_probs top-k / top-p filtering (src/nn/layer.cpp:1451-1471) on the device
+# sampler: both uniform sources, filters alone and combined.
+@pytest.mark.parametrize("name", ["small", "cfg1"])
+@pytest.mark.parametrize("top_k,top_p", [(5, 1.0), (0, 0.8), (40, 0.9), (3, 0.5)])
+@pytest.mark.parametrize("use_uniforms", [False, True])
+def test_sampled_topk_topp(gpu_lib, oracle_built, name, top_k, top_p, use_uniforms):
+    shape, dl = SHAPES[name]
+    pair = make_pair(shape, dl, seed=12, max_batch=4, max_prompt_len=40)
+    _, tg, sg, to, so, mg = run_both(pair, 3, 10, 40, 3, 0.9, seed=77, use_uniforms=use_uniforms,
+                                     top_k=top_k, top_p=top_p)
+    exact, ties = compare_tokens(tg, to, mg, 10, greedy=False)
+    assert exact + ties == 3 and ties <= 1
