@@ -159,6 +159,8 @@ struct specdec_handle {
 
   // caches
   void *tk = nullptr, *tv = nullptr, *dk = nullptr, *dv = nullptr;
+  float *tks = nullptr, *tvs = nullptr, *dks = nullptr, *dvs = nullptr;  // int8 cache: per-row scales
+  float *KVN = nullptr;                                                  // int8 cache: staged K/V rows
   size_t t_layer_stride = 0, d_layer_stride = 0, t_req_stride = 0, d_req_stride = 0;
   int t_cap = 0, d_cap = 0;
   float2 *rope = nullptr;
@@ -423,22 +425,29 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 }
 
 // 2-D TMA view [rows][D] of one layer's K or V cache (row = slot * Hkv * S_cap
-// + kv head * S_cap + position), box = box_cols x box_rows elements, with the
-// 128-byte swizzle when a row is a multiple of 128 bytes.  Rows past the end
-// read as zeros.
-CUtensorMap kv_tensor_map(const void *base, bool bf16, int D, size_t rows, int box_cols, int box_rows) {
-  const size_t elt = bf16 ? 2 : 4;
+// + kv head * S_cap + position), box = the attention kernel's tile with its
+// swizzle (AttnGeom).  Rows past the end read as zeros.
+template <typename KT> CUtensorMapDataType tmap_type();
+template <> CUtensorMapDataType tmap_type<float>() { return CU_TENSOR_MAP_DATA_TYPE_FLOAT32; }
+template <> CUtensorMapDataType tmap_type<__nv_bfloat16>() { return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16; }
+template <> CUtensorMapDataType tmap_type<int8_t>() { return CU_TENSOR_MAP_DATA_TYPE_UINT8; }
+
+template <typename KT, int D>
+CUtensorMap kv_tensor_map(const void *base, size_t rows) {
+  using G = AttnGeom<KT, D>;
   if (rows >= (size_t(1) << 31)) fail(SPECDEC_ERR_UNSUPPORTED, "KV cache too large for 32-bit TMA row coordinates");
   CUtensorMap m;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(D * elt)};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(G::kRowBytes)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(G::kBoxCols), static_cast<cuuint32_t>(G::kTile)};
   cuuint32_t estr[2] = {1, 1};
-  const bool swz = (D * elt) % 128 == 0;
-  const CUresult r = tensor_map_encoder()(
-      &m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base), dims,
-      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
-      CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const CUtensorMapSwizzle sw = G::kSw == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : G::kSw == 64  ? CU_TENSOR_MAP_SWIZZLE_64B
+                                : G::kSw == 32  ? CU_TENSOR_MAP_SWIZZLE_32B
+                                                : CU_TENSOR_MAP_SWIZZLE_NONE;
+  const CUresult r = tensor_map_encoder()(&m, tmap_type<KT>(), 2, const_cast<void *>(base), dims, strides, box, estr,
+                                          CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) fail(SPECDEC_ERR_CUDA, "cuTensorMapEncodeTiled failed with " + std::to_string(static_cast<int>(r)));
   return m;
 }
@@ -524,9 +533,8 @@ template <typename AT, typename KT, int D>
 void launch_attention_d(specdec_handle *h, AttnArgs &a, int ngroups, const void *kc, const void *vc, size_t rows) {
   using G = AttnGeom<KT, D>;
   if (!G::kTma) fail(SPECDEC_ERR_UNSUPPORTED, "a K/V cache row (head_dim x element size) must be a multiple of 16 bytes");
-  constexpr bool kbf = std::is_same<KT, __nv_bfloat16>::value;
-  a.tmk = kv_tensor_map(kc, kbf, D, rows, G::kBoxCols, G::kTile);
-  a.tmv = kv_tensor_map(vc, kbf, D, rows, G::kBoxCols, G::kTile);
+  a.tmk = kv_tensor_map<KT, D>(kc, rows);
+  a.tmv = kv_tensor_map<KT, D>(vc, rows);
   const int qt = a.Q <= 1 ? 1 : a.Q <= 2 ? 2 : a.Q <= 4 ? 4 : kAttnQT;
   const int ngt = (a.Q + qt - 1) / qt;
   const int base = ngroups * ngt * a.H;
@@ -571,17 +579,21 @@ void launch_attention_t(specdec_handle *h, AttnArgs &a, int D, int ngroups, cons
 // one request each.  kc/vc are one layer's caches of `layer_elems` elements
 // ([slot][kv head][S_cap][D]).
 void attention(specdec_handle *h, const Dims &dm, RowsView rows, int R, int Q, const void *kc, const void *vc,
-               size_t layer_elems, int S_cap) {
+               const float *ks, const float *vs, size_t layer_elems, int S_cap) {
   if (R <= 0) return;
   AttnArgs a{};
   a.q = h->Q; a.ldq = dm.d; a.rows = rows; a.R = R; a.Q = Q;
   a.S_cap = S_cap; a.H = dm.H; a.Hkv = dm.Hkv;
+  a.k_scale = ks; a.v_scale = vs;
   a.out = h->ATT; a.ldo = dm.d; a.err = h->st.err;
   const int ngroups = (R + Q - 1) / Q;
   const size_t nrows = layer_elems / dm.D;
   const bool bf = act_bf16(h);
   const bool kvbf = h->cfg.kv_dtype == SPECDEC_BF16;
-  if (bf && kvbf) launch_attention_t<__nv_bfloat16, __nv_bfloat16>(h, a, dm.D, ngroups, kc, vc, nrows);
+  if (h->cfg.kv_dtype == SPECDEC_INT8) {
+    if (bf) launch_attention_t<__nv_bfloat16, int8_t>(h, a, dm.D, ngroups, kc, vc, nrows);
+    else launch_attention_t<float, int8_t>(h, a, dm.D, ngroups, kc, vc, nrows);
+  } else if (bf && kvbf) launch_attention_t<__nv_bfloat16, __nv_bfloat16>(h, a, dm.D, ngroups, kc, vc, nrows);
   else if (bf) launch_attention_t<__nv_bfloat16, float>(h, a, dm.D, ngroups, kc, vc, nrows);
   else if (kvbf) launch_attention_t<float, __nv_bfloat16>(h, a, dm.D, ngroups, kc, vc, nrows);
   else launch_attention_t<float, float>(h, a, dm.D, ngroups, kc, vc, nrows);
@@ -626,7 +638,10 @@ void forward_rows(specdec_handle *h, bool target, int off, int R, int Q, const i
   const size_t lstride = target ? h->t_layer_stride : h->d_layer_stride;
   const size_t rstride = target ? h->t_req_stride : h->d_req_stride;
   const int S_cap = target ? h->t_cap : h->d_cap;
-  const size_t kv_elt = h->cfg.kv_dtype == SPECDEC_BF16 ? 2 : 4;
+  const bool kv8 = h->cfg.kv_dtype == SPECDEC_INT8;
+  const size_t kv_elt = kv8 ? 1 : h->cfg.kv_dtype == SPECDEC_BF16 ? 2 : 4;
+  float *ksc = target ? h->tks : h->dks, *vsc = target ? h->tvs : h->dvs;
+  const size_t lrows = lstride / dm.D;  // cache rows (and int8 scales) per layer
   const bool ref = dm.arch == SPECDEC_ARCH_REF;
 
   if (act_bf16(h))
@@ -650,9 +665,13 @@ void forward_rows(specdec_handle *h, bool target, int off, int R, int Q, const i
       a.x = h->X; a.in_g = L.g1; a.in_b = L.b1;
     }
     a.qkv = QKVArgs{d, dm.kvd, dm.D, h->rope, h->rope_max, kcl, vcl, rstride, S_cap,
-                    h->cfg.kv_dtype == SPECDEC_BF16 ? 1 : 0, h->st.err};
+                    kv8 ? 2 : h->cfg.kv_dtype == SPECDEC_BF16 ? 1 : 0, h->KVN, h->st.err};
     launch_linear<kEpiQKV>(h, a);
-    attention(h, dm, rows, R, Q, kcl, vcl, lstride, S_cap);
+    float *ksl = kv8 ? ksc + l * lrows : nullptr, *vsl = kv8 ? vsc + l * lrows : nullptr;
+    if (kv8)
+      launch(h, kv_quant_kernel, dim3(R), dim3(256), 0, rows, R, static_cast<const float *>(h->KVN), dm.kvd, dm.D,
+             dm.Hkv, S_cap, static_cast<int8_t *>(kcl), static_cast<int8_t *>(vcl), ksl, vsl);
+    attention(h, dm, rows, R, Q, kcl, vcl, ksl, vsl, lstride, S_cap);
     LinearArgs o{};
     o.x = h->ATT; o.ldx = d; o.R = R; o.W = L.wo; o.scale = L.so; o.bias = L.bo; o.N = d; o.K = d;
     o.out = h->H; o.ldo = d; o.resid = h->X; o.ldr = d; o.rows = rows;
@@ -931,8 +950,8 @@ int specdec_create(const specdec_config *cfg, int device, specdec_handle **out) 
     if (cfg->weight_dtype != SPECDEC_F32 && cfg->weight_dtype != SPECDEC_INT8)
       fail(SPECDEC_ERR_INVALID, "weight_dtype must be F32 or INT8");
     if (cfg->act_dtype != SPECDEC_F32 && cfg->act_dtype != SPECDEC_BF16) fail(SPECDEC_ERR_INVALID, "bad act_dtype");
-    if (cfg->kv_dtype == SPECDEC_INT8) fail(SPECDEC_ERR_UNSUPPORTED, "int8 KV cache is not implemented on the device path");
-    if (cfg->kv_dtype != SPECDEC_F32 && cfg->kv_dtype != SPECDEC_BF16) fail(SPECDEC_ERR_INVALID, "bad kv_dtype");
+    if (cfg->kv_dtype != SPECDEC_F32 && cfg->kv_dtype != SPECDEC_BF16 && cfg->kv_dtype != SPECDEC_INT8)
+      fail(SPECDEC_ERR_INVALID, "bad kv_dtype");
     if (cfg->max_batch < 1 || cfg->max_lookahead < 1 || cfg->max_lookahead > 32 || cfg->max_prompt_len < 1)
       fail(SPECDEC_ERR_INVALID, "max_batch / max_lookahead / max_prompt_len out of range");
     if (td.V > 51200) fail(SPECDEC_ERR_UNSUPPORTED, "vocabularies above 51200 entries are not supported");
@@ -944,6 +963,8 @@ int specdec_create(const specdec_config *cfg, int device, specdec_handle **out) 
     set_attn_attrs<float, __nv_bfloat16>();
     set_attn_attrs<__nv_bfloat16, float>();
     set_attn_attrs<__nv_bfloat16, __nv_bfloat16>();
+    set_attn_attrs<float, int8_t>();
+    set_attn_attrs<__nv_bfloat16, int8_t>();
     set_linear_attrs();
     {
       const int vs = td.V * static_cast<int>(sizeof(float));
@@ -953,7 +974,8 @@ int specdec_create(const specdec_config *cfg, int device, specdec_handle **out) 
     }
 
     const int B = cfg->max_batch, k = cfg->max_lookahead;
-    const size_t kv_elt = cfg->kv_dtype == SPECDEC_BF16 ? 2 : 4;
+    const bool kv8 = cfg->kv_dtype == SPECDEC_INT8;
+    const size_t kv_elt = kv8 ? 1 : cfg->kv_dtype == SPECDEC_BF16 ? 2 : 4;
     // KV caches: [layer][B][Hkv][cap][D]
     h->t_cap = td.max_seq;
     h->d_cap = dd.max_seq;
@@ -965,6 +987,13 @@ int specdec_create(const specdec_config *cfg, int device, specdec_handle **out) 
     h->tv = h->dalloc(h->t_layer_stride * td.L * kv_elt);
     h->dk = h->dalloc(h->d_layer_stride * dd.L * kv_elt);
     h->dv = h->dalloc(h->d_layer_stride * dd.L * kv_elt);
+    if (kv8) {
+      auto fb = [&](size_t n) { return static_cast<float *>(h->dalloc(n * sizeof(float))); };
+      h->tks = fb(h->t_layer_stride / td.D * td.L);
+      h->tvs = fb(h->t_layer_stride / td.D * td.L);
+      h->dks = fb(h->d_layer_stride / dd.D * dd.L);
+      h->dvs = fb(h->d_layer_stride / dd.D * dd.L);
+    }
     // RoPE table, computed with the reference's float formula
     // (src/core/tensor.cpp:1147-1152): theta = pow(10000, -2j/D), omega = m*theta.
     h->rope_max = std::max(td.max_seq, dd.max_seq);
@@ -993,6 +1022,9 @@ int specdec_create(const specdec_config *cfg, int device, specdec_handle **out) 
     h->Q = h->dalloc(rowb);
     h->ATT = h->dalloc(rowb);
     h->A = h->dalloc(static_cast<size_t>(h->R_max) * Fmax * h->act_elt);
+    if (kv8)
+      h->KVN = static_cast<float *>(
+          h->dalloc(static_cast<size_t>(h->R_max) * 2 * std::max(td.kvd, dd.kvd) * sizeof(float)));
     h->logits = static_cast<float *>(h->dalloc(static_cast<size_t>(R_round) * td.V * sizeof(float)));
     const size_t pool_rows =
         static_cast<size_t>(h->R_max) + 2 * B + static_cast<size_t>(k - 1) * B + static_cast<size_t>(B) * (k + 1);
@@ -1273,18 +1305,21 @@ extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const
   // duration of the call and restored on every exit path.
   struct Saved {
     void *X, *H, *X1, *A, *Q, *ATT, *tk, *tv, *dk, *dv;
+    float *tks, *tvs, *dks, *dvs, *KVN;
     int *err;
     RowPool pool;
     size_t tls, dls, trs, drs;
     int tcap, dcap, R_max;
     cudaStream_t stream;
   };
-  Saved sv{h->X, h->H, h->X1, h->A, h->Q, h->ATT, h->tk, h->tv, h->dk, h->dv, h->st.err, h->pool,
+  Saved sv{h->X, h->H, h->X1, h->A, h->Q, h->ATT, h->tk, h->tv, h->dk, h->dv, h->tks, h->tvs, h->dks, h->dvs, h->KVN,
+           h->st.err, h->pool,
            h->t_layer_stride, h->d_layer_stride, h->t_req_stride, h->d_req_stride, h->t_cap, h->d_cap, h->R_max,
            h->stream};
   auto restore = [&] {
     h->X = sv.X; h->H = sv.H; h->X1 = sv.X1; h->A = sv.A; h->Q = sv.Q; h->ATT = sv.ATT;
     h->tk = sv.tk; h->tv = sv.tv; h->dk = sv.dk; h->dv = sv.dv;
+    h->tks = sv.tks; h->tvs = sv.tvs; h->dks = sv.dks; h->dvs = sv.dvs; h->KVN = sv.KVN;
     h->st.err = sv.err; h->pool = sv.pool;
     h->t_layer_stride = sv.tls; h->d_layer_stride = sv.dls; h->t_req_stride = sv.trs; h->d_req_stride = sv.drs;
     h->t_cap = sv.tcap; h->d_cap = sv.dcap; h->R_max = sv.R_max; h->stream = sv.stream;
@@ -1299,7 +1334,8 @@ extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const
     const Dims &dm = m.dm;
     if (S < 1 || S > h->rope_max) fail(SPECDEC_ERR_INVALID, "sequence length out of range");
     const size_t act = h->act_elt;
-    const size_t kv_elt = h->cfg.kv_dtype == SPECDEC_BF16 ? 2 : 4;
+    const bool kv8 = h->cfg.kv_dtype == SPECDEC_INT8;
+    const size_t kv_elt = kv8 ? 1 : h->cfg.kv_dtype == SPECDEC_BF16 ? 2 : 4;
     auto layout = [&](ArenaCarver &c, void **ptrs) {
       const size_t rows_d = static_cast<size_t>(S) * dm.d * act;
       ptrs[0] = c.take(rows_d);                                // X
@@ -1315,8 +1351,12 @@ extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const
       ptrs[9] = c.take(S * sizeof(int));                       // row positions
       ptrs[10] = c.take(S * sizeof(int));                      // row requests
       ptrs[11] = c.take(sizeof(int));                          // error word
+      const size_t nsc = kv8 ? static_cast<size_t>(std::max(1, dm.L)) * dm.Hkv * S : 0;
+      ptrs[12] = c.take(nsc * sizeof(float));                  // int8 cache: K scales
+      ptrs[13] = c.take(nsc * sizeof(float));                  // int8 cache: V scales
+      ptrs[14] = c.take(kv8 ? static_cast<size_t>(S) * 2 * dm.kvd * sizeof(float) : 0);  // int8 cache: staged rows
     };
-    void *ptrs[12];
+    void *ptrs[15];
     ArenaCarver sizing{nullptr};
     layout(sizing, ptrs);
     if (sizing.used > SPECDEC_NOALLOC_SCRATCH_BYTES)
@@ -1330,6 +1370,9 @@ extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : h->stream;
     h->X = ptrs[0]; h->H = ptrs[1]; h->X1 = ptrs[2]; h->A = ptrs[3]; h->Q = ptrs[4]; h->ATT = ptrs[5];
     if (target) { h->tk = ptrs[6]; h->tv = ptrs[7]; } else { h->dk = ptrs[6]; h->dv = ptrs[7]; }
+    if (target) { h->tks = static_cast<float *>(ptrs[12]); h->tvs = static_cast<float *>(ptrs[13]); }
+    else { h->dks = static_cast<float *>(ptrs[12]); h->dvs = static_cast<float *>(ptrs[13]); }
+    h->KVN = static_cast<float *>(ptrs[14]);
     h->pool.tok = static_cast<int *>(ptrs[8]);
     h->pool.pos = static_cast<int *>(ptrs[9]);
     h->pool.req = static_cast<int *>(ptrs[10]);

@@ -86,7 +86,8 @@ struct QKVArgs {
   void *kc, *vc;             // this layer's caches
   size_t kv_req_stride;      // elements per request slot
   int S_cap;                 // positions per (request, head)
-  int kv_bf16;               // cache element type: 0 fp32, 1 bf16
+  int kv_mode;               // cache element type: 0 fp32, 1 bf16, 2 int8 (rows staged for kv_quant_kernel)
+  float *stage;              // kv_mode 2: [R][2 * kvd] fp32 K and V of this pass's rows
   int *err;
 };
 
@@ -292,7 +293,11 @@ __device__ __forceinline__ void linear_epilogue(const LinearArgs &a, int r, int 
       const int nn = is_k ? n - q.d : n - q.d - q.kvd;
       const int h = nn / q.D, e = nn % q.D;
       const size_t off = static_cast<size_t>(p.req) * q.kv_req_stride + (static_cast<size_t>(h) * q.S_cap + pos) * q.D + e;
-      if (q.kv_bf16) {
+      if (q.kv_mode == 2) {
+        float *st = q.stage + static_cast<size_t>(r) * 2 * q.kvd + (is_k ? 0 : q.kvd) + nn;
+        st[0] = v0;
+        st[1] = v1;
+      } else if (q.kv_mode == 1) {
         __nv_bfloat16 *c = static_cast<__nv_bfloat16 *>(is_k ? q.kc : q.vc);
         c[off] = __float2bfloat16_rn(v0);
         c[off + 1] = __float2bfloat16_rn(v1);
@@ -477,6 +482,38 @@ __global__ void __launch_bounds__(32 * kLinWarps, 2) linear_kernel(LinearArgs a)
 }
 
 // ---------------------------------------------------------------------------
+// int8 KV append: quantize_kv (src/nn/layer.cpp:635-665) of the K and V rows a
+// QKV pass staged, per (row, kv head): s = absmax / 127 (0 -> 1), q =
+// round(x * (1 / s)) clamped to +-127.  One warp per (row, head, K|V).
+__global__ void kv_quant_kernel(RowsView rows, int R, const float *__restrict__ stage, int kvd, int D, int Hkv,
+                                int S_cap, int8_t *__restrict__ kc, int8_t *__restrict__ vc, float *__restrict__ ks,
+                                float *__restrict__ vs) {
+  const int r = blockIdx.x;
+  if (r >= R) return;
+  const int req = rows.req[r], pos = rows.pos[r];
+  if (req < 0 || pos < 0 || pos >= S_cap) return;  // the QKV pass flagged an out-of-range position
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int t = warp; t < 2 * Hkv; t += nw) {
+    const bool is_v = t >= Hkv;
+    const int h = is_v ? t - Hkv : t;
+    const float *src = stage + static_cast<size_t>(r) * 2 * kvd + (is_v ? kvd : 0) + h * D;
+    float mx = 0.f;
+    for (int e = lane; e < D; e += 32) mx = fmaxf(mx, fabsf(src[e]));
+    mx = warp_max(mx);
+    float sc = __fdiv_rn(mx, 127.0f);
+    if (sc == 0.0f) sc = 1.0f;
+    const float inv = __fdiv_rn(1.0f, sc);
+    const size_t row = (static_cast<size_t>(req) * Hkv + h) * S_cap + pos;
+    int8_t *dst = (is_v ? vc : kc) + row * D;
+    for (int e = lane; e < D; e += 32) {
+      const float qv = fminf(127.0f, fmaxf(-127.0f, roundf(__fmul_rn(src[e], inv))));
+      dst[e] = static_cast<int8_t>(qv);
+    }
+    if (lane == 0) (is_v ? vs : ks)[row] = sc;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Causal attention (src/nn/layer.cpp:859-948): score = (q . k) / sqrt(D)
 // (layer.cpp:870, 891-897), softmax over positions j <= pos, then P.V.
 //
@@ -510,19 +547,30 @@ template <typename KT, int D>
 struct AttnGeom {
   static constexpr int kRowBytes = D * static_cast<int>(sizeof(KT));
   static constexpr bool kTma = kRowBytes % 16 == 0;  // else the host rejects the shape
-  static constexpr bool kSwz = kRowBytes % 128 == 0;
+  // TMA swizzle span: the widest of 128, 64 or 32 bytes that divides a row
+  // (0: rows of 16 bytes, which are conflict-free as they are)
+  static constexpr int kSw = kRowBytes % 128 == 0 ? 128 : kRowBytes % 64 == 0 ? 64 : kRowBytes % 32 == 0 ? 32 : 0;
   static constexpr int kTile = kRowBytes > 256 ? 64 : 128;  // rows per stage
   static constexpr int kE = 16 / static_cast<int>(sizeof(KT));  // elements per 16-byte unit
   static constexpr int kNC = kRowBytes / 16;                      // 16-byte units per row
   static constexpr int kStageBytes = 2 * kTile * kRowBytes;       // K tile + V tile
   static constexpr int kEPL = D >= 32 ? D / 32 : 1;               // P.V: head dims per lane
   static constexpr int kLanesPV = D / kEPL;
-  static constexpr int kBoxCols = kSwz ? 128 / static_cast<int>(sizeof(KT)) : D;  // TMA box width
+  static constexpr int kBoxBytes = kSw ? kSw : kRowBytes;         // TMA box width
+  static constexpr int kBoxCols = kBoxBytes / static_cast<int>(sizeof(KT));
   static constexpr int smem_bytes(int stages) { return stages * kStageBytes + 1024; }
-  // byte offset of 16-byte unit c of tile row r within a K or V tile
+  // Byte offset of 16-byte unit c of tile row r within a K or V tile.  A box
+  // of kSw-byte rows lands with its 16-byte unit j of row r at unit
+  // j ^ ((r * kSw / 128) & (kSw / 16 - 1)) (the TMA swizzle XORs address bits
+  // [4, 4 + log2(kSw / 16)) with bits [7, ...)), so 8 consecutive rows read
+  // at one logical unit hit 8 different bank groups.
   __device__ static __forceinline__ int unit(int r, int c) {
-    if constexpr (kSwz) return (c >> 3) * (kTile * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4);
-    else return r * kRowBytes + c * 16;
+    if constexpr (kSw != 0) {
+      constexpr int per = kSw / 16;
+      return (c / per) * (kTile * kSw) + r * kSw + (((c % per) ^ ((r * kSw / 128) & (per - 1))) << 4);
+    } else {
+      return r * kRowBytes + c * 16;
+    }
   }
 };
 
@@ -534,6 +582,7 @@ struct alignas(64) AttnArgs {
   int R, Q;      // rows, queries per group
   int S_cap, H, Hkv;
   int chunk, nsplit;
+  const float *k_scale, *v_scale;  // int8 cache: per-row dequantisation scales (same row index as the maps)
   void *out;
   int ldo;
   int *err;
@@ -580,6 +629,12 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
 }
 
 // 16 bytes of cache elements -> fp32
+__device__ __forceinline__ void unpack16(uint4 u, float *f, int8_t) {
+  i8x4_to_f32(u.x, f);
+  i8x4_to_f32(u.y, f + 4);
+  i8x4_to_f32(u.z, f + 8);
+  i8x4_to_f32(u.w, f + 12);
+}
 __device__ __forceinline__ void unpack16(uint4 u, float *f, float) {
   f[0] = __uint_as_float(u.x); f[1] = __uint_as_float(u.y);
   f[2] = __uint_as_float(u.z); f[3] = __uint_as_float(u.w);
@@ -597,7 +652,17 @@ __device__ __forceinline__ void unpack16(uint4 u, float *f, __nv_bfloat16) {
 template <typename KT, int N>
 __device__ __forceinline__ void lds_elems(const unsigned char *p, float *f) {
   constexpr int bytes = N * static_cast<int>(sizeof(KT));
-  if constexpr (std::is_same<KT, float>::value) {
+  if constexpr (std::is_same<KT, int8_t>::value) {
+    if constexpr (bytes == 4) {
+      i8x4_to_f32(*reinterpret_cast<const uint32_t *>(p), f);
+    } else if constexpr (bytes == 2) {
+      const int16_t v = *reinterpret_cast<const int16_t *>(p);
+      f[0] = static_cast<float>(static_cast<int8_t>(v & 0xff));
+      f[1] = static_cast<float>(static_cast<int8_t>(v >> 8));
+    } else {
+      f[0] = static_cast<float>(*reinterpret_cast<const int8_t *>(p));
+    }
+  } else if constexpr (std::is_same<KT, float>::value) {
     if constexpr (bytes == 16) {
       const float4 v = *reinterpret_cast<const float4 *>(p);
       f[0] = v.x; f[1] = v.y; f[2] = v.z; f[3] = v.w;
@@ -630,6 +695,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
   constexpr int kTile = G::kTile;
   constexpr int EPL = G::kEPL;
   constexpr int NACC = QT == 1 ? 4 : (QT == 2 ? 2 : 1);  // independent partial dots per query
+  constexpr bool kI8 = std::is_same<KT, int8_t>::value;
   constexpr bool kSqrtPow2 = D == 4 || D == 16 || D == 64;
   constexpr float kInvSqrt = D == 4 ? 0.5f : D == 16 ? 0.25f : 0.125f;
   extern __shared__ unsigned char attn_smem_raw[];
@@ -671,8 +737,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
                  : "memory");
 #pragma unroll
     for (int cb = 0; cb < D / G::kBoxCols; ++cb) {
-      tma_load_2d(kdst + cb * kTile * 128, &a.tmk, cb * G::kBoxCols, y, &bars[s]);
-      tma_load_2d(vdst + cb * kTile * 128, &a.tmv, cb * G::kBoxCols, y, &bars[s]);
+      tma_load_2d(kdst + cb * kTile * G::kBoxBytes, &a.tmk, cb * G::kBoxCols, y, &bars[s]);
+      tma_load_2d(vdst + cb * kTile * G::kBoxBytes, &a.tmv, cb * G::kBoxCols, y, &bars[s]);
     }
   };
   if (threadIdx.x == 0) {
@@ -748,6 +814,13 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
     // scores: thread = tile row
     const int r = threadIdx.x;
     const int pos = t0 + r;
+    float ksc = 1.f, vsc = 1.f;
+    if constexpr (kI8) {
+      if (r < nt) {
+        ksc = __ldg(a.k_scale + row0 + pos);
+        vsc = __ldg(a.v_scale + row0 + pos);
+      }
+    }
     float sc[QT];
     {
       float dot[QT][NACC];
@@ -780,6 +853,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
         float dd = dot[i][0];
 #pragma unroll
         for (int u = 1; u < NACC; ++u) dd += dot[i][u];
+        if constexpr (kI8) dd *= ksc;  // q . (k_q * s) = s * (q . k_q)
         // sqrt(D) is a power of two for D = 4, 16, 64: the product by its
         // reciprocal is then the correctly rounded quotient
         const float sv = kSqrtPow2 ? dd * kInvSqrt : __fdiv_rn(dd, scale);
@@ -803,7 +877,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
       l[i] = l[i] * alpha + p;  // per-lane partial sum, reduced after the loop
 #pragma unroll
       for (int e = 0; e < EPL; ++e) acc[i][e] *= alpha;
-      s_p[warp][i][lane] = p;
+      s_p[warp][i][lane] = kI8 ? p * vsc : p;  // p * (v_q * s) = (p * s) * v_q
     }
     __syncwarp();
     // P.V over the warp's 32 rows; rows past the tile's end re-read its last

@@ -108,3 +108,48 @@ def test_sampled_topk_topp(gpu_lib, oracle_built, name, top_k, top_p, use_unifor
                                      top_k=top_k, top_p=top_p)
     exact, ties = compare_tokens(tg, to, mg, 10, greedy=False)
     assert exact + ties == 3 and ties <= 1
+
+
+# Head dims whose cache rows take the other TMA swizzle spans: D=16 (int8 rows
+# of 16 bytes: no swizzle; fp32 64 bytes: 64B), D=32 (int8 32 bytes: 32B;
+# bf16 64 bytes: 64B; fp32 128 bytes: 128B).
+SWZ_SHAPES = {
+    "d16": (ModelShape(vocab=300, d_model=64, n_heads=4, d_ff=128, n_layers=2, max_seq_len=96), 1),
+    "d32": (ModelShape(vocab=300, d_model=128, n_heads=4, d_ff=256, n_layers=2, max_seq_len=96), 1),
+}
+SHAPES_KV = {**SWZ_SHAPES, "cfg1": SHAPES["cfg1"]}
+
+
+@pytest.mark.parametrize("name", list(SWZ_SHAPES))
+@pytest.mark.parametrize("kv_mode", [0, 1])
+def test_forward_logits_swizzle_spans(gpu_lib, oracle_built, name, kv_mode):
+    shape, dl = SWZ_SHAPES[name]
+    pair = make_pair(shape, dl, seed=16, kv_mode=kv_mode, max_prompt_len=64)
+    toks = make_prompts(1, 57, shape.vocab, seed=17)[0]
+    g = pair.engine.forward_logits(sd.TARGET, toks)
+    o = pair.target.forward(toks, kv_mode=kv_mode)
+    assert rel_err(g, o) < (FP32_REL if kv_mode == 0 else BF16_REL)
+
+
+# int8 KV cache (quantize_kv, src/nn/layer.cpp:635-665): per (position, kv
+# head) absmax scales, dequantised inside attention.  Rows must be at least
+# 16 bytes (head_dim >= 16).
+@pytest.mark.parametrize("name", list(SHAPES_KV))
+def test_forward_logits_int8_kv(gpu_lib, oracle_built, name):
+    shape, dl = SHAPES_KV[name]
+    pair = make_pair(shape, dl, seed=13, kv_mode=2, max_prompt_len=40)
+    toks = make_prompts(1, 33, shape.vocab, seed=14)[0]
+    for role, om in ((sd.TARGET, pair.target), (sd.DRAFT, pair.draft)):
+        g = pair.engine.forward_logits(role, toks)
+        o = om.forward(toks, kv_mode=2)
+        assert rel_err(g, o) < FP32_REL, (name, role, rel_err(g, o))
+
+
+@pytest.mark.parametrize("name", list(SHAPES_KV))
+@pytest.mark.parametrize("T", [0.0, 1.0])
+def test_spec_int8_kv(gpu_lib, oracle_built, name, T):
+    shape, dl = SHAPES_KV[name]
+    pair = make_pair(shape, dl, seed=15, int8=True, kv_mode=2, max_batch=4, max_prompt_len=40)
+    _, tg, sg, to, so, mg = run_both(pair, 3, 12, 40, 4, T, seed=31, use_uniforms=T > 0)
+    exact, ties = compare_tokens(tg, to, mg, 12, greedy=T <= 0)
+    assert exact + ties == 3 and ties <= 1
