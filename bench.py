@@ -347,8 +347,17 @@ def main():
     avg_ctx = S + wl.max_new / 2
     ab = algorithmic_bytes_per_round(wl, wl.weights_int8, avg_ctx)
     round_ms = ms_per_step / max(1, rounds)
-    achieved = ab["total"] / (round_ms * 1e-3) / 1e9
+    round_achieved = ab["total"] / (round_ms * 1e-3) / 1e9
     clocks = clk.summary()
+
+    # Dominant kernels, timed alone on the library's stream with CUDA events
+    # (L2 flushed before every launch) over the verify pass's row count.
+    R_verify = B * (wl.lookahead + 1)
+    probes = {}
+    for name, which, layer in (("ffn_out", sd.LIN_FFN_OUT, 0), ("ffn_in", sd.LIN_FFN_IN, 0),
+                               ("qkv", sd.LIN_QKV, 1), ("head", sd.LIN_HEAD, wl.target.n_layers - 1)):
+        us, nbytes = eng.time_linear(sd.TARGET, layer, which, R_verify, 20, flush.data_ptr(), flush.numel() * 4)
+        probes[name] = {"us": us, "bytes": nbytes, "GBps": nbytes / (us * 1e-6) / 1e9}
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
@@ -358,10 +367,14 @@ def main():
                         "h2d_bytes_per_step": int(prompts.size * 4 + uni.nbytes),
                         "d2h_bytes_per_step": int(B * out_len * 4 + B * 4 * 8 + 4)},
                 "gpu_launches": int(launches),
-                "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                             "frac": achieved / hbm, "traffic": None,
-                             "kernel": "whole speculative round (k draft steps + verify + accept)",
-                             "peak_source": peak_kind},
+                "roofline": {"bound": "hbm", "achieved": probes["ffn_out"]["GBps"], "peak": hbm, "unit": "GB/s",
+                             "frac": probes["ffn_out"]["GBps"] / hbm, "traffic": None,
+                             "kernel": f"linear_kernel<int8,f32,Resid> (target FFN down-projection, {R_verify} verify rows)",
+                             "launch_us": probes["ffn_out"]["us"], "alg_bytes_per_launch": probes["ffn_out"]["bytes"],
+                             "peak_source": peak_kind,
+                             "other_kernels": {k: v for k, v in probes.items() if k != "ffn_out"},
+                             "round": {"alg_bytes": ab["total"], "achieved": round_achieved,
+                                       "frac": round_achieved / hbm}},
                 "spec": {"rounds_per_step": int(rounds), "mean_accepted_per_round": float(accepted) / max(1, stats[:, 0].sum()),
                          "acceptance_rate": float(accepted) / max(1, drafted), "round_us": round_ms * 1e3},
                 "clocks": clocks}

@@ -153,7 +153,7 @@ int specdec_philox_uniforms(uint64_t seed, int B, int rounds, int slots,
  * d_tokens [S] int32 and d_logits [S][vocab] fp32 are DEVICE buffers the caller
  * owns; the call is asynchronous on `stream` (a cudaStream_t; NULL selects
  * specdec_stream(h)).  Every byte of working memory (activations, row tables,
- * the sequence's KV cache, attention partials) comes from one fixed 8 MiB
+ * the sequence's KV cache and its int8 scales) comes from one fixed 8 MiB
  * device array inside the library; work that needs more is rejected with
  * SPECDEC_ERR_INVALID.  No cudaMalloc, cudaFree or other allocating call is
  * made.  The array is shared by all calls on a device and keeps the last
@@ -166,6 +166,26 @@ int specdec_forward_logits_noalloc(specdec_handle *h, int role,
 
 /* Number of kernel launches the last generate call issued on the device. */
 int64_t specdec_last_launch_count(const specdec_handle *h);
+
+/* Which linear layer specdec_time_linear launches. */
+enum specdec_linear {
+  SPECDEC_LIN_QKV = 0,     /* fused q/k/v projection (+ RoPE, cache append) */
+  SPECDEC_LIN_OPROJ = 1,   /* attention output projection + residual */
+  SPECDEC_LIN_FFN_IN = 2,  /* SwiGLU gate/up (arch ref) or fc1 + GELU (arch cfg), with its LayerNorm */
+  SPECDEC_LIN_FFN_OUT = 3, /* down / fc2 + residual */
+  SPECDEC_LIN_HEAD = 4     /* lm_head over normalised rows */
+};
+
+/* Measurement probe (no counterpart in the reference): launches the kernel of
+ * one linear layer of `role` exactly as a forward pass over `rows` rows builds
+ * it, `reps` times on specdec_stream(h), each launch alone between CUDA
+ * events with the L2 cache flushed before it by writing `flush_bytes` of the
+ * caller's device buffer `flush`.  Writes the mean launch time in
+ * microseconds and the launch's algorithmic bytes (weights, scales, biases,
+ * LayerNorm parameters, input and output rows).  Overwrites activation
+ * buffers; a QKV launch writes no cache rows (its rows are marked unused). */
+int specdec_time_linear(specdec_handle *h, int role, int layer, int which, int rows, int reps,
+                        void *flush, size_t flush_bytes, float *avg_us, double *alg_bytes);
 
 #ifdef __cplusplus
 }

@@ -452,15 +452,23 @@ CUtensorMap kv_tensor_map(const void *base, size_t rows) {
   return m;
 }
 
-// K-split: enough warps per column pair that each lane streams one or two
-// weight vectors, while the grid stays within about two waves.
-int pick_ksplit(int N, int R, int K, int E) {
+// Columns per warp: one pair while the grid of one-pair warps fits a wave
+// (two blocks per SM), else two pairs (each input vector then feeds four
+// weight columns and the grid halves).  K-split: the smallest power of two (at
+// most 8) that gives about one block per SM or leaves each lane at most one
+// weight vector per column.
+int pick_ncols(int N, int R, int K, int E, int num_sms) {
+  const int row_tiles = (R + kRowTile - 1) / kRowTile;
+  const long blocks2 = static_cast<long>((N + 2 * kLinWarps - 1) / (2 * kLinWarps)) * row_tiles;
+  return blocks2 > 2L * num_sms ? 4 : 2;
+}
+int pick_ksplit(int N, int R, int K, int E, int nc, int num_sms) {
   const int row_tiles = (R + kRowTile - 1) / kRowTile;
   int ks = 1;
   while (ks < 8) {
-    const int pairs = kLinWarps / (2 * ks);
-    const long blocks = static_cast<long>((N + 2 * pairs - 1) / (2 * pairs)) * row_tiles;
-    if (K / E <= 64 * ks || blocks > 2 * 148) break;
+    const int cols = nc * (kLinWarps / ks);
+    const long blocks = static_cast<long>((N + cols - 1) / cols) * row_tiles;
+    if (blocks >= num_sms || K / E <= 32 * ks) break;
     ks *= 2;
   }
   return ks;
@@ -468,38 +476,51 @@ int pick_ksplit(int N, int R, int K, int E) {
 
 constexpr size_t kLinLnSmemMax = 128 * 1024;
 
-template <int EPI>
-void launch_linear(specdec_handle *h, LinearArgs a) {
-  if (a.R <= 0) return;
+template <int EPI, int NC>
+void launch_linear_nc(specdec_handle *h, const LinearArgs &a, dim3 grid, dim3 block) {
   const bool bf = act_bf16(h), i8 = w_int8(h);
-  a.ksplit = pick_ksplit(a.N, a.R, a.K, i8 ? WVec<int8_t>::E : WVec<float>::E);
-  const int pairs = kLinWarps / a.ksplit;
-  dim3 grid((a.N + 2 * pairs - 1) / (2 * pairs), (a.R + kRowTile - 1) / kRowTile);
-  dim3 block(32 * kLinWarps);
   if (a.in_g) {
     const size_t smem = static_cast<size_t>(kRowTile) * a.K * h->act_elt;
     if (smem > kLinLnSmemMax) fail(SPECDEC_ERR_UNSUPPORTED, "input rows too wide for the fused LayerNorm");
-    if (i8 && bf) launch(h, linear_kernel<int8_t, __nv_bfloat16, EPI, true>, grid, block, smem, a);
-    else if (i8) launch(h, linear_kernel<int8_t, float, EPI, true>, grid, block, smem, a);
-    else if (bf) launch(h, linear_kernel<float, __nv_bfloat16, EPI, true>, grid, block, smem, a);
-    else launch(h, linear_kernel<float, float, EPI, true>, grid, block, smem, a);
+    if (i8 && bf) launch(h, linear_kernel<int8_t, __nv_bfloat16, EPI, true, NC>, grid, block, smem, a);
+    else if (i8) launch(h, linear_kernel<int8_t, float, EPI, true, NC>, grid, block, smem, a);
+    else if (bf) launch(h, linear_kernel<float, __nv_bfloat16, EPI, true, NC>, grid, block, smem, a);
+    else launch(h, linear_kernel<float, float, EPI, true, NC>, grid, block, smem, a);
   } else {
-    if (i8 && bf) launch(h, linear_kernel<int8_t, __nv_bfloat16, EPI, false>, grid, block, 0, a);
-    else if (i8) launch(h, linear_kernel<int8_t, float, EPI, false>, grid, block, 0, a);
-    else if (bf) launch(h, linear_kernel<float, __nv_bfloat16, EPI, false>, grid, block, 0, a);
-    else launch(h, linear_kernel<float, float, EPI, false>, grid, block, 0, a);
+    if (i8 && bf) launch(h, linear_kernel<int8_t, __nv_bfloat16, EPI, false, NC>, grid, block, 0, a);
+    else if (i8) launch(h, linear_kernel<int8_t, float, EPI, false, NC>, grid, block, 0, a);
+    else if (bf) launch(h, linear_kernel<float, __nv_bfloat16, EPI, false, NC>, grid, block, 0, a);
+    else launch(h, linear_kernel<float, float, EPI, false, NC>, grid, block, 0, a);
   }
+}
+
+template <int EPI>
+void launch_linear(specdec_handle *h, LinearArgs a) {
+  if (a.R <= 0) return;
+  const int E = w_int8(h) ? WVec<int8_t>::E : WVec<float>::E;
+  const int nc = pick_ncols(a.N, a.R, a.K, E, h->num_sms);
+  a.ksplit = pick_ksplit(a.N, a.R, a.K, E, nc, h->num_sms);
+  const int cols = nc * (kLinWarps / a.ksplit);
+  dim3 grid((a.N + cols - 1) / cols, (a.R + kRowTile - 1) / kRowTile);
+  dim3 block(32 * kLinWarps);
+  if (nc == 4) launch_linear_nc<EPI, 4>(h, a, grid, block);
+  else launch_linear_nc<EPI, 2>(h, a, grid, block);
 }
 
 // Dynamic shared memory of the input-LayerNorm linear kernels: kLinLnSmemMax
 // holds kRowTile rows of up to 4096 fp32 or 8192 bf16 elements.
+template <int EPI, int NC>
+void set_linear_attr_nc() {
+  const int b = static_cast<int>(kLinLnSmemMax);
+  CK(cudaFuncSetAttribute(linear_kernel<int8_t, __nv_bfloat16, EPI, true, NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
+  CK(cudaFuncSetAttribute(linear_kernel<int8_t, float, EPI, true, NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
+  CK(cudaFuncSetAttribute(linear_kernel<float, __nv_bfloat16, EPI, true, NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
+  CK(cudaFuncSetAttribute(linear_kernel<float, float, EPI, true, NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
+}
 template <int EPI>
 void set_linear_attr_epi() {
-  const int b = static_cast<int>(kLinLnSmemMax);
-  CK(cudaFuncSetAttribute(linear_kernel<int8_t, __nv_bfloat16, EPI, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
-  CK(cudaFuncSetAttribute(linear_kernel<int8_t, float, EPI, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
-  CK(cudaFuncSetAttribute(linear_kernel<float, __nv_bfloat16, EPI, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
-  CK(cudaFuncSetAttribute(linear_kernel<float, float, EPI, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
+  set_linear_attr_nc<EPI, 2>();
+  set_linear_attr_nc<EPI, 4>();
 }
 void set_linear_attrs() {
   set_linear_attr_epi<kEpiStore>();
@@ -1093,6 +1114,91 @@ int64_t specdec_last_launch_count(const specdec_handle *h) {
       cudaStreamSynchronize(h->stream) != cudaSuccess)
     return -1;
   return h->graph_fixed + h->graph_body * h->h_pinned[1] + h->extra_launches;
+}
+
+int specdec_time_linear(specdec_handle *h, int role, int layer, int which, int rows, int reps, void *flush,
+                        size_t flush_bytes, float *avg_us, double *alg_bytes) {
+  if (!h || !avg_us || !alg_bytes || reps < 1) return SPECDEC_ERR_INVALID;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  try {
+    CK(cudaSetDevice(h->device));
+    if (role != SPECDEC_TARGET && role != SPECDEC_DRAFT) fail(SPECDEC_ERR_INVALID, "unknown role");
+    ModelW &m = role == SPECDEC_TARGET ? h->tgt : h->dft;
+    if (!m.loaded) fail(SPECDEC_ERR_STATE, "weights not loaded");
+    const Dims &dm = m.dm;
+    if (layer < 0 || layer >= dm.L) fail(SPECDEC_ERR_INVALID, "layer out of range");
+    if (rows < 1 || rows > h->R_max) fail(SPECDEC_ERR_INVALID, "rows out of range");
+    const LayerW &L = m.layers[layer];
+    const bool ref = dm.arch == SPECDEC_ARCH_REF;
+    const int d = dm.d;
+    // rows of the prefill region marked unused, so a QKV launch appends nothing
+    CK(cudaMemsetAsync(h->pool.req, 0xff, static_cast<size_t>(rows) * sizeof(int), h->stream));
+    RowsView rv{h->pool.tok, h->pool.pos, h->pool.req};
+    const double wb = w_int8(h) ? 1.0 : 4.0, ab = static_cast<double>(h->act_elt);
+    LinearArgs a{};
+    a.R = rows; a.rows = rv; a.K = d; a.ldx = d;
+    int epi = kEpiStore;
+    double in_w = d, out_w = d;  // input / output row widths
+    switch (which) {
+      case SPECDEC_LIN_QKV:
+        a.x = h->H; a.W = L.wqkv; a.scale = L.sqkv; a.bias = L.bqkv; a.N = d + 2 * dm.kvd; a.out = h->Q; a.ldo = d;
+        a.in_g = L.g1; a.in_b = L.b1;
+        a.qkv = QKVArgs{d, dm.kvd, dm.D, h->rope, h->rope_max, h->tk, h->tv, 0, 1, 0, nullptr, nullptr};
+        epi = kEpiQKV; out_w = d + 2 * dm.kvd;
+        break;
+      case SPECDEC_LIN_OPROJ:
+        a.x = h->ATT; a.W = L.wo; a.scale = L.so; a.bias = L.bo; a.N = d; a.out = h->H; a.ldo = d;
+        a.resid = h->X; a.ldr = d; epi = kEpiResid; out_w = 2.0 * d;
+        break;
+      case SPECDEC_LIN_FFN_IN:
+        a.x = h->H; a.W = L.wgu; a.scale = L.sgu; a.bias = L.bgu; a.N = ref ? 2 * dm.F : dm.F; a.out = h->A;
+        a.ldo = dm.F; a.in_g = ref ? L.g1 : L.g2; a.in_b = ref ? L.b1 : L.b2; a.norm_out = ref ? h->X1 : nullptr;
+        epi = ref ? kEpiSwiGLU : kEpiGelu; out_w = dm.F + (ref ? d : 0);
+        break;
+      case SPECDEC_LIN_FFN_OUT:
+        a.x = h->A; a.ldx = dm.F; a.K = dm.F; a.W = L.wd; a.scale = L.sd; a.bias = L.bd; a.N = d; a.out = h->H;
+        a.ldo = d; a.resid = h->X1; a.ldr = d; epi = kEpiResid; in_w = dm.F; out_w = 2.0 * d;
+        break;
+      case SPECDEC_LIN_HEAD:
+        a.x = h->H; a.W = m.whead; a.scale = m.shead; a.bias = m.bhead; a.N = dm.V; a.out = h->logits; a.ldo = dm.V;
+        a.out_f32 = 1; a.in_g = m.layers[dm.L - 1].g2; a.in_b = m.layers[dm.L - 1].b2; out_w = dm.V;
+        if (rows > std::max(h->cfg.max_batch * (h->cfg.max_lookahead + 1), 2 * h->cfg.max_batch))
+          fail(SPECDEC_ERR_INVALID, "rows exceed the logits buffer");
+        break;
+      default:
+        fail(SPECDEC_ERR_INVALID, "unknown linear layer");
+    }
+    *alg_bytes = static_cast<double>(a.N) * a.K * wb + (w_int8(h) ? 4.0 * a.N : 0.0) + 4.0 * a.N +
+                 (a.in_g ? 8.0 * a.K : 0.0) + rows * in_w * ab + rows * out_w * (which == SPECDEC_LIN_HEAD ? 4.0 : ab);
+    CK(cudaEventCreate(&e0));
+    CK(cudaEventCreate(&e1));
+    double tot_ms = 0.0;
+    for (int i = 0; i < reps; ++i) {
+      if (flush && flush_bytes) CK(cudaMemsetAsync(flush, i & 0xff, flush_bytes, h->stream));
+      CK(cudaEventRecord(e0, h->stream));
+      switch (epi) {
+        case kEpiQKV: launch_linear<kEpiQKV>(h, a); break;
+        case kEpiResid: launch_linear<kEpiResid>(h, a); break;
+        case kEpiSwiGLU: launch_linear<kEpiSwiGLU>(h, a); break;
+        case kEpiGelu: launch_linear<kEpiGelu>(h, a); break;
+        default: launch_linear<kEpiStore>(h, a); break;
+      }
+      CK(cudaEventRecord(e1, h->stream));
+      CK(cudaEventSynchronize(e1));
+      float ms = 0.f;
+      CK(cudaEventElapsedTime(&ms, e0, e1));
+      tot_ms += ms;
+    }
+    *avg_us = static_cast<float>(tot_ms * 1000.0 / reps);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+  } catch (const SpecErr &e) {
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    h->err = e.msg;
+    return e.code;
+  }
+  return SPECDEC_OK;
 }
 
 int specdec_load_params(specdec_handle *h, int role, int n_params, const float *const *params, const int64_t *numels) {

@@ -59,11 +59,13 @@ __global__ void embed_kernel(RowsView rows, int R, const float *__restrict__ emb
 // Linear layer y = x . W + b on CUDA cores for the small row counts of draft
 // steps and verify blocks (a GEMV per tile of kRowTile rows).
 //
-// A warp owns a PAIR of adjacent output columns (so RoPE pairs and SwiGLU
-// gate/up pairs land in one lane); `ksplit` warps of a block share one pair
-// and split K, so each lane issues its weight and input vectors in one go.
-// Everything the epilogue needs (scale, bias, residual, row position, RoPE
-// factors) is loaded before the dot products.
+// A warp owns four adjacent output columns, i.e. two whole pairs (RoPE pairs
+// and SwiGLU gate/up pairs each land in one lane), for kRowTile rows, so each
+// input vector it loads feeds four weight columns; `ksplit` warps of a block
+// share the four columns and split K, so each lane issues its weight and input
+// vectors in one go.  A 32-value warp reduce-scatter leaves every lane one
+// finished (row, column).  Everything the epilogue needs (scale, bias,
+// residual, row position, RoPE factors) is loaded before the dot products.
 //
 // LayerNorm is applied by the consumer: with `in_g` set, each block first
 // normalises its kRowTile input rows into shared memory (every block holds
@@ -114,6 +116,7 @@ struct LinearArgs {
 
 constexpr int kLinWarps = 8;
 constexpr int kRowTile = 8;
+constexpr int kLinColsMax = 4;  // output columns per warp: one pair, or two adjacent pairs
 
 template <typename WT> struct WVec;
 template <> struct WVec<float> { static constexpr int E = 4; };
@@ -139,44 +142,50 @@ __device__ __forceinline__ void load_wvec(const int8_t *p, float (&w)[8]) {
   i8x4_to_f32(t.y, w + 4);
 }
 
-// Reduce-scatter of 2*kRowTile per-lane partial sums over the warp in 16
-// shuffles: afterwards lane l holds the full sum of value (column
-// (l >> 4) & 1, row ((l >> 1) & 7)); lanes differing only in bit 0 agree.
-__device__ __forceinline__ float warp_reduce16(const float (&a0)[kRowTile], const float (&a1)[kRowTile]) {
+// Reduce-scatter of NV (16 or 32) per-lane partial sums over the warp: at
+// each halving, lanes with the offset bit set keep the upper half and send the
+// lower one.  Afterwards lane l holds the full sum of value l / (32 / NV)
+// (with NV = 16 the two lanes of a value agree after a final butterfly).
+template <int NV>
+__device__ __forceinline__ float warp_reduce_scatter(const float (&v)[NV]) {
+  static_assert(NV == 16 || NV == 32, "16 or 32 values");
   const int lane = threadIdx.x & 31;
-  float v8[8];
-  {
+  float a16[16];
+  if constexpr (NV == 32) {
     const bool hi = lane & 16;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float send = hi ? a0[i] : a1[i];
-      const float keep = hi ? a1[i] : a0[i];
-      v8[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-    }
-  }
-  float v4[4];
-  {
-    const bool hi = lane & 8;
+    for (int i = 0; i < 16; ++i)
+      a16[i] = (hi ? v[i + 16] : v[i]) + __shfl_xor_sync(0xffffffffu, hi ? v[i] : v[i + 16], 16);
+  } else {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float send = hi ? v8[i] : v8[i + 4];
-      const float keep = hi ? v8[i + 4] : v8[i];
-      v4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-    }
+    for (int i = 0; i < 16; ++i) a16[i] = v[i];
   }
-  float v2[2];
+  constexpr int o8 = NV == 32 ? 8 : 16, o4 = o8 / 2, o2 = o4 / 2, o1 = o2 / 2;
+  float a8[8];
   {
-    const bool hi = lane & 4;
+    const bool hi = lane & o8;
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const float send = hi ? v4[i] : v4[i + 2];
-      const float keep = hi ? v4[i + 2] : v4[i];
-      v2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-    }
+    for (int i = 0; i < 8; ++i)
+      a8[i] = (hi ? a16[i + 8] : a16[i]) + __shfl_xor_sync(0xffffffffu, hi ? a16[i] : a16[i + 8], o8);
   }
-  const bool hi = lane & 2;
-  float v = (hi ? v2[1] : v2[0]) + __shfl_xor_sync(0xffffffffu, hi ? v2[0] : v2[1], 2);
-  return v + __shfl_xor_sync(0xffffffffu, v, 1);
+  float a4[4];
+  {
+    const bool hi = lane & o4;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      a4[i] = (hi ? a8[i + 4] : a8[i]) + __shfl_xor_sync(0xffffffffu, hi ? a8[i] : a8[i + 4], o4);
+  }
+  float a2[2];
+  {
+    const bool hi = lane & o2;
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+      a2[i] = (hi ? a4[i + 2] : a4[i]) + __shfl_xor_sync(0xffffffffu, hi ? a4[i] : a4[i + 2], o2);
+  }
+  const bool hi = lane & o1;
+  float r = (hi ? a2[1] : a2[0]) + __shfl_xor_sync(0xffffffffu, hi ? a2[0] : a2[1], o1);
+  if constexpr (NV == 16) r += __shfl_xor_sync(0xffffffffu, r, 1);
+  return r;
 }
 
 // E consecutive input elements as fp32 (kShared: p points into shared memory).
@@ -310,42 +319,49 @@ __device__ __forceinline__ void linear_epilogue(const LinearArgs &a, int r, int 
   }
 }
 
-// grid: (ceil(N / (2 * kLinWarps / ksplit)), ceil(R / kRowTile)); block: 32 * kLinWarps.
-// IN_LN: dynamic shared memory of kRowTile * K activation elements holds the
-// block's normalised input rows.
-template <typename WT, typename AT, int EPI, bool IN_LN>
+// grid: (ceil(N / (NC * kLinWarps / ksplit)), ceil(R / kRowTile)); block: 32 * kLinWarps.
+// NC: output columns per warp (2 or 4).  IN_LN: dynamic shared memory of
+// kRowTile * K activation elements holds the block's normalised input rows.
+template <typename WT, typename AT, int EPI, bool IN_LN, int NC>
 __global__ void __launch_bounds__(32 * kLinWarps, 2) linear_kernel(LinearArgs a) {
   constexpr int E = WVec<WT>::E;
-  __shared__ float s_red[kLinWarps][2 * kRowTile];
+  constexpr int NV = kRowTile * NC;  // partial sums per lane
+  constexpr int LPV = 32 / NV;       // lanes holding each finished value
+  static_assert(NC == 2 || NC == 4, "one or two column pairs per warp");
+  __shared__ float s_red[kLinWarps][32];
   extern __shared__ __align__(16) unsigned char lin_smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int ks = a.ksplit;
-  const int pairs = kLinWarps / ks;
-  const int pair = warp / ks, kidx = warp % ks;
-  const int n0 = (blockIdx.x * pairs + pair) * 2;
+  const int quads = kLinWarps / ks;
+  const int quad = warp / ks, kidx = warp % ks;
+  const int n0 = (blockIdx.x * quads + quad) * NC;
   const int r0 = blockIdx.y * kRowTile;
   const int nrows = min(kRowTile, a.R - r0);
   const bool col_ok = n0 < a.N;
-  const bool has1 = (n0 + 1) < a.N;
 
+  // After the reduction lane l holds value l / LPV = (row, column n0 + c) with
+  // value = row * NC + c; one lane of each even column finishes the pair
+  // (n, n + 1) of its row.
+  const int vi = lane / LPV;
+  const int er = vi / NC, en = n0 + vi % NC;
+  const bool epi_lane = col_ok && kidx == 0 && !((vi % NC) & 1) && (lane % LPV) == 0 && en < a.N && er < nrows;
   EpiPre pre{};
-  // lane 2i finishes row i: fetch its epilogue operands early
-  if (col_ok && kidx == 0 && lane < 16 && !(lane & 1) && (lane >> 1) < nrows)
-    epilogue_prefetch<AT, EPI>(a, r0 + (lane >> 1), n0, pre);
+  if (epi_lane) epilogue_prefetch<AT, EPI>(a, r0 + er, en, pre);
 
-  const WT *w0 = static_cast<const WT *>(a.W) + static_cast<size_t>(n0) * a.K;
-  const WT *w1 = has1 ? w0 + a.K : w0;
+  const WT *wc[NC];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) wc[c] = static_cast<const WT *>(a.W) + static_cast<size_t>(min(n0 + c, a.N - 1)) * a.K;
   const int ldx = IN_LN ? a.K : a.ldx;
   const bool vec_ok = (a.K % E == 0) && (ldx % 4 == 0);
   const int kvec = vec_ok ? a.K / E : 0;
   const int vstart = kidx * 32 + lane;
   // the first K step's weights are requested before anything else, so their
   // latency overlaps the input rows (and their LayerNorm)
-  float wa0[E], wb0[E];
+  float wf[NC][E];
   const bool first = col_ok && vstart < kvec;
   if (first) {
-    load_wvec(w0 + vstart * E, wa0);
-    load_wvec(w1 + vstart * E, wb0);
+#pragma unroll
+    for (int c = 0; c < NC; ++c) load_wvec(wc[c] + vstart * E, wf[c]);
   }
 
   const AT *xrow[kRowTile];
@@ -422,63 +438,68 @@ __global__ void __launch_bounds__(32 * kLinWarps, 2) linear_kernel(LinearArgs a)
     }
   }
 
-  float acc0[kRowTile], acc1[kRowTile];
+  float acc[NV];
 #pragma unroll
-  for (int i = 0; i < kRowTile; ++i) acc0[i] = acc1[i] = 0.f;
-  auto step = [&](int v, const float (&wa)[E], const float (&wb)[E]) {
-    float xv[kRowTile][E];
+  for (int i = 0; i < NV; ++i) acc[i] = 0.f;
+  // The input vectors of RB rows are requested together before their FMAs
+  // (one memory round trip per group): all rows with one column pair, half of
+  // them with two pairs to stay within the register budget.
+  constexpr int RB = NC == 2 ? kRowTile : kRowTile / 2;
+  auto step = [&](int v, const float (&w)[NC][E]) {
 #pragma unroll
-    for (int i = 0; i < kRowTile; ++i)
-      if (i < nrows) load_xvec<AT, E, IN_LN>(xrow[i] + v * E, xv[i]);
+    for (int h0 = 0; h0 < kRowTile; h0 += RB) {
+      float xv[RB][E];
 #pragma unroll
-    for (int i = 0; i < kRowTile; ++i) {
-      if (i < nrows) {
-        float t0 = 0.f, t1 = 0.f;
+      for (int i = 0; i < RB; ++i)
+        if (h0 + i < nrows) load_xvec<AT, E, IN_LN>(xrow[h0 + i] + v * E, xv[i]);
 #pragma unroll
-        for (int e = 0; e < E; ++e) {
-          t0 = fmaf(xv[i][e], wa[e], t0);
-          t1 = fmaf(xv[i][e], wb[e], t1);
+      for (int i = 0; i < RB; ++i) {
+        if (h0 + i < nrows) {
+#pragma unroll
+          for (int c = 0; c < NC; ++c) {
+            float t = 0.f;
+#pragma unroll
+            for (int e = 0; e < E; ++e) t = fmaf(xv[i][e], w[c][e], t);
+            acc[(h0 + i) * NC + c] += t;
+          }
         }
-        acc0[i] += t0;
-        acc1[i] += t1;
       }
     }
   };
   if (col_ok) {
-    if (first) step(vstart, wa0, wb0);
+    if (first) step(vstart, wf);
 #pragma unroll 2
     for (int v = vstart + 32 * ks; v < kvec; v += 32 * ks) {
-      float wa[E], wb[E];
-      load_wvec(w0 + v * E, wa);
-      load_wvec(w1 + v * E, wb);
-      step(v, wa, wb);
+      float w[NC][E];
+#pragma unroll
+      for (int c = 0; c < NC; ++c) load_wvec(wc[c] + v * E, w[c]);
+      step(v, w);
     }
     for (int k = kvec * E + kidx * 32 + lane; k < a.K; k += 32 * ks) {  // scalar tail / unaligned rows
-      const float wa = static_cast<float>(w0[k]), wb = static_cast<float>(w1[k]);
+      float wk[NC];
+#pragma unroll
+      for (int c = 0; c < NC; ++c) wk[c] = static_cast<float>(wc[c][k]);
 #pragma unroll
       for (int i = 0; i < kRowTile; ++i)
         if (i < nrows) {
           const float xv = to_f32(xrow[i][k]);
-          acc0[i] = fmaf(xv, wa, acc0[i]);
-          acc1[i] = fmaf(xv, wb, acc1[i]);
+#pragma unroll
+          for (int c = 0; c < NC; ++c) acc[i * NC + c] = fmaf(xv, wk[c], acc[i * NC + c]);
         }
     }
   }
-  // warp totals: lane l holds (column (l >> 4) & 1, row (l >> 1) & 7)
-  float tot = warp_reduce16(acc0, acc1);
-  const int vidx = ((lane >> 4) & 1) * kRowTile + ((lane >> 1) & 7);
+  float tot = warp_reduce_scatter<NV>(acc);
   if (ks > 1) {
-    if (!(lane & 1)) s_red[warp][vidx] = tot;
+    s_red[warp][lane] = tot;
     __syncthreads();
     if (kidx == 0) {
       float t = 0.f;
-      for (int j = 0; j < ks; ++j) t += s_red[warp + j][vidx];
+      for (int j = 0; j < ks; ++j) t += s_red[warp + j][lane];
       tot = t;
     }
   }
-  const float tot1 = __shfl_xor_sync(0xffffffffu, tot, 16);
-  if (col_ok && kidx == 0 && lane < 16 && !(lane & 1) && (lane >> 1) < nrows)
-    linear_epilogue<AT, EPI>(a, r0 + (lane >> 1), n0, tot, tot1, pre);
+  const float tot1 = __shfl_xor_sync(0xffffffffu, tot, LPV);  // column n + 1 of the same row
+  if (epi_lane) linear_epilogue<AT, EPI>(a, r0 + er, en, tot, tot1, pre);
 }
 
 // ---------------------------------------------------------------------------

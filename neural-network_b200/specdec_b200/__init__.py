@@ -34,7 +34,11 @@ STATUS = {0: "OK", 1: "ERR_INVALID", 2: "ERR_CUDA", 3: "ERR_OOM", 4: "ERR_SEQ_LE
 # Every symbol include/specdec.h declares.
 EXPORTS = ("specdec_create", "specdec_destroy", "specdec_last_error", "specdec_load_params",
            "specdec_generate", "specdec_generate_device", "specdec_stream", "specdec_forward_logits",
-           "specdec_philox_uniforms", "specdec_last_launch_count", "specdec_forward_logits_noalloc")
+           "specdec_philox_uniforms", "specdec_last_launch_count", "specdec_forward_logits_noalloc",
+           "specdec_time_linear")
+
+# linear layers of specdec_time_linear
+LIN_QKV, LIN_OPROJ, LIN_FFN_IN, LIN_FFN_OUT, LIN_HEAD = 0, 1, 2, 3, 4
 
 
 class SpecDecError(RuntimeError):
@@ -90,6 +94,8 @@ def load_library(path: str = LIB_PATH):
                                                    C.c_void_p]
     lib.specdec_last_launch_count.restype = C.c_int64
     lib.specdec_last_launch_count.argtypes = [C.c_void_p]
+    lib.specdec_time_linear.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                        C.c_size_t, C.POINTER(C.c_float), C.POINTER(C.c_double)]
     _lib = lib
     return lib
 
@@ -204,3 +210,12 @@ class Engine:
 
     def last_launch_count(self) -> int:
         return int(self._lib.specdec_last_launch_count(self.h))
+
+    def time_linear(self, role: int, layer: int, which: int, rows: int, reps: int, flush_ptr: int = 0,
+                    flush_bytes: int = 0):
+        """Mean device time (us) of one linear layer's kernel over `rows` rows, each
+        launch alone with the L2 flushed before it, and its algorithmic bytes."""
+        us, nb = C.c_float(0.0), C.c_double(0.0)
+        self._check(self._lib.specdec_time_linear(self.h, role, layer, which, rows, reps, C.c_void_p(flush_ptr),
+                                                  C.c_size_t(flush_bytes), C.byref(us), C.byref(nb)))
+        return float(us.value), float(nb.value)
