@@ -34,6 +34,7 @@
 
 #include "../../include/specdec.h"
 #include "forward.cuh"
+#include "gemm.cuh"
 #include "sample.cuh"
 
 using namespace specdec;
@@ -156,6 +157,7 @@ struct specdec_handle {
   ModelW tgt, dft;
   std::vector<void *> allocs;
   std::vector<void *> weight_allocs[2];
+  std::map<const void *, void *> w_bf16;  // int8 weight matrix -> its bf16 image (tensor-core path)
 
   // caches
   void *tk = nullptr, *tv = nullptr, *dk = nullptr, *dv = nullptr;
@@ -298,6 +300,16 @@ void upload_stacked(specdec_handle *h, int role, const std::vector<DenseSrc> &sr
   if (i8) {
     ds = static_cast<float *>(h->dalloc(Ntot * sizeof(float), &own));
     CK(cudaMemcpy(ds, scale.data(), Ntot * sizeof(float), cudaMemcpyHostToDevice));
+  }
+  if (i8 && act_bf16(h)) {
+    // exact bf16 image of the codes for the tensor-core GEMM (large row batches)
+    const size_t n = static_cast<size_t>(Ntot) * K;
+    void *dw16 = h->dalloc(n * 2, &own);
+    i8_to_bf16_kernel<<<static_cast<unsigned>(std::min<size_t>((n + 255) / 256, 4096)), 256, 0, h->stream>>>(
+        static_cast<const int8_t *>(dw), static_cast<__nv_bfloat16 *>(dw16), n);
+    CK(cudaGetLastError());
+    CK(cudaStreamSynchronize(h->stream));
+    h->w_bf16[dw] = dw16;
   }
   *wout = dw;
   *sout = ds;
@@ -494,9 +506,62 @@ void launch_linear_nc(specdec_handle *h, const LinearArgs &a, dim3 grid, dim3 bl
   }
 }
 
+// 2-D TMA view [rows][K] of a bf16 matrix with row stride ld elements, box
+// kBK x box_rows, 128-byte swizzle (the K-major operand layout of the GEMM).
+CUtensorMap gemm_operand_map(const void *base, int K, int rows, int ld, int box_rows) {
+  if ((ld * 2) % 16 != 0 || (reinterpret_cast<uintptr_t>(base) & 15) != 0)
+    fail(SPECDEC_ERR_UNSUPPORTED, "tensor-core GEMM operands need 16-byte aligned rows");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = tensor_map_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims,
+                                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) fail(SPECDEC_ERR_CUDA, "cuTensorMapEncodeTiled failed with " + std::to_string(static_cast<int>(r)));
+  return m;
+}
+
+// The tensor-core path: bf16 activations, int8 weights with a bf16 image, at
+// least kGemmMinRows rows.  An input LayerNorm runs first as its own kernel,
+// writing the normalised rows where the GEMV would have stored them
+// (norm_out) or into X1, which is free whenever a LayerNorm feeds a GEMM.
+template <int EPI>
+bool try_launch_gemm(specdec_handle *h, LinearArgs a) {
+  if (!act_bf16(h) || !w_int8(h) || a.R < kGemmMinRows || (a.K % 8) != 0) return false;
+  auto it = h->w_bf16.find(a.W);
+  if (it == h->w_bf16.end()) return false;
+  const void *A = a.x;
+  int lda = a.ldx;
+  if (a.in_g) {
+    void *dst = a.norm_out ? a.norm_out : h->X1;
+    launch(h, ln_rows_kernel<__nv_bfloat16>, dim3((a.R + 7) / 8), dim3(256), 0,
+           static_cast<const __nv_bfloat16 *>(a.x), a.ldx, a.in_rows, a.R, a.K, a.in_g, a.in_b,
+           static_cast<__nv_bfloat16 *>(dst), static_cast<__nv_bfloat16 *>(nullptr));
+    A = dst;
+    lda = a.K;
+  } else if (a.in_rows) {
+    return false;  // row gathers only come with a LayerNorm
+  }
+  GemmArgs g{};
+  g.tma_a = gemm_operand_map(A, a.K, a.R, lda, kBM);
+  g.tma_b = gemm_operand_map(it->second, a.K, a.N, a.K, kBN);
+  a.in_g = a.in_b = nullptr;
+  a.in_rows = nullptr;
+  a.norm_out = nullptr;
+  g.lin = a;
+  g.err = h->st.err;
+  launch(h, gemm_kernel<EPI>, dim3((a.N + kBN - 1) / kBN, (a.R + kBM - 1) / kBM), dim3(kGemmThreads),
+         static_cast<size_t>(kGemmSmem), g);
+  return true;
+}
+
 template <int EPI>
 void launch_linear(specdec_handle *h, LinearArgs a) {
   if (a.R <= 0) return;
+  if (try_launch_gemm<EPI>(h, a)) return;
   const int E = w_int8(h) ? WVec<int8_t>::E : WVec<float>::E;
   const int nc = pick_ncols(a.N, a.R, a.K, E, h->num_sms);
   a.ksplit = pick_ksplit(a.N, a.R, a.K, E, nc, h->num_sms);
@@ -521,6 +586,13 @@ template <int EPI>
 void set_linear_attr_epi() {
   set_linear_attr_nc<EPI, 2>();
   set_linear_attr_nc<EPI, 4>();
+}
+void set_gemm_attrs() {
+  CK(cudaFuncSetAttribute(gemm_kernel<kEpiStore>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
+  CK(cudaFuncSetAttribute(gemm_kernel<kEpiResid>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
+  CK(cudaFuncSetAttribute(gemm_kernel<kEpiQKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
+  CK(cudaFuncSetAttribute(gemm_kernel<kEpiSwiGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
+  CK(cudaFuncSetAttribute(gemm_kernel<kEpiGelu>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
 }
 void set_linear_attrs() {
   set_linear_attr_epi<kEpiStore>();
@@ -987,6 +1059,7 @@ int specdec_create(const specdec_config *cfg, int device, specdec_handle **out) 
     set_attn_attrs<float, int8_t>();
     set_attn_attrs<__nv_bfloat16, int8_t>();
     set_linear_attrs();
+    set_gemm_attrs();
     {
       const int vs = td.V * static_cast<int>(sizeof(float));
       CK(cudaFuncSetAttribute(first_token_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, vs));

@@ -1,0 +1,229 @@
+// Tensor-core linear layer for large row batches (prefill, wide verify and
+// tree blocks) with bf16 activations: y = x . W^T on tcgen05, fp32
+// accumulators in tensor memory, the same epilogues as the GEMV
+// (scale and bias, residual, RoPE + cache append, SwiGLU, GELU, logits).
+//
+// CTA tile kBM x kBN = 128 x 256, K in steps of kBK = 64 bf16 (one 128-byte
+// swizzle span).  Thread 0 streams A (activation rows, [R][K]) and B
+// (weight rows, [N][K]) tiles with TMA (128-byte swizzle, no multicast) into
+// a kStages-deep ring; thread 32 issues tcgen05.mma (M = 128, N = 256,
+// K = 16 per instruction, both operands K-major from shared memory) and
+// releases each stage with tcgen05.commit; after the last commit all four
+// warps read their 32 accumulator lanes (= rows) with tcgen05.ld and run the
+// epilogue on column pairs.  int8 weights are multiplied as their exact bf16
+// images (|q| <= 127) and scaled per output column in the epilogue, the
+// reassociation sum(x * q) * s that the GEMV uses too.
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+#include "forward.cuh"
+
+namespace specdec {
+
+constexpr int kBM = 128;
+constexpr int kBN = 256;
+constexpr int kBK = 64;
+constexpr int kStages = 4;
+constexpr int kGemmThreads = 128;
+constexpr int kGemmMinRows = 64;                        // below this the GEMV is used
+constexpr int kGemmABytes = kBM * kBK * 2;              // 16 KB
+constexpr int kGemmBBytes = kBN * kBK * 2;              // 32 KB
+constexpr int kGemmStageBytes = kGemmABytes + kGemmBBytes;
+constexpr int kGemmSmem = kStages * kGemmStageBytes + 1024;
+constexpr int kTmemCols = 256;                          // fp32 accumulator columns (one per output column)
+
+struct alignas(64) GemmArgs {
+  CUtensorMap tma_a;  // [R][K] bf16 rows, box kBK x kBM, 128-byte swizzle
+  CUtensorMap tma_b;  // [N][K] bf16 weights, box kBK x kBN, 128-byte swizzle
+  LinearArgs lin;     // epilogue operands (out, scale, bias, resid, rows, qkv), R, N, K
+  int *err;
+};
+
+// Shared-memory matrix descriptor of a K-major operand tile whose rows are
+// 128 bytes with the 128-byte swizzle: 8-row core groups 1024 bytes apart
+// (stride byte offset), version 1, layout type 2 (128-byte swizzle).
+__device__ __forceinline__ uint64_t umma_desc_k128(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) |
+         (2ull << 61);
+}
+
+// Instruction descriptor of kind::f16: D fp32, A and B bf16, both K-major,
+// N = kBN, M = kBM.
+constexpr uint32_t kGemmIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kBN >> 3) << 17) |
+                                (static_cast<uint32_t>(kBM >> 4) << 24);
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+      : "memory");
+}
+// Arrives on `bar` once every tcgen05.mma this thread issued so far has completed.
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
+      "[%16];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_constant__ GemmArgs g) {
+  extern __shared__ unsigned char gemm_smem_raw[];
+  unsigned char *tiles =
+      reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(gemm_smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full[kStages], empty[kStages], done;
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_fail;
+
+  const LinearArgs &a = g.lin;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * kBN, m0 = blockIdx.y * kBM;
+  const int nk = (a.K + kBK - 1) / kBK;
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (threadIdx.x == 32) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&done, 1);
+    s_fail = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+
+  if (threadIdx.x == 0) {
+    // producer: TMA tiles into the ring
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % kStages;
+      if (kb >= kStages && !mbar_wait(&empty[s], ((kb / kStages) - 1) & 1)) {
+        s_fail = 1;
+        break;
+      }
+      unsigned char *sa = tiles + s * kGemmStageBytes;
+      unsigned char *sb = sa + kGemmABytes;
+      mbar_expect_tx(&full[s], kGemmStageBytes);
+      tma_load_2d(sa, &g.tma_a, kb * kBK, m0, &full[s]);
+      tma_load_2d(sb, &g.tma_b, kb * kBK, n0, &full[s]);
+    }
+  } else if (threadIdx.x == 32) {
+    // MMA issuer
+    bool ok = true;
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % kStages;
+      if (!mbar_wait(&full[s], (kb / kStages) & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t sa = smem_u32(tiles + s * kGemmStageBytes);
+      const uint32_t sb = sa + kGemmABytes;
+#pragma unroll
+      for (int k = 0; k < kBK / 16; ++k)
+        tc_mma(tmem, umma_desc_k128(sa + 32 * k), umma_desc_k128(sb + 32 * k), kGemmIdesc, (kb | k) ? 1u : 0u);
+      tc_commit(&empty[s]);  // the stage is free once these MMAs have read it
+    }
+    if (!ok) s_fail = 1;
+    tc_commit(&done);
+  }
+  __syncwarp();
+
+  // epilogue: warp w owns accumulator lanes (rows) 32w .. 32w + 31
+  const bool ok = __all_sync(0xffffffffu, mbar_wait(&done, 0) ? 1 : 0) != 0;  // tcgen05.ld is warp-collective
+  if (!ok) s_fail = 1;
+  tc_fence_after();
+  const int row = m0 + warp * 32 + lane;
+  if (ok) {
+    for (int c = 0; c < kBN; c += 16) {
+      if (n0 + c >= a.N) break;  // warp-uniform
+      float v[16];
+      tmem_ld16(tmem + (static_cast<uint32_t>(warp * 32) << 16) + c, v);
+      if (row < a.R) {
+#pragma unroll
+        for (int j = 0; j < 16; j += 2) {
+          const int n = n0 + c + j;
+          if (n < a.N) {
+            EpiPre pre{};
+            epilogue_prefetch<__nv_bfloat16, EPI>(a, row, n, pre);
+            linear_epilogue<__nv_bfloat16, EPI>(a, row, n, v[j], v[j + 1], pre);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && s_fail && g.err) atomicOr(g.err, kErrTimeout);
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+}
+
+// LayerNorm of R input rows (optionally gathered through in_rows), one warp
+// per row, in the operation order of the GEMV's input LayerNorm, written as
+// contiguous rows [R][K] of the activation type (the GEMM's A operand) and,
+// when norm_out is set, also there.
+template <typename AT>
+__global__ void ln_rows_kernel(const AT *__restrict__ x, int ldx, const int *__restrict__ in_rows, int R, int K,
+                               const float *__restrict__ g, const float *__restrict__ b, AT *__restrict__ out,
+                               AT *__restrict__ norm_out) {
+  const int lane = threadIdx.x & 31;
+  const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (r >= R) return;
+  const int pr = in_rows ? in_rows[r] : r;
+  const AT *xr = x + static_cast<size_t>(pr) * ldx;
+  AT *y = out + static_cast<size_t>(r) * K;
+  float s = 0.f;
+  for (int c = lane; c < K; c += 32) s += to_f32(xr[c]);
+  const float mean = __fdiv_rn(warp_sum(s), static_cast<float>(K));
+  float q = 0.f;
+  for (int c = lane; c < K; c += 32) {
+    const float df = to_f32(xr[c]) - mean;
+    q = fmaf(df, df, q);
+  }
+  const float sd = sqrtf(__fdiv_rn(warp_sum(q), static_cast<float>(K)) + 1e-5f);
+  AT *no = norm_out ? norm_out + static_cast<size_t>(r) * K : nullptr;
+  for (int c = lane; c < K; c += 32) {
+    const AT v = from_f32<AT>(__fadd_rn(__fmul_rn(__fdiv_rn(to_f32(xr[c]) - mean, sd), __ldg(g + c)), __ldg(b + c)));
+    y[c] = v;
+    if (no) no[c] = v;
+  }
+}
+
+// int8 weight codes -> their exact bf16 values.
+__global__ void i8_to_bf16_kernel(const int8_t *__restrict__ q, __nv_bfloat16 *__restrict__ out, size_t n) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    out[i] = __float2bfloat16_rn(static_cast<float>(q[i]));
+}
+
+}  // namespace specdec

@@ -17,6 +17,10 @@ from specdec_b200.synth import ModelShape, draft_params, make_params, make_promp
 # Decision-margin thresholds below which a token mismatch counts as a near-tie.
 GREEDY_REL_GAP = 1e-4      # relative top-2 logit gap
 SAMPLED_MARGIN = 2e-5      # |r*q - p| or |cdf - u|
+# With bf16 activations every layer output is rounded to 8 significant bits,
+# so logits agree to about 1e-2 relative (the bf16 logits tolerance is 2e-2):
+# a greedy mismatch is a near-tie below this relative top-2 gap.
+BF16_GREEDY_GAP = 2e-2
 
 
 @dataclass
@@ -48,9 +52,11 @@ def make_pair(shape: ModelShape, draft_layers: int, seed: int = 0, int8: bool = 
     return Pair(shape, draft_layers, P, DP, eng, t, d, int8, act_bf16, kv_mode)
 
 
-def compare_tokens(gpu: np.ndarray, ref: np.ndarray, margins: np.ndarray, prompt_len: int, greedy: bool):
+def compare_tokens(gpu: np.ndarray, ref: np.ndarray, margins: np.ndarray, prompt_len: int, greedy: bool,
+                   tol: Optional[float] = None):
     """Returns (n_exact_requests, n_near_ties).  Raises on a real mismatch."""
-    tol = GREEDY_REL_GAP if greedy else SAMPLED_MARGIN
+    if tol is None:
+        tol = GREEDY_REL_GAP if greedy else SAMPLED_MARGIN
     exact, ties = 0, 0
     assert gpu.shape == ref.shape, (gpu.shape, ref.shape)
     for b in range(gpu.shape[0]):

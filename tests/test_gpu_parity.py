@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 
 import specdec_b200 as sd
-from helpers import compare_tokens, make_pair, run_both
+from helpers import BF16_GREEDY_GAP, compare_tokens, make_pair, run_both
 from specdec_b200.synth import ARCH_CFG, ModelShape, make_prompts
 
 pytestmark = pytest.mark.gpu
@@ -153,3 +153,33 @@ def test_spec_int8_kv(gpu_lib, oracle_built, name, T):
     _, tg, sg, to, so, mg = run_both(pair, 3, 12, 40, 4, T, seed=31, use_uniforms=T > 0)
     exact, ties = compare_tokens(tg, to, mg, 12, greedy=T <= 0)
     assert exact + ties == 3 and ties <= 1
+
+
+# Tensor-core GEMM path (bf16 activations, int8 weights, >= 64 rows): long
+# prefills, and a vocabulary / width that are not multiples of the 256 x 64
+# tile (column and K tails).
+GEMM_SHAPES = {
+    "cfg1": SHAPES["cfg1"],
+    "ragged": (ModelShape(vocab=1000, d_model=192, n_heads=3, d_ff=320, n_layers=2, max_seq_len=200), 1),
+}
+
+
+@pytest.mark.parametrize("name", list(GEMM_SHAPES))
+@pytest.mark.parametrize("kv_mode", [0, 1])
+def test_forward_logits_bf16_gemm(gpu_lib, oracle_built, name, kv_mode):
+    shape, dl = GEMM_SHAPES[name]
+    pair = make_pair(shape, dl, seed=21, int8=True, act_bf16=True, kv_mode=kv_mode, max_prompt_len=160)
+    toks = make_prompts(1, 150, shape.vocab, seed=22)[0]
+    for role, om in ((sd.TARGET, pair.target), (sd.DRAFT, pair.draft)):
+        g = pair.engine.forward_logits(role, toks)
+        o = om.forward(toks, act_bf16=True, kv_mode=kv_mode)
+        assert rel_err(g, o) < BF16_REL, (name, role, rel_err(g, o))
+
+
+def test_greedy_spec_bf16_gemm(gpu_lib, oracle_built):
+    # 16 requests x (k + 1) = 80 verify rows and 16 x 80 prefill rows take the GEMM
+    shape, dl = GEMM_SHAPES["ragged"]
+    pair = make_pair(shape, dl, seed=23, int8=True, act_bf16=True, kv_mode=1, max_batch=16, max_prompt_len=80)
+    _, tg, sg, to, so, mg = run_both(pair, 16, 80, 24, 4, 0.0)
+    exact, ties = compare_tokens(tg, to, mg, 80, greedy=True, tol=BF16_GREEDY_GAP)
+    assert exact + ties == 16 and ties <= 4
