@@ -531,6 +531,12 @@ CUtensorMap gemm_operand_map(const void *base, int K, int rows, int ld, int box_
 template <int EPI>
 bool try_launch_gemm(specdec_handle *h, LinearArgs a) {
   if (!act_bf16(h) || !w_int8(h) || a.R < kGemmMinRows || (a.K % 8) != 0) return false;
+  // the chunked epilogue's 16-byte vectors: aligned output / residual rows,
+  // and q / k / v sections and heads in whole 16-column chunks
+  if (a.ldo % (a.out_f32 ? 4 : 8) != 0) return false;
+  if (EPI == kEpiResid && a.ldr % 8 != 0) return false;
+  if (EPI == kEpiSwiGLU && a.ldo % 8 != 0) return false;
+  if (EPI == kEpiQKV && (a.qkv.d % 16 != 0 || a.qkv.kvd % 16 != 0 || a.qkv.D % 16 != 0)) return false;
   auto it = h->w_bf16.find(a.W);
   if (it == h->w_bf16.end()) return false;
   const void *A = a.x;

@@ -88,6 +88,154 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Row operands of one 16-column chunk (columns n .. n + 15 of row `row`),
+// fetched one chunk ahead of use: the residual values (Resid) or the RoPE
+// (cos, sin) pairs (QKV).  kBN and the q / k / v section widths are multiples
+// of 16 and head_dim is a multiple of 16 on this path, so a chunk never
+// straddles a head or a section.
+struct ChunkOps {
+  float v[16];
+};
+
+__device__ __forceinline__ void bf16x8_to_f32(uint4 u, float *f) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+__device__ __forceinline__ uint4 f32x8_to_bf16(const float *f) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 t = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+    w[i] = *reinterpret_cast<const uint32_t *>(&t);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+template <int EPI>
+__device__ __forceinline__ void chunk_load(const LinearArgs &a, int row, int n, int req, int pos, ChunkOps &op) {
+  if constexpr (EPI == kEpiResid) {
+    const __nv_bfloat16 *rs = static_cast<const __nv_bfloat16 *>(a.resid) + static_cast<size_t>(row) * a.ldr + n;
+    if (n + 16 <= a.N) {
+      bf16x8_to_f32(__ldg(reinterpret_cast<const uint4 *>(rs)), op.v);
+      bf16x8_to_f32(__ldg(reinterpret_cast<const uint4 *>(rs + 8)), op.v + 8);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) op.v[j] = (n + j < a.N) ? __bfloat162float(rs[j]) : 0.f;
+    }
+  } else if constexpr (EPI == kEpiQKV) {
+    const QKVArgs &q = a.qkv;
+    if (req >= 0 && pos >= 0 && pos < q.rope_max_pos && n < q.d + q.kvd) {
+      const int e = (n < q.d ? n : n - q.d) % q.D;
+      const float4 *t = reinterpret_cast<const float4 *>(q.rope + static_cast<size_t>(pos) * (q.D / 2) + (e >> 1));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 c = __ldg(t + i);
+        op.v[4 * i] = c.x; op.v[4 * i + 1] = c.y; op.v[4 * i + 2] = c.z; op.v[4 * i + 3] = c.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; j += 2) {
+        op.v[j] = 1.f;
+        op.v[j + 1] = 0.f;
+      }
+    }
+  }
+}
+
+// Epilogue of one chunk: the arithmetic of linear_epilogue, with the
+// chunk's outputs stored as 16-byte vectors.
+template <int EPI>
+__device__ __forceinline__ void chunk_store(const LinearArgs &a, int row, int n, float (&v)[16], const ChunkOps &op,
+                                            const float *ssc, const float *sbi, int req, int pos) {
+  using AT = __nv_bfloat16;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = v[j] * ssc[j] + sbi[j];
+  const bool full = n + 16 <= a.N;
+  if constexpr (EPI == kEpiStore || EPI == kEpiResid || EPI == kEpiGelu) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if constexpr (EPI == kEpiResid) v[j] = v[j] + op.v[j];
+      if constexpr (EPI == kEpiGelu) v[j] = 0.5f * v[j] * (1.0f + erff(v[j] * 0.70710678118654752f));
+    }
+    if (a.out_f32) {
+      float *o = static_cast<float *>(a.out) + static_cast<size_t>(row) * a.ldo + n;
+      if (full) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          reinterpret_cast<float4 *>(o)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      } else {
+        for (int j = 0; j < 16 && n + j < a.N; ++j) o[j] = v[j];
+      }
+    } else {
+      AT *o = static_cast<AT *>(a.out) + static_cast<size_t>(row) * a.ldo + n;
+      if (full) {
+        reinterpret_cast<uint4 *>(o)[0] = f32x8_to_bf16(v);
+        reinterpret_cast<uint4 *>(o)[1] = f32x8_to_bf16(v + 8);
+      } else {
+        for (int j = 0; j < 16 && n + j < a.N; ++j) o[j] = __float2bfloat16_rn(v[j]);
+      }
+    }
+  } else if constexpr (EPI == kEpiSwiGLU) {
+    // SwiGLU::forward (src/nn/layer.cpp:1704-1710) on the interleaved pairs
+    float y[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float g = v[2 * i], u = v[2 * i + 1];
+      const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
+      y[i] = __fmul_rn(__fmul_rn(g, sg), u);
+    }
+    AT *o = static_cast<AT *>(a.out) + static_cast<size_t>(row) * a.ldo + (n >> 1);
+    if (full) *reinterpret_cast<uint4 *>(o) = f32x8_to_bf16(y);
+    else
+      for (int i = 0; i < 8 && n + 2 * i + 1 < a.N; ++i) o[i] = __float2bfloat16_rn(y[i]);
+  } else if constexpr (EPI == kEpiQKV) {
+    if (req < 0) return;
+    const QKVArgs &q = a.qkv;
+    if (pos < 0 || pos >= q.S_cap || pos >= q.rope_max_pos) {
+      if (q.err) atomicOr(q.err, kErrSeqLen);
+      return;
+    }
+    if (n < q.d + q.kvd) {
+      // Tensor::rope (src/core/tensor.cpp:1144-1163) on pairs (2j, 2j+1)
+#pragma unroll
+      for (int j = 0; j < 16; j += 2) {
+        const float c = op.v[j], sn = op.v[j + 1];
+        const float x0 = __fsub_rn(__fmul_rn(v[j], c), __fmul_rn(v[j + 1], sn));
+        const float x1 = __fadd_rn(__fmul_rn(v[j], sn), __fmul_rn(v[j + 1], c));
+        v[j] = x0;
+        v[j + 1] = x1;
+      }
+    }
+    if (n < q.d) {
+      uint4 *o = reinterpret_cast<uint4 *>(static_cast<AT *>(a.out) + static_cast<size_t>(row) * a.ldo + n);
+      o[0] = f32x8_to_bf16(v);
+      o[1] = f32x8_to_bf16(v + 8);
+    } else {
+      const bool is_k = n < q.d + q.kvd;
+      const int nn = is_k ? n - q.d : n - q.d - q.kvd;
+      const int h = nn / q.D, e = nn % q.D;
+      const size_t off = static_cast<size_t>(req) * q.kv_req_stride + (static_cast<size_t>(h) * q.S_cap + pos) * q.D + e;
+      if (q.kv_mode == 2) {
+        float4 *st = reinterpret_cast<float4 *>(q.stage + static_cast<size_t>(row) * 2 * q.kvd + (is_k ? 0 : q.kvd) + nn);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) st[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      } else if (q.kv_mode == 1) {
+        uint4 *c = reinterpret_cast<uint4 *>(static_cast<AT *>(is_k ? q.kc : q.vc) + off);
+        c[0] = f32x8_to_bf16(v);
+        c[1] = f32x8_to_bf16(v + 8);
+      } else {
+        float4 *c = reinterpret_cast<float4 *>(static_cast<float *>(is_k ? q.kc : q.vc) + off);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) c[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      }
+    }
+  }
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_constant__ GemmArgs g) {
   extern __shared__ unsigned char gemm_smem_raw[];
@@ -96,6 +244,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
   __shared__ __align__(8) uint64_t full[kStages], empty[kStages], done;
   __shared__ uint32_t s_tmem;
   __shared__ int s_fail;
+  __shared__ __align__(16) float s_scale[kBN], s_bias[kBN];
 
   const LinearArgs &a = g.lin;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -122,6 +271,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
   tc_fence_after();
   const uint32_t tmem = s_tmem;
 
+  if (warp >= 2) {
+    // the epilogue's per-column operands, while the main loop runs
+    for (int j = threadIdx.x - 64; j < kBN; j += 64) {
+      const int n = n0 + j;
+      s_scale[j] = (n < a.N && a.scale) ? __ldg(a.scale + n) : 1.f;
+      s_bias[j] = n < a.N ? __ldg(a.bias + n) : 0.f;
+    }
+  }
   if (threadIdx.x == 0) {
     // producer: TMA tiles into the ring
     for (int kb = 0; kb < nk; ++kb) {
@@ -162,23 +319,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
   const bool ok = __all_sync(0xffffffffu, mbar_wait(&done, 0) ? 1 : 0) != 0;  // tcgen05.ld is warp-collective
   if (!ok) s_fail = 1;
   tc_fence_after();
+  __syncthreads();  // the per-column scale and bias are in shared memory
   const int row = m0 + warp * 32 + lane;
+  const bool row_ok = row < a.R;
+  int req = 0, pos = 0;
+  if constexpr (EPI == kEpiQKV) {
+    req = row_ok ? a.rows.req[row] : -1;
+    pos = row_ok ? a.rows.pos[row] : 0;
+  }
+  const int ncols = min(kBN, a.N - n0);
   if (ok) {
-    for (int c = 0; c < kBN; c += 16) {
-      if (n0 + c >= a.N) break;  // warp-uniform
+    // chunks of 16 columns, the next chunk's row operands in flight
+    const uint32_t tbase = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    ChunkOps op0, op1;
+    if (row_ok) chunk_load<EPI>(a, row, n0, req, pos, op0);
+    for (int c = 0; c < ncols; c += 32) {
       float v[16];
-      tmem_ld16(tmem + (static_cast<uint32_t>(warp * 32) << 16) + c, v);
-      if (row < a.R) {
-#pragma unroll
-        for (int j = 0; j < 16; j += 2) {
-          const int n = n0 + c + j;
-          if (n < a.N) {
-            EpiPre pre{};
-            epilogue_prefetch<__nv_bfloat16, EPI>(a, row, n, pre);
-            linear_epilogue<__nv_bfloat16, EPI>(a, row, n, v[j], v[j + 1], pre);
-          }
-        }
-      }
+      if (row_ok && c + 16 < ncols) chunk_load<EPI>(a, row, n0 + c + 16, req, pos, op1);
+      tmem_ld16(tbase + c, v);
+      if (row_ok) chunk_store<EPI>(a, row, n0 + c, v, op0, s_scale + c, s_bias + c, req, pos);
+      if (c + 16 >= ncols) break;  // warp-uniform
+      if (row_ok && c + 32 < ncols) chunk_load<EPI>(a, row, n0 + c + 32, req, pos, op0);
+      tmem_ld16(tbase + c + 16, v);
+      if (row_ok) chunk_store<EPI>(a, row, n0 + c + 16, v, op1, s_scale + c + 16, s_bias + c + 16, req, pos);
     }
   }
   tc_fence_before();
