@@ -185,6 +185,23 @@ class _SpecParams(C.Structure):
                 ("catchup", C.c_int32), ("num", _Numerics), ("cache_cap", C.c_int32)]
 
 
+class _TreeParams(C.Structure):
+    _fields_ = [("depth", C.c_int32), ("branch", C.c_int32 * 8)]
+
+
+def tree_slots(branching) -> int:
+    """Uniform slots per round of tree speculation: depth * max branch + 1."""
+    return len(branching) * max(branching) + 1
+
+
+def tree_nodes(branching) -> int:
+    n, level = 0, 1
+    for b in branching:
+        level *= b
+        n += level
+    return n
+
+
 class _OracleLib:
     _lib = None
 
@@ -206,6 +223,8 @@ class _OracleLib:
             lib.oc_forward_chunked.argtypes = [C.c_void_p, C.POINTER(_Numerics), _i64p, _i32p, C.c_int, _f32p]
             lib.oc_generate_speculative.argtypes = [C.c_void_p, C.c_void_p, C.POINTER(_SpecParams), _i64p,
                                                     C.c_int, C.c_int, _i64p, _i64p, C.c_void_p, C.c_int]
+            lib.oc_generate_tree.argtypes = [C.c_void_p, C.c_void_p, C.POINTER(_SpecParams), C.POINTER(_TreeParams),
+                                             _i64p, C.c_int, C.c_int, _i64p, _i64p, C.c_void_p, C.c_int]
             lib.oc_generate_advanced.argtypes = [C.c_void_p, C.POINTER(_Numerics), _i64p, C.c_int, C.c_int,
                                                  C.c_float, C.c_int, C.c_float, C.c_uint32, _i64p]
             lib.oc_get_probs.argtypes = [_f32p, C.c_int, C.c_float, C.c_int, C.c_float, _f32p]
@@ -301,6 +320,34 @@ def oracle_generate_speculative(target: Oracle, draft: Oracle, prompts: np.ndarr
                      n_rounds, catchup, _Numerics(1 if act_bf16 else 0, kv_mode), cache_cap)
     _oc_check(_OracleLib.get().oc_generate_speculative(target.h, draft.h, C.byref(sp), prompts, B, S,
                                                        out, stats, margins.ctypes.data, n_threads))
+    del keep
+    return out, stats, margins
+
+
+def oracle_generate_tree(target: Oracle, draft: Oracle, prompts: np.ndarray, max_new: int, branching,
+                         temperature: float = 1.0, top_k: int = 0, top_p: float = 1.0, seed: int = 42,
+                         uniforms: Optional[np.ndarray] = None, act_bf16: bool = False, kv_mode: int = 0,
+                         cache_cap: int = 0, n_threads: int = 0):
+    """Tree speculation (oracle/specdec_oracle.cpp: tree_one).  Returns
+    (tokens [B, S+max_new], stats [B, 4] = rounds, tree nodes drafted, accepted, rejections,
+    margins [B, max_new])."""
+    prompts = np.ascontiguousarray(np.atleast_2d(prompts), np.int64)
+    B, S = prompts.shape
+    out = np.zeros((B, S + max_new), np.int64)
+    stats = np.zeros((B, 4), np.int64)
+    margins = np.full((B, max_new), np.inf, np.float64)
+    keep = None
+    if uniforms is not None:
+        keep = np.ascontiguousarray(uniforms, np.float32)
+        assert keep.shape[0] == B and keep.shape[2] == tree_slots(branching)
+        uptr, n_rounds, mode = keep.ctypes.data, keep.shape[1], 1
+    else:
+        uptr, n_rounds, mode = None, 0, 0
+    sp = _SpecParams(max_new, len(branching), temperature, top_k, top_p, mode, seed & 0xFFFFFFFF, uptr,
+                     n_rounds, 1, _Numerics(1 if act_bf16 else 0, kv_mode), cache_cap)
+    tp = _TreeParams(len(branching), (C.c_int32 * 8)(*list(branching)))
+    _oc_check(_OracleLib.get().oc_generate_tree(target.h, draft.h, C.byref(sp), C.byref(tp), prompts, B, S,
+                                                out, stats, margins.ctypes.data, n_threads))
     del keep
     return out, stats, margins
 

@@ -707,6 +707,247 @@ void spec_one(const Model &tgt, const Model &dft, const SpecParams &sp, const in
   }
 }
 
+// ---------------------------------------------------------------------------
+// Tree speculation (no counterpart in the reference).  Per round the draft
+// expands a token tree level by level: every node at depth l < L gets the
+// branch[l] most likely next tokens of the draft as children (largest
+// logits, ties to the lower id).  The target scores every node; acceptance
+// walks from the root, trying a node's children in rank order as point-mass
+// proposals: greedy accepts the child equal to the target's argmax; sampled
+// accepts child c when u < p(c) and otherwise sets p(c) = 0 and renormalises
+// p, which samples exactly from p.  When no child is accepted the token is
+// drawn from the remaining p; after an accepted leaf a bonus token is drawn
+// from the leaf's p.  Here each node's logits come from running the model on
+// the committed sequence plus the node's path (what an ancestor-masked tree
+// forward computes).  Uniform slots per round: depth * bmax + rank for the
+// test of a child, L * bmax for the drawn token.
+struct TreeParams {
+  int32_t depth;
+  int32_t branch[8];
+};
+
+int tree_nodes(const TreeParams &tp) {
+  int n = 0, level = 1;
+  for (int l = 0; l < tp.depth; ++l) {
+    level *= tp.branch[l];
+    n += level;
+  }
+  return n;
+}
+
+// the `b` largest logits (ties to the lower id), best first
+std::vector<int> top_b(const float *lg, int V, int b, double *margin) {
+  std::vector<int> idx(V);
+  for (int v = 0; v < V; ++v) idx[v] = v;
+  std::stable_sort(idx.begin(), idx.end(), [&](int x, int y) { return lg[x] > lg[y]; });
+  idx.resize(b);
+  if (margin && b < V) {
+    std::vector<float> srt(lg, lg + V);
+    std::sort(srt.begin(), srt.end(), std::greater<float>());
+    const double gap = static_cast<double>(srt[b - 1] - srt[b]) / std::max(1e-30, static_cast<double>(std::abs(srt[b - 1])));
+    *margin = std::min(*margin, gap);
+  }
+  return idx;
+}
+
+void tree_one(const Model &tgt, const Model &dft, const SpecParams &sp, const TreeParams &tp, const int64_t *prompt,
+              int S, int b, int64_t *out, int64_t *stats, double *margins) {
+  const int V = tgt.c.vocab;
+  const float T = sp.temperature;
+  const int L = tp.depth;
+  int bmax = 1;
+  for (int l = 0; l < L; ++l) bmax = std::max(bmax, tp.branch[l]);
+  const int nslots = L * bmax + 1;
+  Rng rng;
+  rng.mode = sp.rng_mode;
+  rng.gen.seed(sp.seed + static_cast<uint32_t>(b));
+  rng.slots = nslots;
+  rng.n_rounds = sp.n_rounds;
+  if (sp.rng_mode == 1) rng.table = sp.uniforms + static_cast<size_t>(b) * sp.n_rounds * nslots;
+
+  Cache tc, dc;
+  cache_init(tc, tgt, sp.cache_cap ? sp.cache_cap : tgt.c.max_seq_len, sp.num.kv_mode);
+  cache_init(dc, dft, sp.cache_cap ? sp.cache_cap : dft.c.max_seq_len, sp.num.kv_mode);
+  std::vector<int64_t> gen(prompt, prompt + S);
+  std::vector<float> tl, dl;
+  forward(tgt, sp.num, tc, prompt, S, tl);
+  forward(dft, sp.num, dc, prompt, S, dl);
+
+  double mg = 1e300;
+  auto tok_margin = [&](const float *lg) {
+    float a = -INFINITY, bb = -INFINITY;
+    for (int v = 0; v < V; ++v) {
+      if (lg[v] > a) { bb = a; a = lg[v]; }
+      else if (lg[v] > bb) bb = lg[v];
+    }
+    return static_cast<double>(a - bb) / std::max(1e-30, static_cast<double>(std::abs(a)));
+  };
+  auto note = [&](size_t idx) {
+    if (margins && idx < static_cast<size_t>(sp.max_new)) margins[idx] = mg;
+    mg = 1e300;
+  };
+  const float *last_row = &tl[static_cast<size_t>(S - 1) * V];
+  auto p0 = get_probs(last_row, V, T, sp.top_k, sp.top_p);
+  if (T <= 0.0f) mg = std::min(mg, tok_margin(last_row));
+  gen.push_back(sample(rng, p0, 0, L * bmax, T > 0 ? &mg : nullptr));
+  note(0);
+  int ngen = 1;
+  int64_t rounds = 0, drafted = 0, accepted_n = 0, rejections = 0;
+
+  // tree structure (BFS order): node j's parent and depth
+  const int N = tree_nodes(tp);
+  std::vector<int> parent(N), depth(N), first_child(N + 1, -1);
+  {
+    int base = 0, prev_base = -1, level = 1;
+    for (int l = 0; l < L; ++l) {
+      const int nl = level * tp.branch[l];
+      for (int i = 0; i < nl; ++i) {
+        parent[base + i] = l == 0 ? -1 : prev_base + i / tp.branch[l];
+        depth[base + i] = l + 1;
+      }
+      prev_base = base;
+      base += nl;
+      level = nl;
+    }
+  }
+  while (ngen < sp.max_new) {
+    const int round = static_cast<int>(++rounds);
+    const int Leff = std::min(L, sp.max_new - ngen);
+    const int64_t root = gen.back();
+    // draft expansion: caches after root + path, per node
+    std::vector<int64_t> tok(N);
+    std::vector<Cache> dcs(N + 1);  // [N] = after the root
+    dcs[N] = dc;
+    forward(dft, sp.num, dcs[N], &root, 1, dl);
+    std::vector<std::vector<float>> dlog(N + 1);
+    dlog[N] = dl;
+    int base = 0, level = 1;
+    for (int l = 0; l < L; ++l) {
+      const int nl = level * tp.branch[l];
+      for (int i = 0; i < nl; ++i) {
+        const int j = base + i;
+        const int par = parent[j] < 0 ? N : parent[j];
+        const int rank = i % tp.branch[l];
+        if (rank == 0) {
+          double m1 = 1e300;
+          auto kids = top_b(dlog[par].data(), V, tp.branch[l], &m1);
+          mg = std::min(mg, m1);
+          for (int r = 0; r < tp.branch[l]; ++r) tok[j + r] = kids[r];
+        }
+        if (l + 1 < L) {  // leaves are not fed to the draft
+          dcs[j] = dcs[par];
+          forward(dft, sp.num, dcs[j], &tok[j], 1, dl);
+          dlog[j] = dl;
+        }
+      }
+      base += nl;
+      level = nl;
+    }
+    drafted += N;
+    // target scores: root and every node
+    std::vector<std::vector<float>> tlog(N + 1);
+    std::vector<Cache> tcs(N + 1);
+    tcs[N] = tc;
+    forward(tgt, sp.num, tcs[N], &root, 1, tl);
+    tlog[N] = tl;
+    for (int j = 0; j < N; ++j) {
+      const int par = parent[j] < 0 ? N : parent[j];
+      tcs[j] = tcs[par];
+      forward(tgt, sp.num, tcs[j], &tok[j], 1, tl);
+      tlog[j] = tl;
+    }
+    tcs.clear();
+    dcs.clear();
+    // acceptance walk
+    int node = N, d = 0, child0 = 0, nb = tp.branch[0];  // root's children start at node 0
+    std::vector<int64_t> path;
+    bool rejected = false;
+    int out_tok = -1;
+    auto children_of = [&](int nd, int dd, int &c0, int &cnt) {
+      cnt = tp.branch[dd];
+      if (nd == N) { c0 = 0; return; }
+      // BFS: children of node nd (depth dd) start at level_base(dd+1) + (nd - level_base(dd)) * branch[dd]
+      int lb = 0, lv = 1, lb_next = 0;
+      for (int l = 0; l < dd; ++l) { lv *= tp.branch[l]; if (l + 1 < dd) lb += lv; }
+      lb_next = lb + lv;
+      c0 = lb_next + (nd - lb) * tp.branch[dd];
+    };
+    while (d < Leff) {
+      int c0, cnt;
+      children_of(node, d, c0, cnt);
+      (void)child0; (void)nb;
+      const float *lg = tlog[node].data();
+      int acc = -1;
+      if (T <= 0.0f) {
+        mg = std::min(mg, tok_margin(lg));
+        const int am = argmax_first(lg, V);
+        for (int r = 0; r < cnt; ++r)
+          if (tok[c0 + r] == am) { acc = c0 + r; break; }
+        if (acc < 0) out_tok = am;
+      } else {
+        auto p = get_probs(lg, V, T, sp.top_k, sp.top_p);
+        for (int r = 0; r < cnt && acc < 0; ++r) {
+          const int c = static_cast<int>(tok[c0 + r]);
+          const float u = accept_uniform(rng, round, d * bmax + r);
+          mg = std::min(mg, static_cast<double>(std::abs(u - p[c])));
+          if (u < p[c]) {
+            acc = c0 + r;
+          } else {
+            p[c] = 0.0f;
+            float s = 0.f;
+            for (int v = 0; v < V; ++v) s += p[v];
+            if (s > 0.f)
+              for (int v = 0; v < V; ++v) p[v] /= s;
+          }
+        }
+        if (acc < 0) out_tok = sample(rng, p, round, L * bmax, &mg);
+      }
+      if (acc < 0) {
+        rejected = true;
+        break;
+      }
+      path.push_back(tok[acc]);
+      gen.push_back(tok[acc]);
+      note(static_cast<size_t>(ngen));
+      ngen++;
+      accepted_n++;
+      node = acc;
+      d++;
+    }
+    if (rejected) {
+      rejections++;
+      gen.push_back(out_tok);
+      note(static_cast<size_t>(ngen));
+      ngen++;
+    } else if (ngen < sp.max_new) {
+      const float *lg = tlog[node].data();
+      int fin;
+      if (T <= 0.0f) {
+        mg = std::min(mg, tok_margin(lg));
+        fin = argmax_first(lg, V);
+      } else {
+        auto p = get_probs(lg, V, T, sp.top_k, sp.top_p);
+        fin = sample(rng, p, round, L * bmax, &mg);
+      }
+      gen.push_back(fin);
+      note(static_cast<size_t>(ngen));
+      ngen++;
+    }
+    // commit root + accepted path to both caches
+    std::vector<int64_t> commit(1, root);
+    commit.insert(commit.end(), path.begin(), path.end());
+    forward(tgt, sp.num, tc, commit.data(), static_cast<int>(commit.size()), tl);
+    forward(dft, sp.num, dc, commit.data(), static_cast<int>(commit.size()), dl);
+  }
+  std::copy(gen.begin(), gen.end(), out);
+  if (stats) {
+    stats[0] = rounds;
+    stats[1] = drafted;
+    stats[2] = accepted_n;
+    stats[3] = rejections;
+  }
+}
+
 template <class F> int guard(F &&f) {
   try {
     f();
@@ -810,6 +1051,39 @@ int oc_generate_speculative(void *tgt, void *dft, const SpecParams *sp, const in
     auto work = [&](int b) {
       try {
         spec_one(*t, *d, *sp, prompts + static_cast<size_t>(b) * S, S, b, out + b * row,
+                 stats ? stats + 4 * b : nullptr, margins ? margins + static_cast<size_t>(b) * sp->max_new : nullptr);
+      } catch (const std::exception &e) {
+        errs[b] = e.what();
+      }
+    };
+    int nt = n_threads > 0 ? n_threads : static_cast<int>(std::thread::hardware_concurrency());
+    nt = std::max(1, std::min(nt, B));
+    std::vector<std::thread> th;
+    for (int w = 0; w < nt; ++w)
+      th.emplace_back([&, w] {
+        for (int b = w; b < B; b += nt) work(b);
+      });
+    for (auto &x : th) x.join();
+    for (auto &e : errs)
+      if (!e.empty()) throw std::runtime_error(e);
+  });
+}
+
+// Tree speculation for B requests (tree_one), threads over requests.
+int oc_generate_tree(void *tgt, void *dft, const SpecParams *sp, const TreeParams *tp, const int64_t *prompts, int B,
+                     int S, int64_t *out, int64_t *stats, double *margins, int n_threads) {
+  return guard([&] {
+    auto *t = static_cast<Model *>(tgt);
+    auto *d = static_cast<Model *>(dft);
+    if (t->c.vocab != d->c.vocab) throw std::runtime_error("target and draft vocab differ");
+    if (tp->depth < 1 || tp->depth > 8) throw std::runtime_error("tree depth must be 1..8");
+    for (int l = 0; l < tp->depth; ++l)
+      if (tp->branch[l] < 1 || tp->branch[l] > t->c.vocab) throw std::runtime_error("bad tree branching");
+    const size_t row = static_cast<size_t>(S) + sp->max_new;
+    std::vector<std::string> errs(B);
+    auto work = [&](int b) {
+      try {
+        tree_one(*t, *d, *sp, *tp, prompts + static_cast<size_t>(b) * S, S, b, out + b * row,
                  stats ? stats + 4 * b : nullptr, margins ? margins + static_cast<size_t>(b) * sp->max_new : nullptr);
       } catch (const std::exception &e) {
         errs[b] = e.what();
