@@ -78,6 +78,7 @@ typedef struct specdec_config {
   int32_t max_batch;               /* concurrent requests per generate call */
   int32_t max_lookahead;           /* largest k */
   int32_t max_prompt_len;          /* longest prompt */
+  int32_t max_tree_nodes;          /* 0: no token trees; else the largest tree (<= 64 nodes) specdec_generate_tree accepts */
 } specdec_config;
 
 /* The arguments of generate_speculative (include/nn/layer.hpp:318-323) plus
@@ -163,6 +164,30 @@ int specdec_philox_uniforms(uint64_t seed, int B, int rounds, int slots,
 int specdec_forward_logits_noalloc(specdec_handle *h, int role,
                                    const int32_t *d_tokens, int S,
                                    float *d_logits, void *stream);
+
+/* Token tree of specdec_generate_tree: `depth` levels (1..8), every node at
+ * depth t < depth has branch[t] children (the draft's most likely next
+ * tokens); at most max_tree_nodes nodes in all (config 4: depth 4, branching
+ * 4, 3, 2, 1 = 64 nodes). */
+typedef struct specdec_tree {
+  int32_t depth;
+  int32_t branch[8];
+} specdec_tree;
+
+/* Tree speculation (no counterpart in the reference, which drafts one chain;
+ * this is generate_speculative with a token tree per round): the draft
+ * expands `tree` level by level, the target verifies all nodes in one pass
+ * with an ancestor mask, and acceptance walks the tree trying each node's
+ * children in order as point-mass proposals (greedy: the child equal to the
+ * target's argmax; sampled: child c with probability p(c), p renormalised
+ * without c after each rejection), which keeps the target's distribution.
+ * Same buffers and statuses as specdec_generate; `lookahead` and
+ * `draft_catchup` are not used; host-uniform tables have depth * max(branch)
+ * + 1 slots per round (slot t * max(branch) + r tests child r at depth t, the
+ * last slot draws the emitted token; round 0's last slot the first token).
+ * out_stats per request: rounds, tree nodes drafted, accepted, rejections. */
+int specdec_generate_tree(specdec_handle *h, const specdec_gen_params *p, const specdec_tree *tree,
+                          const int32_t *prompts, int B, int S, int32_t *out_tokens, int64_t *out_stats);
 
 /* Number of kernel launches the last generate call issued on the device. */
 int64_t specdec_last_launch_count(const specdec_handle *h);

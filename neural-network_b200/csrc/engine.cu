@@ -36,6 +36,7 @@
 #include "forward.cuh"
 #include "gemm.cuh"
 #include "sample.cuh"
+#include "tree.cuh"
 
 using namespace specdec;
 
@@ -62,6 +63,19 @@ struct Dims {
   int V, d, H, Hkv, D, F, L, max_seq, arch, kvd;
 };
 
+// A validated token tree: depth, branching, node counts per depth.
+struct TreeCfg {
+  int depth = 0;
+  int branch[kTreeMaxDepth] = {};
+  int lev[kTreeMaxDepth + 1] = {};  // lev[t]: nodes at depths 1 .. t
+  int N = 0, bmax = 1;
+  uint64_t sig() const {
+    uint64_t g = static_cast<uint64_t>(depth);
+    for (int l = 0; l < depth; ++l) g = g * 131 + static_cast<uint64_t>(branch[l]);
+    return g;
+  }
+};
+
 struct LayerW {
   void *wqkv = nullptr; float *sqkv = nullptr, *bqkv = nullptr;
   void *wo = nullptr; float *so = nullptr, *bo = nullptr;
@@ -84,10 +98,11 @@ struct GraphKey {
   uint32_t seed;
   int top_k;
   float top_p;
+  uint64_t tree_sig;  // 0: chain; else depth and branching
   bool operator<(const GraphKey &o) const {
-    return std::tie(B, S, k, greedy, rng_mode, catchup, max_new, u_rounds, T, seed, top_k, top_p) <
+    return std::tie(B, S, k, greedy, rng_mode, catchup, max_new, u_rounds, T, seed, top_k, top_p, tree_sig) <
            std::tie(o.B, o.S, o.k, o.greedy, o.rng_mode, o.catchup, o.max_new, o.u_rounds, o.T, o.seed, o.top_k,
-                    o.top_p);
+                    o.top_p, o.tree_sig);
   }
 };
 
@@ -187,6 +202,7 @@ struct specdec_handle {
   int *d_iters = nullptr;
   int *h_pinned = nullptr;
 
+  int max_tree = 0, tree_base = 0;  // token trees: largest tree, first pool row of the tree regions
   std::map<GraphKey, GraphEntry> graphs;
   int64_t launches = 0;        // direct mode: kernels enqueued by the last call; -1 in graph mode
   int64_t graph_fixed = 0, graph_body = 0, extra_launches = 0;
@@ -727,11 +743,17 @@ HeadInput head_input(specdec_handle *h, const ModelW &m) {
 //   head   LN2_last(H) -> logits
 // cfg arch (pre-LN): QKV reads LN1(X); OPROJ H = X + attn; FC1 GELU over
 // LN2(H) -> A; FC2 X = H + ffn; the head reads LN_final(X).
-void forward_rows(specdec_handle *h, bool target, int off, int R, int Q, const int *sel, int n_sel, float *logits) {
+void forward_rows(specdec_handle *h, bool target, int off, int R, int Q, const int *sel, int n_sel, float *logits,
+                  bool tree = false) {
   ModelW &m = target ? h->tgt : h->dft;
   const Dims &dm = m.dm;
   const int d = dm.d;
   RowsView rows{h->pool.tok + off, h->pool.pos + off, h->pool.req + off};
+  if (tree) {
+    rows.slot = h->pool.slot + off;
+    rows.tb = h->pool.tb + off;
+    rows.mask = h->pool.mask + off;
+  }
   void *kc = target ? h->tk : h->dk;
   void *vc = target ? h->tv : h->dv;
   const size_t lstride = target ? h->t_layer_stride : h->d_layer_stride;
@@ -807,12 +829,13 @@ namespace {
 
 void sync_check(specdec_handle *h) { CK(cudaStreamSynchronize(h->stream)); }
 
-void validate_gen(specdec_handle *h, const specdec_gen_params *p, int B, int S) {
+void validate_gen(specdec_handle *h, const specdec_gen_params *p, int B, int S, const TreeCfg *tree) {
   if (!p) fail(SPECDEC_ERR_INVALID, "null params");
   if (!h->tgt.loaded || !h->dft.loaded) fail(SPECDEC_ERR_STATE, "target and draft weights must be loaded first");
   if (B < 1 || B > h->cfg.max_batch) fail(SPECDEC_ERR_INVALID, "batch out of range");
   if (S < 1 || S > h->cfg.max_prompt_len) fail(SPECDEC_ERR_INVALID, "prompt length out of range");
-  if (p->lookahead < 1 || p->lookahead > h->cfg.max_lookahead) fail(SPECDEC_ERR_INVALID, "lookahead out of range");
+  if (!tree && (p->lookahead < 1 || p->lookahead > h->cfg.max_lookahead))
+    fail(SPECDEC_ERR_INVALID, "lookahead out of range");
   if (p->max_new_tokens < 0) fail(SPECDEC_ERR_INVALID, "max_new_tokens < 0");
   // The target cache ends at S + max_new positions (every round verifies
   // M = min(k, remaining) drafts); the reference throws when that exceeds
@@ -825,16 +848,78 @@ void validate_gen(specdec_handle *h, const specdec_gen_params *p, int B, int S) 
   } else if (p->rng_mode != SPECDEC_RNG_MT19937 && p->rng_mode != SPECDEC_RNG_HOST_UNIFORM) {
     fail(SPECDEC_ERR_INVALID, "unknown rng_mode");
   }
-  if (p->draft_catchup != SPECDEC_CATCHUP_REF && p->draft_catchup != SPECDEC_CATCHUP_CORRECT)
+  if (!tree && p->draft_catchup != SPECDEC_CATCHUP_REF && p->draft_catchup != SPECDEC_CATCHUP_CORRECT)
     fail(SPECDEC_ERR_INVALID, "unknown draft_catchup");
+}
+
+TreeCfg make_tree(const specdec_handle *h, const specdec_tree *t) {
+  if (!t) fail(SPECDEC_ERR_INVALID, "null tree");
+  if (h->max_tree == 0) fail(SPECDEC_ERR_STATE, "the handle was created with max_tree_nodes = 0");
+  if (t->depth < 1 || t->depth > kTreeMaxDepth) fail(SPECDEC_ERR_INVALID, "tree depth must be 1..8");
+  TreeCfg c;
+  c.depth = t->depth;
+  int level = 1;
+  for (int l = 0; l < t->depth; ++l) {
+    if (t->branch[l] < 1 || t->branch[l] > h->tgt.dm.V) fail(SPECDEC_ERR_INVALID, "tree branching out of range");
+    c.branch[l] = t->branch[l];
+    c.bmax = std::max(c.bmax, t->branch[l]);
+    level *= t->branch[l];
+    if (level > kTreeMaxNodes) fail(SPECDEC_ERR_INVALID, "tree too large");
+    c.lev[l + 1] = c.lev[l] + level;
+    if (c.lev[l + 1] > h->max_tree) fail(SPECDEC_ERR_INVALID, "tree has more nodes than max_tree_nodes");
+  }
+  c.N = c.lev[t->depth];
+  return c;
 }
 
 int samp_threads(const specdec_handle *h) { return h->tgt.dm.V <= 4096 ? 512 : kSampThreads; }
 size_t samp_smem(const specdec_handle *h) { return static_cast<size_t>(h->tgt.dm.V) * sizeof(float); }
 
 // Enqueues one full round (everything between two accept kernels).
+CacheView cache_view(specdec_handle *h, bool target) {
+  const ModelW &m = target ? h->tgt : h->dft;
+  CacheView c{};
+  c.k = target ? h->tk : h->dk;
+  c.v = target ? h->tv : h->dv;
+  c.ks = target ? h->tks : h->dks;
+  c.vs = target ? h->tvs : h->dvs;
+  c.layer_elems = target ? h->t_layer_stride : h->d_layer_stride;
+  c.req_stride = target ? h->t_req_stride : h->d_req_stride;
+  c.S_cap = target ? h->t_cap : h->d_cap;
+  c.Hkv = m.dm.Hkv;
+  c.D = m.dm.D;
+  c.L = m.dm.L;
+  c.elt = h->cfg.kv_dtype == SPECDEC_INT8 ? 1 : h->cfg.kv_dtype == SPECDEC_BF16 ? 2 : 4;
+  return c;
+}
+
+// One round of tree speculation (tree.cuh): draft levels 0 .. L-1, verify,
+// accept, compaction.
+void enqueue_tree_round(specdec_handle *h) {
+  SpecState &st = h->st;
+  const int B = st.B;
+  const dim3 sb(samp_threads(h));
+  const float *lg = h->logits;
+  forward_rows(h, false, st.rows.off_step0, 2 * B, 2, h->sel_odd, B, h->logits);
+  launch(h, tree_topk_kernel, dim3(B, 1), sb, samp_smem(h), st, 0, lg);
+  for (int t = 1; t < st.tL; ++t) {
+    const int n = st.tlev[t] - st.tlev[t - 1];
+    forward_rows(h, false, st.rows.off_tlevel[t], B * n, n, nullptr, B * n, h->logits, true);
+    launch(h, tree_topk_kernel, dim3(B, n), sb, samp_smem(h), st, t, lg);
+  }
+  const int W = st.tN + 1;
+  forward_rows(h, true, st.rows.off_tverify, B * W, W, nullptr, B * W, h->logits, true);
+  launch(h, tree_accept_kernel, dim3(B), sb, samp_smem(h), st, lg);
+  launch(h, tree_compact_kernel, dim3(B, h->tgt.dm.L + h->dft.dm.L), dim3(256), 0, st, cache_view(h, true),
+         cache_view(h, false));
+}
+
 void enqueue_round(specdec_handle *h) {
   SpecState &st = h->st;
+  if (st.tree) {
+    enqueue_tree_round(h);
+    return;
+  }
   const int B = st.B, k = st.k;
   const dim3 sb(samp_threads(h));
   forward_rows(h, false, st.rows.off_step0, 2 * B, 2, h->sel_odd, B, h->logits);
@@ -847,7 +932,7 @@ void enqueue_round(specdec_handle *h) {
   launch(h, accept_kernel, dim3(B), sb, samp_smem(h), st, static_cast<const float *>(h->logits));
 }
 
-void setup_state(specdec_handle *h, const specdec_gen_params *p, int B, int S) {
+void setup_state(specdec_handle *h, const specdec_gen_params *p, int B, int S, const TreeCfg *tree) {
   SpecState &st = h->st;
   st.B = B;
   st.k = p->lookahead;
@@ -872,6 +957,21 @@ void setup_state(specdec_handle *h, const specdec_gen_params *p, int B, int S) {
   st.rows.off_step0 = h->R_max;
   st.rows.off_step1 = h->R_max + 2 * B;
   st.rows.off_verify = h->R_max + 2 * B + (st.kmax - 1) * B;
+  st.tree = tree ? 1 : 0;
+  if (tree) {
+    st.k = 1;  // the chain rows are cleared with one draft step; a tree round does not use k
+    st.catchup = SPECDEC_CATCHUP_CORRECT;
+    st.tL = tree->depth;
+    st.tN = tree->N;
+    st.tbmax = tree->bmax;
+    for (int l = 0; l < kTreeMaxDepth; ++l) st.tbr[l] = tree->branch[l];
+    for (int l = 0; l <= kTreeMaxDepth; ++l) st.tlev[l] = tree->lev[l];
+    st.u_slots = tree->depth * tree->bmax + 1;
+    // tree regions: levels 1 .. L-1 (B * nodes at that depth each), then the
+    // verify block (B * (N + 1))
+    for (int t = 1; t < tree->depth; ++t) st.rows.off_tlevel[t] = h->tree_base + B * tree->lev[t - 1];
+    st.rows.off_tverify = h->tree_base + B * h->max_tree;
+  }
 }
 
 // Everything up to and including the first token (src/nn/layer.cpp:1396-1512).
@@ -958,16 +1058,16 @@ GraphEntry build_graph(specdec_handle *h, int B, int S, uint32_t seed, int max_i
 // d_prompts may be any device buffer; it is staged into the handle's prompt
 // buffer so captured graphs stay valid across calls.
 int generate_impl(specdec_handle *h, const specdec_gen_params *p, const int32_t *d_prompts, int B, int S, int32_t *d_out,
-                  int64_t *d_stats_out) {
-  validate_gen(h, p, B, S);
+                  int64_t *d_stats_out, const TreeCfg *tree = nullptr) {
+  validate_gen(h, p, B, S, tree);
   SpecState &st = h->st;
-  setup_state(h, p, B, S);
+  setup_state(h, p, B, S, tree);
   if (d_prompts != h->d_prompts)
     CK(cudaMemcpyAsync(h->d_prompts, d_prompts, static_cast<size_t>(B) * S * sizeof(int), cudaMemcpyDeviceToDevice,
                        h->stream));
   const bool table = p->rng_mode == SPECDEC_RNG_HOST_UNIFORM && p->temperature > 0.f;
   if (table) {
-    const size_t n = static_cast<size_t>(B) * p->uniform_rounds * (2 * p->lookahead + 1);
+    const size_t n = static_cast<size_t>(B) * p->uniform_rounds * st.u_slots;
     if (n > h->uniforms_cap) {
       destroy_graphs(h);
       if (h->d_uniforms) cudaFree(h->d_uniforms);
@@ -987,7 +1087,7 @@ int generate_impl(specdec_handle *h, const specdec_gen_params *p, const int32_t 
   if (h->use_graph) {
     GraphKey key{B, S, p->lookahead, st.greedy, table ? 1 : 0, p->draft_catchup, p->max_new_tokens,
                  table ? p->uniform_rounds : 0, p->temperature, (!st.greedy && !table) ? p->seed : 0u,
-                 st.greedy ? 0 : p->top_k, st.greedy ? 1.f : p->top_p};
+                 st.greedy ? 0 : p->top_k, st.greedy ? 1.f : p->top_p, tree ? tree->sig() : 0ull};
     auto it = h->graphs.find(key);
     if (it == h->graphs.end()) it = h->graphs.emplace(key, build_graph(h, B, S, p->seed, max_iters)).first;
     CK(cudaGraphLaunch(it->second.exec, h->stream));
@@ -1111,7 +1211,10 @@ int specdec_create(const specdec_config *cfg, int device, specdec_handle **out) 
       CK(cudaMemcpy(h->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
     }
     // activations
-    const int R_round = std::max(B * (k + 1), 2 * B);
+    if (cfg->max_tree_nodes < 0 || cfg->max_tree_nodes > kTreeMaxNodes)
+      fail(SPECDEC_ERR_INVALID, "max_tree_nodes must be 0..64");
+    h->max_tree = cfg->max_tree_nodes;
+    const int R_round = std::max(std::max(B * (k + 1), 2 * B), h->max_tree ? B * (h->max_tree + 1) : 0);
     h->R_max = std::max(R_round, std::min(B * cfg->max_prompt_len, std::max(8192, R_round)));
     h->act_elt = act_bf16(h.get()) ? 2 : 4;
     const int dmax = std::max(td.d, dd.d), Fmax = std::max(td.F, dd.F);
@@ -1126,15 +1229,23 @@ int specdec_create(const specdec_config *cfg, int device, specdec_handle **out) 
       h->KVN = static_cast<float *>(
           h->dalloc(static_cast<size_t>(h->R_max) * 2 * std::max(td.kvd, dd.kvd) * sizeof(float)));
     h->logits = static_cast<float *>(h->dalloc(static_cast<size_t>(R_round) * td.V * sizeof(float)));
-    const size_t pool_rows =
-        static_cast<size_t>(h->R_max) + 2 * B + static_cast<size_t>(k - 1) * B + static_cast<size_t>(B) * (k + 1);
+    h->tree_base =
+        h->R_max + 2 * B + (k - 1) * B + B * (k + 1);
+    const size_t pool_rows = static_cast<size_t>(h->tree_base) +
+                             (h->max_tree ? static_cast<size_t>(B) * h->max_tree + static_cast<size_t>(B) * (h->max_tree + 1) : 0);
     auto ib = [&](size_t n) { return static_cast<int *>(h->dalloc(n * sizeof(int))); };
     h->pool.tok = ib(pool_rows);
     h->pool.pos = ib(pool_rows);
     h->pool.req = ib(pool_rows);
+    h->pool.slot = ib(pool_rows);
+    h->pool.tb = ib(pool_rows);
+    h->pool.mask = static_cast<unsigned long long *>(h->dalloc(pool_rows * sizeof(unsigned long long)));
     CK(cudaMemset(h->pool.tok, 0, pool_rows * sizeof(int)));
     CK(cudaMemset(h->pool.pos, 0, pool_rows * sizeof(int)));
     CK(cudaMemset(h->pool.req, 0xff, pool_rows * sizeof(int)));
+    CK(cudaMemset(h->pool.slot, 0, pool_rows * sizeof(int)));
+    CK(cudaMemset(h->pool.tb, 0x7f, pool_rows * sizeof(int)));
+    CK(cudaMemset(h->pool.mask, 0, pool_rows * sizeof(unsigned long long)));
     h->sel_odd = ib(B);
     h->sel_prefill = ib(B);
     fill_odd_kernel<<<(B + 127) / 128, 128, 0, h->stream>>>(h->sel_odd, B);
@@ -1150,6 +1261,10 @@ int specdec_create(const specdec_config *cfg, int device, specdec_handle **out) 
     st.stats = static_cast<long long *>(h->dalloc(static_cast<size_t>(B) * 4 * sizeof(long long)));
     st.mt = static_cast<uint32_t *>(h->dalloc(static_cast<size_t>(B) * kMtN * sizeof(uint32_t)));
     st.mt_idx = ib(B);
+    st.ttok = ib(static_cast<size_t>(B) * kTreeMaxNodes);
+    st.d_root = ib(B);
+    st.cp_t0 = ib(B); st.cp_d0 = ib(B); st.cp_n = ib(B); st.cp_dn = ib(B);
+    st.cp_path = ib(static_cast<size_t>(B) * kTreeMaxDepth);
     st.active_count = ib(1);
     st.err = ib(1);
     CK(cudaMemset(st.err, 0, sizeof(int)));
@@ -1324,8 +1439,30 @@ int specdec_generate_device(specdec_handle *h, const specdec_gen_params *p, cons
   }
 }
 
+namespace {
+int host_generate(specdec_handle *h, const specdec_gen_params *p, const specdec_tree *tr, const int32_t *prompts, int B,
+                  int S, int32_t *out_tokens, int64_t *out_stats);
+}
+
 int specdec_generate(specdec_handle *h, const specdec_gen_params *p, const int32_t *prompts, int B, int S,
                      int32_t *out_tokens, int64_t *out_stats) {
+  return host_generate(h, p, nullptr, prompts, B, S, out_tokens, out_stats);
+}
+
+int specdec_generate_tree(specdec_handle *h, const specdec_gen_params *p, const specdec_tree *tree,
+                          const int32_t *prompts, int B, int S, int32_t *out_tokens, int64_t *out_stats) {
+  if (!tree) {
+    if (h) h->err = "null tree";
+    return SPECDEC_ERR_INVALID;
+  }
+  return host_generate(h, p, tree, prompts, B, S, out_tokens, out_stats);
+}
+
+}  // extern "C"
+
+namespace {
+int host_generate(specdec_handle *h, const specdec_gen_params *p, const specdec_tree *tr, const int32_t *prompts, int B,
+                  int S, int32_t *out_tokens, int64_t *out_stats) {
   if (!h) return SPECDEC_ERR_INVALID;
   try {
     CK(cudaSetDevice(h->device));
@@ -1333,8 +1470,11 @@ int specdec_generate(specdec_handle *h, const specdec_gen_params *p, const int32
     if (!p) fail(SPECDEC_ERR_INVALID, "null params");
     if (B < 1 || B > h->cfg.max_batch || S < 1 || S > h->cfg.max_prompt_len)
       fail(SPECDEC_ERR_INVALID, "batch or prompt length out of range");
+    TreeCfg tc;
+    if (tr) tc = make_tree(h, tr);
     CK(cudaMemcpyAsync(h->d_prompts, prompts, static_cast<size_t>(B) * S * sizeof(int), cudaMemcpyHostToDevice, h->stream));
-    int rc = generate_impl(h, p, h->d_prompts, B, S, h->d_out, reinterpret_cast<int64_t *>(h->d_stats));
+    int rc = generate_impl(h, p, h->d_prompts, B, S, h->d_out, reinterpret_cast<int64_t *>(h->d_stats),
+                           tr ? &tc : nullptr);
     if (rc != SPECDEC_OK) return rc;
     const int n = S + std::max(1, p->max_new_tokens);
     CK(cudaMemcpyAsync(out_tokens, h->d_out, static_cast<size_t>(B) * n * sizeof(int), cudaMemcpyDeviceToHost, h->stream));
@@ -1353,6 +1493,9 @@ int specdec_generate(specdec_handle *h, const specdec_gen_params *p, const int32
   }
   return SPECDEC_OK;
 }
+}  // namespace
+
+extern "C" {
 
 int specdec_forward_logits(specdec_handle *h, int role, const int32_t *tokens, int S, float *logits) {
   if (!h) return SPECDEC_ERR_INVALID;

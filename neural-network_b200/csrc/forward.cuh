@@ -33,9 +33,16 @@ namespace specdec {
 
 struct RowsView {
   const int *tok;  // embedding row (clamped to [0, V) by whoever wrote the row)
-  const int *pos;
+  const int *pos;  // RoPE position
   const int *req;
+  // Token trees (all null otherwise): the cache row the row's K/V go to, and
+  // its visibility: cache rows <= slot that are below tb, or whose bit
+  // (row - tb) is set in mask (the row's ancestors and itself).
+  const int *slot;
+  const int *tb;
+  const unsigned long long *mask;
 };
+__device__ __forceinline__ int row_slot(const RowsView &rv, int r) { return rv.slot ? rv.slot[r] : rv.pos[r]; }
 
 // ---------------------------------------------------------------------------
 // Embedding gather (Embedding::forward -> CpuBackend::embedding,
@@ -213,7 +220,7 @@ struct EpiPre {
   float s0, s1, b0, b1;  // scale and bias
   float r0, r1;          // residual
   float c, sn;           // RoPE (cos, sin)
-  int req, pos;
+  int req, pos, slot;
 };
 
 template <typename AT, int EPI>
@@ -228,6 +235,7 @@ __device__ __forceinline__ void epilogue_prefetch(const LinearArgs &a, int r, in
   p.sn = 0.f;
   p.req = 0;
   p.pos = 0;
+  p.slot = 0;
   if constexpr (EPI == kEpiResid) {
     const AT *rs = static_cast<const AT *>(a.resid) + static_cast<size_t>(r) * a.ldr;
     p.r0 = to_f32(rs[n]);
@@ -237,6 +245,7 @@ __device__ __forceinline__ void epilogue_prefetch(const LinearArgs &a, int r, in
     const QKVArgs &q = a.qkv;
     p.req = a.rows.req[r];
     p.pos = a.rows.pos[r];
+    p.slot = row_slot(a.rows, r);
     if (p.req >= 0 && p.pos >= 0 && p.pos < q.rope_max_pos && n < q.d + q.kvd) {
       const int e = (n < q.d ? n : n - q.d) % q.D;
       const float2 cs = q.rope[static_cast<size_t>(p.pos) * (q.D / 2) + (e >> 1)];
@@ -279,8 +288,8 @@ __device__ __forceinline__ void linear_epilogue(const LinearArgs &a, int r, int 
   } else if constexpr (EPI == kEpiQKV) {
     if (p.req < 0) return;
     const QKVArgs &q = a.qkv;
-    const int pos = p.pos;
-    if (pos < 0 || pos >= q.S_cap || pos >= q.rope_max_pos) {
+    const int pos = p.pos, slot = p.slot;
+    if (pos < 0 || pos >= q.rope_max_pos || slot < 0 || slot >= q.S_cap) {
       if (q.err) atomicOr(q.err, kErrSeqLen);
       return;
     }
@@ -301,7 +310,7 @@ __device__ __forceinline__ void linear_epilogue(const LinearArgs &a, int r, int 
       const bool is_k = n < q.d + q.kvd;
       const int nn = is_k ? n - q.d : n - q.d - q.kvd;
       const int h = nn / q.D, e = nn % q.D;
-      const size_t off = static_cast<size_t>(p.req) * q.kv_req_stride + (static_cast<size_t>(h) * q.S_cap + pos) * q.D + e;
+      const size_t off = static_cast<size_t>(p.req) * q.kv_req_stride + (static_cast<size_t>(h) * q.S_cap + slot) * q.D + e;
       if (q.kv_mode == 2) {
         float *st = q.stage + static_cast<size_t>(r) * 2 * q.kvd + (is_k ? 0 : q.kvd) + nn;
         st[0] = v0;
@@ -511,8 +520,8 @@ __global__ void kv_quant_kernel(RowsView rows, int R, const float *__restrict__ 
                                 float *__restrict__ vs) {
   const int r = blockIdx.x;
   if (r >= R) return;
-  const int req = rows.req[r], pos = rows.pos[r];
-  if (req < 0 || pos < 0 || pos >= S_cap) return;  // the QKV pass flagged an out-of-range position
+  const int req = rows.req[r], pos = row_slot(rows, r);
+  if (req < 0 || pos < 0 || pos >= S_cap) return;  // the QKV pass flagged an out-of-range cache row
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   for (int t = warp; t < 2 * Hkv; t += nw) {
     const bool is_v = t >= Hkv;
@@ -727,7 +736,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
   __shared__ __align__(16) float s_acc[kAttnWarps][QT][D];  // [0] holds the CTA's merged P.V
   __shared__ float s_m[kAttnWarps][QT], s_l[kAttnWarps][QT];
   __shared__ float c_m[QT], c_l[QT];  // the CTA's merged max and sum
-  __shared__ int s_pos[QT], s_req[QT];
+  __shared__ int s_pos[QT], s_req[QT], s_tb[QT];  // s_pos: the query's cache row (visibility limit)
+  __shared__ unsigned long long s_mask[QT];
   __shared__ __align__(8) uint64_t bars[2];
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -767,7 +777,9 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
 #pragma unroll
     for (int i = 0; i < QT; ++i) {
       rr[i] = (i < nq) ? a.rows.req[rq0 + i] : -1;
-      pr[i] = (i < nq) ? a.rows.pos[rq0 + i] : -1;
+      pr[i] = (i < nq) ? row_slot(a.rows, rq0 + i) : -1;
+      s_tb[i] = (i < nq && a.rows.tb) ? a.rows.tb[rq0 + i] : 0x7fffffff;
+      s_mask[i] = (i < nq && a.rows.mask) ? a.rows.mask[rq0 + i] : 0ull;
     }
     int req = -1, maxpos = -1;
 #pragma unroll
@@ -808,12 +820,15 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
   const int row0 = (req * a.Hkv + hk) * a.S_cap;
 
   float m[QT], l[QT], acc[QT][EPL];
-  int qpos[QT];
+  int qpos[QT], qtb[QT];
+  unsigned long long qmask[QT];
 #pragma unroll
   for (int i = 0; i < QT; ++i) {
     m[i] = -INFINITY;
     l[i] = 0.f;
     qpos[i] = s_pos[i];
+    qtb[i] = s_tb[i];
+    qmask[i] = s_mask[i];
 #pragma unroll
     for (int e = 0; e < EPL; ++e) acc[i][e] = 0.f;
   }
@@ -878,7 +893,10 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
         // sqrt(D) is a power of two for D = 4, 16, 64: the product by its
         // reciprocal is then the correctly rounded quotient
         const float sv = kSqrtPow2 ? dd * kInvSqrt : __fdiv_rn(dd, scale);
-        sc[i] = (i < nq && r < nt && pos <= qpos[i]) ? sv : -INFINITY;
+        // causal, and inside a token tree only the prefix, the ancestors and itself
+        const bool vis = pos <= qpos[i] &&
+                         (pos < qtb[i] || (pos - qtb[i] < 64 && ((qmask[i] >> (pos - qtb[i])) & 1ull)));
+        sc[i] = (i < nq && r < nt && vis) ? sv : -INFINITY;
       }
     }
     // online softmax per warp: the warp's running max is shared by its lanes

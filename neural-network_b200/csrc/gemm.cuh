@@ -150,7 +150,7 @@ __device__ __forceinline__ void chunk_load(const LinearArgs &a, int row, int n, 
 // chunk's outputs stored as 16-byte vectors.
 template <int EPI>
 __device__ __forceinline__ void chunk_store(const LinearArgs &a, int row, int n, float (&v)[16], const ChunkOps &op,
-                                            const float *ssc, const float *sbi, int req, int pos) {
+                                            const float *ssc, const float *sbi, int req, int pos, int slot) {
   using AT = __nv_bfloat16;
 #pragma unroll
   for (int j = 0; j < 16; ++j) v[j] = v[j] * ssc[j] + sbi[j];
@@ -195,7 +195,7 @@ __device__ __forceinline__ void chunk_store(const LinearArgs &a, int row, int n,
   } else if constexpr (EPI == kEpiQKV) {
     if (req < 0) return;
     const QKVArgs &q = a.qkv;
-    if (pos < 0 || pos >= q.S_cap || pos >= q.rope_max_pos) {
+    if (pos < 0 || pos >= q.rope_max_pos || slot < 0 || slot >= q.S_cap) {
       if (q.err) atomicOr(q.err, kErrSeqLen);
       return;
     }
@@ -218,7 +218,7 @@ __device__ __forceinline__ void chunk_store(const LinearArgs &a, int row, int n,
       const bool is_k = n < q.d + q.kvd;
       const int nn = is_k ? n - q.d : n - q.d - q.kvd;
       const int h = nn / q.D, e = nn % q.D;
-      const size_t off = static_cast<size_t>(req) * q.kv_req_stride + (static_cast<size_t>(h) * q.S_cap + pos) * q.D + e;
+      const size_t off = static_cast<size_t>(req) * q.kv_req_stride + (static_cast<size_t>(h) * q.S_cap + slot) * q.D + e;
       if (q.kv_mode == 2) {
         float4 *st = reinterpret_cast<float4 *>(q.stage + static_cast<size_t>(row) * 2 * q.kvd + (is_k ? 0 : q.kvd) + nn);
 #pragma unroll
@@ -322,10 +322,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
   __syncthreads();  // the per-column scale and bias are in shared memory
   const int row = m0 + warp * 32 + lane;
   const bool row_ok = row < a.R;
-  int req = 0, pos = 0;
+  int req = 0, pos = 0, slot = 0;
   if constexpr (EPI == kEpiQKV) {
     req = row_ok ? a.rows.req[row] : -1;
     pos = row_ok ? a.rows.pos[row] : 0;
+    slot = row_ok ? row_slot(a.rows, row) : 0;
   }
   const int ncols = min(kBN, a.N - n0);
   if (ok) {
@@ -337,11 +338,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
       float v[16];
       if (row_ok && c + 16 < ncols) chunk_load<EPI>(a, row, n0 + c + 16, req, pos, op1);
       tmem_ld16(tbase + c, v);
-      if (row_ok) chunk_store<EPI>(a, row, n0 + c, v, op0, s_scale + c, s_bias + c, req, pos);
+      if (row_ok) chunk_store<EPI>(a, row, n0 + c, v, op0, s_scale + c, s_bias + c, req, pos, slot);
       if (c + 16 >= ncols) break;  // warp-uniform
       if (row_ok && c + 32 < ncols) chunk_load<EPI>(a, row, n0 + c + 32, req, pos, op0);
       tmem_ld16(tbase + c + 16, v);
-      if (row_ok) chunk_store<EPI>(a, row, n0 + c + 16, v, op1, s_scale + c + 16, s_bias + c + 16, req, pos);
+      if (row_ok) chunk_store<EPI>(a, row, n0 + c + 16, v, op1, s_scale + c + 16, s_bias + c + 16, req, pos, slot);
     }
   }
   tc_fence_before();

@@ -73,7 +73,15 @@ __device__ __forceinline__ float canon_f32(uint32_t g) {
 struct RowPool {
   int *tok, *pos, *req;
   int off_step0, off_step1, off_verify;  // region offsets (the prefill region is at 0)
+  // token trees: per-row cache slot, tree base and ancestor mask, and the
+  // regions of the tree levels 1 .. depth-1 (draft) and of the tree verify block
+  int *slot, *tb;
+  unsigned long long *mask;
+  int off_tlevel[9], off_tverify;
 };
+
+constexpr int kTreeMaxDepth = 8;
+constexpr int kTreeMaxNodes = 64;  // one bit per node in a row's ancestor mask
 
 struct SpecState {
   int *tokens_out;     // [B][out_len]
@@ -103,7 +111,37 @@ struct SpecState {
   int u_rounds, u_slots;
   int catchup;         // 0 reference, 1 consistent
   int t_cap, d_cap;
+  // token trees (tree = 1): depth, branching per level, node count, first node
+  // of each depth (tlev[t] = first node at depth t + 1, tlev[depth] = nodes),
+  // largest branching; per request the node tokens, the draft cache slot of
+  // the round's root and the accepted path handed to the compaction kernel
+  int tree, tL, tN, tbmax;
+  int tbr[kTreeMaxDepth], tlev[kTreeMaxDepth + 1];
+  int *ttok;           // [B][kTreeMaxNodes]
+  int *d_root;         // [B]
+  int *cp_t0, *cp_d0, *cp_n, *cp_dn;  // [B] root slots and path lengths of the last accept
+  int *cp_path;        // [B][kTreeMaxDepth] accepted node indices, root side first
 };
+
+// Tree structure (BFS order; the nodes at depth t >= 1 are tlev[t-1] .. tlev[t]-1).
+__device__ __forceinline__ int tree_depth_of(const SpecState &st, int j) {
+  int t = 1;
+  while (t < st.tL && j >= st.tlev[t]) ++t;
+  return t;
+}
+__device__ __forceinline__ int tree_parent(const SpecState &st, int j) {
+  const int t = tree_depth_of(st, j);
+  return t == 1 ? -1 : st.tlev[t - 2] + (j - st.tlev[t - 1]) / st.tbr[t - 1];
+}
+__device__ __forceinline__ unsigned long long tree_mask(const SpecState &st, int j) {
+  unsigned long long m = 0;
+  for (int x = j; x >= 0; x = tree_parent(st, x)) m |= 1ull << x;
+  return m;
+}
+// first child of node j (j < 0: the root) and its depth
+__device__ __forceinline__ int tree_first_child(const SpecState &st, int j, int depth) {
+  return j < 0 ? 0 : st.tlev[depth] + (j - st.tlev[depth - 1]) * st.tbr[depth];
+}
 
 __device__ __forceinline__ void set_row(const SpecState &st, int idx, int tok, int pos, int req) {
   st.rows.tok[idx] = (tok >= 0 && tok < st.V) ? tok : 0;  // an out-of-range id embeds as row 0
@@ -147,6 +185,52 @@ __device__ bool start_round(const SpecState &st, int b, int catch_tok) {
   set_row(st, st.rows.off_step0 + 2 * b + 1, st.last_tok[b], d, b);
   st.d_len[b] = d + 1;
   st.M[b] = M;
+  return true;
+}
+
+__device__ __forceinline__ void set_tree_row(const SpecState &st, int idx, int tok, int pos, int req, int slot, int tb,
+                                             unsigned long long mask) {
+  set_row(st, idx, tok, pos, req);
+  st.rows.slot[idx] = slot;
+  st.rows.tb[idx] = tb;
+  st.rows.mask[idx] = mask;
+}
+__device__ __forceinline__ int tree_verify_row(const SpecState &st, int b, int i) {
+  return st.rows.off_tverify + b * (st.tN + 1) + i;  // i = 0: the root, 1 + j: node j
+}
+__device__ __forceinline__ int tree_level_row(const SpecState &st, int b, int depth, int i) {
+  const int n = st.tlev[depth] - st.tlev[depth - 1];
+  return st.rows.off_tlevel[depth] + b * n + i;
+}
+__device__ void tree_clear_rows(const SpecState &st, int b) {
+  clear_row(st, st.rows.off_step0 + 2 * b);
+  clear_row(st, st.rows.off_step0 + 2 * b + 1);
+  for (int t = 1; t < st.tL; ++t)
+    for (int i = 0; i < st.tlev[t] - st.tlev[t - 1]; ++i) clear_row(st, tree_level_row(st, b, t, i));
+  for (int i = 0; i <= st.tN; ++i) clear_row(st, tree_verify_row(st, b, i));
+}
+
+// Rows of a tree round's first draft pass, [catch-up (if any), root], and the
+// root row of the verify block; the tree's rows follow as the draft expands.
+// Returns false (and flags the error) when the tree would not fit a cache.
+__device__ bool tree_start_round(const SpecState &st, int b, int catch_tok) {
+  int d = st.d_len[b];
+  const int t = st.t_len[b];
+  const int has_c = catch_tok >= 0 ? 1 : 0;
+  const int draft_nodes = st.tL > 1 ? st.tlev[st.tL - 1] : 0;  // leaves are not fed to the draft
+  if (d + has_c + 1 + draft_nodes > st.d_cap || t + 1 + st.tN > st.t_cap) {
+    atomicOr(st.err, kErrSeqLen);
+    st.active[b] = 0;
+    tree_clear_rows(st, b);
+    return false;
+  }
+  if (has_c) set_row(st, st.rows.off_step0 + 2 * b, catch_tok, d++, b);
+  else clear_row(st, st.rows.off_step0 + 2 * b);
+  set_row(st, st.rows.off_step0 + 2 * b + 1, st.last_tok[b], d, b);
+  st.d_root[b] = d;
+  st.d_len[b] = d + 1;
+  st.t_start[b] = t;
+  set_tree_row(st, tree_verify_row(st, b, 0), st.last_tok[b], t, b, t, t + 1, 0ull);
   return true;
 }
 
@@ -513,6 +597,7 @@ __global__ void init_state_kernel(SpecState st, const int *__restrict__ prompts,
     for (int i = 0; i < 4; ++i) st.stats[4 * b + i] = 0;
     if (S > st.t_cap || S > st.d_cap) atomicOr(st.err, kErrSeqLen);
     clear_request_rows(st, b);
+    if (st.tree) tree_clear_rows(st, b);
   }
 }
 
@@ -544,7 +629,7 @@ __global__ void __launch_bounds__(kSampThreads) first_token_kernel(SpecState st,
   } else {
     rng_prepare(st, b, 2, rc);
     probs_smem(srow, st.V, st.T, st.top_k, st.top_p, sh.red, sh.cut);
-    if (threadIdx.x == 0) sh.u = draw_sample_u(st, b, 0, 2 * st.k, rc);
+    if (threadIdx.x == 0) sh.u = draw_sample_u(st, b, 0, st.u_slots - 1, rc);
     __syncthreads();
     tok = sample_smem(srow, st.V, sh.u, st.rng_mode, sh.redd, sh.redi);
     rng_commit(st, b, rc);
@@ -553,9 +638,9 @@ __global__ void __launch_bounds__(kSampThreads) first_token_kernel(SpecState st,
     emit(st, b, tok);
     st.last_tok[b] = tok;
     st.round[b] = 1;
-    const bool more = st.n_new[b] < st.max_new;
+    bool more = st.n_new[b] < st.max_new;
+    if (more) more = st.tree ? tree_start_round(st, b, -1) : start_round(st, b, -1);
     st.active[b] = more ? 1 : 0;
-    if (more) start_round(st, b, -1);
   }
 }
 

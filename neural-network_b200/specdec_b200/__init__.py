@@ -35,7 +35,7 @@ STATUS = {0: "OK", 1: "ERR_INVALID", 2: "ERR_CUDA", 3: "ERR_OOM", 4: "ERR_SEQ_LE
 EXPORTS = ("specdec_create", "specdec_destroy", "specdec_last_error", "specdec_load_params",
            "specdec_generate", "specdec_generate_device", "specdec_stream", "specdec_forward_logits",
            "specdec_philox_uniforms", "specdec_last_launch_count", "specdec_forward_logits_noalloc",
-           "specdec_time_linear")
+           "specdec_time_linear", "specdec_generate_tree")
 
 # linear layers of specdec_time_linear
 LIN_QKV, LIN_OPROJ, LIN_FFN_IN, LIN_FFN_OUT, LIN_HEAD = 0, 1, 2, 3, 4
@@ -56,7 +56,12 @@ class _ModelConfig(C.Structure):
 class _Config(C.Structure):
     _fields_ = [("target", _ModelConfig), ("draft", _ModelConfig), ("draft_shares_target", C.c_int32),
                 ("weight_dtype", C.c_int32), ("act_dtype", C.c_int32), ("kv_dtype", C.c_int32),
-                ("max_batch", C.c_int32), ("max_lookahead", C.c_int32), ("max_prompt_len", C.c_int32)]
+                ("max_batch", C.c_int32), ("max_lookahead", C.c_int32), ("max_prompt_len", C.c_int32),
+                ("max_tree_nodes", C.c_int32)]
+
+
+class _Tree(C.Structure):
+    _fields_ = [("depth", C.c_int32), ("branch", C.c_int32 * 8)]
 
 
 class _GenParams(C.Structure):
@@ -94,6 +99,8 @@ def load_library(path: str = LIB_PATH):
                                                    C.c_void_p]
     lib.specdec_last_launch_count.restype = C.c_int64
     lib.specdec_last_launch_count.argtypes = [C.c_void_p]
+    lib.specdec_generate_tree.argtypes = [C.c_void_p, C.POINTER(_GenParams), C.POINTER(_Tree), C.c_void_p, C.c_int,
+                                          C.c_int, C.c_void_p, C.c_void_p]
     lib.specdec_time_linear.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                         C.c_size_t, C.POINTER(C.c_float), C.POINTER(C.c_double)]
     _lib = lib
@@ -118,14 +125,14 @@ class Engine:
 
     def __init__(self, target: ModelShape, draft_layers: Optional[int] = None, draft: Optional[ModelShape] = None,
                  weight_dtype: int = F32, act_dtype: int = F32, kv_dtype: int = F32, max_batch: int = 1,
-                 max_lookahead: int = 4, max_prompt_len: int = 128, device: int = 0):
+                 max_lookahead: int = 4, max_prompt_len: int = 128, device: int = 0, max_tree_nodes: int = 0):
         lib = load_library()
         shares = draft is None
         if shares and draft_layers is None:
             raise ValueError("give draft_layers (shared draft) or a draft shape")
         dshape = target.with_layers(draft_layers) if shares else draft
         cfg = _Config(_mcfg(target), _mcfg(dshape), 1 if shares else 0, weight_dtype, act_dtype, kv_dtype,
-                      max_batch, max_lookahead, max_prompt_len)
+                      max_batch, max_lookahead, max_prompt_len, max_tree_nodes)
         h = C.c_void_p()
         rc = lib.specdec_create(C.byref(cfg), device, C.byref(h))
         if rc:
@@ -176,6 +183,24 @@ class Engine:
         stats = np.zeros((B, 4), np.int64)
         self._check(self._lib.specdec_generate(self.h, C.byref(prm), p.ctypes.data, B, S, out.ctypes.data,
                                                stats.ctypes.data))
+        del keep
+        return out.astype(np.int64), stats
+
+    def generate_tree(self, prompts, max_new_tokens: int, branching, temperature: float = 1.0, top_k: int = 0,
+                      top_p: float = 1.0, seed: int = 42,
+                      uniforms: Optional[np.ndarray] = None) -> Tuple[np.ndarray, np.ndarray]:
+        """Tree speculation (specdec_generate_tree): branching = children per level,
+        e.g. (4, 3, 2, 1).  Host uniforms: [B][rounds][depth * max(branching) + 1].
+        Returns (tokens [B, S + max(1, max_new)], stats [B, 4])."""
+        p = np.ascontiguousarray(np.atleast_2d(prompts), np.int32)
+        B, S = p.shape
+        prm, keep = self._params(max_new_tokens, 1, temperature, top_k, top_p, seed, uniforms, CATCHUP_CORRECT)
+        br = list(branching)
+        tree = _Tree(len(br), (C.c_int32 * 8)(*br))
+        out = np.zeros((B, S + max(1, max_new_tokens)), np.int32)
+        stats = np.zeros((B, 4), np.int64)
+        self._check(self._lib.specdec_generate_tree(self.h, C.byref(prm), C.byref(tree), p.ctypes.data, B, S,
+                                                    out.ctypes.data, stats.ctypes.data))
         del keep
         return out.astype(np.int64), stats
 

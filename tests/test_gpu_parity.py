@@ -7,6 +7,7 @@ except at logged near-ties (helpers.compare_tokens)."""
 import numpy as np
 import pytest
 
+import oracle
 import specdec_b200 as sd
 from helpers import BF16_GREEDY_GAP, compare_tokens, make_pair, run_both
 from specdec_b200.synth import ARCH_CFG, ModelShape, make_prompts
@@ -183,3 +184,56 @@ def test_greedy_spec_bf16_gemm(gpu_lib, oracle_built):
     _, tg, sg, to, so, mg = run_both(pair, 16, 80, 24, 4, 0.0)
     exact, ties = compare_tokens(tg, to, mg, 80, greedy=True, tol=BF16_GREEDY_GAP)
     assert exact + ties == 16 and ties <= 4
+
+
+# Token trees (tree.cuh) against the oracle's path-by-path restatement
+# (oracle/specdec_oracle.cpp: tree_one): greedy and both uniform sources.
+def _tree_pair(name, seed, **kw):
+    shape, dl = SHAPES[name]
+    return make_pair(shape, dl, seed=seed, max_batch=4, max_prompt_len=40, **kw)
+
+
+def _tree_both(pair, B, S, max_new, br, T, seed=9, use_uniforms=False, top_k=0, top_p=1.0):
+    prompts = make_prompts(B, S, pair.shape.vocab, seed=4)
+    uni = sd.philox_uniforms(seed, B, max_new + 2, oracle.tree_slots(br)) if use_uniforms else None
+    tg, sg = pair.engine.generate_tree(prompts, max_new, br, T, top_k, top_p, seed, uniforms=uni)
+    to, so, mg = oracle.oracle_generate_tree(pair.target, pair.draft, prompts, max_new, br, T, top_k, top_p, seed,
+                                             uniforms=uni, act_bf16=pair.act_bf16, kv_mode=pair.kv_mode,
+                                             cache_cap=pair.shape.max_seq_len)
+    return tg, sg, to, so, mg
+
+
+@pytest.mark.parametrize("name", ["small", "cfg1"])
+@pytest.mark.parametrize("br", [(4, 3, 2, 1), (2, 2), (1, 1, 1, 1)])
+def test_tree_greedy(gpu_lib, name, br):
+    pair = _tree_pair(name, 41, max_tree_nodes=64)
+    tg, sg, to, so, mg = _tree_both(pair, 3, 10, 30, list(br), 0.0)
+    exact, ties = compare_tokens(tg, to, mg, 10, greedy=True)
+    assert exact + ties == 3 and ties <= 1
+    if ties == 0:
+        assert np.array_equal(sg, so)
+
+
+@pytest.mark.parametrize("name", ["small", "cfg1"])
+@pytest.mark.parametrize("use_uniforms", [False, True])
+def test_tree_sampled(gpu_lib, name, use_uniforms):
+    pair = _tree_pair(name, 42, max_tree_nodes=64)
+    tg, sg, to, so, mg = _tree_both(pair, 3, 10, 30, [4, 3, 2, 1], 1.0, use_uniforms=use_uniforms)
+    exact, ties = compare_tokens(tg, to, mg, 10, greedy=False)
+    assert exact + ties == 3 and ties <= 1
+
+
+def test_tree_int8_kv_and_weights(gpu_lib):
+    pair = _tree_pair("cfg1", 43, max_tree_nodes=64, int8=True, kv_mode=2)
+    tg, sg, to, so, mg = _tree_both(pair, 2, 10, 24, [3, 2, 1], 1.0, use_uniforms=True)
+    exact, ties = compare_tokens(tg, to, mg, 10, greedy=False)
+    assert exact + ties == 2 and ties <= 1
+
+
+def test_tree_chain_equivalence_gpu(gpu_lib):
+    # a 1/1/1/1 tree is the k = 4 chain (greedy, consistent catch-up)
+    pair = _tree_pair("cfg1", 44, max_tree_nodes=64)
+    prompts = make_prompts(3, 12, pair.shape.vocab, seed=5)
+    tt, st = pair.engine.generate_tree(prompts, 40, [1, 1, 1, 1], 0.0)
+    tc, sc = pair.engine.generate_speculative(prompts, 40, 4, 0.0, draft_catchup=sd.CATCHUP_CORRECT)
+    assert np.array_equal(tt, tc)
