@@ -52,6 +52,38 @@ def peaks():
     return 6650.0, "fallback"
 
 
+def bf16_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f).get("bf16_tflops", 1590.0))
+    return 1590.0
+
+
+def tree_nodes(branching) -> int:
+    n, level = 0, 1
+    for b in branching:
+        level *= b
+        n += level
+    return n
+
+
+KV_DTYPE = {0: 0, 1: 1, 2: 2}  # workload kv_mode -> SPECDEC_F32 / BF16 / INT8
+
+
+def roofline_entry(p, hbm, tflops, wl, rows):
+    """The FFN down-projection at the verify row count: HBM-bound below the
+    bf16 ridge (peak flops / peak bytes), tensor-bound above it."""
+    ridge = tflops * 1e12 / (hbm * 1e9)
+    what = "tcgen05 GEMM" if (wl.act_bf16 and rows >= 64) else "linear_kernel GEMV"
+    kern = f"{what}, residual epilogue (target FFN down-projection, {rows} verify rows)"
+    if p["flops_per_byte"] > ridge:
+        return {"bound": "tensor", "achieved": p["TFLOPs"], "peak": tflops, "unit": "TFLOP/s",
+                "frac": p["TFLOPs"] / tflops, "traffic": None, "kernel": kern}
+    return {"bound": "hbm", "achieved": p["GBps"], "peak": hbm, "unit": "GB/s", "frac": p["GBps"] / hbm,
+            "traffic": None, "kernel": kern}
+
+
 def dist_env():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -155,7 +187,7 @@ def reference_arm(args, wl, rank, world):
     ncores = os.cpu_count() or 1
     P = make_params(wl.target, seed=0)
     DP = draft_params(wl.target, P, wl.draft_layers)
-    new_per_step = 32
+    new_per_step = 32 if wl.name == "int8" else 8
     prompts = make_prompts(wl.batch, wl.prompt_len, wl.target.vocab, seed=1)
     if kind == "reference":
         # int8 target: the reference multiplies by the dequantised weight q*s
@@ -201,12 +233,14 @@ def reference_arm(args, wl, rank, world):
 
 
 def config_dict(wl, args):
-    return {"workload": f"{wl.name} (BASELINE configs[1])", "arch": args.arch,
+    idx = {"int8": 1, "medium": 2, "tree": 3}.get(wl.name, 1)
+    return {"workload": f"{wl.name} (BASELINE configs[{idx}])", "arch": args.arch,
             "model": f"L{wl.target.n_layers} d{wl.target.d_model} H{wl.target.n_heads} F{wl.target.d_ff} V{wl.target.vocab}",
             "draft": f"first {wl.draft_layers} layer(s) + shared head", "batch_per_gpu": wl.batch,
             "global_batch": wl.batch * args.gpus, "prompt_len": wl.prompt_len, "max_new": wl.max_new,
             "lookahead": wl.lookahead, "temperature": wl.temperature, "weights": "int8" if wl.weights_int8 else "f32",
-            "act": "bf16" if wl.act_bf16 else "f32", "kv": "f32", "rng": "philox host uniforms",
+            "act": "bf16" if wl.act_bf16 else "f32", "kv": ["f32", "bf16", "int8"][wl.kv_mode],
+            "rng": "philox host uniforms", "tree": list(wl.tree) if wl.tree else None,
             "parallelism": f"request-parallel x{args.gpus}", "l2": "flushed between timed steps (256 MiB write)"}
 
 
@@ -217,9 +251,11 @@ def cpu_baseline_sample(wl):
 
     kind = "reference" if oracle.reference_available() else "port"
     P = make_params(wl.target, seed=0)
-    prompts = make_prompts(2, wl.prompt_len, wl.target.vocab, seed=1)
+    small = wl.name == "int8"
+    nreq = 2 if small else 1
+    prompts = make_prompts(nreq, wl.prompt_len, wl.target.vocab, seed=1)
     om = oracle.Oracle(wl.target, P, int8=wl.weights_int8)
-    new = 64
+    new = 64 if small else 8
     t0 = time.perf_counter()
     toks = 0
     if kind == "reference":
@@ -227,7 +263,7 @@ def cpu_baseline_sample(wl):
         tgt = oracle.Reference(wl.target, Pq, requires_grad=False)
         dft = oracle.Reference(wl.target.with_layers(wl.draft_layers), draft_params(wl.target, Pq, wl.draft_layers),
                                requires_grad=False)
-        for b in range(2):
+        for b in range(nreq):
             toks += len(tgt.generate_speculative(dft, prompts[b], new, wl.lookahead, wl.temperature, 0, 1.0, 7 + b)) - wl.prompt_len
     else:
         dft = oracle.Oracle(wl.target.with_layers(wl.draft_layers), draft_params(wl.target, P, wl.draft_layers),
@@ -236,8 +272,10 @@ def cpu_baseline_sample(wl):
                                                        n_threads=1)
         toks = out.size - prompts.size
     dt = time.perf_counter() - t0
+    what = "k = 4 chain speculation (the reference has no token trees), " if wl.tree else ""
     return {"value": toks / dt, "unit": UNIT, "cores": os.cpu_count() if kind == "reference" else 1, "kind": kind,
-            "sample": f"2 requests x {new} new tokens of the same workload, batch 1 each (the reference is batch-1)"}
+            "sample": f"{what}{nreq} request(s) x {new} new tokens of the same models and prompts, batch 1 each "
+                      "(the reference is batch-1)"}
 
 
 def main():
@@ -248,10 +286,13 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--arch", default="ref", choices=["ref", "cfg"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="int8", choices=["int8", "medium", "tree"],
+                    help="int8 = BASELINE configs[1] (the metric's config, default); medium = configs[2]; "
+                         "tree = configs[3]")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     rank, world, local = dist_env()
-    wl = workload("int8", ARCH_CFG if args.arch == "cfg" else ARCH_REF)
+    wl = workload(args.workload, ARCH_CFG if args.arch == "cfg" else ARCH_REF)
     if args.impl == "reference":
         return reference_arm(args, wl, rank, world)
 
@@ -268,14 +309,16 @@ def main():
                                 device_id=torch.device("cuda", local))
     P = make_params(wl.target, seed=0)
     eng = sd.Engine(wl.target, draft_layers=wl.draft_layers, weight_dtype=sd.INT8 if wl.weights_int8 else sd.F32,
-                    act_dtype=sd.BF16 if wl.act_bf16 else sd.F32, max_batch=wl.batch,
-                    max_lookahead=wl.lookahead, max_prompt_len=wl.prompt_len, device=local)
+                    act_dtype=sd.BF16 if wl.act_bf16 else sd.F32, kv_dtype=KV_DTYPE[wl.kv_mode],
+                    max_batch=wl.batch, max_lookahead=wl.lookahead, max_prompt_len=wl.prompt_len, device=local,
+                    max_tree_nodes=tree_nodes(wl.tree) if wl.tree else 0)
     eng.load_params(sd.TARGET, P)
     B, S = wl.batch, wl.prompt_len
     # request partition: rank r serves requests [r*B, (r+1)*B) of the global set
     prompts = shard(make_prompts(B * world, S, wl.target.vocab, seed=1), B, rank, world)
     n_rounds = wl.max_new + 2
-    uni = shard(sd.philox_uniforms(1234, B * world, n_rounds, 2 * wl.lookahead + 1), B, rank, world)
+    slots = (len(wl.tree) * max(wl.tree) + 1) if wl.tree else 2 * wl.lookahead + 1
+    uni = shard(sd.philox_uniforms(1234, B * world, n_rounds, slots), B, rank, world)
 
     dev = torch.device("cuda", local)
     d_prompts = torch.from_numpy(prompts.astype(np.int32)).to(dev)
@@ -286,8 +329,12 @@ def main():
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
 
     def step():
-        eng.generate_device(d_prompts.data_ptr(), B, S, d_out.data_ptr(), d_stats.data_ptr(), wl.max_new,
-                            wl.lookahead, wl.temperature, seed=1234, uniforms=uni)
+        if wl.tree:
+            eng.generate_tree_device(d_prompts.data_ptr(), B, S, d_out.data_ptr(), d_stats.data_ptr(), wl.max_new,
+                                     wl.tree, wl.temperature, seed=1234, uniforms=uni)
+        else:
+            eng.generate_device(d_prompts.data_ptr(), B, S, d_out.data_ptr(), d_stats.data_ptr(), wl.max_new,
+                                wl.lookahead, wl.temperature, seed=1234, uniforms=uni)
 
     for _ in range(args.warmup):
         step()
@@ -330,8 +377,12 @@ def main():
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(stream):
             e0.record(stream)
-        eng.generate_speculative(pin_prompts.numpy(), wl.max_new, wl.lookahead, wl.temperature, seed=1234,
-                                 uniforms=pin_uni.numpy())
+        if wl.tree:
+            eng.generate_tree(pin_prompts.numpy(), wl.max_new, wl.tree, wl.temperature, seed=1234,
+                              uniforms=pin_uni.numpy())
+        else:
+            eng.generate_speculative(pin_prompts.numpy(), wl.max_new, wl.lookahead, wl.temperature, seed=1234,
+                                     uniforms=pin_uni.numpy())
         with torch.cuda.stream(stream):
             e1.record(stream)
         torch.cuda.synchronize()
@@ -344,6 +395,7 @@ def main():
     e2e_value = new_tokens * world * len(e2e_ms) / (e2e_tot / 1e3)
 
     hbm, peak_kind = peaks()
+    tflops = bf16_peak()
     avg_ctx = S + wl.max_new / 2
     ab = algorithmic_bytes_per_round(wl, wl.weights_int8, avg_ctx)
     round_ms = ms_per_step / max(1, rounds)
@@ -352,24 +404,28 @@ def main():
 
     # Dominant kernels, timed alone on the library's stream with CUDA events
     # (L2 flushed before every launch) over the verify pass's row count.
-    R_verify = B * (wl.lookahead + 1)
+    R_verify = B * ((tree_nodes(wl.tree) + 1) if wl.tree else (wl.lookahead + 1))
+    m = wl.target
+    nk = {"ffn_out": (m.d_model, m.d_ff), "ffn_in": (2 * m.d_ff, m.d_model),
+          "qkv": (m.d_model + 2 * m.kv_heads * m.head_dim, m.d_model), "head": (m.vocab, m.d_model)}
     probes = {}
     for name, which, layer in (("ffn_out", sd.LIN_FFN_OUT, 0), ("ffn_in", sd.LIN_FFN_IN, 0),
                                ("qkv", sd.LIN_QKV, 1), ("head", sd.LIN_HEAD, wl.target.n_layers - 1)):
         us, nbytes = eng.time_linear(sd.TARGET, layer, which, R_verify, 20, flush.data_ptr(), flush.numel() * 4)
-        probes[name] = {"us": us, "bytes": nbytes, "GBps": nbytes / (us * 1e-6) / 1e9}
+        flops = 2.0 * R_verify * nk[name][0] * nk[name][1]
+        probes[name] = {"us": us, "bytes": nbytes, "GBps": nbytes / (us * 1e-6) / 1e9,
+                        "TFLOPs": flops / (us * 1e-6) / 1e12, "flops_per_byte": flops / nbytes}
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": "int8" if wl.weights_int8 else "f32", "data": "synthetic",
+                "vs_baseline": None, "dtype": ("int8 weights, bf16 activations" if wl.act_bf16 else "int8")
+                if wl.weights_int8 else "f32", "data": "synthetic",
                 "config": config_dict(wl, args),
                 "e2e": {"value": e2e_value, "unit": UNIT,
                         "h2d_bytes_per_step": int(prompts.size * 4 + uni.nbytes),
                         "d2h_bytes_per_step": int(B * out_len * 4 + B * 4 * 8 + 4)},
                 "gpu_launches": int(launches),
-                "roofline": {"bound": "hbm", "achieved": probes["ffn_out"]["GBps"], "peak": hbm, "unit": "GB/s",
-                             "frac": probes["ffn_out"]["GBps"] / hbm, "traffic": None,
-                             "kernel": f"linear_kernel<int8,f32,Resid> (target FFN down-projection, {R_verify} verify rows)",
+                "roofline": {**roofline_entry(probes["ffn_out"], hbm, tflops, wl, R_verify),
                              "launch_us": probes["ffn_out"]["us"], "alg_bytes_per_launch": probes["ffn_out"]["bytes"],
                              "peak_source": peak_kind,
                              "other_kernels": {k: v for k, v in probes.items() if k != "ffn_out"},
@@ -380,6 +436,9 @@ def main():
                 "clocks": clocks}
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_sample(wl)
+        if wl.tree:
+            line["tree"] = {"branching": list(wl.tree), "nodes": tree_nodes(wl.tree),
+                            "mean_accepted_per_round": line["spec"]["mean_accepted_per_round"]}
         print(json.dumps(line), flush=True)
     eng.close()
     if world > 1:

@@ -189,6 +189,13 @@ typedef struct specdec_tree {
 int specdec_generate_tree(specdec_handle *h, const specdec_gen_params *p, const specdec_tree *tree,
                           const int32_t *prompts, int B, int S, int32_t *out_tokens, int64_t *out_stats);
 
+/* specdec_generate_tree on device buffers, enqueued on specdec_stream(h)
+ * like specdec_generate_device (no synchronisation, no status from the
+ * device side: read the statistics to check). */
+int specdec_generate_tree_device(specdec_handle *h, const specdec_gen_params *p, const specdec_tree *tree,
+                                 const int32_t *d_prompts, int B, int S, int32_t *d_out_tokens,
+                                 int64_t *d_out_stats);
+
 /* Number of kernel launches the last generate call issued on the device. */
 int64_t specdec_last_launch_count(const specdec_handle *h);
 

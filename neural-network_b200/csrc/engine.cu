@@ -202,7 +202,8 @@ struct specdec_handle {
   int *d_iters = nullptr;
   int *h_pinned = nullptr;
 
-  int max_tree = 0, tree_base = 0;  // token trees: largest tree, first pool row of the tree regions
+  int max_tree = 0, tree_base = 0;
+  int logits_rows = 0;              // rows of the logits buffer  // token trees: largest tree, first pool row of the tree regions
   std::map<GraphKey, GraphEntry> graphs;
   int64_t launches = 0;        // direct mode: kernels enqueued by the last call; -1 in graph mode
   int64_t graph_fixed = 0, graph_body = 0, extra_launches = 0;
@@ -1171,6 +1172,8 @@ int specdec_create(const specdec_config *cfg, int device, specdec_handle **out) 
       CK(cudaFuncSetAttribute(first_token_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, vs));
       CK(cudaFuncSetAttribute(draft_sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, vs));
       CK(cudaFuncSetAttribute(accept_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, vs));
+      CK(cudaFuncSetAttribute(tree_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, vs));
+      CK(cudaFuncSetAttribute(tree_accept_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, vs));
     }
 
     const int B = cfg->max_batch, k = cfg->max_lookahead;
@@ -1229,6 +1232,7 @@ int specdec_create(const specdec_config *cfg, int device, specdec_handle **out) 
       h->KVN = static_cast<float *>(
           h->dalloc(static_cast<size_t>(h->R_max) * 2 * std::max(td.kvd, dd.kvd) * sizeof(float)));
     h->logits = static_cast<float *>(h->dalloc(static_cast<size_t>(R_round) * td.V * sizeof(float)));
+    h->logits_rows = R_round;
     h->tree_base =
         h->R_max + 2 * B + (k - 1) * B + B * (k + 1);
     const size_t pool_rows = static_cast<size_t>(h->tree_base) +
@@ -1356,8 +1360,7 @@ int specdec_time_linear(specdec_handle *h, int role, int layer, int which, int r
       case SPECDEC_LIN_HEAD:
         a.x = h->H; a.W = m.whead; a.scale = m.shead; a.bias = m.bhead; a.N = dm.V; a.out = h->logits; a.ldo = dm.V;
         a.out_f32 = 1; a.in_g = m.layers[dm.L - 1].g2; a.in_b = m.layers[dm.L - 1].b2; out_w = dm.V;
-        if (rows > std::max(h->cfg.max_batch * (h->cfg.max_lookahead + 1), 2 * h->cfg.max_batch))
-          fail(SPECDEC_ERR_INVALID, "rows exceed the logits buffer");
+        if (rows > h->logits_rows) fail(SPECDEC_ERR_INVALID, "rows exceed the logits buffer");
         break;
       default:
         fail(SPECDEC_ERR_INVALID, "unknown linear layer");
@@ -1447,6 +1450,21 @@ int host_generate(specdec_handle *h, const specdec_gen_params *p, const specdec_
 int specdec_generate(specdec_handle *h, const specdec_gen_params *p, const int32_t *prompts, int B, int S,
                      int32_t *out_tokens, int64_t *out_stats) {
   return host_generate(h, p, nullptr, prompts, B, S, out_tokens, out_stats);
+}
+
+int specdec_generate_tree_device(specdec_handle *h, const specdec_gen_params *p, const specdec_tree *tree,
+                                 const int32_t *d_prompts, int B, int S, int32_t *d_out_tokens,
+                                 int64_t *d_out_stats) {
+  if (!h) return SPECDEC_ERR_INVALID;
+  try {
+    CK(cudaSetDevice(h->device));
+    if (!d_prompts || !d_out_tokens) fail(SPECDEC_ERR_INVALID, "null buffer");
+    const TreeCfg tc = make_tree(h, tree);
+    return generate_impl(h, p, d_prompts, B, S, d_out_tokens, d_out_stats, &tc);
+  } catch (const SpecErr &e) {
+    h->err = e.msg;
+    return e.code;
+  }
 }
 
 int specdec_generate_tree(specdec_handle *h, const specdec_gen_params *p, const specdec_tree *tree,

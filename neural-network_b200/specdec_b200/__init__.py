@@ -35,7 +35,7 @@ STATUS = {0: "OK", 1: "ERR_INVALID", 2: "ERR_CUDA", 3: "ERR_OOM", 4: "ERR_SEQ_LE
 EXPORTS = ("specdec_create", "specdec_destroy", "specdec_last_error", "specdec_load_params",
            "specdec_generate", "specdec_generate_device", "specdec_stream", "specdec_forward_logits",
            "specdec_philox_uniforms", "specdec_last_launch_count", "specdec_forward_logits_noalloc",
-           "specdec_time_linear", "specdec_generate_tree")
+           "specdec_time_linear", "specdec_generate_tree", "specdec_generate_tree_device")
 
 # linear layers of specdec_time_linear
 LIN_QKV, LIN_OPROJ, LIN_FFN_IN, LIN_FFN_OUT, LIN_HEAD = 0, 1, 2, 3, 4
@@ -101,6 +101,8 @@ def load_library(path: str = LIB_PATH):
     lib.specdec_last_launch_count.argtypes = [C.c_void_p]
     lib.specdec_generate_tree.argtypes = [C.c_void_p, C.POINTER(_GenParams), C.POINTER(_Tree), C.c_void_p, C.c_int,
                                           C.c_int, C.c_void_p, C.c_void_p]
+    lib.specdec_generate_tree_device.argtypes = [C.c_void_p, C.POINTER(_GenParams), C.POINTER(_Tree), C.c_void_p,
+                                                 C.c_int, C.c_int, C.c_void_p, C.c_void_p]
     lib.specdec_time_linear.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                         C.c_size_t, C.POINTER(C.c_float), C.POINTER(C.c_double)]
     _lib = lib
@@ -203,6 +205,16 @@ class Engine:
                                                     out.ctypes.data, stats.ctypes.data))
         del keep
         return out.astype(np.int64), stats
+
+    def generate_tree_device(self, d_prompts: int, B: int, S: int, d_out: int, d_stats: int, max_new_tokens: int,
+                             branching, temperature: float = 1.0, seed: int = 42, uniforms=None) -> None:
+        """Device-pointer variant of generate_tree, enqueued on `stream`."""
+        prm, keep = self._params(max_new_tokens, 1, temperature, 0, 1.0, seed, uniforms, CATCHUP_CORRECT)
+        br = list(branching)
+        tree = _Tree(len(br), (C.c_int32 * 8)(*br))
+        self._check(self._lib.specdec_generate_tree_device(self.h, C.byref(prm), C.byref(tree), C.c_void_p(d_prompts),
+                                                           B, S, C.c_void_p(d_out), C.c_void_p(d_stats)))
+        del keep
 
     def generate_device(self, d_prompts: int, B: int, S: int, d_out: int, d_stats: int, max_new_tokens: int,
                         lookahead: int = 4, temperature: float = 1.0, seed: int = 42, uniforms=None,

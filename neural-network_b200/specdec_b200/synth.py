@@ -201,6 +201,7 @@ class Workload:
     weights_int8: bool
     act_bf16: bool
     kv_mode: int = 0  # 0 fp32, 1 bf16, 2 int8
+    tree: tuple = ()  # token-tree branching per level (tree speculation), () for a chain
 
 
 def _shape(V, d, H, F, L, max_seq, arch=ARCH_REF):
@@ -216,6 +217,11 @@ def workload(name: str, arch: int = ARCH_REF) -> Workload:
         return Workload("int8", _shape(2048, 256, 4, 1024, 4, 64 + 2 * 256 + 8, arch), 1, 8, 64, 256, 4, 1.0, True, False)
     if name == "medium":
         return Workload("medium", _shape(32000, 768, 12, 3072, 12, 256 + 2 * 256 + 16, arch), 2, 32, 256, 256, 6, 0.8, True, True, 1)
+    if name == "tree":
+        # config-3 models, 64 requests, 512-token prompts,
+        # a 4/3/2/1 tree (64 nodes); 256 new tokens
+        return Workload("tree", _shape(32000, 768, 12, 3072, 12, 512 + 256 + 80, arch), 2, 64, 512, 256, 4, 1.0, True, True,
+                        1, (4, 3, 2, 1))
     if name == "large":
         return Workload("large", _shape(32000, 4096, 32, 11008, 32, 2048 + 2 * 512 + 8, arch), 4, 256, 2048, 512, 4, 1.0, True, True, 1)
     raise KeyError(name)
