@@ -199,6 +199,21 @@ int specdec_generate_tree_device(specdec_handle *h, const specdec_gen_params *p,
 /* Number of kernel launches the last generate call issued on the device. */
 int64_t specdec_last_launch_count(const specdec_handle *h);
 
+/* Tensor parallelism (the large configuration's variant; no counterpart in
+ * the reference, which runs on one device): `world` handles, one per GPU and
+ * process (or thread), each created with its rank and the same 128-byte NCCL
+ * unique id, which one rank makes with specdec_tp_unique_id and hands to the
+ * others.  Every rank loads the whole model's parameters; each keeps its
+ * share of the attention heads (and their KV cache) and of the FFN columns,
+ * and the attention output and FFN down projections end in an NCCL
+ * all-reduce (sum) over NVLink.  Embedding, LayerNorm, lm_head and sampling
+ * are replicated, and every rank returns the same tokens.  All ranks must
+ * make the same calls in the same order.  Heads, kv heads and d_ff must
+ * divide by `world`.  NCCL (libnccl.so.2) is loaded on first use. */
+int specdec_tp_unique_id(void *out128);
+int specdec_create_tp(const specdec_config *cfg, int device, int rank, int world, const void *unique_id,
+                      specdec_handle **out);
+
 /* Which linear layer specdec_time_linear launches. */
 enum specdec_linear {
   SPECDEC_LIN_QKV = 0,     /* fused q/k/v projection (+ RoPE, cache append) */

@@ -17,6 +17,8 @@
 // profiling (ncu cannot profile kernel nodes of graphs with conditional nodes).
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <dlfcn.h>
+#include <nccl.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -59,8 +61,12 @@ struct SpecErr {
 
 [[noreturn]] void fail(int code, const std::string &m) { throw SpecErr{code, m}; }
 
+// Model dimensions as this rank holds them: with tensor parallelism H, Hkv
+// and F are the rank's share (heads and FFN columns), Hg, Hkvg and Fg the
+// model's; dq = H * D is the rank's query width (d without parallelism).
 struct Dims {
   int V, d, H, Hkv, D, F, L, max_seq, arch, kvd;
+  int dq, Hg, Hkvg, Fg;
 };
 
 // A validated token tree: depth, branching, node counts per depth.
@@ -202,6 +208,9 @@ struct specdec_handle {
   int *d_iters = nullptr;
   int *h_pinned = nullptr;
 
+  // tensor parallelism: this rank's index, the group size and its communicator
+  int tp_rank = 0, tp_world = 1;
+  ncclComm_t comm = nullptr;
   int max_tree = 0, tree_base = 0;
   int logits_rows = 0;              // rows of the logits buffer  // token trees: largest tree, first pool row of the tree regions
   std::map<GraphKey, GraphEntry> graphs;
@@ -234,7 +243,23 @@ Dims make_dims(const specdec_model_config &m) {
   d.max_seq = m.max_seq_len;
   d.arch = m.arch;
   d.kvd = d.Hkv * d.D;
+  d.dq = d.H * d.D;
+  d.Hg = d.H;
+  d.Hkvg = d.Hkv;
+  d.Fg = d.F;
   return d;
+}
+
+// This rank's share of a model under `world`-way tensor parallelism.
+void shard_dims(Dims &d, int world, const char *who) {
+  if (world <= 1) return;
+  if (d.H % world || d.Hkv % world || d.F % world)
+    fail(SPECDEC_ERR_INVALID, std::string(who) + ": heads, kv heads and d_ff must divide by the tensor-parallel size");
+  d.H /= world;
+  d.Hkv /= world;
+  d.F /= world;
+  d.kvd = d.Hkv * d.D;
+  d.dq = d.H * d.D;
 }
 
 void check_dims(const Dims &d, const char *who) {
@@ -271,14 +296,27 @@ void quantize_columns(const float *w, int K, int N, std::vector<int8_t> &q, std:
 // A set of reference Dense weights [K][N_i] (+ bias [N_i]) stacked into one
 // output-major device matrix [sum N_i][K]; `interleave` stacks two equally
 // wide matrices column by column (SwiGLU gate/up).
+// One Dense of the reference ([K][ld] row-major, parameters() order) or the
+// slice of it this rank holds: output columns col0 .. col0 + N - 1; the bias
+// is replaced by zeros when !bias_on (every rank but one under tensor
+// parallelism, so the bias is added once).
 struct DenseSrc {
   const float *w;
   const float *b;
   int N;
+  int ld = 0;    // columns of the full matrix (0: N)
+  int col0 = 0;
+  bool bias_on = true;
 };
 
+// Uploads the given Dense sources stacked (or, with `interleave`, row by row)
+// as one output-major matrix [sum N][K].  K is the rank's input slice, rows
+// row0 .. row0 + K - 1 of the Kfull input rows (Kfull = 0: K).  int8 scales
+// are per output column over all Kfull rows, as QuantizedDense computes them
+// on the whole matrix.
 void upload_stacked(specdec_handle *h, int role, const std::vector<DenseSrc> &src, int K, bool interleave,
-                    void **wout, float **sout, float **bout) {
+                    void **wout, float **sout, float **bout, int Kfull = 0, int row0 = 0) {
+  if (Kfull == 0) Kfull = K;
   int Ntot = 0;
   for (auto &s : src) Ntot += s.N;
   std::vector<float> bias(Ntot);
@@ -291,15 +329,17 @@ void upload_stacked(specdec_handle *h, int role, const std::vector<DenseSrc> &sr
   int base = 0;
   for (size_t m = 0; m < src.size(); ++m) {
     const DenseSrc &s = src[m];
+    const int ld = s.ld ? s.ld : s.N;
     std::vector<int8_t> q;
     std::vector<float> sc;
-    if (i8) quantize_columns(s.w, K, s.N, q, sc);
+    if (i8) quantize_columns(s.w, Kfull, ld, q, sc);
     for (int c = 0; c < s.N; ++c) {
+      const int gc = s.col0 + c;
       const int row = interleave ? (2 * c + static_cast<int>(m)) : (base + c);
-      bias[row] = s.b[c];
-      if (i8) scale[row] = sc[c];
+      bias[row] = s.bias_on ? s.b[gc] : 0.f;
+      if (i8) scale[row] = sc[gc];
       for (int k = 0; k < K; ++k) {
-        const size_t si = static_cast<size_t>(k) * s.N + c;
+        const size_t si = static_cast<size_t>(row0 + k) * ld + gc;
         if (i8) wq[static_cast<size_t>(row) * K + k] = q[si];
         else wf[static_cast<size_t>(row) * K + k] = s.w[si];
       }
@@ -341,7 +381,11 @@ float *upload_vec(specdec_handle *h, int role, const float *p, size_t n) {
 
 void load_model(specdec_handle *h, int role, ModelW &m, int n, const float *const *P, const int64_t *numel) {
   const Dims &dm = m.dm;
-  const int d = dm.d, F = dm.F, V = dm.V, kvd = dm.kvd;
+  // parameter shapes are the whole model's; this rank keeps its slices
+  const int d = dm.d, F = dm.Fg, V = dm.V, kvd = dm.Hkvg * dm.D;
+  const int r = h->tp_rank;
+  const int dq = dm.dq, kvl = dm.kvd, Fl = dm.F;
+  const bool bias_rank = r == 0;  // the rank that adds the biases of the row-sliced layers
   const bool ref = dm.arch == SPECDEC_ARCH_REF;
   const int per = ref ? 18 : 16;
   const int lead = ref ? 1 : 2, tail = ref ? 2 : 4;
@@ -386,13 +430,14 @@ void load_model(specdec_handle *h, int role, ModelW &m, int n, const float *cons
     const float *qw = P[i], *qb = P[i + 1], *kw = P[i + 2], *kb = P[i + 3], *vw = P[i + 4], *vb = P[i + 5];
     const float *ow = P[i + 6], *ob = P[i + 7];
     i += 8;
-    upload_stacked(h, role, {{qw, qb, d}, {kw, kb, kvd}, {vw, vb, kvd}}, d, false, &L.wqkv, &L.sqkv, &L.bqkv);
-    upload_stacked(h, role, {{ow, ob, d}}, d, false, &L.wo, &L.so, &L.bo);
+    upload_stacked(h, role, {{qw, qb, dq, d, r * dq}, {kw, kb, kvl, kvd, r * kvl}, {vw, vb, kvl, kvd, r * kvl}}, d,
+                   false, &L.wqkv, &L.sqkv, &L.bqkv);
+    upload_stacked(h, role, {{ow, ob, d, d, 0, bias_rank}}, dq, false, &L.wo, &L.so, &L.bo, d, r * dq);
     if (ref) {
       const float *gw = P[i], *gb = P[i + 1], *uw = P[i + 2], *ub = P[i + 3], *dw = P[i + 4], *db = P[i + 5];
       i += 6;
-      upload_stacked(h, role, {{gw, gb, F}, {uw, ub, F}}, d, true, &L.wgu, &L.sgu, &L.bgu);
-      upload_stacked(h, role, {{dw, db, d}}, F, false, &L.wd, &L.sd, &L.bd);
+      upload_stacked(h, role, {{gw, gb, Fl, F, r * Fl}, {uw, ub, Fl, F, r * Fl}}, d, true, &L.wgu, &L.sgu, &L.bgu);
+      upload_stacked(h, role, {{dw, db, d, d, 0, bias_rank}}, Fl, false, &L.wd, &L.sd, &L.bd, F, r * Fl);
       L.g1 = upload_vec(h, role, P[i], d); L.b1 = upload_vec(h, role, P[i + 1], d);
       L.g2 = upload_vec(h, role, P[i + 2], d); L.b2 = upload_vec(h, role, P[i + 3], d);
       i += 4;
@@ -401,8 +446,8 @@ void load_model(specdec_handle *h, int role, ModelW &m, int n, const float *cons
       i += 2;
       const float *f1w = P[i], *f1b = P[i + 1], *f2w = P[i + 2], *f2b = P[i + 3];
       i += 4;
-      upload_stacked(h, role, {{f1w, f1b, F}}, d, false, &L.wgu, &L.sgu, &L.bgu);
-      upload_stacked(h, role, {{f2w, f2b, d}}, F, false, &L.wd, &L.sd, &L.bd);
+      upload_stacked(h, role, {{f1w, f1b, Fl, F, r * Fl}}, d, false, &L.wgu, &L.sgu, &L.bgu);
+      upload_stacked(h, role, {{f2w, f2b, d, d, 0, bias_rank}}, Fl, false, &L.wd, &L.sd, &L.bd, F, r * Fl);
     }
   }
   if (!ref) { m.gf = upload_vec(h, role, P[i], d); m.bfin = upload_vec(h, role, P[i + 1], d); i += 2; }
@@ -698,10 +743,10 @@ void attention(specdec_handle *h, const Dims &dm, RowsView rows, int R, int Q, c
                const float *ks, const float *vs, size_t layer_elems, int S_cap) {
   if (R <= 0) return;
   AttnArgs a{};
-  a.q = h->Q; a.ldq = dm.d; a.rows = rows; a.R = R; a.Q = Q;
+  a.q = h->Q; a.ldq = dm.dq; a.rows = rows; a.R = R; a.Q = Q;
   a.S_cap = S_cap; a.H = dm.H; a.Hkv = dm.Hkv;
   a.k_scale = ks; a.v_scale = vs;
-  a.out = h->ATT; a.ldo = dm.d; a.err = h->st.err;
+  a.out = h->ATT; a.ldo = dm.dq; a.err = h->st.err;
   const int ngroups = (R + Q - 1) / Q;
   const size_t nrows = layer_elems / dm.D;
   const bool bf = act_bf16(h);
@@ -713,6 +758,46 @@ void attention(specdec_handle *h, const Dims &dm, RowsView rows, int R, int Q, c
   else if (bf) launch_attention_t<__nv_bfloat16, float>(h, a, dm.D, ngroups, kc, vc, nrows);
   else if (kvbf) launch_attention_t<float, __nv_bfloat16>(h, a, dm.D, ngroups, kc, vc, nrows);
   else launch_attention_t<float, float>(h, a, dm.D, ngroups, kc, vc, nrows);
+}
+
+// NCCL, looked up at run time (dlopen of libnccl.so.2 returns the copy the
+// process already has, e.g. the one torch loaded), so the library itself has
+// no link-time NCCL dependency and single-GPU use never touches it.
+struct NcclApi {
+  ncclResult_t (*get_unique_id)(ncclUniqueId *) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  const char *(*error_string)(ncclResult_t) = nullptr;
+};
+const NcclApi &nccl() {
+  static NcclApi api = [] {
+    NcclApi a;
+    void *lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!lib) return a;
+    a.get_unique_id = reinterpret_cast<decltype(a.get_unique_id)>(dlsym(lib, "ncclGetUniqueId"));
+    a.comm_init_rank = reinterpret_cast<decltype(a.comm_init_rank)>(dlsym(lib, "ncclCommInitRank"));
+    a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(dlsym(lib, "ncclAllReduce"));
+    a.comm_destroy = reinterpret_cast<decltype(a.comm_destroy)>(dlsym(lib, "ncclCommDestroy"));
+    a.error_string = reinterpret_cast<decltype(a.error_string)>(dlsym(lib, "ncclGetErrorString"));
+    return a;
+  }();
+  if (!api.get_unique_id || !api.comm_init_rank || !api.all_reduce || !api.comm_destroy)
+    fail(SPECDEC_ERR_UNSUPPORTED, "libnccl.so.2 is not available");
+  return api;
+}
+void nccl_check(ncclResult_t r, const char *what) {
+  if (r != ncclSuccess)
+    fail(SPECDEC_ERR_CUDA, std::string(what) + ": " + (nccl().error_string ? nccl().error_string(r) : "NCCL error"));
+}
+
+// Sum of the ranks' partial rows [R][d] in place (tensor parallelism: after
+// the attention output projection and the FFN down projection).
+void tp_all_reduce(specdec_handle *h, void *rows, int R, int d) {
+  if (h->tp_world <= 1 || R <= 0) return;
+  nccl_check(nccl().all_reduce(rows, rows, static_cast<size_t>(R) * d, act_bf16(h) ? ncclBfloat16 : ncclFloat, ncclSum,
+                               h->comm, h->stream),
+             "ncclAllReduce");
 }
 
 // Where the lm_head reads the last hidden rows, and the LayerNorm it applies
@@ -779,14 +864,14 @@ void forward_rows(specdec_handle *h, bool target, int off, int R, int Q, const i
     void *vcl = static_cast<char *>(vc) + l * lstride * kv_elt;
     LinearArgs a{};
     a.ldx = d; a.R = R; a.W = L.wqkv; a.scale = L.sqkv; a.bias = L.bqkv;
-    a.N = d + 2 * dm.kvd; a.K = d; a.out = h->Q; a.ldo = d; a.rows = rows;
+    a.N = dm.dq + 2 * dm.kvd; a.K = d; a.out = h->Q; a.ldo = dm.dq; a.rows = rows;
     if (ref) {
       a.x = l == 0 ? h->X : h->H;
       if (l > 0) { a.in_g = m.layers[l - 1].g2; a.in_b = m.layers[l - 1].b2; a.norm_out = h->X; }
     } else {
       a.x = h->X; a.in_g = L.g1; a.in_b = L.b1;
     }
-    a.qkv = QKVArgs{d, dm.kvd, dm.D, h->rope, h->rope_max, kcl, vcl, rstride, S_cap,
+    a.qkv = QKVArgs{dm.dq, dm.kvd, dm.D, h->rope, h->rope_max, kcl, vcl, rstride, S_cap,
                     kv8 ? 2 : h->cfg.kv_dtype == SPECDEC_BF16 ? 1 : 0, h->KVN, h->st.err};
     launch_linear<kEpiQKV>(h, a);
     float *ksl = kv8 ? ksc + l * lrows : nullptr, *vsl = kv8 ? vsc + l * lrows : nullptr;
@@ -794,10 +879,15 @@ void forward_rows(specdec_handle *h, bool target, int off, int R, int Q, const i
       launch(h, kv_quant_kernel, dim3(R), dim3(256), 0, rows, R, static_cast<const float *>(h->KVN), dm.kvd, dm.D,
              dm.Hkv, S_cap, static_cast<int8_t *>(kcl), static_cast<int8_t *>(vcl), ksl, vsl);
     attention(h, dm, rows, R, Q, kcl, vcl, ksl, vsl, lstride, S_cap);
+    // With tensor parallelism each rank multiplies its heads' slice; one rank
+    // adds bias and residual, and the all-reduce sums the partial rows.
+    const bool lead = h->tp_rank == 0;
     LinearArgs o{};
-    o.x = h->ATT; o.ldx = d; o.R = R; o.W = L.wo; o.scale = L.so; o.bias = L.bo; o.N = d; o.K = d;
+    o.x = h->ATT; o.ldx = dm.dq; o.R = R; o.W = L.wo; o.scale = L.so; o.bias = L.bo; o.N = d; o.K = dm.dq;
     o.out = h->H; o.ldo = d; o.resid = h->X; o.ldr = d; o.rows = rows;
-    launch_linear<kEpiResid>(h, o);
+    if (lead) launch_linear<kEpiResid>(h, o);
+    else launch_linear<kEpiStore>(h, o);
+    tp_all_reduce(h, h->H, R, d);
     LinearArgs g{};
     g.x = h->H; g.ldx = d; g.R = R; g.W = L.wgu; g.scale = L.sgu; g.bias = L.bgu; g.K = d; g.rows = rows;
     g.out = h->A; g.ldo = dm.F; g.N = ref ? 2 * dm.F : dm.F;
@@ -813,7 +903,9 @@ void forward_rows(specdec_handle *h, bool target, int off, int R, int Q, const i
     dn.rows = rows; dn.ldo = d; dn.ldr = d;
     if (ref) { dn.out = h->H; dn.resid = h->X1; }
     else { dn.out = h->X; dn.resid = h->H; }
-    launch_linear<kEpiResid>(h, dn);
+    if (lead) launch_linear<kEpiResid>(h, dn);
+    else launch_linear<kEpiStore>(h, dn);
+    tp_all_reduce(h, dn.out, R, d);
   }
   if (!logits) return;
   const HeadInput hi = head_input(h, m);
@@ -1123,7 +1215,41 @@ extern "C" {
 
 const char *specdec_last_error(const specdec_handle *h) { return h ? h->err.c_str() : g_create_err.c_str(); }
 
+namespace {
+int create_impl(const specdec_config *cfg, int device, int rank, int world, const void *uid, specdec_handle **out);
+}
+
 int specdec_create(const specdec_config *cfg, int device, specdec_handle **out) {
+  return create_impl(cfg, device, 0, 1, nullptr, out);
+}
+
+int specdec_tp_unique_id(void *out128) {
+  if (!out128) return SPECDEC_ERR_INVALID;
+  try {
+    ncclUniqueId id;
+    nccl_check(nccl().get_unique_id(&id), "ncclGetUniqueId");
+    static_assert(sizeof(ncclUniqueId) == 128, "NCCL unique id is 128 bytes");
+    std::memcpy(out128, &id, sizeof(id));
+  } catch (const SpecErr &e) {
+    g_create_err = e.msg;
+    return e.code;
+  }
+  return SPECDEC_OK;
+}
+
+int specdec_create_tp(const specdec_config *cfg, int device, int rank, int world, const void *unique_id,
+                      specdec_handle **out) {
+  if (world < 1 || rank < 0 || rank >= world || (world > 1 && !unique_id)) {
+    g_create_err = "bad tensor-parallel rank / size / id";
+    return SPECDEC_ERR_INVALID;
+  }
+  return create_impl(cfg, device, rank, world, unique_id, out);
+}
+
+}  // extern "C"
+
+namespace {
+int create_impl(const specdec_config *cfg, int device, int rank, int world, const void *uid, specdec_handle **out) {
   if (!out) return SPECDEC_ERR_INVALID;
   *out = nullptr;
   auto h = std::make_unique<specdec_handle>();
@@ -1131,10 +1257,13 @@ int specdec_create(const specdec_config *cfg, int device, specdec_handle **out) 
     if (!cfg) fail(SPECDEC_ERR_INVALID, "null config");
     h->cfg = *cfg;
     h->device = device;
+    h->tp_rank = rank;
+    h->tp_world = world;
     CK(cudaSetDevice(device));
     CK(cudaDeviceGetAttribute(&h->num_sms, cudaDevAttrMultiProcessorCount, device));
     Dims td = make_dims(cfg->target);
     check_dims(td, "target");
+    shard_dims(td, world, "target");
     specdec_model_config dcfg = cfg->draft;
     if (cfg->draft_shares_target) {
       const int nl = cfg->draft.n_layers;
@@ -1144,6 +1273,7 @@ int specdec_create(const specdec_config *cfg, int device, specdec_handle **out) 
     }
     Dims dd = make_dims(dcfg);
     check_dims(dd, "draft");
+    shard_dims(dd, world, "draft");
     if (dd.V != td.V) fail(SPECDEC_ERR_INVALID, "target and draft vocab differ");
     if (dd.arch != td.arch) fail(SPECDEC_ERR_INVALID, "target and draft arch differ");
     if (td.L < 1 || dd.L < 1) fail(SPECDEC_ERR_INVALID, "models need at least one layer");
@@ -1279,6 +1409,15 @@ int specdec_create(const specdec_config *cfg, int device, specdec_handle **out) 
     h->d_stats = static_cast<long long *>(h->dalloc(static_cast<size_t>(B) * 4 * sizeof(long long)));
     CK(cudaMallocHost(&h->h_pinned, 64));
     CK(cudaDeviceSynchronize());
+    if (world > 1) {
+      // NCCL operations cannot sit in the body of a conditional graph node,
+      // so tensor-parallel rounds are driven from the host
+      h->use_graph = false;
+      // collective over the `world` ranks; each calls it with its device current
+      ncclUniqueId id;
+      std::memcpy(&id, uid, sizeof(id));
+      nccl_check(nccl().comm_init_rank(&h->comm, world, id, rank), "ncclCommInitRank");
+    }
   } catch (const SpecErr &e) {
     g_create_err = e.msg;
     specdec_destroy(h.release());
@@ -1287,12 +1426,19 @@ int specdec_create(const specdec_config *cfg, int device, specdec_handle **out) 
   *out = h.release();
   return SPECDEC_OK;
 }
+}  // namespace
+
+extern "C" {
 
 int specdec_destroy(specdec_handle *h) {
   if (!h) return SPECDEC_OK;
   cudaSetDevice(h->device);
   if (h->stream) cudaStreamSynchronize(h->stream);
-  destroy_graphs(h);
+  destroy_graphs(h);  // graphs holding NCCL calls go before the communicator
+  if (h->comm) {
+    nccl().comm_destroy(h->comm);
+    h->comm = nullptr;
+  }
   for (int r = 0; r < 2; ++r)
     for (void *p : h->weight_allocs[r]) cudaFree(p);
   for (void *p : h->allocs) cudaFree(p);
@@ -1339,14 +1485,14 @@ int specdec_time_linear(specdec_handle *h, int role, int layer, int which, int r
     double in_w = d, out_w = d;  // input / output row widths
     switch (which) {
       case SPECDEC_LIN_QKV:
-        a.x = h->H; a.W = L.wqkv; a.scale = L.sqkv; a.bias = L.bqkv; a.N = d + 2 * dm.kvd; a.out = h->Q; a.ldo = d;
-        a.in_g = L.g1; a.in_b = L.b1;
-        a.qkv = QKVArgs{d, dm.kvd, dm.D, h->rope, h->rope_max, h->tk, h->tv, 0, 1, 0, nullptr, nullptr};
-        epi = kEpiQKV; out_w = d + 2 * dm.kvd;
+        a.x = h->H; a.W = L.wqkv; a.scale = L.sqkv; a.bias = L.bqkv; a.N = dm.dq + 2 * dm.kvd; a.out = h->Q;
+        a.ldo = dm.dq; a.in_g = L.g1; a.in_b = L.b1;
+        a.qkv = QKVArgs{dm.dq, dm.kvd, dm.D, h->rope, h->rope_max, h->tk, h->tv, 0, 1, 0, nullptr, nullptr};
+        epi = kEpiQKV; out_w = dm.dq + 2 * dm.kvd;
         break;
       case SPECDEC_LIN_OPROJ:
-        a.x = h->ATT; a.W = L.wo; a.scale = L.so; a.bias = L.bo; a.N = d; a.out = h->H; a.ldo = d;
-        a.resid = h->X; a.ldr = d; epi = kEpiResid; out_w = 2.0 * d;
+        a.x = h->ATT; a.ldx = dm.dq; a.K = dm.dq; a.W = L.wo; a.scale = L.so; a.bias = L.bo; a.N = d; a.out = h->H;
+        a.ldo = d; a.resid = h->X; a.ldr = d; epi = kEpiResid; in_w = dm.dq; out_w = 2.0 * d;
         break;
       case SPECDEC_LIN_FFN_IN:
         a.x = h->H; a.W = L.wgu; a.scale = L.sgu; a.bias = L.bgu; a.N = ref ? 2 * dm.F : dm.F; a.out = h->A;

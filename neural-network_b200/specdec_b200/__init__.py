@@ -35,7 +35,8 @@ STATUS = {0: "OK", 1: "ERR_INVALID", 2: "ERR_CUDA", 3: "ERR_OOM", 4: "ERR_SEQ_LE
 EXPORTS = ("specdec_create", "specdec_destroy", "specdec_last_error", "specdec_load_params",
            "specdec_generate", "specdec_generate_device", "specdec_stream", "specdec_forward_logits",
            "specdec_philox_uniforms", "specdec_last_launch_count", "specdec_forward_logits_noalloc",
-           "specdec_time_linear", "specdec_generate_tree", "specdec_generate_tree_device")
+           "specdec_time_linear", "specdec_generate_tree", "specdec_generate_tree_device", "specdec_tp_unique_id",
+           "specdec_create_tp")
 
 # linear layers of specdec_time_linear
 LIN_QKV, LIN_OPROJ, LIN_FFN_IN, LIN_FFN_OUT, LIN_HEAD = 0, 1, 2, 3, 4
@@ -103,6 +104,9 @@ def load_library(path: str = LIB_PATH):
                                           C.c_int, C.c_void_p, C.c_void_p]
     lib.specdec_generate_tree_device.argtypes = [C.c_void_p, C.POINTER(_GenParams), C.POINTER(_Tree), C.c_void_p,
                                                  C.c_int, C.c_int, C.c_void_p, C.c_void_p]
+    lib.specdec_tp_unique_id.argtypes = [C.c_void_p]
+    lib.specdec_create_tp.argtypes = [C.POINTER(_Config), C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                      C.POINTER(C.c_void_p)]
     lib.specdec_time_linear.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                         C.c_size_t, C.POINTER(C.c_float), C.POINTER(C.c_double)]
     _lib = lib
@@ -122,12 +126,24 @@ def philox_uniforms(seed: int, B: int, rounds: int, slots: int) -> np.ndarray:
     return out
 
 
+def tp_unique_id() -> bytes:
+    """The 128-byte NCCL id that all ranks of a tensor-parallel group pass to
+    Engine(tp_rank=..., tp_world=..., tp_id=...)."""
+    lib = load_library()
+    buf = C.create_string_buffer(128)
+    rc = lib.specdec_tp_unique_id(buf)
+    if rc:
+        raise SpecDecError(rc, lib.specdec_last_error(None).decode())
+    return buf.raw
+
+
 class Engine:
     """A target/draft pair on one B200 (one handle of the C ABI)."""
 
     def __init__(self, target: ModelShape, draft_layers: Optional[int] = None, draft: Optional[ModelShape] = None,
                  weight_dtype: int = F32, act_dtype: int = F32, kv_dtype: int = F32, max_batch: int = 1,
-                 max_lookahead: int = 4, max_prompt_len: int = 128, device: int = 0, max_tree_nodes: int = 0):
+                 max_lookahead: int = 4, max_prompt_len: int = 128, device: int = 0, max_tree_nodes: int = 0,
+                 tp_rank: int = 0, tp_world: int = 1, tp_id: Optional[bytes] = None):
         lib = load_library()
         shares = draft is None
         if shares and draft_layers is None:
@@ -136,7 +152,11 @@ class Engine:
         cfg = _Config(_mcfg(target), _mcfg(dshape), 1 if shares else 0, weight_dtype, act_dtype, kv_dtype,
                       max_batch, max_lookahead, max_prompt_len, max_tree_nodes)
         h = C.c_void_p()
-        rc = lib.specdec_create(C.byref(cfg), device, C.byref(h))
+        if tp_world > 1:
+            uid = C.create_string_buffer(bytes(tp_id), 128)
+            rc = lib.specdec_create_tp(C.byref(cfg), device, tp_rank, tp_world, uid, C.byref(h))
+        else:
+            rc = lib.specdec_create(C.byref(cfg), device, C.byref(h))
         if rc:
             raise SpecDecError(rc, lib.specdec_last_error(None).decode())
         self._lib = lib
