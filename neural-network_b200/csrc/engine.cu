@@ -542,7 +542,9 @@ int pick_ksplit(int N, int R, int K, int E, int nc, int num_sms) {
   while (ks < 8) {
     const int cols = nc * (kLinWarps / ks);
     const long blocks = static_cast<long>((N + cols - 1) / cols) * row_tiles;
-    if (blocks >= num_sms || K / E <= 32 * ks) break;
+    // stop once the grid fills the GPU, unless lanes would still stream more
+    // than two weight vectors each (long K: the loop's load latency adds up)
+    if ((blocks >= num_sms && K / E <= 64 * ks) || K / E <= 32 * ks) break;
     ks *= 2;
   }
   return ks;
@@ -586,13 +588,28 @@ CUtensorMap gemm_operand_map(const void *base, int K, int rows, int ld, int box_
   return m;
 }
 
+// LayerNorm of a's input rows (bf16) into contiguous rows at dst.
+bool ln_rows_ok(const LinearArgs &a) {
+  return a.K % 8 == 0 && a.ldx % 8 == 0 && a.K <= 4096 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
+}
+void launch_ln_rows(specdec_handle *h, const LinearArgs &a, void *dst) {
+  if (!ln_rows_ok(a)) fail(SPECDEC_ERR_UNSUPPORTED, "LayerNorm rows must be a multiple of 8 wide and 16-byte aligned");
+  auto ln = a.K <= 1024 ? ln_rows_kernel<4> : a.K <= 2048 ? ln_rows_kernel<8> : ln_rows_kernel<16>;
+  launch(h, ln, dim3((a.R + 7) / 8), dim3(256), 0, static_cast<const __nv_bfloat16 *>(a.x), a.ldx, a.in_rows, a.R,
+         a.K, a.in_g, a.in_b, static_cast<__nv_bfloat16 *>(dst), static_cast<__nv_bfloat16 *>(nullptr));
+}
+
 // The tensor-core path: bf16 activations, int8 weights with a bf16 image, at
 // least kGemmMinRows rows.  An input LayerNorm runs first as its own kernel,
 // writing the normalised rows where the GEMV would have stored them
 // (norm_out) or into X1, which is free whenever a LayerNorm feeds a GEMM.
 template <int EPI>
 bool try_launch_gemm(specdec_handle *h, LinearArgs a) {
-  if (!act_bf16(h) || !w_int8(h) || a.R < kGemmMinRows || (a.K % 8) != 0) return false;
+  // >= kGemmMinRows rows, or >= 16 rows of a wide layer (the lm_head): the GEMM
+  // reads each weight once, where 8-row GEMV tiles would re-read it per tile
+  const bool wide = a.R >= 16 && static_cast<long long>(a.N) * a.K >= (4ll << 20);
+  if (!act_bf16(h) || !w_int8(h) || (a.R < kGemmMinRows && !wide) || (a.K % 8) != 0) return false;
+  if (a.in_g && !ln_rows_ok(a)) return false;
   // the chunked epilogue's 16-byte vectors: aligned output / residual rows,
   // and q / k / v sections and heads in whole 16-column chunks
   if (a.ldo % (a.out_f32 ? 4 : 8) != 0) return false;
@@ -605,9 +622,7 @@ bool try_launch_gemm(specdec_handle *h, LinearArgs a) {
   int lda = a.ldx;
   if (a.in_g) {
     void *dst = a.norm_out ? a.norm_out : h->X1;
-    launch(h, ln_rows_kernel<__nv_bfloat16>, dim3((a.R + 7) / 8), dim3(256), 0,
-           static_cast<const __nv_bfloat16 *>(a.x), a.ldx, a.in_rows, a.R, a.K, a.in_g, a.in_b,
-           static_cast<__nv_bfloat16 *>(dst), static_cast<__nv_bfloat16 *>(nullptr));
+    launch_ln_rows(h, a, dst);
     A = dst;
     lda = a.K;
   } else if (a.in_rows) {
@@ -636,6 +651,16 @@ void launch_linear(specdec_handle *h, LinearArgs a) {
   const int cols = nc * (kLinWarps / a.ksplit);
   dim3 grid((a.N + cols - 1) / cols, (a.R + kRowTile - 1) / kRowTile);
   dim3 block(32 * kLinWarps);
+  if (a.in_g && act_bf16(h) && static_cast<long long>(grid.x) * a.K > 65536 && ln_rows_ok(a)) {
+    // every column block would normalise the same rows again: do it once
+    void *dst = a.norm_out ? a.norm_out : h->X1;
+    launch_ln_rows(h, a, dst);
+    a.x = dst;
+    a.ldx = a.K;
+    a.in_g = a.in_b = nullptr;
+    a.in_rows = nullptr;
+    a.norm_out = nullptr;
+  }
   if (nc == 4) launch_linear_nc<EPI, 4>(h, a, grid, block);
   else launch_linear_nc<EPI, 2>(h, a, grid, block);
 }

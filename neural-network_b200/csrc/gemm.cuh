@@ -353,33 +353,63 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
 }
 
 // LayerNorm of R input rows (optionally gathered through in_rows), one warp
-// per row, in the operation order of the GEMV's input LayerNorm, written as
-// contiguous rows [R][K] of the activation type (the GEMM's A operand) and,
-// when norm_out is set, also there.
-template <typename AT>
-__global__ void ln_rows_kernel(const AT *__restrict__ x, int ldx, const int *__restrict__ in_rows, int R, int K,
-                               const float *__restrict__ g, const float *__restrict__ b, AT *__restrict__ out,
-                               AT *__restrict__ norm_out) {
+// per row, written as contiguous rows [R][K] of the activation type (the A
+// operand of the GEMM, or the input of a GEMV) and, when norm_out is set,
+// also there.  Lane l holds elements 8 (l + 32 j) .. + 7 from 16-byte loads,
+// NV of them per lane (rows up to 256 NV wide).  Requires K % 8 == 0 and
+// 16-byte aligned rows.
+template <int NV>
+__global__ void ln_rows_kernel(const __nv_bfloat16 *__restrict__ x, int ldx, const int *__restrict__ in_rows, int R,
+                               int K, const float *__restrict__ g, const float *__restrict__ b,
+                               __nv_bfloat16 *__restrict__ out, __nv_bfloat16 *__restrict__ norm_out) {
   const int lane = threadIdx.x & 31;
   const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (r >= R) return;
   const int pr = in_rows ? in_rows[r] : r;
-  const AT *xr = x + static_cast<size_t>(pr) * ldx;
-  AT *y = out + static_cast<size_t>(r) * K;
+  const uint4 *xr = reinterpret_cast<const uint4 *>(x + static_cast<size_t>(pr) * ldx);
+  const int nv = K / 8;
+  float v[NV][8];
   float s = 0.f;
-  for (int c = lane; c < K; c += 32) s += to_f32(xr[c]);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = lane + 32 * j;
+    if (c < nv) {
+      bf16x8_to_f32(__ldg(xr + c), v[j]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[j][e] = 0.f;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s += v[j][e];
+  }
   const float mean = __fdiv_rn(warp_sum(s), static_cast<float>(K));
   float q = 0.f;
-  for (int c = lane; c < K; c += 32) {
-    const float df = to_f32(xr[c]) - mean;
-    q = fmaf(df, df, q);
-  }
+#pragma unroll
+  for (int j = 0; j < NV; ++j)
+    if (lane + 32 * j < nv)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float df = v[j][e] - mean;
+        q = fmaf(df, df, q);
+      }
   const float sd = sqrtf(__fdiv_rn(warp_sum(q), static_cast<float>(K)) + 1e-5f);
-  AT *no = norm_out ? norm_out + static_cast<size_t>(r) * K : nullptr;
-  for (int c = lane; c < K; c += 32) {
-    const AT v = from_f32<AT>(__fadd_rn(__fmul_rn(__fdiv_rn(to_f32(xr[c]) - mean, sd), __ldg(g + c)), __ldg(b + c)));
-    y[c] = v;
-    if (no) no[c] = v;
+  uint4 *y = reinterpret_cast<uint4 *>(out + static_cast<size_t>(r) * K);
+  uint4 *no = norm_out ? reinterpret_cast<uint4 *>(norm_out + static_cast<size_t>(r) * K) : nullptr;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = lane + 32 * j;
+    if (c < nv) {
+      const float4 g0 = __ldg(reinterpret_cast<const float4 *>(g) + 2 * c), g1 = __ldg(reinterpret_cast<const float4 *>(g) + 2 * c + 1);
+      const float4 b0 = __ldg(reinterpret_cast<const float4 *>(b) + 2 * c), b1 = __ldg(reinterpret_cast<const float4 *>(b) + 2 * c + 1);
+      const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+      const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = __fadd_rn(__fmul_rn(__fdiv_rn(v[j][e] - mean, sd), gg[e]), bb[e]);
+      const uint4 w = f32x8_to_bf16(o);
+      y[c] = w;
+      if (no) no[c] = w;
+    }
   }
 }
 
