@@ -26,6 +26,16 @@ template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(flo
   return __float2bfloat16_rn(v);
 }
 
+// Programmatic dependent launch (griddepcontrol, sm_90+).  A kernel launched
+// with programmatic stream serialization may start before its predecessor
+// has finished: it calls pdl_launch() to let its own successor start early,
+// does only work that reads no predecessor's output (weights), and calls
+// pdl_wait() -- which returns once the predecessor grid has completed and
+// its memory is visible -- before anything else and before any early exit.
+// Both are no-ops for kernels launched without the attribute.
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

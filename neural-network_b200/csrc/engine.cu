@@ -217,6 +217,7 @@ struct specdec_handle {
   int64_t launches = 0;        // direct mode: kernels enqueued by the last call; -1 in graph mode
   int64_t graph_fixed = 0, graph_body = 0, extra_launches = 0;
   bool use_graph = true;
+  bool use_pdl = true;  // programmatic dependent launch for the kernels that support it
 
   void *dalloc(size_t bytes, std::vector<void *> *owner = nullptr) {
     void *p = nullptr;
@@ -463,24 +464,44 @@ void launch(specdec_handle *h, void (*kern)(KArgs...), dim3 grid, dim3 block, si
   ++h->launches;
 }
 
-// A launch whose CTAs form thread-block clusters of `cluster` CTAs.
+// A launch whose CTAs form thread-block clusters of `cluster` CTAs (1 x 1 x 1:
+// no cluster), with programmatic stream serialization when the kernel
+// supports it (pdl_launch / pdl_wait, common.cuh) and the handle allows it.
 template <typename... KArgs, typename... Args>
-void launch_cluster(specdec_handle *h, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, dim3 cluster,
-                    Args... args) {
+void launch_ex(specdec_handle *h, bool pdl, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, dim3 cluster,
+               Args... args) {
   cudaLaunchConfig_t lc{};
   lc.gridDim = grid;
   lc.blockDim = block;
   lc.dynamicSmemBytes = smem;
   lc.stream = h->stream;
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeClusterDimension;
-  at[0].val.clusterDim.x = cluster.x;
-  at[0].val.clusterDim.y = cluster.y;
-  at[0].val.clusterDim.z = cluster.z;
+  cudaLaunchAttribute at[2];
+  int na = 0;
+  if (cluster.x * cluster.y * cluster.z > 1) {
+    at[na].id = cudaLaunchAttributeClusterDimension;
+    at[na].val.clusterDim.x = cluster.x;
+    at[na].val.clusterDim.y = cluster.y;
+    at[na].val.clusterDim.z = cluster.z;
+    ++na;
+  }
+  if (pdl && h->use_pdl) {
+    at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
   lc.attrs = at;
-  lc.numAttrs = 1;
+  lc.numAttrs = na;
   CK(cudaLaunchKernelEx(&lc, kern, static_cast<KArgs>(args)...));
   ++h->launches;
+}
+template <typename... KArgs, typename... Args>
+void launch_cluster(specdec_handle *h, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, dim3 cluster,
+                    Args... args) {
+  launch_ex(h, true, kern, grid, block, smem, cluster, args...);
+}
+template <typename... KArgs, typename... Args>
+void launch_pdl(specdec_handle *h, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, Args... args) {
+  launch_ex(h, true, kern, grid, block, smem, dim3(1, 1, 1), args...);
 }
 
 // cuTensorMapEncodeTiled, looked up from the driver once (no link-time
@@ -558,15 +579,15 @@ void launch_linear_nc(specdec_handle *h, const LinearArgs &a, dim3 grid, dim3 bl
   if (a.in_g) {
     const size_t smem = static_cast<size_t>(kRowTile) * a.K * h->act_elt;
     if (smem > kLinLnSmemMax) fail(SPECDEC_ERR_UNSUPPORTED, "input rows too wide for the fused LayerNorm");
-    if (i8 && bf) launch(h, linear_kernel<int8_t, __nv_bfloat16, EPI, true, NC>, grid, block, smem, a);
-    else if (i8) launch(h, linear_kernel<int8_t, float, EPI, true, NC>, grid, block, smem, a);
-    else if (bf) launch(h, linear_kernel<float, __nv_bfloat16, EPI, true, NC>, grid, block, smem, a);
-    else launch(h, linear_kernel<float, float, EPI, true, NC>, grid, block, smem, a);
+    if (i8 && bf) launch_pdl(h, linear_kernel<int8_t, __nv_bfloat16, EPI, true, NC>, grid, block, smem, a);
+    else if (i8) launch_pdl(h, linear_kernel<int8_t, float, EPI, true, NC>, grid, block, smem, a);
+    else if (bf) launch_pdl(h, linear_kernel<float, __nv_bfloat16, EPI, true, NC>, grid, block, smem, a);
+    else launch_pdl(h, linear_kernel<float, float, EPI, true, NC>, grid, block, smem, a);
   } else {
-    if (i8 && bf) launch(h, linear_kernel<int8_t, __nv_bfloat16, EPI, false, NC>, grid, block, 0, a);
-    else if (i8) launch(h, linear_kernel<int8_t, float, EPI, false, NC>, grid, block, 0, a);
-    else if (bf) launch(h, linear_kernel<float, __nv_bfloat16, EPI, false, NC>, grid, block, 0, a);
-    else launch(h, linear_kernel<float, float, EPI, false, NC>, grid, block, 0, a);
+    if (i8 && bf) launch_pdl(h, linear_kernel<int8_t, __nv_bfloat16, EPI, false, NC>, grid, block, 0, a);
+    else if (i8) launch_pdl(h, linear_kernel<int8_t, float, EPI, false, NC>, grid, block, 0, a);
+    else if (bf) launch_pdl(h, linear_kernel<float, __nv_bfloat16, EPI, false, NC>, grid, block, 0, a);
+    else launch_pdl(h, linear_kernel<float, float, EPI, false, NC>, grid, block, 0, a);
   }
 }
 
@@ -736,7 +757,7 @@ void launch_attention_d(specdec_handle *h, AttnArgs &a, int ngroups, const void 
   dim3 grid(ngroups * ngt, a.H, ns);
   dim3 block(kAttnThreads);
   auto go = [&](auto kern) {
-    if (ns == 1) launch(h, kern, grid, block, smem, a);
+    if (ns == 1) launch_pdl(h, kern, grid, block, smem, a);
     else launch_cluster(h, kern, grid, block, smem, dim3(1, 1, ns), a);
   };
   switch (qt) {
@@ -877,11 +898,11 @@ void forward_rows(specdec_handle *h, bool target, int off, int R, int Q, const i
   const bool ref = dm.arch == SPECDEC_ARCH_REF;
 
   if (act_bf16(h))
-    launch(h, embed_kernel<__nv_bfloat16>, dim3(R), dim3(128), 0, rows, R, m.emb, m.pos, d, dm.max_seq,
-           static_cast<__nv_bfloat16 *>(h->X));
+    launch_pdl(h, embed_kernel<__nv_bfloat16>, dim3(R), dim3(128), 0, rows, R, m.emb, m.pos, d, dm.max_seq,
+               static_cast<__nv_bfloat16 *>(h->X));
   else
-    launch(h, embed_kernel<float>, dim3(R), dim3(128), 0, rows, R, m.emb, m.pos, d, dm.max_seq,
-           static_cast<float *>(h->X));
+    launch_pdl(h, embed_kernel<float>, dim3(R), dim3(128), 0, rows, R, m.emb, m.pos, d, dm.max_seq,
+               static_cast<float *>(h->X));
 
   for (int l = 0; l < dm.L; ++l) {
     const LayerW &L = m.layers[l];
@@ -1041,13 +1062,13 @@ void enqueue_round(specdec_handle *h) {
   const int B = st.B, k = st.k;
   const dim3 sb(samp_threads(h));
   forward_rows(h, false, st.rows.off_step0, 2 * B, 2, h->sel_odd, B, h->logits);
-  launch(h, draft_sample_kernel, dim3(B), sb, samp_smem(h), st, 0, static_cast<const float *>(h->logits));
+  launch_pdl(h, draft_sample_kernel, dim3(B), sb, samp_smem(h), st, 0, static_cast<const float *>(h->logits));
   for (int j = 1; j < k; ++j) {
     forward_rows(h, false, st.rows.off_step1 + (j - 1) * B, B, 1, nullptr, B, h->logits);
-    launch(h, draft_sample_kernel, dim3(B), sb, samp_smem(h), st, j, static_cast<const float *>(h->logits));
+    launch_pdl(h, draft_sample_kernel, dim3(B), sb, samp_smem(h), st, j, static_cast<const float *>(h->logits));
   }
   forward_rows(h, true, st.rows.off_verify, B * (k + 1), k + 1, nullptr, B * (k + 1), h->logits);
-  launch(h, accept_kernel, dim3(B), sb, samp_smem(h), st, static_cast<const float *>(h->logits));
+  launch_pdl(h, accept_kernel, dim3(B), sb, samp_smem(h), st, static_cast<const float *>(h->logits));
 }
 
 void setup_state(specdec_handle *h, const specdec_gen_params *p, int B, int S, const TreeCfg *tree) {
@@ -1110,7 +1131,7 @@ void enqueue_prologue(specdec_handle *h, int B, int S, uint32_t seed) {
       forward_rows(h, target, 0, R, clen, h->sel_prefill, B, (target && last) ? h->logits : nullptr);
     }
   }
-  launch(h, first_token_kernel, dim3(B), dim3(samp_threads(h)), samp_smem(h), st, static_cast<const float *>(h->logits));
+  launch_pdl(h, first_token_kernel, dim3(B), dim3(samp_threads(h)), samp_smem(h), st, static_cast<const float *>(h->logits));
 }
 
 void destroy_graphs(specdec_handle *h) {
@@ -1314,6 +1335,7 @@ int create_impl(const specdec_config *cfg, int device, int rank, int world, cons
     h->dft.dm = dd;
     CK(cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking));
     h->use_graph = std::getenv("SPECDEC_NO_GRAPH") == nullptr;
+    h->use_pdl = std::getenv("SPECDEC_NO_PDL") == nullptr;
     set_attn_attrs<float, float>();
     set_attn_attrs<float, __nv_bfloat16>();
     set_attn_attrs<__nv_bfloat16, float>();

@@ -51,6 +51,8 @@ __device__ __forceinline__ int row_slot(const RowsView &rv, int r) { return rv.s
 template <typename AT>
 __global__ void embed_kernel(RowsView rows, int R, const float *__restrict__ emb, const float *__restrict__ pos_emb,
                              int d, int max_pos, AT *__restrict__ x) {
+  pdl_launch();
+  pdl_wait();
   const int r = blockIdx.x;
   if (r >= R) return;
   const int id = rows.tok[r];
@@ -223,13 +225,20 @@ struct EpiPre {
   int req, pos, slot;
 };
 
-template <typename AT, int EPI>
-__device__ __forceinline__ void epilogue_prefetch(const LinearArgs &a, int r, int n, EpiPre &p) {
+// Per-column operands (weights' scale and bias): no kernel writes them.
+__device__ __forceinline__ void epilogue_prefetch_cols(const LinearArgs &a, int n, EpiPre &p) {
   const bool has1 = (n + 1) < a.N;
   p.s0 = a.scale ? __ldg(a.scale + n) : 1.f;
   p.s1 = (a.scale && has1) ? __ldg(a.scale + n + 1) : 1.f;
   p.b0 = __ldg(a.bias + n);
   p.b1 = has1 ? __ldg(a.bias + n + 1) : 0.f;
+}
+
+// Per-row operands (residual, row position, RoPE factors): written by earlier
+// kernels of the pass.
+template <typename AT, int EPI>
+__device__ __forceinline__ void epilogue_prefetch_rows(const LinearArgs &a, int r, int n, EpiPre &p) {
+  const bool has1 = (n + 1) < a.N;
   p.r0 = p.r1 = 0.f;
   p.c = 1.f;
   p.sn = 0.f;
@@ -355,7 +364,7 @@ __global__ void __launch_bounds__(32 * kLinWarps, 2) linear_kernel(LinearArgs a)
   const int er = vi / NC, en = n0 + vi % NC;
   const bool epi_lane = col_ok && kidx == 0 && !((vi % NC) & 1) && (lane % LPV) == 0 && en < a.N && er < nrows;
   EpiPre pre{};
-  if (epi_lane) epilogue_prefetch<AT, EPI>(a, r0 + er, en, pre);
+  if (epi_lane) epilogue_prefetch_cols(a, en, pre);
 
   const WT *wc[NC];
 #pragma unroll
@@ -372,6 +381,9 @@ __global__ void __launch_bounds__(32 * kLinWarps, 2) linear_kernel(LinearArgs a)
 #pragma unroll
     for (int c = 0; c < NC; ++c) load_wvec(wc[c] + vstart * E, wf[c]);
   }
+  // everything above reads weights only; the rows come from earlier kernels
+  pdl_wait();
+  if (epi_lane) epilogue_prefetch_rows<AT, EPI>(a, r0 + er, en, pre);
 
   const AT *xrow[kRowTile];
   if constexpr (IN_LN) {
@@ -497,6 +509,7 @@ __global__ void __launch_bounds__(32 * kLinWarps, 2) linear_kernel(LinearArgs a)
         }
     }
   }
+  pdl_launch();  // the successor may start fetching its weights during the reduction
   float tot = warp_reduce_scatter<NV>(acc);
   if (ks > 1) {
     s_red[warp][lane] = tot;
@@ -719,6 +732,7 @@ __device__ __forceinline__ void lds_elems(const unsigned char *p, float *f) {
 template <typename AT, typename KT, int D, int QT>
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_constant__ AttnArgs a) {
   using G = AttnGeom<KT, D>;
+  pdl_wait();
   if constexpr (!G::kTma) {
     return;  // unreachable: the host rejects rows that are not a multiple of 16 bytes
   } else {
@@ -964,6 +978,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
 #pragma unroll
     for (int i = 0; i < QT; ++i) l[i] += __shfl_xor_sync(0xffffffffu, l[i], o);
 
+  pdl_launch();
   // merge the CTA's warps
   if (lane == 0) {
 #pragma unroll

@@ -618,6 +618,7 @@ __global__ void plan_prefill_kernel(const int *__restrict__ prompts, int B, int 
 // First new token from the target's prefill logits (src/nn/layer.cpp:1500-1510),
 // then the rows of the first round's draft step 0.
 __global__ void __launch_bounds__(kSampThreads) first_token_kernel(SpecState st, const float *__restrict__ logits) {
+  pdl_wait();
   __shared__ SampShared sh;
   extern __shared__ float srow[];  // [V]
   const int b = blockIdx.x;
@@ -649,6 +650,7 @@ __global__ void __launch_bounds__(kSampThreads) first_token_kernel(SpecState st,
 // of draft step j+1, and after the last draft step the verify rows
 // [last, c_0 .. c_{M-1}] at t_len + i (src/nn/layer.cpp:1560-1567).
 __global__ void __launch_bounds__(kSampThreads) draft_sample_kernel(SpecState st, int j, const float *__restrict__ logits) {
+  pdl_wait();
   __shared__ SampShared sh;
   extern __shared__ float srow[];  // [V]
   const int b = blockIdx.x;
@@ -672,6 +674,7 @@ __global__ void __launch_bounds__(kSampThreads) draft_sample_kernel(SpecState st
     tok = sample_smem(srow, st.V, sh.u, st.rng_mode, sh.redd, sh.redi);
     rng_commit(st, b, rc);
   }
+  pdl_launch();  // the next pass may launch while this block writes its rows
   if (threadIdx.x == 0) {
     int *cand = st.cand + b * st.kmax;
     cand[j] = tok;
@@ -699,6 +702,7 @@ __global__ void __launch_bounds__(kSampThreads) draft_sample_kernel(SpecState st
 // past the new length are simply overwritten by later rows.  Ends by writing
 // the next round's draft step 0 rows.
 __global__ void __launch_bounds__(kSampThreads) accept_kernel(SpecState st, const float *__restrict__ logits) {
+  pdl_wait();
   __shared__ SampShared sh;
   extern __shared__ float srow[];  // [V]
   const int b = blockIdx.x;
@@ -777,6 +781,7 @@ __global__ void __launch_bounds__(kSampThreads) accept_kernel(SpecState st, cons
     }
   }
   if (!st.greedy) rng_commit(st, b, rc);
+  pdl_launch();  // the next pass may launch while this block writes its rows
   if (threadIdx.x == 0) {
     for (int j = 0; j < naccept; ++j) emit(st, b, cand[j]);
     int catch_tok = -1;
