@@ -1013,6 +1013,13 @@ TreeCfg make_tree(const specdec_handle *h, const specdec_tree *t) {
 
 int samp_threads(const specdec_handle *h) { return h->tgt.dm.V <= 4096 ? 512 : kSampThreads; }
 size_t samp_smem(const specdec_handle *h) { return static_cast<size_t>(h->tgt.dm.V) * sizeof(float); }
+// Verify rows accept_kernel stages in shared memory at a time (at least one).
+constexpr size_t kAcceptStageBytes = 200 * 1024;
+int accept_stage_rows(const specdec_handle *h) {
+  const size_t row = samp_smem(h);
+  return static_cast<int>(std::max<size_t>(1, std::min<size_t>(h->cfg.max_lookahead + 1, kAcceptStageBytes / row)));
+}
+size_t accept_smem(const specdec_handle *h) { return static_cast<size_t>(accept_stage_rows(h)) * samp_smem(h); }
 
 // Enqueues one full round (everything between two accept kernels).
 CacheView cache_view(specdec_handle *h, bool target) {
@@ -1068,7 +1075,8 @@ void enqueue_round(specdec_handle *h) {
     launch_pdl(h, draft_sample_kernel, dim3(B), sb, samp_smem(h), st, j, static_cast<const float *>(h->logits));
   }
   forward_rows(h, true, st.rows.off_verify, B * (k + 1), k + 1, nullptr, B * (k + 1), h->logits);
-  launch_pdl(h, accept_kernel, dim3(B), sb, samp_smem(h), st, static_cast<const float *>(h->logits));
+  launch_pdl(h, accept_kernel, dim3(B), dim3(kSampThreads), accept_smem(h), st, static_cast<const float *>(h->logits),
+             accept_stage_rows(h));
 }
 
 void setup_state(specdec_handle *h, const specdec_gen_params *p, int B, int S, const TreeCfg *tree) {
@@ -1328,7 +1336,7 @@ int create_impl(const specdec_config *cfg, int device, int rank, int world, cons
     if (cfg->act_dtype != SPECDEC_F32 && cfg->act_dtype != SPECDEC_BF16) fail(SPECDEC_ERR_INVALID, "bad act_dtype");
     if (cfg->kv_dtype != SPECDEC_F32 && cfg->kv_dtype != SPECDEC_BF16 && cfg->kv_dtype != SPECDEC_INT8)
       fail(SPECDEC_ERR_INVALID, "bad kv_dtype");
-    if (cfg->max_batch < 1 || cfg->max_lookahead < 1 || cfg->max_lookahead > 32 || cfg->max_prompt_len < 1)
+    if (cfg->max_batch < 1 || cfg->max_lookahead < 1 || cfg->max_lookahead > kMaxLookahead || cfg->max_prompt_len < 1)
       fail(SPECDEC_ERR_INVALID, "max_batch / max_lookahead / max_prompt_len out of range");
     if (td.V > 51200) fail(SPECDEC_ERR_UNSUPPORTED, "vocabularies above 51200 entries are not supported");
     h->tgt.dm = td;
@@ -1348,7 +1356,8 @@ int create_impl(const specdec_config *cfg, int device, int rank, int world, cons
       const int vs = td.V * static_cast<int>(sizeof(float));
       CK(cudaFuncSetAttribute(first_token_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, vs));
       CK(cudaFuncSetAttribute(draft_sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, vs));
-      CK(cudaFuncSetAttribute(accept_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, vs));
+      CK(cudaFuncSetAttribute(accept_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(accept_smem(h.get()))));
       CK(cudaFuncSetAttribute(tree_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, vs));
       CK(cudaFuncSetAttribute(tree_accept_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, vs));
     }

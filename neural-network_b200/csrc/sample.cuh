@@ -169,11 +169,12 @@ __device__ void clear_request_rows(const SpecState &st, int b) {
 // (src/nn/layer.cpp:1639-1642, 1649-1653) into the next round's first draft
 // step computes the same cache and the same logits for the last row.  Returns
 // false (and flags the error) when the round would overflow a cache.
-__device__ bool start_round(const SpecState &st, int b, int catch_tok) {
-  const int M = min(st.k, st.max_new - st.n_new[b]);
-  int d = st.d_len[b];
+// start_round_at takes the request's n_new, d_len, t_len and last token as
+// read by the caller.
+__device__ bool start_round_at(const SpecState &st, int b, int catch_tok, int n_new, int d, int t_len, int last_tok) {
+  const int M = min(st.k, st.max_new - n_new);
   const int has_c = catch_tok >= 0 ? 1 : 0;
-  if (d + has_c + M > st.d_cap || st.t_len[b] + M + 1 > st.t_cap) {
+  if (d + has_c + M > st.d_cap || t_len + M + 1 > st.t_cap) {
     atomicOr(st.err, kErrSeqLen);
     st.active[b] = 0;
     clear_request_rows(st, b);
@@ -182,10 +183,13 @@ __device__ bool start_round(const SpecState &st, int b, int catch_tok) {
   if (has_c) set_row(st, st.rows.off_step0 + 2 * b, catch_tok, d++, b);
   else clear_row(st, st.rows.off_step0 + 2 * b);
   st.d_start[b] = d;
-  set_row(st, st.rows.off_step0 + 2 * b + 1, st.last_tok[b], d, b);
+  set_row(st, st.rows.off_step0 + 2 * b + 1, last_tok, d, b);
   st.d_len[b] = d + 1;
   st.M[b] = M;
   return true;
+}
+__device__ bool start_round(const SpecState &st, int b, int catch_tok) {
+  return start_round_at(st, b, catch_tok, st.n_new[b], st.d_len[b], st.t_len[b], st.last_tok[b]);
 }
 
 __device__ __forceinline__ void set_tree_row(const SpecState &st, int idx, int tok, int pos, int req, int slot, int tb,
@@ -428,8 +432,9 @@ __device__ void radix_cut(const float *srow, int V, bool by_mass, unsigned long 
 // unspecified).
 __device__ void probs_smem(float *srow, int V, float T, int top_k, float top_p, float *red, CutShared &cut) {
   float mx = -INFINITY, se = 0.f;
+  const bool t1 = T == 1.f;
   for (int v = threadIdx.x; v < V; v += blockDim.x) {
-    const float x = __fdiv_rn(srow[v], T);
+    const float x = t1 ? srow[v] : __fdiv_rn(srow[v], T);  // x / 1 is x
     srow[v] = x;
     if (x > mx) {
       se = se * expf(mx - x) + 1.f;
@@ -554,6 +559,8 @@ __device__ int sample_smem(const float *p, int V, double u, int mode, double *re
 }
 
 constexpr int kSampThreads = 1024;
+constexpr int kAcceptRows = 32;
+constexpr int kMaxLookahead = 32;  // largest draft length k the handle accepts  // verify rows whose normalisers accept_kernel finds in parallel
 
 struct SampShared {
   float red[32];
@@ -660,6 +667,17 @@ __global__ void __launch_bounds__(kSampThreads) draft_sample_kernel(SpecState st
     if (threadIdx.x == 0 && j + 1 < st.k) clear_row(st, step_row(st, j + 1, b));
     return;
   }
+  // the state the tail of thread 0 writes from, read up front (the earlier
+  // candidates only for the last step, which writes the verify rows)
+  __shared__ int s_cand[kMaxLookahead];
+  __shared__ int s_len[3];  // d_len, t_len, last_tok
+  int *cand = st.cand + b * st.kmax;
+  if (j == M - 1 && static_cast<int>(threadIdx.x) < j) s_cand[threadIdx.x] = cand[threadIdx.x];
+  if (threadIdx.x == 0) {
+    s_len[0] = st.d_len[b];
+    s_len[1] = st.t_len[b];
+    s_len[2] = st.last_tok[b];
+  }
   RngCtx rc = make_rng(sh);
   load_row(logits + static_cast<size_t>(b) * st.V, st.V, srow);
   int tok;
@@ -676,19 +694,18 @@ __global__ void __launch_bounds__(kSampThreads) draft_sample_kernel(SpecState st
   }
   pdl_launch();  // the next pass may launch while this block writes its rows
   if (threadIdx.x == 0) {
-    int *cand = st.cand + b * st.kmax;
     cand[j] = tok;
     if (j + 1 < M) {
-      const int d = st.d_len[b];
+      const int d = s_len[0];
       set_row(st, step_row(st, j + 1, b), tok, d, b);
       st.d_len[b] = d + 1;
     } else if (j + 1 < st.k) {
       clear_row(st, step_row(st, j + 1, b));
     }
     if (j == M - 1) {
-      const int t = st.t_len[b];
+      const int t = s_len[1];
       for (int i = 0; i <= st.k; ++i) {
-        if (i <= M) set_row(st, verify_row(st, b, i), i == 0 ? st.last_tok[b] : cand[i - 1], t + i, b);
+        if (i <= M) set_row(st, verify_row(st, b, i), i == 0 ? s_len[2] : i - 1 < j ? s_cand[i - 1] : tok, t + i, b);
         else clear_row(st, verify_row(st, b, i));
       }
       st.t_start[b] = t;
@@ -697,16 +714,125 @@ __global__ void __launch_bounds__(kSampThreads) draft_sample_kernel(SpecState st
   }
 }
 
+// Scratch of accept_kernel's unfiltered path: per verify row the get_probs
+// normalisers (or the argmax), warp partials, the candidates.
+struct AcceptShared {
+  float M[kAcceptRows], S[kAcceptRows], F[kAcceptRows];
+  int am[kAcceptRows];
+  int cand[kAcceptRows];
+  float wf[32];
+  int wi[32];
+  int rj;
+  int t_start, t_len, d_len, d_start, last_tok;  // thread 0's bookkeeping state
+};
+
+// x = l / T as get_probs forms it (x / 1 is x itself, so T = 1 skips the divide).
+__device__ __forceinline__ float scaled_logit(float l, float T, bool t1) { return t1 ? l : __fdiv_rn(l, T); }
+
+// Normalisers of the verify rows [r0, r0 + n) of one request: for sampling
+// the max of l/T, the exp-sum and the sum of the normalised values
+// (probs_smem's three reductions), for greedy the argmax.  The rows are
+// staged in shared memory (row r0 + i at srow + i * V) and a group of warps
+// works on each.
+__device__ void accept_row_stats(const SpecState &st, const float *lg0, int r0, int n, float *srow, AcceptShared &a) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const bool t1 = st.T == 1.f;
+  {
+    load_row(lg0 + static_cast<size_t>(r0) * st.V, n * st.V, srow);  // ends with a barrier
+    const int G = max(1, nw / n);  // warps past G * n only join the barriers
+    const int j = warp / G, gw = warp % G;
+    const bool mine = j < n;
+    const float *row = srow + static_cast<size_t>(mine ? j : 0) * st.V;
+    const int v0 = gw * 32 + lane, dv = G * 32;
+    if (st.greedy) {
+      ArgMax am{-INFINITY, 0x7fffffff};
+      if (mine)
+        for (int v = v0; v < st.V; v += dv) am = argmax_merge(am, ArgMax{row[v], v});
+      am = warp_argmax(am);
+      if (lane == 0) {
+        a.wf[warp] = am.v;
+        a.wi[warp] = am.i;
+      }
+      __syncthreads();
+      if (mine && gw == 0 && lane == 0) {
+        for (int w = 1; w < G; ++w) am = argmax_merge(am, ArgMax{a.wf[warp + w], a.wi[warp + w]});
+        a.am[r0 + j] = am.i == 0x7fffffff ? 0 : am.i;
+      }
+    } else {
+      // probs_smem's online max / exp-sum, reduced over the row's warps
+      float mx = -INFINITY, se = 0.f;
+      if (mine)
+        for (int v = v0; v < st.V; v += dv) {
+          const float x = scaled_logit(row[v], st.T, t1);
+          if (x > mx) {
+            se = se * expf(mx - x) + 1.f;
+            mx = x;
+          } else {
+            se += expf(x - mx);
+          }
+        }
+      float r = warp_max(mx);
+      if (lane == 0) a.wf[warp] = r;
+      __syncthreads();
+      float Mx = -INFINITY;
+      if (mine)
+        for (int w = 0; w < G; ++w) Mx = fmaxf(Mx, a.wf[j * G + w]);
+      __syncthreads();
+      r = warp_sum(mx == -INFINITY ? 0.f : se * expf(mx - Mx));
+      if (lane == 0) a.wf[warp] = r;
+      __syncthreads();
+      float S = 0.f;
+      if (mine)
+        for (int w = 0; w < G; ++w) S += a.wf[j * G + w];
+      __syncthreads();
+      float fs = 0.f;
+      if (mine)
+        for (int v = v0; v < st.V; v += dv) fs += __fdiv_rn(expf(__fsub_rn(scaled_logit(row[v], st.T, t1), Mx)), S);
+      r = warp_sum(fs);
+      if (lane == 0) a.wf[warp] = r;
+      __syncthreads();
+      if (mine && gw == 0 && lane == 0) {
+        float F = 0.f;
+        for (int w = 0; w < G; ++w) F += a.wf[j * G + w];
+        a.M[r0 + j] = Mx;
+        a.S[r0 + j] = S;
+        a.F[r0 + j] = F;
+      }
+    }
+    __syncthreads();
+  }
+}
+
 // Acceptance, residual / bonus sample and rollback for one request
 // (src/nn/layer.cpp:1581-1655).  Rollback is a length reset: the cache slots
 // past the new length are simply overwritten by later rows.  Ends by writing
 // the next round's draft step 0 rows.
-__global__ void __launch_bounds__(kSampThreads) accept_kernel(SpecState st, const float *__restrict__ logits) {
+//
+// Without top-k / top-p, get_probs of a row is fixed by its three normalisers.
+// The verify rows are staged in shared memory `stage_rows` at a time; the
+// normalisers of a staged chunk are found together (accept_row_stats), its
+// acceptance tests need p at one token each and run in parallel, one lane
+// per test (test j draws the j-th uniform of the round, as the sequential
+// walk does when tests 0 .. j-1 accept), and the walk ends at the chunk with
+// the first rejection.  Only the row a token is drawn from gets a full pass.
+// With a filter the rows are walked one by one through probs_smem.
+__global__ void __launch_bounds__(kSampThreads) accept_kernel(SpecState st, const float *__restrict__ logits,
+                                                               int stage_rows) {
   pdl_wait();
   __shared__ SampShared sh;
-  extern __shared__ float srow[];  // [V]
+  __shared__ AcceptShared ash;
+  extern __shared__ float srow[];  // [V], or stage_rows rows of V on the unfiltered path
   const int b = blockIdx.x;
   if (!st.active[b]) return;
+  // thread 0's bookkeeping state, read up front so that its tail does not
+  // wait on a chain of loads
+  if (threadIdx.x == 0) {
+    ash.t_start = st.t_start[b];
+    ash.t_len = st.t_len[b];
+    ash.d_len = st.d_len[b];
+    ash.d_start = st.d_start[b];
+    ash.last_tok = st.last_tok[b];
+  }
   RngCtx rc = make_rng(sh);
   const int M = st.M[b];
   const int W = st.k + 1;
@@ -717,31 +843,83 @@ __global__ void __launch_bounds__(kSampThreads) accept_kernel(SpecState st, cons
 
   const int n0 = st.n_new[b];
   int rj = -1, am_rj = 0, naccept = 0;
-  for (int j = 0; j < M; ++j) {
-    const int c = cand[j];
-    load_row(lg0 + static_cast<size_t>(j) * st.V, st.V, srow);
-    bool acc;
-    if (st.greedy) {
-      const int am = argmax_smem(srow, st.V, sh.redv, sh.redi);
-      acc = (c == am);
-      am_rj = am;
-    } else {
-      probs_smem(srow, st.V, st.T, st.top_k, st.top_p, sh.red, sh.cut);
-      if (threadIdx.x == 0) {
-        const float qv = st.q[(static_cast<size_t>(b) * st.kmax + j) * st.V + c];
-        const float pv = srow[c];
-        const float r = draw_accept_u(st, b, round, st.k + j, rc);
-        sh.flag = (__fmul_rn(r, qv) < pv) ? 1 : 0;
+  const bool filtered = (st.top_k > 0 && st.top_k < st.V) || (st.top_p > 0.f && st.top_p < 1.f);
+  const bool fast = !filtered && M + 1 <= kAcceptRows;
+  if (fast) {
+    // chunks of staged rows; the walk stops at the chunk with the first rejection
+    int r0 = 0;
+    for (;; r0 += stage_rows) {
+      const int n = min(stage_rows, M + 1 - r0);
+      accept_row_stats(st, lg0, r0, n, srow, ash);
+      if (threadIdx.x < 32) {
+        const int j = r0 + threadIdx.x;
+        bool acc = true;
+        if (j < min(M, r0 + n)) {
+          const int c = cand[j];
+          ash.cand[j] = c;
+          if (st.greedy) {
+            acc = c == ash.am[j];
+          } else {
+            const float x = scaled_logit(__ldg(lg0 + static_cast<size_t>(j) * st.V + c), st.T, st.T == 1.f);
+            const float pv = __fdiv_rn(__fdiv_rn(expf(__fsub_rn(x, ash.M[j])), ash.S[j]), ash.F[j]);
+            const float qv = st.q[(static_cast<size_t>(b) * st.kmax + j) * st.V + c];
+            const float r = st.rng_mode == 0 ? canon_f32(rc.win[j]) : static_cast<float>(table_u(st, b, round, st.k + j));
+            acc = __fmul_rn(r, qv) < pv;
+          }
+        }
+        const unsigned rej = __ballot_sync(0xffffffffu, !acc);
+        if (threadIdx.x == 0) {
+          ash.rj = rej ? r0 + __ffs(rej) - 1 : -1;
+          if (!st.greedy) *rc.used = rej ? r0 + __ffs(rej) : M;  // uniforms the tests consumed
+        }
       }
       __syncthreads();
-      acc = sh.flag != 0;
+      rj = ash.rj;
+      if (rj >= 0 || r0 + n > M) break;
+    }
+    naccept = rj >= 0 ? rj : M;
+    const int row = rj >= 0 ? rj : M;
+    if (st.greedy) {
+      am_rj = ash.am[row];
+    } else if (rj >= 0 || n0 + naccept < st.max_new) {
+      // p of the row the token is drawn from, as probs_smem leaves it (the
+      // last chunk staged holds that row)
+      const float *src = srow + static_cast<size_t>(row - r0) * st.V;
+      const float Mr = ash.M[row], Sr = ash.S[row], Fr = ash.F[row];
+      const bool t1 = st.T == 1.f;
+      for (int v = threadIdx.x; v < st.V; v += blockDim.x)
+        srow[v] = __fdiv_rn(__fdiv_rn(expf(__fsub_rn(scaled_logit(src[v], st.T, t1), Mr)), Sr), Fr);
       __syncthreads();
     }
-    if (!acc) {
-      rj = j;
-      break;
+  } else {
+    for (int j = 0; j < M; ++j) {
+      const int c = cand[j];
+      load_row(lg0 + static_cast<size_t>(j) * st.V, st.V, srow);
+      bool acc;
+      if (st.greedy) {
+        const int am = argmax_smem(srow, st.V, sh.redv, sh.redi);
+        acc = (c == am);
+        am_rj = am;
+      } else {
+        probs_smem(srow, st.V, st.T, st.top_k, st.top_p, sh.red, sh.cut);
+        if (threadIdx.x == 0) {
+          const float qv = st.q[(static_cast<size_t>(b) * st.kmax + j) * st.V + c];
+          const float pv = srow[c];
+          const float r = draw_accept_u(st, b, round, st.k + j, rc);
+          sh.flag = (__fmul_rn(r, qv) < pv) ? 1 : 0;
+        }
+        __syncthreads();
+        acc = sh.flag != 0;
+        __syncthreads();
+      }
+      if (!acc) {
+        rj = j;
+        break;
+      }
+      ++naccept;
     }
-    ++naccept;
+    if (threadIdx.x == 0)
+      for (int j = 0; j < min(M, kAcceptRows); ++j) ash.cand[j] = cand[j];
   }
 
   int out_tok = -1;
@@ -749,7 +927,8 @@ __global__ void __launch_bounds__(kSampThreads) accept_kernel(SpecState st, cons
     if (st.greedy) {
       out_tok = am_rj;
     } else {
-      // residual max(0, p - q), renormalised; p itself when the residual is empty
+      // residual max(0, p - q), renormalised; p itself when the residual is
+      // empty (srow holds p of row rj)
       const float *q = st.q + (static_cast<size_t>(b) * st.kmax + rj) * st.V;
       float s = 0.f;
       for (int v = threadIdx.x; v < st.V; v += blockDim.x) {
@@ -770,11 +949,12 @@ __global__ void __launch_bounds__(kSampThreads) accept_kernel(SpecState st, cons
       out_tok = sample_smem(srow, st.V, sh.u, st.rng_mode, sh.redd, sh.redi);
     }
   } else if (n0 + naccept < st.max_new) {
-    load_row(lg0 + static_cast<size_t>(M) * st.V, st.V, srow);
+    // bonus token from row M (the unfiltered path has its argmax, or its p in srow)
+    if (!fast) load_row(lg0 + static_cast<size_t>(M) * st.V, st.V, srow);
     if (st.greedy) {
-      out_tok = argmax_smem(srow, st.V, sh.redv, sh.redi);
+      out_tok = fast ? am_rj : argmax_smem(srow, st.V, sh.redv, sh.redi);
     } else {
-      probs_smem(srow, st.V, st.T, st.top_k, st.top_p, sh.red, sh.cut);
+      if (!fast) probs_smem(srow, st.V, st.T, st.top_k, st.top_p, sh.red, sh.cut);
       if (threadIdx.x == 0) sh.u = draw_sample_u(st, b, round, 2 * st.k, rc);
       __syncthreads();
       out_tok = sample_smem(srow, st.V, sh.u, st.rng_mode, sh.redd, sh.redi);
@@ -783,29 +963,43 @@ __global__ void __launch_bounds__(kSampThreads) accept_kernel(SpecState st, cons
   if (!st.greedy) rng_commit(st, b, rc);
   pdl_launch();  // the next pass may launch while this block writes its rows
   if (threadIdx.x == 0) {
-    for (int j = 0; j < naccept; ++j) emit(st, b, cand[j]);
+    int t_len = ash.t_len, d_len = ash.d_len, last_tok = ash.last_tok;
+    const int t_start = ash.t_start, d_start = ash.d_start;
+    int n = n0;
+    const int cap = st.out_len - st.prompt_len;
+    int *out = st.tokens_out + static_cast<size_t>(b) * st.out_len + st.prompt_len;
+    auto put = [&](int tok) {
+      if (n < cap) out[n] = tok;
+      ++n;
+    };
+    for (int j = 0; j < naccept; ++j) put(j < kAcceptRows ? ash.cand[j] : cand[j]);
     int catch_tok = -1;
+    const int last_c = M > 0 ? (M - 1 < kAcceptRows ? ash.cand[M - 1] : cand[M - 1]) : -1;
     if (rj >= 0) {
-      emit(st, b, out_tok);
-      st.t_len[b] = st.t_start[b] + rj + 1;
-      st.d_len[b] = min(st.d_len[b], st.d_start[b] + rj + 1);
+      put(out_tok);
+      t_len = t_start + rj + 1;
+      d_len = min(d_len, d_start + rj + 1);
       catch_tok = (st.catchup == 0) ? out_tok : -1;
-      st.last_tok[b] = out_tok;
+      last_tok = out_tok;
     } else if (out_tok >= 0) {
-      emit(st, b, out_tok);
-      catch_tok = cand[M - 1];
-      st.last_tok[b] = out_tok;
-    } else {
-      st.last_tok[b] = M > 0 ? cand[M - 1] : st.last_tok[b];
+      put(out_tok);
+      catch_tok = last_c;
+      last_tok = out_tok;
+    } else if (M > 0) {
+      last_tok = last_c;
     }
-    long long *sx = st.stats + 4 * b;
-    sx[0] += 1;
-    sx[1] += M;
-    sx[2] += naccept;
-    sx[3] += (rj >= 0) ? 1 : 0;
+    st.n_new[b] = n;
+    st.t_len[b] = t_len;
+    st.d_len[b] = d_len;
+    st.last_tok[b] = last_tok;
+    unsigned long long *sx = reinterpret_cast<unsigned long long *>(st.stats + 4 * b);
+    atomicAdd(sx + 0, 1ull);
+    atomicAdd(sx + 1, static_cast<unsigned long long>(M));
+    atomicAdd(sx + 2, static_cast<unsigned long long>(naccept));
+    if (rj >= 0) atomicAdd(sx + 3, 1ull);
     st.round[b] = round + 1;
-    bool still = st.n_new[b] < st.max_new;
-    if (still) still = start_round(st, b, catch_tok);
+    bool still = n < st.max_new;
+    if (still) still = start_round_at(st, b, catch_tok, n, d_len, t_len, last_tok);
     else clear_request_rows(st, b);
     st.active[b] = still ? 1 : 0;
     if (still) atomicAdd(st.active_count, 1);
