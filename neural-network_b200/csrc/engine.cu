@@ -1013,6 +1013,12 @@ TreeCfg make_tree(const specdec_handle *h, const specdec_tree *t) {
 
 int samp_threads(const specdec_handle *h) { return h->tgt.dm.V <= 4096 ? 512 : kSampThreads; }
 size_t samp_smem(const specdec_handle *h) { return static_cast<size_t>(h->tgt.dm.V) * sizeof(float); }
+// Draft sampling after draft step j (one block per request).
+void launch_draft_sample(specdec_handle *h, const SpecState &st, int j) {
+  launch_pdl(h, draft_sample_kernel, dim3(st.B), dim3(samp_threads(h)), samp_smem(h), st, j,
+             static_cast<const float *>(h->logits));
+}
+
 // Verify rows accept_kernel stages in shared memory at a time (at least one).
 constexpr size_t kAcceptStageBytes = 200 * 1024;
 int accept_stage_rows(const specdec_handle *h) {
@@ -1067,12 +1073,11 @@ void enqueue_round(specdec_handle *h) {
     return;
   }
   const int B = st.B, k = st.k;
-  const dim3 sb(samp_threads(h));
   forward_rows(h, false, st.rows.off_step0, 2 * B, 2, h->sel_odd, B, h->logits);
-  launch_pdl(h, draft_sample_kernel, dim3(B), sb, samp_smem(h), st, 0, static_cast<const float *>(h->logits));
+  launch_draft_sample(h, st, 0);
   for (int j = 1; j < k; ++j) {
     forward_rows(h, false, st.rows.off_step1 + (j - 1) * B, B, 1, nullptr, B, h->logits);
-    launch_pdl(h, draft_sample_kernel, dim3(B), sb, samp_smem(h), st, j, static_cast<const float *>(h->logits));
+    launch_draft_sample(h, st, j);
   }
   forward_rows(h, true, st.rows.off_verify, B * (k + 1), k + 1, nullptr, B * (k + 1), h->logits);
   launch_pdl(h, accept_kernel, dim3(B), dim3(kSampThreads), accept_smem(h), st, static_cast<const float *>(h->logits),

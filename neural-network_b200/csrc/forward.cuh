@@ -764,11 +764,13 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
   const int hk = h / (a.H / a.Hkv);
   const float scale = sqrtf(static_cast<float>(D));
   __shared__ int s_meta[2];
-  // Thread 0 reads the queries' rows, then issues the first tile while the
-  // other threads fetch the query vectors.
+  // The splits share the positions the group's queries see (0 .. maxpos), so
+  // every split has work while the cache is shorter than its capacity; a
+  // split never exceeds a.chunk positions (the staging the host sized).
   auto span = [&](int maxpos, int &j0, int &j1) {
-    j0 = split * a.chunk;
-    j1 = min(maxpos + 1, j0 + a.chunk);
+    const int ch = min(a.chunk, (maxpos + a.nsplit) / a.nsplit);
+    j0 = split * ch;
+    j1 = min(maxpos + 1, j0 + ch);
     return (j1 > j0) ? (j1 - j0 + kTile - 1) / kTile : 0;
   };
   auto issue = [&](int t, int row0, int j0) {  // thread 0 only
@@ -786,6 +788,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
       tma_load_2d(vdst + cb * kTile * G::kBoxBytes, &a.tmv, cb * G::kBoxCols, y, &bars[s]);
     }
   };
+  // Thread 0 reads the queries' rows, then issues the first tile while the
+  // other threads fetch the query vectors.
   if (threadIdx.x == 0) {
     int rr[QT], pr[QT];
 #pragma unroll

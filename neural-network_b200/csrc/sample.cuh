@@ -242,9 +242,12 @@ struct RngCtx {
   uint32_t *old_s, *new_s;  // shared [624] each
   uint32_t *win;            // shared window
   int *used;                // shared counter
+  int *twisted;             // shared: new_s holds the regenerated state
 };
 
 // Prepares `need` consecutive tempered words of request b's stream in `win`.
+// mt_idx = 624 (fresh seed, or every word of the state drawn) regenerates the
+// state before the first word, as std::mt19937 does on its next draw.
 __device__ void rng_prepare(const SpecState &st, int b, int need, RngCtx &c) {
   if (st.rng_mode != 0) return;
   const int idx = st.mt_idx[b];
@@ -259,7 +262,10 @@ __device__ void rng_prepare(const SpecState &st, int b, int need, RngCtx &c) {
     for (int t = threadIdx.x; t < need; t += blockDim.x)
       c.win[t] = mt_temper(t < rem ? c.old_s[idx + t] : c.new_s[t - rem]);
   }
-  if (threadIdx.x == 0) *c.used = 0;
+  if (threadIdx.x == 0) {
+    *c.used = 0;
+    *c.twisted = idx + need > kMtN ? 1 : 0;
+  }
   __syncthreads();
 }
 
@@ -267,12 +273,14 @@ __device__ void rng_commit(const SpecState &st, int b, RngCtx &c) {
   if (st.rng_mode != 0) return;
   __syncthreads();
   const int idx = st.mt_idx[b] + *c.used;
+  const bool wrap = idx >= kMtN && *c.twisted;  // the draws reached the regenerated state
   __syncthreads();
-  if (idx >= kMtN) {
+  if (wrap) {
     uint32_t *g = st.mt + static_cast<size_t>(b) * kMtN;
     for (int t = threadIdx.x; t < kMtN; t += blockDim.x) g[t] = c.new_s[t];
   }
-  if (threadIdx.x == 0) st.mt_idx[b] = idx >= kMtN ? idx - kMtN : idx;
+  // without a regeneration the index stops at 624 at most (state used up)
+  if (threadIdx.x == 0) st.mt_idx[b] = wrap ? idx - kMtN : idx;
 }
 
 __device__ __forceinline__ double table_u(const SpecState &st, int b, int round, int slot) {
@@ -559,8 +567,8 @@ __device__ int sample_smem(const float *p, int V, double u, int mode, double *re
 }
 
 constexpr int kSampThreads = 1024;
-constexpr int kAcceptRows = 32;
-constexpr int kMaxLookahead = 32;  // largest draft length k the handle accepts  // verify rows whose normalisers accept_kernel finds in parallel
+constexpr int kAcceptRows = 32;    // verify rows whose normalisers accept_kernel finds in parallel
+constexpr int kMaxLookahead = 32;  // largest draft length k the handle accepts
 
 struct SampShared {
   float red[32];
@@ -570,13 +578,15 @@ struct SampShared {
   uint32_t old_s[kMtN];
   uint32_t new_s[kMtN];
   uint32_t win[40];
-  int used;
+  int used, twisted;
   double u;
   int flag;
   CutShared cut;
 };
 
-__device__ __forceinline__ RngCtx make_rng(SampShared &s) { return RngCtx{s.old_s, s.new_s, s.win, &s.used}; }
+__device__ __forceinline__ RngCtx make_rng(SampShared &s) {
+  return RngCtx{s.old_s, s.new_s, s.win, &s.used, &s.twisted};
+}
 
 __device__ __forceinline__ void emit(const SpecState &st, int b, int tok) {
   const int n = st.n_new[b];

@@ -49,6 +49,20 @@ def test_forward_logits_bf16(gpu_lib, oracle_built):
     assert rel_err(g, o) < BF16_REL
 
 
+@pytest.mark.parametrize("name", ["tiny8", "small", "cfg1"])
+@pytest.mark.parametrize("int8", [False, True])
+def test_forward_logits_short(gpu_lib, oracle_built, name, int8):
+    # short inputs, down to a single token
+    shape, dl = SHAPES[name]
+    pair = make_pair(shape, dl, seed=12, int8=int8, max_prompt_len=40)
+    for S in (1, 5, 16):
+        toks = make_prompts(1, S, shape.vocab, seed=20 + S)[0]
+        for role, om in ((sd.TARGET, pair.target), (sd.DRAFT, pair.draft)):
+            g = pair.engine.forward_logits(role, toks)
+            o = om.forward(toks)
+            assert rel_err(g, o) < FP32_REL, (name, S, role, rel_err(g, o))
+
+
 def test_forward_logits_cfg_arch(gpu_lib, oracle_built):
     shape = ModelShape(vocab=300, d_model=64, n_heads=4, d_ff=128, n_layers=3, max_seq_len=64, arch=ARCH_CFG)
     pair = make_pair(shape, 1, seed=5, max_prompt_len=40)
@@ -76,6 +90,16 @@ def test_sampled_mt19937(gpu_lib, oracle_built, name, T):
     pair = make_pair(shape, dl, seed=7, max_batch=4, max_prompt_len=40)
     _, tg, sg, to, so, mg = run_both(pair, 3, 10, 48, 3, T, seed=123)
     exact, ties = compare_tokens(tg, to, mg, 10, greedy=False)
+    assert exact + ties == 3 and ties <= 1
+
+
+def test_sampled_mt19937_long(gpu_lib, oracle_built):
+    # enough draws that every request's MT19937 state is regenerated several
+    # times, including draws that end exactly on the state's last word
+    shape, dl = SHAPES["small"]
+    pair = make_pair(shape, dl, seed=13, max_batch=4, max_prompt_len=40)
+    _, tg, sg, to, so, mg = run_both(pair, 3, 8, 140, 3, 1.0, seed=77)
+    exact, ties = compare_tokens(tg, to, mg, 8, greedy=False)
     assert exact + ties == 3 and ties <= 1
 
 
