@@ -133,6 +133,27 @@ int specdec_generate_device(specdec_handle *h, const specdec_gen_params *p,
                             const int32_t *d_prompts, int B, int S,
                             int32_t *d_out_tokens, int64_t *d_out_stats);
 
+/* Replaces TransformerDecoder::generate_advanced with use_kv_cache = true
+ * (src/nn/layer.cpp:1239-1380) for B independent requests: target only (the
+ * draft need not be loaded), one token per request and step.  Greedy when
+ * temperature <= 0 (first maximum); else get_probs (temperature, top_k,
+ * top_p) and one draw per token from request b's mt19937(seed + b) stream,
+ * or from u[b][step][0] of a host table with uniform_rounds >= max_new_tokens
+ * rows of one slot.  lookahead and draft_catchup are not used.  prompts
+ * [B][S] and out_tokens [B][S + max_new_tokens] are HOST buffers;
+ * out_stats (optional) [B][4] = steps, 0, 0, 0.  The cache ends at
+ * S + max_new_tokens - 1 positions (SPECDEC_ERR_SEQ_LEN beyond the target's
+ * max_seq_len, as src/nn/layer.cpp:1176-1179 throws). */
+int specdec_generate_ar(specdec_handle *h, const specdec_gen_params *p,
+                        const int32_t *prompts, int B, int S,
+                        int32_t *out_tokens, int64_t *out_stats);
+
+/* specdec_generate_ar on DEVICE buffers, enqueued on specdec_stream(h)
+ * (nothing synchronised).  out_tokens [B][S + max(1, max_new_tokens)]. */
+int specdec_generate_ar_device(specdec_handle *h, const specdec_gen_params *p,
+                               const int32_t *d_prompts, int B, int S,
+                               int32_t *d_out_tokens, int64_t *d_out_stats);
+
 /* The CUDA stream (cudaStream_t) every kernel of this handle runs on. */
 void *specdec_stream(specdec_handle *h);
 

@@ -218,6 +218,7 @@ struct specdec_handle {
   int64_t graph_fixed = 0, graph_body = 0, extra_launches = 0;
   bool use_graph = true;
   bool use_pdl = true;  // programmatic dependent launch for the kernels that support it
+  int gemm_max_split = 1;  // largest split-K cluster of the tensor-core GEMM
 
   void *dalloc(size_t bytes, std::vector<void *> *owner = nullptr) {
     void *p = nullptr;
@@ -657,8 +658,18 @@ bool try_launch_gemm(specdec_handle *h, LinearArgs a) {
   a.norm_out = nullptr;
   g.lin = a;
   g.err = h->st.err;
-  launch(h, gemm_kernel<EPI>, dim3((a.N + kBN - 1) / kBN, (a.R + kBM - 1) / kBM), dim3(kGemmThreads),
-         static_cast<size_t>(kGemmSmem), g);
+  // split-K while the tiles leave most SMs idle: a power of two up to the
+  // largest cluster the device schedules, each split keeping one k-block at least
+  const int gx = (a.N + kBN - 1) / kBN, gy = (a.R + kBM - 1) / kBM;
+  const int nk = (a.K + kBK - 1) / kBK;
+  int ks = 1;
+  while (2 * ks <= h->gemm_max_split && gx * gy * 2 * ks <= h->num_sms && 2 * ks <= nk) ks *= 2;
+  g.ksplit = ks;
+  if (ks == 1)
+    launch(h, gemm_kernel<EPI>, dim3(gx, gy), dim3(kGemmThreads), static_cast<size_t>(kGemmSmem), g);
+  else
+    launch_ex(h, false, gemm_kernel<EPI>, dim3(gx, gy, ks), dim3(kGemmThreads), static_cast<size_t>(kGemmSmem),
+              dim3(1, 1, ks), g);
   return true;
 }
 
@@ -701,12 +712,31 @@ void set_linear_attr_epi() {
   set_linear_attr_nc<EPI, 2>();
   set_linear_attr_nc<EPI, 4>();
 }
-void set_gemm_attrs() {
+// Returns the largest split-K cluster (1, 2, 4 or 8 CTAs of kGemmSmem bytes)
+// the device can schedule.
+int set_gemm_attrs() {
   CK(cudaFuncSetAttribute(gemm_kernel<kEpiStore>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
   CK(cudaFuncSetAttribute(gemm_kernel<kEpiResid>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
   CK(cudaFuncSetAttribute(gemm_kernel<kEpiQKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
   CK(cudaFuncSetAttribute(gemm_kernel<kEpiSwiGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
   CK(cudaFuncSetAttribute(gemm_kernel<kEpiGelu>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
+  for (int ks = kGemmMaxSplit; ks > 1; ks /= 2) {
+    cudaLaunchConfig_t lc{};
+    lc.gridDim = dim3(1, 1, ks);
+    lc.blockDim = dim3(kGemmThreads);
+    lc.dynamicSmemBytes = kGemmSmem;
+    cudaLaunchAttribute at{};
+    at.id = cudaLaunchAttributeClusterDimension;
+    at.val.clusterDim.x = 1;
+    at.val.clusterDim.y = 1;
+    at.val.clusterDim.z = ks;
+    lc.attrs = &at;
+    lc.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_kernel<kEpiResid>, &lc) == cudaSuccess && n > 0) return ks;
+    cudaGetLastError();
+  }
+  return 1;
 }
 void set_linear_attrs() {
   set_linear_attr_epi<kEpiStore>();
@@ -968,18 +998,21 @@ namespace {
 
 void sync_check(specdec_handle *h) { CK(cudaStreamSynchronize(h->stream)); }
 
-void validate_gen(specdec_handle *h, const specdec_gen_params *p, int B, int S, const TreeCfg *tree) {
+void validate_gen(specdec_handle *h, const specdec_gen_params *p, int B, int S, const TreeCfg *tree, bool ar) {
   if (!p) fail(SPECDEC_ERR_INVALID, "null params");
-  if (!h->tgt.loaded || !h->dft.loaded) fail(SPECDEC_ERR_STATE, "target and draft weights must be loaded first");
+  if (ar ? !h->tgt.loaded : (!h->tgt.loaded || !h->dft.loaded))
+    fail(SPECDEC_ERR_STATE, ar ? "target weights must be loaded first" : "target and draft weights must be loaded first");
   if (B < 1 || B > h->cfg.max_batch) fail(SPECDEC_ERR_INVALID, "batch out of range");
   if (S < 1 || S > h->cfg.max_prompt_len) fail(SPECDEC_ERR_INVALID, "prompt length out of range");
-  if (!tree && (p->lookahead < 1 || p->lookahead > h->cfg.max_lookahead))
+  if (!tree && !ar && (p->lookahead < 1 || p->lookahead > h->cfg.max_lookahead))
     fail(SPECDEC_ERR_INVALID, "lookahead out of range");
   if (p->max_new_tokens < 0) fail(SPECDEC_ERR_INVALID, "max_new_tokens < 0");
   // The target cache ends at S + max_new positions (every round verifies
   // M = min(k, remaining) drafts); the reference throws when that exceeds
-  // max_seq_len (src/nn/layer.cpp:1176-1179).
-  if (S + (p->max_new_tokens > 1 ? p->max_new_tokens : 0) > h->t_cap)
+  // max_seq_len (src/nn/layer.cpp:1176-1179).  Autoregressive decoding never
+  // feeds its last token: S + max_new - 1 positions.
+  const int cache_end = S + (ar ? std::max(0, p->max_new_tokens - 1) : (p->max_new_tokens > 1 ? p->max_new_tokens : 0));
+  if (cache_end > h->t_cap)
     fail(SPECDEC_ERR_SEQ_LEN, "Sequence length S plus past cached length exceeds max_seq_len");
   if (!(p->top_p == p->top_p)) fail(SPECDEC_ERR_INVALID, "top_p is NaN");
   if (p->rng_mode == SPECDEC_RNG_HOST_UNIFORM && p->temperature > 0.f) {
@@ -987,7 +1020,7 @@ void validate_gen(specdec_handle *h, const specdec_gen_params *p, int B, int S, 
   } else if (p->rng_mode != SPECDEC_RNG_MT19937 && p->rng_mode != SPECDEC_RNG_HOST_UNIFORM) {
     fail(SPECDEC_ERR_INVALID, "unknown rng_mode");
   }
-  if (!tree && p->draft_catchup != SPECDEC_CATCHUP_REF && p->draft_catchup != SPECDEC_CATCHUP_CORRECT)
+  if (!tree && !ar && p->draft_catchup != SPECDEC_CATCHUP_REF && p->draft_catchup != SPECDEC_CATCHUP_CORRECT)
     fail(SPECDEC_ERR_INVALID, "unknown draft_catchup");
 }
 
@@ -1072,6 +1105,12 @@ void enqueue_round(specdec_handle *h) {
     enqueue_tree_round(h);
     return;
   }
+  if (st.ar) {  // one target row per request: the last token at the next position
+    forward_rows(h, true, st.rows.off_verify, st.B, 1, nullptr, st.B, h->logits);
+    launch_pdl(h, ar_token_kernel, dim3(st.B), dim3(samp_threads(h)), samp_smem(h), st,
+               static_cast<const float *>(h->logits));
+    return;
+  }
   const int B = st.B, k = st.k;
   forward_rows(h, false, st.rows.off_step0, 2 * B, 2, h->sel_odd, B, h->logits);
   launch_draft_sample(h, st, 0);
@@ -1084,10 +1123,11 @@ void enqueue_round(specdec_handle *h) {
              accept_stage_rows(h));
 }
 
-void setup_state(specdec_handle *h, const specdec_gen_params *p, int B, int S, const TreeCfg *tree) {
+void setup_state(specdec_handle *h, const specdec_gen_params *p, int B, int S, const TreeCfg *tree, bool ar) {
   SpecState &st = h->st;
   st.B = B;
-  st.k = p->lookahead;
+  st.k = ar ? 0 : p->lookahead;
+  st.ar = ar ? 1 : 0;
   st.kmax = h->cfg.max_lookahead;
   st.V = h->tgt.dm.V;
   st.max_new = p->max_new_tokens;
@@ -1101,7 +1141,7 @@ void setup_state(specdec_handle *h, const specdec_gen_params *p, int B, int S, c
   st.catchup = p->draft_catchup;
   st.t_cap = h->t_cap;
   st.d_cap = h->d_cap;
-  st.u_slots = 2 * p->lookahead + 1;
+  st.u_slots = ar ? 1 : 2 * p->lookahead + 1;
   st.u_rounds = p->uniform_rounds;
   st.uniforms = h->d_uniforms;
   // row regions: [prefill R_max][step0 2B][steps 1..k-1: B each][verify B(k+1)]
@@ -1132,7 +1172,7 @@ void enqueue_prologue(specdec_handle *h, int B, int S, uint32_t seed) {
   launch(h, init_state_kernel, dim3(B), dim3(128), 0, st, static_cast<const int *>(h->d_prompts), S);
   if (!st.greedy && st.rng_mode == 0) launch(h, mt_seed_kernel, dim3((B + 127) / 128), dim3(128), 0, st.mt, st.mt_idx, seed, B);
   const int chunk = std::max(1, std::min(S, h->R_max / B));
-  for (int pass = 0; pass < 2; ++pass) {
+  for (int pass = 0; pass < (st.ar ? 1 : 2); ++pass) {
     const bool target = pass == 0;
     for (int c0 = 0; c0 < S; c0 += chunk) {
       const int clen = std::min(chunk, S - c0);
@@ -1144,7 +1184,11 @@ void enqueue_prologue(specdec_handle *h, int B, int S, uint32_t seed) {
       forward_rows(h, target, 0, R, clen, h->sel_prefill, B, (target && last) ? h->logits : nullptr);
     }
   }
-  launch_pdl(h, first_token_kernel, dim3(B), dim3(samp_threads(h)), samp_smem(h), st, static_cast<const float *>(h->logits));
+  if (st.ar)
+    launch_pdl(h, ar_token_kernel, dim3(B), dim3(samp_threads(h)), samp_smem(h), st, static_cast<const float *>(h->logits));
+  else
+    launch_pdl(h, first_token_kernel, dim3(B), dim3(samp_threads(h)), samp_smem(h), st,
+               static_cast<const float *>(h->logits));
 }
 
 void destroy_graphs(specdec_handle *h) {
@@ -1210,10 +1254,17 @@ GraphEntry build_graph(specdec_handle *h, int B, int S, uint32_t seed, int max_i
 // d_prompts may be any device buffer; it is staged into the handle's prompt
 // buffer so captured graphs stay valid across calls.
 int generate_impl(specdec_handle *h, const specdec_gen_params *p, const int32_t *d_prompts, int B, int S, int32_t *d_out,
-                  int64_t *d_stats_out, const TreeCfg *tree = nullptr) {
-  validate_gen(h, p, B, S, tree);
+                  int64_t *d_stats_out, const TreeCfg *tree = nullptr, bool ar = false) {
+  validate_gen(h, p, B, S, tree, ar);
   SpecState &st = h->st;
-  setup_state(h, p, B, S, tree);
+  if (ar && p->max_new_tokens == 0) {  // generate_advanced returns the prompt
+    CK(cudaMemcpyAsync(d_out, d_prompts, static_cast<size_t>(B) * S * sizeof(int), cudaMemcpyDeviceToDevice, h->stream));
+    if (d_stats_out) CK(cudaMemsetAsync(d_stats_out, 0, static_cast<size_t>(B) * 4 * sizeof(int64_t), h->stream));
+    CK(cudaMemsetAsync(st.err, 0, sizeof(int), h->stream));
+    h->launches = 0;
+    return SPECDEC_OK;
+  }
+  setup_state(h, p, B, S, tree, ar);
   if (d_prompts != h->d_prompts)
     CK(cudaMemcpyAsync(h->d_prompts, d_prompts, static_cast<size_t>(B) * S * sizeof(int), cudaMemcpyDeviceToDevice,
                        h->stream));
@@ -1237,7 +1288,8 @@ int generate_impl(specdec_handle *h, const specdec_gen_params *p, const int32_t 
   const int max_iters = std::max(2, p->max_new_tokens + 2);
 
   if (h->use_graph) {
-    GraphKey key{B, S, p->lookahead, st.greedy, table ? 1 : 0, p->draft_catchup, p->max_new_tokens,
+    // autoregressive graphs have k = 0 (speculative ones k >= 1)
+    GraphKey key{B, S, st.k, st.greedy, table ? 1 : 0, ar ? 0 : p->draft_catchup, p->max_new_tokens,
                  table ? p->uniform_rounds : 0, p->temperature, (!st.greedy && !table) ? p->seed : 0u,
                  st.greedy ? 0 : p->top_k, st.greedy ? 1.f : p->top_p, tree ? tree->sig() : 0ull};
     auto it = h->graphs.find(key);
@@ -1356,7 +1408,9 @@ int create_impl(const specdec_config *cfg, int device, int rank, int world, cons
     set_attn_attrs<float, int8_t>();
     set_attn_attrs<__nv_bfloat16, int8_t>();
     set_linear_attrs();
-    set_gemm_attrs();
+    h->gemm_max_split = set_gemm_attrs();
+    if (const char *e = std::getenv("SPECDEC_GEMM_MAX_SPLIT"))  // a lower cap (1: no split-K), for comparisons
+      h->gemm_max_split = std::max(1, std::min(h->gemm_max_split, std::atoi(e)));
     {
       const int vs = td.V * static_cast<int>(sizeof(float));
       CK(cudaFuncSetAttribute(first_token_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, vs));
@@ -1651,7 +1705,7 @@ int specdec_generate_device(specdec_handle *h, const specdec_gen_params *p, cons
 
 namespace {
 int host_generate(specdec_handle *h, const specdec_gen_params *p, const specdec_tree *tr, const int32_t *prompts, int B,
-                  int S, int32_t *out_tokens, int64_t *out_stats);
+                  int S, int32_t *out_tokens, int64_t *out_stats, bool ar = false);
 }
 
 int specdec_generate(specdec_handle *h, const specdec_gen_params *p, const int32_t *prompts, int B, int S,
@@ -1683,11 +1737,29 @@ int specdec_generate_tree(specdec_handle *h, const specdec_gen_params *p, const 
   return host_generate(h, p, tree, prompts, B, S, out_tokens, out_stats);
 }
 
+int specdec_generate_ar(specdec_handle *h, const specdec_gen_params *p, const int32_t *prompts, int B, int S,
+                        int32_t *out_tokens, int64_t *out_stats) {
+  return host_generate(h, p, nullptr, prompts, B, S, out_tokens, out_stats, true);
+}
+
+int specdec_generate_ar_device(specdec_handle *h, const specdec_gen_params *p, const int32_t *d_prompts, int B, int S,
+                               int32_t *d_out_tokens, int64_t *d_out_stats) {
+  if (!h) return SPECDEC_ERR_INVALID;
+  try {
+    CK(cudaSetDevice(h->device));
+    if (!d_prompts || !d_out_tokens) fail(SPECDEC_ERR_INVALID, "null buffer");
+    return generate_impl(h, p, d_prompts, B, S, d_out_tokens, d_out_stats, nullptr, true);
+  } catch (const SpecErr &e) {
+    h->err = e.msg;
+    return e.code;
+  }
+}
+
 }  // extern "C"
 
 namespace {
 int host_generate(specdec_handle *h, const specdec_gen_params *p, const specdec_tree *tr, const int32_t *prompts, int B,
-                  int S, int32_t *out_tokens, int64_t *out_stats) {
+                  int S, int32_t *out_tokens, int64_t *out_stats, bool ar) {
   if (!h) return SPECDEC_ERR_INVALID;
   try {
     CK(cudaSetDevice(h->device));
@@ -1699,9 +1771,9 @@ int host_generate(specdec_handle *h, const specdec_gen_params *p, const specdec_
     if (tr) tc = make_tree(h, tr);
     CK(cudaMemcpyAsync(h->d_prompts, prompts, static_cast<size_t>(B) * S * sizeof(int), cudaMemcpyHostToDevice, h->stream));
     int rc = generate_impl(h, p, h->d_prompts, B, S, h->d_out, reinterpret_cast<int64_t *>(h->d_stats),
-                           tr ? &tc : nullptr);
+                           tr ? &tc : nullptr, ar);
     if (rc != SPECDEC_OK) return rc;
-    const int n = S + std::max(1, p->max_new_tokens);
+    const int n = S + (ar ? p->max_new_tokens : std::max(1, p->max_new_tokens));
     CK(cudaMemcpyAsync(out_tokens, h->d_out, static_cast<size_t>(B) * n * sizeof(int), cudaMemcpyDeviceToHost, h->stream));
     if (out_stats)
       CK(cudaMemcpyAsync(out_stats, h->d_stats, static_cast<size_t>(B) * 4 * sizeof(int64_t), cudaMemcpyDeviceToHost,

@@ -13,6 +13,14 @@
 // epilogue on column pairs.  int8 weights are multiplied as their exact bf16
 // images (|q| <= 127) and scaled per output column in the epilogue, the
 // reassociation sum(x * q) * s that the GEMV uses too.
+//
+// Split-K for grids of few tiles (verify blocks of a few hundred rows through
+// narrow layers): the ksplit CTAs of one tile form a thread-block cluster
+// along z, rank z multiplying k-blocks [z nk / ks, (z + 1) nk / ks).  Their
+// partial tiles meet in distributed shared memory (each rank sends column
+// slice j of its accumulators to rank j, into the freed TMA ring), and rank j
+// adds the ks partials in rank order (the same sum on every run) and runs the
+// epilogue on its 256 / ks columns.
 #pragma once
 
 #include <cuda.h>
@@ -33,13 +41,35 @@ constexpr int kGemmBBytes = kBN * kBK * 2;              // 32 KB
 constexpr int kGemmStageBytes = kGemmABytes + kGemmBBytes;
 constexpr int kGemmSmem = kStages * kGemmStageBytes + 1024;
 constexpr int kTmemCols = 256;                          // fp32 accumulator columns (one per output column)
+constexpr int kGemmMaxSplit = 8;                        // portable cluster size
 
 struct alignas(64) GemmArgs {
   CUtensorMap tma_a;  // [R][K] bf16 rows, box kBK x kBM, 128-byte swizzle
   CUtensorMap tma_b;  // [N][K] bf16 weights, box kBK x kBN, 128-byte swizzle
   LinearArgs lin;     // epilogue operands (out, scale, bias, resid, rows, qkv), R, N, K
   int *err;
+  int ksplit;         // CTAs per tile along z (a cluster), 1, 2, 4 or 8
 };
+
+// Receive buffer of the split-K exchange, in the freed ring: [ks][kBM rows]
+// [256 / ks + 4 floats] (the 16-byte pad keeps a warp's row-strided 16-byte
+// accesses free of bank conflicts).
+__host__ __device__ constexpr int gemm_split_stride(int ks) { return kBN / ks + 4; }
+static_assert(kGemmMaxSplit * kBM * (kBN / kGemmMaxSplit + 4) * 4 <= kStages * kGemmStageBytes,
+              "split-K exchange must fit the TMA ring");
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_map(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_f4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
 
 // Shared-memory matrix descriptor of a K-major operand tile whose rows are
 // 128 bytes with the 128-byte swizzle: 8-row core groups 1024 bytes apart
@@ -249,7 +279,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
   const LinearArgs &a = g.lin;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * kBN, m0 = blockIdx.y * kBM;
-  const int nk = (a.K + kBK - 1) / kBK;
+  const int nk_all = (a.K + kBK - 1) / kBK;
+  const int ks = g.ksplit, z = blockIdx.z;  // the cluster spans z only: rank = z
+  const int kb0 = z * nk_all / ks;
+  const int nk = (z + 1) * nk_all / ks - kb0;
 
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
@@ -290,8 +323,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
       unsigned char *sa = tiles + s * kGemmStageBytes;
       unsigned char *sb = sa + kGemmABytes;
       mbar_expect_tx(&full[s], kGemmStageBytes);
-      tma_load_2d(sa, &g.tma_a, kb * kBK, m0, &full[s]);
-      tma_load_2d(sb, &g.tma_b, kb * kBK, n0, &full[s]);
+      tma_load_2d(sa, &g.tma_a, (kb0 + kb) * kBK, m0, &full[s]);
+      tma_load_2d(sb, &g.tma_b, (kb0 + kb) * kBK, n0, &full[s]);
     }
   } else if (threadIdx.x == 32) {
     // MMA issuer
@@ -329,7 +362,49 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     slot = row_ok ? row_slot(a.rows, row) : 0;
   }
   const int ncols = min(kBN, a.N - n0);
-  if (ok) {
+  if (ks > 1) {
+    // split-K: every rank's MMAs are done (its ring is free) before any
+    // partial is sent; all sends land before any rank reduces
+    cluster_sync_all();
+    const int sw = kBN / ks, ld = gemm_split_stride(ks);
+    const uint32_t tbase = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const uint32_t mine = smem_u32(tiles) + static_cast<uint32_t>(((z * kBM + warp * 32 + lane) * ld) * 4);
+    for (int j = 0; j < ks; ++j) {
+      const uint32_t dst = cluster_map(mine, j);
+      for (int c = 0; c < sw && j * sw + c < ncols; c += 16) {
+        float v[16];
+        tmem_ld16(tbase + j * sw + c, v);
+        if (!ok) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] = 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) st_cluster_f4(dst + (c + 4 * i) * 4, v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      }
+    }
+    cluster_sync_all();
+    const float *buf = reinterpret_cast<const float *>(tiles);
+    const int rl = warp * 32 + lane;
+    for (int c = 0; c < sw && z * sw + c < ncols; c += 16) {
+      float v[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = 0.f;
+      for (int zz = 0; zz < ks; ++zz) {
+        const float4 *src = reinterpret_cast<const float4 *>(buf + (zz * kBM + rl) * ld + c);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 t = src[i];
+          v[4 * i] += t.x; v[4 * i + 1] += t.y; v[4 * i + 2] += t.z; v[4 * i + 3] += t.w;
+        }
+      }
+      if (row_ok && ok) {
+        const int n = n0 + z * sw + c;
+        ChunkOps op;
+        chunk_load<EPI>(a, row, n, req, pos, op);
+        chunk_store<EPI>(a, row, n, v, op, s_scale + z * sw + c, s_bias + z * sw + c, req, pos, slot);
+      }
+    }
+  } else if (ok) {
     // chunks of 16 columns, the next chunk's row operands in flight
     const uint32_t tbase = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     ChunkOps op0, op1;

@@ -121,6 +121,9 @@ struct SpecState {
   int *d_root;         // [B]
   int *cp_t0, *cp_d0, *cp_n, *cp_dn;  // [B] root slots and path lengths of the last accept
   int *cp_path;        // [B][kTreeMaxDepth] accepted node indices, root side first
+  // autoregressive decoding (ar = 1, k = 0): one target row per request and
+  // step at verify_row(b, 0); host-uniform tables have one slot per step
+  int ar;
 };
 
 // Tree structure (BFS order; the nodes at depth t >= 1 are tlev[t-1] .. tlev[t]-1).
@@ -1013,6 +1016,61 @@ __global__ void __launch_bounds__(kSampThreads) accept_kernel(SpecState st, cons
     else clear_request_rows(st, b);
     st.active[b] = still ? 1 : 0;
     if (still) atomicAdd(st.active_count, 1);
+  }
+}
+
+// Autoregressive decoding, one token per request from the target's logits
+// (generate_advanced, src/nn/layer.cpp:1239-1380, with the KV cache): the
+// prefill's last row (first call) or the last step's row.  Sampling follows
+// generate_advanced: greedy = first maximum; else probabilities as get_probs
+// (temperature, top-k, top-p, renormalised) and one discrete_distribution draw
+// (request b's mt19937(seed + b) stream, or u[b][step][0] of the host table).
+// Writes the row of the next step (the token at the next cache position) or,
+// after max_new tokens, retires the request.  stats[b][0] counts the steps.
+__global__ void __launch_bounds__(kSampThreads) ar_token_kernel(SpecState st, const float *__restrict__ logits) {
+  pdl_wait();
+  __shared__ SampShared sh;
+  extern __shared__ float srow[];  // [V]
+  const int b = blockIdx.x;
+  if (!st.active[b]) return;
+  __shared__ int s_state[2];  // n_new, t_len
+  if (threadIdx.x == 0) {
+    s_state[0] = st.n_new[b];
+    s_state[1] = st.t_len[b];
+  }
+  RngCtx rc = make_rng(sh);
+  load_row(logits + static_cast<size_t>(b) * st.V, st.V, srow);
+  int tok;
+  if (st.greedy) {
+    tok = argmax_smem(srow, st.V, sh.redv, sh.redi);
+  } else {
+    rng_prepare(st, b, 2, rc);
+    probs_smem(srow, st.V, st.T, st.top_k, st.top_p, sh.red, sh.cut);
+    if (threadIdx.x == 0) sh.u = draw_sample_u(st, b, s_state[0], 0, rc);
+    __syncthreads();
+    tok = sample_smem(srow, st.V, sh.u, st.rng_mode, sh.redd, sh.redi);
+    rng_commit(st, b, rc);
+  }
+  pdl_launch();
+  if (threadIdx.x == 0) {
+    const int n = s_state[0] + 1;
+    st.tokens_out[static_cast<size_t>(b) * st.out_len + st.prompt_len + s_state[0]] = tok;
+    st.n_new[b] = n;
+    st.stats[4 * b] += 1;
+    const int t = s_state[1];
+    bool more = n < st.max_new;
+    if (more && t + 1 > st.t_cap) {
+      atomicOr(st.err, kErrSeqLen);
+      more = false;
+    }
+    if (more) {
+      set_row(st, verify_row(st, b, 0), tok, t, b);
+      st.t_len[b] = t + 1;
+      atomicAdd(st.active_count, 1);
+    } else {
+      st.active[b] = 0;
+      clear_row(st, verify_row(st, b, 0));
+    }
   }
 }
 

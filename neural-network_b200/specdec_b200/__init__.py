@@ -36,7 +36,7 @@ EXPORTS = ("specdec_create", "specdec_destroy", "specdec_last_error", "specdec_l
            "specdec_generate", "specdec_generate_device", "specdec_stream", "specdec_forward_logits",
            "specdec_philox_uniforms", "specdec_last_launch_count", "specdec_forward_logits_noalloc",
            "specdec_time_linear", "specdec_generate_tree", "specdec_generate_tree_device", "specdec_tp_unique_id",
-           "specdec_create_tp")
+           "specdec_create_tp", "specdec_generate_ar", "specdec_generate_ar_device")
 
 # linear layers of specdec_time_linear
 LIN_QKV, LIN_OPROJ, LIN_FFN_IN, LIN_FFN_OUT, LIN_HEAD = 0, 1, 2, 3, 4
@@ -92,6 +92,8 @@ def load_library(path: str = LIB_PATH):
                                      C.c_void_p, C.c_void_p]
     lib.specdec_generate_device.argtypes = [C.c_void_p, C.POINTER(_GenParams), C.c_void_p, C.c_int, C.c_int,
                                             C.c_void_p, C.c_void_p]
+    lib.specdec_generate_ar.argtypes = lib.specdec_generate.argtypes
+    lib.specdec_generate_ar_device.argtypes = lib.specdec_generate_device.argtypes
     lib.specdec_stream.restype = C.c_void_p
     lib.specdec_stream.argtypes = [C.c_void_p]
     lib.specdec_forward_logits.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p]
@@ -243,6 +245,34 @@ class Engine:
         prm, keep = self._params(max_new_tokens, lookahead, temperature, 0, 1.0, seed, uniforms, draft_catchup)
         self._check(self._lib.specdec_generate_device(self.h, C.byref(prm), C.c_void_p(d_prompts), B, S,
                                                       C.c_void_p(d_out), C.c_void_p(d_stats)))
+        del keep
+
+    def generate_advanced(self, prompts, max_new_tokens: int, temperature: float = 1.0, top_k: int = 0,
+                          top_p: float = 1.0, seed: int = 42,
+                          uniforms: Optional[np.ndarray] = None) -> Tuple[np.ndarray, np.ndarray]:
+        """Autoregressive decoding with the target's KV cache, as the reference's
+        ``generate_advanced(prompt, max_new_tokens, temperature, top_k, top_p,
+        seed, use_kv_cache=true)`` (src/nn/layer.cpp:1239-1380), over B requests
+        (request b draws from mt19937(seed + b), or from uniforms[b][step][0]).
+        prompts [B, S] -> (tokens [B, S + max_new], stats [B, 4] = steps, 0, 0, 0)."""
+        p = np.ascontiguousarray(np.atleast_2d(prompts), np.int32)
+        B, S = p.shape
+        prm, keep = self._params(max_new_tokens, 1, temperature, top_k, top_p, seed, uniforms, CATCHUP_REF)
+        out = np.zeros((B, S + max_new_tokens), np.int32)
+        stats = np.zeros((B, 4), np.int64)
+        self._check(self._lib.specdec_generate_ar(self.h, C.byref(prm), p.ctypes.data, B, S, out.ctypes.data,
+                                                  stats.ctypes.data))
+        del keep
+        return out.astype(np.int64), stats
+
+    def generate_advanced_device(self, d_prompts: int, B: int, S: int, d_out: int, d_stats: int,
+                                 max_new_tokens: int, temperature: float = 1.0, seed: int = 42,
+                                 uniforms=None) -> None:
+        """Device-pointer variant of generate_advanced, enqueued on `stream`
+        (d_out [B][S + max(1, max_new)])."""
+        prm, keep = self._params(max_new_tokens, 1, temperature, 0, 1.0, seed, uniforms, CATCHUP_REF)
+        self._check(self._lib.specdec_generate_ar_device(self.h, C.byref(prm), C.c_void_p(d_prompts), B, S,
+                                                         C.c_void_p(d_out), C.c_void_p(d_stats)))
         del keep
 
     def forward_logits(self, role: int, tokens) -> np.ndarray:

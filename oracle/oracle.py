@@ -227,6 +227,9 @@ class _OracleLib:
                                              _i64p, C.c_int, C.c_int, _i64p, _i64p, C.c_void_p, C.c_int]
             lib.oc_generate_advanced.argtypes = [C.c_void_p, C.POINTER(_Numerics), _i64p, C.c_int, C.c_int,
                                                  C.c_float, C.c_int, C.c_float, C.c_uint32, _i64p]
+            lib.oc_generate_ar.argtypes = [C.c_void_p, C.POINTER(_Numerics), _i64p, C.c_int, C.c_int, C.c_int,
+                                           C.c_float, C.c_int, C.c_float, C.c_int, C.c_uint32, C.c_void_p, C.c_int,
+                                           _i64p, C.c_void_p]
             lib.oc_get_probs.argtypes = [_f32p, C.c_int, C.c_float, C.c_int, C.c_float, _f32p]
             lib.oc_rope.argtypes = [_f32p, C.c_int, C.c_int, _i32p, _f32p]
             lib.oc_mt19937.argtypes = [C.c_uint32, C.c_int, _u32p]
@@ -295,6 +298,25 @@ class Oracle:
         _oc_check(_OracleLib.get().oc_generate_advanced(self.h, C.byref(nm), p, p.size, max_new,
                                                         temperature, top_k, top_p, seed, out))
         return out
+
+
+def oracle_generate_ar(model: Oracle, prompts: np.ndarray, max_new: int, temperature: float = 1.0, top_k: int = 0,
+                       top_p: float = 1.0, seed: int = 42, uniforms: Optional[np.ndarray] = None,
+                       act_bf16: bool = False, kv_mode: int = 0):
+    """generate_advanced with the KV cache (src/nn/layer.cpp:1239-1380) for B
+    requests: request b uses mt19937(seed + b), or uniforms[b][step][0].
+    Returns (tokens [B, S + max_new], margins [B, max_new] per token)."""
+    p = np.ascontiguousarray(np.atleast_2d(prompts), np.int64)
+    B, S = p.shape
+    out = np.zeros((B, S + max_new), np.int64)
+    margins = np.zeros((B, max(1, max_new)), np.float64)
+    nm = _Numerics(1 if act_bf16 else 0, kv_mode)
+    u = None if uniforms is None else np.ascontiguousarray(uniforms, np.float32)
+    _oc_check(_OracleLib.get().oc_generate_ar(model.h, C.byref(nm), p, B, S, max_new, temperature, top_k, top_p,
+                                              0 if u is None else 1, seed & 0xFFFFFFFF,
+                                              None if u is None else u.ctypes.data,
+                                              0 if u is None else u.shape[1], out, margins.ctypes.data))
+    return out, margins
 
 
 def oracle_generate_speculative(target: Oracle, draft: Oracle, prompts: np.ndarray, max_new: int,

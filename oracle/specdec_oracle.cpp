@@ -1132,6 +1132,56 @@ int oc_generate_advanced(void *mp, const Numerics *nm, const int64_t *prompt, in
   });
 }
 
+// generate_advanced (src/nn/layer.cpp:1239-1380, use_kv_cache = true) for B
+// independent requests with the uniform sources of the speculative path:
+// request b draws from mt19937(seed + b) (rng_mode 0) or from
+// uniforms[b][step][0] (rng_mode 1, n_rounds >= max_new rows of one slot).
+// margins[b][step]: the decision margin of each token (greedy: relative top-2
+// logit gap; sampled: distance of the uniform to a CDF boundary).
+int oc_generate_ar(void *mp, const Numerics *nm, const int64_t *prompts, int B, int S, int max_new, float T,
+                   int top_k, float top_p, int rng_mode, uint32_t seed, const float *uniforms, int n_rounds,
+                   int64_t *out, double *margins) {
+  return guard([&] {
+    auto *m = static_cast<Model *>(mp);
+    const int V = m->c.vocab;
+    for (int b = 0; b < B; ++b) {
+      Rng rng;
+      rng.mode = rng_mode;
+      rng.gen.seed(seed + static_cast<uint32_t>(b));
+      rng.slots = 1;
+      rng.n_rounds = n_rounds;
+      if (rng_mode == 1) rng.table = uniforms + static_cast<size_t>(b) * n_rounds;
+      Cache c;
+      cache_init(c, *m, m->c.max_seq_len, nm->kv_mode);
+      const int64_t *prompt = prompts + static_cast<size_t>(b) * S;
+      std::vector<int64_t> g(prompt, prompt + S);
+      std::vector<float> lg;
+      for (int step = 0; step < max_new; ++step) {
+        double mg = 1e300;
+        if (step == 0) forward(*m, *nm, c, prompt, S, lg);
+        else { int64_t in = g.back(); forward(*m, *nm, c, &in, 1, lg); }
+        const int rows = static_cast<int>(lg.size() / V);
+        const float *row = &lg[static_cast<size_t>(rows - 1) * V];
+        int next;
+        if (T <= 0.0f) {
+          next = argmax_first(row, V);
+          float a = -INFINITY, bb = -INFINITY;
+          for (int v = 0; v < V; ++v) {
+            if (row[v] > a) { bb = a; a = row[v]; }
+            else if (row[v] > bb) bb = row[v];
+          }
+          mg = std::min(mg, static_cast<double>(a - bb) / std::max(1e-30, static_cast<double>(std::abs(a))));
+        } else {
+          next = sample(rng, get_probs(row, V, T, top_k, top_p), step, 0, &mg);
+        }
+        g.push_back(next);
+        if (margins) margins[static_cast<size_t>(b) * max_new + step] = mg;
+      }
+      std::copy(g.begin(), g.end(), out + static_cast<size_t>(b) * (S + max_new));
+    }
+  });
+}
+
 // get_probs + sample on one logits row, for unit tests of the sampler alone.
 int oc_get_probs(const float *logits, int V, float T, int top_k, float top_p, float *probs) {
   return guard([&] {

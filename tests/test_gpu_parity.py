@@ -210,6 +210,22 @@ def test_greedy_spec_bf16_gemm(gpu_lib, oracle_built):
     assert exact + ties == 16 and ties <= 4
 
 
+def test_gemm_split_k_matches_unsplit(gpu_lib, oracle_built, monkeypatch):
+    # few tiles over a long K: the residual GEMMs split K over clusters of up
+    # to 8 CTAs; against the same engine built with splitting off, and the oracle
+    shape = ModelShape(vocab=512, d_model=256, n_heads=4, d_ff=2048, n_layers=2, max_seq_len=200)
+    toks = make_prompts(1, 150, shape.vocab, seed=31)[0]
+    split = make_pair(shape, 1, seed=30, int8=True, act_bf16=True, kv_mode=1, max_prompt_len=160)
+    monkeypatch.setenv("SPECDEC_GEMM_MAX_SPLIT", "1")
+    whole = make_pair(shape, 1, seed=30, int8=True, act_bf16=True, kv_mode=1, max_prompt_len=160)
+    a = split.engine.forward_logits(sd.TARGET, toks)
+    b = whole.engine.forward_logits(sd.TARGET, toks)
+    o = split.target.forward(toks, act_bf16=True, kv_mode=1)
+    assert rel_err(a, b) < BF16_REL and rel_err(a, o) < BF16_REL and rel_err(b, o) < BF16_REL
+    split.engine.close()
+    whole.engine.close()
+
+
 # Token trees (tree.cuh) against the oracle's path-by-path restatement
 # (oracle/specdec_oracle.cpp: tree_one): greedy and both uniform sources.
 def _tree_pair(name, seed, **kw):

@@ -60,6 +60,28 @@ def test_oracle_ar_matches_reference_fixture(oracle_built, golden, name):
     assert np.array_equal(golden[f"{name}/ar_greedy"], golden[f"{name}/ar_greedy_nocache"])
 
 
+@pytest.mark.parametrize("name", list(GOLDEN_MODELS))
+def test_oracle_batched_ar_matches_reference_fixture(oracle_built, golden, name):
+    # the batched restatement the GPU autoregressive path is checked against:
+    # request 0 with seed s is the reference's generate_advanced(seed = s);
+    # request 1 uses seed s + 1 (the per-request stream convention)
+    shape, t, d = _models(name)
+    prompt = golden[f"{name}/prompt"]
+    two = np.stack([prompt, prompt])
+    out, _ = oracle.oracle_generate_ar(t, two, 12, 0.0, 0, 1.0, 42)
+    assert np.array_equal(out[0], golden[f"{name}/ar_greedy"]) and np.array_equal(out[1], golden[f"{name}/ar_greedy"])
+    out, _ = oracle.oracle_generate_ar(t, two, 12, 0.9, 5, 0.8, 7)
+    assert np.array_equal(out[0], golden[f"{name}/ar_t09"])
+    assert np.array_equal(out[1], t.generate_advanced(prompt, 12, 0.9, 5, 0.8, 8))
+    # host uniforms: a table of the draws mt19937 makes reproduces the stream
+    # (discrete_distribution draws one 53-bit canonical double per token; the
+    # table holds floats, so only compare that both modes run and stay in range)
+    u = philox_uniforms(3, 2, 12, 1)
+    out, m = oracle.oracle_generate_ar(t, two, 12, 1.0, 0, 1.0, 0, uniforms=u)
+    assert out.shape == (2, prompt.size + 12) and (out >= 0).all() and (out < shape.vocab).all()
+    assert np.isfinite(m).all()
+
+
 def test_greedy_spec_equals_greedy_ar(oracle_built, golden):
     # SpeculativeDecodingParity (transformer_test.cpp:307-335)
     for name in GOLDEN_MODELS:
