@@ -71,17 +71,27 @@ def tree_nodes(branching) -> int:
 KV_DTYPE = {0: 0, 1: 1, 2: 2}  # workload kv_mode -> SPECDEC_F32 / BF16 / INT8
 
 
+# DRAM bytes (read + write) of one launch of the roofline kernel, from the ncu
+# capture named beside it (caches flushed before the launch, as the live probe
+# does); None where no capture of the current kernel exists.
+TRAFFIC = {
+    "int8": (503808, "profiles/linear_resid_int8_verify_dram.md"),
+}
+
+
 def roofline_entry(p, hbm, tflops, wl, rows):
     """The FFN down-projection at the verify row count: HBM-bound below the
     bf16 ridge (peak flops / peak bytes), tensor-bound above it."""
     ridge = tflops * 1e12 / (hbm * 1e9)
     what = "tcgen05 GEMM" if (wl.act_bf16 and rows >= 64) else "linear_kernel GEMV"
     kern = f"{what}, residual epilogue (target FFN down-projection, {rows} verify rows)"
+    traffic, src = TRAFFIC.get(wl.name, (None, None))
+    extra = {"kernel": kern, "traffic_source": src}
     if p["flops_per_byte"] > ridge:
         return {"bound": "tensor", "achieved": p["TFLOPs"], "peak": tflops, "unit": "TFLOP/s",
-                "frac": p["TFLOPs"] / tflops, "traffic": None, "kernel": kern}
+                "frac": p["TFLOPs"] / tflops, "traffic": traffic, **extra}
     return {"bound": "hbm", "achieved": p["GBps"], "peak": hbm, "unit": "GB/s", "frac": p["GBps"] / hbm,
-            "traffic": None, "kernel": kern}
+            "traffic": traffic, **extra}
 
 
 def dist_env():
@@ -101,8 +111,9 @@ def algorithmic_bytes_per_round(wl, int8: bool, avg_ctx: float) -> dict:
     head = d * V * wb
     w_t = L * per_layer + head
     w_d = wl.draft_layers * per_layer + head
-    kv_elt = 4
-    kv_tok_layer = 2 * kvd * kv_elt
+    # cache element bytes by KV dtype (f32, bf16, int8 + one fp32 scale per
+    # position and kv head for K and for V)
+    kv_tok_layer = 2 * kvd * {0: 4, 1: 2, 2: 1}[wl.kv_mode] + (2 * 4 * m.kv_heads if wl.kv_mode == 2 else 0)
     B, k = wl.batch, wl.lookahead
     kv_read = B * avg_ctx * kv_tok_layer * (k * wl.draft_layers + L)
     kv_write = B * kv_tok_layer * ((k + 1) * wl.draft_layers + (k + 1) * L)
@@ -389,7 +400,26 @@ def main():
         e2e_ms.append(e0.elapsed_time(e1))
     e2e_tot = float(sum(e2e_ms))
 
-    tot_ms, e2e_tot = max_over_ranks([tot_ms, e2e_tot], dist if world > 1 else None, dev)
+    # Autoregressive decoding of the same requests on the same kernels
+    # (generate_advanced): the speculative path's speed-up over plain decoding.
+    ar_ms = []
+    if not wl.tree:
+        ar_uni = np.ascontiguousarray(uni[:, : wl.max_new, :1])
+        for i in range(args.warmup + 3):
+            with torch.cuda.stream(stream):
+                flush.fill_(float(i))
+                a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a0.record(stream)
+            eng.generate_advanced_device(d_prompts.data_ptr(), B, S, d_out.data_ptr(), d_stats.data_ptr(),
+                                         wl.max_new, wl.temperature, seed=1234, uniforms=ar_uni)
+            with torch.cuda.stream(stream):
+                a1.record(stream)
+            torch.cuda.synchronize()
+            if i >= args.warmup:
+                ar_ms.append(a0.elapsed_time(a1))
+    ar_tot = float(sum(ar_ms)) if ar_ms else 0.0
+
+    tot_ms, e2e_tot, ar_tot = max_over_ranks([tot_ms, e2e_tot, ar_tot], dist if world > 1 else None, dev)
     ms_per_step = tot_ms / args.steps
     value = new_tokens * world * args.steps / (tot_ms / 1e3)
     e2e_value = new_tokens * world * len(e2e_ms) / (e2e_tot / 1e3)
@@ -430,10 +460,16 @@ def main():
                              "peak_source": peak_kind,
                              "other_kernels": {k: v for k, v in probes.items() if k != "ffn_out"},
                              "round": {"alg_bytes": ab["total"], "achieved": round_achieved,
-                                       "frac": round_achieved / hbm}},
+                                       "frac": round_achieved / hbm, "weight_bytes": ab["weights"],
+                                       "kv_bytes": ab["kv"],
+                                       "weights_frac": ab["weights"] / (round_ms * 1e-3) / 1e9 / hbm}},
                 "spec": {"rounds_per_step": int(rounds), "mean_accepted_per_round": float(accepted) / max(1, stats[:, 0].sum()),
                          "acceptance_rate": float(accepted) / max(1, drafted), "round_us": round_ms * 1e3},
                 "clocks": clocks}
+        if ar_ms:
+            line["ar_decode"] = {"value": new_tokens * world * len(ar_ms) / (ar_tot / 1e3), "unit": UNIT,
+                                 "what": "generate_advanced (autoregressive, KV cache) of the same requests, "
+                                         "models and uniforms on the same kernels, device-resident"}
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_sample(wl)
         if wl.tree:

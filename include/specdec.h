@@ -117,6 +117,16 @@ const char *specdec_last_error(const specdec_handle *h);
 int specdec_load_params(specdec_handle *h, int role, int n_params,
                         const float *const *params, const int64_t *numels);
 
+/* Replaces Layer::load_weights (src/nn/layer.cpp:467-469 ->
+ * serialization::load_parameters, src/core/serialization.cpp:49-107) on the
+ * model of `role`: reads a NETW version-1 file (magic "NETW", u16 version,
+ * u32 tensor count, per tensor u32 dims, u64 shape, u64 element count,
+ * float32 data) whose tensors are the model's parameters() in order and
+ * shape, then loads them as specdec_load_params does.  A wrong signature,
+ * version, count, rank, shape or element count fails with
+ * SPECDEC_ERR_INVALID and the reference's message. */
+int specdec_load_netw(specdec_handle *h, int role, const char *path);
+
 /* Replaces TransformerDecoder::generate_speculative (src/nn/layer.cpp:1382-1661)
  * for B independent requests with equal prompt length S.  prompts [B][S] and
  * out_tokens [B][S + max(1, max_new_tokens)] are HOST buffers (the tokens are

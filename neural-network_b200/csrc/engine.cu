@@ -26,6 +26,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <fstream>
 #include <map>
 #include <memory>
 #include <mutex>
@@ -219,6 +220,15 @@ struct specdec_handle {
   bool use_graph = true;
   bool use_pdl = true;  // programmatic dependent launch for the kernels that support it
   int gemm_max_split = 1;  // largest split-K cluster of the tensor-core GEMM
+  int gemm_clusters[kGemmMaxSplit + 1] = {};  // split-K clusters of ks CTAs resident at once
+  int samp_max_cluster = 1;  // largest cluster of draft_sample_cluster_kernel
+  int attn_ctas_per_sm = 2;  // attention splits the cache while the grid stays within this many CTAs per SM
+  // row batches that take the tensor-core GEMM instead of the GEMV: at least
+  // gemm_min_rows rows, or gemm_wide_rows rows of a layer with at least
+  // gemm_wide_elems weights
+  int gemm_min_rows = kGemmMinRows;
+  int gemm_wide_rows = 16;
+  long long gemm_wide_elems = 4ll << 20;
 
   void *dalloc(size_t bytes, std::vector<void *> *owner = nullptr) {
     void *p = nullptr;
@@ -379,6 +389,37 @@ float *upload_vec(specdec_handle *h, int role, const float *p, size_t n) {
   float *d = static_cast<float *>(h->dalloc(n * sizeof(float), &h->weight_allocs[role]));
   CK(cudaMemcpy(d, p, n * sizeof(float), cudaMemcpyHostToDevice));
   return d;
+}
+
+// Tensor shapes of TransformerDecoder::parameters() (the order load_model
+// reads): Embedding [V, d] (src/nn/layer.cpp:267), Dense weight [in, out] and
+// bias [1, out] (src/nn/layer.cpp:153-157), LayerNorm gamma / beta [d]
+// (src/nn/layer.cpp:1063-1064).  The cfg architecture (no reference
+// counterpart) adds positions [max_seq, d] and a final LayerNorm.
+std::vector<std::vector<uint64_t>> param_shapes(const Dims &dm) {
+  const uint64_t d = dm.d, F = dm.Fg, V = dm.V, kvd = static_cast<uint64_t>(dm.Hkvg) * dm.D;
+  const bool ref = dm.arch == SPECDEC_ARCH_REF;
+  std::vector<std::vector<uint64_t>> s;
+  auto dense = [&](uint64_t in, uint64_t out) {
+    s.push_back({in, out});
+    s.push_back({1, out});
+  };
+  s.push_back({V, d});
+  if (!ref) s.push_back({static_cast<uint64_t>(dm.max_seq), d});
+  for (int l = 0; l < dm.L; ++l) {
+    if (!ref) { s.push_back({d}); s.push_back({d}); }
+    dense(d, d); dense(d, kvd); dense(d, kvd); dense(d, d);
+    if (ref) {
+      dense(d, F); dense(d, F); dense(F, d);
+      for (int i = 0; i < 4; ++i) s.push_back({d});
+    } else {
+      s.push_back({d}); s.push_back({d});
+      dense(d, F); dense(F, d);
+    }
+  }
+  if (!ref) { s.push_back({d}); s.push_back({d}); }
+  dense(d, V);
+  return s;
 }
 
 void load_model(specdec_handle *h, int role, ModelW &m, int n, const float *const *P, const int64_t *numel) {
@@ -629,8 +670,8 @@ template <int EPI>
 bool try_launch_gemm(specdec_handle *h, LinearArgs a) {
   // >= kGemmMinRows rows, or >= 16 rows of a wide layer (the lm_head): the GEMM
   // reads each weight once, where 8-row GEMV tiles would re-read it per tile
-  const bool wide = a.R >= 16 && static_cast<long long>(a.N) * a.K >= (4ll << 20);
-  if (!act_bf16(h) || !w_int8(h) || (a.R < kGemmMinRows && !wide) || (a.K % 8) != 0) return false;
+  const bool wide = a.R >= h->gemm_wide_rows && static_cast<long long>(a.N) * a.K >= h->gemm_wide_elems;
+  if (!act_bf16(h) || !w_int8(h) || (a.R < h->gemm_min_rows && !wide) || (a.K % 8) != 0) return false;
   if (a.in_g && !ln_rows_ok(a)) return false;
   // the chunked epilogue's 16-byte vectors: aligned output / residual rows,
   // and q / k / v sections and heads in whole 16-column chunks
@@ -663,7 +704,9 @@ bool try_launch_gemm(specdec_handle *h, LinearArgs a) {
   const int gx = (a.N + kBN - 1) / kBN, gy = (a.R + kBM - 1) / kBM;
   const int nk = (a.K + kBK - 1) / kBK;
   int ks = 1;
-  while (2 * ks <= h->gemm_max_split && gx * gy * 2 * ks <= h->num_sms && 2 * ks <= nk) ks *= 2;
+  while (2 * ks <= h->gemm_max_split && gx * gy * 2 * ks <= h->num_sms && 2 * ks <= nk &&
+         gx * gy <= h->gemm_clusters[2 * ks])  // all clusters in one wave
+    ks *= 2;
   g.ksplit = ks;
   if (ks == 1)
     launch(h, gemm_kernel<EPI>, dim3(gx, gy), dim3(kGemmThreads), static_cast<size_t>(kGemmSmem), g);
@@ -712,15 +755,17 @@ void set_linear_attr_epi() {
   set_linear_attr_nc<EPI, 2>();
   set_linear_attr_nc<EPI, 4>();
 }
-// Returns the largest split-K cluster (1, 2, 4 or 8 CTAs of kGemmSmem bytes)
-// the device can schedule.
-int set_gemm_attrs() {
+// Records in active[ks] how many split-K clusters of ks CTAs (kGemmSmem
+// bytes each) the device runs at once (0: none) and returns the largest ks
+// it can schedule.
+int set_gemm_attrs(int *active) {
   CK(cudaFuncSetAttribute(gemm_kernel<kEpiStore>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
   CK(cudaFuncSetAttribute(gemm_kernel<kEpiResid>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
   CK(cudaFuncSetAttribute(gemm_kernel<kEpiQKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
   CK(cudaFuncSetAttribute(gemm_kernel<kEpiSwiGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
   CK(cudaFuncSetAttribute(gemm_kernel<kEpiGelu>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
-  for (int ks = kGemmMaxSplit; ks > 1; ks /= 2) {
+  int best = 1;
+  for (int ks = 2; ks <= kGemmMaxSplit; ks *= 2) {
     cudaLaunchConfig_t lc{};
     lc.gridDim = dim3(1, 1, ks);
     lc.blockDim = dim3(kGemmThreads);
@@ -733,10 +778,48 @@ int set_gemm_attrs() {
     lc.attrs = &at;
     lc.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, gemm_kernel<kEpiResid>, &lc) == cudaSuccess && n > 0) return ks;
-    cudaGetLastError();
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_kernel<kEpiResid>, &lc) != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+    active[ks] = n;
+    if (n > 0) best = ks;
   }
-  return 1;
+  return best;
+}
+
+// Sets the shared-memory size of the cluster samplers for vocabulary V and
+// returns the largest cluster (8, 4 or 2 CTAs) the device can schedule.
+int set_samp_cluster_attrs(int V) {
+  auto one = [&](auto kern, int cs) -> bool {
+    const int bytes = static_cast<int>(((V + cs - 1) / cs + 3) & ~3) * static_cast<int>(sizeof(float));
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    cudaLaunchConfig_t lc{};
+    lc.gridDim = dim3(cs);
+    lc.blockDim = dim3(kSampThreads);
+    lc.dynamicSmemBytes = bytes;
+    cudaLaunchAttribute at{};
+    at.id = cudaLaunchAttributeClusterDimension;
+    at.val.clusterDim.x = cs;
+    at.val.clusterDim.y = 1;
+    at.val.clusterDim.z = 1;
+    lc.attrs = &at;
+    lc.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &lc) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    return n > 0;
+  };
+  int best = 1;
+  if (one(draft_sample_cluster_kernel<2>, 2)) best = 2;
+  if (best == 2 && one(draft_sample_cluster_kernel<4>, 4)) best = 4;
+  if (best == 4 && one(draft_sample_cluster_kernel<8>, 8)) best = 8;
+  return best;
 }
 void set_linear_attrs() {
   set_linear_attr_epi<kEpiStore>();
@@ -765,7 +848,8 @@ void set_attn_attrs() {
 }
 
 // Splits: one tile of positions per split where the cache is long, at most a
-// portable cluster (8) of them, and about two CTAs per SM over the grid.
+// portable cluster (8) of them, and about attn_ctas_per_sm (2) CTAs per SM
+// over the grid.
 template <typename AT, typename KT, int D>
 void launch_attention_d(specdec_handle *h, AttnArgs &a, int ngroups, const void *kc, const void *vc, size_t rows) {
   using G = AttnGeom<KT, D>;
@@ -778,7 +862,7 @@ void launch_attention_d(specdec_handle *h, AttnArgs &a, int ngroups, const void 
   int ns = 1;
   if (a.S_cap > G::kTile) {
     const int want = (a.S_cap + G::kTile - 1) / G::kTile;
-    const int fit = std::max(1, 2 * h->num_sms / base);
+    const int fit = std::max(1, h->attn_ctas_per_sm * h->num_sms / base);
     ns = std::min(std::min(kAttnMaxSplit, want), fit);
   }
   a.nsplit = ns;
@@ -1047,9 +1131,30 @@ TreeCfg make_tree(const specdec_handle *h, const specdec_tree *t) {
 int samp_threads(const specdec_handle *h) { return h->tgt.dm.V <= 4096 ? 512 : kSampThreads; }
 size_t samp_smem(const specdec_handle *h) { return static_cast<size_t>(h->tgt.dm.V) * sizeof(float); }
 // Draft sampling after draft step j (one block per request).
+// Vocabularies of at least kSampClusterMinV entries without top-k / top-p
+// are sampled by clusters of CTAs per request while the grid stays within
+// two CTAs per SM.
+constexpr int kSampClusterMinV = 8192;
+int draft_sample_cluster(const specdec_handle *h, const SpecState &st) {
+  if (h->samp_max_cluster < 2 || st.V < kSampClusterMinV || st.tree) return 1;
+  if (!st.greedy && ((st.top_k > 0 && st.top_k < st.V) || (st.top_p > 0.f && st.top_p < 1.f))) return 1;
+  int cs = h->samp_max_cluster;
+  while (cs > 1 && st.B * cs > 2 * h->num_sms) cs /= 2;
+  return cs;
+}
+size_t samp_cluster_smem(int V, int cs) { return static_cast<size_t>(((V + cs - 1) / cs + 3) & ~3) * sizeof(float); }
+
 void launch_draft_sample(specdec_handle *h, const SpecState &st, int j) {
-  launch_pdl(h, draft_sample_kernel, dim3(st.B), dim3(samp_threads(h)), samp_smem(h), st, j,
-             static_cast<const float *>(h->logits));
+  const int cs = draft_sample_cluster(h, st);
+  const float *lg = h->logits;
+  if (cs > 1) {
+    auto kern = cs >= 8 ? draft_sample_cluster_kernel<8> : cs == 4 ? draft_sample_cluster_kernel<4>
+                                                                    : draft_sample_cluster_kernel<2>;
+    launch_cluster(h, kern, dim3(st.B * cs), dim3(kSampThreads), samp_cluster_smem(st.V, cs), dim3(cs, 1, 1), st,
+                   j, lg);
+    return;
+  }
+  launch_pdl(h, draft_sample_kernel, dim3(st.B), dim3(samp_threads(h)), samp_smem(h), st, j, lg);
 }
 
 // Verify rows accept_kernel stages in shared memory at a time (at least one).
@@ -1408,9 +1513,14 @@ int create_impl(const specdec_config *cfg, int device, int rank, int world, cons
     set_attn_attrs<float, int8_t>();
     set_attn_attrs<__nv_bfloat16, int8_t>();
     set_linear_attrs();
-    h->gemm_max_split = set_gemm_attrs();
+    h->gemm_max_split = set_gemm_attrs(h->gemm_clusters);
     if (const char *e = std::getenv("SPECDEC_GEMM_MAX_SPLIT"))  // a lower cap (1: no split-K), for comparisons
       h->gemm_max_split = std::max(1, std::min(h->gemm_max_split, std::atoi(e)));
+    if (const char *e = std::getenv("SPECDEC_ATTN_CTAS_PER_SM")) h->attn_ctas_per_sm = std::max(1, std::atoi(e));
+    // GEMV / GEMM routing thresholds, for tuning measurements
+    if (const char *e = std::getenv("SPECDEC_GEMM_MIN_ROWS")) h->gemm_min_rows = std::max(1, std::atoi(e));
+    if (const char *e = std::getenv("SPECDEC_GEMM_WIDE_ROWS")) h->gemm_wide_rows = std::max(1, std::atoi(e));
+    if (const char *e = std::getenv("SPECDEC_GEMM_WIDE_ELEMS")) h->gemm_wide_elems = std::max(1ll, std::atoll(e));
     {
       const int vs = td.V * static_cast<int>(sizeof(float));
       CK(cudaFuncSetAttribute(first_token_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, vs));
@@ -1419,6 +1529,10 @@ int create_impl(const specdec_config *cfg, int device, int rank, int world, cons
                               static_cast<int>(accept_smem(h.get()))));
       CK(cudaFuncSetAttribute(tree_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, vs));
       CK(cudaFuncSetAttribute(tree_accept_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, vs));
+      CK(cudaFuncSetAttribute(ar_token_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, vs));
+      h->samp_max_cluster = set_samp_cluster_attrs(td.V);
+      if (const char *e = std::getenv("SPECDEC_SAMPLE_MAX_CLUSTER"))  // a lower cap (1: one CTA per request)
+        h->samp_max_cluster = std::max(1, std::min(h->samp_max_cluster, std::atoi(e)));
     }
 
     const int B = cfg->max_batch, k = cfg->max_lookahead;
@@ -1688,6 +1802,63 @@ int specdec_load_params(specdec_handle *h, int role, int n_params, const float *
     return e.code;
   }
   return SPECDEC_OK;
+}
+
+int specdec_load_netw(specdec_handle *h, int role, const char *path) {
+  if (!h) return SPECDEC_ERR_INVALID;
+  try {
+    if (!path) fail(SPECDEC_ERR_INVALID, "null path");
+    if (role != SPECDEC_TARGET && role != SPECDEC_DRAFT) fail(SPECDEC_ERR_INVALID, "unknown role");
+    const auto shapes = param_shapes(role == SPECDEC_TARGET ? h->tgt.dm : h->dft.dm);
+    // serialization::load_parameters (src/core/serialization.cpp:49-107):
+    // "NETW", u16 version 1, u32 count, then per tensor u32 dims, u64 shape
+    // [dims], u64 element count, float32 data; every check throws there.
+    std::ifstream in(path, std::ios::binary);
+    if (!in) fail(SPECDEC_ERR_INVALID, std::string("Failed to open file for reading: ") + path);
+    char magic[4];
+    in.read(magic, 4);
+    if (in.gcount() != 4 || std::string(magic, 4) != "NETW") fail(SPECDEC_ERR_INVALID, "Invalid file format signature.");
+    uint16_t version = 0;
+    in.read(reinterpret_cast<char *>(&version), sizeof(version));
+    if (!in || version != 1)
+      fail(SPECDEC_ERR_INVALID, "Unsupported serialization file version: " + std::to_string(version));
+    uint32_t count = 0;
+    in.read(reinterpret_cast<char *>(&count), sizeof(count));
+    if (!in || count != shapes.size())
+      fail(SPECDEC_ERR_INVALID, "Tensor count mismatch (file has " + std::to_string(count) + ", model has " +
+                                    std::to_string(shapes.size()) + ").");
+    std::vector<std::vector<float>> data(count);
+    for (uint32_t t = 0; t < count; ++t) {
+      uint32_t dims = 0;
+      in.read(reinterpret_cast<char *>(&dims), sizeof(dims));
+      if (!in || dims != shapes[t].size()) fail(SPECDEC_ERR_INVALID, "Tensor dimension count mismatch.");
+      uint64_t total = 1;
+      for (uint32_t i = 0; i < dims; ++i) {
+        uint64_t v = 0;
+        in.read(reinterpret_cast<char *>(&v), sizeof(v));
+        if (!in || v != shapes[t][i])
+          fail(SPECDEC_ERR_INVALID, "Tensor shape mismatch at dimension " + std::to_string(i));
+        total *= v;
+      }
+      uint64_t ne = 0;
+      in.read(reinterpret_cast<char *>(&ne), sizeof(ne));
+      if (!in || ne != total) fail(SPECDEC_ERR_INVALID, "Tensor element count mismatch.");
+      data[t].resize(total);
+      in.read(reinterpret_cast<char *>(data[t].data()), static_cast<std::streamsize>(total * sizeof(float)));
+      if (static_cast<uint64_t>(in.gcount()) != total * sizeof(float))
+        fail(SPECDEC_ERR_INVALID, "truncated tensor data in " + std::string(path));
+    }
+    std::vector<const float *> ptrs(count);
+    std::vector<int64_t> numels(count);
+    for (uint32_t t = 0; t < count; ++t) {
+      ptrs[t] = data[t].data();
+      numels[t] = static_cast<int64_t>(data[t].size());
+    }
+    return specdec_load_params(h, role, static_cast<int>(count), ptrs.data(), numels.data());
+  } catch (const SpecErr &e) {
+    h->err = e.msg;
+    return e.code;
+  }
 }
 
 int specdec_generate_device(specdec_handle *h, const specdec_gen_params *p, const int32_t *d_prompts, int B, int S,

@@ -7,6 +7,8 @@
 // batches the forward kernels consume.
 #pragma once
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "forward.cuh"
 
@@ -706,6 +708,207 @@ __global__ void __launch_bounds__(kSampThreads) draft_sample_kernel(SpecState st
     rng_commit(st, b, rc);
   }
   pdl_launch();  // the next pass may launch while this block writes its rows
+  if (threadIdx.x == 0) {
+    cand[j] = tok;
+    if (j + 1 < M) {
+      const int d = s_len[0];
+      set_row(st, step_row(st, j + 1, b), tok, d, b);
+      st.d_len[b] = d + 1;
+    } else if (j + 1 < st.k) {
+      clear_row(st, step_row(st, j + 1, b));
+    }
+    if (j == M - 1) {
+      const int t = s_len[1];
+      for (int i = 0; i <= st.k; ++i) {
+        if (i <= M) set_row(st, verify_row(st, b, i), i == 0 ? s_len[2] : i - 1 < j ? s_cand[i - 1] : tok, t + i, b);
+        else clear_row(st, verify_row(st, b, i));
+      }
+      st.t_start[b] = t;
+      st.t_len[b] = t + M + 1;
+    }
+  }
+}
+
+// draft_sample_kernel for large vocabularies without top-k / top-p: the
+// row of request b is split over a thread-block cluster of CS CTAs (rank r
+// holds columns [r Vc, (r + 1) Vc)), so the per-element passes (scale, exp,
+// the two normalisations, the fp64 inverse-CDF scan) run on CS SMs.  The CTAs
+// publish their partials (row max and exp-sum, the filtered sum, the fp64
+// slice sum, the first hit) in their own shared memory; after a cluster
+// barrier every rank combines all CS partials in rank order, so every rank
+// computes the same normalisers.  Rank 0 owns the request's mt19937 state and
+// the bookkeeping of draft_sample_kernel.  Same probabilities and token as
+// draft_sample_kernel up to the summation order of the normalisers.
+constexpr int kSampMaxCluster = 8;
+
+struct SampClusterEx {
+  float mx, se, fs;
+  float amax;
+  int aidx;
+  int pick, lastnz;
+  double u, tot;
+};
+
+template <int CS>
+__global__ void __launch_bounds__(kSampThreads) draft_sample_cluster_kernel(SpecState st, int j,
+                                                                            const float *__restrict__ logits) {
+  namespace cg = cooperative_groups;
+  pdl_wait();
+  __shared__ SampShared sh;
+  __shared__ SampClusterEx ex;
+  __shared__ int s_cand[kMaxLookahead];
+  __shared__ int s_len[3];
+  extern __shared__ float srow[];  // [Vc]: this rank's columns
+  cg::cluster_group cl = cg::this_cluster();
+  const int rank = static_cast<int>(cl.block_rank());
+  const int b = blockIdx.x / CS;
+  // exits that depend on the request only: every rank of the cluster takes them
+  if (!st.active[b]) return;
+  const int M = st.M[b];
+  if (j >= M) {
+    if (rank == 0 && threadIdx.x == 0 && j + 1 < st.k) clear_row(st, step_row(st, j + 1, b));
+    return;
+  }
+  const int V = st.V;
+  const int Vc = ((V + CS - 1) / CS + 3) & ~3;
+  const int v0 = min(V, rank * Vc);
+  const int n = min(V, v0 + Vc) - v0;
+  int *cand = st.cand + b * st.kmax;
+  if (rank == 0) {
+    if (j == M - 1 && static_cast<int>(threadIdx.x) < j) s_cand[threadIdx.x] = cand[threadIdx.x];
+    if (threadIdx.x == 0) {
+      s_len[0] = st.d_len[b];
+      s_len[1] = st.t_len[b];
+      s_len[2] = st.last_tok[b];
+    }
+  }
+  RngCtx rc = make_rng(sh);
+  load_row(logits + static_cast<size_t>(b) * V + v0, n, srow);
+  int tok;
+  if (st.greedy) {
+    ArgMax a{-INFINITY, 0x7fffffff};
+    for (int v = threadIdx.x; v < n; v += blockDim.x) a = argmax_merge(a, ArgMax{srow[v], v0 + v});
+    a = block_argmax(a, sh.redv, sh.redi);
+    if (threadIdx.x == 0) { ex.amax = a.v; ex.aidx = a.i; }
+    cl.sync();
+    ArgMax g{-INFINITY, 0x7fffffff};
+    for (int r = 0; r < CS; ++r) {
+      const SampClusterEx *e = cl.map_shared_rank(&ex, r);
+      g = argmax_merge(g, ArgMax{e->amax, e->aidx});
+    }
+    tok = g.i == 0x7fffffff ? 0 : g.i;
+  } else {
+    if (rank == 0) {
+      rng_prepare(st, b, 2, rc);
+      if (threadIdx.x == 0) ex.u = draw_sample_u(st, b, st.round[b], j, rc);
+    }
+    // get_probs (src/nn/layer.cpp:1425-1449): x / T, the row max, exp-sum
+    const float T = st.T;
+    const bool t1 = T == 1.f;
+    float mx = -INFINITY, se = 0.f;
+    for (int v = threadIdx.x; v < n; v += blockDim.x) {
+      const float x = t1 ? srow[v] : __fdiv_rn(srow[v], T);
+      srow[v] = x;
+      if (x > mx) {
+        se = se * expf(mx - x) + 1.f;
+        mx = x;
+      } else {
+        se += expf(x - mx);
+      }
+    }
+    const float bm = block_max(mx, sh.red);
+    const float bs = block_sum(mx == -INFINITY ? 0.f : se * expf(mx - bm), sh.red);
+    if (threadIdx.x == 0) { ex.mx = bm; ex.se = bs; }
+    cl.sync();
+    float Mx = -INFINITY;
+    for (int r = 0; r < CS; ++r) Mx = fmaxf(Mx, cl.map_shared_rank(&ex, r)->mx);
+    float S = 0.f;
+    for (int r = 0; r < CS; ++r) {
+      const SampClusterEx *e = cl.map_shared_rank(&ex, r);
+      if (e->mx != -INFINITY) S += e->se * expf(e->mx - Mx);
+    }
+    const double u = cl.map_shared_rank(&ex, 0)->u;
+    float fs = 0.f;
+    for (int v = threadIdx.x; v < n; v += blockDim.x) {
+      const float p = __fdiv_rn(expf(__fsub_rn(srow[v], Mx)), S);
+      srow[v] = p;
+      fs += p;
+    }
+    fs = block_sum(fs, sh.red);
+    __syncthreads();
+    if (threadIdx.x == 0) ex.fs = fs;
+    cl.sync();
+    float FS = 0.f;
+    for (int r = 0; r < CS; ++r) FS += cl.map_shared_rank(&ex, r)->fs;
+    for (int v = threadIdx.x; v < n; v += blockDim.x) srow[v] = __fdiv_rn(srow[v], FS);
+    __syncthreads();
+    store_row(srow, n, st.q + (static_cast<size_t>(b) * st.kmax + j) * V + v0);  // q_j, read by accept
+    // sample_token (src/nn/layer.cpp:1493-1498) over the whole row: this
+    // rank's fp64 slice sum, the ranks below it, then the first hit
+    const int C = (n + blockDim.x - 1) / blockDim.x;
+    const int lo = min(n, static_cast<int>(threadIdx.x) * C), hi = min(n, lo + C);
+    double loc = 0.0;
+    int last_nz = -1;
+    for (int v = lo; v < hi; ++v) {
+      loc += static_cast<double>(srow[v]);
+      if (srow[v] > 0.f) last_nz = v0 + v;
+    }
+    double slice_tot;
+    double cum = block_exscan_d(loc, sh.redd, &slice_tot);
+    if (threadIdx.x == 0) ex.tot = slice_tot;
+    cl.sync();
+    double below = 0.0, total = 0.0;
+    for (int r = 0; r < CS; ++r) {
+      const double t = cl.map_shared_rank(&ex, r)->tot;
+      if (r < rank) below += t;
+      total += t;
+    }
+    cum += below;
+    int pick = 0x7fffffff;
+    const double thr = u * total;
+    for (int v = lo; v < hi; ++v) {
+      cum += static_cast<double>(srow[v]);
+      const bool hit = (st.rng_mode == 0) ? (v0 + v == V - 1 || cum / total >= u) : (cum > thr);
+      if (hit) {
+        pick = v0 + v;
+        break;
+      }
+    }
+    int m = pick, lz = last_nz;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      m = min(m, __shfl_xor_sync(0xffffffffu, m, o));
+      lz = max(lz, __shfl_xor_sync(0xffffffffu, lz, o));
+    }
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    __syncthreads();
+    if (lane == 0) {
+      sh.redi[wid] = m;
+      sh.redi[32 + wid] = lz;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int bm2 = 0x7fffffff, bl = -1;
+      for (int w = 0; w < nw; ++w) {
+        bm2 = min(bm2, sh.redi[w]);
+        bl = max(bl, sh.redi[32 + w]);
+      }
+      ex.pick = bm2;
+      ex.lastnz = bl;
+    }
+    cl.sync();
+    int gm = 0x7fffffff, gl = -1;
+    for (int r = 0; r < CS; ++r) {
+      const SampClusterEx *e = cl.map_shared_rank(&ex, r);
+      gm = min(gm, e->pick);
+      gl = max(gl, e->lastnz);
+    }
+    tok = gm != 0x7fffffff ? gm : (gl < 0 ? 0 : gl);
+    if (rank == 0) rng_commit(st, b, rc);
+  }
+  cl.sync();  // no rank leaves while another still reads its shared memory
+  if (rank != 0) return;
+  pdl_launch();
   if (threadIdx.x == 0) {
     cand[j] = tok;
     if (j + 1 < M) {

@@ -36,7 +36,7 @@ EXPORTS = ("specdec_create", "specdec_destroy", "specdec_last_error", "specdec_l
            "specdec_generate", "specdec_generate_device", "specdec_stream", "specdec_forward_logits",
            "specdec_philox_uniforms", "specdec_last_launch_count", "specdec_forward_logits_noalloc",
            "specdec_time_linear", "specdec_generate_tree", "specdec_generate_tree_device", "specdec_tp_unique_id",
-           "specdec_create_tp", "specdec_generate_ar", "specdec_generate_ar_device")
+           "specdec_create_tp", "specdec_generate_ar", "specdec_generate_ar_device", "specdec_load_netw")
 
 # linear layers of specdec_time_linear
 LIN_QKV, LIN_OPROJ, LIN_FFN_IN, LIN_FFN_OUT, LIN_HEAD = 0, 1, 2, 3, 4
@@ -92,6 +92,7 @@ def load_library(path: str = LIB_PATH):
                                      C.c_void_p, C.c_void_p]
     lib.specdec_generate_device.argtypes = [C.c_void_p, C.POINTER(_GenParams), C.c_void_p, C.c_int, C.c_int,
                                             C.c_void_p, C.c_void_p]
+    lib.specdec_load_netw.argtypes = [C.c_void_p, C.c_int, C.c_char_p]
     lib.specdec_generate_ar.argtypes = lib.specdec_generate.argtypes
     lib.specdec_generate_ar_device.argtypes = lib.specdec_generate_device.argtypes
     lib.specdec_stream.restype = C.c_void_p
@@ -186,6 +187,11 @@ class Engine:
         ptrs = (C.c_void_p * len(arrs))(*[a.ctypes.data for a in arrs])
         nums = (C.c_int64 * len(arrs))(*[a.size for a in arrs])
         self._check(self._lib.specdec_load_params(self.h, role, len(arrs), ptrs, nums))
+
+    def load_weights(self, role: int, path: str) -> None:
+        """Layer::load_weights: the model's parameters from a NETW v1 file (the
+        reference's serialization format, src/core/serialization.cpp:49-107)."""
+        self._check(self._lib.specdec_load_netw(self.h, role, os.fsencode(path)))
 
     def _params(self, max_new, lookahead, temperature, top_k, top_p, seed, uniforms, draft_catchup):
         if uniforms is not None:

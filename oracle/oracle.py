@@ -62,6 +62,8 @@ class _RefLib:
             lib.nnref_get_param.argtypes = [C.c_void_p, C.c_int, _f32p, C.c_size_t]
             lib.nnref_set_requires_grad.argtypes = [C.c_void_p, C.c_int]
             lib.nnref_forward.argtypes = [C.c_void_p, _i64p, C.c_size_t, _f32p]
+            lib.nnref_save_weights.argtypes = [C.c_void_p, C.c_char_p]
+            lib.nnref_load_weights.argtypes = [C.c_void_p, C.c_char_p]
             lib.nnref_generate.argtypes = [C.c_void_p, _i64p, C.c_size_t, C.c_size_t, _i64p, C.c_size_t,
                                            C.POINTER(C.c_size_t)]
             lib.nnref_generate_advanced.argtypes = [C.c_void_p, _i64p, C.c_size_t, C.c_size_t, C.c_float,
@@ -111,6 +113,13 @@ class Reference:
         out = np.zeros((t.size, self.shape.vocab), np.float32)
         _ref_check(_RefLib.get().nnref_forward(self.h, t, t.size, out))
         return out
+
+    def save_weights(self, path: str) -> None:
+        """Layer::save_weights: the reference's NETW v1 parameter file."""
+        _ref_check(_RefLib.get().nnref_save_weights(self.h, os.fsencode(path)))
+
+    def load_weights(self, path: str) -> None:
+        _ref_check(_RefLib.get().nnref_load_weights(self.h, os.fsencode(path)))
 
     def _tokens_call(self, fn, prompt, max_new, *args):
         p = np.ascontiguousarray(prompt, np.int64)

@@ -11,6 +11,8 @@
 //   * TransformerDecoder::forward (src/nn/layer.cpp:1161-1193),
 //   * generate / generate_advanced / generate_speculative
 //     (src/nn/layer.cpp:1195-1661),
+//   * Layer::save_weights / load_weights, the NETW v1 parameter file
+//     (src/nn/layer.cpp:463-469, src/core/serialization.cpp:8-107),
 //   * Tensor::rope (src/core/tensor.cpp:1126-1166) and the QuantizedDense
 //     per-channel int8 quantiser (src/nn/quantization.cpp:7-66).
 //
@@ -169,6 +171,14 @@ int nnref_generate_speculative(void *target, void *draft, const int64_t *prompt,
                  temperature, top_k, top_p, seed, quantized_cache != 0),
              out, cap, n_out);
   });
+}
+
+// Layer::save_weights / Layer::load_weights of the decoder.
+int nnref_save_weights(void *h, const char *path) {
+  return guard([&] { static_cast<RefModel *>(h)->dec->save_weights(path); });
+}
+int nnref_load_weights(void *h, const char *path) {
+  return guard([&] { static_cast<RefModel *>(h)->dec->load_weights(path); });
 }
 
 // Tensor::rope on a [B, H, S, D] tensor at offset S_past.

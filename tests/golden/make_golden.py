@@ -8,7 +8,9 @@ its own sources by oracle/Makefile into oracle/_ref/libnnref.so):
 Every case injects seeded weights (neural-network_b200/specdec_b200/synth.py)
 into reference TransformerDecoder objects and records what the reference
 returns: forward logits, generate_advanced and generate_speculative tokens in
-greedy, sampled (std::mt19937), top-k/top-p and int8-KV modes.  The shapes
+greedy, sampled (std::mt19937), top-k/top-p and int8-KV modes, and the NETW
+v1 weight files the reference writes for two of the targets.  (Logits depend
+on OpenBLAS's thread count at the 1e-7 level; the tests allow 1e-5.)  The shapes
 include the reference's own test models (tests/nn/transformer_test.cpp:
 vocab 8/6, d_model 8, 2 heads, FFN 16, 2 target layers, 1 draft layer) and a
 config-1-shaped model cut down to two layers.  These fixtures pin the CPU
@@ -37,6 +39,9 @@ MODELS = [
     ("small", ModelShape(vocab=97, d_model=32, n_heads=4, d_ff=64, n_layers=2, max_seq_len=160), 1, 13, 9, 0.02),
     ("cfg1cut", ModelShape(vocab=2048, d_model=256, n_heads=4, d_ff=1024, n_layers=2, max_seq_len=96), 1, 0, 6, 0.0),
 ]
+
+# targets whose NETW v1 weight file (Layer::save_weights) is kept as a fixture
+NETW_MODELS = ("tiny8", "small")
 
 # (tag, max_new, lookahead, T, top_k, top_p, seed, quantized_cache)
 SPEC_CASES = [
@@ -76,6 +81,9 @@ def main() -> None:
         out[f"{name}/ar_greedy"] = tgt.generate_advanced(prompt, 12, 0.0, 0, 1.0, 42, True)
         out[f"{name}/ar_greedy_nocache"] = tgt.generate_advanced(prompt, 12, 0.0, 0, 1.0, 42, False)
         out[f"{name}/ar_t09"] = tgt.generate_advanced(prompt, 12, 0.9, 5, 0.8, 7, True)
+        if name in NETW_MODELS:
+            # the reference's own weight file of this target (Layer::save_weights)
+            tgt.save_weights(os.path.join(os.path.dirname(OUT), f"{name}_target.netw"))
         print(f"{name}: {n_case} speculative cases")
     # known answers of the reference's own unit tests
     x = np.array([1, 2, 3, 4, 5, 6, 7, 8], np.float32).reshape(1, 1, 2, 4)
