@@ -221,6 +221,7 @@ struct specdec_handle {
   bool use_pdl = true;  // programmatic dependent launch for the kernels that support it
   int gemm_max_split = 1;  // largest split-K cluster of the tensor-core GEMM
   int gemm_clusters[kGemmMaxSplit + 1] = {};  // split-K clusters of ks CTAs resident at once
+  float *gemm_ws = nullptr;  // split-K partial tiles [tile * ks + rank][column][row]
   int samp_max_cluster = 1;  // largest cluster of draft_sample_cluster_kernel
   int attn_ctas_per_sm = 2;  // attention splits the cache while the grid stays within this many CTAs per SM
   // row batches that take the tensor-core GEMM instead of the GEMV: at least
@@ -228,7 +229,7 @@ struct specdec_handle {
   // gemm_wide_elems weights
   int gemm_min_rows = kGemmMinRows;
   int gemm_wide_rows = 16;
-  long long gemm_wide_elems = 4ll << 20;
+  long long gemm_wide_elems = 2ll << 20;  // measured: the medium model's FFN down-projection (2.4M) at 32 rows
 
   void *dalloc(size_t bytes, std::vector<void *> *owner = nullptr) {
     void *p = nullptr;
@@ -668,8 +669,9 @@ void launch_ln_rows(specdec_handle *h, const LinearArgs &a, void *dst) {
 // (norm_out) or into X1, which is free whenever a LayerNorm feeds a GEMM.
 template <int EPI>
 bool try_launch_gemm(specdec_handle *h, LinearArgs a) {
-  // >= kGemmMinRows rows, or >= 16 rows of a wide layer (the lm_head): the GEMM
-  // reads each weight once, where 8-row GEMV tiles would re-read it per tile
+  // >= kGemmMinRows rows, or >= 16 rows of a layer of >= 2M weights (the
+  // lm_head, long FFN projections): the GEMM reads each weight once, where
+  // 8-row GEMV tiles would re-read it per tile
   const bool wide = a.R >= h->gemm_wide_rows && static_cast<long long>(a.N) * a.K >= h->gemm_wide_elems;
   if (!act_bf16(h) || !w_int8(h) || (a.R < h->gemm_min_rows && !wide) || (a.K % 8) != 0) return false;
   if (a.in_g && !ln_rows_ok(a)) return false;
@@ -704,10 +706,11 @@ bool try_launch_gemm(specdec_handle *h, LinearArgs a) {
   const int gx = (a.N + kBN - 1) / kBN, gy = (a.R + kBM - 1) / kBM;
   const int nk = (a.K + kBK - 1) / kBK;
   int ks = 1;
-  while (2 * ks <= h->gemm_max_split && gx * gy * 2 * ks <= h->num_sms && 2 * ks <= nk &&
+  while (h->gemm_ws && 2 * ks <= h->gemm_max_split && gx * gy * 2 * ks <= h->num_sms && 2 * ks <= nk &&
          gx * gy <= h->gemm_clusters[2 * ks])  // all clusters in one wave
     ks *= 2;
   g.ksplit = ks;
+  g.ws = h->gemm_ws;
   if (ks == 1)
     launch(h, gemm_kernel<EPI>, dim3(gx, gy), dim3(kGemmThreads), static_cast<size_t>(kGemmSmem), g);
   else
@@ -1591,6 +1594,10 @@ int create_impl(const specdec_config *cfg, int device, int rank, int world, cons
       h->KVN = static_cast<float *>(
           h->dalloc(static_cast<size_t>(h->R_max) * 2 * std::max(td.kvd, dd.kvd) * sizeof(float)));
     h->logits = static_cast<float *>(h->dalloc(static_cast<size_t>(R_round) * td.V * sizeof(float)));
+    // split-K partial tiles of the tensor-core GEMM: at most one per SM
+    // (tiles x splits <= SMs), fp32 128 x 256 each
+    if (cfg->act_dtype == SPECDEC_BF16 && cfg->weight_dtype == SPECDEC_INT8 && h->gemm_max_split > 1)
+      h->gemm_ws = static_cast<float *>(h->dalloc(static_cast<size_t>(h->num_sms) * kBM * kBN * sizeof(float)));
     h->logits_rows = R_round;
     h->tree_base =
         h->R_max + 2 * B + (k - 1) * B + B * (k + 1);

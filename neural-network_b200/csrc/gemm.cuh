@@ -17,10 +17,16 @@
 // Split-K for grids of few tiles (verify blocks of a few hundred rows through
 // narrow layers): the ksplit CTAs of one tile form a thread-block cluster
 // along z, rank z multiplying k-blocks [z nk / ks, (z + 1) nk / ks).  Their
-// partial tiles meet in distributed shared memory (each rank sends column
-// slice j of its accumulators to rank j, into the freed TMA ring), and rank j
-// adds the ks partials in rank order (the same sum on every run) and runs the
-// epilogue on its 256 / ks columns.
+// partial tiles meet in an L2-resident workspace (column-major, so a warp's
+// stores and loads are contiguous; distributed shared memory measured several
+// times slower for 128 KB per CTA), the cluster barrier orders them, and rank
+// j adds the ks partials of its column slice in rank order (the same sum on
+// every run) and runs the epilogue on its 256 / ks columns.
+//
+// Epilogue.  The residual operand is staged in the freed ring with
+// coalesced row loads (one memory round trip instead of one per chunk), and
+// store / residual / GELU / SwiGLU outputs are staged there too and written
+// by whole rows with coalesced 16-byte stores.
 #pragma once
 
 #include <cuda.h>
@@ -49,27 +55,18 @@ struct alignas(64) GemmArgs {
   LinearArgs lin;     // epilogue operands (out, scale, bias, resid, rows, qkv), R, N, K
   int *err;
   int ksplit;         // CTAs per tile along z (a cluster), 1, 2, 4 or 8
+  float *ws;          // split-K partial tiles: [tile * ksplit + rank][kBN columns][kBM rows] fp32
 };
 
-// Receive buffer of the split-K exchange, in the freed ring: [ks][kBM rows]
-// [256 / ks + 4 floats] (the 16-byte pad keeps a warp's row-strided 16-byte
-// accesses free of bank conflicts).
-__host__ __device__ constexpr int gemm_split_stride(int ks) { return kBN / ks + 4; }
-static_assert(kGemmMaxSplit * kBM * (kBN / kGemmMaxSplit + 4) * 4 <= kStages * kGemmStageBytes,
-              "split-K exchange must fit the TMA ring");
+// The freed ring holds the epilogue's residual slice and output staging,
+// rows padded by 16 bytes.
+static_assert(kBM * (kBN * 2 + 16) * 2 <= kStages * kGemmStageBytes && kBM * (kBN * 4 + 16) <= kStages * kGemmStageBytes,
+              "epilogue staging must fit the TMA ring");
 
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-__device__ __forceinline__ uint32_t cluster_map(uint32_t saddr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-  return r;
-}
-__device__ __forceinline__ void st_cluster_f4(uint32_t addr, float a, float b, float c, float d) {
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
-}
+
 
 // Shared-memory matrix descriptor of a K-major operand tile whose rows are
 // 128 bytes with the 128-byte swizzle: 8-row core groups 1024 bytes apart
@@ -116,6 +113,30 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Loads without waiting: 16 accumulator columns of the warp's 32 lanes; the
+// values are valid after tmem_wait_ld().  Several loads share one wait, so
+// their latencies overlap.
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
+      "[%16];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// 64 consecutive accumulator columns (four loads, one wait).
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
+  uint32_t r[4][16];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) tmem_ld16_nowait(taddr + 16 * q, r[q]);
+  tmem_wait_ld();
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[16 * q + i] = __uint_as_float(r[q][i]);
 }
 
 // Row operands of one 16-column chunk (columns n .. n + 15 of row `row`),
@@ -172,6 +193,29 @@ __device__ __forceinline__ void chunk_load(const LinearArgs &a, int row, int n, 
         op.v[j] = 1.f;
         op.v[j + 1] = 0.f;
       }
+    }
+  }
+}
+
+// Arithmetic of the staged epilogues (store, residual, GELU, SwiGLU) on one
+// 16-column chunk in place; SwiGLU leaves its 8 outputs in v[0 .. 7].  The
+// same operations, in the same order, as chunk_store.
+template <int EPI>
+__device__ __forceinline__ void chunk_apply(float (&v)[16], const ChunkOps &op, const float *ssc, const float *sbi) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = v[j] * ssc[j] + sbi[j];
+  if constexpr (EPI == kEpiResid) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = v[j] + op.v[j];
+  } else if constexpr (EPI == kEpiGelu) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = 0.5f * v[j] * (1.0f + erff(v[j] * 0.70710678118654752f));
+  } else if constexpr (EPI == kEpiSwiGLU) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float g = v[2 * i], u = v[2 * i + 1];
+      const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
+      v[i] = __fmul_rn(__fmul_rn(g, sg), u);
     }
   }
 }
@@ -362,62 +406,149 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     slot = row_ok ? row_slot(a.rows, row) : 0;
   }
   const int ncols = min(kBN, a.N - n0);
-  if (ks > 1) {
-    // split-K: every rank's MMAs are done (its ring is free) before any
-    // partial is sent; all sends land before any rank reduces
-    cluster_sync_all();
-    const int sw = kBN / ks, ld = gemm_split_stride(ks);
-    const uint32_t tbase = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    const uint32_t mine = smem_u32(tiles) + static_cast<uint32_t>(((z * kBM + warp * 32 + lane) * ld) * 4);
-    for (int j = 0; j < ks; ++j) {
-      const uint32_t dst = cluster_map(mine, j);
-      for (int c = 0; c < sw && j * sw + c < ncols; c += 16) {
-        float v[16];
-        tmem_ld16(tbase + j * sw + c, v);
-        if (!ok) {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) v[i] = 0.f;
+  const int lr = warp * 32 + lane;  // this thread's tile row (accumulator lane)
+  const uint32_t tbase = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+  // this CTA's output columns within the tile: all 256, or its split-K slice
+  const int ew = kBN / ks, ec0 = z * ew;
+  const int ecols = max(0, min(ew, ncols - ec0));
+  const int wrows = max(0, min(32, a.R - m0 - warp * 32));  // valid rows of this warp (uniform)
+  // The ring is free once every MMA is done: [split-K exchange][residual
+  // slice][output staging], each row padded by 16 bytes (a warp's row-strided
+  // 16-byte accesses then hit distinct bank groups).
+  unsigned char *rstage = tiles;
+  const int rs_ld = ew * 2 + 16;
+  if constexpr (EPI == kEpiResid) {
+    // the residual slice, row by row with coalesced 16-byte asynchronous
+    // copies, all in flight at once (one memory round trip)
+    const int nu = (ecols + 7) / 8;
+    if (ok && lane < nu) {
+      for (int rr = 0; rr < wrows; ++rr) {
+        const __nv_bfloat16 *src =
+            static_cast<const __nv_bfloat16 *>(a.resid) + static_cast<size_t>(m0 + warp * 32 + rr) * a.ldr + n0 + ec0;
+        unsigned char *dst = rstage + (warp * 32 + rr) * rs_ld + lane * 16;
+        if (lane * 8 + 8 <= ecols) {
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)),
+                       "l"(reinterpret_cast<const uint4 *>(src) + lane)
+                       : "memory");
+        } else {
+          uint32_t w[4] = {0u, 0u, 0u, 0u};
+          const unsigned short *sp = reinterpret_cast<const unsigned short *>(src);
+          for (int e = 0; e < 8 && lane * 8 + e < ecols; ++e)
+            w[e >> 1] |= static_cast<uint32_t>(sp[lane * 8 + e]) << ((e & 1) * 16);
+          *reinterpret_cast<uint4 *>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
         }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) st_cluster_f4(dst + (c + 4 * i) * 4, v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
       }
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncwarp();
+  }
+  auto resid_chunk = [&](int c, ChunkOps &op) {  // c: column within this CTA's slice
+    const uint4 *sp = reinterpret_cast<const uint4 *>(rstage + lr * rs_ld + c * 2);
+    bf16x8_to_f32(sp[0], op.v);
+    bf16x8_to_f32(sp[1], op.v + 8);
+  };
+
+  if (ks > 1) {
+    // split-K: every rank stores its partial tile column by column (a warp
+    // covers 128 contiguous bytes) into the L2-resident workspace; after the
+    // cluster barrier rank z sums column slice z of the ks partials in rank
+    // order (the same sum on every run) and runs the epilogue on it.
+    const size_t tile = static_cast<size_t>(blockIdx.x) + static_cast<size_t>(gridDim.x) * blockIdx.y;
+    float *mine = g.ws + (tile * ks + z) * (kBN * kBM) + lr;
+    for (int c0 = 0; c0 < ncols; c0 += 64) {
+      float v[64];
+      tmem_ld64(tbase + c0, v);
+#pragma unroll
+      for (int i = 0; i < 64; ++i)
+        if (c0 + i < ncols) mine[(c0 + i) * kBM] = ok ? v[i] : 0.f;
+    }
+    __threadfence();
     cluster_sync_all();
-    const float *buf = reinterpret_cast<const float *>(tiles);
-    const int rl = warp * 32 + lane;
-    for (int c = 0; c < sw && z * sw + c < ncols; c += 16) {
+    const float *part = g.ws + tile * ks * (kBN * kBM) + static_cast<size_t>(ec0) * kBM + lr;
+    for (int c = 0; c < ecols; c += 16) {
       float v[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) v[i] = 0.f;
-      for (int zz = 0; zz < ks; ++zz) {
-        const float4 *src = reinterpret_cast<const float4 *>(buf + (zz * kBM + rl) * ld + c);
+      for (int zz = 0; zz < ks; ++zz)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float4 t = src[i];
-          v[4 * i] += t.x; v[4 * i + 1] += t.y; v[4 * i + 2] += t.z; v[4 * i + 3] += t.w;
-        }
-      }
+        for (int i = 0; i < 16; ++i) v[i] += __ldcg(part + static_cast<size_t>(zz) * (kBN * kBM) + (c + i) * kBM);
       if (row_ok && ok) {
-        const int n = n0 + z * sw + c;
+        const int n = n0 + ec0 + c;
         ChunkOps op;
-        chunk_load<EPI>(a, row, n, req, pos, op);
-        chunk_store<EPI>(a, row, n, v, op, s_scale + z * sw + c, s_bias + z * sw + c, req, pos, slot);
+        if constexpr (EPI == kEpiResid) resid_chunk(c, op);
+        else chunk_load<EPI>(a, row, n, req, pos, op);
+        chunk_store<EPI>(a, row, n, v, op, s_scale + ec0 + c, s_bias + ec0 + c, req, pos, slot);
       }
     }
   } else if (ok) {
-    // chunks of 16 columns, the next chunk's row operands in flight
-    const uint32_t tbase = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    ChunkOps op0, op1;
-    if (row_ok) chunk_load<EPI>(a, row, n0, req, pos, op0);
-    for (int c = 0; c < ncols; c += 32) {
-      float v[16];
-      if (row_ok && c + 16 < ncols) chunk_load<EPI>(a, row, n0 + c + 16, req, pos, op1);
-      tmem_ld16(tbase + c, v);
-      if (row_ok) chunk_store<EPI>(a, row, n0 + c, v, op0, s_scale + c, s_bias + c, req, pos, slot);
-      if (c + 16 >= ncols) break;  // warp-uniform
-      if (row_ok && c + 32 < ncols) chunk_load<EPI>(a, row, n0 + c + 32, req, pos, op0);
-      tmem_ld16(tbase + c + 16, v);
-      if (row_ok) chunk_store<EPI>(a, row, n0 + c + 16, v, op1, s_scale + c + 16, s_bias + c + 16, req, pos, slot);
+    if constexpr (EPI == kEpiQKV) {
+      // chunks of 16 columns, the next chunk's RoPE operands in flight
+      ChunkOps op0, op1;
+      if (row_ok) chunk_load<EPI>(a, row, n0, req, pos, op0);
+      for (int c = 0; c < ncols; c += 32) {
+        float v[16];
+        if (row_ok && c + 16 < ncols) chunk_load<EPI>(a, row, n0 + c + 16, req, pos, op1);
+        tmem_ld16(tbase + c, v);
+        if (row_ok) chunk_store<EPI>(a, row, n0 + c, v, op0, s_scale + c, s_bias + c, req, pos, slot);
+        if (c + 16 >= ncols) break;  // warp-uniform
+        if (row_ok && c + 32 < ncols) chunk_load<EPI>(a, row, n0 + c + 32, req, pos, op0);
+        tmem_ld16(tbase + c + 16, v);
+        if (row_ok) chunk_store<EPI>(a, row, n0 + c + 16, v, op1, s_scale + c + 16, s_bias + c + 16, req, pos, slot);
+      }
+    } else {
+      // outputs staged in shared memory by row, then stored by the warp with
+      // coalesced 16-byte stores
+      const bool f32 = a.out_f32 != 0 && EPI != kEpiSwiGLU;
+      const int oelt = f32 ? 4 : 2;
+      const int ow = EPI == kEpiSwiGLU ? ew / 2 : ew;
+      const int os_ld = ow * oelt + 16;
+      unsigned char *ostage = rstage + (EPI == kEpiResid ? kBM * rs_ld : 0);
+      unsigned char *orow = ostage + lr * os_ld;
+      for (int c0 = 0; c0 < ncols; c0 += 64) {
+        float vv[64];
+        tmem_ld64(tbase + c0, vv);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int c = c0 + 16 * q;
+          if (c >= ncols) break;  // warp-uniform
+          float v[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] = vv[16 * q + i];
+          ChunkOps op;
+          if constexpr (EPI == kEpiResid) resid_chunk(c, op);
+          chunk_apply<EPI>(v, op, s_scale + c, s_bias + c);
+          if constexpr (EPI == kEpiSwiGLU) {
+            *reinterpret_cast<uint4 *>(orow + (c / 2) * 2) = f32x8_to_bf16(v);
+          } else if (f32) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              reinterpret_cast<float4 *>(orow + c * 4)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          } else {
+            reinterpret_cast<uint4 *>(orow + c * 2)[0] = f32x8_to_bf16(v);
+            reinterpret_cast<uint4 *>(orow + c * 2)[1] = f32x8_to_bf16(v + 8);
+          }
+        }
+      }
+      __syncwarp();
+      const int ocols = EPI == kEpiSwiGLU ? ncols / 2 : ncols;  // valid output columns (N even for SwiGLU)
+      const int obytes = ocols * oelt;
+      const size_t ocol0 = EPI == kEpiSwiGLU ? static_cast<size_t>(n0 / 2) : static_cast<size_t>(n0);
+      for (int rr = 0; rr < wrows; ++rr) {
+        unsigned char *gdst = static_cast<unsigned char *>(a.out) +
+                              (static_cast<size_t>(m0 + warp * 32 + rr) * a.ldo + ocol0) * oelt;
+        const unsigned char *ssrc = ostage + (warp * 32 + rr) * os_ld;
+        for (int u = lane; u * 16 < obytes; u += 32) {
+          if (u * 16 + 16 <= obytes) {
+            *reinterpret_cast<uint4 *>(gdst + u * 16) = *reinterpret_cast<const uint4 *>(ssrc + u * 16);
+          } else if (f32) {
+            for (int e = u * 4; e < ocols; ++e)
+              reinterpret_cast<float *>(gdst)[e] = reinterpret_cast<const float *>(ssrc)[e];
+          } else {
+            for (int e = u * 8; e < ocols; ++e)
+              reinterpret_cast<unsigned short *>(gdst)[e] = reinterpret_cast<const unsigned short *>(ssrc)[e];
+          }
+        }
+      }
     }
   }
   tc_fence_before();
