@@ -1,0 +1,267 @@
+// Attention on the tensor cores for bf16 queries and a bf16 K/V cache with
+// head_dim 64, for groups of many queries (token-tree verify blocks, prefill
+// chunks): the same arithmetic as attention_kernel (src/nn/layer.cpp:859-948,
+// score = q . k / sqrt(D), softmax over the visible positions, then P.V) with
+// the two products as tcgen05 MMAs.
+//
+// A CTA takes up to 128 queries of one group (one request) and one head and
+// walks the request's cache in tiles of 128 positions:
+//   S = Q K^T      M = 128 queries, N = 128 positions, K = 64: A = the query
+//                  tile (TMA, 128-byte swizzle, K-major), B = the K tile as
+//                  the cache stores it (positions x dims: K-major);
+//                  fp32 accumulators in TMEM columns [0, 128)
+//   softmax        thread = query row = TMEM lane: the row's 128 scores are
+//                  read with tcgen05.ld, masked (causal, tree ancestors),
+//                  scaled by 1/8 and folded into the row's running max / sum
+//   O_t = P V      M = 128, N = 64 dims, K = 128 positions: A = P as bf16 in
+//                  shared memory (written by the threads in the 128-byte
+//                  swizzled K-major layout), B = the V tile as the cache
+//                  stores it (positions x dims: MN-major, 1024-byte groups of
+//                  8 positions); TMEM columns [128, 192)
+//   o = o * alpha + O_t in registers (the running rescale of the online softmax).
+// K and V tiles stream through a two-stage TMA ring: tile t + 1 loads while
+// tile t is multiplied.  P is rounded to bf16 for the second product (an
+// error of at most 2^-9 relative per probability; bf16 activations already
+// round every layer output to 8 bits).  Every mbarrier wait is bounded; on
+// a timeout the CTA flags kErrTimeout and writes nothing.
+#pragma once
+
+#include "gemm.cuh"
+
+namespace specdec {
+
+constexpr int kAtcThreads = 128;
+constexpr int kAtcTile = 128;            // positions per tile
+constexpr int kAtcD = 64;                // head dimension of this path
+constexpr int kAtcMinQ = 16;             // groups with fewer queries keep attention_kernel
+constexpr int kAtcQBytes = 128 * 128;    // Q tile: 128 rows x 64 bf16
+constexpr int kAtcKVBytes = 128 * 128;   // K or V tile: 128 positions x 64 bf16
+constexpr int kAtcPBytes = 2 * 128 * 128;  // P: 128 queries x 128 positions bf16, two 64-position blocks
+constexpr int kAtcSmem = kAtcQBytes + 2 * 2 * kAtcKVBytes + kAtcPBytes + 1024;
+constexpr int kAtcTmemCols = 256;        // S: 128 columns, O_t: 64 columns
+
+// kind::f16, D fp32, A and B bf16; S: both K-major, N = 128; O: B MN-major, N = 64.
+constexpr uint32_t kAtcIdescS = (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(128 >> 3) << 17) |
+                                (static_cast<uint32_t>(128 >> 4) << 24);
+constexpr uint32_t kAtcIdescO = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) |
+                                (static_cast<uint32_t>(64 >> 3) << 17) | (static_cast<uint32_t>(128 >> 4) << 24);
+
+// MN-major operand with the 128-byte swizzle whose MN extent is one 128-byte
+// atom (64 bf16): rows along K 128 bytes apart, groups of 8 rows 1024 bytes
+// apart (stride byte offset); the leading byte offset (between atoms along
+// MN) is not used.
+__device__ __forceinline__ uint64_t umma_desc_mn128(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+struct alignas(64) AttnTcArgs {
+  CUtensorMap tmq;       // [R][dq] bf16 query rows, box 64 x 128
+  CUtensorMap tmk, tmv;  // [slot * Hkv * S_cap + position][64] bf16, box 64 x 128 (the attention_kernel maps)
+  RowsView rows;
+  int R, Q;              // rows, queries per group
+  int S_cap, H, Hkv;
+  __nv_bfloat16 *out;    // [R][ldo]
+  int ldo;
+  int *err;
+};
+
+__global__ void __launch_bounds__(kAtcThreads, 1) attn_tc_kernel(const __grid_constant__ AttnTcArgs a) {
+  pdl_wait();
+  extern __shared__ unsigned char atc_smem_raw[];
+  unsigned char *sm =
+      reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(atc_smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char *sq = sm;                                   // Q tile
+  unsigned char *skv = sq + kAtcQBytes;                     // stage s: K at skv + s * 2 * kAtcKVBytes, V after it
+  unsigned char *sp = skv + 2 * 2 * kAtcKVBytes;            // P, two blocks of 64 positions
+  __shared__ __align__(8) uint64_t bar_q, bar_kv[2], bar_s, bar_o;
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_req, s_maxpos, s_fail;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ngt = (a.Q + 127) / 128;
+  const int g = blockIdx.x / ngt, qt = blockIdx.x % ngt;
+  const int h = blockIdx.y;
+  const int rq0 = g * a.Q + qt * 128;
+  const int nq = max(0, min(128, min(a.Q - qt * 128, a.R - rq0)));
+  const int hk = h / (a.H / a.Hkv);
+
+  // this thread's query row
+  const int r = threadIdx.x;
+  const bool qv = r < nq;
+  const int qreq = qv ? a.rows.req[rq0 + r] : -1;
+  const int qpos = (qv && qreq >= 0) ? row_slot(a.rows, rq0 + r) : -1;
+  const int qtb = (qv && a.rows.tb) ? a.rows.tb[rq0 + r] : 0x7fffffff;
+  const unsigned long long qmask = (qv && a.rows.mask) ? a.rows.mask[rq0 + r] : 0ull;
+
+  if (threadIdx.x == 0) {
+    s_req = -1;
+    s_maxpos = -1;
+    s_fail = 0;
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                 "r"(kAtcTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (threadIdx.x == 32) {
+    mbar_init(&bar_q, 1);
+    mbar_init(&bar_kv[0], 1);
+    mbar_init(&bar_kv[1], 1);
+    mbar_init(&bar_s, 1);
+    mbar_init(&bar_o, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (qreq >= 0) {
+    atomicMax(&s_maxpos, qpos);
+    s_req = qreq;  // every valid row of a group belongs to the same request
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  const int req = s_req, maxpos = s_maxpos;
+  const bool work = req >= 0 && maxpos >= 0 && maxpos < a.S_cap;
+  const int ntiles = work ? maxpos / kAtcTile + 1 : 0;
+  const int row0 = (req * a.Hkv + hk) * a.S_cap;
+
+  auto issue_kv = [&](int t) {  // thread 0
+    const int s = t & 1;
+    unsigned char *kd = skv + s * 2 * kAtcKVBytes;
+    mbar_expect_tx(&bar_kv[s], 2 * kAtcKVBytes);
+    tma_load_2d(kd, &a.tmk, 0, row0 + t * kAtcTile, &bar_kv[s]);
+    tma_load_2d(kd + kAtcKVBytes, &a.tmv, 0, row0 + t * kAtcTile, &bar_kv[s]);
+  };
+  if (threadIdx.x == 0 && ntiles > 0) {
+    mbar_expect_tx(&bar_q, kAtcQBytes);
+    tma_load_2d(sq, &a.tmq, h * kAtcD, rq0, &bar_q);
+    issue_kv(0);
+  }
+
+  float m = -INFINITY, l = 0.f;
+  float o[kAtcD];
+#pragma unroll
+  for (int e = 0; e < kAtcD; ++e) o[e] = 0.f;
+  const uint32_t trow = tmem + (static_cast<uint32_t>(warp * 32) << 16);  // this warp's lanes
+  bool ok = true;
+  if (ntiles > 0 && threadIdx.x == 32) ok = mbar_wait(&bar_q, 0);
+  int t = 0, failed_at = 0;  // 1: waiting for S, 2: waiting for O_t
+  for (; t < ntiles; ++t) {
+    const int s = t & 1;
+    // S = Q K^T (thread 32 issues; the whole CTA waits for the product)
+    if (threadIdx.x == 0 && t + 1 < ntiles) issue_kv(t + 1);  // its stage was released after O_{t-1}
+    if (threadIdx.x == 32) {
+      if (ok) ok = mbar_wait(&bar_kv[s], (t >> 1) & 1);
+      if (ok) {
+        tc_fence_after();
+        const uint32_t qa = smem_u32(sq), ka = smem_u32(skv + s * 2 * kAtcKVBytes);
+#pragma unroll
+        for (int k = 0; k < kAtcD / 16; ++k)
+          tc_mma(tmem, umma_desc_k128(qa + 32 * k), umma_desc_k128(ka + 32 * k), kAtcIdescS, k ? 1u : 0u);
+      }
+      tc_commit(&bar_s);
+    }
+    __syncwarp();
+    ok = __syncthreads_and((threadIdx.x == 32 ? ok : true) && mbar_wait(&bar_s, t & 1)) != 0;
+    if (!ok) {
+      failed_at = 1;
+      break;
+    }
+    tc_fence_after();
+
+    // softmax of this row's 128 scores, read from TMEM twice (max, then P)
+    const int t0 = t * kAtcTile;
+    float tmax = -INFINITY;
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      float sc[64];
+      tmem_ld64(trow + 64 * hf, sc);
+#pragma unroll
+      for (int j = 0; j < 64; ++j) {
+        const int pos = t0 + 64 * hf + j;
+        const bool vis = pos <= qpos && (pos < qtb || (pos - qtb < 64 && ((qmask >> (pos - qtb)) & 1ull)));
+        if (vis) tmax = fmaxf(tmax, sc[j] * 0.125f);  // / sqrt(64): a power of two, so exact
+      }
+    }
+    const float mnew = fmaxf(m, tmax);
+    const float alpha = (m == -INFINITY) ? 0.f : expf(m - mnew);
+    float psum = 0.f;
+    // P (bf16) into the swizzled K-major tile: row r, 16-byte unit uu of
+    // block hf (positions 64 hf ..) lands at unit uu ^ (r & 7) of the row
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      float sc[64];
+      tmem_ld64(trow + 64 * hf, sc);
+#pragma unroll
+      for (int uu = 0; uu < 8; ++uu) {
+        float p[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int pos = t0 + 64 * hf + 8 * uu + e;
+          const bool vis = pos <= qpos && (pos < qtb || (pos - qtb < 64 && ((qmask >> (pos - qtb)) & 1ull)));
+          p[e] = vis ? expf(sc[8 * uu + e] * 0.125f - mnew) : 0.f;
+          psum += p[e];
+        }
+        *reinterpret_cast<uint4 *>(sp + hf * (128 * 128) + r * 128 + ((uu ^ (r & 7)) << 4)) = f32x8_to_bf16(p);
+      }
+    }
+    m = mnew;
+    l = l * alpha + psum;
+    // the P stores must reach the tensor core's (async) view of shared memory
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc_fence_before();
+    __syncthreads();
+    // O_t = P V
+    if (threadIdx.x == 32) {
+      tc_fence_after();
+      const uint32_t pa = smem_u32(sp), va = smem_u32(skv + s * 2 * kAtcKVBytes + kAtcKVBytes);
+#pragma unroll
+      for (int k = 0; k < kAtcTile / 16; ++k)
+        tc_mma(tmem + 128, umma_desc_k128(pa + (k >> 2) * (128 * 128) + 32 * (k & 3)), umma_desc_mn128(va + 2048 * k),
+               kAtcIdescO, k ? 1u : 0u);
+      tc_commit(&bar_o);
+    }
+    __syncwarp();
+    ok = __syncthreads_and(mbar_wait(&bar_o, t & 1) ? 1 : 0) != 0;
+    if (!ok) {
+      failed_at = 2;
+      break;
+    }
+    tc_fence_after();
+    float ot[kAtcD];
+    tmem_ld64(trow + 128, ot);
+#pragma unroll
+    for (int e = 0; e < kAtcD; ++e) o[e] = o[e] * alpha + ot[e];
+    tc_fence_before();
+    __syncthreads();  // S, O_t and P are free for the next tile; so is this K/V stage
+  }
+
+  if (!ok) {
+    // bounded waits for this CTA's copies and products still in flight,
+    // then the error flag
+    if (threadIdx.x == 0) {
+      s_fail = 1;
+      mbar_wait(&bar_q, 0);
+      mbar_wait(&bar_kv[t & 1], (t >> 1) & 1);  // tile t's K / V
+      if (t + 1 < ntiles) mbar_wait(&bar_kv[(t + 1) & 1], ((t + 1) >> 1) & 1);  // the prefetch
+      mbar_wait(failed_at == 1 ? &bar_s : &bar_o, t & 1);  // the product being waited for
+      if (a.err) atomicOr(a.err, kErrTimeout);
+    }
+  } else if (qv && qreq >= 0 && ntiles > 0) {
+    uint4 *dst = reinterpret_cast<uint4 *>(a.out + static_cast<size_t>(rq0 + r) * a.ldo + h * kAtcD);
+#pragma unroll
+    for (int u = 0; u < kAtcD / 8; ++u) {
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = __fdiv_rn(o[8 * u + e], l);
+      dst[u] = f32x8_to_bf16(v);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kAtcTmemCols) : "memory");
+}
+
+}  // namespace specdec

@@ -38,6 +38,7 @@
 #include "../../include/specdec.h"
 #include "forward.cuh"
 #include "gemm.cuh"
+#include "attn_tc.cuh"
 #include "sample.cuh"
 #include "tree.cuh"
 
@@ -224,6 +225,7 @@ struct specdec_handle {
   float *gemm_ws = nullptr;  // split-K partial tiles [tile * ks + rank][column][row]
   int samp_max_cluster = 1;  // largest cluster of draft_sample_cluster_kernel
   int attn_ctas_per_sm = 2;  // attention splits the cache while the grid stays within this many CTAs per SM
+  bool attn_tc = true;       // tensor-core attention for bf16 caches, head_dim 64, groups of >= kAtcMinQ queries
   // row batches that take the tensor-core GEMM instead of the GEMV: at least
   // gemm_min_rows rows, or gemm_wide_rows rows of a layer with at least
   // gemm_wide_elems weights
@@ -914,6 +916,18 @@ void attention(specdec_handle *h, const Dims &dm, RowsView rows, int R, int Q, c
   const size_t nrows = layer_elems / dm.D;
   const bool bf = act_bf16(h);
   const bool kvbf = h->cfg.kv_dtype == SPECDEC_BF16;
+  if (h->attn_tc && bf && kvbf && dm.D == kAtcD && Q >= kAtcMinQ && dm.dq % 8 == 0) {
+    // groups of many queries (token trees, prefill chunks): tensor cores
+    AttnTcArgs t{};
+    t.tmq = gemm_operand_map(h->Q, dm.dq, R, dm.dq, 128);
+    t.tmk = kv_tensor_map<__nv_bfloat16, kAtcD>(kc, nrows);
+    t.tmv = kv_tensor_map<__nv_bfloat16, kAtcD>(vc, nrows);
+    t.rows = rows; t.R = R; t.Q = Q; t.S_cap = S_cap; t.H = dm.H; t.Hkv = dm.Hkv;
+    t.out = static_cast<__nv_bfloat16 *>(h->ATT); t.ldo = dm.dq; t.err = h->st.err;
+    launch_pdl(h, attn_tc_kernel, dim3(ngroups * ((Q + 127) / 128), dm.H), dim3(kAtcThreads),
+               static_cast<size_t>(kAtcSmem), t);
+    return;
+  }
   if (h->cfg.kv_dtype == SPECDEC_INT8) {
     if (bf) launch_attention_t<__nv_bfloat16, int8_t>(h, a, dm.D, ngroups, kc, vc, nrows);
     else launch_attention_t<float, int8_t>(h, a, dm.D, ngroups, kc, vc, nrows);
@@ -1520,6 +1534,8 @@ int create_impl(const specdec_config *cfg, int device, int rank, int world, cons
     if (const char *e = std::getenv("SPECDEC_GEMM_MAX_SPLIT"))  // a lower cap (1: no split-K), for comparisons
       h->gemm_max_split = std::max(1, std::min(h->gemm_max_split, std::atoi(e)));
     if (const char *e = std::getenv("SPECDEC_ATTN_CTAS_PER_SM")) h->attn_ctas_per_sm = std::max(1, std::atoi(e));
+    if (const char *e = std::getenv("SPECDEC_ATTN_TC")) h->attn_tc = std::atoi(e) != 0;  // 0: CUDA-core attention only
+    CK(cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAtcSmem));
     // GEMV / GEMM routing thresholds, for tuning measurements
     if (const char *e = std::getenv("SPECDEC_GEMM_MIN_ROWS")) h->gemm_min_rows = std::max(1, std::atoi(e));
     if (const char *e = std::getenv("SPECDEC_GEMM_WIDE_ROWS")) h->gemm_wide_rows = std::max(1, std::atoi(e));

@@ -317,3 +317,30 @@ def test_spec_large_vocab_cluster_sampler(gpu_lib, oracle_built, monkeypatch, vo
             assert mg[b, : int(d[0]) - 9 + 1].min() < (1e-4 if T <= 0 else 2e-5)
     pair.engine.close()
     one.engine.close()
+
+
+# Tensor-core attention (attn_tc.cuh: bf16 caches, head_dim 64, groups of 16
+# or more queries): prefill chunks and token-tree verify blocks, against the
+# CUDA-core attention kernel and the oracle.
+def test_attention_tc_prefill_matches_cuda_core(gpu_lib, oracle_built, monkeypatch):
+    shape = ModelShape(vocab=1000, d_model=256, n_heads=4, d_ff=512, n_layers=2, max_seq_len=400)
+    toks = make_prompts(1, 300, shape.vocab, seed=61)[0]  # 3 query tiles, 3 cache tiles
+    tc = make_pair(shape, 1, seed=60, int8=True, act_bf16=True, kv_mode=1, max_prompt_len=320)
+    monkeypatch.setenv("SPECDEC_ATTN_TC", "0")
+    cc = make_pair(shape, 1, seed=60, int8=True, act_bf16=True, kv_mode=1, max_prompt_len=320)
+    a = tc.engine.forward_logits(sd.TARGET, toks)
+    b = cc.engine.forward_logits(sd.TARGET, toks)
+    o = tc.target.forward(toks, act_bf16=True, kv_mode=1)
+    assert rel_err(a, b) < BF16_REL and rel_err(a, o) < BF16_REL, (rel_err(a, b), rel_err(a, o))
+    tc.engine.close()
+    cc.engine.close()
+
+
+@pytest.mark.parametrize("br", [(4, 3, 2, 1), (2, 2, 2, 2)])
+def test_tree_greedy_bf16_tensor_core_attention(gpu_lib, oracle_built, br):
+    shape, dl = SHAPES["cfg1"]
+    pair = make_pair(shape, dl, seed=62, int8=True, act_bf16=True, kv_mode=1, max_batch=4, max_prompt_len=40,
+                     max_tree_nodes=64)
+    tg, sg, to, so, mg = _tree_both(pair, 3, 20, 30, list(br), 0.0)
+    exact, ties = compare_tokens(tg, to, mg, 20, greedy=True, tol=BF16_GREEDY_GAP)
+    assert exact + ties == 3
