@@ -19,8 +19,10 @@
 //                  stores it (positions x dims: MN-major, 1024-byte groups of
 //                  8 positions); TMEM columns [128, 192)
 //   o = o * alpha + O_t in registers (the running rescale of the online softmax).
-// K and V tiles stream through a two-stage TMA ring: tile t + 1 loads while
-// tile t is multiplied.  P is rounded to bf16 for the second product (an
+// K tiles stream through a two-stage TMA ring (tile t + 1 loads while tile t
+// is multiplied); V has one buffer, refilled as soon as O_t is done, which
+// leaves S_{t+1} and the softmax to cover its load and keeps the CTA at 97 KB
+// of shared memory (two CTAs per SM).  P is rounded to bf16 for the second product (an
 // error of at most 2^-9 relative per probability; bf16 activations already
 // round every layer output to 8 bits).  Every mbarrier wait is bounded; on
 // a timeout the CTA flags kErrTimeout and writes nothing.
@@ -37,7 +39,8 @@ constexpr int kAtcMinQ = 16;             // groups with fewer queries keep atten
 constexpr int kAtcQBytes = 128 * 128;    // Q tile: 128 rows x 64 bf16
 constexpr int kAtcKVBytes = 128 * 128;   // K or V tile: 128 positions x 64 bf16
 constexpr int kAtcPBytes = 2 * 128 * 128;  // P: 128 queries x 128 positions bf16, two 64-position blocks
-constexpr int kAtcSmem = kAtcQBytes + 2 * 2 * kAtcKVBytes + kAtcPBytes + 1024;
+// Q, two K stages, one V buffer, P: 96 KB (+ alignment), two CTAs per SM
+constexpr int kAtcSmem = kAtcQBytes + 3 * kAtcKVBytes + kAtcPBytes + 1024;
 constexpr int kAtcTmemCols = 256;        // S: 128 columns, O_t: 64 columns
 
 // kind::f16, D fp32, A and B bf16; S: both K-major, N = 128; O: B MN-major, N = 64.
@@ -52,6 +55,20 @@ constexpr uint32_t kAtcIdescO = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) 
 // MN) is not used.
 __device__ __forceinline__ uint64_t umma_desc_mn128(uint32_t saddr) {
   return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Visibility of positions base .. base + 63 for a query at cache row qpos
+// whose tree (if any) starts at qtb with ancestor mask qmask: bit j is set iff
+// base + j <= qpos and (base + j < qtb, or bit base + j - qtb of qmask).
+__device__ __forceinline__ uint64_t low_bits(long long n) {
+  return n <= 0 ? 0ull : n >= 64 ? ~0ull : ((1ull << n) - 1ull);
+}
+__device__ __forceinline__ uint64_t vis_word(int base, int qpos, int qtb, unsigned long long qmask) {
+  const uint64_t causal = low_bits(static_cast<long long>(qpos) + 1 - base);
+  const uint64_t prefix = low_bits(static_cast<long long>(qtb) - base);
+  const long long d = static_cast<long long>(base) - qtb;  // bit j <-> bit d + j of qmask
+  const uint64_t tree = (d >= 64 || d <= -64) ? 0ull : d >= 0 ? (qmask >> d) : (qmask << (-d));
+  return causal & (prefix | tree);
 }
 
 struct alignas(64) AttnTcArgs {
@@ -70,10 +87,11 @@ __global__ void __launch_bounds__(kAtcThreads, 1) attn_tc_kernel(const __grid_co
   extern __shared__ unsigned char atc_smem_raw[];
   unsigned char *sm =
       reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(atc_smem_raw) + 1023) & ~uintptr_t(1023));
-  unsigned char *sq = sm;                                   // Q tile
-  unsigned char *skv = sq + kAtcQBytes;                     // stage s: K at skv + s * 2 * kAtcKVBytes, V after it
-  unsigned char *sp = skv + 2 * 2 * kAtcKVBytes;            // P, two blocks of 64 positions
-  __shared__ __align__(8) uint64_t bar_q, bar_kv[2], bar_s, bar_o;
+  unsigned char *sq = sm;                       // Q tile
+  unsigned char *sk = sq + kAtcQBytes;          // K stage s at sk + s * kAtcKVBytes
+  unsigned char *sv = sk + 2 * kAtcKVBytes;     // V (one buffer: V_{t+1} loads once O_t is done)
+  unsigned char *sp = sv + kAtcKVBytes;         // P, two blocks of 64 positions
+  __shared__ __align__(8) uint64_t bar_q, bar_kv[2], bar_v, bar_s, bar_o;
   __shared__ uint32_t s_tmem;
   __shared__ int s_req, s_maxpos, s_fail;
 
@@ -108,6 +126,7 @@ __global__ void __launch_bounds__(kAtcThreads, 1) attn_tc_kernel(const __grid_co
     mbar_init(&bar_q, 1);
     mbar_init(&bar_kv[0], 1);
     mbar_init(&bar_kv[1], 1);
+    mbar_init(&bar_v, 1);
     mbar_init(&bar_s, 1);
     mbar_init(&bar_o, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -126,17 +145,20 @@ __global__ void __launch_bounds__(kAtcThreads, 1) attn_tc_kernel(const __grid_co
   const int ntiles = work ? maxpos / kAtcTile + 1 : 0;
   const int row0 = (req * a.Hkv + hk) * a.S_cap;
 
-  auto issue_kv = [&](int t) {  // thread 0
+  auto issue_k = [&](int t) {  // thread 0
     const int s = t & 1;
-    unsigned char *kd = skv + s * 2 * kAtcKVBytes;
-    mbar_expect_tx(&bar_kv[s], 2 * kAtcKVBytes);
-    tma_load_2d(kd, &a.tmk, 0, row0 + t * kAtcTile, &bar_kv[s]);
-    tma_load_2d(kd + kAtcKVBytes, &a.tmv, 0, row0 + t * kAtcTile, &bar_kv[s]);
+    mbar_expect_tx(&bar_kv[s], kAtcKVBytes);
+    tma_load_2d(sk + s * kAtcKVBytes, &a.tmk, 0, row0 + t * kAtcTile, &bar_kv[s]);
+  };
+  auto issue_v = [&](int t) {  // thread 0
+    mbar_expect_tx(&bar_v, kAtcKVBytes);
+    tma_load_2d(sv, &a.tmv, 0, row0 + t * kAtcTile, &bar_v);
   };
   if (threadIdx.x == 0 && ntiles > 0) {
     mbar_expect_tx(&bar_q, kAtcQBytes);
     tma_load_2d(sq, &a.tmq, h * kAtcD, rq0, &bar_q);
-    issue_kv(0);
+    issue_k(0);
+    issue_v(0);
   }
 
   float m = -INFINITY, l = 0.f;
@@ -150,12 +172,12 @@ __global__ void __launch_bounds__(kAtcThreads, 1) attn_tc_kernel(const __grid_co
   for (; t < ntiles; ++t) {
     const int s = t & 1;
     // S = Q K^T (thread 32 issues; the whole CTA waits for the product)
-    if (threadIdx.x == 0 && t + 1 < ntiles) issue_kv(t + 1);  // its stage was released after O_{t-1}
+    if (threadIdx.x == 0 && t + 1 < ntiles) issue_k(t + 1);  // its stage was released after S_{t-1}
     if (threadIdx.x == 32) {
       if (ok) ok = mbar_wait(&bar_kv[s], (t >> 1) & 1);
       if (ok) {
         tc_fence_after();
-        const uint32_t qa = smem_u32(sq), ka = smem_u32(skv + s * 2 * kAtcKVBytes);
+        const uint32_t qa = smem_u32(sq), ka = smem_u32(sk + s * kAtcKVBytes);
 #pragma unroll
         for (int k = 0; k < kAtcD / 16; ++k)
           tc_mma(tmem, umma_desc_k128(qa + 32 * k), umma_desc_k128(ka + 32 * k), kAtcIdescS, k ? 1u : 0u);
@@ -170,27 +192,27 @@ __global__ void __launch_bounds__(kAtcThreads, 1) attn_tc_kernel(const __grid_co
     }
     tc_fence_after();
 
-    // softmax of this row's 128 scores, read from TMEM twice (max, then P)
+    // softmax of this row's 128 scores, read from TMEM twice (max, then P);
+    // the row's visible positions of the tile as two 64-bit words
     const int t0 = t * kAtcTile;
+    const uint64_t vis0 = vis_word(t0, qpos, qtb, qmask), vis1 = vis_word(t0 + 64, qpos, qtb, qmask);
     float tmax = -INFINITY;
-#pragma unroll
+#pragma unroll 1
     for (int hf = 0; hf < 2; ++hf) {
+      const uint64_t vw = hf ? vis1 : vis0;
       float sc[64];
       tmem_ld64(trow + 64 * hf, sc);
 #pragma unroll
-      for (int j = 0; j < 64; ++j) {
-        const int pos = t0 + 64 * hf + j;
-        const bool vis = pos <= qpos && (pos < qtb || (pos - qtb < 64 && ((qmask >> (pos - qtb)) & 1ull)));
-        if (vis) tmax = fmaxf(tmax, sc[j] * 0.125f);  // / sqrt(64): a power of two, so exact
-      }
+      for (int j = 0; j < 64; ++j) tmax = fmaxf(tmax, ((vw >> j) & 1ull) ? sc[j] * 0.125f : -INFINITY);
     }
-    const float mnew = fmaxf(m, tmax);
+    const float mnew = fmaxf(m, tmax);  // / sqrt(64) above: a power of two, so exact
     const float alpha = (m == -INFINITY) ? 0.f : expf(m - mnew);
     float psum = 0.f;
     // P (bf16) into the swizzled K-major tile: row r, 16-byte unit uu of
     // block hf (positions 64 hf ..) lands at unit uu ^ (r & 7) of the row
-#pragma unroll
+#pragma unroll 1
     for (int hf = 0; hf < 2; ++hf) {
+      const uint64_t vw = hf ? vis1 : vis0;
       float sc[64];
       tmem_ld64(trow + 64 * hf, sc);
 #pragma unroll
@@ -198,9 +220,7 @@ __global__ void __launch_bounds__(kAtcThreads, 1) attn_tc_kernel(const __grid_co
         float p[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const int pos = t0 + 64 * hf + 8 * uu + e;
-          const bool vis = pos <= qpos && (pos < qtb || (pos - qtb < 64 && ((qmask >> (pos - qtb)) & 1ull)));
-          p[e] = vis ? expf(sc[8 * uu + e] * 0.125f - mnew) : 0.f;
+          p[e] = ((vw >> (8 * uu + e)) & 1ull) ? expf(sc[8 * uu + e] * 0.125f - mnew) : 0.f;
           psum += p[e];
         }
         *reinterpret_cast<uint4 *>(sp + hf * (128 * 128) + r * 128 + ((uu ^ (r & 7)) << 4)) = f32x8_to_bf16(p);
@@ -214,27 +234,30 @@ __global__ void __launch_bounds__(kAtcThreads, 1) attn_tc_kernel(const __grid_co
     __syncthreads();
     // O_t = P V
     if (threadIdx.x == 32) {
+      ok = mbar_wait(&bar_v, t & 1);
       tc_fence_after();
-      const uint32_t pa = smem_u32(sp), va = smem_u32(skv + s * 2 * kAtcKVBytes + kAtcKVBytes);
+      const uint32_t pa = smem_u32(sp), va = smem_u32(sv);
+      if (ok)
 #pragma unroll
-      for (int k = 0; k < kAtcTile / 16; ++k)
-        tc_mma(tmem + 128, umma_desc_k128(pa + (k >> 2) * (128 * 128) + 32 * (k & 3)), umma_desc_mn128(va + 2048 * k),
-               kAtcIdescO, k ? 1u : 0u);
+        for (int k = 0; k < kAtcTile / 16; ++k)
+          tc_mma(tmem + 128, umma_desc_k128(pa + (k >> 2) * (128 * 128) + 32 * (k & 3)),
+                 umma_desc_mn128(va + 2048 * k), kAtcIdescO, k ? 1u : 0u);
       tc_commit(&bar_o);
     }
     __syncwarp();
-    ok = __syncthreads_and(mbar_wait(&bar_o, t & 1) ? 1 : 0) != 0;
+    ok = __syncthreads_and((threadIdx.x == 32 ? ok : true) && mbar_wait(&bar_o, t & 1)) != 0;
     if (!ok) {
       failed_at = 2;
       break;
     }
     tc_fence_after();
+    if (threadIdx.x == 0 && t + 1 < ntiles) issue_v(t + 1);  // V is free once O_t is done
     float ot[kAtcD];
     tmem_ld64(trow + 128, ot);
 #pragma unroll
     for (int e = 0; e < kAtcD; ++e) o[e] = o[e] * alpha + ot[e];
     tc_fence_before();
-    __syncthreads();  // S, O_t and P are free for the next tile; so is this K/V stage
+    __syncthreads();  // S, O_t and P are free for the next tile
   }
 
   if (!ok) {
@@ -243,8 +266,9 @@ __global__ void __launch_bounds__(kAtcThreads, 1) attn_tc_kernel(const __grid_co
     if (threadIdx.x == 0) {
       s_fail = 1;
       mbar_wait(&bar_q, 0);
-      mbar_wait(&bar_kv[t & 1], (t >> 1) & 1);  // tile t's K / V
-      if (t + 1 < ntiles) mbar_wait(&bar_kv[(t + 1) & 1], ((t + 1) >> 1) & 1);  // the prefetch
+      mbar_wait(&bar_kv[t & 1], (t >> 1) & 1);  // tile t's K
+      if (t + 1 < ntiles) mbar_wait(&bar_kv[(t + 1) & 1], ((t + 1) >> 1) & 1);  // the prefetched K
+      mbar_wait(&bar_v, t & 1);  // tile t's V
       mbar_wait(failed_at == 1 ? &bar_s : &bar_o, t & 1);  // the product being waited for
       if (a.err) atomicOr(a.err, kErrTimeout);
     }
