@@ -32,7 +32,7 @@
 
 namespace specdec {
 
-constexpr int kAtcThreads = 128;
+constexpr int kAtcThreads = 256;  // two threads per query row (warps w and w + 4 share TMEM lanes)
 constexpr int kAtcTile = 128;            // positions per tile
 constexpr int kAtcD = 64;                // head dimension of this path
 constexpr int kAtcMinQ = 16;             // groups with fewer queries keep attention_kernel
@@ -82,7 +82,7 @@ struct alignas(64) AttnTcArgs {
   int *err;
 };
 
-__global__ void __launch_bounds__(kAtcThreads, 1) attn_tc_kernel(const __grid_constant__ AttnTcArgs a) {
+__global__ void __launch_bounds__(kAtcThreads, 2) attn_tc_kernel(const __grid_constant__ AttnTcArgs a) {
   pdl_wait();
   extern __shared__ unsigned char atc_smem_raw[];
   unsigned char *sm =
@@ -94,6 +94,7 @@ __global__ void __launch_bounds__(kAtcThreads, 1) attn_tc_kernel(const __grid_co
   __shared__ __align__(8) uint64_t bar_q, bar_kv[2], bar_v, bar_s, bar_o;
   __shared__ uint32_t s_tmem;
   __shared__ int s_req, s_maxpos, s_fail;
+  __shared__ float s_rmax[2][128], s_rsum[2][128];  // per column half: the rows' tile max / P sum
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ngt = (a.Q + 127) / 128;
@@ -103,8 +104,8 @@ __global__ void __launch_bounds__(kAtcThreads, 1) attn_tc_kernel(const __grid_co
   const int nq = max(0, min(128, min(a.Q - qt * 128, a.R - rq0)));
   const int hk = h / (a.H / a.Hkv);
 
-  // this thread's query row
-  const int r = threadIdx.x;
+  // this thread's query row (its warp's TMEM lane quadrant) and column half
+  const int r = 32 * (warp & 3) + lane, half = warp >> 2;
   const bool qv = r < nq;
   const int qreq = qv ? a.rows.req[rq0 + r] : -1;
   const int qpos = (qv && qreq >= 0) ? row_slot(a.rows, rq0 + r) : -1;
@@ -162,10 +163,10 @@ __global__ void __launch_bounds__(kAtcThreads, 1) attn_tc_kernel(const __grid_co
   }
 
   float m = -INFINITY, l = 0.f;
-  float o[kAtcD];
+  float o[kAtcD / 2];  // this thread's half of the row's output dims
 #pragma unroll
-  for (int e = 0; e < kAtcD; ++e) o[e] = 0.f;
-  const uint32_t trow = tmem + (static_cast<uint32_t>(warp * 32) << 16);  // this warp's lanes
+  for (int e = 0; e < kAtcD / 2; ++e) o[e] = 0.f;
+  const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);  // this warp's lanes
   bool ok = true;
   if (ntiles > 0 && threadIdx.x == 32) ok = mbar_wait(&bar_q, 0);
   int t = 0, failed_at = 0;  // 1: waiting for S, 2: waiting for O_t
@@ -192,29 +193,29 @@ __global__ void __launch_bounds__(kAtcThreads, 1) attn_tc_kernel(const __grid_co
     }
     tc_fence_after();
 
-    // softmax of this row's 128 scores, read from TMEM twice (max, then P);
-    // the row's visible positions of the tile as two 64-bit words
+    // softmax of this row's 128 scores: this thread takes the 64 positions of
+    // its half (read from TMEM twice: max, then P); the row's visible
+    // positions of that half as a 64-bit word
     const int t0 = t * kAtcTile;
-    const uint64_t vis0 = vis_word(t0, qpos, qtb, qmask), vis1 = vis_word(t0 + 64, qpos, qtb, qmask);
+    const uint64_t vw = vis_word(t0 + 64 * half, qpos, qtb, qmask);
     float tmax = -INFINITY;
-#pragma unroll 1
-    for (int hf = 0; hf < 2; ++hf) {
-      const uint64_t vw = hf ? vis1 : vis0;
+    {
       float sc[64];
-      tmem_ld64(trow + 64 * hf, sc);
+      tmem_ld64(trow + 64 * half, sc);
 #pragma unroll
       for (int j = 0; j < 64; ++j) tmax = fmaxf(tmax, ((vw >> j) & 1ull) ? sc[j] * 0.125f : -INFINITY);
     }
+    s_rmax[half][r] = tmax;
+    __syncthreads();
+    tmax = fmaxf(s_rmax[0][r], s_rmax[1][r]);
     const float mnew = fmaxf(m, tmax);  // / sqrt(64) above: a power of two, so exact
     const float alpha = (m == -INFINITY) ? 0.f : expf(m - mnew);
     float psum = 0.f;
     // P (bf16) into the swizzled K-major tile: row r, 16-byte unit uu of
-    // block hf (positions 64 hf ..) lands at unit uu ^ (r & 7) of the row
-#pragma unroll 1
-    for (int hf = 0; hf < 2; ++hf) {
-      const uint64_t vw = hf ? vis1 : vis0;
+    // block `half` (positions 64 half ..) lands at unit uu ^ (r & 7) of the row
+    {
       float sc[64];
-      tmem_ld64(trow + 64 * hf, sc);
+      tmem_ld64(trow + 64 * half, sc);
 #pragma unroll
       for (int uu = 0; uu < 8; ++uu) {
         float p[8];
@@ -223,15 +224,16 @@ __global__ void __launch_bounds__(kAtcThreads, 1) attn_tc_kernel(const __grid_co
           p[e] = ((vw >> (8 * uu + e)) & 1ull) ? expf(sc[8 * uu + e] * 0.125f - mnew) : 0.f;
           psum += p[e];
         }
-        *reinterpret_cast<uint4 *>(sp + hf * (128 * 128) + r * 128 + ((uu ^ (r & 7)) << 4)) = f32x8_to_bf16(p);
+        *reinterpret_cast<uint4 *>(sp + half * (128 * 128) + r * 128 + ((uu ^ (r & 7)) << 4)) = f32x8_to_bf16(p);
       }
     }
+    s_rsum[half][r] = psum;
     m = mnew;
-    l = l * alpha + psum;
     // the P stores must reach the tensor core's (async) view of shared memory
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tc_fence_before();
     __syncthreads();
+    l = l * alpha + (s_rsum[0][r] + s_rsum[1][r]);  // both threads of the row add the halves in the same order
     // O_t = P V
     if (threadIdx.x == 32) {
       ok = mbar_wait(&bar_v, t & 1);
@@ -252,10 +254,17 @@ __global__ void __launch_bounds__(kAtcThreads, 1) attn_tc_kernel(const __grid_co
     }
     tc_fence_after();
     if (threadIdx.x == 0 && t + 1 < ntiles) issue_v(t + 1);  // V is free once O_t is done
-    float ot[kAtcD];
-    tmem_ld64(trow + 128, ot);
+    {
+      uint32_t u0[16], u1[16];
+      tmem_ld16_nowait(trow + 128 + 32 * half, u0);
+      tmem_ld16_nowait(trow + 128 + 32 * half + 16, u1);
+      tmem_wait_ld();
 #pragma unroll
-    for (int e = 0; e < kAtcD; ++e) o[e] = o[e] * alpha + ot[e];
+      for (int e = 0; e < 16; ++e) {
+        o[e] = o[e] * alpha + __uint_as_float(u0[e]);
+        o[16 + e] = o[16 + e] * alpha + __uint_as_float(u1[e]);
+      }
+    }
     tc_fence_before();
     __syncthreads();  // S, O_t and P are free for the next tile
   }
@@ -273,9 +282,9 @@ __global__ void __launch_bounds__(kAtcThreads, 1) attn_tc_kernel(const __grid_co
       if (a.err) atomicOr(a.err, kErrTimeout);
     }
   } else if (qv && qreq >= 0 && ntiles > 0) {
-    uint4 *dst = reinterpret_cast<uint4 *>(a.out + static_cast<size_t>(rq0 + r) * a.ldo + h * kAtcD);
+    uint4 *dst = reinterpret_cast<uint4 *>(a.out + static_cast<size_t>(rq0 + r) * a.ldo + h * kAtcD + 32 * half);
 #pragma unroll
-    for (int u = 0; u < kAtcD / 8; ++u) {
+    for (int u = 0; u < kAtcD / 16; ++u) {
       float v[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) v[e] = __fdiv_rn(o[8 * u + e], l);
