@@ -225,7 +225,8 @@ struct specdec_handle {
   float *gemm_ws = nullptr;  // split-K partial tiles [tile * ks + rank][column][row]
   int samp_max_cluster = 1;  // largest cluster of draft_sample_cluster_kernel
   int attn_ctas_per_sm = 2;  // attention splits the cache while the grid stays within this many CTAs per SM
-  bool attn_tc = true;       // tensor-core attention for bf16 caches, head_dim 64, groups of >= kAtcMinQ queries
+  bool attn_tc = true;       // tensor-core attention for bf16 caches, head_dim 64, groups of >= attn_tc_min_q queries
+  int attn_tc_min_q = kAtcMinQ;
   // row batches that take the tensor-core GEMM instead of the GEMV: at least
   // gemm_min_rows rows, or gemm_wide_rows rows of a layer with at least
   // gemm_wide_elems weights
@@ -916,7 +917,7 @@ void attention(specdec_handle *h, const Dims &dm, RowsView rows, int R, int Q, c
   const size_t nrows = layer_elems / dm.D;
   const bool bf = act_bf16(h);
   const bool kvbf = h->cfg.kv_dtype == SPECDEC_BF16;
-  if (h->attn_tc && bf && kvbf && dm.D == kAtcD && Q >= kAtcMinQ && dm.dq % 8 == 0) {
+  if (h->attn_tc && bf && kvbf && dm.D == kAtcD && Q >= h->attn_tc_min_q && dm.dq % 8 == 0) {
     // groups of many queries (token trees, prefill chunks): tensor cores
     AttnTcArgs t{};
     t.tmq = gemm_operand_map(h->Q, dm.dq, R, dm.dq, 128);
@@ -1535,6 +1536,7 @@ int create_impl(const specdec_config *cfg, int device, int rank, int world, cons
       h->gemm_max_split = std::max(1, std::min(h->gemm_max_split, std::atoi(e)));
     if (const char *e = std::getenv("SPECDEC_ATTN_CTAS_PER_SM")) h->attn_ctas_per_sm = std::max(1, std::atoi(e));
     if (const char *e = std::getenv("SPECDEC_ATTN_TC")) h->attn_tc = std::atoi(e) != 0;  // 0: CUDA-core attention only
+    if (const char *e = std::getenv("SPECDEC_ATTN_TC_MIN_Q")) h->attn_tc_min_q = std::max(1, std::atoi(e));
     CK(cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAtcSmem));
     // GEMV / GEMM routing thresholds, for tuning measurements
     if (const char *e = std::getenv("SPECDEC_GEMM_MIN_ROWS")) h->gemm_min_rows = std::max(1, std::atoi(e));
