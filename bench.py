@@ -24,6 +24,7 @@ scaling, no data-path collective); timing is the max over ranks.
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
 import os
 import statistics
@@ -69,6 +70,36 @@ def tree_nodes(branching) -> int:
 
 
 KV_DTYPE = {0: 0, 1: 1, 2: 2}  # workload kv_mode -> SPECDEC_F32 / BF16 / INT8
+
+# The large workload at one GPU's share of its 256
+# requests when they are split over 8 GPUs.
+LARGE_REQUESTS_PER_GPU = 32
+
+
+def device_params(shape, seed: int, dev):
+    """Seeded synthetic weights of make_params' distributions (N(0, 0.02)
+    weights and embedding, N(0, 4/sqrt(d)) lm_head, zero biases, unit LayerNorm)
+    drawn on the GPU and returned as host fp32 arrays.  The large model has
+    6.9 G parameters, which numpy draws in minutes; the stream differs from
+    make_params', which only the parity tests need."""
+    import torch
+
+    from specdec_b200.synth import param_kinds, param_shapes
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    out = []
+    for shp, kind in zip(param_shapes(shape), param_kinds(shape)):
+        n = int(np.prod(shp))
+        if kind in ("emb", "pos", "w", "head_w"):
+            std = 4.0 / np.sqrt(shape.d_model) if kind == "head_w" else 0.02
+            a = torch.empty(n, dtype=torch.float32, device=dev).normal_(0.0, std, generator=g).cpu().numpy()
+        elif kind == "g":
+            a = np.ones(n, np.float32)
+        else:
+            a = np.zeros(n, np.float32)
+        out.append(a.reshape(shp))
+    return out
 
 
 # DRAM bytes (read + write) of one launch of the roofline kernel, from the ncu
@@ -191,6 +222,14 @@ def reference_arm(args, wl, rank, world):
             import torch.distributed as dist
             dist.destroy_process_group()
         return
+    if wl.name == "large":
+        print(json.dumps({"impl": "reference", "unavailable": "the reference dequantises the large model's 6.6 G "
+                          "int8 weights to fp32 (26 GB) on every Dense call; its CPU arm runs on the int8 workload"}),
+              flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle  # the reference arm times the reference (oracle/_ref) or the CPU restatement
 
@@ -244,7 +283,7 @@ def reference_arm(args, wl, rank, world):
 
 
 def config_dict(wl, args):
-    idx = {"int8": 1, "medium": 2, "tree": 3}.get(wl.name, 1)
+    idx = {"int8": 1, "medium": 2, "tree": 3, "large": 4}.get(wl.name, 1)
     return {"workload": f"{wl.name} (BASELINE configs[{idx}])", "arch": args.arch,
             "model": f"L{wl.target.n_layers} d{wl.target.d_model} H{wl.target.n_heads} F{wl.target.d_ff} V{wl.target.vocab}",
             "draft": f"first {wl.draft_layers} layer(s) + shared head", "batch_per_gpu": wl.batch,
@@ -252,7 +291,9 @@ def config_dict(wl, args):
             "lookahead": wl.lookahead, "temperature": wl.temperature, "weights": "int8" if wl.weights_int8 else "f32",
             "act": "bf16" if wl.act_bf16 else "f32", "kv": ["f32", "bf16", "int8"][wl.kv_mode],
             "rng": "philox host uniforms", "tree": list(wl.tree) if wl.tree else None,
-            "parallelism": f"request-parallel x{args.gpus}", "l2": "flushed between timed steps (256 MiB write)"}
+            "parallelism": f"request-parallel x{args.gpus}", "l2": "flushed between timed steps (256 MiB write)",
+            **({"requests": f"{wl.batch} per GPU: configs[4]'s 256 requests split over 8 GPUs"}
+               if wl.name == "large" else {})}
 
 
 def cpu_baseline_sample(wl):
@@ -297,13 +338,16 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--arch", default="ref", choices=["ref", "cfg"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="int8", choices=["int8", "medium", "tree"],
+    ap.add_argument("--workload", default="int8", choices=["int8", "medium", "tree", "large"],
                     help="int8 = BASELINE configs[1] (the metric's config, default); medium = configs[2]; "
-                         "tree = configs[3]")
+                         "tree = configs[3]; large = configs[4] at 32 requests per GPU (its 256 over 8 GPUs)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     rank, world, local = dist_env()
     wl = workload(args.workload, ARCH_CFG if args.arch == "cfg" else ARCH_REF)
+    large = wl.name == "large"
+    if large:
+        wl = dataclasses.replace(wl, batch=LARGE_REQUESTS_PER_GPU)
     if args.impl == "reference":
         return reference_arm(args, wl, rank, world)
 
@@ -318,12 +362,16 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", init_method="env://", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
-    P = make_params(wl.target, seed=0)
+    t_setup = time.perf_counter()
+    P = device_params(wl.target, 0, torch.device("cuda", local)) if large else make_params(wl.target, seed=0)
     eng = sd.Engine(wl.target, draft_layers=wl.draft_layers, weight_dtype=sd.INT8 if wl.weights_int8 else sd.F32,
                     act_dtype=sd.BF16 if wl.act_bf16 else sd.F32, kv_dtype=KV_DTYPE[wl.kv_mode],
                     max_batch=wl.batch, max_lookahead=wl.lookahead, max_prompt_len=wl.prompt_len, device=local,
                     max_tree_nodes=tree_nodes(wl.tree) if wl.tree else 0)
     eng.load_params(sd.TARGET, P)
+    del P
+    if rank == 0:
+        print(f"[bench] weights made and loaded in {time.perf_counter() - t_setup:.1f} s", file=sys.stderr, flush=True)
     B, S = wl.batch, wl.prompt_len
     # request partition: rank r serves requests [r*B, (r+1)*B) of the global set
     prompts = shard(make_prompts(B * world, S, wl.target.vocab, seed=1), B, rank, world)
@@ -347,9 +395,12 @@ def main():
             eng.generate_device(d_prompts.data_ptr(), B, S, d_out.data_ptr(), d_stats.data_ptr(), wl.max_new,
                                 wl.lookahead, wl.temperature, seed=1234, uniforms=uni)
 
-    for _ in range(args.warmup):
+    for i in range(args.warmup):
+        t0 = time.perf_counter()
         step()
-    torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        if rank == 0:
+            print(f"[bench] warm-up step {i}: {time.perf_counter() - t0:.2f} s", file=sys.stderr, flush=True)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     if world > 1:
@@ -381,7 +432,8 @@ def main():
     pin_prompts = torch.from_numpy(prompts.astype(np.int32)).pin_memory()
     pin_uni = torch.from_numpy(uni).pin_memory()
     e2e_ms = []
-    for i in range(max(3, args.steps // 2)):
+    # (the large workload's steps take seconds each: one e2e step there)
+    for i in range(1 if large else max(3, args.steps // 2)):
         with torch.cuda.stream(stream):
             flush.fill_(float(i))
         torch.cuda.synchronize()
@@ -403,7 +455,7 @@ def main():
     # Autoregressive decoding of the same requests on the same kernels
     # (generate_advanced): the speculative path's speed-up over plain decoding.
     ar_ms = []
-    if not wl.tree:
+    if not wl.tree and not large:
         ar_uni = np.ascontiguousarray(uni[:, : wl.max_new, :1])
         for i in range(args.warmup + 3):
             with torch.cuda.stream(stream):
@@ -470,8 +522,13 @@ def main():
             line["ar_decode"] = {"value": new_tokens * world * len(ar_ms) / (ar_tot / 1e3), "unit": UNIT,
                                  "what": "generate_advanced (autoregressive, KV cache) of the same requests, "
                                          "models and uniforms on the same kernels, device-resident"}
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and not large:
             line["cpu_baseline"] = cpu_baseline_sample(wl)
+        if large:
+            line["cpu_baseline"] = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "reference",
+                                    "sample": "not sampled: the reference dequantises the 6.6 G int8 weights to "
+                                              "fp32 (26 GB) on every Dense call; the int8 workload's line "
+                                              "carries the CPU baseline"}
         if wl.tree:
             line["tree"] = {"branching": list(wl.tree), "nodes": tree_nodes(wl.tree),
                             "mean_accepted_per_round": line["spec"]["mean_accepted_per_round"]}

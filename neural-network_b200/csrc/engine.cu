@@ -290,23 +290,50 @@ void check_dims(const Dims &d, const char *who) {
 }
 
 // --- weights ---------------------------------------------------------------
+// Runs fn(i0, i1) over [0, n) in contiguous ranges, one per host thread (at
+// most 16; one range when n is small).  The loader's passes over a 6.6 G-weight
+// model take minutes on one core.
+template <class F>
+void parallel_ranges(size_t n, F fn) {
+  const size_t hw = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+  const size_t T = std::min(hw, std::max<size_t>(1, n / 64));
+  if (T <= 1) {
+    fn(static_cast<size_t>(0), n);
+    return;
+  }
+  std::vector<std::thread> th;
+  const size_t per = (n + T - 1) / T;
+  for (size_t t = 0; t < T; ++t) {
+    const size_t a = t * per, b = std::min(n, a + per);
+    if (a < b) th.emplace_back(fn, a, b);
+  }
+  for (auto &x : th) x.join();
+}
+
 // QuantizedDense (src/nn/quantization.cpp:40-66): per-output-column scale
-// max|W[:, c]| / 127 (0 -> 1), q = clamp(round(W / s), -127, 127).
+// max|W[:, c]| / 127 (0 -> 1), q = clamp(round(W / s), -127, 127).  Each
+// thread owns a range of columns and walks the rows in order, so the column
+// maxima see the same values in the same order as a column-by-column loop.
 void quantize_columns(const float *w, int K, int N, std::vector<int8_t> &q, std::vector<float> &s) {
   s.assign(N, 1.f);
   q.assign(static_cast<size_t>(K) * N, 0);
-  for (int c = 0; c < N; ++c) {
-    float mx = 0.f;
-    for (int r = 0; r < K; ++r) mx = std::max(mx, std::abs(w[static_cast<size_t>(r) * N + c]));
-    const float sc = mx / 127.0f;
-    s[c] = (sc == 0.0f) ? 1.0f : sc;
-  }
-  for (int r = 0; r < K; ++r)
-    for (int c = 0; c < N; ++c) {
-      float v = std::round(w[static_cast<size_t>(r) * N + c] / s[c]);
-      v = std::max(-127.0f, std::min(127.0f, v));
-      q[static_cast<size_t>(r) * N + c] = static_cast<int8_t>(v);
+  parallel_ranges(static_cast<size_t>(N), [&](size_t c0, size_t c1) {
+    std::vector<float> mx(c1 - c0, 0.f);
+    for (int r = 0; r < K; ++r) {
+      const float *row = w + static_cast<size_t>(r) * N;
+      for (size_t c = c0; c < c1; ++c) mx[c - c0] = std::max(mx[c - c0], std::abs(row[c]));
     }
+    for (size_t c = c0; c < c1; ++c) {
+      const float sc = mx[c - c0] / 127.0f;
+      s[c] = (sc == 0.0f) ? 1.0f : sc;
+    }
+    for (int r = 0; r < K; ++r)
+      for (size_t c = c0; c < c1; ++c) {
+        float v = std::round(w[static_cast<size_t>(r) * N + c] / s[c]);
+        v = std::max(-127.0f, std::min(127.0f, v));
+        q[static_cast<size_t>(r) * N + c] = static_cast<int8_t>(v);
+      }
+  });
 }
 
 // A set of reference Dense weights [K][N_i] (+ bias [N_i]) stacked into one
@@ -354,12 +381,26 @@ void upload_stacked(specdec_handle *h, int role, const std::vector<DenseSrc> &sr
       const int row = interleave ? (2 * c + static_cast<int>(m)) : (base + c);
       bias[row] = s.bias_on ? s.b[gc] : 0.f;
       if (i8) scale[row] = sc[gc];
-      for (int k = 0; k < K; ++k) {
-        const size_t si = static_cast<size_t>(row0 + k) * ld + gc;
-        if (i8) wq[static_cast<size_t>(row) * K + k] = q[si];
-        else wf[static_cast<size_t>(row) * K + k] = s.w[si];
-      }
     }
+    // the transpose to output-major rows, in 32-column x 256-row blocks so the
+    // strided source rows stay in cache; threads own disjoint output rows
+    parallel_ranges(static_cast<size_t>(s.N), [&](size_t cb, size_t ce) {
+      for (size_t c0 = cb; c0 < ce; c0 += 32) {
+        const size_t c1 = std::min(ce, c0 + 32);
+        for (int k0 = 0; k0 < K; k0 += 256) {
+          const int k1 = std::min(K, k0 + 256);
+          for (size_t c = c0; c < c1; ++c) {
+            const size_t gc = static_cast<size_t>(s.col0) + c;
+            const size_t row = interleave ? (2 * c + m) : (static_cast<size_t>(base) + c);
+            for (int k = k0; k < k1; ++k) {
+              const size_t si = static_cast<size_t>(row0 + k) * ld + gc;
+              if (i8) wq[row * K + k] = q[si];
+              else wf[row * K + k] = s.w[si];
+            }
+          }
+        }
+      }
+    });
     base += s.N;
   }
   auto &own = h->weight_allocs[role];
