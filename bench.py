@@ -38,7 +38,8 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "neural-network_b200"))
 
-from specdec_b200.synth import ARCH_CFG, ARCH_REF, draft_params, make_params, make_prompts, workload  # noqa: E402
+from specdec_b200.synth import (ARCH_CFG, ARCH_REF, device_params, draft_params, make_params,  # noqa: E402
+                                 make_prompts, workload)
 
 METRIC = "accepted tokens/sec per GPU (spec-decode, k=4) at 1/2/4/8 B200; % HBM roofline"
 UNIT = "tokens/s"
@@ -74,32 +75,6 @@ KV_DTYPE = {0: 0, 1: 1, 2: 2}  # workload kv_mode -> SPECDEC_F32 / BF16 / INT8
 # The large workload at one GPU's share of its 256
 # requests when they are split over 8 GPUs.
 LARGE_REQUESTS_PER_GPU = 32
-
-
-def device_params(shape, seed: int, dev):
-    """Seeded synthetic weights of make_params' distributions (N(0, 0.02)
-    weights and embedding, N(0, 4/sqrt(d)) lm_head, zero biases, unit LayerNorm)
-    drawn on the GPU and returned as host fp32 arrays.  The large model has
-    6.9 G parameters, which numpy draws in minutes; the stream differs from
-    make_params', which only the parity tests need."""
-    import torch
-
-    from specdec_b200.synth import param_kinds, param_shapes
-
-    g = torch.Generator(device=dev)
-    g.manual_seed(seed)
-    out = []
-    for shp, kind in zip(param_shapes(shape), param_kinds(shape)):
-        n = int(np.prod(shp))
-        if kind in ("emb", "pos", "w", "head_w"):
-            std = 4.0 / np.sqrt(shape.d_model) if kind == "head_w" else 0.02
-            a = torch.empty(n, dtype=torch.float32, device=dev).normal_(0.0, std, generator=g).cpu().numpy()
-        elif kind == "g":
-            a = np.ones(n, np.float32)
-        else:
-            a = np.zeros(n, np.float32)
-        out.append(a.reshape(shp))
-    return out
 
 
 # DRAM bytes (read + write) of one launch of the roofline kernel, from the ncu

@@ -130,6 +130,31 @@ def make_params(m: ModelShape, seed: int = 0, std: float = 0.02,
     return out
 
 
+def device_params(m: ModelShape, seed: int, dev) -> List[np.ndarray]:
+    """Seeded synthetic weights with make_params' distributions (N(0, 0.02)
+    weights and embedding, N(0, 4/sqrt(d_model)) lm_head, zero biases, unit
+    LayerNorm), drawn by torch on `dev` (a CUDA device: seconds for the large
+    model's 6.9 G values, which numpy draws in minutes) and returned as host
+    fp32 arrays.  The stream differs from make_params'; the benchmarks and
+    profiling probes use it, the parity tests use make_params."""
+    import torch
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    out: List[np.ndarray] = []
+    for shape, kind in zip(param_shapes(m), param_kinds(m)):
+        n = int(np.prod(shape))
+        if kind in ("emb", "pos", "w", "head_w"):
+            std = 4.0 / np.sqrt(m.d_model) if kind == "head_w" else 0.02
+            a = torch.empty(n, dtype=torch.float32, device=dev).normal_(0.0, std, generator=g).cpu().numpy()
+        elif kind == "g":
+            a = np.ones(n, np.float32)
+        else:
+            a = np.zeros(n, np.float32)
+        out.append(a.reshape(shape))
+    return out
+
+
 def draft_params(target: ModelShape, params: List[np.ndarray], n_draft_layers: int) -> List[np.ndarray]:
     """The draft used by every config: the target's first n layers + shared lm_head."""
     per = params_per_layer(target)
