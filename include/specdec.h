@@ -10,7 +10,8 @@
  * backend (RoPE, KV append/truncate, attention, sampling are host loops), so
  * this library replaces the whole method rather than individual backend
  * virtuals.  The entry points below are what the reference-side glue binds;
- * see INTEGRATION.md for the C++ call site.
+ * the C++ call site is a
+ * CudaSpecBackend class beside the reference.
  *
  * Conventions: plain pointers and sizes only; every function returns a
  * specdec_status (0 = success).  On failure specdec_last_error(handle) holds
@@ -143,6 +144,50 @@ int specdec_generate_device(specdec_handle *h, const specdec_gen_params *p,
                             const int32_t *d_prompts, int B, int S,
                             int32_t *d_out_tokens, int64_t *d_out_stats);
 
+/* Round-level session: generate_speculative split at its round loop
+ * (src/nn/layer.cpp:1514-1656), so a caller (a serving loop, a benchmark)
+ * drives rounds itself.  specdec_prefill runs everything up to and including
+ * the first token (src/nn/layer.cpp:1396-1512: target and draft prefill, the
+ * first sample) for B requests with equal prompt length S (prompts [B][S],
+ * HOST) and opens a session on the handle; specdec_generate* and loading
+ * weights close it.  Chain speculation only (no trees, no autoregressive
+ * mode).  In host-uniform mode the session's table holds
+ * max(uniform_rounds, max_new_tokens + 2) rounds: p->uniforms fills its first
+ * uniform_rounds rows (row 0 draws the first token), the rest start at 0 and
+ * may be supplied by the steps. */
+int specdec_prefill(specdec_handle *h, const specdec_gen_params *p,
+                    const int32_t *prompts, int B, int S);
+
+/* specdec_prefill with a DEVICE prompt buffer, enqueued on specdec_stream(h)
+ * (nothing synchronised, no device-side status). */
+int specdec_prefill_device(specdec_handle *h, const specdec_gen_params *p,
+                           const int32_t *d_prompts, int B, int S);
+
+/* Up to `rounds` speculative rounds (k draft steps, one verify pass,
+ * acceptance and rollback each; src/nn/layer.cpp:1514-1656) of the open
+ * session; it stops early once every request has its max_new_tokens.
+ * `uniforms` (optional, HOST; host-uniform sessions only) are these rounds'
+ * draws [B][rounds][2k+1] and replace the table rows of the rounds about to
+ * run.  out_tokens [B][rounds * (k + 1)] and out_counts [B] are HOST
+ * buffers: request b emitted out_counts[b] tokens in this call, in
+ * out_tokens[b][0 .. out_counts[b]).  Synchronises and reports device-side
+ * errors like specdec_generate. */
+int specdec_step(specdec_handle *h, int rounds, const float *uniforms,
+                 int32_t *out_tokens, int32_t *out_counts);
+
+/* specdec_step on DEVICE output buffers (d_out_tokens [B][cap], at most cap
+ * tokens per request are stored; d_out_counts [B] counts them all), enqueued
+ * on specdec_stream(h) with nothing synchronised.  `uniforms` may be a host or
+ * device pointer. */
+int specdec_step_device(specdec_handle *h, int rounds, const float *uniforms,
+                        int32_t *d_out_tokens, int32_t *d_out_counts, int cap);
+
+/* The open session's sequences so far (HOST out_tokens [B][S +
+ * max(1, max_new_tokens)], prompt then new tokens, unfilled tail
+ * unspecified) and statistics (optional HOST out_stats [B][4], as
+ * specdec_generate). */
+int specdec_session_tokens(specdec_handle *h, int32_t *out_tokens, int64_t *out_stats);
+
 /* Replaces TransformerDecoder::generate_advanced with use_kv_cache = true
  * (src/nn/layer.cpp:1239-1380) for B independent requests: target only (the
  * draft need not be loaded), one token per request and step.  Greedy when
@@ -190,11 +235,21 @@ int specdec_philox_uniforms(uint64_t seed, int B, int rounds, int slots,
  * SPECDEC_ERR_INVALID.  No cudaMalloc, cudaFree or other allocating call is
  * made.  The array is shared by all calls on a device and keeps the last
  * call's contents: calls that overlap on the GPU race and must be serialised
- * by the caller.  The first call on each device looks the array's address up
- * (that device current); make it before any stream capture begins. */
+ * by the caller, and so must a call that overlaps other work of the same
+ * handle on another stream (both read the handle's weights; this call leaves
+ * the handle's own workspaces alone).  The first call on each device looks
+ * the array's address up (that device current); make it before any stream
+ * capture begins.  S is at most the model's max_seq_len
+ * (SPECDEC_ERR_SEQ_LEN, as the reference throws, src/nn/layer.cpp:1176-1179).
+ * Tensor-parallel handles are rejected (SPECDEC_ERR_UNSUPPORTED): NCCL may
+ * allocate and needs every rank.  Device-side failures (a bounded wait that
+ * gave up, a cache row out of range) cannot be returned by an asynchronous
+ * call: when d_status (a caller-owned DEVICE int32, may be NULL) is given,
+ * the call's last kernel writes the error bits there (0 = none; 1 = cache
+ * capacity, 4 = a wait gave up) for the caller to read after it synchronises. */
 int specdec_forward_logits_noalloc(specdec_handle *h, int role,
                                    const int32_t *d_tokens, int S,
-                                   float *d_logits, void *stream);
+                                   float *d_logits, void *stream, int32_t *d_status);
 
 /* Token tree of specdec_generate_tree: `depth` levels (1..8), every node at
  * depth t < depth has branch[t] children (the draft's most likely next

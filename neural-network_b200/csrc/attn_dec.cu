@@ -1,0 +1,468 @@
+// Decode / verify attention on the tensor cores for head_dim 128: the
+// arithmetic of attention_kernel (src/nn/layer.cpp:859-948: score = q . k /
+// sqrt(D), softmax over the visible positions, then P.V) for groups of at
+// most 16 query rows of one request -- draft steps (1 or 2 rows) and the
+// (k+1)-row verify block -- over a bf16 cache, with both products on tcgen05.
+//
+// The cache is what these passes stream (2 x 128 x 2 bytes per position and
+// head, about 1.2 MB per request and head on the large configuration), so the
+// kernel is built to keep HBM busy: with few queries per group the positions
+// go on the MMA's M side, one 128-position tile per product:
+//   S^T = K Q^T    M = 128 positions, N = 16 query columns, K = 128 dims:
+//                  A = the K tile as the cache stores it (K-major, 128-byte
+//                  swizzle, two 64-dim atoms), B = the group's query rows
+//                  (TMA, K-major); fp32 accumulators in TMEM, lane = position
+//   softmax        thread = position: its 16 scores from one tcgen05.ld,
+//                  masked (causal limit, tree ancestors) and divided by
+//                  sqrt(128); per query the tile maximum over the 128 threads
+//                  (warp shuffles + one named barrier), p = exp(s - m), P^T
+//                  written as bf16 into a K-major swizzled tile
+//   O^T = V^T P^T  M = 128 dims, N = 16, K = 128 positions: A = the V tile
+//                  as the cache stores it (positions x dims: MN-major, two
+//                  64-dim atoms 16 KB apart), B = P^T; TMEM lane = dim
+//   o = o * alpha + O_t in registers (thread = dim), one tile behind, so the
+//   fold overlaps the next tile's products.
+// Warp 0 streams K and V tiles through a six-slot TMA ring (32 KB per slot,
+// 192 KB in flight per SM), warp 1 issues the MMAs, warps 2-5 do the softmax
+// and the output.  CTAs are persistent (one per SM) and walk work items
+// (group, head, split) in a fixed order, so the ring never drains between
+// items.  A (group, head) whose cache is split writes unnormalised partials;
+// the last of its splits to finish (an arrival counter) merges them with the
+// log-sum-exp rule.  Every mbarrier wait is bounded; a timeout raises
+// kErrTimeout, the roles stop together and wait (bounded) for the copies and
+// products still in flight before the CTA frees its tensor memory.
+#include "attn_dec.cuh"
+#include "gemm.cuh"
+
+namespace specdec {
+
+namespace {
+
+constexpr int kAdSlots = 6;                      // ring slots of half a tile (K or V)
+constexpr int kAdHalf = kAdTile * kAdD * 2;      // 32 KB: 128 positions x 128 bf16
+constexpr int kAdBox = kAdTile * 64 * 2;         // 16 KB: one 64-dim atom of a half tile
+constexpr int kAdQBytes = kAdN * kAdD * 2;       // 4 KB: 16 query rows, two 2 KB atoms
+constexpr int kAdPBytes = kAdN * kAdTile * 2;    // 4 KB: 16 query rows x 128 positions, two atoms
+constexpr int kAdThreads = 192;
+constexpr int kAdSmem = kAdSlots * kAdHalf + 2 * kAdQBytes + 2 * kAdPBytes + 1024;
+constexpr int kAdTmemCols = 64;                  // S0 S1 O0 O1, 16 columns each
+
+// kind::f16, D fp32, A and B bf16, M = 128, N = 16.  S: A and B K-major.
+// O: A (V^T) MN-major, B (P^T) K-major.
+constexpr uint32_t kAdIdescS = (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kAdN >> 3) << 17) |
+                               (static_cast<uint32_t>(128 >> 4) << 24);
+constexpr uint32_t kAdIdescO = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) |
+                               (static_cast<uint32_t>(kAdN >> 3) << 17) | (static_cast<uint32_t>(128 >> 4) << 24);
+
+// MN-major operand, 128-byte swizzle, MN extent of two 64-element atoms
+// kAdBox bytes apart (leading byte offset); along K, rows 128 bytes apart and
+// groups of 8 rows 1024 bytes apart (stride byte offset).
+__device__ __forceinline__ uint64_t umma_desc_mn128_2atoms(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(kAdBox >> 4) << 16) |
+         (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Named barrier of the four softmax warps that also ANDs a predicate over
+// them, so a decision to stop is taken by all of them at the same point.
+__device__ __forceinline__ bool bar_and_softmax(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 1, 128, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v))
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void bar_softmax() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// One work item: (group g, head h, split) and the range of cache tiles it
+// covers.  The splits of a (group, head) share the tiles up to the group's
+// last visible position, so every split has work while the cache is shorter
+// than its capacity.
+struct AdItem {
+  int g, h, split, req, t0, nt, nq, rq0;
+};
+__device__ __forceinline__ AdItem ad_item(const AttnDecArgs &a, int item) {
+  AdItem it;
+  it.split = item % a.nsplit;
+  const int gh = item / a.nsplit;
+  it.h = gh % a.H;
+  it.g = gh / a.H;
+  it.rq0 = it.g * a.Q;
+  it.nq = max(0, min(a.Q, a.R - it.rq0));
+  it.req = -1;
+  int maxpos = -1;
+  for (int i = 0; i < it.nq; ++i) {
+    const int r = a.rows.req[it.rq0 + i];
+    if (r >= 0) {
+      it.req = r;
+      maxpos = max(maxpos, row_slot(a.rows, it.rq0 + i));
+    }
+  }
+  it.t0 = 0;
+  it.nt = 0;
+  if (it.req >= 0 && maxpos >= 0 && maxpos < a.S_cap) {
+    const int ntot = maxpos / kAdTile + 1;
+    const int tps = (ntot + a.nsplit - 1) / a.nsplit;
+    it.t0 = it.split * tps;
+    it.nt = max(0, min(ntot, it.t0 + tps) - it.t0);
+  }
+  return it;
+}
+
+__global__ void __launch_bounds__(kAdThreads, 1) attn_dec_kernel(const __grid_constant__ AttnDecArgs a) {
+  pdl_wait();
+  extern __shared__ unsigned char ad_smem_raw[];
+  unsigned char *ring =
+      reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(ad_smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char *sq = ring + kAdSlots * kAdHalf;  // two query buffers
+  unsigned char *sp = sq + 2 * kAdQBytes;         // two P buffers
+  __shared__ __align__(8) uint64_t full[kAdSlots], empty[kAdSlots], q_full[2], q_empty[2], s_full[2], s_free[2],
+      p_full[2], o_full[2], o_free[2], mma_done;
+  __shared__ uint32_t s_tmem;
+  __shared__ volatile int s_abort;
+  __shared__ int s_issued, s_consumed, s_q_issued, s_q_consumed, s_last;
+  __shared__ float red[2][4][kAdN];   // per softmax warp and query: the tile maximum (double buffered)
+  __shared__ float lred[2][4][kAdN];  // per softmax warp and query: the row sum (double buffered)
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                 "r"(kAdTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (threadIdx.x == 32) {
+    for (int i = 0; i < kAdSlots; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_free[i], 4);
+    }
+    mbar_init(&mma_done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    s_abort = 0;
+    s_issued = s_consumed = s_q_issued = s_q_consumed = 0;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  auto give_up = [&]() {
+    if (!s_abort) {
+      s_abort = 1;
+      if (a.err) atomicOr(a.err, kErrTimeout);
+    }
+  };
+
+  if (warp == 0) {
+    // ---- producer: query rows per item, then K and V half tiles ----------
+    if (lane == 0) {
+      int idx = 0, qi = 0;
+      for (int item = blockIdx.x; item < a.n_items && !s_abort; item += gridDim.x) {
+        const AdItem it = ad_item(a, item);
+        if (it.nt == 0) continue;
+        const int qb = qi & 1;
+        if (!mbar_wait(&q_empty[qb], ((qi >> 1) & 1) ^ 1)) { give_up(); break; }
+        mbar_expect_tx(&q_full[qb], kAdQBytes);
+        tma_load_2d(sq + qb * kAdQBytes, &a.tmq, it.h * kAdD, it.rq0, &q_full[qb]);
+        tma_load_2d(sq + qb * kAdQBytes + kAdQBytes / 2, &a.tmq, it.h * kAdD + 64, it.rq0, &q_full[qb]);
+        s_q_issued = ++qi;
+        const int base = (it.req * a.Hkv + it.h) * a.S_cap;
+        bool stop = false;
+        for (int t = 0; t < it.nt && !stop; ++t) {
+          const int y = base + (it.t0 + t) * kAdTile;
+          for (int kv = 0; kv < 2; ++kv) {
+            const int s = idx % kAdSlots;
+            if (!mbar_wait(&empty[s], ((idx / kAdSlots) & 1) ^ 1) || s_abort) {
+              give_up();
+              stop = true;
+              break;
+            }
+            mbar_expect_tx(&full[s], kAdHalf);
+            const CUtensorMap *m = kv ? &a.tmv : &a.tmk;
+            tma_load_2d(ring + s * kAdHalf, m, 0, y, &full[s]);
+            tma_load_2d(ring + s * kAdHalf + kAdBox, m, 64, y, &full[s]);
+            s_issued = ++idx;
+          }
+        }
+        if (stop) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer --------------------------------------------------------
+    if (lane == 0) {
+      int idx = 0, qi = 0, T = 0;
+      bool stop = false;
+      for (int item = blockIdx.x; item < a.n_items && !stop && !s_abort; item += gridDim.x) {
+        const AdItem it = ad_item(a, item);
+        if (it.nt == 0) continue;
+        const int qb = qi & 1;
+        if (!mbar_wait(&q_full[qb], (qi >> 1) & 1)) { give_up(); break; }
+        s_q_consumed = qi + 1;
+        const uint32_t qa = smem_u32(sq + qb * kAdQBytes);
+        for (int t = 0; t < it.nt; ++t, ++T) {
+          const int sb = T & 1;
+          const uint32_t ph = (T >> 1) & 1;
+          // S^T = K Q^T into S[sb]
+          const int sk = idx % kAdSlots;
+          if (!mbar_wait(&full[sk], (idx / kAdSlots) & 1) || !mbar_wait(&s_free[sb], ph ^ 1) || s_abort) {
+            give_up();
+            stop = true;
+            break;
+          }
+          s_consumed = ++idx;
+          tc_fence_after();
+          const uint32_t ka = smem_u32(ring + sk * kAdHalf);
+#pragma unroll
+          for (int kk = 0; kk < kAdD / 16; ++kk)
+            tc_mma(tmem + 16 * sb, umma_desc_k128(ka + (kk >> 2) * kAdBox + 32 * (kk & 3)),
+                   umma_desc_k128(qa + (kk >> 2) * (kAdQBytes / 2) + 32 * (kk & 3)), kAdIdescS, kk ? 1u : 0u);
+          tc_commit(&empty[sk]);
+          tc_commit(&s_full[sb]);
+          // O^T = V^T P^T into O[sb], once P is written and O[sb] was folded
+          const int sv = idx % kAdSlots;
+          if (!mbar_wait(&full[sv], (idx / kAdSlots) & 1) || !mbar_wait(&p_full[sb], ph) ||
+              !mbar_wait(&o_free[sb], ph ^ 1) || s_abort) {
+            give_up();
+            stop = true;
+            break;
+          }
+          s_consumed = ++idx;
+          tc_fence_after();
+          const uint32_t va = smem_u32(ring + sv * kAdHalf);
+          const uint32_t pa = smem_u32(sp + sb * kAdPBytes);
+#pragma unroll
+          for (int kk = 0; kk < kAdTile / 16; ++kk)
+            tc_mma(tmem + 32 + 16 * sb, umma_desc_mn128_2atoms(va + 2048 * kk),
+                   umma_desc_k128(pa + (kk >> 2) * (kAdPBytes / 2) + 32 * (kk & 3)), kAdIdescO, kk ? 1u : 0u);
+          tc_commit(&empty[sv]);
+          tc_commit(&o_full[sb]);
+        }
+        tc_commit(&q_empty[qb]);
+        ++qi;
+      }
+      // every product this thread issued has completed before the CTA moves on
+      tc_commit(&mma_done);
+      if (!mbar_wait(&mma_done, 0)) give_up();
+    }
+  } else {
+    // ---- softmax and output: thread = position of a tile, and = dim of O ---
+    const int qd = warp & 3;  // TMEM lane quadrant of this warp
+    const int p = 32 * qd + lane;
+    const uint32_t tl = tmem + (static_cast<uint32_t>(32 * qd) << 16);
+    const float sqrt_d = sqrtf(static_cast<float>(kAdD));
+    int T = 0, ni = 0;
+    // ok: the last barrier's verdict (the same in every softmax thread); lok:
+    // this thread's own waits so far, folded into ok at the next barrier, so
+    // the four warps always stop at the same point
+    bool ok = true, lok = true;
+    for (int item = blockIdx.x; item < a.n_items; item += gridDim.x, ++ni) {
+      const AdItem it = ad_item(a, item);
+      int qpos[kAdN], qtb[kAdN];
+      unsigned long long qmask[kAdN];
+      bool qv[kAdN];
+#pragma unroll
+      for (int q = 0; q < kAdN; ++q) {
+        const int r = it.rq0 + q;
+        qv[q] = q < it.nq && a.rows.req[r] >= 0;
+        qpos[q] = qv[q] ? row_slot(a.rows, r) : -1;
+        qtb[q] = (qv[q] && a.rows.tb) ? a.rows.tb[r] : 0x7fffffff;
+        qmask[q] = (qv[q] && a.rows.mask) ? a.rows.mask[r] : 0ull;
+      }
+      float m[kAdN], l[kAdN], o[kAdN], al_prev[kAdN];
+#pragma unroll
+      for (int q = 0; q < kAdN; ++q) {
+        m[q] = -INFINITY;
+        l[q] = 0.f;
+        o[q] = 0.f;
+        al_prev[q] = 0.f;
+      }
+      auto fold = [&](int Tp) -> bool {  // o = o * alpha + O_{Tp}
+        const int ob = Tp & 1;
+        const bool w = mbar_wait(&o_full[ob], (Tp >> 1) & 1);
+        tc_fence_after();
+        float ov[kAdN];
+        tmem_ld16(tl + 32 + 16 * ob, ov);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&o_free[ob]);
+#pragma unroll
+        for (int q = 0; q < kAdN; ++q) o[q] = o[q] * al_prev[q] + ov[q];
+        return w;
+      };
+      for (int t = 0; t < it.nt; ++t, ++T) {
+        const int sb = T & 1;
+        lok = mbar_wait(&s_full[sb], (T >> 1) & 1) && lok;
+        tc_fence_after();
+        float s[kAdN];
+        tmem_ld16(tl + 16 * sb, s);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[sb]);
+        const int pos = (it.t0 + t) * kAdTile + p;
+#pragma unroll
+        for (int q = 0; q < kAdN; ++q) {
+          const bool vis = qv[q] && pos <= qpos[q] &&
+                           (pos < qtb[q] || (pos - qtb[q] < 64 && ((qmask[q] >> (pos - qtb[q])) & 1ull)));
+          s[q] = vis ? __fdiv_rn(s[q], sqrt_d) : -INFINITY;
+        }
+#pragma unroll
+        for (int q = 0; q < kAdN; ++q) {
+          if (q < it.nq) {  // uniform over the CTA
+            const float mx = warp_max(s[q]);
+            if (lane == 0) red[sb][qd][q] = mx;
+          }
+        }
+        ok = bar_and_softmax(lok && !s_abort);
+        if (!ok) break;
+        float al[kAdN], pr[kAdN];
+#pragma unroll
+        for (int q = 0; q < kAdN; ++q) {
+          al[q] = 0.f;
+          pr[q] = 0.f;
+          if (q < it.nq) {
+            const float mt = fmaxf(fmaxf(red[sb][0][q], red[sb][1][q]), fmaxf(red[sb][2][q], red[sb][3][q]));
+            const float mn = fmaxf(m[q], mt);
+            al[q] = (m[q] == -INFINITY) ? 0.f : expf(m[q] - mn);
+            pr[q] = (s[q] == -INFINITY) ? 0.f : expf(s[q] - mn);
+            l[q] = l[q] * al[q] + pr[q];
+            m[q] = mn;
+          }
+        }
+        // P^T as bf16: row q, position p of the K-major swizzled tile
+        {
+          unsigned char *pt = sp + sb * kAdPBytes + (p >> 6) * (kAdPBytes / 2);
+          const int chunk = (p & 63) >> 3, byte = (p & 7) * 2;
+#pragma unroll
+          for (int q = 0; q < kAdN; ++q)
+            *reinterpret_cast<__nv_bfloat16 *>(pt + q * 128 + ((chunk ^ (q & 7)) << 4) + byte) =
+                __float2bfloat16_rn(pr[q]);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[sb]);
+        if (t > 0) lok = fold(T - 1) && lok;
+#pragma unroll
+        for (int q = 0; q < kAdN; ++q) al_prev[q] = al[q];
+      }
+      if (ok && it.nt > 0) lok = fold(T - 1) && lok;
+      // the row sums over the 128 positions
+      const int lb = ni & 1;
+#pragma unroll
+      for (int q = 0; q < kAdN; ++q) {
+        if (q < it.nq) {
+          const float sm = warp_sum(l[q]);
+          if (lane == 0) lred[lb][qd][q] = sm;
+        }
+      }
+      ok = bar_and_softmax(ok && lok && !s_abort);
+      if (!ok) break;
+      float L[kAdN];
+#pragma unroll
+      for (int q = 0; q < kAdN; ++q) L[q] = (q < it.nq) ? (lred[lb][0][q] + lred[lb][1][q]) + (lred[lb][2][q] + lred[lb][3][q]) : 0.f;
+      if (a.nsplit == 1) {
+#pragma unroll
+        for (int q = 0; q < kAdN; ++q)
+          if (qv[q] && qpos[q] < a.S_cap)
+            a.out[static_cast<size_t>(it.rq0 + q) * a.ldo + it.h * kAdD + p] =
+                __float2bfloat16_rn(L[q] > 0.f ? __fdiv_rn(o[q], L[q]) : 0.f);
+        continue;
+      }
+      // split: this item's partial, then the last split of (group, head) merges
+      bool any = false;
+#pragma unroll
+      for (int q = 0; q < kAdN; ++q) any |= qv[q];
+      if (!any) continue;  // the same for every split of the group
+      float *pp = a.part + static_cast<size_t>(item) * kAdPartFloats;
+#pragma unroll
+      for (int q = 0; q < kAdN; ++q) pp[q * kAdD + p] = o[q];
+#pragma unroll
+      for (int q = 0; q < kAdN; ++q)
+        if (p == q) {
+          pp[kAdN * kAdD + q] = m[q];
+          pp[kAdN * kAdD + kAdN + q] = L[q];
+        }
+      __threadfence();
+      bar_softmax();
+      const int gh = item / a.nsplit;
+      if (p == 0) s_last = (atomicAdd(a.ticket + gh, 1) == a.nsplit - 1) ? 1 : 0;
+      bar_softmax();
+      if (s_last) {
+        __threadfence();
+        const float *p0 = a.part + static_cast<size_t>(gh) * a.nsplit * kAdPartFloats;
+#pragma unroll 1
+        for (int q = 0; q < kAdN; ++q) {
+          if (!qv[q] || qpos[q] >= a.S_cap) continue;
+          float M = -INFINITY;
+          for (int sp2 = 0; sp2 < a.nsplit; ++sp2) {
+            const float *ps = p0 + static_cast<size_t>(sp2) * kAdPartFloats;
+            if (__ldcg(ps + kAdN * kAdD + kAdN + q) > 0.f) M = fmaxf(M, __ldcg(ps + kAdN * kAdD + q));
+          }
+          float num = 0.f, den = 0.f;
+          for (int sp2 = 0; sp2 < a.nsplit; ++sp2) {
+            const float *ps = p0 + static_cast<size_t>(sp2) * kAdPartFloats;
+            const float Ls = __ldcg(ps + kAdN * kAdD + kAdN + q);
+            if (Ls > 0.f) {
+              const float wgt = expf(__ldcg(ps + kAdN * kAdD + q) - M);
+              num += wgt * __ldcg(ps + q * kAdD + p);
+              den += wgt * Ls;
+            }
+          }
+          a.out[static_cast<size_t>(it.rq0 + q) * a.ldo + it.h * kAdD + p] =
+              __float2bfloat16_rn(den > 0.f ? __fdiv_rn(num, den) : 0.f);
+        }
+        if (p == 0) a.ticket[gh] = 0;
+      }
+      bar_softmax();  // s_last is rewritten by the next item
+    }
+    if (!ok) give_up();
+  }
+
+  pdl_launch();
+  __syncthreads();
+  // after a timeout: bounded waits for the copies still in flight
+  if (s_abort && threadIdx.x == 0) {
+    for (int idx = s_consumed; idx < s_issued; ++idx) mbar_wait(&full[idx % kAdSlots], (idx / kAdSlots) & 1);
+    for (int qi = s_q_consumed; qi < s_q_issued; ++qi) mbar_wait(&q_full[qi & 1], (qi >> 1) & 1);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kAdTmemCols) : "memory");
+}
+
+}  // namespace
+
+int attn_dec_smem_bytes() { return kAdSmem; }
+
+cudaError_t attn_dec_set_attrs() {
+  return cudaFuncSetAttribute(attn_dec_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAdSmem);
+}
+
+cudaError_t attn_dec_launch(const AttnDecArgs &a, int grid, cudaStream_t stream, bool pdl) {
+  cudaLaunchConfig_t lc{};
+  lc.gridDim = dim3(grid);
+  lc.blockDim = dim3(kAdThreads);
+  lc.dynamicSmemBytes = kAdSmem;
+  lc.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = at;
+  lc.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&lc, attn_dec_kernel, a);
+}
+
+}  // namespace specdec

@@ -41,6 +41,8 @@
 #include "attn_tc.cuh"
 #include "sample.cuh"
 #include "tree.cuh"
+#include "kern_table.cuh"
+#include "attn_dec.cuh"
 
 using namespace specdec;
 
@@ -107,10 +109,11 @@ struct GraphKey {
   int top_k;
   float top_p;
   uint64_t tree_sig;  // 0: chain; else depth and branching
+  int mode = 0;       // 0: a whole generation; 1: rounds of the step API
   bool operator<(const GraphKey &o) const {
-    return std::tie(B, S, k, greedy, rng_mode, catchup, max_new, u_rounds, T, seed, top_k, top_p, tree_sig) <
+    return std::tie(B, S, k, greedy, rng_mode, catchup, max_new, u_rounds, T, seed, top_k, top_p, tree_sig, mode) <
            std::tie(o.B, o.S, o.k, o.greedy, o.rng_mode, o.catchup, o.max_new, o.u_rounds, o.T, o.seed, o.top_k,
-                    o.top_p, o.tree_sig);
+                    o.top_p, o.tree_sig, o.mode);
   }
 };
 
@@ -151,6 +154,8 @@ __global__ void round_cond_kernel(cudaGraphConditionalHandle hnd, int *active_co
   cudaGraphSetConditional(hnd, more);
 }
 
+__global__ void set_int_kernel(int *p, int v) { *p = v; }
+
 __global__ void count_iter_kernel(int *iters, int *active_count) {
   *iters = *iters + 1;
   *active_count = 0;
@@ -168,6 +173,44 @@ __global__ void prime_cond_kernel(cudaGraphConditionalHandle hnd, const int *act
 __global__ void fill_odd_kernel(int *sel, int B) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b < B) sel[b] = 2 * b + 1;
+}
+
+// Step API (one call = a bounded number of rounds).  Before the rounds: each
+// request's emitted-token count, so the call can return the tokens it added.
+__global__ void step_begin_kernel(const int *n_new, int *base, int B) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < B) base[b] = n_new[b];
+}
+
+// Enters the round loop when a request is active and the call asked for rounds.
+__global__ void step_prime_kernel(cudaGraphConditionalHandle hnd, const int *active, int B, const int *target) {
+  int any = 0;
+  for (int b = threadIdx.x; b < B; b += blockDim.x) any |= active[b];
+  any = __any_sync(0xffffffffu, any);
+  if (threadIdx.x == 0) cudaGraphSetConditional(hnd, (any && *target > 0) ? 1u : 0u);
+}
+
+// Last kernel of a step round: another round while a request is active and
+// fewer than *target rounds have run in this call.
+__global__ void step_cond_kernel(cudaGraphConditionalHandle hnd, int *active_count, int *iters, const int *target) {
+  const int it = *iters + 1;
+  *iters = it;
+  const unsigned int more = (*active_count > 0 && it < *target) ? 1u : 0u;
+  *active_count = 0;
+  cudaGraphSetConditional(hnd, more);
+}
+
+// After the rounds: the tokens each request emitted in this call (at most
+// cap per request; count = all it emitted).
+__global__ void step_collect_kernel(const int *tokens_out, int out_len, int prompt_len, const int *n_new,
+                                    const int *base, int B, int cap, int *out, int *counts) {
+  const int b = blockIdx.x;
+  if (b >= B) return;
+  const int b0 = base[b], n = n_new[b] - b0;
+  const int lim = min(max(n, 0), min(cap, out_len - prompt_len - b0));
+  for (int i = threadIdx.x; i < lim; i += blockDim.x)
+    out[static_cast<size_t>(b) * cap + i] = tokens_out[static_cast<size_t>(b) * out_len + prompt_len + b0 + i];
+  if (threadIdx.x == 0) counts[b] = n;
 }
 
 }  // namespace
@@ -209,6 +252,14 @@ struct specdec_handle {
   size_t uniforms_cap = 0;
   int *d_iters = nullptr;
   int *h_pinned = nullptr;
+  // step API: open after specdec_prefill; the graph key of its rounds, the
+  // next round's index (host uniforms of a step go to that row), the
+  // per-request counts before the current call and its round target
+  bool step_open = false;
+  GraphKey step_key{};
+  int step_round = 0;
+  int *d_step_base = nullptr, *d_step_target = nullptr, *d_step_tok = nullptr, *d_step_cnt = nullptr;
+  size_t step_tok_cap = 0;
 
   // tensor parallelism: this rank's index, the group size and its communicator
   int tp_rank = 0, tp_world = 1;
@@ -226,6 +277,10 @@ struct specdec_handle {
   int samp_max_cluster = 1;  // largest cluster of draft_sample_cluster_kernel
   int attn_ctas_per_sm = 2;  // attention splits the cache while the grid stays within this many CTAs per SM
   bool attn_tc = true;       // tensor-core attention for bf16 caches, head_dim 64, groups of >= attn_tc_min_q queries
+  bool attn_dec = true;      // tensor-core decode attention for bf16 caches, head_dim 128, groups of <= 16 queries
+  float *ad_part = nullptr;  // its split partials [groups * heads * kAdMaxSplit][kAdPartFloats]
+  int *ad_ticket = nullptr;  // its per-(group, head) split counters
+  int ad_groups = 0;         // groups the partial buffer holds
   int attn_tc_min_q = kAtcMinQ;
   // row batches that take the tensor-core GEMM instead of the GEMV: at least
   // gemm_min_rows rows, or gemm_wide_rows rows of a layer with at least
@@ -591,6 +646,39 @@ void launch_pdl(specdec_handle *h, void (*kern)(KArgs...), dim3 grid, dim3 block
   launch_ex(h, true, kern, grid, block, smem, dim3(1, 1, 1), args...);
 }
 
+// Launch of a kernel given by pointer (a table entry of kern_linear.cu /
+// kern_attn.cu) whose one parameter is `arg`, with clusters and programmatic
+// stream serialization as launch_ex.
+template <typename Arg>
+void launch_fn(specdec_handle *h, bool pdl, const void *fn, dim3 grid, dim3 block, size_t smem, dim3 cluster,
+               const Arg &arg) {
+  if (!fn) fail(SPECDEC_ERR_UNSUPPORTED, "no kernel variant for this shape");
+  cudaLaunchConfig_t lc{};
+  lc.gridDim = grid;
+  lc.blockDim = block;
+  lc.dynamicSmemBytes = smem;
+  lc.stream = h->stream;
+  cudaLaunchAttribute at[2];
+  int na = 0;
+  if (cluster.x * cluster.y * cluster.z > 1) {
+    at[na].id = cudaLaunchAttributeClusterDimension;
+    at[na].val.clusterDim.x = cluster.x;
+    at[na].val.clusterDim.y = cluster.y;
+    at[na].val.clusterDim.z = cluster.z;
+    ++na;
+  }
+  if (pdl && h->use_pdl) {
+    at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  lc.attrs = at;
+  lc.numAttrs = na;
+  void *args[1] = {const_cast<Arg *>(&arg)};
+  CK(cudaLaunchKernelExC(&lc, fn, args));
+  ++h->launches;
+}
+
 // cuTensorMapEncodeTiled, looked up from the driver once (no link-time
 // dependency on libcuda).
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
@@ -663,19 +751,12 @@ constexpr size_t kLinLnSmemMax = 128 * 1024;
 template <int EPI, int NC>
 void launch_linear_nc(specdec_handle *h, const LinearArgs &a, dim3 grid, dim3 block) {
   const bool bf = act_bf16(h), i8 = w_int8(h);
+  size_t smem = 0;
   if (a.in_g) {
-    const size_t smem = static_cast<size_t>(kRowTile) * a.K * h->act_elt;
+    smem = static_cast<size_t>(kRowTile) * a.K * h->act_elt;
     if (smem > kLinLnSmemMax) fail(SPECDEC_ERR_UNSUPPORTED, "input rows too wide for the fused LayerNorm");
-    if (i8 && bf) launch_pdl(h, linear_kernel<int8_t, __nv_bfloat16, EPI, true, NC>, grid, block, smem, a);
-    else if (i8) launch_pdl(h, linear_kernel<int8_t, float, EPI, true, NC>, grid, block, smem, a);
-    else if (bf) launch_pdl(h, linear_kernel<float, __nv_bfloat16, EPI, true, NC>, grid, block, smem, a);
-    else launch_pdl(h, linear_kernel<float, float, EPI, true, NC>, grid, block, smem, a);
-  } else {
-    if (i8 && bf) launch_pdl(h, linear_kernel<int8_t, __nv_bfloat16, EPI, false, NC>, grid, block, 0, a);
-    else if (i8) launch_pdl(h, linear_kernel<int8_t, float, EPI, false, NC>, grid, block, 0, a);
-    else if (bf) launch_pdl(h, linear_kernel<float, __nv_bfloat16, EPI, false, NC>, grid, block, 0, a);
-    else launch_pdl(h, linear_kernel<float, float, EPI, false, NC>, grid, block, 0, a);
   }
+  launch_fn(h, true, linear_kernel_fn(i8, bf, EPI, a.in_g ? 1 : 0, NC), grid, block, smem, dim3(1, 1, 1), a);
 }
 
 // 2-D TMA view [rows][K] of a bf16 matrix with row stride ld elements, box
@@ -789,18 +870,13 @@ void launch_linear(specdec_handle *h, LinearArgs a) {
 
 // Dynamic shared memory of the input-LayerNorm linear kernels: kLinLnSmemMax
 // holds kRowTile rows of up to 4096 fp32 or 8192 bf16 elements.
-template <int EPI, int NC>
-void set_linear_attr_nc() {
+void set_linear_attrs() {
   const int b = static_cast<int>(kLinLnSmemMax);
-  CK(cudaFuncSetAttribute(linear_kernel<int8_t, __nv_bfloat16, EPI, true, NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
-  CK(cudaFuncSetAttribute(linear_kernel<int8_t, float, EPI, true, NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
-  CK(cudaFuncSetAttribute(linear_kernel<float, __nv_bfloat16, EPI, true, NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
-  CK(cudaFuncSetAttribute(linear_kernel<float, float, EPI, true, NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, b));
-}
-template <int EPI>
-void set_linear_attr_epi() {
-  set_linear_attr_nc<EPI, 2>();
-  set_linear_attr_nc<EPI, 4>();
+  for (int w8 = 0; w8 < 2; ++w8)
+    for (int abf = 0; abf < 2; ++abf)
+      for (int epi = kEpiStore; epi <= kEpiGelu; ++epi)
+        for (int nc : {2, 4})
+          CK(cudaFuncSetAttribute(linear_kernel_fn(w8, abf, epi, 1, nc), cudaFuncAttributeMaxDynamicSharedMemorySize, b));
 }
 // Records in active[ks] how many split-K clusters of ks CTAs (kGemmSmem
 // bytes each) the device runs at once (0: none) and returns the largest ks
@@ -868,30 +944,22 @@ int set_samp_cluster_attrs(int V) {
   if (best == 4 && one(draft_sample_cluster_kernel<8>, 8)) best = 8;
   return best;
 }
-void set_linear_attrs() {
-  set_linear_attr_epi<kEpiStore>();
-  set_linear_attr_epi<kEpiResid>();
-  set_linear_attr_epi<kEpiQKV>();
-  set_linear_attr_epi<kEpiSwiGLU>();
-  set_linear_attr_epi<kEpiGelu>();
-}
 
-template <typename AT, typename KT, int D>
-void set_attn_attr() {
+template <typename KT, int D>
+void set_attn_attr(int kt) {
   const int bytes = AttnGeom<KT, D>::smem_bytes(2);
-  CK(cudaFuncSetAttribute(attention_kernel<AT, KT, D, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-  CK(cudaFuncSetAttribute(attention_kernel<AT, KT, D, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-  CK(cudaFuncSetAttribute(attention_kernel<AT, KT, D, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-  CK(cudaFuncSetAttribute(attention_kernel<AT, KT, D, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  for (int abf = 0; abf < 2; ++abf)
+    for (int qt : {1, 2, 4, 8})
+      CK(cudaFuncSetAttribute(attention_kernel_fn(abf, kt, D, qt), cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
 }
-template <typename AT, typename KT>
-void set_attn_attrs() {
-  set_attn_attr<AT, KT, 4>();
-  set_attn_attr<AT, KT, 8>();
-  set_attn_attr<AT, KT, 16>();
-  set_attn_attr<AT, KT, 32>();
-  set_attn_attr<AT, KT, 64>();
-  set_attn_attr<AT, KT, 128>();
+template <typename KT>
+void set_attn_attrs(int kt) {
+  set_attn_attr<KT, 4>(kt);
+  set_attn_attr<KT, 8>(kt);
+  set_attn_attr<KT, 16>(kt);
+  set_attn_attr<KT, 32>(kt);
+  set_attn_attr<KT, 64>(kt);
+  set_attn_attr<KT, 128>(kt);
 }
 
 // Splits: one tile of positions per split where the cache is long, at most a
@@ -917,16 +985,9 @@ void launch_attention_d(specdec_handle *h, AttnArgs &a, int ngroups, const void 
   const size_t smem = static_cast<size_t>(G::smem_bytes(a.chunk > G::kTile ? 2 : 1));
   dim3 grid(ngroups * ngt, a.H, ns);
   dim3 block(kAttnThreads);
-  auto go = [&](auto kern) {
-    if (ns == 1) launch_pdl(h, kern, grid, block, smem, a);
-    else launch_cluster(h, kern, grid, block, smem, dim3(1, 1, ns), a);
-  };
-  switch (qt) {
-    case 1: go(attention_kernel<AT, KT, D, 1>); break;
-    case 2: go(attention_kernel<AT, KT, D, 2>); break;
-    case 4: go(attention_kernel<AT, KT, D, 4>); break;
-    default: go(attention_kernel<AT, KT, D, 8>); break;
-  }
+  const int kt = std::is_same<KT, int8_t>::value ? 2 : std::is_same<KT, __nv_bfloat16>::value ? 1 : 0;
+  const void *fn = attention_kernel_fn(std::is_same<AT, __nv_bfloat16>::value ? 1 : 0, kt, D, qt);
+  launch_fn(h, true, fn, grid, block, smem, ns == 1 ? dim3(1, 1, 1) : dim3(1, 1, ns), a);
 }
 
 template <typename AT, typename KT>
@@ -968,6 +1029,32 @@ void attention(specdec_handle *h, const Dims &dm, RowsView rows, int R, int Q, c
     t.out = static_cast<__nv_bfloat16 *>(h->ATT); t.ldo = dm.dq; t.err = h->st.err;
     launch_pdl(h, attn_tc_kernel, dim3(ngroups * ((Q + 127) / 128), dm.H), dim3(kAtcThreads),
                static_cast<size_t>(kAtcSmem), t);
+    return;
+  }
+  if (h->attn_dec && h->ad_part && bf && kvbf && dm.D == kAdD && dm.H == dm.Hkv && Q <= kAdN && ngroups <= h->ad_groups &&
+      dm.dq % 8 == 0) {
+    // few queries per request (draft steps, verify blocks): positions on the
+    // MMA's M side, persistent CTAs streaming the cache
+    AttnDecArgs d{};
+    d.tmq = gemm_operand_map(h->Q, dm.dq, R, dm.dq, kAdN);
+    d.tmk = kv_tensor_map<__nv_bfloat16, kAdD>(kc, nrows);
+    d.tmv = kv_tensor_map<__nv_bfloat16, kAdD>(vc, nrows);
+    d.rows = rows; d.R = R; d.Q = Q; d.S_cap = S_cap; d.H = dm.H; d.Hkv = dm.Hkv;
+    // splits while the (group, head) items would spread unevenly over the SMs
+    const int base = ngroups * dm.H;
+    const int tiles = (S_cap + kAdTile - 1) / kAdTile;
+    int ns = 1;
+    auto waste = [&](int n) {
+      const double per = static_cast<double>(base) * n / h->num_sms;
+      return std::ceil(per) / per - 1.0;
+    };
+    while (ns < kAdMaxSplit && 2 * ns <= tiles && waste(ns) > 0.05) ns *= 2;
+    d.nsplit = ns;
+    d.n_items = base * ns;
+    d.out = static_cast<__nv_bfloat16 *>(h->ATT); d.ldo = dm.dq;
+    d.part = h->ad_part; d.ticket = h->ad_ticket; d.err = h->st.err;
+    CK(attn_dec_launch(d, std::min(d.n_items, h->num_sms), h->stream, h->use_pdl));
+    ++h->launches;
     return;
   }
   if (h->cfg.kv_dtype == SPECDEC_INT8) {
@@ -1363,8 +1450,11 @@ void destroy_graphs(specdec_handle *h) {
   h->graphs.clear();
 }
 
-// Builds prologue -> WHILE(active) { round } as one executable graph.
-GraphEntry build_graph(specdec_handle *h, int B, int S, uint32_t seed, int max_iters) {
+// Builds pre -> WHILE(cond) { body } as one executable graph: pre() and
+// body() enqueue on the handle's stream (captured); pre ends with the kernel
+// that primes the condition, body with the one that re-evaluates it.
+template <class Pre, class Body>
+GraphEntry build_loop_graph(specdec_handle *h, Pre pre, Body body) {
   GraphEntry ge;
   CK(cudaGraphCreate(&ge.graph, 0));
   cudaGraphConditionalHandle hnd;
@@ -1372,8 +1462,7 @@ GraphEntry build_graph(specdec_handle *h, int B, int S, uint32_t seed, int max_i
   CK(cudaStreamBeginCaptureToGraph(h->stream, ge.graph, nullptr, nullptr, 0, cudaStreamCaptureModeThreadLocal));
   h->launches = 0;
   try {
-    enqueue_prologue(h, B, S, seed);
-    launch(h, prime_cond_kernel, dim3(1), dim3(32), 0, hnd, static_cast<const int *>(h->st.active), B);
+    pre(hnd);
   } catch (...) {
     cudaGraph_t g;
     cudaStreamEndCapture(h->stream, &g);
@@ -1398,21 +1487,50 @@ GraphEntry build_graph(specdec_handle *h, int B, int S, uint32_t seed, int max_i
   cp.conditional.size = 1;
   cudaGraphNode_t wnode;
   CK(cudaGraphAddNode(&wnode, ge.graph, sinks.data(), sinks.size(), &cp));
-  cudaGraph_t body = cp.conditional.phGraph_out[0];
-  CK(cudaStreamBeginCaptureToGraph(h->stream, body, nullptr, nullptr, 0, cudaStreamCaptureModeThreadLocal));
+  cudaGraph_t bg = cp.conditional.phGraph_out[0];
+  CK(cudaStreamBeginCaptureToGraph(h->stream, bg, nullptr, nullptr, 0, cudaStreamCaptureModeThreadLocal));
   h->launches = 0;
   try {
-    enqueue_round(h);
-    launch(h, round_cond_kernel, dim3(1), dim3(1), 0, hnd, h->st.active_count, h->d_iters, max_iters, h->st.err);
+    body(hnd);
   } catch (...) {
     cudaGraph_t g;
     cudaStreamEndCapture(h->stream, &g);
     throw;
   }
   ge.body_kernels = h->launches;
-  CK(cudaStreamEndCapture(h->stream, &body));
+  CK(cudaStreamEndCapture(h->stream, &bg));
   CK(cudaGraphInstantiate(&ge.exec, ge.graph, 0));
   return ge;
+}
+
+// Builds prologue -> WHILE(active) { round } as one executable graph.
+GraphEntry build_graph(specdec_handle *h, int B, int S, uint32_t seed, int max_iters) {
+  return build_loop_graph(
+      h,
+      [&](cudaGraphConditionalHandle hnd) {
+        enqueue_prologue(h, B, S, seed);
+        launch(h, prime_cond_kernel, dim3(1), dim3(32), 0, hnd, static_cast<const int *>(h->st.active), B);
+      },
+      [&](cudaGraphConditionalHandle hnd) {
+        enqueue_round(h);
+        launch(h, round_cond_kernel, dim3(1), dim3(1), 0, hnd, h->st.active_count, h->d_iters, max_iters, h->st.err);
+      });
+}
+
+// The step API's rounds: WHILE(active and fewer than *d_step_target rounds) { round }.
+GraphEntry build_step_graph(specdec_handle *h) {
+  const int B = h->st.B;
+  return build_loop_graph(
+      h,
+      [&](cudaGraphConditionalHandle hnd) {
+        launch(h, step_prime_kernel, dim3(1), dim3(32), 0, hnd, static_cast<const int *>(h->st.active), B,
+               static_cast<const int *>(h->d_step_target));
+      },
+      [&](cudaGraphConditionalHandle hnd) {
+        enqueue_round(h);
+        launch(h, step_cond_kernel, dim3(1), dim3(1), 0, hnd, h->st.active_count, h->d_iters,
+               static_cast<const int *>(h->d_step_target));
+      });
 }
 
 // d_prompts may be any device buffer; it is staged into the handle's prompt
@@ -1421,6 +1539,7 @@ int generate_impl(specdec_handle *h, const specdec_gen_params *p, const int32_t 
                   int64_t *d_stats_out, const TreeCfg *tree = nullptr, bool ar = false) {
   validate_gen(h, p, B, S, tree, ar);
   SpecState &st = h->st;
+  h->step_open = false;  // a generation reuses the speculative state of a step session
   if (ar && p->max_new_tokens == 0) {  // generate_advanced returns the prompt
     CK(cudaMemcpyAsync(d_out, d_prompts, static_cast<size_t>(B) * S * sizeof(int), cudaMemcpyDeviceToDevice, h->stream));
     if (d_stats_out) CK(cudaMemsetAsync(d_stats_out, 0, static_cast<size_t>(B) * 4 * sizeof(int64_t), h->stream));
@@ -1481,6 +1600,113 @@ int generate_impl(specdec_handle *h, const specdec_gen_params *p, const int32_t 
   h->extra_launches = 1;
   h->launches = h->use_graph ? -1 : direct + 1;
   return SPECDEC_OK;
+}
+
+// Grows the device uniform table to `n` floats (the graphs that hold the old
+// table are dropped).
+void ensure_uniform_table(specdec_handle *h, size_t n) {
+  if (n <= h->uniforms_cap) return;
+  destroy_graphs(h);
+  if (h->d_uniforms) cudaFree(h->d_uniforms);
+  h->d_uniforms = nullptr;
+  h->uniforms_cap = 0;
+  CK(cudaMalloc(&h->d_uniforms, n * sizeof(float)));
+  h->uniforms_cap = n;
+}
+
+// specdec_prefill: everything of generate_speculative up to and including the
+// first token (src/nn/layer.cpp:1396-1512), then the session stays open for
+// specdec_step.  A host uniform table gets room for max_new_tokens + 2 rounds
+// at least, so steps can supply the rounds they run.
+void prefill_impl(specdec_handle *h, const specdec_gen_params *p, const int32_t *d_prompts, int B, int S) {
+  validate_gen(h, p, B, S, nullptr, false);
+  h->step_open = false;
+  SpecState &st = h->st;
+  setup_state(h, p, B, S, nullptr, false);
+  if (d_prompts != h->d_prompts)
+    CK(cudaMemcpyAsync(h->d_prompts, d_prompts, static_cast<size_t>(B) * S * sizeof(int), cudaMemcpyDeviceToDevice,
+                       h->stream));
+  const bool table = p->rng_mode == SPECDEC_RNG_HOST_UNIFORM && p->temperature > 0.f;
+  int cap = 0;
+  if (table) {
+    cap = std::max(p->uniform_rounds, p->max_new_tokens + 2);
+    const size_t row = static_cast<size_t>(st.u_slots) * sizeof(float);
+    ensure_uniform_table(h, static_cast<size_t>(B) * cap * st.u_slots);
+    st.uniforms = h->d_uniforms;
+    st.u_rounds = cap;
+    CK(cudaMemsetAsync(h->d_uniforms, 0, static_cast<size_t>(B) * cap * row, h->stream));
+    CK(cudaMemcpy2DAsync(h->d_uniforms, cap * row, p->uniforms, static_cast<size_t>(p->uniform_rounds) * row,
+                         static_cast<size_t>(p->uniform_rounds) * row, B, cudaMemcpyDefault, h->stream));
+  }
+  CK(cudaMemsetAsync(st.err, 0, sizeof(int), h->stream));
+  CK(cudaMemsetAsync(h->d_iters, 0, sizeof(int), h->stream));
+  CK(cudaMemsetAsync(st.active_count, 0, sizeof(int), h->stream));
+  h->launches = 0;
+  enqueue_prologue(h, B, S, p->seed);
+  GraphKey key{B, S, st.k, st.greedy, table ? 1 : 0, p->draft_catchup, p->max_new_tokens, table ? cap : 0,
+               p->temperature, 0u, st.greedy ? 0 : p->top_k, st.greedy ? 1.f : p->top_p, 0ull};
+  key.mode = 1;
+  h->step_key = key;
+  h->step_open = true;
+  h->step_round = 1;  // round 0 drew the first token
+}
+
+// specdec_step: `rounds` rounds of the reference's round loop
+// (src/nn/layer.cpp:1514-1656) on the open session, stopping early once no
+// request is active.  h_uniforms (optional, host or device) are the rounds'
+// draws [B][rounds][2k+1]; they replace the table rows of those rounds.  The
+// tokens each request emitted go to d_out [B][cap] and their number to
+// d_counts [B] (device buffers).
+void step_impl(specdec_handle *h, int rounds, const float *h_uniforms, int32_t *d_out, int32_t *d_counts, int cap) {
+  if (!h->step_open) fail(SPECDEC_ERR_STATE, "no open session: call specdec_prefill first");
+  if (rounds < 1) fail(SPECDEC_ERR_INVALID, "rounds must be at least 1");
+  if (!d_out || !d_counts || cap < 1) fail(SPECDEC_ERR_INVALID, "null output buffer");
+  SpecState &st = h->st;
+  const int B = st.B;
+  const bool table = h->step_key.rng_mode == 1;
+  if (h_uniforms) {
+    if (!table) fail(SPECDEC_ERR_INVALID, "the session was not opened in host-uniform mode");
+    if (h->step_round + rounds > st.u_rounds) fail(SPECDEC_ERR_RNG, "the host uniform table has too few rounds");
+    const size_t row = static_cast<size_t>(st.u_slots) * sizeof(float);
+    CK(cudaMemcpy2DAsync(h->d_uniforms + static_cast<size_t>(h->step_round) * st.u_slots, st.u_rounds * row,
+                         h_uniforms, rounds * row, rounds * row, B, cudaMemcpyDefault, h->stream));
+  }
+  if (h->use_graph) {
+    launch(h, step_begin_kernel, dim3((B + 127) / 128), dim3(128), 0, static_cast<const int *>(st.n_new),
+           h->d_step_base, B);
+    auto it = h->graphs.find(h->step_key);
+    if (it == h->graphs.end()) it = h->graphs.emplace(h->step_key, build_step_graph(h)).first;
+    CK(cudaMemsetAsync(h->d_iters, 0, sizeof(int), h->stream));
+    CK(cudaMemsetAsync(st.active_count, 0, sizeof(int), h->stream));
+    launch(h, set_int_kernel, dim3(1), dim3(1), 0, h->d_step_target, rounds);
+    CK(cudaGraphLaunch(it->second.exec, h->stream));
+    h->graph_fixed = it->second.fixed_kernels + 3;  // + step_begin, set_int, step_collect
+    h->graph_body = it->second.body_kernels;
+    h->extra_launches = 0;
+  } else {
+    h->launches = 0;
+    launch(h, step_begin_kernel, dim3((B + 127) / 128), dim3(128), 0, static_cast<const int *>(st.n_new),
+           h->d_step_base, B);
+    for (int r = 0; r < rounds; ++r) {
+      enqueue_round(h);
+      launch(h, count_iter_kernel, dim3(1), dim3(1), 0, h->d_iters, st.active_count);
+    }
+  }
+  launch(h, step_collect_kernel, dim3(B), dim3(128), 0, static_cast<const int *>(st.tokens_out), st.out_len,
+         st.prompt_len, static_cast<const int *>(st.n_new), static_cast<const int *>(h->d_step_base), B, cap, d_out,
+         d_counts);
+  if (h->use_graph) h->launches = -1;
+  h->step_round += rounds;
+}
+
+// Reads the device error word (after a synchronisation) into a status.
+void check_device_err(specdec_handle *h) {
+  CK(cudaMemcpyAsync(h->h_pinned, h->st.err, sizeof(int), cudaMemcpyDeviceToHost, h->stream));
+  sync_check(h);
+  const int err = h->h_pinned[0];
+  if (err & kErrSeqLen) fail(SPECDEC_ERR_SEQ_LEN, "Sequence length S plus past cached length exceeds max_seq_len");
+  if (err & kErrRngTable) fail(SPECDEC_ERR_RNG, "the host uniform table has too few rounds");
+  if (err & kErrTimeout) fail(SPECDEC_ERR_CUDA, "an asynchronous copy did not complete within its wait limit");
 }
 
 }  // namespace
@@ -1565,12 +1791,9 @@ int create_impl(const specdec_config *cfg, int device, int rank, int world, cons
     CK(cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking));
     h->use_graph = std::getenv("SPECDEC_NO_GRAPH") == nullptr;
     h->use_pdl = std::getenv("SPECDEC_NO_PDL") == nullptr;
-    set_attn_attrs<float, float>();
-    set_attn_attrs<float, __nv_bfloat16>();
-    set_attn_attrs<__nv_bfloat16, float>();
-    set_attn_attrs<__nv_bfloat16, __nv_bfloat16>();
-    set_attn_attrs<float, int8_t>();
-    set_attn_attrs<__nv_bfloat16, int8_t>();
+    set_attn_attrs<float>(0);
+    set_attn_attrs<__nv_bfloat16>(1);
+    set_attn_attrs<int8_t>(2);
     set_linear_attrs();
     h->gemm_max_split = set_gemm_attrs(h->gemm_clusters);
     if (const char *e = std::getenv("SPECDEC_GEMM_MAX_SPLIT"))  // a lower cap (1: no split-K), for comparisons
@@ -1579,6 +1802,8 @@ int create_impl(const specdec_config *cfg, int device, int rank, int world, cons
     if (const char *e = std::getenv("SPECDEC_ATTN_TC")) h->attn_tc = std::atoi(e) != 0;  // 0: CUDA-core attention only
     if (const char *e = std::getenv("SPECDEC_ATTN_TC_MIN_Q")) h->attn_tc_min_q = std::max(1, std::atoi(e));
     CK(cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAtcSmem));
+    CK(attn_dec_set_attrs());
+    if (const char *e = std::getenv("SPECDEC_ATTN_DEC")) h->attn_dec = std::atoi(e) != 0;  // 0: not the decode kernel
     // GEMV / GEMM routing thresholds, for tuning measurements
     if (const char *e = std::getenv("SPECDEC_GEMM_MIN_ROWS")) h->gemm_min_rows = std::max(1, std::atoi(e));
     if (const char *e = std::getenv("SPECDEC_GEMM_WIDE_ROWS")) h->gemm_wide_rows = std::max(1, std::atoi(e));
@@ -1611,6 +1836,20 @@ int create_impl(const specdec_config *cfg, int device, int rank, int world, cons
     h->tv = h->dalloc(h->t_layer_stride * td.L * kv_elt);
     h->dk = h->dalloc(h->d_layer_stride * dd.L * kv_elt);
     h->dv = h->dalloc(h->d_layer_stride * dd.L * kv_elt);
+    // cache rows past a request's length enter the P.V products with
+    // probability 0; zeroed, they are finite from the start
+    CK(cudaMemset(h->tk, 0, h->t_layer_stride * td.L * kv_elt));
+    CK(cudaMemset(h->tv, 0, h->t_layer_stride * td.L * kv_elt));
+    CK(cudaMemset(h->dk, 0, h->d_layer_stride * dd.L * kv_elt));
+    CK(cudaMemset(h->dv, 0, h->d_layer_stride * dd.L * kv_elt));
+    if (cfg->kv_dtype == SPECDEC_BF16 && cfg->act_dtype == SPECDEC_BF16 && (td.D == kAdD || dd.D == kAdD)) {
+      h->ad_groups = B;
+      const int Hm = std::max(td.H, dd.H);
+      h->ad_part = static_cast<float *>(
+          h->dalloc(static_cast<size_t>(B) * Hm * kAdMaxSplit * kAdPartFloats * sizeof(float)));
+      h->ad_ticket = static_cast<int *>(h->dalloc(static_cast<size_t>(B) * Hm * sizeof(int)));
+      CK(cudaMemset(h->ad_ticket, 0, static_cast<size_t>(B) * Hm * sizeof(int)));
+    }
     if (kv8) {
       auto fb = [&](size_t n) { return static_cast<float *>(h->dalloc(n * sizeof(float))); };
       h->tks = fb(h->t_layer_stride / td.D * td.L);
@@ -1702,6 +1941,11 @@ int create_impl(const specdec_config *cfg, int device, int rank, int world, cons
     h->d_prompts = ib(static_cast<size_t>(B) * cfg->max_prompt_len);
     h->d_out = ib(static_cast<size_t>(B) * out_len_max);
     h->d_stats = static_cast<long long *>(h->dalloc(static_cast<size_t>(B) * 4 * sizeof(long long)));
+    h->d_step_base = ib(B);
+    h->d_step_cnt = ib(B);
+    h->d_step_target = ib(1);
+    h->step_tok_cap = static_cast<size_t>(out_len_max);
+    h->d_step_tok = ib(static_cast<size_t>(B) * h->step_tok_cap);
     CK(cudaMallocHost(&h->h_pinned, 64));
     CK(cudaDeviceSynchronize());
     if (world > 1) {
@@ -1862,6 +2106,7 @@ int specdec_load_params(specdec_handle *h, int role, int n_params, const float *
       fail(SPECDEC_ERR_INVALID, "unknown role");
     }
     destroy_graphs(h);
+    h->step_open = false;
     CK(cudaDeviceSynchronize());
   } catch (const SpecErr &e) {
     h->err = e.msg;
@@ -1990,6 +2235,97 @@ int specdec_generate_ar_device(specdec_handle *h, const specdec_gen_params *p, c
     h->err = e.msg;
     return e.code;
   }
+}
+
+int specdec_prefill(specdec_handle *h, const specdec_gen_params *p, const int32_t *prompts, int B, int S) {
+  if (!h) return SPECDEC_ERR_INVALID;
+  try {
+    CK(cudaSetDevice(h->device));
+    if (!prompts) fail(SPECDEC_ERR_INVALID, "null buffer");
+    if (B < 1 || B > h->cfg.max_batch || S < 1 || S > h->cfg.max_prompt_len)
+      fail(SPECDEC_ERR_INVALID, "batch or prompt length out of range");
+    CK(cudaMemcpyAsync(h->d_prompts, prompts, static_cast<size_t>(B) * S * sizeof(int), cudaMemcpyHostToDevice,
+                       h->stream));
+    prefill_impl(h, p, h->d_prompts, B, S);
+    check_device_err(h);
+  } catch (const SpecErr &e) {
+    h->step_open = false;
+    h->err = e.msg;
+    return e.code;
+  }
+  return SPECDEC_OK;
+}
+
+int specdec_prefill_device(specdec_handle *h, const specdec_gen_params *p, const int32_t *d_prompts, int B, int S) {
+  if (!h) return SPECDEC_ERR_INVALID;
+  try {
+    CK(cudaSetDevice(h->device));
+    if (!d_prompts) fail(SPECDEC_ERR_INVALID, "null buffer");
+    prefill_impl(h, p, d_prompts, B, S);
+  } catch (const SpecErr &e) {
+    h->step_open = false;
+    h->err = e.msg;
+    return e.code;
+  }
+  return SPECDEC_OK;
+}
+
+int specdec_step(specdec_handle *h, int rounds, const float *uniforms, int32_t *out_tokens, int32_t *out_counts) {
+  if (!h) return SPECDEC_ERR_INVALID;
+  try {
+    CK(cudaSetDevice(h->device));
+    if (!out_tokens || !out_counts) fail(SPECDEC_ERR_INVALID, "null buffer");
+    if (!h->step_open) fail(SPECDEC_ERR_STATE, "no open session: call specdec_prefill first");
+    const int B = h->st.B;
+    const long long want = static_cast<long long>(rounds) * (h->st.k + 1);
+    const int cap = static_cast<int>(std::max(1LL, std::min<long long>(want, static_cast<long long>(h->step_tok_cap))));
+    step_impl(h, rounds, uniforms, h->d_step_tok, h->d_step_cnt, cap);
+    // the device rows are cap wide, the caller's rounds * (k + 1)
+    CK(cudaMemcpy2DAsync(out_tokens, static_cast<size_t>(want) * sizeof(int), h->d_step_tok, cap * sizeof(int),
+                         cap * sizeof(int), B, cudaMemcpyDeviceToHost, h->stream));
+    CK(cudaMemcpyAsync(out_counts, h->d_step_cnt, B * sizeof(int), cudaMemcpyDeviceToHost, h->stream));
+    check_device_err(h);
+  } catch (const SpecErr &e) {
+    h->err = e.msg;
+    return e.code;
+  }
+  return SPECDEC_OK;
+}
+
+int specdec_step_device(specdec_handle *h, int rounds, const float *uniforms, int32_t *d_out_tokens,
+                        int32_t *d_out_counts, int cap) {
+  if (!h) return SPECDEC_ERR_INVALID;
+  try {
+    CK(cudaSetDevice(h->device));
+    step_impl(h, rounds, uniforms, d_out_tokens, d_out_counts, cap);
+  } catch (const SpecErr &e) {
+    h->err = e.msg;
+    return e.code;
+  }
+  return SPECDEC_OK;
+}
+
+int specdec_session_tokens(specdec_handle *h, int32_t *out_tokens, int64_t *out_stats) {
+  if (!h) return SPECDEC_ERR_INVALID;
+  try {
+    CK(cudaSetDevice(h->device));
+    if (!out_tokens) fail(SPECDEC_ERR_INVALID, "null buffer");
+    if (!h->step_open) fail(SPECDEC_ERR_STATE, "no open session: call specdec_prefill first");
+    const SpecState &st = h->st;
+    launch(h, finalize_kernel, dim3(st.B), dim3(128), 0, st, static_cast<int *>(h->d_out),
+           reinterpret_cast<long long *>(h->d_stats));
+    const int n = st.prompt_len + std::max(1, st.max_new);
+    CK(cudaMemcpyAsync(out_tokens, h->d_out, static_cast<size_t>(st.B) * n * sizeof(int), cudaMemcpyDeviceToHost,
+                       h->stream));
+    if (out_stats)
+      CK(cudaMemcpyAsync(out_stats, h->d_stats, static_cast<size_t>(st.B) * 4 * sizeof(int64_t),
+                         cudaMemcpyDeviceToHost, h->stream));
+    check_device_err(h);
+  } catch (const SpecErr &e) {
+    h->err = e.msg;
+    return e.code;
+  }
+  return SPECDEC_OK;
 }
 
 }  // extern "C"
@@ -2149,6 +2485,9 @@ cudaError_t noalloc_base(int device, unsigned char **out) {
   return cudaSuccess;
 }
 
+// Copies the scratch array's error word to the caller's status word.
+__global__ void copy_status_kernel(const int *err, int32_t *status) { *status = *err; }
+
 struct ArenaCarver {
   unsigned char *base;
   size_t used = 0;
@@ -2161,7 +2500,7 @@ struct ArenaCarver {
 }  // namespace
 
 extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const int32_t *d_tokens, int S,
-                                              float *d_logits, void *stream) {
+                                              float *d_logits, void *stream, int32_t *d_status) {
   if (!h) return SPECDEC_ERR_INVALID;
   // The handle's working buffers are pointed at the scratch array for the
   // duration of the call and restored on every exit path.
@@ -2173,11 +2512,12 @@ extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const
     size_t tls, dls, trs, drs;
     int tcap, dcap, R_max;
     cudaStream_t stream;
+    float *gemm_ws, *ad_part;
   };
   Saved sv{h->X, h->H, h->X1, h->A, h->Q, h->ATT, h->tk, h->tv, h->dk, h->dv, h->tks, h->tvs, h->dks, h->dvs, h->KVN,
            h->st.err, h->pool,
            h->t_layer_stride, h->d_layer_stride, h->t_req_stride, h->d_req_stride, h->t_cap, h->d_cap, h->R_max,
-           h->stream};
+           h->stream, h->gemm_ws, h->ad_part};
   auto restore = [&] {
     h->X = sv.X; h->H = sv.H; h->X1 = sv.X1; h->A = sv.A; h->Q = sv.Q; h->ATT = sv.ATT;
     h->tk = sv.tk; h->tv = sv.tv; h->dk = sv.dk; h->dv = sv.dv;
@@ -2185,6 +2525,7 @@ extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const
     h->st.err = sv.err; h->pool = sv.pool;
     h->t_layer_stride = sv.tls; h->d_layer_stride = sv.dls; h->t_req_stride = sv.trs; h->d_req_stride = sv.drs;
     h->t_cap = sv.tcap; h->d_cap = sv.dcap; h->R_max = sv.R_max; h->stream = sv.stream;
+    h->gemm_ws = sv.gemm_ws; h->ad_part = sv.ad_part;
   };
   try {
     CK(cudaSetDevice(h->device));
@@ -2194,7 +2535,12 @@ extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const
     if (!m.loaded) fail(SPECDEC_ERR_STATE, "weights not loaded");
     if (!d_tokens || !d_logits) fail(SPECDEC_ERR_INVALID, "null device buffer");
     const Dims &dm = m.dm;
-    if (S < 1 || S > h->rope_max) fail(SPECDEC_ERR_INVALID, "sequence length out of range");
+    // NCCL may allocate on first use and its collectives need every rank in
+    // lockstep: tensor-parallel handles have no allocation-free forward
+    if (h->tp_world > 1) fail(SPECDEC_ERR_UNSUPPORTED, "the no-allocation forward does not run on tensor-parallel handles");
+    // the model's own capacity (the reference throws past max_seq_len,
+    // src/nn/layer.cpp:1176-1179); learned position tables end there
+    if (S < 1 || S > dm.max_seq) fail(SPECDEC_ERR_SEQ_LEN, "Sequence length S plus past cached length exceeds max_seq_len");
     const size_t act = h->act_elt;
     const bool kv8 = h->cfg.kv_dtype == SPECDEC_INT8;
     const size_t kv_elt = kv8 ? 1 : h->cfg.kv_dtype == SPECDEC_BF16 ? 2 : 4;
@@ -2244,10 +2590,17 @@ extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const
     else { h->d_req_stride = req_stride; h->d_layer_stride = req_stride; h->d_cap = S; }
     h->R_max = S;
     h->stream = st;
+    // the handle's split-K workspace and decode-attention partials belong to
+    // its own stream: this call uses neither (no split-K, no split attention)
+    h->gemm_ws = nullptr;
+    h->ad_part = nullptr;
     CK(cudaMemsetAsync(h->st.err, 0, sizeof(int), st));
     launch(h, plan_prefill_kernel, dim3((S + 255) / 256), dim3(256), 0, d_tokens, 1, S, 0, S, dm.V, h->pool.tok,
            h->pool.pos, h->pool.req, static_cast<int *>(nullptr));
     forward_rows(h, target, 0, S, S, nullptr, S, d_logits);
+    // the device-side status (bounded waits that gave up, cache rows out of
+    // range) for callers that cannot synchronise here
+    if (d_status) launch(h, copy_status_kernel, dim3(1), dim3(1), 0, static_cast<const int *>(h->st.err), d_status);
     restore();
   } catch (const SpecErr &e) {
     restore();

@@ -528,7 +528,7 @@ __global__ void __launch_bounds__(32 * kLinWarps, 2) linear_kernel(LinearArgs a)
 // int8 KV append: quantize_kv (src/nn/layer.cpp:635-665) of the K and V rows a
 // QKV pass staged, per (row, kv head): s = absmax / 127 (0 -> 1), q =
 // round(x * (1 / s)) clamped to +-127.  One warp per (row, head, K|V).
-__global__ void kv_quant_kernel(RowsView rows, int R, const float *__restrict__ stage, int kvd, int D, int Hkv,
+static __global__ void kv_quant_kernel(RowsView rows, int R, const float *__restrict__ stage, int kvd, int D, int Hkv,
                                 int S_cap, int8_t *__restrict__ kc, int8_t *__restrict__ vc, float *__restrict__ ks,
                                 float *__restrict__ vs) {
   const int r = blockIdx.x;

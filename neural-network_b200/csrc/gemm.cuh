@@ -620,7 +620,7 @@ __global__ void ln_rows_kernel(const __nv_bfloat16 *__restrict__ x, int ldx, con
 }
 
 // int8 weight codes -> their exact bf16 values.
-__global__ void i8_to_bf16_kernel(const int8_t *__restrict__ q, __nv_bfloat16 *__restrict__ out, size_t n) {
+static __global__ void i8_to_bf16_kernel(const int8_t *__restrict__ q, __nv_bfloat16 *__restrict__ out, size_t n) {
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<size_t>(gridDim.x) * blockDim.x)
     out[i] = __float2bfloat16_rn(static_cast<float>(q[i]));

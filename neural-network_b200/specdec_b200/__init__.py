@@ -36,7 +36,9 @@ EXPORTS = ("specdec_create", "specdec_destroy", "specdec_last_error", "specdec_l
            "specdec_generate", "specdec_generate_device", "specdec_stream", "specdec_forward_logits",
            "specdec_philox_uniforms", "specdec_last_launch_count", "specdec_forward_logits_noalloc",
            "specdec_time_linear", "specdec_generate_tree", "specdec_generate_tree_device", "specdec_tp_unique_id",
-           "specdec_create_tp", "specdec_generate_ar", "specdec_generate_ar_device", "specdec_load_netw")
+           "specdec_create_tp", "specdec_generate_ar", "specdec_generate_ar_device", "specdec_load_netw",
+           "specdec_prefill", "specdec_prefill_device", "specdec_step", "specdec_step_device",
+           "specdec_session_tokens")
 
 # linear layers of specdec_time_linear
 LIN_QKV, LIN_OPROJ, LIN_FFN_IN, LIN_FFN_OUT, LIN_HEAD = 0, 1, 2, 3, 4
@@ -93,6 +95,11 @@ def load_library(path: str = LIB_PATH):
     lib.specdec_generate_device.argtypes = [C.c_void_p, C.POINTER(_GenParams), C.c_void_p, C.c_int, C.c_int,
                                             C.c_void_p, C.c_void_p]
     lib.specdec_load_netw.argtypes = [C.c_void_p, C.c_int, C.c_char_p]
+    lib.specdec_prefill.argtypes = [C.c_void_p, C.POINTER(_GenParams), C.c_void_p, C.c_int, C.c_int]
+    lib.specdec_prefill_device.argtypes = lib.specdec_prefill.argtypes
+    lib.specdec_step.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]
+    lib.specdec_step_device.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
+    lib.specdec_session_tokens.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p]
     lib.specdec_generate_ar.argtypes = lib.specdec_generate.argtypes
     lib.specdec_generate_ar_device.argtypes = lib.specdec_generate_device.argtypes
     lib.specdec_stream.restype = C.c_void_p
@@ -100,7 +107,7 @@ def load_library(path: str = LIB_PATH):
     lib.specdec_forward_logits.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p]
     lib.specdec_philox_uniforms.argtypes = [C.c_uint64, C.c_int, C.c_int, C.c_int, C.c_void_p]
     lib.specdec_forward_logits_noalloc.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p,
-                                                   C.c_void_p]
+                                                   C.c_void_p, C.c_void_p]
     lib.specdec_last_launch_count.restype = C.c_int64
     lib.specdec_last_launch_count.argtypes = [C.c_void_p]
     lib.specdec_generate_tree.argtypes = [C.c_void_p, C.POINTER(_GenParams), C.POINTER(_Tree), C.c_void_p, C.c_int,
@@ -216,6 +223,54 @@ class Engine:
         del keep
         return out.astype(np.int64), stats
 
+    # -- round-level session (specdec_prefill / specdec_step) ---------------
+    def prefill(self, prompts, max_new_tokens: int, lookahead: int = 4, temperature: float = 1.0, top_k: int = 0,
+                top_p: float = 1.0, seed: int = 42, uniforms: Optional[np.ndarray] = None,
+                draft_catchup: int = CATCHUP_REF) -> None:
+        """Opens a session: prefill of target and draft and the first token for
+        prompts [B, S] (generate_speculative up to its round loop)."""
+        p = np.ascontiguousarray(np.atleast_2d(prompts), np.int32)
+        B, S = p.shape
+        prm, keep = self._params(max_new_tokens, lookahead, temperature, top_k, top_p, seed, uniforms, draft_catchup)
+        self._session = (B, S, lookahead, max_new_tokens)
+        self._check(self._lib.specdec_prefill(self.h, C.byref(prm), p.ctypes.data, B, S))
+        del keep
+
+    def prefill_device(self, d_prompts: int, B: int, S: int, max_new_tokens: int, lookahead: int = 4,
+                       temperature: float = 1.0, seed: int = 42, uniforms=None,
+                       draft_catchup: int = CATCHUP_REF) -> None:
+        """Device-pointer variant of prefill, enqueued on `stream`."""
+        prm, keep = self._params(max_new_tokens, lookahead, temperature, 0, 1.0, seed, uniforms, draft_catchup)
+        self._session = (B, S, lookahead, max_new_tokens)
+        self._check(self._lib.specdec_prefill_device(self.h, C.byref(prm), C.c_void_p(d_prompts), B, S))
+        del keep
+
+    def step(self, rounds: int = 1, uniforms: Optional[np.ndarray] = None):
+        """Up to `rounds` speculative rounds; returns (tokens [B, rounds*(k+1)],
+        counts [B]): request b emitted tokens[b, :counts[b]] in this call.
+        `uniforms` [B, rounds, 2k+1] replace the session table's rows of these rounds."""
+        B, _, k, _ = self._session
+        out = np.zeros((B, rounds * (k + 1)), np.int32)
+        cnt = np.zeros(B, np.int32)
+        u = None if uniforms is None else np.ascontiguousarray(uniforms, np.float32)
+        self._check(self._lib.specdec_step(self.h, rounds, None if u is None else u.ctypes.data, out.ctypes.data,
+                                           cnt.ctypes.data))
+        return out, cnt
+
+    def step_device(self, rounds: int, d_out: int, d_counts: int, cap: int, uniforms_ptr: int = 0) -> None:
+        """Device-pointer variant of step (d_out [B][cap] int32, d_counts [B] int32),
+        enqueued on `stream`; uniforms_ptr is a host or device [B][rounds][2k+1] table or 0."""
+        self._check(self._lib.specdec_step_device(self.h, rounds, C.c_void_p(uniforms_ptr or None),
+                                                  C.c_void_p(d_out), C.c_void_p(d_counts), cap))
+
+    def session_tokens(self) -> Tuple[np.ndarray, np.ndarray]:
+        """The open session's sequences [B, S + max(1, max_new)] and stats [B, 4]."""
+        B, S, _, max_new = self._session
+        out = np.zeros((B, S + max(1, max_new)), np.int32)
+        stats = np.zeros((B, 4), np.int64)
+        self._check(self._lib.specdec_session_tokens(self.h, out.ctypes.data, stats.ctypes.data))
+        return out.astype(np.int64), stats
+
     def generate_tree(self, prompts, max_new_tokens: int, branching, temperature: float = 1.0, top_k: int = 0,
                       top_p: float = 1.0, seed: int = 42,
                       uniforms: Optional[np.ndarray] = None) -> Tuple[np.ndarray, np.ndarray]:
@@ -288,14 +343,17 @@ class Engine:
         self._check(self._lib.specdec_forward_logits(self.h, role, t.ctypes.data, t.size, out.ctypes.data))
         return out
 
-    def forward_logits_noalloc(self, role: int, d_tokens: int, S: int, d_logits: int, stream: int = 0) -> None:
+    def forward_logits_noalloc(self, role: int, d_tokens: int, S: int, d_logits: int, stream: int = 0,
+                               d_status: int = 0) -> None:
         """Device-buffer forward that allocates nothing (see include/specdec.h).
 
         For callers that may not allocate device memory at call time; all
         working memory comes from the library's fixed 8 MiB device array, so
-        overlapping calls on one device must be serialised by the caller."""
+        overlapping calls on one device must be serialised by the caller.
+        d_status (a device int32, optional) receives the device-side error bits."""
         self._check(self._lib.specdec_forward_logits_noalloc(self.h, role, C.c_void_p(d_tokens), S,
-                                                             C.c_void_p(d_logits), C.c_void_p(stream or None)))
+                                                             C.c_void_p(d_logits), C.c_void_p(stream or None),
+                                                             C.c_void_p(d_status or None)))
 
     @property
     def stream(self) -> int:

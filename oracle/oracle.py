@@ -21,7 +21,16 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF_SO = os.path.join(HERE, "_ref", "libnnref.so")
 ORACLE_SO = os.path.join(HERE, "_build", "liboracle.so")
-REFERENCE_TREE = "/root/reference"
+
+
+def reference_tree() -> str:
+    """The reference source tree used to compile oracle/_ref: $NN_REFERENCE_SRC,
+    else a `reference` checkout beside this repository ("" when neither exists)."""
+    env = os.environ.get("NN_REFERENCE_SRC", "")
+    if env:
+        return env if os.path.isdir(env) else ""
+    sib = os.path.normpath(os.path.join(HERE, "..", "..", "reference"))
+    return sib if os.path.isdir(os.path.join(sib, "src", "nn")) else ""
 
 _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 _i64p = np.ctypeslib.ndpointer(np.int64, flags="C_CONTIGUOUS")
@@ -34,8 +43,9 @@ _i8p = np.ctypeslib.ndpointer(np.int8, flags="C_CONTIGUOUS")
 def build(ref: bool = True) -> None:
     """Compile the restatement (and the reference shim when its sources exist)."""
     targets = ["oracle"]
-    if ref and os.path.isdir(REFERENCE_TREE):
-        targets.append("ref")
+    tree = reference_tree() if ref else ""
+    if tree:
+        targets += ["ref", f"REF={tree}"]
     subprocess.run(["make", "-s", "-C", HERE] + targets, check=True)
 
 
