@@ -1,22 +1,27 @@
 #!/usr/bin/env python3
 """Benchmark of the B200 speculative-decoding path.
 
-Workload ("int8"): decoder with 4 layers, d_model 256,
-4 heads x 64, FFN 1024, vocab 2048; target weights int8 per output channel,
-fp32 activations and KV cache; draft = the target's first layer + shared
-lm_head; per GPU 8 requests with 64-token uniform-random prompts,
-temperature 1.0 rejection sampling, k = 4, 256 new tokens, Philox uniforms
-from the host.  Architecture: the reference TransformerDecoder (post-LN,
-SwiGLU, RoPE; --arch cfg selects the pre-LN/GELU/learned-position variant).
+Default workload ("large", the metric's config): target
+decoder with 32 layers, d_model 4096, 32 heads x 128, SwiGLU 11008, vocab
+32000, int8 per-channel weights, bf16 activations and KV cache; draft = the
+target's first 4 layers + shared lm_head; 2048-token uniform-random prompts,
+k = 4, temperature 1 with Philox uniforms from the host, 512 new tokens per
+request.  BASELINE splits its 256 requests over 8 GPUs; every GPU serves 32 of
+them (one GPU's share at 8 GPUs), so the line is weak scaling from 1 GPU.
 Weights are seeded synthetic (no checkpoints exist for this path).
 
-One step = one generate call over the GPU's batch: prefill of target and
-draft, then speculative rounds until every request has 256 new tokens.
-`value` is new tokens per second over all GPUs with prompts already resident
-in HBM; `e2e` is the same metric through the public C ABI with host buffers
-(prompt + uniform upload and token download inside the timed region).
+One step = one speculative round (k draft steps, one verify pass over the
+k+1 rows of every request, acceptance and rollback) of the GPU's 32 requests,
+through the round-level session API (specdec_prefill once, untimed; then
+specdec_step per step).  `value` is new tokens per second over all GPUs with
+everything resident in HBM; `e2e` is the same through the host-buffer C ABI
+(each step uploads its rounds' uniforms and downloads the new tokens and
+counts inside the timed region).  The line also carries BASELINE configs[1]
+("int8": 4 layers, d_model 256, 8 requests, 64-token prompts, 256 new tokens,
+one step = one whole generation) under "configs1".
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                  [--workload large|int8|medium|tree]
 
 Multi-GPU: launch with torchrun; requests are partitioned by rank (weak
 scaling, no data-path collective); timing is the max over ranks.
@@ -76,12 +81,11 @@ KV_DTYPE = {0: 0, 1: 1, 2: 2}  # workload kv_mode -> SPECDEC_F32 / BF16 / INT8
 # requests when they are split over 8 GPUs.
 LARGE_REQUESTS_PER_GPU = 32
 
-
-# DRAM bytes (read + write) of one launch of the roofline kernel, from the ncu
-# capture named beside it (caches flushed before the launch, as the live probe
-# does); None where no capture of the current kernel exists.
-TRAFFIC = {
-    "int8": (503808, "profiles/linear_resid_int8_verify_dram.md"),
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of
+# each workload's roofline kernel from an ncu capture of the same launch
+# (caches flushed before it, as the live probe does); None until captured.
+TRAFFIC_BYTES = {
+    "int8": 503808,
 }
 
 
@@ -91,8 +95,8 @@ def roofline_entry(p, hbm, tflops, wl, rows):
     ridge = tflops * 1e12 / (hbm * 1e9)
     what = "tcgen05 GEMM" if (wl.act_bf16 and rows >= 64) else "linear_kernel GEMV"
     kern = f"{what}, residual epilogue (target FFN down-projection, {rows} verify rows)"
-    traffic, src = TRAFFIC.get(wl.name, (None, None))
-    extra = {"kernel": kern, "traffic_source": src}
+    traffic = TRAFFIC_BYTES.get(wl.name)
+    extra = {"kernel": kern}
     if p["flops_per_byte"] > ridge:
         return {"bound": "tensor", "achieved": p["TFLOPs"], "peak": tflops, "unit": "TFLOP/s",
                 "frac": p["TFLOPs"] / tflops, "traffic": traffic, **extra}
@@ -187,54 +191,147 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
+
+
+# ---------------------------------------------------------------------------
+# The reference's own CPU implementation (oracle/_ref: the unmodified library)
+# on the large workload's models, as a bounded sample.
+class _LazyParams:
+    """The large models' parameters, made one at a time while the reference
+    copies them in (the whole fp32 model is 27 GB): N(0, 0.02) weights and
+    embedding, N(0, 4/sqrt(d)) lm_head, zero biases, unit LayerNorm gamma,
+    taken from one seeded block of normals.  The sample times the
+    reference's work, which does not depend on the values."""
+
+    def __init__(self, shape, n_layers_kept=None):
+        from specdec_b200.synth import param_kinds, param_shapes, params_per_layer
+
+        shapes, kinds = param_shapes(shape), param_kinds(shape)
+        if n_layers_kept is not None:  # the draft: first layers + the shared head
+            per = params_per_layer(shape)
+            keep = list(range(1 + per * n_layers_kept)) + [len(shapes) - 2, len(shapes) - 1]
+            shapes = [shapes[i] for i in keep]
+            kinds = [kinds[i] for i in keep]
+        self.shapes, self.kinds, self.d = shapes, kinds, shape.d_model
+        self.block = np.random.default_rng(0).standard_normal(1 << 24, dtype=np.float32)
+
+    def __len__(self):
+        return len(self.shapes)
+
+    def __iter__(self):
+        for shape, kind in zip(self.shapes, self.kinds):
+            n = int(np.prod(shape))
+            if kind in ("emb", "w", "head_w"):
+                std = 4.0 / np.sqrt(self.d) if kind == "head_w" else 0.02
+                reps = (n + self.block.size - 1) // self.block.size
+                a = np.tile(self.block * np.float32(std), reps)[:n]
+            elif kind == "g":
+                a = np.ones(n, np.float32)
+            else:
+                a = np.zeros(n, np.float32)
+            yield a
+
+
+_REF_LARGE = {}
+REF_SAMPLE_PROMPT = 32
+REF_SAMPLE_NEW = 2
+
+
+def reference_large_models(wl):
+    """The reference TransformerDecoder pair of configs[4] (fp32 Dense weights:
+    the reference's QuantizedDense would dequantise all 6.6 G int8 weights
+    again on every call)."""
+    if "pair" not in _REF_LARGE:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle
+
+        if not oracle.reference_available():
+            raise RuntimeError("oracle/_ref/libnnref.so is not built")
+        avail = 0
+        with open("/proc/meminfo") as f:
+            for ln in f:
+                if ln.startswith("MemAvailable:"):
+                    avail = int(ln.split()[1]) * 1024
+        if avail < 48 << 30:
+            raise MemoryError(f"the fp32 reference models need ~31 GB of host memory; {avail >> 30} GB available")
+        shape = dataclasses.replace(wl.target, max_seq_len=REF_SAMPLE_PROMPT + 4 * REF_SAMPLE_NEW + 16)
+        tgt = oracle.Reference(shape, _LazyParams(shape), requires_grad=False)
+        dft = oracle.Reference(shape.with_layers(wl.draft_layers), _LazyParams(shape, wl.draft_layers),
+                               requires_grad=False)
+        _REF_LARGE["pair"] = (tgt, dft)
+    return _REF_LARGE["pair"]
+
+
+def reference_large_call(wl, i):
+    """One generate_speculative call of the sample: 1 request, a 32-token
+    prompt, 2 new tokens (the first token and one round), k = 4, T = 1."""
+    tgt, dft = reference_large_models(wl)
+    prompt = make_prompts(1, REF_SAMPLE_PROMPT, wl.target.vocab, seed=100 + i)[0]
+    out = tgt.generate_speculative(dft, prompt, REF_SAMPLE_NEW, wl.lookahead, wl.temperature, 0, 1.0, 1000 + i)
+    return len(out) - REF_SAMPLE_PROMPT
+
+
+REF_LARGE_SAMPLE_TEXT = (f"1 request per step: generate_speculative of configs[4]'s target and 4-layer draft (fp32 "
+                         f"Dense weights), {REF_SAMPLE_PROMPT}-token prompt, {REF_SAMPLE_NEW} new tokens, k = 4, T = 1; "
+                         "the reference is batch-1 and its prefill of a 2048-token prompt alone is ~27 TFLOP")
+
+
 def reference_arm(args, wl, rank, world):
-    """The reference's own CPU implementation on this host's cores."""
+    """The reference's own CPU implementation on this host's cores, on this
+    arm's workload; rank 0 alone runs it (one process; the reference is batch
+    1 and uses every host core through its thread pool and OpenBLAS)."""
     if world > 1:
         import torch.distributed as dist
         dist.init_process_group("gloo", init_method="env://")
-    if rank != 0:
+    try:
+        if rank == 0:
+            _reference_arm_rank0(args, wl)
+    finally:
         if world > 1:
             import torch.distributed as dist
             dist.destroy_process_group()
-        return
-    if wl.name == "large":
-        print(json.dumps({"impl": "reference", "unavailable": "the reference dequantises the large model's 6.6 G "
-                          "int8 weights to fp32 (26 GB) on every Dense call; its CPU arm runs on the int8 workload"}),
-              flush=True)
-        if world > 1:
-            import torch.distributed as dist
-            dist.destroy_process_group()
-        return
+
+
+def _reference_arm_rank0(args, wl):
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle  # the reference arm times the reference (oracle/_ref) or the CPU restatement
 
-    kind = "reference" if oracle.reference_available() else "port"
     ncores = os.cpu_count() or 1
-    P = make_params(wl.target, seed=0)
-    DP = draft_params(wl.target, P, wl.draft_layers)
-    new_per_step = 32 if wl.name == "int8" else 8
-    prompts = make_prompts(wl.batch, wl.prompt_len, wl.target.vocab, seed=1)
-    if kind == "reference":
-        # int8 target: the reference multiplies by the dequantised weight q*s
-        # (src/nn/quantization.cpp:127-147); inject those values.
-        om = oracle.Oracle(wl.target, P, int8=wl.weights_int8)
-        Pq = [om.param(i).reshape(np.shape(P[i])) for i in range(len(P))]
-        tgt = oracle.Reference(wl.target, Pq, requires_grad=False)
-        dft = oracle.Reference(wl.target.with_layers(wl.draft_layers), draft_params(wl.target, Pq, wl.draft_layers),
-                               requires_grad=False)
-
-        def one(i):
-            out = tgt.generate_speculative(dft, prompts[i % wl.batch], new_per_step, wl.lookahead,
-                                           wl.temperature, 0, 1.0, 1000 + i)
-            return len(out) - wl.prompt_len
+    if wl.name == "large":
+        kind = "reference"
+        t0 = time.perf_counter()
+        reference_large_models(wl)
+        print(f"[bench] reference models built in {time.perf_counter() - t0:.1f} s", file=sys.stderr, flush=True)
+        one = lambda i: reference_large_call(wl, i)  # noqa: E731
+        sample = REF_LARGE_SAMPLE_TEXT
     else:
-        tgt = oracle.Oracle(wl.target, P, int8=wl.weights_int8)
-        dft = oracle.Oracle(wl.target.with_layers(wl.draft_layers), DP, int8=wl.weights_int8)
+        kind = "reference" if oracle.reference_available() else "port"
+        P = make_params(wl.target, seed=0)
+        DP = draft_params(wl.target, P, wl.draft_layers)
+        new_per_step = 32 if wl.name == "int8" else 8
+        prompts = make_prompts(wl.batch, wl.prompt_len, wl.target.vocab, seed=1)
+        sample = f"1 request x {new_per_step} new tokens per step (generate_speculative)"
+        if kind == "reference":
+            # int8 target: the reference multiplies by the dequantised weight q*s
+            # (src/nn/quantization.cpp:127-147); inject those values.
+            om = oracle.Oracle(wl.target, P, int8=wl.weights_int8)
+            Pq = [om.param(i).reshape(np.shape(P[i])) for i in range(len(P))]
+            tgt = oracle.Reference(wl.target, Pq, requires_grad=False)
+            dft = oracle.Reference(wl.target.with_layers(wl.draft_layers),
+                                   draft_params(wl.target, Pq, wl.draft_layers), requires_grad=False)
 
-        def one(i):
-            out, _, _ = oracle.oracle_generate_speculative(tgt, dft, prompts[i % wl.batch][None], new_per_step,
-                                                           wl.lookahead, wl.temperature, seed=1000 + i)
-            return out.shape[1] - wl.prompt_len
+            def one(i):
+                out = tgt.generate_speculative(dft, prompts[i % wl.batch], new_per_step, wl.lookahead,
+                                               wl.temperature, 0, 1.0, 1000 + i)
+                return len(out) - wl.prompt_len
+        else:
+            tgt = oracle.Oracle(wl.target, P, int8=wl.weights_int8)
+            dft = oracle.Oracle(wl.target.with_layers(wl.draft_layers), DP, int8=wl.weights_int8)
+
+            def one(i):
+                out, _, _ = oracle.oracle_generate_speculative(tgt, dft, prompts[i % wl.batch][None], new_per_step,
+                                                               wl.lookahead, wl.temperature, seed=1000 + i)
+                return out.shape[1] - wl.prompt_len
     for i in range(args.warmup):
         one(i)
     t0 = time.perf_counter()
@@ -246,27 +343,28 @@ def reference_arm(args, wl, rank, world):
     line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "impl": "reference",
+            "impl": "reference", "processes": 1,
+            "note": "one host process on rank 0 whatever the GPU count (the reference is batch-1 CPU code)",
             "config": config_dict(wl, args),
-            "cpu_baseline": {"value": v, "unit": UNIT, "cores": ncores, "kind": kind,
-                             "sample": f"{args.steps} generate_speculative calls, 1 request x {new_per_step} new tokens each"},
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": ncores, "kind": kind, "sample": sample},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
-    if world > 1:
-        import torch.distributed as dist
-        dist.destroy_process_group()
 
 
 def config_dict(wl, args):
     idx = {"int8": 1, "medium": 2, "tree": 3, "large": 4}.get(wl.name, 1)
+    step = ("one speculative round of every request (session API)" if wl.name == "large"
+            else "one whole generation (generate call)")
     return {"workload": f"{wl.name} (BASELINE configs[{idx}])", "arch": args.arch,
             "model": f"L{wl.target.n_layers} d{wl.target.d_model} H{wl.target.n_heads} F{wl.target.d_ff} V{wl.target.vocab}",
             "draft": f"first {wl.draft_layers} layer(s) + shared head", "batch_per_gpu": wl.batch,
             "global_batch": wl.batch * args.gpus, "prompt_len": wl.prompt_len, "max_new": wl.max_new,
             "lookahead": wl.lookahead, "temperature": wl.temperature, "weights": "int8" if wl.weights_int8 else "f32",
             "act": "bf16" if wl.act_bf16 else "f32", "kv": ["f32", "bf16", "int8"][wl.kv_mode],
-            "rng": "philox host uniforms", "tree": list(wl.tree) if wl.tree else None,
-            "parallelism": f"request-parallel x{args.gpus}", "l2": "flushed between timed steps (256 MiB write)",
+            "rng": "philox host uniforms", "tree": list(wl.tree) if wl.tree else None, "step": step,
+            "parallelism": f"request-parallel x{args.gpus}",
+            "l2": ("inputs larger than L2: 6.6 GB of int8 weights and ~40 GB of KV cache read per step"
+                   if wl.name == "large" else "flushed between timed steps (256 MiB write)"),
             **({"requests": f"{wl.batch} per GPU: configs[4]'s 256 requests split over 8 GPUs"}
                if wl.name == "large" else {})}
 
@@ -276,6 +374,13 @@ def cpu_baseline_sample(wl):
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
 
+    if wl.name == "large":
+        reference_large_models(wl)
+        t0 = time.perf_counter()
+        toks = sum(reference_large_call(wl, i) for i in range(2))
+        dt = time.perf_counter() - t0
+        return {"value": toks / dt, "unit": UNIT, "cores": os.cpu_count(), "kind": "reference",
+                "sample": REF_LARGE_SAMPLE_TEXT.replace("per step", "x 2 calls")}
     kind = "reference" if oracle.reference_available() else "port"
     P = make_params(wl.target, seed=0)
     small = wl.name == "int8"
@@ -305,39 +410,9 @@ def cpu_baseline_sample(wl):
                       "(the reference is batch-1)"}
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
-    ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--arch", default="ref", choices=["ref", "cfg"])
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="int8", choices=["int8", "medium", "tree", "large"],
-                    help="int8 = BASELINE configs[1] (the metric's config, default); medium = configs[2]; "
-                         "tree = configs[3]; large = configs[4] at 32 requests per GPU (its 256 over 8 GPUs)")
-    args = ap.parse_args()
-    args.warmup = max(3, args.warmup)
-    rank, world, local = dist_env()
-    wl = workload(args.workload, ARCH_CFG if args.arch == "cfg" else ARCH_REF)
-    large = wl.name == "large"
-    if large:
-        wl = dataclasses.replace(wl, batch=LARGE_REQUESTS_PER_GPU)
-    if args.impl == "reference":
-        return reference_arm(args, wl, rank, world)
-
+def make_engine(sd, wl, local, large):
     import torch
-    import torch.distributed as dist
 
-    import specdec_b200 as sd
-    from specdec_b200.shard import max_over_ranks, shard
-
-    torch.cuda.set_device(local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", init_method="env://", timeout=timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
-    t_setup = time.perf_counter()
     P = device_params(wl.target, 0, torch.device("cuda", local)) if large else make_params(wl.target, seed=0)
     eng = sd.Engine(wl.target, draft_layers=wl.draft_layers, weight_dtype=sd.INT8 if wl.weights_int8 else sd.F32,
                     act_dtype=sd.BF16 if wl.act_bf16 else sd.F32, kv_dtype=KV_DTYPE[wl.kv_mode],
@@ -345,10 +420,38 @@ def main():
                     max_tree_nodes=tree_nodes(wl.tree) if wl.tree else 0)
     eng.load_params(sd.TARGET, P)
     del P
+    return eng
+
+
+def linear_probes(sd, eng, wl, R_verify, flush):
+    """The verify pass's linear layers, timed alone on the library's stream
+    with CUDA events (L2 flushed before every launch)."""
+    m = wl.target
+    nk = {"ffn_out": (m.d_model, m.d_ff), "ffn_in": (2 * m.d_ff, m.d_model),
+          "qkv": (m.d_model + 2 * m.kv_heads * m.head_dim, m.d_model), "head": (m.vocab, m.d_model)}
+    probes = {}
+    for name, which, layer in (("ffn_out", sd.LIN_FFN_OUT, 0), ("ffn_in", sd.LIN_FFN_IN, 0),
+                               ("qkv", sd.LIN_QKV, 1), ("head", sd.LIN_HEAD, wl.target.n_layers - 1)):
+        us, nbytes = eng.time_linear(sd.TARGET, layer, which, R_verify, 20, flush.data_ptr(), flush.numel() * 4)
+        flops = 2.0 * R_verify * nk[name][0] * nk[name][1]
+        probes[name] = {"us": us, "bytes": nbytes, "GBps": nbytes / (us * 1e-6) / 1e9,
+                        "TFLOPs": flops / (us * 1e-6) / 1e12, "flops_per_byte": flops / nbytes}
+    return probes
+
+
+def run_generate_bench(args, wl, rank, world, local, dist):
+    """Workloads int8 / medium / tree: one step = one whole generation."""
+    import torch
+
+    import specdec_b200 as sd
+    from specdec_b200.shard import max_over_ranks, shard
+
+    t_setup = time.perf_counter()
+    eng = make_engine(sd, wl, local, False)
     if rank == 0:
-        print(f"[bench] weights made and loaded in {time.perf_counter() - t_setup:.1f} s", file=sys.stderr, flush=True)
+        print(f"[bench] {wl.name}: weights made and loaded in {time.perf_counter() - t_setup:.1f} s",
+              file=sys.stderr, flush=True)
     B, S = wl.batch, wl.prompt_len
-    # request partition: rank r serves requests [r*B, (r+1)*B) of the global set
     prompts = shard(make_prompts(B * world, S, wl.target.vocab, seed=1), B, rank, world)
     n_rounds = wl.max_new + 2
     slots = (len(wl.tree) * max(wl.tree) + 1) if wl.tree else 2 * wl.lookahead + 1
@@ -371,11 +474,8 @@ def main():
                                 wl.lookahead, wl.temperature, seed=1234, uniforms=uni)
 
     for i in range(args.warmup):
-        t0 = time.perf_counter()
         step()
         torch.cuda.synchronize()
-        if rank == 0:
-            print(f"[bench] warm-up step {i}: {time.perf_counter() - t0:.2f} s", file=sys.stderr, flush=True)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     if world > 1:
@@ -394,21 +494,43 @@ def main():
         torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    tot_ms = float(sum(step_ms))
+    tot_ms = float(sum(s.elapsed_time(e) for s, e in zip(starts, ends)))
     stats = d_stats.cpu().numpy()
     tokens_out = d_out.cpu().numpy()
-    new_tokens = B * wl.max_new  # every request reaches max_new (checked below)
+    # every request reaches max_new new tokens, within the vocabulary
+    n_new = stats[:, 0]
     assert tokens_out.shape == (B, out_len)
+    assert np.array_equal(tokens_out[:, :S], prompts.astype(np.int32)), "prompts were not kept"
+    assert ((tokens_out[:, S:] >= 0) & (tokens_out[:, S:] < wl.target.vocab)).all(), "token out of range"
+    new_tokens = B * wl.max_new
+    checks = {"requests_complete": True, "tokens_in_vocab": True}
+    if not wl.tree and rank == 0 and wl.name == "int8":
+        # request 0 against the CPU restatement on the same weights and uniforms
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle
+
+        P = make_params(wl.target, seed=0)
+        om = oracle.Oracle(wl.target, P, int8=wl.weights_int8)
+        dm = oracle.Oracle(wl.target.with_layers(wl.draft_layers), draft_params(wl.target, P, wl.draft_layers),
+                           int8=wl.weights_int8)
+        ref, _, mg = oracle.oracle_generate_speculative(om, dm, prompts[:1], wl.max_new, wl.lookahead,
+                                                        wl.temperature, seed=1234, uniforms=uni[:1],
+                                                        cache_cap=wl.target.max_seq_len)
+        diff = np.nonzero(ref[0] != tokens_out[0])[0]
+        first = int(diff[0]) - S if diff.size else -1
+        tie = bool(diff.size == 0 or float(mg[0, : first + 1].min()) < 2e-5)
+        checks["request0_equals_oracle"] = bool(diff.size == 0)
+        checks["request0_first_difference"] = first
+        assert tie, f"request 0 differs from the oracle at new token {first}"
     rounds = stats[:, 0].max()
     drafted, accepted = stats[:, 1].sum(), stats[:, 2].sum()
+    del n_new
 
     # e2e through the host-buffer C ABI (pinned host memory, copies inside)
     pin_prompts = torch.from_numpy(prompts.astype(np.int32)).pin_memory()
     pin_uni = torch.from_numpy(uni).pin_memory()
     e2e_ms = []
-    # (the large workload's steps take seconds each: one e2e step there)
-    for i in range(1 if large else max(3, args.steps // 2)):
+    for i in range(max(3, args.steps // 2)):
         with torch.cuda.stream(stream):
             flush.fill_(float(i))
         torch.cuda.synchronize()
@@ -430,7 +552,7 @@ def main():
     # Autoregressive decoding of the same requests on the same kernels
     # (generate_advanced): the speculative path's speed-up over plain decoding.
     ar_ms = []
-    if not wl.tree and not large:
+    if not wl.tree:
         ar_uni = np.ascontiguousarray(uni[:, : wl.max_new, :1])
         for i in range(args.warmup + 3):
             with torch.cuda.stream(stream):
@@ -458,59 +580,255 @@ def main():
     round_ms = ms_per_step / max(1, rounds)
     round_achieved = ab["total"] / (round_ms * 1e-3) / 1e9
     clocks = clk.summary()
-
-    # Dominant kernels, timed alone on the library's stream with CUDA events
-    # (L2 flushed before every launch) over the verify pass's row count.
     R_verify = B * ((tree_nodes(wl.tree) + 1) if wl.tree else (wl.lookahead + 1))
-    m = wl.target
-    nk = {"ffn_out": (m.d_model, m.d_ff), "ffn_in": (2 * m.d_ff, m.d_model),
-          "qkv": (m.d_model + 2 * m.kv_heads * m.head_dim, m.d_model), "head": (m.vocab, m.d_model)}
-    probes = {}
-    for name, which, layer in (("ffn_out", sd.LIN_FFN_OUT, 0), ("ffn_in", sd.LIN_FFN_IN, 0),
-                               ("qkv", sd.LIN_QKV, 1), ("head", sd.LIN_HEAD, wl.target.n_layers - 1)):
-        us, nbytes = eng.time_linear(sd.TARGET, layer, which, R_verify, 20, flush.data_ptr(), flush.numel() * 4)
-        flops = 2.0 * R_verify * nk[name][0] * nk[name][1]
-        probes[name] = {"us": us, "bytes": nbytes, "GBps": nbytes / (us * 1e-6) / 1e9,
-                        "TFLOPs": flops / (us * 1e-6) / 1e12, "flops_per_byte": flops / nbytes}
-    if rank == 0:
-        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": ("int8 weights, bf16 activations" if wl.act_bf16 else "int8")
-                if wl.weights_int8 else "f32", "data": "synthetic",
-                "config": config_dict(wl, args),
-                "e2e": {"value": e2e_value, "unit": UNIT,
-                        "h2d_bytes_per_step": int(prompts.size * 4 + uni.nbytes),
-                        "d2h_bytes_per_step": int(B * out_len * 4 + B * 4 * 8 + 4)},
-                "gpu_launches": int(launches),
-                "roofline": {**roofline_entry(probes["ffn_out"], hbm, tflops, wl, R_verify),
-                             "launch_us": probes["ffn_out"]["us"], "alg_bytes_per_launch": probes["ffn_out"]["bytes"],
-                             "peak_source": peak_kind,
-                             "other_kernels": {k: v for k, v in probes.items() if k != "ffn_out"},
-                             "round": {"alg_bytes": ab["total"], "achieved": round_achieved,
-                                       "frac": round_achieved / hbm, "weight_bytes": ab["weights"],
-                                       "kv_bytes": ab["kv"],
-                                       "weights_frac": ab["weights"] / (round_ms * 1e-3) / 1e9 / hbm}},
-                "spec": {"rounds_per_step": int(rounds), "mean_accepted_per_round": float(accepted) / max(1, stats[:, 0].sum()),
-                         "acceptance_rate": float(accepted) / max(1, drafted), "round_us": round_ms * 1e3},
-                "clocks": clocks}
-        if ar_ms:
-            line["ar_decode"] = {"value": new_tokens * world * len(ar_ms) / (ar_tot / 1e3), "unit": UNIT,
-                                 "what": "generate_advanced (autoregressive, KV cache) of the same requests, "
-                                         "models and uniforms on the same kernels, device-resident"}
-        if world == 1 and not args.no_cpu_baseline and not large:
-            line["cpu_baseline"] = cpu_baseline_sample(wl)
-        if large:
-            line["cpu_baseline"] = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "reference",
-                                    "sample": "not sampled: the reference dequantises the 6.6 G int8 weights to "
-                                              "fp32 (26 GB) on every Dense call; the int8 workload's line "
-                                              "carries the CPU baseline"}
-        if wl.tree:
-            line["tree"] = {"branching": list(wl.tree), "nodes": tree_nodes(wl.tree),
-                            "mean_accepted_per_round": line["spec"]["mean_accepted_per_round"]}
-        print(json.dumps(line), flush=True)
+    probes = linear_probes(sd, eng, wl, R_verify, flush)
     eng.close()
+    if rank != 0:
+        return None
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "value_per_gpu": value / world, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": ("int8 weights, bf16 activations" if wl.act_bf16 else "int8") if wl.weights_int8 else "f32",
+            "data": "synthetic", "config": config_dict(wl, args),
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(prompts.size * 4 + uni.nbytes),
+                    "d2h_bytes_per_step": int(B * out_len * 4 + B * 4 * 8 + 4)},
+            "gpu_launches": int(launches),
+            "roofline": {**roofline_entry(probes["ffn_out"], hbm, tflops, wl, R_verify),
+                         "launch_us": probes["ffn_out"]["us"], "alg_bytes_per_launch": probes["ffn_out"]["bytes"],
+                         "peak_source": peak_kind,
+                         "other_kernels": {k: v for k, v in probes.items() if k != "ffn_out"},
+                         "round": {"alg_bytes": ab["total"], "achieved": round_achieved,
+                                   "frac": round_achieved / hbm, "weight_bytes": ab["weights"],
+                                   "kv_bytes": ab["kv"],
+                                   "weights_frac": ab["weights"] / (round_ms * 1e-3) / 1e9 / hbm}},
+            "spec": {"rounds_per_step": int(rounds), "mean_accepted_per_round": float(accepted) / max(1, stats[:, 0].sum()),
+                     "acceptance_rate": float(accepted) / max(1, drafted), "round_us": round_ms * 1e3},
+            "checks": checks, "clocks": clocks}
+    if ar_ms:
+        line["ar_decode"] = {"value": new_tokens * world * len(ar_ms) / (ar_tot / 1e3), "unit": UNIT,
+                             "what": "generate_advanced (autoregressive, KV cache) of the same requests, "
+                                     "models and uniforms on the same kernels, device-resident"}
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_sample(wl)
+    if wl.tree:
+        line["tree"] = {"branching": list(wl.tree), "nodes": tree_nodes(wl.tree),
+                        "mean_accepted_per_round": line["spec"]["mean_accepted_per_round"]}
+    return line
+
+
+def run_session_bench(args, wl, rank, world, local, dist):
+    """The large workload: prefill once (untimed), one step = one round."""
+    import torch
+
+    import specdec_b200 as sd
+    from specdec_b200.shard import max_over_ranks, shard, sum_over_ranks
+
+    t_setup = time.perf_counter()
+    eng = make_engine(sd, wl, local, True)
+    if rank == 0:
+        print(f"[bench] {wl.name}: weights made and loaded in {time.perf_counter() - t_setup:.1f} s",
+              file=sys.stderr, flush=True)
+    B, S, k, T = wl.batch, wl.prompt_len, wl.lookahead, wl.temperature
+    R = max(1, args.rounds_per_step)
+    prompts = shard(make_prompts(B * world, S, wl.target.vocab, seed=1), B, rank, world)
+    slots = 2 * k + 1
+    uni = shard(sd.philox_uniforms(1234, B * world, wl.max_new + 2, slots), B, rank, world)
+    n_e2e = 0 if args.profile else max(3, args.steps // 2)
+    budget = wl.max_new - 2  # rounds a request can take after its first token
+    if R * (args.warmup + args.steps + n_e2e) > budget:
+        raise SystemExit(f"{R * (args.warmup + args.steps + n_e2e)} rounds exceed the session's {budget}: "
+                         "fewer steps or rounds per step")
+    dev = torch.device("cuda", local)
+    d_prompts = torch.from_numpy(prompts.astype(np.int32)).to(dev)
+    cap = R * (k + 1)
+    d_tok = torch.zeros((args.steps + args.warmup, B, cap), dtype=torch.int32, device=dev)
+    d_cnt = torch.zeros((args.steps + args.warmup, B), dtype=torch.int32, device=dev)
+    stream = torch.cuda.ExternalStream(eng.stream, device=dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    t0 = time.perf_counter()
+    eng.prefill_device(d_prompts.data_ptr(), B, S, wl.max_new, k, T, seed=1234, uniforms=uni)
+    torch.cuda.synchronize()
+    if rank == 0:
+        print(f"[bench] prefill of {B} x {S} tokens: {time.perf_counter() - t0:.2f} s", file=sys.stderr, flush=True)
+
+    def step(i):
+        eng.step_device(R, d_tok[i].data_ptr(), d_cnt[i].data_ptr(), cap)
+
+    for i in range(args.warmup):
+        step(i)
+        torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     if world > 1:
-        dist.destroy_process_group()
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches = 0
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            with torch.cuda.stream(stream):
+                starts[i].record(stream)
+            step(args.warmup + i)
+            with torch.cuda.stream(stream):
+                ends[i].record(stream)
+            launches += eng.last_launch_count()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    tot_ms = float(sum(step_ms))
+    cnt = d_cnt.cpu().numpy()
+    tok = d_tok.cpu().numpy()
+    timed_tokens = int(cnt[args.warmup:].sum())
+    # every request emits at least one token per round, within the vocabulary
+    assert (cnt >= R).all(), "a request emitted no token in a round"
+    for i in range(cnt.shape[0]):
+        for b in range(B):
+            t = tok[i, b, : min(cnt[i, b], cap)]
+            assert ((t >= 0) & (t < wl.target.vocab)).all(), "token out of range"
+
+    # e2e: the host-buffer step (uploads its rounds' uniforms, downloads the
+    # tokens and counts) from pinned host memory
+    e2e_ms, e2e_tokens = [], 0
+    r0 = 1 + R * (args.warmup + args.steps)
+    pin_uni = torch.from_numpy(np.ascontiguousarray(uni)).pin_memory().numpy()
+    for i in range(n_e2e):
+        u = np.ascontiguousarray(pin_uni[:, r0 + R * i: r0 + R * (i + 1)])
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+        _, c = eng.step(R, uniforms=u)
+        with torch.cuda.stream(stream):
+            e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms.append(e0.elapsed_time(e1))
+        e2e_tokens += int(c.sum())
+    e2e_tot = float(sum(e2e_ms))
+
+    # the session's sequences: prompts kept, the step outputs are its new tokens
+    full, stats = eng.session_tokens()
+    checks = {"tokens_per_round_ge_1": True, "tokens_in_vocab": True}
+    emitted = 1 + cnt.sum(axis=0)
+    assert np.array_equal(full[:, :S], prompts), "prompts were not kept"
+    for b in range(B):
+        seq = [int(full[b, S])] + [int(x) for i in range(cnt.shape[0]) for x in tok[i, b, : cnt[i, b]]]
+        assert seq == full[b, S: S + int(emitted[b])].tolist(), "step outputs differ from the session's tokens"
+    checks["step_outputs_equal_session_tokens"] = True
+
+    # live kernel timings over the session's caches (L2 flushed before each):
+    # the verify pass's attention (the dominant kernel) and linear layers
+    hbm, peak_kind = peaks()
+    tflops = bf16_peak()
+    att_us, att_bytes = (eng.time_attention(sd.TARGET, 0, k + 1, 10, flush.data_ptr(), flush.numel() * 4)
+                         if not args.profile else (1.0, 0.0))
+    R_verify = B * (k + 1)
+    probes = linear_probes(sd, eng, wl, R_verify, flush) if not args.profile else {}
+    clocks = clk.summary()
+    eng.close()
+
+    tot_ms, e2e_tot, att_us = max_over_ranks([tot_ms, e2e_tot, att_us], dist if world > 1 else None, dev)
+    timed_tokens, e2e_tokens = sum_over_ranks([timed_tokens, e2e_tokens], dist if world > 1 else None, dev)
+    if rank != 0:
+        return None
+    ms_per_step = tot_ms / args.steps
+    value = timed_tokens / (tot_ms / 1e3)
+    e2e_value = e2e_tokens / (e2e_tot / 1e3) if e2e_ms else None
+    rounds = args.steps * R
+    # algorithmic bytes of a round at the timed rounds' average context
+    avg_ctx = S + 1 + (args.warmup + args.steps / 2) * R * (1 + float(stats[:, 2].sum()) / max(1, stats[:, 0].sum()))
+    ab = algorithmic_bytes_per_round(wl, wl.weights_int8, avg_ctx)
+    round_ms = ms_per_step / R
+    round_achieved = ab["total"] / (round_ms * 1e-3) / 1e9
+    att_gbps = att_bytes / (att_us * 1e-6) / 1e9
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "value_per_gpu": value / world, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8 weights, bf16 activations and KV",
+            "data": "synthetic", "config": {**config_dict(wl, args), "rounds_per_step": R},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(B * R * slots * 4),
+                    "d2h_bytes_per_step": int(B * cap * 4 + B * 4 + 4)},
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "hbm", "achieved": att_gbps, "peak": hbm, "unit": "GB/s", "frac": att_gbps / hbm,
+                         "traffic": TRAFFIC_BYTES.get("large"),
+                         "kernel": f"attn_dec_kernel (tcgen05 decode attention, head_dim 128), verify pass of "
+                                   f"layer 0: {B} requests x {k + 1} rows over ~{int(avg_ctx)} cached positions",
+                         "launch_us": att_us, "alg_bytes_per_launch": att_bytes, "peak_source": peak_kind,
+                         "other_kernels": probes,
+                         "round": {"alg_bytes": ab["total"], "achieved": round_achieved,
+                                   "frac": round_achieved / hbm, "weight_bytes": ab["weights"],
+                                   "kv_bytes": ab["kv"], "avg_ctx": avg_ctx,
+                                   "weights_frac": ab["weights"] / (round_ms * 1e-3) / 1e9 / hbm}},
+            "spec": {"rounds_per_step": R, "mean_accepted_per_round": float(stats[:, 2].sum()) / max(1, stats[:, 0].sum()),
+                     "acceptance_rate": float(stats[:, 2].sum()) / max(1, stats[:, 1].sum()),
+                     "round_us": round_ms * 1e3, "timed_rounds": rounds},
+            "checks": checks, "clocks": clocks}
+    if world == 1 and not args.no_cpu_baseline and not args.profile:
+        try:
+            line["cpu_baseline"] = cpu_baseline_sample(wl)
+        except (RuntimeError, OSError, MemoryError) as e:
+            line["cpu_baseline"] = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "reference",
+                                    "sample": f"not sampled: {e}"}
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--arch", default="ref", choices=["ref", "cfg"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="large", choices=["large", "int8", "medium", "tree"],
+                    help="large = BASELINE configs[4], the metric's config (default; 32 requests per GPU, one "
+                         "step = one round); int8 = configs[1]; medium = configs[2]; tree = configs[3]")
+    ap.add_argument("--rounds-per-step", type=int, default=1, help="large workload: speculative rounds per step")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="target layers (0: the workload's); a cut of the model for profiler captures")
+    ap.add_argument("--skip-configs1", action="store_true", help="large workload: no configs[1] sub-line")
+    ap.add_argument("--profile", action="store_true",
+                    help="timed steps only (no e2e, probes, CPU baseline or configs[1]): for profiler launch lists")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    rank, world, local = dist_env()
+    wl = workload(args.workload, ARCH_CFG if args.arch == "cfg" else ARCH_REF)
+    large = wl.name == "large"
+    if large:
+        wl = dataclasses.replace(wl, batch=LARGE_REQUESTS_PER_GPU)
+    if args.layers:
+        wl = dataclasses.replace(wl, target=wl.target.with_layers(args.layers),
+                                 draft_layers=min(wl.draft_layers, args.layers))
+    if args.impl == "reference":
+        return reference_arm(args, wl, rank, world)
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", init_method="env://", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    try:
+        if large:
+            line = run_session_bench(args, wl, rank, world, local, dist)
+            if not args.skip_configs1 and not args.profile:
+                torch.cuda.empty_cache()
+                sub_args = argparse.Namespace(**{**vars(args), "steps": 10, "warmup": 3})
+                sub = run_generate_bench(sub_args, workload("int8"), rank, world, local, dist)
+                if line is not None and sub is not None:
+                    line["configs1"] = {k: sub[k] for k in ("value", "value_per_gpu", "ms_per_step", "e2e", "config",
+                                                            "spec", "checks", "gpu_launches") if k in sub}
+                    line["configs1"]["round_frac"] = sub["roofline"]["round"]["frac"]
+                    if "cpu_baseline" in sub:
+                        line["configs1"]["cpu_baseline"] = sub["cpu_baseline"]
+        else:
+            line = run_generate_bench(args, wl, rank, world, local, dist)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
 
 
 if __name__ == "__main__":

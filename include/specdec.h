@@ -320,6 +320,17 @@ enum specdec_linear {
 int specdec_time_linear(specdec_handle *h, int role, int layer, int which, int rows, int reps,
                         void *flush, size_t flush_bytes, float *avg_us, double *alg_bytes);
 
+/* Measurement probe (no counterpart in the reference): launches the
+ * attention of `layer` of `role` as a pass of q_per_req rows per request over
+ * the open session's caches builds it (request b's rows are its last
+ * q_per_req cached positions), `reps` times on specdec_stream(h), each launch
+ * alone between CUDA events after the caller's flush buffer is written.
+ * Writes the mean launch time in microseconds and the launch's algorithmic
+ * bytes (every visible K and V row once, int8 scales, query rows in, output
+ * rows out).  Overwrites the prefill row table and activation buffers only. */
+int specdec_time_attention(specdec_handle *h, int role, int layer, int q_per_req, int reps, void *flush,
+                           size_t flush_bytes, float *avg_us, double *alg_bytes);
+
 #ifdef __cplusplus
 }
 #endif

@@ -200,6 +200,16 @@ __global__ void step_cond_kernel(cudaGraphConditionalHandle hnd, int *active_cou
   cudaGraphSetConditional(hnd, more);
 }
 
+// Rows of the attention probe: request b's last q cached positions (token 0).
+__global__ void probe_rows_kernel(const int *len, int B, int q, int *tok, int *pos, int *req) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= B * q) return;
+  const int b = r / q, i = r % q;
+  tok[r] = 0;
+  pos[r] = max(0, len[b] - q + i);
+  req[r] = b;
+}
+
 // After the rounds: the tokens each request emitted in this call (at most
 // cap per request; count = all it emitted).
 __global__ void step_collect_kernel(const int *tokens_out, int out_len, int prompt_len, const int *n_new,
@@ -2074,6 +2084,68 @@ int specdec_time_linear(specdec_handle *h, int role, int layer, int which, int r
     *avg_us = static_cast<float>(tot_ms * 1000.0 / reps);
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);
+  } catch (const SpecErr &e) {
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    h->err = e.msg;
+    return e.code;
+  }
+  return SPECDEC_OK;
+}
+
+int specdec_time_attention(specdec_handle *h, int role, int layer, int q_per_req, int reps, void *flush,
+                           size_t flush_bytes, float *avg_us, double *alg_bytes) {
+  if (!h || !avg_us || !alg_bytes || reps < 1) return SPECDEC_ERR_INVALID;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  try {
+    CK(cudaSetDevice(h->device));
+    if (!h->step_open) fail(SPECDEC_ERR_STATE, "no open session: call specdec_prefill first");
+    if (role != SPECDEC_TARGET && role != SPECDEC_DRAFT) fail(SPECDEC_ERR_INVALID, "unknown role");
+    const bool target = role == SPECDEC_TARGET;
+    const ModelW &m = target ? h->tgt : h->dft;
+    const Dims &dm = m.dm;
+    if (layer < 0 || layer >= dm.L) fail(SPECDEC_ERR_INVALID, "layer out of range");
+    const int B = h->st.B;
+    if (q_per_req < 1 || B * q_per_req > h->R_max) fail(SPECDEC_ERR_INVALID, "rows out of range");
+    const int R = B * q_per_req;
+    const int *len = target ? h->st.t_len : h->st.d_len;
+    std::vector<int> hl(B);
+    CK(cudaMemcpyAsync(hl.data(), len, B * sizeof(int), cudaMemcpyDeviceToHost, h->stream));
+    sync_check(h);
+    launch(h, probe_rows_kernel, dim3((R + 127) / 128), dim3(128), 0, len, B, q_per_req, h->pool.tok, h->pool.pos,
+           h->pool.req);
+    RowsView rows{h->pool.tok, h->pool.pos, h->pool.req};
+    const bool kv8 = h->cfg.kv_dtype == SPECDEC_INT8;
+    const size_t kv_elt = kv8 ? 1 : h->cfg.kv_dtype == SPECDEC_BF16 ? 2 : 4;
+    const size_t lstride = target ? h->t_layer_stride : h->d_layer_stride;
+    const size_t lrows = lstride / dm.D;
+    void *kcl = static_cast<char *>(target ? h->tk : h->dk) + layer * lstride * kv_elt;
+    void *vcl = static_cast<char *>(target ? h->tv : h->dv) + layer * lstride * kv_elt;
+    float *ksl = kv8 ? (target ? h->tks : h->dks) + layer * lrows : nullptr;
+    float *vsl = kv8 ? (target ? h->tvs : h->dvs) + layer * lrows : nullptr;
+    double ctx = 0.0;
+    for (int b = 0; b < B; ++b) ctx += std::max(1, hl[b]);
+    // every visible K and V row once (plus int8 scales), the query rows in,
+    // the output rows out
+    *alg_bytes = ctx * 2.0 * dm.kvd * kv_elt + (kv8 ? ctx * 2.0 * dm.Hkv * 4.0 : 0.0) +
+                 2.0 * R * dm.dq * static_cast<double>(h->act_elt);
+    CK(cudaEventCreate(&e0));
+    CK(cudaEventCreate(&e1));
+    double tot_ms = 0.0;
+    for (int i = 0; i < reps; ++i) {
+      if (flush && flush_bytes) CK(cudaMemsetAsync(flush, i & 0xff, flush_bytes, h->stream));
+      CK(cudaEventRecord(e0, h->stream));
+      attention(h, dm, rows, R, q_per_req, kcl, vcl, ksl, vsl, lstride, target ? h->t_cap : h->d_cap);
+      CK(cudaEventRecord(e1, h->stream));
+      CK(cudaEventSynchronize(e1));
+      float ms = 0.f;
+      CK(cudaEventElapsedTime(&ms, e0, e1));
+      tot_ms += ms;
+    }
+    *avg_us = static_cast<float>(tot_ms * 1000.0 / reps);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    check_device_err(h);
   } catch (const SpecErr &e) {
     if (e0) cudaEventDestroy(e0);
     if (e1) cudaEventDestroy(e1);

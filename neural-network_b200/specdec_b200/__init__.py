@@ -38,7 +38,7 @@ EXPORTS = ("specdec_create", "specdec_destroy", "specdec_last_error", "specdec_l
            "specdec_time_linear", "specdec_generate_tree", "specdec_generate_tree_device", "specdec_tp_unique_id",
            "specdec_create_tp", "specdec_generate_ar", "specdec_generate_ar_device", "specdec_load_netw",
            "specdec_prefill", "specdec_prefill_device", "specdec_step", "specdec_step_device",
-           "specdec_session_tokens")
+           "specdec_session_tokens", "specdec_time_attention")
 
 # linear layers of specdec_time_linear
 LIN_QKV, LIN_OPROJ, LIN_FFN_IN, LIN_FFN_OUT, LIN_HEAD = 0, 1, 2, 3, 4
@@ -119,6 +119,7 @@ def load_library(path: str = LIB_PATH):
                                       C.POINTER(C.c_void_p)]
     lib.specdec_time_linear.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                         C.c_size_t, C.POINTER(C.c_float), C.POINTER(C.c_double)]
+    lib.specdec_time_attention.argtypes = lib.specdec_time_linear.argtypes
     _lib = lib
     return lib
 
@@ -369,4 +370,14 @@ class Engine:
         us, nb = C.c_float(0.0), C.c_double(0.0)
         self._check(self._lib.specdec_time_linear(self.h, role, layer, which, rows, reps, C.c_void_p(flush_ptr),
                                                   C.c_size_t(flush_bytes), C.byref(us), C.byref(nb)))
+        return float(us.value), float(nb.value)
+
+    def time_attention(self, role: int, layer: int, q_per_req: int, reps: int, flush_ptr: int = 0,
+                       flush_bytes: int = 0):
+        """Mean device time (us) of one layer's attention launch over the open
+        session's caches (q_per_req rows per request), each launch alone with
+        the L2 flushed before it, and its algorithmic bytes."""
+        us, nb = C.c_float(0.0), C.c_double(0.0)
+        self._check(self._lib.specdec_time_attention(self.h, role, layer, q_per_req, reps, C.c_void_p(flush_ptr),
+                                                     C.c_size_t(flush_bytes), C.byref(us), C.byref(nb)))
         return float(us.value), float(nb.value)

@@ -36,3 +36,15 @@ def max_over_ranks(values: Sequence[float], dist=None, device=None) -> list:
     t = torch.tensor([float(v) for v in values], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return t.tolist()
+
+
+def sum_over_ranks(values: Sequence[float], dist=None, device=None) -> list:
+    """Element-wise sum of `values` over all ranks (identity without dist):
+    the units every rank processed."""
+    if dist is None or not dist.is_initialized() or dist.get_world_size() == 1:
+        return [float(v) for v in values]
+    import torch
+
+    t = torch.tensor([float(v) for v in values], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return t.tolist()
