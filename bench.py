@@ -785,6 +785,8 @@ def main():
     ap.add_argument("--rounds-per-step", type=int, default=1, help="large workload: speculative rounds per step")
     ap.add_argument("--layers", type=int, default=0,
                     help="target layers (0: the workload's); a cut of the model for profiler captures")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="requests per GPU (0: the workload's); a smaller case for profiler captures")
     ap.add_argument("--skip-configs1", action="store_true", help="large workload: no configs[1] sub-line")
     ap.add_argument("--profile", action="store_true",
                     help="timed steps only (no e2e, probes, CPU baseline or configs[1]): for profiler launch lists")
@@ -795,6 +797,8 @@ def main():
     large = wl.name == "large"
     if large:
         wl = dataclasses.replace(wl, batch=LARGE_REQUESTS_PER_GPU)
+    if args.batch:
+        wl = dataclasses.replace(wl, batch=args.batch)
     if args.layers:
         wl = dataclasses.replace(wl, target=wl.target.with_layers(args.layers),
                                  draft_layers=min(wl.draft_layers, args.layers))

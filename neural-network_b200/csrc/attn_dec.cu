@@ -38,14 +38,19 @@ namespace specdec {
 
 namespace {
 
-constexpr int kAdSlots = 6;                      // ring slots of half a tile (K or V)
+constexpr int kAdSlots = 3;                      // ring slots of half a tile (K or V)
 constexpr int kAdHalf = kAdTile * kAdD * 2;      // 32 KB: 128 positions x 128 bf16
 constexpr int kAdBox = kAdTile * 64 * 2;         // 16 KB: one 64-dim atom of a half tile
 constexpr int kAdQBytes = kAdN * kAdD * 2;       // 4 KB: 16 query rows, two 2 KB atoms
 constexpr int kAdPBytes = kAdN * kAdTile * 2;    // 4 KB: 16 query rows x 128 positions, two atoms
 constexpr int kAdThreads = 192;
-constexpr int kAdSmem = kAdSlots * kAdHalf + 2 * kAdQBytes + 2 * kAdPBytes + 1024;
+// three ring slots, two query buffers, one P buffer: 111 KB, two CTAs per SM
+constexpr int kAdSmem = kAdSlots * kAdHalf + 2 * kAdQBytes + kAdPBytes + 1024;
 constexpr int kAdTmemCols = 64;                  // S0 S1 O0 O1, 16 columns each
+// 1 / sqrt(128) in fp32: the scores are scaled by a product (the reference
+// divides by sqrt(D); the two differ by at most one rounding, far inside the
+// bf16 tolerance of this path)
+constexpr float kAdScale = 0.0883883476483184f;
 
 // kind::f16, D fp32, A and B bf16, M = 128, N = 16.  S: A and B K-major.
 // O: A (V^T) MN-major, B (P^T) K-major.
@@ -78,6 +83,49 @@ __device__ __forceinline__ bool bar_and_softmax(bool v) {
   return r != 0;
 }
 __device__ __forceinline__ void bar_softmax() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// NC accumulator columns of the warp's 32 TMEM lanes (NC = 8 or 16), waited for.
+template <int NC>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&v)[NC]) {
+  if constexpr (NC == 16) {
+    tmem_ld16(taddr, v);
+  } else {
+    static_assert(NC == 8, "8 or 16 columns");
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+  }
+}
+
+// Warp reduction of NQ values per lane that leaves lane l with the result for
+// query (l / (32 / NQ)): each halving step trades half of the values with
+// the partner lane, so NQ queries cost NQ - 1 + log2(32) shuffles, not
+// NQ * log2(32).  MAX: maximum, else sum.
+template <int NQ, bool MAX>
+__device__ __forceinline__ float warp_reduce_scatter(const float (&v)[NQ], int lane) {
+  float w[NQ];
+#pragma unroll
+  for (int i = 0; i < NQ; ++i) w[i] = v[i];
+  auto op = [](float a, float b) { return MAX ? fmaxf(a, b) : a + b; };
+  int off = 16;
+#pragma unroll
+  for (int n = NQ; n > 1; n >>= 1, off >>= 1) {
+    const bool hi = (lane & off) != 0;
+#pragma unroll
+    for (int j = 0; j < n / 2; ++j) {
+      const float keep = hi ? w[j + n / 2] : w[j];
+      const float send = hi ? w[j] : w[j + n / 2];
+      w[j] = op(keep, __shfl_xor_sync(0xffffffffu, send, off));
+    }
+  }
+#pragma unroll
+  for (; off > 0; off >>= 1) w[0] = op(w[0], __shfl_xor_sync(0xffffffffu, w[0], off));
+  return w[0];
+}
 
 // One work item: (group g, head h, split) and the range of cache tiles it
 // covers.  The splits of a (group, head) share the tiles up to the group's
@@ -114,20 +162,24 @@ __device__ __forceinline__ AdItem ad_item(const AttnDecArgs &a, int item) {
   return it;
 }
 
-__global__ void __launch_bounds__(kAdThreads, 1) attn_dec_kernel(const __grid_constant__ AttnDecArgs a) {
+// NQ: the group's queries rounded up to 1, 2, 8 or 16 (the columns the
+// softmax threads carry; the MMAs always have 16).
+template <int NQ>
+__global__ void __launch_bounds__(kAdThreads, 2) attn_dec_kernel(const __grid_constant__ AttnDecArgs a) {
+  constexpr int NC = NQ <= 8 ? 8 : 16;  // TMEM columns read per product
   pdl_wait();
   extern __shared__ unsigned char ad_smem_raw[];
   unsigned char *ring =
       reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(ad_smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char *sq = ring + kAdSlots * kAdHalf;  // two query buffers
-  unsigned char *sp = sq + 2 * kAdQBytes;         // two P buffers
+  unsigned char *sp = sq + 2 * kAdQBytes;         // the P buffer
   __shared__ __align__(8) uint64_t full[kAdSlots], empty[kAdSlots], q_full[2], q_empty[2], s_full[2], s_free[2],
       p_full[2], o_full[2], o_free[2], mma_done;
   __shared__ uint32_t s_tmem;
   __shared__ volatile int s_abort;
   __shared__ int s_issued, s_consumed, s_q_issued, s_q_consumed, s_last;
-  __shared__ float red[2][4][kAdN];   // per softmax warp and query: the tile maximum (double buffered)
-  __shared__ float lred[2][4][kAdN];  // per softmax warp and query: the row sum (double buffered)
+  __shared__ __align__(16) float red[2][NQ][4];   // per query and softmax warp: the tile maximum
+  __shared__ __align__(16) float lred[2][NQ][4];  // per query and softmax warp: the row sum
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == 0) {
@@ -202,57 +254,89 @@ __global__ void __launch_bounds__(kAdThreads, 1) attn_dec_kernel(const __grid_co
     }
   } else if (warp == 1) {
     // ---- MMA issuer --------------------------------------------------------
+    // Order S_0, S_1, O_0, S_2, O_1, ...: the scores of tile T + 1 are on the
+    // tensor cores while the softmax of tile T runs.  K of tile T sits in
+    // ring slot 2T, V in slot 2T + 1 (the producer's order).
     if (lane == 0) {
-      int idx = 0, qi = 0, T = 0;
-      bool stop = false;
-      for (int item = blockIdx.x; item < a.n_items && !stop && !s_abort; item += gridDim.x) {
-        const AdItem it = ad_item(a, item);
-        if (it.nt == 0) continue;
-        const int qb = qi & 1;
-        if (!mbar_wait(&q_full[qb], (qi >> 1) & 1)) { give_up(); break; }
-        s_q_consumed = qi + 1;
-        const uint32_t qa = smem_u32(sq + qb * kAdQBytes);
-        for (int t = 0; t < it.nt; ++t, ++T) {
-          const int sb = T & 1;
-          const uint32_t ph = (T >> 1) & 1;
-          // S^T = K Q^T into S[sb]
-          const int sk = idx % kAdSlots;
-          if (!mbar_wait(&full[sk], (idx / kAdSlots) & 1) || !mbar_wait(&s_free[sb], ph ^ 1) || s_abort) {
-            give_up();
-            stop = true;
-            break;
-          }
-          s_consumed = ++idx;
-          tc_fence_after();
-          const uint32_t ka = smem_u32(ring + sk * kAdHalf);
-#pragma unroll
-          for (int kk = 0; kk < kAdD / 16; ++kk)
-            tc_mma(tmem + 16 * sb, umma_desc_k128(ka + (kk >> 2) * kAdBox + 32 * (kk & 3)),
-                   umma_desc_k128(qa + (kk >> 2) * (kAdQBytes / 2) + 32 * (kk & 3)), kAdIdescS, kk ? 1u : 0u);
-          tc_commit(&empty[sk]);
-          tc_commit(&s_full[sb]);
-          // O^T = V^T P^T into O[sb], once P is written and O[sb] was folded
-          const int sv = idx % kAdSlots;
-          if (!mbar_wait(&full[sv], (idx / kAdSlots) & 1) || !mbar_wait(&p_full[sb], ph) ||
-              !mbar_wait(&o_free[sb], ph ^ 1) || s_abort) {
-            give_up();
-            stop = true;
-            break;
-          }
-          s_consumed = ++idx;
-          tc_fence_after();
-          const uint32_t va = smem_u32(ring + sv * kAdHalf);
-          const uint32_t pa = smem_u32(sp + sb * kAdPBytes);
-#pragma unroll
-          for (int kk = 0; kk < kAdTile / 16; ++kk)
-            tc_mma(tmem + 32 + 16 * sb, umma_desc_mn128_2atoms(va + 2048 * kk),
-                   umma_desc_k128(pa + (kk >> 2) * (kAdPBytes / 2) + 32 * (kk & 3)), kAdIdescO, kk ? 1u : 0u);
-          tc_commit(&empty[sv]);
-          tc_commit(&o_full[sb]);
+      struct Cur {
+        int item, t, qb;
+        AdItem it;
+      };
+      auto seek = [&](int item, AdItem &it) {  // the next item with tiles, at or after `item`
+        for (; item < a.n_items; item += gridDim.x) {
+          it = ad_item(a, item);
+          if (it.nt > 0) return item;
         }
-        tc_commit(&q_empty[qb]);
-        ++qi;
+        return a.n_items;
+      };
+      auto issue_s = [&](int T, const Cur &c) -> bool {
+        const int idx = 2 * T, sk = idx % kAdSlots, sb = T & 1;
+        if (!mbar_wait(&full[sk], (idx / kAdSlots) & 1) || !mbar_wait(&s_free[sb], ((T >> 1) & 1) ^ 1) || s_abort)
+          return false;
+        tc_fence_after();
+        const uint32_t ka = smem_u32(ring + sk * kAdHalf), qa = smem_u32(sq + c.qb * kAdQBytes);
+#pragma unroll
+        for (int kk = 0; kk < kAdD / 16; ++kk)
+          tc_mma(tmem + 16 * sb, umma_desc_k128(ka + (kk >> 2) * kAdBox + 32 * (kk & 3)),
+                 umma_desc_k128(qa + (kk >> 2) * (kAdQBytes / 2) + 32 * (kk & 3)), kAdIdescS, kk ? 1u : 0u);
+        tc_commit(&empty[sk]);
+        tc_commit(&s_full[sb]);
+        return true;
+      };
+      auto issue_o = [&](int T) -> bool {
+        const int idx = 2 * T + 1, sv = idx % kAdSlots, sb = T & 1;
+        const uint32_t ph = (T >> 1) & 1;
+        if (!mbar_wait(&full[sv], (idx / kAdSlots) & 1) || !mbar_wait(&p_full[sb], ph) ||
+            !mbar_wait(&o_free[sb], ph ^ 1) || s_abort)
+          return false;
+        tc_fence_after();
+        const uint32_t va = smem_u32(ring + sv * kAdHalf), pa = smem_u32(sp);
+#pragma unroll
+        for (int kk = 0; kk < kAdTile / 16; ++kk)
+          tc_mma(tmem + 32 + 16 * sb, umma_desc_mn128_2atoms(va + 2048 * kk),
+                 umma_desc_k128(pa + (kk >> 2) * (kAdPBytes / 2) + 32 * (kk & 3)), kAdIdescO, kk ? 1u : 0u);
+        tc_commit(&empty[sv]);
+        tc_commit(&o_full[sb]);
+        return true;
+      };
+      int qcount = 0;  // items whose queries were waited for
+      Cur c;
+      c.item = seek(blockIdx.x, c.it);
+      c.t = 0;
+      c.qb = 0;
+      const bool work = c.item < a.n_items;  // this CTA may have only empty splits
+      bool ok = true;
+      if (work) {
+        ok = mbar_wait(&q_full[0], 0);
+        s_q_consumed = qcount = 1;
+        if (ok) ok = issue_s(0, c);
+        if (ok) s_consumed = 1;  // the lowest ring slot not yet taken: V of tile 0
       }
+      for (int T = 0; work && ok; ++T) {
+        Cur n = c;
+        bool more = true;
+        if (c.t + 1 < c.it.nt) {
+          n.t = c.t + 1;
+        } else {
+          n.item = seek(c.item + gridDim.x, n.it);
+          n.t = 0;
+          more = n.item < a.n_items;
+          if (more) {
+            n.qb = qcount & 1;
+            ok = mbar_wait(&q_full[n.qb], (qcount >> 1) & 1);
+            s_q_consumed = ++qcount;
+          }
+        }
+        if (ok && more) ok = issue_s(T + 1, n);
+        if (ok) {
+          ok = issue_o(T);
+          if (ok) s_consumed = 2 * T + 3;
+        }
+        if (ok && c.t + 1 == c.it.nt) tc_commit(&q_empty[c.qb]);
+        if (!more) break;
+        c = n;
+      }
+      if (!ok) give_up();
       // every product this thread issued has completed before the CTA moves on
       tc_commit(&mma_done);
       if (!mbar_wait(&mma_done, 0)) give_up();
@@ -261,8 +345,9 @@ __global__ void __launch_bounds__(kAdThreads, 1) attn_dec_kernel(const __grid_co
     // ---- softmax and output: thread = position of a tile, and = dim of O ---
     const int qd = warp & 3;  // TMEM lane quadrant of this warp
     const int p = 32 * qd + lane;
+    const int own = lane / (32 / NQ);  // the query this lane holds after a reduce-scatter
+    const bool owner = (lane % (32 / NQ)) == 0;
     const uint32_t tl = tmem + (static_cast<uint32_t>(32 * qd) << 16);
-    const float sqrt_d = sqrtf(static_cast<float>(kAdD));
     int T = 0, ni = 0;
     // ok: the last barrier's verdict (the same in every softmax thread); lok:
     // this thread's own waits so far, folded into ok at the next barrier, so
@@ -270,20 +355,19 @@ __global__ void __launch_bounds__(kAdThreads, 1) attn_dec_kernel(const __grid_co
     bool ok = true, lok = true;
     for (int item = blockIdx.x; item < a.n_items; item += gridDim.x, ++ni) {
       const AdItem it = ad_item(a, item);
-      int qpos[kAdN], qtb[kAdN];
-      unsigned long long qmask[kAdN];
-      bool qv[kAdN];
+      int qpos[NQ], qtb[NQ];
+      unsigned long long qmask[NQ];
 #pragma unroll
-      for (int q = 0; q < kAdN; ++q) {
+      for (int q = 0; q < NQ; ++q) {
         const int r = it.rq0 + q;
-        qv[q] = q < it.nq && a.rows.req[r] >= 0;
-        qpos[q] = qv[q] ? row_slot(a.rows, r) : -1;
-        qtb[q] = (qv[q] && a.rows.tb) ? a.rows.tb[r] : 0x7fffffff;
-        qmask[q] = (qv[q] && a.rows.mask) ? a.rows.mask[r] : 0ull;
+        const bool v = q < it.nq && a.rows.req[r] >= 0;
+        qpos[q] = v ? row_slot(a.rows, r) : -1;
+        qtb[q] = (v && a.rows.tb) ? a.rows.tb[r] : 0x7fffffff;
+        qmask[q] = (v && a.rows.mask) ? a.rows.mask[r] : 0ull;
       }
-      float m[kAdN], l[kAdN], o[kAdN], al_prev[kAdN];
+      float m[NQ], l[NQ], o[NQ], al_prev[NQ];
 #pragma unroll
-      for (int q = 0; q < kAdN; ++q) {
+      for (int q = 0; q < NQ; ++q) {
         m[q] = -INFINITY;
         l[q] = 0.f;
         o[q] = 0.f;
@@ -293,89 +377,92 @@ __global__ void __launch_bounds__(kAdThreads, 1) attn_dec_kernel(const __grid_co
         const int ob = Tp & 1;
         const bool w = mbar_wait(&o_full[ob], (Tp >> 1) & 1);
         tc_fence_after();
-        float ov[kAdN];
-        tmem_ld16(tl + 32 + 16 * ob, ov);
+        float ov[NC];
+        tmem_ld_cols<NC>(tl + 32 + 16 * ob, ov);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&o_free[ob]);
 #pragma unroll
-        for (int q = 0; q < kAdN; ++q) o[q] = o[q] * al_prev[q] + ov[q];
+        for (int q = 0; q < NQ; ++q) o[q] = o[q] * al_prev[q] + ov[q];
         return w;
       };
       for (int t = 0; t < it.nt; ++t, ++T) {
         const int sb = T & 1;
         lok = mbar_wait(&s_full[sb], (T >> 1) & 1) && lok;
         tc_fence_after();
-        float s[kAdN];
-        tmem_ld16(tl + 16 * sb, s);
+        float sc[NC];
+        tmem_ld_cols<NC>(tl + 16 * sb, sc);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_free[sb]);
         const int pos = (it.t0 + t) * kAdTile + p;
+        float s[NQ];
 #pragma unroll
-        for (int q = 0; q < kAdN; ++q) {
-          const bool vis = qv[q] && pos <= qpos[q] &&
+        for (int q = 0; q < NQ; ++q) {
+          // causal, and inside a token tree only the prefix, the ancestors and itself
+          const bool vis = pos <= qpos[q] &&
                            (pos < qtb[q] || (pos - qtb[q] < 64 && ((qmask[q] >> (pos - qtb[q])) & 1ull)));
-          s[q] = vis ? __fdiv_rn(s[q], sqrt_d) : -INFINITY;
+          s[q] = vis ? sc[q] * kAdScale : -INFINITY;
         }
-#pragma unroll
-        for (int q = 0; q < kAdN; ++q) {
-          if (q < it.nq) {  // uniform over the CTA
-            const float mx = warp_max(s[q]);
-            if (lane == 0) red[sb][qd][q] = mx;
-          }
+        {
+          const float wm = warp_reduce_scatter<NQ, true>(s, lane);
+          if (owner) red[sb][own][qd] = wm;
         }
         ok = bar_and_softmax(lok && !s_abort);
         if (!ok) break;
-        float al[kAdN], pr[kAdN];
+        float al[NQ], pr[NQ];
 #pragma unroll
-        for (int q = 0; q < kAdN; ++q) {
-          al[q] = 0.f;
-          pr[q] = 0.f;
-          if (q < it.nq) {
-            const float mt = fmaxf(fmaxf(red[sb][0][q], red[sb][1][q]), fmaxf(red[sb][2][q], red[sb][3][q]));
-            const float mn = fmaxf(m[q], mt);
-            al[q] = (m[q] == -INFINITY) ? 0.f : expf(m[q] - mn);
-            pr[q] = (s[q] == -INFINITY) ? 0.f : expf(s[q] - mn);
-            l[q] = l[q] * al[q] + pr[q];
-            m[q] = mn;
-          }
+        for (int q = 0; q < NQ; ++q) {
+          const float4 r4 = *reinterpret_cast<const float4 *>(&red[sb][q][0]);
+          const float mn = fmaxf(m[q], fmaxf(fmaxf(r4.x, r4.y), fmaxf(r4.z, r4.w)));
+          // P is rounded to bf16 for the product: the fast exponential's
+          // error (a few ulp of fp32) is far below that rounding
+          al[q] = (m[q] == -INFINITY) ? 0.f : __expf(m[q] - mn);
+          pr[q] = (s[q] == -INFINITY) ? 0.f : __expf(s[q] - mn);
+          l[q] = l[q] * al[q] + pr[q];
+          m[q] = mn;
         }
-        // P^T as bf16: row q, position p of the K-major swizzled tile
+        // O_{T-1} into the registers: then its product has read P, which
+        // tile T overwrites
+        if (t > 0) lok = fold(T - 1) && lok;
+        // P^T as bf16: row q, position p of the K-major swizzled tile.  Rows
+        // of the columns past the group's queries keep whatever they hold:
+        // column q of O^T depends on row q of P^T alone, and those columns are
+        // never read.
         {
-          unsigned char *pt = sp + sb * kAdPBytes + (p >> 6) * (kAdPBytes / 2);
+          unsigned char *pt = sp + (p >> 6) * (kAdPBytes / 2);
           const int chunk = (p & 63) >> 3, byte = (p & 7) * 2;
 #pragma unroll
-          for (int q = 0; q < kAdN; ++q)
-            *reinterpret_cast<__nv_bfloat16 *>(pt + q * 128 + ((chunk ^ (q & 7)) << 4) + byte) =
-                __float2bfloat16_rn(pr[q]);
+          for (int q = 0; q < NQ; ++q)
+            if (q < it.nq)
+              *reinterpret_cast<__nv_bfloat16 *>(pt + q * 128 + ((chunk ^ (q & 7)) << 4) + byte) =
+                  __float2bfloat16_rn(pr[q]);
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[sb]);
-        if (t > 0) lok = fold(T - 1) && lok;
 #pragma unroll
-        for (int q = 0; q < kAdN; ++q) al_prev[q] = al[q];
+        for (int q = 0; q < NQ; ++q) al_prev[q] = al[q];
       }
       if (ok && it.nt > 0) lok = fold(T - 1) && lok;
       // the row sums over the 128 positions
       const int lb = ni & 1;
-#pragma unroll
-      for (int q = 0; q < kAdN; ++q) {
-        if (q < it.nq) {
-          const float sm = warp_sum(l[q]);
-          if (lane == 0) lred[lb][qd][q] = sm;
-        }
+      {
+        const float ws = warp_reduce_scatter<NQ, false>(l, lane);
+        if (owner) lred[lb][own][qd] = ws;
       }
       ok = bar_and_softmax(ok && lok && !s_abort);
       if (!ok) break;
-      float L[kAdN];
+      float L[NQ];
 #pragma unroll
-      for (int q = 0; q < kAdN; ++q) L[q] = (q < it.nq) ? (lred[lb][0][q] + lred[lb][1][q]) + (lred[lb][2][q] + lred[lb][3][q]) : 0.f;
+      for (int q = 0; q < NQ; ++q) {
+        const float4 r4 = *reinterpret_cast<const float4 *>(&lred[lb][q][0]);
+        L[q] = (r4.x + r4.y) + (r4.z + r4.w);
+      }
       if (a.nsplit == 1) {
 #pragma unroll
-        for (int q = 0; q < kAdN; ++q)
-          if (qv[q] && qpos[q] < a.S_cap)
+        for (int q = 0; q < NQ; ++q)
+          if (qpos[q] >= 0 && qpos[q] < a.S_cap)
             a.out[static_cast<size_t>(it.rq0 + q) * a.ldo + it.h * kAdD + p] =
                 __float2bfloat16_rn(L[q] > 0.f ? __fdiv_rn(o[q], L[q]) : 0.f);
         continue;
@@ -383,13 +470,13 @@ __global__ void __launch_bounds__(kAdThreads, 1) attn_dec_kernel(const __grid_co
       // split: this item's partial, then the last split of (group, head) merges
       bool any = false;
 #pragma unroll
-      for (int q = 0; q < kAdN; ++q) any |= qv[q];
+      for (int q = 0; q < NQ; ++q) any |= qpos[q] >= 0;
       if (!any) continue;  // the same for every split of the group
       float *pp = a.part + static_cast<size_t>(item) * kAdPartFloats;
 #pragma unroll
-      for (int q = 0; q < kAdN; ++q) pp[q * kAdD + p] = o[q];
+      for (int q = 0; q < NQ; ++q) pp[q * kAdD + p] = o[q];
 #pragma unroll
-      for (int q = 0; q < kAdN; ++q)
+      for (int q = 0; q < NQ; ++q)
         if (p == q) {
           pp[kAdN * kAdD + q] = m[q];
           pp[kAdN * kAdD + kAdN + q] = L[q];
@@ -403,16 +490,16 @@ __global__ void __launch_bounds__(kAdThreads, 1) attn_dec_kernel(const __grid_co
         __threadfence();
         const float *p0 = a.part + static_cast<size_t>(gh) * a.nsplit * kAdPartFloats;
 #pragma unroll 1
-        for (int q = 0; q < kAdN; ++q) {
-          if (!qv[q] || qpos[q] >= a.S_cap) continue;
+        for (int q = 0; q < NQ; ++q) {
+          if (qpos[q] < 0 || qpos[q] >= a.S_cap) continue;
           float M = -INFINITY;
-          for (int sp2 = 0; sp2 < a.nsplit; ++sp2) {
-            const float *ps = p0 + static_cast<size_t>(sp2) * kAdPartFloats;
+          for (int s2 = 0; s2 < a.nsplit; ++s2) {
+            const float *ps = p0 + static_cast<size_t>(s2) * kAdPartFloats;
             if (__ldcg(ps + kAdN * kAdD + kAdN + q) > 0.f) M = fmaxf(M, __ldcg(ps + kAdN * kAdD + q));
           }
           float num = 0.f, den = 0.f;
-          for (int sp2 = 0; sp2 < a.nsplit; ++sp2) {
-            const float *ps = p0 + static_cast<size_t>(sp2) * kAdPartFloats;
+          for (int s2 = 0; s2 < a.nsplit; ++s2) {
+            const float *ps = p0 + static_cast<size_t>(s2) * kAdPartFloats;
             const float Ls = __ldcg(ps + kAdN * kAdD + kAdN + q);
             if (Ls > 0.f) {
               const float wgt = expf(__ldcg(ps + kAdN * kAdD + q) - M);
@@ -447,11 +534,13 @@ __global__ void __launch_bounds__(kAdThreads, 1) attn_dec_kernel(const __grid_co
 
 int attn_dec_smem_bytes() { return kAdSmem; }
 
-cudaError_t attn_dec_set_attrs() {
-  return cudaFuncSetAttribute(attn_dec_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAdSmem);
+namespace {
+template <int NQ>
+cudaError_t set_one() {
+  return cudaFuncSetAttribute(attn_dec_kernel<NQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, kAdSmem);
 }
-
-cudaError_t attn_dec_launch(const AttnDecArgs &a, int grid, cudaStream_t stream, bool pdl) {
+template <int NQ>
+cudaError_t launch_one(const AttnDecArgs &a, int grid, cudaStream_t stream, bool pdl) {
   cudaLaunchConfig_t lc{};
   lc.gridDim = dim3(grid);
   lc.blockDim = dim3(kAdThreads);
@@ -462,7 +551,25 @@ cudaError_t attn_dec_launch(const AttnDecArgs &a, int grid, cudaStream_t stream,
   at[0].val.programmaticStreamSerializationAllowed = 1;
   lc.attrs = at;
   lc.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&lc, attn_dec_kernel, a);
+  return cudaLaunchKernelEx(&lc, attn_dec_kernel<NQ>, a);
 }
+}  // namespace
+
+cudaError_t attn_dec_set_attrs() {
+  cudaError_t e = set_one<1>();
+  if (e == cudaSuccess) e = set_one<2>();
+  if (e == cudaSuccess) e = set_one<8>();
+  if (e == cudaSuccess) e = set_one<16>();
+  return e;
+}
+
+cudaError_t attn_dec_launch(const AttnDecArgs &a, int grid, cudaStream_t stream, bool pdl) {
+  if (a.Q <= 1) return launch_one<1>(a, grid, stream, pdl);
+  if (a.Q <= 2) return launch_one<2>(a, grid, stream, pdl);
+  if (a.Q <= 8) return launch_one<8>(a, grid, stream, pdl);
+  return launch_one<16>(a, grid, stream, pdl);
+}
+
+int attn_dec_ctas_per_sm() { return 2; }
 
 }  // namespace specdec

@@ -38,7 +38,10 @@ int attn_dec_smem_bytes();
 // Sets the kernel's shared-memory attribute (once per device).
 cudaError_t attn_dec_set_attrs();
 // Launches attn_dec_kernel with `grid` persistent CTAs on `stream`
-// (programmatic stream serialization when pdl is set).
+// (programmatic stream serialization when pdl is set).  Its variant carries
+// the group's queries rounded up to 1, 2, 8 or 16.
 cudaError_t attn_dec_launch(const AttnDecArgs &a, int grid, cudaStream_t stream, bool pdl);
+// CTAs of the kernel resident per SM (its shared memory fits two).
+int attn_dec_ctas_per_sm();
 
 }  // namespace specdec

@@ -1054,8 +1054,9 @@ void attention(specdec_handle *h, const Dims &dm, RowsView rows, int R, int Q, c
     const int base = ngroups * dm.H;
     const int tiles = (S_cap + kAdTile - 1) / kAdTile;
     int ns = 1;
+    const int slots = attn_dec_ctas_per_sm() * h->num_sms;
     auto waste = [&](int n) {
-      const double per = static_cast<double>(base) * n / h->num_sms;
+      const double per = static_cast<double>(base) * n / slots;
       return std::ceil(per) / per - 1.0;
     };
     while (ns < kAdMaxSplit && 2 * ns <= tiles && waste(ns) > 0.05) ns *= 2;
@@ -1063,7 +1064,7 @@ void attention(specdec_handle *h, const Dims &dm, RowsView rows, int R, int Q, c
     d.n_items = base * ns;
     d.out = static_cast<__nv_bfloat16 *>(h->ATT); d.ldo = dm.dq;
     d.part = h->ad_part; d.ticket = h->ad_ticket; d.err = h->st.err;
-    CK(attn_dec_launch(d, std::min(d.n_items, h->num_sms), h->stream, h->use_pdl));
+    CK(attn_dec_launch(d, std::min(d.n_items, slots), h->stream, h->use_pdl));
     ++h->launches;
     return;
   }

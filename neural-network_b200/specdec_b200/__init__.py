@@ -119,7 +119,8 @@ def load_library(path: str = LIB_PATH):
                                       C.POINTER(C.c_void_p)]
     lib.specdec_time_linear.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                         C.c_size_t, C.POINTER(C.c_float), C.POINTER(C.c_double)]
-    lib.specdec_time_attention.argtypes = lib.specdec_time_linear.argtypes
+    lib.specdec_time_attention.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_size_t,
+                                           C.POINTER(C.c_float), C.POINTER(C.c_double)]
     _lib = lib
     return lib
 
