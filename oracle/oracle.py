@@ -20,6 +20,8 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF_SO = os.path.join(HERE, "_ref", "libnnref.so")
+# the reference library with the B200 dispatch of oracle/binding/ (make bind)
+REF_CUDA_SO = os.path.join(HERE, "_ref", "libnnref_cuda.so")
 ORACLE_SO = os.path.join(HERE, "_build", "liboracle.so")
 
 
@@ -46,6 +48,9 @@ def build(ref: bool = True) -> None:
     tree = reference_tree() if ref else ""
     if tree:
         targets += ["ref", f"REF={tree}"]
+        # the reference with the B200 dispatch, once the product library is built
+        if os.path.exists(os.path.join(HERE, "..", "neural-network_b200", "specdec_b200", "libspecdec_b200.so")):
+            targets.insert(-1, "bind")
     subprocess.run(["make", "-s", "-C", HERE] + targets, check=True)
 
 
@@ -55,12 +60,12 @@ def reference_available() -> bool:
 
 # ---------------------------------------------------------------------------
 class _RefLib:
-    _lib = None
+    _libs = {}
 
     @classmethod
-    def get(cls):
-        if cls._lib is None:
-            lib = C.CDLL(REF_SO)
+    def get(cls, cuda: bool = False):
+        if cuda not in cls._libs:
+            lib = C.CDLL(REF_CUDA_SO if cuda else REF_SO)
             lib.nnref_last_error.restype = C.c_char_p
             lib.nnref_decoder_new.restype = C.c_void_p
             lib.nnref_decoder_new.argtypes = [C.c_size_t] * 6
@@ -84,85 +89,142 @@ class _RefLib:
                                                        C.c_int, _i64p, C.c_size_t, C.POINTER(C.c_size_t)]
             lib.nnref_rope.argtypes = [_f32p] + [C.c_size_t] * 5 + [_f32p]
             lib.nnref_quantize_int8.argtypes = [_f32p, C.c_size_t, C.c_size_t, _f32p, _i8p, _f32p]
-            cls._lib = lib
-        return cls._lib
+            if cuda:
+                lib.nnref_cuda_backend_new.restype = C.c_void_p
+                lib.nnref_cuda_backend_new.argtypes = [C.c_void_p, C.c_int]
+                lib.nnref_cuda_backend_free.argtypes = [C.c_void_p]
+                lib.nnref_cuda_backend_launches.restype = C.c_longlong
+                lib.nnref_cuda_backend_launches.argtypes = [C.c_void_p]
+                lib.nnref_decoder_new_on.restype = C.c_void_p
+                lib.nnref_decoder_new_on.argtypes = [C.c_void_p] + [C.c_size_t] * 6
+            cls._libs[cuda] = lib
+        return cls._libs[cuda]
 
 
-def _ref_check(rc: int) -> None:
+def _ref_check(rc: int, lib=None) -> None:
     if rc != 0:
-        raise RuntimeError(_RefLib.get().nnref_last_error().decode())
+        raise RuntimeError((lib or _RefLib.get()).nnref_last_error().decode())
+
+
+def bound_reference_available() -> bool:
+    return os.path.exists(REF_CUDA_SO)
+
+
+class _SpecModelCfg(C.Structure):  # specdec_model_config (include/specdec.h)
+    _fields_ = [(n, C.c_int32) for n in ("vocab_size", "d_model", "n_heads", "n_kv_heads", "d_ff", "n_layers",
+                                         "max_seq_len", "arch")]
+
+
+class _SpecCfg(C.Structure):  # specdec_config (include/specdec.h)
+    _fields_ = [("target", _SpecModelCfg), ("draft", _SpecModelCfg)] + [
+        (n, C.c_int32) for n in ("draft_shares_target", "weight_dtype", "act_dtype", "kv_dtype", "max_batch",
+                                 "max_lookahead", "max_prompt_len", "max_tree_nodes")]
+
+
+class CudaSpecBackendRef:
+    """A CudaSpecBackend (oracle/binding/cuda_spec_backend.hpp) in the
+    reference library built with the B200 dispatch: decoders constructed on it
+    (Reference(..., backend=this)) run generate_speculative and
+    generate_advanced through libspecdec_b200.so.  fp32 weights, activations
+    and cache (a quantized_cache call switches the cache to int8)."""
+
+    def __init__(self, target_shape, draft_shape, device: int = 0, max_prompt_len: int = 0):
+        self.lib = _RefLib.get(cuda=True)
+
+        def mc(m):
+            return _SpecModelCfg(m.vocab, m.d_model, m.n_heads, m.kv_heads, m.d_ff, m.n_layers, m.max_seq_len, 0)
+
+        cfg = _SpecCfg(mc(target_shape), mc(draft_shape), 0, 0, 0, 0, 1, 8,
+                       max_prompt_len or target_shape.max_seq_len, 0)
+        self.h = self.lib.nnref_cuda_backend_new(C.byref(cfg), device)
+        if not self.h:
+            _ref_check(-1, self.lib)
+
+    def launches(self) -> int:
+        return int(self.lib.nnref_cuda_backend_launches(self.h))
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.nnref_cuda_backend_free(self.h)
+            self.h = None
 
 
 class Reference:
     """One reference ``TransformerDecoder`` with injected weights."""
 
-    def __init__(self, shape, params: Sequence[np.ndarray], requires_grad: bool = True):
+    def __init__(self, shape, params: Sequence[np.ndarray], requires_grad: bool = True,
+                 backend: Optional[CudaSpecBackendRef] = None):
         if shape.arch != 0 or shape.kv_heads != shape.n_heads:
             raise ValueError("the reference TransformerDecoder is the post-LN SwiGLU MHA model")
-        lib = _RefLib.get()
+        lib = backend.lib if backend is not None else _RefLib.get()
+        self._lib = lib
+        self.backend = backend  # kept alive as long as the decoder
         self.shape = shape
-        self.h = lib.nnref_decoder_new(shape.vocab, shape.d_model, shape.n_heads, shape.d_ff,
-                                       shape.n_layers, shape.max_seq_len)
+        dims = (shape.vocab, shape.d_model, shape.n_heads, shape.d_ff, shape.n_layers, shape.max_seq_len)
+        self.h = lib.nnref_decoder_new_on(backend.h, *dims) if backend is not None else lib.nnref_decoder_new(*dims)
         if not self.h:
-            _ref_check(-1)
+            _ref_check(-1, lib)
         n = lib.nnref_num_params(self.h)
         if n != len(params):
             raise ValueError(f"reference has {n} parameters, got {len(params)}")
         for i, p in enumerate(params):
             a = np.ascontiguousarray(p, np.float32).ravel()
-            _ref_check(lib.nnref_set_param(self.h, i, a, a.size))
+            _ref_check(lib.nnref_set_param(self.h, i, a, a.size), lib)
         lib.nnref_set_requires_grad(self.h, 1 if requires_grad else 0)
+
+    def _chk(self, rc: int) -> None:
+        _ref_check(rc, self._lib)
 
     def __del__(self):
         if getattr(self, "h", None):
-            _RefLib.get().nnref_decoder_free(self.h)
+            self._lib.nnref_decoder_free(self.h)
             self.h = None
 
     def forward(self, tokens: Sequence[int]) -> np.ndarray:
         t = np.ascontiguousarray(tokens, np.int64)
         out = np.zeros((t.size, self.shape.vocab), np.float32)
-        _ref_check(_RefLib.get().nnref_forward(self.h, t, t.size, out))
+        self._chk(self._lib.nnref_forward(self.h, t, t.size, out))
         return out
 
     def save_weights(self, path: str) -> None:
         """Layer::save_weights: the reference's NETW v1 parameter file."""
-        _ref_check(_RefLib.get().nnref_save_weights(self.h, os.fsencode(path)))
+        self._chk(self._lib.nnref_save_weights(self.h, os.fsencode(path)))
 
     def load_weights(self, path: str) -> None:
-        _ref_check(_RefLib.get().nnref_load_weights(self.h, os.fsencode(path)))
+        self._chk(self._lib.nnref_load_weights(self.h, os.fsencode(path)))
 
     def _tokens_call(self, fn, prompt, max_new, *args):
         p = np.ascontiguousarray(prompt, np.int64)
         out = np.zeros(p.size + max_new, np.int64)
         n = C.c_size_t(0)
-        _ref_check(fn(self.h, *args[:1], p, p.size, max_new, *args[1:], out, out.size, C.byref(n)))
+        self._chk(fn(self.h, *args[:1], p, p.size, max_new, *args[1:], out, out.size, C.byref(n)))
         return out[: n.value]
 
     def generate(self, prompt, max_new):
-        lib = _RefLib.get()
+        lib = self._lib
         p = np.ascontiguousarray(prompt, np.int64)
         out = np.zeros(p.size + max_new, np.int64)
         n = C.c_size_t(0)
-        _ref_check(lib.nnref_generate(self.h, p, p.size, max_new, out, out.size, C.byref(n)))
+        self._chk(lib.nnref_generate(self.h, p, p.size, max_new, out, out.size, C.byref(n)))
         return out[: n.value]
 
     def generate_advanced(self, prompt, max_new, temperature=1.0, top_k=0, top_p=1.0, seed=42,
                           use_kv_cache=True):
-        lib = _RefLib.get()
+        lib = self._lib
         p = np.ascontiguousarray(prompt, np.int64)
         out = np.zeros(p.size + max_new, np.int64)
         n = C.c_size_t(0)
-        _ref_check(lib.nnref_generate_advanced(self.h, p, p.size, max_new, temperature, top_k, top_p,
+        self._chk(lib.nnref_generate_advanced(self.h, p, p.size, max_new, temperature, top_k, top_p,
                                                seed, 1 if use_kv_cache else 0, out, out.size, C.byref(n)))
         return out[: n.value]
 
     def generate_speculative(self, draft: "Reference", prompt, max_new, lookahead=4, temperature=1.0,
                              top_k=0, top_p=1.0, seed=42, quantized_cache=False):
-        lib = _RefLib.get()
+        lib = self._lib
         p = np.ascontiguousarray(prompt, np.int64)
         out = np.zeros(p.size + max_new, np.int64)
         n = C.c_size_t(0)
-        _ref_check(lib.nnref_generate_speculative(self.h, draft.h, p, p.size, max_new, lookahead,
+        self._chk(lib.nnref_generate_speculative(self.h, draft.h, p, p.size, max_new, lookahead,
                                                   temperature, top_k, top_p, seed,
                                                   1 if quantized_cache else 0, out, out.size, C.byref(n)))
         return out[: n.value]

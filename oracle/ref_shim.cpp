@@ -18,9 +18,16 @@
 //
 // Every entry returns 0 on success and -1 when the reference threw; the
 // message is then available from nnref_last_error().
+//
+// Built with NNREF_CUDA (oracle/_ref/libnnref_cuda.so, the reference library
+// with the B200 dispatch of oracle/binding/) it also makes decoders on a
+// CudaSpecBackend, so the same calls reach libspecdec_b200.so.
 #include "core/tensor.hpp"
 #include "nn/layer.hpp"
 #include "nn/quantization.hpp"
+#ifdef NNREF_CUDA
+#include "cuda_spec_backend.hpp"
+#endif
 
 #include <cstdint>
 #include <cstring>
@@ -84,6 +91,33 @@ void *nnref_decoder_new(size_t vocab, size_t d_model, size_t n_heads,
 }
 
 void nnref_decoder_free(void *h) { delete static_cast<RefModel *>(h); }
+
+#ifdef NNREF_CUDA
+// A CudaSpecBackend for decoders of the given target / draft shapes (the
+// fields of specdec_config after draft_shares_target are taken as given).
+void *nnref_cuda_backend_new(const specdec_config *cfg, int device) {
+  CudaSpecBackend *be = nullptr;
+  int rc = guard([&] { be = new CudaSpecBackend(*cfg, device); });
+  return rc == 0 ? be : nullptr;
+}
+void nnref_cuda_backend_free(void *be) { delete static_cast<CudaSpecBackend *>(be); }
+long long nnref_cuda_backend_launches(void *be) { return static_cast<CudaSpecBackend *>(be)->last_launches(); }
+
+// TransformerDecoder constructed on the backend (include/nn/layer.hpp:301-303).
+void *nnref_decoder_new_on(void *be, size_t vocab, size_t d_model, size_t n_heads, size_t d_ff, size_t n_layers,
+                           size_t max_seq_len) {
+  RefModel *m = nullptr;
+  int rc = guard([&] {
+    auto rm = std::make_unique<RefModel>();
+    rm->dec = std::make_unique<TransformerDecoder>(vocab, d_model, n_heads, d_ff, n_layers, max_seq_len,
+                                                   static_cast<CudaSpecBackend *>(be));
+    rm->params = rm->dec->parameters();
+    rm->vocab = vocab;
+    m = rm.release();
+  });
+  return rc == 0 ? m : nullptr;
+}
+#endif
 
 int nnref_num_params(void *h) {
   return static_cast<int>(static_cast<RefModel *>(h)->params.size());
