@@ -43,6 +43,7 @@
 #include "tree.cuh"
 #include "kern_table.cuh"
 #include "attn_dec.cuh"
+#include "gemm_w8.cuh"
 
 using namespace specdec;
 
@@ -295,6 +296,8 @@ struct specdec_handle {
   // row batches that take the tensor-core GEMM instead of the GEMV: at least
   // gemm_min_rows rows, or gemm_wide_rows rows of a layer with at least
   // gemm_wide_elems weights
+  bool gemm_w8 = true;  // tensor-core GEMM on the int8 codes for row batches of at most kW8MaxRows
+  int w8_clusters[kW8MaxSplit + 1] = {};  // its split-K clusters of ks CTAs resident at once
   int gemm_min_rows = kGemmMinRows;
   int gemm_wide_rows = 16;
   long long gemm_wide_elems = 2ll << 20;  // measured: the medium model's FFN down-projection (2.4M) at 32 rows
@@ -854,9 +857,71 @@ bool try_launch_gemm(specdec_handle *h, LinearArgs a) {
   return true;
 }
 
+// 2-D TMA view [N][K] of int8 weight codes (output-major), box 64 x 128, no
+// swizzle (the converter warps read it, not the tensor cores).
+CUtensorMap w8_operand_map(const void *base, int K, int N) {
+  if (K % 16 != 0 || (reinterpret_cast<uintptr_t>(base) & 15) != 0)
+    fail(SPECDEC_ERR_UNSUPPORTED, "int8 GEMM operands need 16-byte aligned rows");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(K)};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(kW8Feat)};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = tensor_map_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims,
+                                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) fail(SPECDEC_ERR_CUDA, "cuTensorMapEncodeTiled failed with " + std::to_string(static_cast<int>(r)));
+  return m;
+}
+
+// The int8-code tensor-core path (gemm_w8.cu): bf16 activations, int8
+// weights, at most kW8MaxRows rows, the same row-count routing as the bf16
+// image GEMM.  An input LayerNorm runs first as its own kernel (ln_rows), as
+// for that GEMM.
+template <int EPI>
+bool try_launch_gemm_w8(specdec_handle *h, LinearArgs a) {
+  const bool wide = a.R >= h->gemm_wide_rows && static_cast<long long>(a.N) * a.K >= h->gemm_wide_elems;
+  if (!h->gemm_w8 || !act_bf16(h) || !w_int8(h) || a.R > kW8MaxRows) return false;
+  if ((a.R < h->gemm_min_rows && !wide) || (a.K % 16) != 0) return false;
+  if (a.in_g && !ln_rows_ok(a)) return false;
+  if (EPI == kEpiSwiGLU && a.N % 2 != 0) return false;
+  if (EPI == kEpiQKV && (a.qkv.D % 2 != 0)) return false;
+  if (!a.in_g && a.in_rows) return false;  // row gathers only come with a LayerNorm
+  const void *A = a.x;
+  int lda = a.ldx;
+  if (a.in_g) {
+    void *dst = a.norm_out ? a.norm_out : h->X1;
+    launch_ln_rows(h, a, dst);
+    A = dst;
+    lda = a.K;
+  }
+  GemmW8Args g{};
+  g.np = (a.R + 15) / 16 * 16;
+  g.stages = gemm_w8_stages(g.np);
+  g.tma_x = gemm_operand_map(A, a.K, a.R, lda, g.np);
+  g.tma_w = w8_operand_map(a.W, a.K, a.N);
+  a.in_g = a.in_b = nullptr;
+  a.in_rows = nullptr;
+  a.norm_out = nullptr;
+  g.lin = a;
+  g.err = h->st.err;
+  const int tiles = (a.N + kW8Feat - 1) / kW8Feat;
+  const int nk = (a.K + 63) / 64;
+  int ks = 1;
+  while (h->gemm_ws && 2 * ks <= kW8MaxSplit && tiles * 2 * ks <= h->num_sms && 4 * ks <= nk &&
+         tiles <= h->w8_clusters[2 * ks])
+    ks *= 2;
+  g.ksplit = ks;
+  g.ws = h->gemm_ws;
+  CK(gemm_w8_launch(EPI, g, tiles, h->stream, h->use_pdl));
+  ++h->launches;
+  return true;
+}
+
 template <int EPI>
 void launch_linear(specdec_handle *h, LinearArgs a) {
   if (a.R <= 0) return;
+  if (try_launch_gemm_w8<EPI>(h, a)) return;
   if (try_launch_gemm<EPI>(h, a)) return;
   const int E = w_int8(h) ? WVec<int8_t>::E : WVec<float>::E;
   const int nc = pick_ncols(a.N, a.R, a.K, E, h->num_sms);
@@ -1814,6 +1879,8 @@ int create_impl(const specdec_config *cfg, int device, int rank, int world, cons
     if (const char *e = std::getenv("SPECDEC_ATTN_TC_MIN_Q")) h->attn_tc_min_q = std::max(1, std::atoi(e));
     CK(cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAtcSmem));
     CK(attn_dec_set_attrs());
+    CK(gemm_w8_set_attrs(h->w8_clusters));
+    if (const char *e = std::getenv("SPECDEC_GEMM_W8")) h->gemm_w8 = std::atoi(e) != 0;  // 0: the bf16-image GEMM
     if (const char *e = std::getenv("SPECDEC_ATTN_DEC")) h->attn_dec = std::atoi(e) != 0;  // 0: not the decode kernel
     // GEMV / GEMM routing thresholds, for tuning measurements
     if (const char *e = std::getenv("SPECDEC_GEMM_MIN_ROWS")) h->gemm_min_rows = std::max(1, std::atoi(e));

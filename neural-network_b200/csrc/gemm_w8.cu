@@ -1,0 +1,385 @@
+// Linear layer y = x . W + b on tcgen05 for the row batches of a speculative
+// round -- draft steps (32 rows on the large configuration) and verify blocks
+// (k + 1 rows per request: 160) -- reading the int8 weight codes themselves
+// (QuantizedDense, src/nn/quantization.cpp:7-147: y = x . (q * s) + b).
+//
+// These batches are far below the 128 rows of an MMA's M side, so the
+// product is taken transposed: D^T = W x^T with the output features on M
+// (128 per CTA) and the rows on N (the batch rounded up to 16, at most 256):
+//   A = 128 weight rows x 64 K as bf16: the int8 tile arrives by TMA (8 KB)
+//       and four converter warps write its exact bf16 values (|q| <= 127)
+//       into a 128-byte-swizzled K-major tile
+//   B = the input rows [np][64 K] by TMA, 128-byte swizzle, K-major
+//   D = fp32 in TMEM, lane = feature, column = row
+// so every weight byte crosses HBM once per pass, whatever the row count (a
+// tile of rows on M would re-read the weights for every 128 rows, and the
+// bf16 image of the codes doubles the bytes).  The per-column scale is
+// applied in the epilogue: sum(x * q) * s, the reassociation the GEMV uses.
+//
+// Warp 0 streams (weights, rows) stage pairs through the ring, warp 1 issues
+// the MMAs (4 per 64-wide k-block), warps 2-5 convert and then run the
+// epilogue with thread = feature: for each row the 128 threads of a CTA
+// write 128 consecutive outputs (coalesced), and the pair operations (RoPE
+// pairs, SwiGLU gate/up pairs, interleaved by the loader) meet through a
+// lane shuffle.  Few feature tiles (the 4096-wide residual layers) split K
+// over a cluster along y: partials meet in an L2-resident workspace, and
+// after the cluster barrier rank z sums its slice of the rows in rank order
+// (the same sum on every run).  Every mbarrier wait is bounded; a timeout
+// raises kErrTimeout and the CTA still joins its cluster barriers.
+#include <algorithm>
+
+#include "gemm.cuh"
+#include "gemm_w8.cuh"
+
+namespace specdec {
+
+namespace {
+
+constexpr int kW8Threads = 192;
+constexpr int kW8WBytes = kW8Feat * 64;       // int8 tile: 128 rows x 64 K
+constexpr int kW8ABytes = kW8Feat * 64 * 2;   // its bf16 image: 128 rows x 128 bytes
+constexpr int kW8SmemBudget = 200 * 1024;
+
+
+__device__ __forceinline__ void mbar_arrive_w8(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// 16 int8 codes -> their bf16 values (exact): the 2^23 bias trick of the
+// GEMV (i8x4_to_f32), then round-to-nearest pairs (exact for |q| <= 127).
+__device__ __forceinline__ void i8x16_to_bf16(uint4 u, uint4 &lo, uint4 &hi) {
+  float f[16];
+  i8x4_to_f32(u.x, f);
+  i8x4_to_f32(u.y, f + 4);
+  i8x4_to_f32(u.z, f + 8);
+  i8x4_to_f32(u.w, f + 12);
+  lo = f32x8_to_bf16(f);
+  hi = f32x8_to_bf16(f + 8);
+}
+
+// The epilogue of one (row, feature) value, thread = feature f (lane pairs
+// are feature pairs); v is acc * s + b.  Arithmetic as linear_epilogue.
+template <int EPI>
+__device__ __forceinline__ void w8_epilogue(const LinearArgs &a, int r, int f, bool fok, float v, int req, int pos,
+                                            int slot, int lane) {
+  using AT = __nv_bfloat16;
+  if constexpr (EPI == kEpiStore || EPI == kEpiResid || EPI == kEpiGelu) {
+    if (!fok) return;
+    if constexpr (EPI == kEpiResid) v = v + __bfloat162float(static_cast<const AT *>(a.resid)[static_cast<size_t>(r) * a.ldr + f]);
+    if constexpr (EPI == kEpiGelu) v = 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+    if (a.out_f32) static_cast<float *>(a.out)[static_cast<size_t>(r) * a.ldo + f] = v;
+    else static_cast<AT *>(a.out)[static_cast<size_t>(r) * a.ldo + f] = __float2bfloat16_rn(v);
+  } else if constexpr (EPI == kEpiSwiGLU) {
+    // SwiGLU::forward (src/nn/layer.cpp:1704-1710) on the interleaved pair
+    // (gate = feature 2c, up = 2c + 1)
+    const float u = __shfl_xor_sync(0xffffffffu, v, 1);
+    if (fok && (lane & 1) == 0) {
+      const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v)));
+      static_cast<AT *>(a.out)[static_cast<size_t>(r) * a.ldo + (f >> 1)] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(v, sg), u));
+    }
+  } else if constexpr (EPI == kEpiQKV) {
+    const QKVArgs &q = a.qkv;
+    const float other = __shfl_xor_sync(0xffffffffu, v, 1);
+    if (req < 0 || !fok) return;  // req is the row's: uniform over the CTA
+    if (pos < 0 || pos >= q.rope_max_pos || slot < 0 || slot >= q.S_cap) {
+      if (q.err && f == 0) atomicOr(q.err, kErrSeqLen);
+      return;
+    }
+    if (f < q.d + q.kvd) {
+      // Tensor::rope (src/core/tensor.cpp:1144-1163) on pairs (2j, 2j+1)
+      const int e = (f < q.d ? f : f - q.d) % q.D;
+      const float2 cs = __ldg(q.rope + static_cast<size_t>(pos) * (q.D / 2) + (e >> 1));
+      const float v0 = (lane & 1) ? other : v, v1 = (lane & 1) ? v : other;
+      v = (lane & 1) ? __fadd_rn(__fmul_rn(v0, cs.y), __fmul_rn(v1, cs.x))
+                     : __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y));
+    }
+    if (f < q.d) {
+      static_cast<AT *>(a.out)[static_cast<size_t>(r) * a.ldo + f] = __float2bfloat16_rn(v);
+    } else {
+      const bool is_k = f < q.d + q.kvd;
+      const int nn = is_k ? f - q.d : f - q.d - q.kvd;
+      const int h = nn / q.D, e = nn % q.D;
+      const size_t off = static_cast<size_t>(req) * q.kv_req_stride + (static_cast<size_t>(h) * q.S_cap + slot) * q.D + e;
+      if (q.kv_mode == 2) q.stage[static_cast<size_t>(r) * 2 * q.kvd + (is_k ? 0 : q.kvd) + nn] = v;
+      else if (q.kv_mode == 1) static_cast<AT *>(is_k ? q.kc : q.vc)[off] = __float2bfloat16_rn(v);
+      else static_cast<float *>(is_k ? q.kc : q.vc)[off] = v;
+    }
+  }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kW8Threads, 1) gemm_w8_kernel(const __grid_constant__ GemmW8Args g) {
+  extern __shared__ unsigned char w8_smem_raw[];
+  unsigned char *ring =
+      reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(w8_smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int kMaxStages = 8;
+  __shared__ __align__(8) uint64_t full[kMaxStages], conv[kMaxStages], empty[kMaxStages], done;
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_fail;
+  __shared__ int s_req[kW8MaxRows], s_pos[kW8MaxRows], s_slot[kW8MaxRows];
+
+  const LinearArgs &a = g.lin;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = g.stages, np = g.np;
+  const int sbytes = kW8WBytes + kW8ABytes + np * 128;
+  const int n0 = blockIdx.x * kW8Feat;
+  const int nk_all = (a.K + 63) / 64;
+  const int ks = g.ksplit, z = blockIdx.y;  // the cluster spans y only: rank = z
+  const int kb0 = z * nk_all / ks;
+  const int nk = (z + 1) * nk_all / ks - kb0;
+  // TMEM: np fp32 columns, allocated as a power of two of at least 32
+  const uint32_t tcols = np <= 32 ? 32u : np <= 64 ? 64u : np <= 128 ? 128u : 256u;
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                 "r"(tcols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (threadIdx.x == 32) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&conv[s], 4);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&done, 1);
+    s_fail = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  // kind::f16, D fp32, A and B bf16, both K-major, M = 128, N = np
+  const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(np >> 3) << 17) |
+                         (static_cast<uint32_t>(kW8Feat >> 4) << 24);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // producer: the weight tiles of the first stages before the
+      // predecessor has finished (they do not depend on it), then the rows
+      const int first = min(S, nk);
+      for (int kb = 0; kb < first; ++kb) {
+        unsigned char *st = ring + kb * sbytes;
+        mbar_expect_tx(&full[kb], kW8WBytes + np * 128);
+        tma_load_2d(st, &g.tma_w, (kb0 + kb) * 64, n0, &full[kb]);
+      }
+      pdl_wait();
+      for (int kb = 0; kb < first; ++kb)
+        tma_load_2d(ring + kb * sbytes + kW8WBytes + kW8ABytes, &g.tma_x, (kb0 + kb) * 64, 0, &full[kb]);
+      for (int kb = first; kb < nk; ++kb) {
+        const int s = kb % S;
+        if (!mbar_wait(&empty[s], ((kb / S) - 1) & 1)) {
+          s_fail = 1;
+          break;
+        }
+        unsigned char *st = ring + s * sbytes;
+        mbar_expect_tx(&full[s], kW8WBytes + np * 128);
+        tma_load_2d(st, &g.tma_w, (kb0 + kb) * 64, n0, &full[s]);
+        tma_load_2d(st + kW8WBytes + kW8ABytes, &g.tma_x, (kb0 + kb) * 64, 0, &full[s]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // MMA issuer: four K = 16 products per k-block
+      bool ok = true;
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % S;
+        const uint32_t ph = (kb / S) & 1;
+        if (!mbar_wait(&full[s], ph) || !mbar_wait(&conv[s], ph)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(ring + s * sbytes + kW8WBytes);
+        const uint32_t sb = sa + kW8ABytes;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          tc_mma(tmem, umma_desc_k128(sa + 32 * k), umma_desc_k128(sb + 32 * k), idesc, (kb | k) ? 1u : 0u);
+        tc_commit(&empty[s]);  // the stage is free once these products have read it
+      }
+      if (!ok) s_fail = 1;
+      tc_commit(&done);
+    }
+  } else {
+    // converters: int8 tile -> bf16 tile in the 128-byte-swizzled K-major
+    // layout (row r's 16-byte unit c at unit c ^ (r & 7))
+    const int t = threadIdx.x - 64;
+    bool ok = true;
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % S;
+      ok = ok && mbar_wait(&full[s], (kb / S) & 1);
+      const unsigned char *w8 = ring + s * sbytes;
+      unsigned char *a16 = ring + s * sbytes + kW8WBytes;
+#pragma unroll
+      for (int j = 0; j < kW8WBytes / 16 / 128; ++j) {
+        const int u = t + 128 * j;          // 16-byte unit of the int8 tile
+        const int r = u >> 2, c = (u & 3) * 2;  // row, first bf16 unit
+        uint4 lo, hi;
+        i8x16_to_bf16(*reinterpret_cast<const uint4 *>(w8 + u * 16), lo, hi);
+        *reinterpret_cast<uint4 *>(a16 + r * 128 + ((c ^ (r & 7)) << 4)) = lo;
+        *reinterpret_cast<uint4 *>(a16 + r * 128 + (((c + 1) ^ (r & 7)) << 4)) = hi;
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive_w8(&conv[s]);
+    }
+    if (!ok) s_fail = 1;
+    // row metadata of the QKV epilogue, while the products finish
+    pdl_wait();
+    if constexpr (EPI == kEpiQKV) {
+      for (int r = t; r < a.R; r += 128) {
+        s_req[r] = a.rows.req[r];
+        s_pos[r] = a.rows.pos[r];
+        s_slot[r] = row_slot(a.rows, r);
+      }
+    }
+  }
+  __syncthreads();
+  pdl_launch();
+
+  // epilogue: warps 2-5, thread = feature (its TMEM lane)
+  const bool epi_warp = warp >= 2;
+  const int qd = warp & 3;
+  const int f = n0 + 32 * qd + lane;
+  const bool fok = f < a.N;
+  const uint32_t tl = tmem + (static_cast<uint32_t>(32 * qd) << 16);
+  bool ok = true;
+  if (epi_warp) {
+    ok = __all_sync(0xffffffffu, mbar_wait(&done, 0) ? 1 : 0) != 0;  // tcgen05.ld is warp-collective
+    tc_fence_after();
+  }
+  const float sc = (epi_warp && fok && a.scale) ? __ldg(a.scale + f) : 1.f;
+  const float bi = (epi_warp && fok) ? __ldg(a.bias + f) : 0.f;
+  if (ks == 1) {
+    if (epi_warp && ok && !s_fail) {
+      for (int r0 = 0; r0 < a.R; r0 += 16) {
+        float v[16];
+        tmem_ld16(tl + r0, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int r = r0 + i;
+          if (r >= a.R) break;  // uniform
+          const int req = EPI == kEpiQKV ? s_req[r] : 0, pos = EPI == kEpiQKV ? s_pos[r] : 0;
+          const int slot = EPI == kEpiQKV ? s_slot[r] : 0;
+          w8_epilogue<EPI>(a, r, f, fok, v[i] * sc + bi, req, pos, slot, lane);
+        }
+      }
+    }
+  } else {
+    // split-K: partial [row][feature] of every rank (128 threads write 512
+    // contiguous bytes per row), the cluster barrier, then rank z sums rows
+    // [z R / ks, (z + 1) R / ks) over the ranks in order
+    const size_t tile = blockIdx.x;
+    if (epi_warp) {
+      float *mine = g.ws + (tile * ks + z) * static_cast<size_t>(np) * kW8Feat + 32 * qd + lane;
+      for (int r0 = 0; r0 < a.R; r0 += 16) {
+        float v[16];
+        tmem_ld16(tl + r0, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          if (r0 + i < a.R) mine[static_cast<size_t>(r0 + i) * kW8Feat] = (ok && !s_fail) ? v[i] : 0.f;
+      }
+      __threadfence();
+    }
+    cluster_sync_all();
+    if (epi_warp && ok && !s_fail) {
+      const float *part = g.ws + tile * ks * static_cast<size_t>(np) * kW8Feat + 32 * qd + lane;
+      const int r_lo = z * a.R / ks, r_hi = (z + 1) * a.R / ks;
+      for (int r = r_lo; r < r_hi; ++r) {
+        float acc = 0.f;
+        for (int zz = 0; zz < ks; ++zz) acc += __ldcg(part + (static_cast<size_t>(zz) * np + r) * kW8Feat);
+        const int req = EPI == kEpiQKV ? s_req[r] : 0, pos = EPI == kEpiQKV ? s_pos[r] : 0;
+        const int slot = EPI == kEpiQKV ? s_slot[r] : 0;
+        w8_epilogue<EPI>(a, r, f, fok, acc * sc + bi, req, pos, slot, lane);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && (s_fail || !ok) && g.err) atomicOr(g.err, kErrTimeout);
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tcols) : "memory");
+}
+
+template <int EPI>
+cudaError_t set_attr_epi() {
+  return cudaFuncSetAttribute(gemm_w8_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kW8SmemBudget + 1024);
+}
+
+template <int EPI>
+cudaError_t launch_epi(const GemmW8Args &g, int tiles, cudaStream_t stream, bool pdl) {
+  cudaLaunchConfig_t lc{};
+  lc.gridDim = dim3(tiles, g.ksplit, 1);
+  lc.blockDim = dim3(kW8Threads);
+  lc.dynamicSmemBytes = gemm_w8_smem(g.np);
+  lc.stream = stream;
+  cudaLaunchAttribute at[2];
+  int na = 0;
+  if (g.ksplit > 1) {
+    at[na].id = cudaLaunchAttributeClusterDimension;
+    at[na].val.clusterDim.x = 1;
+    at[na].val.clusterDim.y = g.ksplit;
+    at[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (pdl) {
+    at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  lc.attrs = at;
+  lc.numAttrs = na;
+  return cudaLaunchKernelEx(&lc, gemm_w8_kernel<EPI>, g);
+}
+
+}  // namespace
+
+int gemm_w8_stages(int np) {
+  const int per = kW8WBytes + kW8ABytes + np * 128;
+  return std::max(2, std::min(8, kW8SmemBudget / per));
+}
+
+int gemm_w8_smem(int np) { return gemm_w8_stages(np) * (kW8WBytes + kW8ABytes + np * 128) + 1024; }
+
+cudaError_t gemm_w8_set_attrs(int *active) {
+  cudaError_t e = set_attr_epi<kEpiStore>();
+  if (e == cudaSuccess) e = set_attr_epi<kEpiResid>();
+  if (e == cudaSuccess) e = set_attr_epi<kEpiQKV>();
+  if (e == cudaSuccess) e = set_attr_epi<kEpiSwiGLU>();
+  if (e == cudaSuccess) e = set_attr_epi<kEpiGelu>();
+  if (e != cudaSuccess) return e;
+  for (int ks = 2; ks <= kW8MaxSplit; ks *= 2) {
+    cudaLaunchConfig_t lc{};
+    lc.gridDim = dim3(1, ks, 1);
+    lc.blockDim = dim3(kW8Threads);
+    lc.dynamicSmemBytes = kW8SmemBudget + 1024;
+    cudaLaunchAttribute at{};
+    at.id = cudaLaunchAttributeClusterDimension;
+    at.val.clusterDim.x = 1;
+    at.val.clusterDim.y = ks;
+    at.val.clusterDim.z = 1;
+    lc.attrs = &at;
+    lc.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_w8_kernel<kEpiResid>, &lc) != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+    active[ks] = n;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t gemm_w8_launch(int epi, const GemmW8Args &g, int tiles, cudaStream_t stream, bool pdl) {
+  switch (epi) {
+    case kEpiStore: return launch_epi<kEpiStore>(g, tiles, stream, pdl);
+    case kEpiResid: return launch_epi<kEpiResid>(g, tiles, stream, pdl);
+    case kEpiQKV: return launch_epi<kEpiQKV>(g, tiles, stream, pdl);
+    case kEpiSwiGLU: return launch_epi<kEpiSwiGLU>(g, tiles, stream, pdl);
+    case kEpiGelu: return launch_epi<kEpiGelu>(g, tiles, stream, pdl);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace specdec

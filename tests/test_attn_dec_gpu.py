@@ -98,3 +98,30 @@ def test_spec_batched_d128_kernels_agree(gpu_lib, oracle_built):
     compare_tokens(tc, to, mg, S, greedy=True, tol=BF16_GREEDY_GAP)
     on.engine.close()
     off.engine.close()
+
+
+@pytest.mark.parametrize("S", [16, 40, 96, 160, 256])
+def test_gemm_w8_forward(gpu_lib, oracle_built, S):
+    """The int8-code tensor-core GEMM (csrc/gemm_w8.cu: features on the MMA's
+    M side, rows on N) at row counts from a draft step to its 256-row limit,
+    against the oracle and against the bf16-image GEMM / GEMV it replaces."""
+    old = os.environ.get("SPECDEC_GEMM_W8")
+    try:
+        os.environ["SPECDEC_GEMM_W8"] = "0"
+        off = make_pair(D128, 1, seed=22, int8=True, act_bf16=True, kv_mode=1, max_prompt_len=256, max_batch=2)
+        os.environ["SPECDEC_GEMM_W8"] = "1"
+        on = make_pair(D128, 1, seed=22, int8=True, act_bf16=True, kv_mode=1, max_prompt_len=256, max_batch=2)
+    finally:
+        if old is None:
+            del os.environ["SPECDEC_GEMM_W8"]
+        else:
+            os.environ["SPECDEC_GEMM_W8"] = old
+    toks = make_prompts(1, S, D128.vocab, seed=60 + S)[0]
+    for role, om in ((sd.TARGET, on.target), (sd.DRAFT, on.draft)):
+        g = on.engine.forward_logits(role, toks)
+        c = off.engine.forward_logits(role, toks)
+        o = om.forward(toks, act_bf16=True, kv_mode=1)
+        assert rel_err(g, o) < BF16_REL, (S, role, rel_err(g, o))
+        assert rel_err(g, c) < KERNEL_REL, (S, role, rel_err(g, c))
+    on.engine.close()
+    off.engine.close()
