@@ -297,6 +297,7 @@ struct specdec_handle {
   // gemm_min_rows rows, or gemm_wide_rows rows of a layer with at least
   // gemm_wide_elems weights
   bool gemm_w8 = true;  // tensor-core GEMM on the int8 codes for row batches of at most kW8MaxRows
+  bool w8_bf16_image = false;  // that GEMM reads the codes' bf16 image instead (no conversion)
   int w8_clusters[kW8MaxSplit + 1] = {};  // its split-K clusters of ks CTAs resident at once
   int gemm_min_rows = kGemmMinRows;
   int gemm_wide_rows = 16;
@@ -899,7 +900,13 @@ bool try_launch_gemm_w8(specdec_handle *h, LinearArgs a) {
   g.np = (a.R + 15) / 16 * 16;
   g.stages = gemm_w8_stages(g.np);
   g.tma_x = gemm_operand_map(A, a.K, a.R, lda, g.np);
-  g.tma_w = w8_operand_map(a.W, a.K, a.N);
+  auto img = h->w_bf16.find(a.W);
+  if (h->w8_bf16_image && img != h->w_bf16.end()) {
+    g.w_bf16 = 1;
+    g.tma_w = gemm_operand_map(img->second, a.K, a.N, a.K, kW8Feat);
+  } else {
+    g.tma_w = w8_operand_map(a.W, a.K, a.N);
+  }
   a.in_g = a.in_b = nullptr;
   a.in_rows = nullptr;
   a.norm_out = nullptr;
@@ -1881,6 +1888,7 @@ int create_impl(const specdec_config *cfg, int device, int rank, int world, cons
     CK(attn_dec_set_attrs());
     CK(gemm_w8_set_attrs(h->w8_clusters));
     if (const char *e = std::getenv("SPECDEC_GEMM_W8")) h->gemm_w8 = std::atoi(e) != 0;  // 0: the bf16-image GEMM
+    if (const char *e = std::getenv("SPECDEC_W8_BF16_IMAGE")) h->w8_bf16_image = std::atoi(e) != 0;
     if (const char *e = std::getenv("SPECDEC_ATTN_DEC")) h->attn_dec = std::atoi(e) != 0;  // 0: not the decode kernel
     // GEMV / GEMM routing thresholds, for tuning measurements
     if (const char *e = std::getenv("SPECDEC_GEMM_MIN_ROWS")) h->gemm_min_rows = std::max(1, std::atoi(e));

@@ -575,7 +575,8 @@ __global__ void ln_rows_kernel(const __nv_bfloat16 *__restrict__ x, int ldx, con
   const uint4 *xr = reinterpret_cast<const uint4 *>(x + static_cast<size_t>(pr) * ldx);
   const int nv = K / 8;
   float v[NV][8];
-  float s = 0.f;
+  // eight independent partial sums per lane (no 8 NV-long dependent chain)
+  float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
     const int c = lane + 32 * j;
@@ -586,19 +587,24 @@ __global__ void ln_rows_kernel(const __nv_bfloat16 *__restrict__ x, int ldx, con
       for (int e = 0; e < 8; ++e) v[j][e] = 0.f;
     }
 #pragma unroll
-    for (int e = 0; e < 8; ++e) s += v[j][e];
+    for (int e = 0; e < 8; ++e) s8[e] += v[j][e];
   }
+  const float s = ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
   const float mean = __fdiv_rn(warp_sum(s), static_cast<float>(K));
-  float q = 0.f;
+  float q8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int j = 0; j < NV; ++j)
     if (lane + 32 * j < nv)
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const float df = v[j][e] - mean;
-        q = fmaf(df, df, q);
+        q8[e] = fmaf(df, df, q8[e]);
       }
+  const float q = ((q8[0] + q8[1]) + (q8[2] + q8[3])) + ((q8[4] + q8[5]) + (q8[6] + q8[7]));
   const float sd = sqrtf(__fdiv_rn(warp_sum(q), static_cast<float>(K)) + 1e-5f);
+  // bf16 outputs: the product by the reciprocal of sd differs from the
+  // quotient by at most one fp32 rounding, far below the output's bf16 rounding
+  const float rsd = __fdiv_rn(1.0f, sd);
   uint4 *y = reinterpret_cast<uint4 *>(out + static_cast<size_t>(r) * K);
   uint4 *no = norm_out ? reinterpret_cast<uint4 *>(norm_out + static_cast<size_t>(r) * K) : nullptr;
 #pragma unroll
@@ -611,7 +617,7 @@ __global__ void ln_rows_kernel(const __nv_bfloat16 *__restrict__ x, int ldx, con
       const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
       float o[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = __fadd_rn(__fmul_rn(__fdiv_rn(v[j][e] - mean, sd), gg[e]), bb[e]);
+      for (int e = 0; e < 8; ++e) o[e] = __fadd_rn(__fmul_rn(__fmul_rn(v[j][e] - mean, rsd), gg[e]), bb[e]);
       const uint4 w = f32x8_to_bf16(o);
       y[c] = w;
       if (no) no[c] = w;

@@ -35,7 +35,8 @@ namespace specdec {
 
 namespace {
 
-constexpr int kW8Threads = 192;
+constexpr int kW8Threads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 convert, then the epilogue
+constexpr int kW8Conv = 8;       // converter warps
 constexpr int kW8WBytes = kW8Feat * 64;       // int8 tile: 128 rows x 64 K
 constexpr int kW8ABytes = kW8Feat * 64 * 2;   // its bf16 image: 128 rows x 128 bytes
 constexpr int kW8SmemBudget = 200 * 1024;
@@ -45,16 +46,15 @@ __device__ __forceinline__ void mbar_arrive_w8(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// 16 int8 codes -> their bf16 values (exact): the 2^23 bias trick of the
-// GEMV (i8x4_to_f32), then round-to-nearest pairs (exact for |q| <= 127).
-__device__ __forceinline__ void i8x16_to_bf16(uint4 u, uint4 &lo, uint4 &hi) {
-  float f[16];
-  i8x4_to_f32(u.x, f);
-  i8x4_to_f32(u.y, f + 4);
-  i8x4_to_f32(u.z, f + 8);
-  i8x4_to_f32(u.w, f + 12);
-  lo = f32x8_to_bf16(f);
-  hi = f32x8_to_bf16(f + 8);
+// 4 int8 codes -> 4 bf16 values (exact) in two words: the 2^23 bias trick of
+// the GEMV (i8x4_to_f32) gives fp32 values whose low 16 mantissa bits are zero
+// (|q| <= 127 has at most 7 significant bits), so each bf16 is the upper half
+// of its fp32 word and a byte permute packs a pair -- no conversion unit.
+__device__ __forceinline__ uint2 i8x4_to_bf16x4(uint32_t word) {
+  float f[4];
+  i8x4_to_f32(word, f);
+  return make_uint2(__byte_perm(__float_as_uint(f[0]), __float_as_uint(f[1]), 0x7632),
+                    __byte_perm(__float_as_uint(f[2]), __float_as_uint(f[3]), 0x7632));
 }
 
 // The epilogue of one (row, feature) value, thread = feature f (lane pairs
@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(kW8Threads, 1) gemm_w8_kernel(const __grid_con
   if (threadIdx.x == 32) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&conv[s], 4);
+      mbar_init(&conv[s], kW8Conv);
       mbar_init(&empty[s], 1);
     }
     mbar_init(&done, 1);
@@ -159,10 +159,12 @@ __global__ void __launch_bounds__(kW8Threads, 1) gemm_w8_kernel(const __grid_con
       // producer: the weight tiles of the first stages before the
       // predecessor has finished (they do not depend on it), then the rows
       const int first = min(S, nk);
+      const int wbytes = g.w_bf16 ? kW8ABytes : kW8WBytes;
+      const int woff = g.w_bf16 ? kW8WBytes : 0;  // a bf16 image lands in the A slot directly
       for (int kb = 0; kb < first; ++kb) {
         unsigned char *st = ring + kb * sbytes;
-        mbar_expect_tx(&full[kb], kW8WBytes + np * 128);
-        tma_load_2d(st, &g.tma_w, (kb0 + kb) * 64, n0, &full[kb]);
+        mbar_expect_tx(&full[kb], wbytes + np * 128);
+        tma_load_2d(st + woff, &g.tma_w, (kb0 + kb) * 64, n0, &full[kb]);
       }
       pdl_wait();
       for (int kb = 0; kb < first; ++kb)
@@ -174,8 +176,8 @@ __global__ void __launch_bounds__(kW8Threads, 1) gemm_w8_kernel(const __grid_con
           break;
         }
         unsigned char *st = ring + s * sbytes;
-        mbar_expect_tx(&full[s], kW8WBytes + np * 128);
-        tma_load_2d(st, &g.tma_w, (kb0 + kb) * 64, n0, &full[s]);
+        mbar_expect_tx(&full[s], wbytes + np * 128);
+        tma_load_2d(st + woff, &g.tma_w, (kb0 + kb) * 64, n0, &full[s]);
         tma_load_2d(st + kW8WBytes + kW8ABytes, &g.tma_x, (kb0 + kb) * 64, 0, &full[s]);
       }
     }
@@ -186,7 +188,7 @@ __global__ void __launch_bounds__(kW8Threads, 1) gemm_w8_kernel(const __grid_con
       for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % S;
         const uint32_t ph = (kb / S) & 1;
-        if (!mbar_wait(&full[s], ph) || !mbar_wait(&conv[s], ph)) {
+        if (!mbar_wait(&full[s], ph) || (!g.w_bf16 && !mbar_wait(&conv[s], ph))) {
           ok = false;
           break;
         }
@@ -203,22 +205,22 @@ __global__ void __launch_bounds__(kW8Threads, 1) gemm_w8_kernel(const __grid_con
     }
   } else {
     // converters: int8 tile -> bf16 tile in the 128-byte-swizzled K-major
-    // layout (row r's 16-byte unit c at unit c ^ (r & 7))
+    // layout (row r's 16-byte unit c at unit c ^ (r & 7)); a thread takes
+    // 8-byte pieces (8 codes -> one 16-byte bf16 unit)
     const int t = threadIdx.x - 64;
     bool ok = true;
-    for (int kb = 0; kb < nk; ++kb) {
+    for (int kb = 0; kb < (g.w_bf16 ? 0 : nk); ++kb) {
       const int s = kb % S;
       ok = ok && mbar_wait(&full[s], (kb / S) & 1);
       const unsigned char *w8 = ring + s * sbytes;
       unsigned char *a16 = ring + s * sbytes + kW8WBytes;
 #pragma unroll
-      for (int j = 0; j < kW8WBytes / 16 / 128; ++j) {
-        const int u = t + 128 * j;          // 16-byte unit of the int8 tile
-        const int r = u >> 2, c = (u & 3) * 2;  // row, first bf16 unit
-        uint4 lo, hi;
-        i8x16_to_bf16(*reinterpret_cast<const uint4 *>(w8 + u * 16), lo, hi);
-        *reinterpret_cast<uint4 *>(a16 + r * 128 + ((c ^ (r & 7)) << 4)) = lo;
-        *reinterpret_cast<uint4 *>(a16 + r * 128 + (((c + 1) ^ (r & 7)) << 4)) = hi;
+      for (int j = 0; j < kW8WBytes / 8 / (32 * kW8Conv); ++j) {
+        const int u = t + 32 * kW8Conv * j;   // 8-byte piece of the int8 tile
+        const int r = u >> 3, c = u & 7;      // row, bf16 unit
+        const uint2 w = *reinterpret_cast<const uint2 *>(w8 + u * 8);
+        const uint2 lo = i8x4_to_bf16x4(w.x), hi = i8x4_to_bf16x4(w.y);
+        *reinterpret_cast<uint4 *>(a16 + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(lo.x, lo.y, hi.x, hi.y);
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
@@ -228,7 +230,7 @@ __global__ void __launch_bounds__(kW8Threads, 1) gemm_w8_kernel(const __grid_con
     // row metadata of the QKV epilogue, while the products finish
     pdl_wait();
     if constexpr (EPI == kEpiQKV) {
-      for (int r = t; r < a.R; r += 128) {
+      for (int r = t; r < a.R; r += 32 * kW8Conv) {
         s_req[r] = a.rows.req[r];
         s_pos[r] = a.rows.pos[r];
         s_slot[r] = row_slot(a.rows, r);
@@ -238,9 +240,11 @@ __global__ void __launch_bounds__(kW8Threads, 1) gemm_w8_kernel(const __grid_con
   __syncthreads();
   pdl_launch();
 
-  // epilogue: warps 2-5, thread = feature (its TMEM lane)
+  // epilogue: warps 2-9, thread = feature (its TMEM lane); the two
+  // warpgroups take alternate 16-row chunks
   const bool epi_warp = warp >= 2;
   const int qd = warp & 3;
+  const int grp = (warp - 2) >> 2;
   const int f = n0 + 32 * qd + lane;
   const bool fok = f < a.N;
   const uint32_t tl = tmem + (static_cast<uint32_t>(32 * qd) << 16);
@@ -253,7 +257,7 @@ __global__ void __launch_bounds__(kW8Threads, 1) gemm_w8_kernel(const __grid_con
   const float bi = (epi_warp && fok) ? __ldg(a.bias + f) : 0.f;
   if (ks == 1) {
     if (epi_warp && ok && !s_fail) {
-      for (int r0 = 0; r0 < a.R; r0 += 16) {
+      for (int r0 = 16 * grp; r0 < a.R; r0 += 32) {
         float v[16];
         tmem_ld16(tl + r0, v);
 #pragma unroll
@@ -273,7 +277,7 @@ __global__ void __launch_bounds__(kW8Threads, 1) gemm_w8_kernel(const __grid_con
     const size_t tile = blockIdx.x;
     if (epi_warp) {
       float *mine = g.ws + (tile * ks + z) * static_cast<size_t>(np) * kW8Feat + 32 * qd + lane;
-      for (int r0 = 0; r0 < a.R; r0 += 16) {
+      for (int r0 = 16 * grp; r0 < a.R; r0 += 32) {
         float v[16];
         tmem_ld16(tl + r0, v);
 #pragma unroll
@@ -286,7 +290,7 @@ __global__ void __launch_bounds__(kW8Threads, 1) gemm_w8_kernel(const __grid_con
     if (epi_warp && ok && !s_fail) {
       const float *part = g.ws + tile * ks * static_cast<size_t>(np) * kW8Feat + 32 * qd + lane;
       const int r_lo = z * a.R / ks, r_hi = (z + 1) * a.R / ks;
-      for (int r = r_lo; r < r_hi; ++r) {
+      for (int r = r_lo + grp; r < r_hi; r += 2) {
         float acc = 0.f;
         for (int zz = 0; zz < ks; ++zz) acc += __ldcg(part + (static_cast<size_t>(zz) * np + r) * kW8Feat);
         const int req = EPI == kEpiQKV ? s_req[r] : 0, pos = EPI == kEpiQKV ? s_pos[r] : 0;

@@ -20,6 +20,7 @@ struct alignas(64) GemmW8Args {
   int np;             // R rounded up to 16 (the MMA's N)
   int stages;         // depth of the TMA ring
   int ksplit;         // CTAs per feature tile along y (a cluster): 1, 2, 4 or 8
+  int w_bf16;         // 1: tma_w is the codes' bf16 image [N][K] (box 64 x 128, 128-byte swizzle), no conversion
   float *ws;          // split-K partials: [tile * ksplit + rank][np rows][128 features] fp32
   int *err;
 };

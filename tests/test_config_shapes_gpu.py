@@ -79,10 +79,14 @@ def test_config_shapes_match_oracle(gpu_lib, name):
     greedy = T <= 0
     exact, ties = compare_tokens(tok, g[f"{name}_tokens"], g[f"{name}_margins"], S, greedy=greedy,
                                  tol=BF16_GREEDY_GAP if greedy else BF16_SAMPLED_MARGIN)
-    # every request ends with max_new tokens; most agree with the oracle
-    # token for token (a fork needs a decision within the bf16 tolerance)
     assert exact + ties == B
-    assert exact >= B // 2, (exact, ties)
+    if greedy:
+        # greedy forks need a relative top-2 logit gap inside the bf16
+        # tolerance: most requests agree with the oracle token for token.
+        # Sampled draws over 32000 probabilities sit within the bf16
+        # tolerance of a CDF step almost every time, so there the contract
+        # is the near-tie rule alone.
+        assert exact >= B // 2, (exact, ties)
     if name == "large":
         for e in _ENGINES.values():
             e.close()
