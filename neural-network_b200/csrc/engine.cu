@@ -296,9 +296,13 @@ struct specdec_handle {
   // row batches that take the tensor-core GEMM instead of the GEMV: at least
   // gemm_min_rows rows, or gemm_wide_rows rows of a layer with at least
   // gemm_wide_elems weights
-  bool gemm_w8 = true;  // tensor-core GEMM on the int8 codes for row batches of at most kW8MaxRows
-  bool w8_bf16_image = false;  // that GEMM reads the codes' bf16 image instead (no conversion)
+  // tensor-core GEMM on the int8 codes for row batches of at most kW8MaxRows
+  // (opt-in: measured slower than the bf16-image GEMM on the large config)
+  bool gemm_w8 = false;
   int w8_clusters[kW8MaxSplit + 1] = {};  // its split-K clusters of ks CTAs resident at once
+  bool w8_bf16_image = false;  // that GEMM streams the codes' bf16 image instead (no conversion)
+  float *w8_ws = nullptr;  // its split-K partials: up to kW8WsTiles CTAs of kW8MaxRows x 128 fp32
+  static constexpr int kW8WsTiles = 2 * 148;
   int gemm_min_rows = kGemmMinRows;
   int gemm_wide_rows = 16;
   long long gemm_wide_elems = 2ll << 20;  // measured: the medium model's FFN down-projection (2.4M) at 32 rows
@@ -898,15 +902,11 @@ bool try_launch_gemm_w8(specdec_handle *h, LinearArgs a) {
   }
   GemmW8Args g{};
   g.np = (a.R + 15) / 16 * 16;
-  g.stages = gemm_w8_stages(g.np);
-  g.tma_x = gemm_operand_map(A, a.K, a.R, lda, g.np);
   auto img = h->w_bf16.find(a.W);
-  if (h->w8_bf16_image && img != h->w_bf16.end()) {
-    g.w_bf16 = 1;
-    g.tma_w = gemm_operand_map(img->second, a.K, a.N, a.K, kW8Feat);
-  } else {
-    g.tma_w = w8_operand_map(a.W, a.K, a.N);
-  }
+  g.w_bf16 = (h->w8_bf16_image && img != h->w_bf16.end()) ? 1 : 0;
+  gemm_w8_rings(g.np, g.w_bf16, &g.stages_w, &g.stages_x);
+  g.tma_x = gemm_operand_map(A, a.K, a.R, lda, g.np);
+  g.tma_w = g.w_bf16 ? gemm_operand_map(img->second, a.K, a.N, a.K, kW8Feat) : w8_operand_map(a.W, a.K, a.N);
   a.in_g = a.in_b = nullptr;
   a.in_rows = nullptr;
   a.norm_out = nullptr;
@@ -914,12 +914,16 @@ bool try_launch_gemm_w8(specdec_handle *h, LinearArgs a) {
   g.err = h->st.err;
   const int tiles = (a.N + kW8Feat - 1) / kW8Feat;
   const int nk = (a.K + 63) / 64;
+  // split K while the feature tiles leave SMs idle (one CTA per SM): the
+  // largest power of two that keeps every CTA in one wave and at least 4
+  // k-blocks per split
   int ks = 1;
-  while (h->gemm_ws && 2 * ks <= kW8MaxSplit && tiles * 2 * ks <= h->num_sms && 4 * ks <= nk &&
-         tiles <= h->w8_clusters[2 * ks])
-    ks *= 2;
+  if (h->w8_ws)
+    while (2 * ks <= kW8MaxSplit && tiles * 2 * ks <= std::min(h->num_sms, specdec_handle::kW8WsTiles) &&
+           4 * 2 * ks <= nk && tiles <= h->w8_clusters[2 * ks])
+      ks *= 2;
   g.ksplit = ks;
-  g.ws = h->gemm_ws;
+  g.ws = h->w8_ws;
   CK(gemm_w8_launch(EPI, g, tiles, h->stream, h->use_pdl));
   ++h->launches;
   return true;
@@ -1887,8 +1891,8 @@ int create_impl(const specdec_config *cfg, int device, int rank, int world, cons
     CK(cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAtcSmem));
     CK(attn_dec_set_attrs());
     CK(gemm_w8_set_attrs(h->w8_clusters));
-    if (const char *e = std::getenv("SPECDEC_GEMM_W8")) h->gemm_w8 = std::atoi(e) != 0;  // 0: the bf16-image GEMM
     if (const char *e = std::getenv("SPECDEC_W8_BF16_IMAGE")) h->w8_bf16_image = std::atoi(e) != 0;
+    if (const char *e = std::getenv("SPECDEC_GEMM_W8")) h->gemm_w8 = std::atoi(e) != 0;  // 1: the int8-code GEMM
     if (const char *e = std::getenv("SPECDEC_ATTN_DEC")) h->attn_dec = std::atoi(e) != 0;  // 0: not the decode kernel
     // GEMV / GEMM routing thresholds, for tuning measurements
     if (const char *e = std::getenv("SPECDEC_GEMM_MIN_ROWS")) h->gemm_min_rows = std::max(1, std::atoi(e));
@@ -1983,6 +1987,10 @@ int create_impl(const specdec_config *cfg, int device, int rank, int world, cons
     if (cfg->act_dtype == SPECDEC_BF16 && cfg->weight_dtype == SPECDEC_INT8 && h->gemm_max_split > 1)
       h->gemm_ws = static_cast<float *>(h->dalloc(static_cast<size_t>(h->num_sms) * kBM * kBN * sizeof(float)));
     h->logits_rows = R_round;
+    if (cfg->act_dtype == SPECDEC_BF16 && cfg->weight_dtype == SPECDEC_INT8) {
+      h->w8_ws = static_cast<float *>(
+          h->dalloc(static_cast<size_t>(specdec_handle::kW8WsTiles) * kW8MaxRows * kW8Feat * sizeof(float)));
+    }
     h->tree_base =
         h->R_max + 2 * B + (k - 1) * B + B * (k + 1);
     const size_t pool_rows = static_cast<size_t>(h->tree_base) +
@@ -2660,12 +2668,12 @@ extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const
     size_t tls, dls, trs, drs;
     int tcap, dcap, R_max;
     cudaStream_t stream;
-    float *gemm_ws, *ad_part;
+    float *gemm_ws, *ad_part, *w8_ws;
   };
   Saved sv{h->X, h->H, h->X1, h->A, h->Q, h->ATT, h->tk, h->tv, h->dk, h->dv, h->tks, h->tvs, h->dks, h->dvs, h->KVN,
            h->st.err, h->pool,
            h->t_layer_stride, h->d_layer_stride, h->t_req_stride, h->d_req_stride, h->t_cap, h->d_cap, h->R_max,
-           h->stream, h->gemm_ws, h->ad_part};
+           h->stream, h->gemm_ws, h->ad_part, h->w8_ws};
   auto restore = [&] {
     h->X = sv.X; h->H = sv.H; h->X1 = sv.X1; h->A = sv.A; h->Q = sv.Q; h->ATT = sv.ATT;
     h->tk = sv.tk; h->tv = sv.tv; h->dk = sv.dk; h->dv = sv.dv;
@@ -2673,7 +2681,7 @@ extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const
     h->st.err = sv.err; h->pool = sv.pool;
     h->t_layer_stride = sv.tls; h->d_layer_stride = sv.dls; h->t_req_stride = sv.trs; h->d_req_stride = sv.drs;
     h->t_cap = sv.tcap; h->d_cap = sv.dcap; h->R_max = sv.R_max; h->stream = sv.stream;
-    h->gemm_ws = sv.gemm_ws; h->ad_part = sv.ad_part;
+    h->gemm_ws = sv.gemm_ws; h->ad_part = sv.ad_part; h->w8_ws = sv.w8_ws;
   };
   try {
     CK(cudaSetDevice(h->device));
@@ -2742,6 +2750,7 @@ extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const
     // its own stream: this call uses neither (no split-K, no split attention)
     h->gemm_ws = nullptr;
     h->ad_part = nullptr;
+    h->w8_ws = nullptr;
     CK(cudaMemsetAsync(h->st.err, 0, sizeof(int), st));
     launch(h, plan_prefill_kernel, dim3((S + 255) / 256), dim3(256), 0, d_tokens, 1, S, 0, S, dm.V, h->pool.tok,
            h->pool.pos, h->pool.req, static_cast<int *>(nullptr));

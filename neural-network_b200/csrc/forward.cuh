@@ -642,19 +642,21 @@ __device__ __forceinline__ uint64_t global_ns() {
 }
 
 // Waits for an mbarrier phase for at most about a second; false = gave up.
-// Each try may suspend the thread until the phase completes, for at most the
-// hint (10 us), so waiting warps leave the issue slots to working ones.
+// A failed try sleeps for a few tens of nanoseconds before the next one, so
+// waiting warps leave the issue slots to the working ones (a warp that spins
+// on try_wait takes them from the producer and MMA threads of its SM).
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t phase) {
   const uint32_t addr = smem_u32(bar);
   uint64_t t0 = 0;
   for (uint32_t it = 0;; ++it) {
     uint32_t done;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(done)
-        : "r"(addr), "r"(phase), "r"(10000u)
+        : "r"(addr), "r"(phase)
         : "memory");
     if (done) return true;
+    __nanosleep(32);
     if ((it & 63) == 0) {
       const uint64_t now = global_ns();
       if (it == 0) t0 = now;

@@ -35,8 +35,11 @@ namespace specdec {
 
 namespace {
 
-constexpr int kW8Threads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 convert, then the epilogue
+constexpr int kW8Threads = 352;  // warp 0 weight TMA, warp 1 MMA, warp 2 row TMA, warps 3-10 convert + epilogue
 constexpr int kW8Conv = 8;       // converter warps
+constexpr int kW8RingA = 3;      // bf16 tiles between the converters and the MMAs
+constexpr int kW8MaxW = 16;      // int8 weight tiles in flight (the HBM stream)
+constexpr int kW8MaxX = 4;       // input-row tiles (L2-resident)
 constexpr int kW8WBytes = kW8Feat * 64;       // int8 tile: 128 rows x 64 K
 constexpr int kW8ABytes = kW8Feat * 64 * 2;   // its bf16 image: 128 rows x 128 bytes
 constexpr int kW8SmemBudget = 200 * 1024;
@@ -110,21 +113,25 @@ __device__ __forceinline__ void w8_epilogue(const LinearArgs &a, int r, int f, b
 template <int EPI>
 __global__ void __launch_bounds__(kW8Threads, 1) gemm_w8_kernel(const __grid_constant__ GemmW8Args g) {
   extern __shared__ unsigned char w8_smem_raw[];
-  unsigned char *ring =
+  unsigned char *base =
       reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(w8_smem_raw) + 1023) & ~uintptr_t(1023));
-  constexpr int kMaxStages = 8;
-  __shared__ __align__(8) uint64_t full[kMaxStages], conv[kMaxStages], empty[kMaxStages], done;
+  __shared__ __align__(8) uint64_t wfull[kW8MaxW], wempty[kW8MaxW], afull[kW8RingA], aempty[kW8RingA],
+      xfull[kW8MaxX], xempty[kW8MaxX], done;
   __shared__ uint32_t s_tmem;
   __shared__ int s_fail;
   __shared__ int s_req[kW8MaxRows], s_pos[kW8MaxRows], s_slot[kW8MaxRows];
 
   const LinearArgs &a = g.lin;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int S = g.stages, np = g.np;
-  const int sbytes = kW8WBytes + kW8ABytes + np * 128;
+  const int np = g.np, SW = g.stages_w, SX = g.stages_x;
+  const bool wb = g.w_bf16 != 0;                        // weights as bf16 tiles, straight to the MMAs
+  const int wslot = wb ? kW8ABytes : kW8WBytes;
+  unsigned char *wring = base;                          // SW weight tiles (8 KB int8 or 16 KB bf16)
+  unsigned char *aring = wring + SW * wslot;            // kW8RingA x 16 KB bf16 tiles (int8 weights)
+  unsigned char *xring = aring + (wb ? 0 : kW8RingA * kW8ABytes);  // SX x np rows of 128 bytes
   const int n0 = blockIdx.x * kW8Feat;
   const int nk_all = (a.K + 63) / 64;
-  const int ks = g.ksplit, z = blockIdx.y;  // the cluster spans y only: rank = z
+  const int ks = g.ksplit, z = blockIdx.y;
   const int kb0 = z * nk_all / ks;
   const int nk = (z + 1) * nk_all / ks - kb0;
   // TMEM: np fp32 columns, allocated as a power of two of at least 32
@@ -137,10 +144,17 @@ __global__ void __launch_bounds__(kW8Threads, 1) gemm_w8_kernel(const __grid_con
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   if (threadIdx.x == 32) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&conv[s], kW8Conv);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < SW; ++s) {
+      mbar_init(&wfull[s], 1);
+      mbar_init(&wempty[s], wb ? 1 : kW8Conv);  // bf16 tiles are freed by the MMAs' commit
+    }
+    for (int s = 0; s < kW8RingA; ++s) {
+      mbar_init(&afull[s], kW8Conv);
+      mbar_init(&aempty[s], 1);
+    }
+    for (int s = 0; s < SX; ++s) {
+      mbar_init(&xfull[s], 1);
+      mbar_init(&xempty[s], 1);
     }
     mbar_init(&done, 1);
     s_fail = 0;
@@ -156,29 +170,16 @@ __global__ void __launch_bounds__(kW8Threads, 1) gemm_w8_kernel(const __grid_con
 
   if (warp == 0) {
     if (lane == 0) {
-      // producer: the weight tiles of the first stages before the
-      // predecessor has finished (they do not depend on it), then the rows
-      const int first = min(S, nk);
-      const int wbytes = g.w_bf16 ? kW8ABytes : kW8WBytes;
-      const int woff = g.w_bf16 ? kW8WBytes : 0;  // a bf16 image lands in the A slot directly
-      for (int kb = 0; kb < first; ++kb) {
-        unsigned char *st = ring + kb * sbytes;
-        mbar_expect_tx(&full[kb], wbytes + np * 128);
-        tma_load_2d(st + woff, &g.tma_w, (kb0 + kb) * 64, n0, &full[kb]);
-      }
-      pdl_wait();
-      for (int kb = 0; kb < first; ++kb)
-        tma_load_2d(ring + kb * sbytes + kW8WBytes + kW8ABytes, &g.tma_x, (kb0 + kb) * 64, 0, &full[kb]);
-      for (int kb = first; kb < nk; ++kb) {
-        const int s = kb % S;
-        if (!mbar_wait(&empty[s], ((kb / S) - 1) & 1)) {
+      // weight producer: SW tiles ahead; the weights do not depend on the
+      // preceding kernel, so they stream before it has finished
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % SW;
+        if (kb >= SW && !mbar_wait(&wempty[s], ((kb / SW) - 1) & 1)) {
           s_fail = 1;
           break;
         }
-        unsigned char *st = ring + s * sbytes;
-        mbar_expect_tx(&full[s], wbytes + np * 128);
-        tma_load_2d(st + woff, &g.tma_w, (kb0 + kb) * 64, n0, &full[s]);
-        tma_load_2d(st + kW8WBytes + kW8ABytes, &g.tma_x, (kb0 + kb) * 64, 0, &full[s]);
+        mbar_expect_tx(&wfull[s], wslot);
+        tma_load_2d(wring + s * wslot, &g.tma_w, (kb0 + kb) * 64, n0, &wfull[s]);
       }
     }
   } else if (warp == 1) {
@@ -186,45 +187,68 @@ __global__ void __launch_bounds__(kW8Threads, 1) gemm_w8_kernel(const __grid_con
       // MMA issuer: four K = 16 products per k-block
       bool ok = true;
       for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % S;
-        const uint32_t ph = (kb / S) & 1;
-        if (!mbar_wait(&full[s], ph) || (!g.w_bf16 && !mbar_wait(&conv[s], ph))) {
+        const int sa = kb % kW8RingA, sx = kb % SX, sw = kb % SW;
+        const bool got = wb ? mbar_wait(&wfull[sw], (kb / SW) & 1) : mbar_wait(&afull[sa], (kb / kW8RingA) & 1);
+        if (!got || !mbar_wait(&xfull[sx], (kb / SX) & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t sa = smem_u32(ring + s * sbytes + kW8WBytes);
-        const uint32_t sb = sa + kW8ABytes;
+        const uint32_t ua = wb ? smem_u32(wring + sw * kW8ABytes) : smem_u32(aring + sa * kW8ABytes);
+        const uint32_t ux = smem_u32(xring + sx * np * 128);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          tc_mma(tmem, umma_desc_k128(sa + 32 * k), umma_desc_k128(sb + 32 * k), idesc, (kb | k) ? 1u : 0u);
-        tc_commit(&empty[s]);  // the stage is free once these products have read it
+          tc_mma(tmem, umma_desc_k128(ua + 32 * k), umma_desc_k128(ux + 32 * k), idesc, (kb | k) ? 1u : 0u);
+        // the slots are free once these products have read them
+        tc_commit(wb ? &wempty[sw] : &aempty[sa]);
+        tc_commit(&xempty[sx]);
       }
       if (!ok) s_fail = 1;
       tc_commit(&done);
+    }
+  } else if (warp == 2) {
+    if (lane == 0) {
+      // row producer: the input rows are the preceding kernel's output
+      pdl_wait();
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % SX;
+        if (kb >= SX && !mbar_wait(&xempty[s], ((kb / SX) - 1) & 1)) {
+          s_fail = 1;
+          break;
+        }
+        mbar_expect_tx(&xfull[s], np * 128);
+        tma_load_2d(xring + s * np * 128, &g.tma_x, (kb0 + kb) * 64, 0, &xfull[s]);
+      }
     }
   } else {
     // converters: int8 tile -> bf16 tile in the 128-byte-swizzled K-major
     // layout (row r's 16-byte unit c at unit c ^ (r & 7)); a thread takes
     // 8-byte pieces (8 codes -> one 16-byte bf16 unit)
-    const int t = threadIdx.x - 64;
+    const int t = threadIdx.x - 96;
     bool ok = true;
-    for (int kb = 0; kb < (g.w_bf16 ? 0 : nk); ++kb) {
-      const int s = kb % S;
-      ok = ok && mbar_wait(&full[s], (kb / S) & 1);
-      const unsigned char *w8 = ring + s * sbytes;
-      unsigned char *a16 = ring + s * sbytes + kW8WBytes;
+    for (int kb = 0; kb < (wb ? 0 : nk); ++kb) {
+      const int sw = kb % SW, sa = kb % kW8RingA;
+      ok = ok && mbar_wait(&wfull[sw], (kb / SW) & 1);
+      if (kb >= kW8RingA) ok = ok && mbar_wait(&aempty[sa], ((kb / kW8RingA) - 1) & 1);
+      const unsigned char *w8 = wring + sw * kW8WBytes;
+      unsigned char *a16 = aring + sa * kW8ABytes;
+      uint2 w[kW8WBytes / 8 / (32 * kW8Conv)];
+#pragma unroll
+      for (int j = 0; j < kW8WBytes / 8 / (32 * kW8Conv); ++j)
+        w[j] = *reinterpret_cast<const uint2 *>(w8 + (t + 32 * kW8Conv * j) * 8);
+      // the int8 slot is read: the producer may refill it
+      __syncwarp();
+      if (lane == 0) mbar_arrive_w8(&wempty[sw]);
 #pragma unroll
       for (int j = 0; j < kW8WBytes / 8 / (32 * kW8Conv); ++j) {
         const int u = t + 32 * kW8Conv * j;   // 8-byte piece of the int8 tile
         const int r = u >> 3, c = u & 7;      // row, bf16 unit
-        const uint2 w = *reinterpret_cast<const uint2 *>(w8 + u * 8);
-        const uint2 lo = i8x4_to_bf16x4(w.x), hi = i8x4_to_bf16x4(w.y);
+        const uint2 lo = i8x4_to_bf16x4(w[j].x), hi = i8x4_to_bf16x4(w[j].y);
         *reinterpret_cast<uint4 *>(a16 + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(lo.x, lo.y, hi.x, hi.y);
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
-      if (lane == 0) mbar_arrive_w8(&conv[s]);
+      if (lane == 0) mbar_arrive_w8(&afull[sa]);
     }
     if (!ok) s_fail = 1;
     // row metadata of the QKV epilogue, while the products finish
@@ -240,11 +264,11 @@ __global__ void __launch_bounds__(kW8Threads, 1) gemm_w8_kernel(const __grid_con
   __syncthreads();
   pdl_launch();
 
-  // epilogue: warps 2-9, thread = feature (its TMEM lane); the two
-  // warpgroups take alternate 16-row chunks
-  const bool epi_warp = warp >= 2;
+  // epilogue: the 8 converter warps, thread = feature (its TMEM lane); the
+  // two warpgroups take alternate 16-row chunks
+  const bool epi_warp = warp >= 3;
   const int qd = warp & 3;
-  const int grp = (warp - 2) >> 2;
+  const int grp = (warp - 3) >> 2;
   const int f = n0 + 32 * qd + lane;
   const bool fok = f < a.N;
   const uint32_t tl = tmem + (static_cast<uint32_t>(32 * qd) << 16);
@@ -253,10 +277,11 @@ __global__ void __launch_bounds__(kW8Threads, 1) gemm_w8_kernel(const __grid_con
     ok = __all_sync(0xffffffffu, mbar_wait(&done, 0) ? 1 : 0) != 0;  // tcgen05.ld is warp-collective
     tc_fence_after();
   }
+  const bool good = ok && !s_fail;
   const float sc = (epi_warp && fok && a.scale) ? __ldg(a.scale + f) : 1.f;
   const float bi = (epi_warp && fok) ? __ldg(a.bias + f) : 0.f;
   if (ks == 1) {
-    if (epi_warp && ok && !s_fail) {
+    if (epi_warp && good) {
       for (int r0 = 16 * grp; r0 < a.R; r0 += 32) {
         float v[16];
         tmem_ld16(tl + r0, v);
@@ -271,31 +296,42 @@ __global__ void __launch_bounds__(kW8Threads, 1) gemm_w8_kernel(const __grid_con
       }
     }
   } else {
-    // split-K: partial [row][feature] of every rank (128 threads write 512
-    // contiguous bytes per row), the cluster barrier, then rank z sums rows
-    // [z R / ks, (z + 1) R / ks) over the ranks in order
+    // split-K: every rank stores its partial [row][feature] (128 threads
+    // write 512 contiguous bytes per row), the cluster barrier, then rank z
+    // sums rows [z R / ks, (z + 1) R / ks) over the ranks in order (the same
+    // sum on every run), 8 rows per thread at a time
     const size_t tile = blockIdx.x;
+    const float *ws = g.ws + tile * ks * static_cast<size_t>(np) * kW8Feat + 32 * qd + lane;
     if (epi_warp) {
-      float *mine = g.ws + (tile * ks + z) * static_cast<size_t>(np) * kW8Feat + 32 * qd + lane;
+      float *mine = const_cast<float *>(ws) + static_cast<size_t>(z) * np * kW8Feat;
       for (int r0 = 16 * grp; r0 < a.R; r0 += 32) {
         float v[16];
         tmem_ld16(tl + r0, v);
 #pragma unroll
         for (int i = 0; i < 16; ++i)
-          if (r0 + i < a.R) mine[static_cast<size_t>(r0 + i) * kW8Feat] = (ok && !s_fail) ? v[i] : 0.f;
+          if (r0 + i < a.R) mine[static_cast<size_t>(r0 + i) * kW8Feat] = good ? v[i] : 0.f;
       }
       __threadfence();
     }
     cluster_sync_all();
-    if (epi_warp && ok && !s_fail) {
-      const float *part = g.ws + tile * ks * static_cast<size_t>(np) * kW8Feat + 32 * qd + lane;
+    if (epi_warp && good) {
       const int r_lo = z * a.R / ks, r_hi = (z + 1) * a.R / ks;
-      for (int r = r_lo + grp; r < r_hi; r += 2) {
-        float acc = 0.f;
-        for (int zz = 0; zz < ks; ++zz) acc += __ldcg(part + (static_cast<size_t>(zz) * np + r) * kW8Feat);
-        const int req = EPI == kEpiQKV ? s_req[r] : 0, pos = EPI == kEpiQKV ? s_pos[r] : 0;
-        const int slot = EPI == kEpiQKV ? s_slot[r] : 0;
-        w8_epilogue<EPI>(a, r, f, fok, acc * sc + bi, req, pos, slot, lane);
+      for (int rb = r_lo + 8 * grp; rb < r_hi; rb += 16) {
+        float acc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+        for (int zz = 0; zz < ks; ++zz)
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            if (rb + i < r_hi) acc[i] += __ldcg(ws + (static_cast<size_t>(zz) * np + rb + i) * kW8Feat);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int r = rb + i;
+          if (r >= r_hi) break;  // uniform
+          const int req = EPI == kEpiQKV ? s_req[r] : 0, pos = EPI == kEpiQKV ? s_pos[r] : 0;
+          const int slot = EPI == kEpiQKV ? s_slot[r] : 0;
+          w8_epilogue<EPI>(a, r, f, fok, acc[i] * sc + bi, req, pos, slot, lane);
+        }
       }
     }
   }
@@ -316,7 +352,7 @@ cudaError_t launch_epi(const GemmW8Args &g, int tiles, cudaStream_t stream, bool
   cudaLaunchConfig_t lc{};
   lc.gridDim = dim3(tiles, g.ksplit, 1);
   lc.blockDim = dim3(kW8Threads);
-  lc.dynamicSmemBytes = gemm_w8_smem(g.np);
+  lc.dynamicSmemBytes = gemm_w8_smem(g.np, g.w_bf16);
   lc.stream = stream;
   cudaLaunchAttribute at[2];
   int na = 0;
@@ -339,12 +375,20 @@ cudaError_t launch_epi(const GemmW8Args &g, int tiles, cudaStream_t stream, bool
 
 }  // namespace
 
-int gemm_w8_stages(int np) {
-  const int per = kW8WBytes + kW8ABytes + np * 128;
-  return std::max(2, std::min(8, kW8SmemBudget / per));
+// Ring depths for np rows: the row ring (L2-resident tiles) 3-4 deep, the
+// weight ring as deep as the rest of the budget allows (up to 16 tiles).
+void gemm_w8_rings(int np, int w_bf16, int *sw, int *sx) {
+  const int xb = np * 128;
+  *sx = np <= 64 ? 4 : 3;
+  const int left = kW8SmemBudget - (w_bf16 ? 0 : kW8RingA * kW8ABytes) - *sx * xb;
+  *sw = std::max(2, std::min(kW8MaxW, left / (w_bf16 ? kW8ABytes : kW8WBytes)));
 }
 
-int gemm_w8_smem(int np) { return gemm_w8_stages(np) * (kW8WBytes + kW8ABytes + np * 128) + 1024; }
+int gemm_w8_smem(int np, int w_bf16) {
+  int sw, sx;
+  gemm_w8_rings(np, w_bf16, &sw, &sx);
+  return sw * (w_bf16 ? kW8ABytes : kW8WBytes) + (w_bf16 ? 0 : kW8RingA * kW8ABytes) + sx * np * 128 + 1024;
+}
 
 cudaError_t gemm_w8_set_attrs(int *active) {
   cudaError_t e = set_attr_epi<kEpiStore>();

@@ -103,8 +103,9 @@ def test_spec_batched_d128_kernels_agree(gpu_lib, oracle_built):
 @pytest.mark.parametrize("S", [16, 40, 96, 160, 256])
 def test_gemm_w8_forward(gpu_lib, oracle_built, S):
     """The int8-code tensor-core GEMM (csrc/gemm_w8.cu: features on the MMA's
-    M side, rows on N) at row counts from a draft step to its 256-row limit,
-    against the oracle and against the bf16-image GEMM / GEMV it replaces."""
+    M side, rows on N; opt-in with SPECDEC_GEMM_W8=1) at row counts from a
+    draft step to its 256-row limit, against the oracle and against the
+    bf16-image GEMM / GEMV path."""
     old = os.environ.get("SPECDEC_GEMM_W8")
     try:
         os.environ["SPECDEC_GEMM_W8"] = "0"
