@@ -43,8 +43,8 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "neural-network_b200"))
 
-from specdec_b200.synth import (ARCH_CFG, ARCH_REF, device_params, draft_params, make_params,  # noqa: E402
-                                 make_prompts, workload)
+from specdec_b200.synth import (ARCH_CFG, ARCH_REF, device_param_tensors, device_params,  # noqa: E402
+                                 draft_params, make_params, make_prompts, workload)
 
 METRIC = "accepted tokens/sec per GPU (spec-decode, k=4) at 1/2/4/8 B200; % HBM roofline"
 UNIT = "tokens/s"
@@ -411,15 +411,23 @@ def cpu_baseline_sample(wl):
 
 
 def make_engine(sd, wl, local, large):
+    """The engine with seeded synthetic weights.  The large model's weights are
+    drawn on the GPU and loaded from there (quantised and transposed on the
+    device): every rank of a multi-GPU run would otherwise hold a 27 GB fp32
+    copy in host memory."""
     import torch
 
-    P = device_params(wl.target, 0, torch.device("cuda", local)) if large else make_params(wl.target, seed=0)
     eng = sd.Engine(wl.target, draft_layers=wl.draft_layers, weight_dtype=sd.INT8 if wl.weights_int8 else sd.F32,
                     act_dtype=sd.BF16 if wl.act_bf16 else sd.F32, kv_dtype=KV_DTYPE[wl.kv_mode],
                     max_batch=wl.batch, max_lookahead=wl.lookahead, max_prompt_len=wl.prompt_len, device=local,
                     max_tree_nodes=tree_nodes(wl.tree) if wl.tree else 0)
-    eng.load_params(sd.TARGET, P)
-    del P
+    if large:
+        P = device_param_tensors(wl.target, 0, torch.device("cuda", local))
+        eng.load_params_device(sd.TARGET, P)
+        del P
+        torch.cuda.empty_cache()
+    else:
+        eng.load_params(sd.TARGET, make_params(wl.target, seed=0))
     return eng
 
 

@@ -118,6 +118,15 @@ const char *specdec_last_error(const specdec_handle *h);
 int specdec_load_params(specdec_handle *h, int role, int n_params,
                         const float *const *params, const int64_t *numels);
 
+/* specdec_load_params with DEVICE arrays (params[i] points to device memory
+ * on this handle's device; the pointer array itself is on the host): the int8
+ * scales, the quantisation and the transpose run on the device, so a model
+ * that already lives there (a checkpoint loaded by another runtime, weights
+ * drawn on the GPU) never passes through host memory.  The same weights give
+ * the same device parameters as specdec_load_params. */
+int specdec_load_params_device(specdec_handle *h, int role, int n_params,
+                               const float *const *params, const int64_t *numels);
+
 /* Replaces Layer::load_weights (src/nn/layer.cpp:467-469 ->
  * serialization::load_parameters, src/core/serialization.cpp:49-107) on the
  * model of `role`: reads a NETW version-1 file (magic "NETW", u16 version,

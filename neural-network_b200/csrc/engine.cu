@@ -280,6 +280,7 @@ struct specdec_handle {
   std::map<GraphKey, GraphEntry> graphs;
   int64_t launches = 0;        // direct mode: kernels enqueued by the last call; -1 in graph mode
   int64_t graph_fixed = 0, graph_body = 0, extra_launches = 0;
+  bool src_device = false;  // the parameters being loaded are device arrays (specdec_load_params_device)
   bool use_graph = true;
   bool use_pdl = true;  // programmatic dependent launch for the kernels that support it
   int gemm_max_split = 1;  // largest split-K cluster of the tensor-core GEMM
@@ -425,6 +426,51 @@ struct DenseSrc {
   bool bias_on = true;
 };
 
+// Device-side loader kernels (weights that already live on the device).
+// Per output column c of a Dense weight [Kfull][ld] (columns col0 .. col0 + N
+// - 1): the QuantizedDense scale max|W[:, c]| / 127, 0 -> 1
+// (src/nn/quantization.cpp:40-66), the same arithmetic as quantize_columns.
+__global__ void col_scale_kernel(const float *__restrict__ w, int Kfull, int ld, int col0, int N,
+                                 float *__restrict__ scale) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= N) return;
+  float mx = 0.f;
+  for (int r = 0; r < Kfull; ++r) mx = fmaxf(mx, fabsf(w[static_cast<size_t>(r) * ld + col0 + c]));
+  const float sc = __fdiv_rn(mx, 127.0f);
+  scale[c] = sc == 0.0f ? 1.0f : sc;
+}
+
+// The transpose to output-major rows through a 32 x 32 shared tile (both
+// sides coalesced): row mul * c + add of dst [.][K] gets input rows row0 ..
+// row0 + K - 1 of column col0 + c, as int8 codes q = clamp(round(w / s),
+// +-127) or as fp32.
+template <bool I8>
+__global__ void quant_transpose_kernel(const float *__restrict__ w, int ld, int col0, int row0, int K, int N,
+                                       const float *__restrict__ scale, void *__restrict__ dst, int mul, int add) {
+  __shared__ float tile[32][33];
+  const int c0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+#pragma unroll
+  for (int j = 0; j < 32; j += 8) {
+    const int k = k0 + ty + j, c = c0 + tx;
+    tile[ty + j][tx] = (k < K && c < N) ? w[static_cast<size_t>(row0 + k) * ld + col0 + c] : 0.f;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < 32; j += 8) {
+    const int c = c0 + ty + j, k = k0 + tx;
+    if (c >= N || k >= K) continue;
+    const float v = tile[tx][ty + j];
+    const size_t o = static_cast<size_t>(mul * c + add) * K + k;
+    if constexpr (I8) {
+      const float q = fminf(127.0f, fmaxf(-127.0f, roundf(__fdiv_rn(v, scale[c]))));
+      static_cast<int8_t *>(dst)[o] = static_cast<int8_t>(q);
+    } else {
+      static_cast<float *>(dst)[o] = v;
+    }
+  }
+}
+
 // Uploads the given Dense sources stacked (or, with `interleave`, row by row)
 // as one output-major matrix [sum N][K].  K is the rank's input slice, rows
 // row0 .. row0 + K - 1 of the Kfull input rows (Kfull = 0: K).  int8 scales
@@ -438,12 +484,48 @@ void upload_stacked(specdec_handle *h, int role, const std::vector<DenseSrc> &sr
   std::vector<float> bias(Ntot);
   std::vector<float> scale(Ntot, 1.f);
   const bool i8 = w_int8(h);
+  auto &own = h->weight_allocs[role];
+  const size_t wbytes = static_cast<size_t>(Ntot) * K * (i8 ? 1 : 4);
+  void *dw = h->dalloc(wbytes, &own);
   std::vector<float> wf;
   std::vector<int8_t> wq;
-  if (i8) wq.assign(static_cast<size_t>(Ntot) * K, 0);
-  else wf.assign(static_cast<size_t>(Ntot) * K, 0.f);
+  if (h->src_device) {
+    // the sources are device arrays: scales and the transpose on the device,
+    // the (small) bias and scale vectors through the host
+    float *dsc = static_cast<float *>(h->dalloc(static_cast<size_t>(std::max(1, Ntot)) * sizeof(float)));
+    int base = 0;
+    for (size_t m = 0; m < src.size(); ++m) {
+      const DenseSrc &s = src[m];
+      const int ld = s.ld ? s.ld : s.N;
+      if (i8)
+        col_scale_kernel<<<(s.N + 255) / 256, 256, 0, h->stream>>>(s.w, Kfull, ld, s.col0, s.N, dsc);
+      const dim3 grid((s.N + 31) / 32, (K + 31) / 32), block(32, 8);
+      const int mul = interleave ? 2 : 1, add = interleave ? static_cast<int>(m) : base;
+      if (i8)
+        quant_transpose_kernel<true><<<grid, block, 0, h->stream>>>(s.w, ld, s.col0, row0, K, s.N, dsc, dw, mul, add);
+      else
+        quant_transpose_kernel<false><<<grid, block, 0, h->stream>>>(s.w, ld, s.col0, row0, K, s.N, nullptr, dw, mul,
+                                                                     add);
+      CK(cudaGetLastError());
+      std::vector<float> hb(s.N), hs(s.N, 1.f);
+      CK(cudaMemcpyAsync(hb.data(), s.b + s.col0, s.N * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
+      if (i8) CK(cudaMemcpyAsync(hs.data(), dsc, s.N * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
+      CK(cudaStreamSynchronize(h->stream));
+      for (int c = 0; c < s.N; ++c) {
+        const int row = interleave ? (2 * c + static_cast<int>(m)) : (base + c);
+        bias[row] = s.bias_on ? hb[c] : 0.f;
+        scale[row] = hs[c];
+      }
+      base += s.N;
+    }
+    cudaFree(dsc);
+    h->allocs.pop_back();
+  } else {
+    if (i8) wq.assign(static_cast<size_t>(Ntot) * K, 0);
+    else wf.assign(static_cast<size_t>(Ntot) * K, 0.f);
+  }
   int base = 0;
-  for (size_t m = 0; m < src.size(); ++m) {
+  for (size_t m = 0; m < (h->src_device ? 0 : src.size()); ++m) {
     const DenseSrc &s = src[m];
     const int ld = s.ld ? s.ld : s.N;
     std::vector<int8_t> q;
@@ -476,11 +558,9 @@ void upload_stacked(specdec_handle *h, int role, const std::vector<DenseSrc> &sr
     });
     base += s.N;
   }
-  auto &own = h->weight_allocs[role];
-  const size_t wbytes = static_cast<size_t>(Ntot) * K * (i8 ? 1 : 4);
-  void *dw = h->dalloc(wbytes, &own);
-  CK(cudaMemcpy(dw, i8 ? static_cast<const void *>(wq.data()) : static_cast<const void *>(wf.data()), wbytes,
-                cudaMemcpyHostToDevice));
+  if (!h->src_device)
+    CK(cudaMemcpy(dw, i8 ? static_cast<const void *>(wq.data()) : static_cast<const void *>(wf.data()), wbytes,
+                  cudaMemcpyHostToDevice));
   float *db = static_cast<float *>(h->dalloc(Ntot * sizeof(float), &own));
   CK(cudaMemcpy(db, bias.data(), Ntot * sizeof(float), cudaMemcpyHostToDevice));
   float *ds = nullptr;
@@ -505,7 +585,7 @@ void upload_stacked(specdec_handle *h, int role, const std::vector<DenseSrc> &sr
 
 float *upload_vec(specdec_handle *h, int role, const float *p, size_t n) {
   float *d = static_cast<float *>(h->dalloc(n * sizeof(float), &h->weight_allocs[role]));
-  CK(cudaMemcpy(d, p, n * sizeof(float), cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(d, p, n * sizeof(float), h->src_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice));
   return d;
 }
 
@@ -2269,6 +2349,15 @@ int specdec_load_params(specdec_handle *h, int role, int n_params, const float *
     return e.code;
   }
   return SPECDEC_OK;
+}
+
+int specdec_load_params_device(specdec_handle *h, int role, int n_params, const float *const *d_params,
+                               const int64_t *numels) {
+  if (!h) return SPECDEC_ERR_INVALID;
+  h->src_device = true;
+  const int rc = specdec_load_params(h, role, n_params, d_params, numels);
+  h->src_device = false;
+  return rc;
 }
 
 int specdec_load_netw(specdec_handle *h, int role, const char *path) {

@@ -38,7 +38,7 @@ EXPORTS = ("specdec_create", "specdec_destroy", "specdec_last_error", "specdec_l
            "specdec_time_linear", "specdec_generate_tree", "specdec_generate_tree_device", "specdec_tp_unique_id",
            "specdec_create_tp", "specdec_generate_ar", "specdec_generate_ar_device", "specdec_load_netw",
            "specdec_prefill", "specdec_prefill_device", "specdec_step", "specdec_step_device",
-           "specdec_session_tokens", "specdec_time_attention")
+           "specdec_session_tokens", "specdec_time_attention", "specdec_load_params_device")
 
 # linear layers of specdec_time_linear
 LIN_QKV, LIN_OPROJ, LIN_FFN_IN, LIN_FFN_OUT, LIN_HEAD = 0, 1, 2, 3, 4
@@ -95,6 +95,7 @@ def load_library(path: str = LIB_PATH):
     lib.specdec_generate_device.argtypes = [C.c_void_p, C.POINTER(_GenParams), C.c_void_p, C.c_int, C.c_int,
                                             C.c_void_p, C.c_void_p]
     lib.specdec_load_netw.argtypes = [C.c_void_p, C.c_int, C.c_char_p]
+    lib.specdec_load_params_device.argtypes = lib.specdec_load_params.argtypes
     lib.specdec_prefill.argtypes = [C.c_void_p, C.POINTER(_GenParams), C.c_void_p, C.c_int, C.c_int]
     lib.specdec_prefill_device.argtypes = lib.specdec_prefill.argtypes
     lib.specdec_step.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]
@@ -196,6 +197,14 @@ class Engine:
         ptrs = (C.c_void_p * len(arrs))(*[a.ctypes.data for a in arrs])
         nums = (C.c_int64 * len(arrs))(*[a.size for a in arrs])
         self._check(self._lib.specdec_load_params(self.h, role, len(arrs), ptrs, nums))
+
+    def load_params_device(self, role: int, tensors) -> None:
+        """load_params from fp32 device tensors (e.g. torch CUDA tensors, any
+        object with data_ptr() and numel()) on this engine's device: quantised
+        and transposed on the device, no host copy."""
+        ptrs = (C.c_void_p * len(tensors))(*[t.data_ptr() for t in tensors])
+        nums = (C.c_int64 * len(tensors))(*[t.numel() for t in tensors])
+        self._check(self._lib.specdec_load_params_device(self.h, role, len(tensors), ptrs, nums))
 
     def load_weights(self, role: int, path: str) -> None:
         """Layer::load_weights: the model's parameters from a NETW v1 file (the

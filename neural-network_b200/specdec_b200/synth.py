@@ -155,6 +155,27 @@ def device_params(m: ModelShape, seed: int, dev) -> List[np.ndarray]:
     return out
 
 
+def device_param_tensors(m: ModelShape, seed: int, dev) -> list:
+    """device_params' weights as contiguous fp32 torch tensors left on `dev`
+    (for Engine.load_params_device: no host copy of a multi-GB model)."""
+    import torch
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    out = []
+    for shape, kind in zip(param_shapes(m), param_kinds(m)):
+        n = int(np.prod(shape))
+        if kind in ("emb", "pos", "w", "head_w"):
+            std = 4.0 / np.sqrt(m.d_model) if kind == "head_w" else 0.02
+            a = torch.empty(n, dtype=torch.float32, device=dev).normal_(0.0, std, generator=g)
+        elif kind == "g":
+            a = torch.ones(n, dtype=torch.float32, device=dev)
+        else:
+            a = torch.zeros(n, dtype=torch.float32, device=dev)
+        out.append(a)
+    return out
+
+
 def draft_params(target: ModelShape, params: List[np.ndarray], n_draft_layers: int) -> List[np.ndarray]:
     """The draft used by every config: the target's first n layers + shared lm_head."""
     per = params_per_layer(target)

@@ -93,3 +93,26 @@ def test_session_call_order(gpu_lib):
         eng.step(1)
     assert e.value.code == 6
     eng.close()
+
+
+@pytest.mark.parametrize("int8,bf16", [(False, False), (True, False), (True, True)])
+def test_load_params_device_equals_host(gpu_lib, int8, bf16):
+    """specdec_load_params_device (scales, codes and transpose on the GPU)
+    gives the same device parameters as the host loader: identical logits."""
+    import torch
+
+    from specdec_b200.synth import make_params
+
+    shape = ModelShape(vocab=384, d_model=128, n_heads=2, d_ff=352, n_layers=2, max_seq_len=64)
+    P = make_params(shape, seed=41, bias_std=0.02, ln_jitter=0.05)
+    kw = dict(weight_dtype=sd.INT8 if int8 else sd.F32, act_dtype=sd.BF16 if bf16 else sd.F32,
+              kv_dtype=sd.BF16 if bf16 else sd.F32, max_batch=2, max_prompt_len=64)
+    host = sd.Engine(shape, draft_layers=1, **kw)
+    host.load_params(sd.TARGET, P)
+    dev = sd.Engine(shape, draft_layers=1, **kw)
+    dev.load_params_device(sd.TARGET, [torch.from_numpy(np.ascontiguousarray(p, np.float32)).cuda() for p in P])
+    toks = make_prompts(1, 40, shape.vocab, seed=2)[0]
+    for role in (sd.TARGET, sd.DRAFT):
+        assert np.array_equal(host.forward_logits(role, toks), dev.forward_logits(role, toks))
+    host.close()
+    dev.close()
