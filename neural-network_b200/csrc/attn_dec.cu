@@ -413,14 +413,20 @@ __global__ void __launch_bounds__(kAdThreads, 2) attn_dec_kernel(const __grid_co
         float al[NQ], pr[NQ];
 #pragma unroll
         for (int q = 0; q < NQ; ++q) {
-          const float4 r4 = *reinterpret_cast<const float4 *>(&red[sb][q][0]);
-          const float mn = fmaxf(m[q], fmaxf(fmaxf(r4.x, r4.y), fmaxf(r4.z, r4.w)));
-          // P is rounded to bf16 for the product: the fast exponential's
-          // error (a few ulp of fp32) is far below that rounding
-          al[q] = (m[q] == -INFINITY) ? 0.f : __expf(m[q] - mn);
-          pr[q] = (s[q] == -INFINITY) ? 0.f : __expf(s[q] - mn);
-          l[q] = l[q] * al[q] + pr[q];
-          m[q] = mn;
+          al[q] = 1.f;
+          pr[q] = 0.f;
+          if (q < it.nq) {  // uniform over the CTA: columns past the group's queries do no work
+            const float4 r4 = *reinterpret_cast<const float4 *>(&red[sb][q][0]);
+            const float mn = fmaxf(m[q], fmaxf(fmaxf(r4.x, r4.y), fmaxf(r4.z, r4.w)));
+            // the running maximum is the same in every thread: when the tile
+            // leaves it unchanged the rescale is 1 without an exponential
+            if (mn != m[q]) al[q] = (m[q] == -INFINITY) ? 0.f : __expf(m[q] - mn);
+            // P is rounded to bf16 for the product: the fast exponential's
+            // error (a few ulp of fp32) is far below that rounding
+            pr[q] = (s[q] == -INFINITY) ? 0.f : __expf(s[q] - mn);
+            l[q] = l[q] * al[q] + pr[q];
+            m[q] = mn;
+          }
         }
         // O_{T-1} into the registers: then its product has read P, which
         // tile T overwrites
