@@ -365,8 +365,15 @@ def config_dict(wl, args):
             "parallelism": f"request-parallel x{args.gpus}",
             "l2": ("inputs larger than L2: 6.6 GB of int8 weights and ~40 GB of KV cache read per step"
                    if wl.name == "large" else "flushed between timed steps (256 MiB write)"),
-            **({"requests": f"{wl.batch} per GPU: configs[4]'s 256 requests split over 8 GPUs"}
+            **({"requests": f"{wl.batch} per GPU: configs[4]'s 256 requests split over 8 GPUs",
+                "kv_pages": f"{kv_pages_needed(wl)} pages of 128 positions per model "
+                            f"(the call's prompt + new tokens + one verify block, not max_seq_len)"}
                if wl.name == "large" else {})}
+
+
+def kv_pages_needed(wl):
+    """Pages of the paged KV cache the large workload's requests reach."""
+    return wl.batch * -(-(wl.prompt_len + wl.max_new + wl.lookahead + 1) // 128)
 
 
 def cpu_baseline_sample(wl):
@@ -420,7 +427,8 @@ def make_engine(sd, wl, local, large):
     eng = sd.Engine(wl.target, draft_layers=wl.draft_layers, weight_dtype=sd.INT8 if wl.weights_int8 else sd.F32,
                     act_dtype=sd.BF16 if wl.act_bf16 else sd.F32, kv_dtype=KV_DTYPE[wl.kv_mode],
                     max_batch=wl.batch, max_lookahead=wl.lookahead, max_prompt_len=wl.prompt_len, device=local,
-                    max_tree_nodes=tree_nodes(wl.tree) if wl.tree else 0)
+                    max_tree_nodes=tree_nodes(wl.tree) if wl.tree else 0,
+                    kv_pages=kv_pages_needed(wl) if large else 0)
     if large:
         P = device_param_tensors(wl.target, 0, torch.device("cuda", local))
         eng.load_params_device(sd.TARGET, P)
@@ -779,6 +787,92 @@ def run_session_bench(args, wl, rank, world, local, dist):
     return line
 
 
+def run_tp_bench(args, wl, rank, world, local, dist):
+    """BASELINE configs[4]'s tensor-parallel variant: 16 requests served by all
+    `world` GPUs together (specdec_create_tp: heads and FFN columns split, an
+    NCCL all-reduce after the attention output and FFN down projections).
+    Rounds through the session API; every rank returns the same tokens.  The
+    all-reduce share is the time of the round's all-reduces (the same sizes,
+    timed with torch's NCCL on this group) over the round's time."""
+    import hashlib
+
+    import torch
+
+    import specdec_b200 as sd
+    from specdec_b200.shard import max_over_ranks
+
+    B, S, k, T = 16, wl.prompt_len, wl.lookahead, wl.temperature
+    dev = torch.device("cuda", local)
+    obj = [sd.tp_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    eng = sd.Engine(wl.target, draft_layers=wl.draft_layers, weight_dtype=sd.INT8, act_dtype=sd.BF16,
+                    kv_dtype=sd.BF16, max_batch=B, max_lookahead=k, max_prompt_len=S, device=local,
+                    tp_rank=rank, tp_world=world, tp_id=obj[0],
+                    kv_pages=B * -(-(S + wl.max_new + k + 1) // 128))
+    P = device_param_tensors(wl.target, 0, dev)
+    eng.load_params_device(sd.TARGET, P)
+    del P
+    torch.cuda.empty_cache()
+    prompts = make_prompts(B, S, wl.target.vocab, seed=2)
+    uni = sd.philox_uniforms(4321, B, wl.max_new + 2, 2 * k + 1)
+    d_prompts = torch.from_numpy(prompts.astype(np.int32)).to(dev)
+    eng.prefill_device(d_prompts.data_ptr(), B, S, wl.max_new, k, T, seed=4321, uniforms=uni)
+    torch.cuda.synchronize()
+    n_w, n_t = 3, 10
+    cap = k + 1
+    d_tok = torch.zeros((n_w + n_t, B, cap), dtype=torch.int32, device=dev)
+    d_cnt = torch.zeros((n_w + n_t, B), dtype=torch.int32, device=dev)
+    stream = torch.cuda.ExternalStream(eng.stream, device=dev)
+    for i in range(n_w):
+        eng.step_device(1, d_tok[i].data_ptr(), d_cnt[i].data_ptr(), cap)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+    for i in range(n_w, n_w + n_t):
+        eng.step_device(1, d_tok[i].data_ptr(), d_cnt[i].data_ptr(), cap)
+    with torch.cuda.stream(stream):
+        e1.record(stream)
+    torch.cuda.synchronize()
+    tot_ms = e0.elapsed_time(e1)
+    tokens = int(d_cnt[n_w:].sum().item())
+    full, _ = eng.session_tokens()
+    eng.close()
+    digest = hashlib.sha256(np.ascontiguousarray(full).tobytes()).hexdigest()
+    digests = [None] * world
+    dist.all_gather_object(digests, digest)
+    # the round's all-reduces: per layer two of [rows][d_model] bf16 -- the
+    # verify pass (B (k + 1) rows, L target layers), draft step 0 (2B rows)
+    # and steps 1 .. k-1 (B rows) over the draft's layers
+    d = wl.target.d_model
+    sizes = ([B * (k + 1)] * (2 * wl.target.n_layers) + [2 * B] * (2 * wl.draft_layers) +
+             [B] * (2 * wl.draft_layers * (k - 1)))
+    ar_ms = 0.0
+    for rows in sorted(set(sizes)):
+        x = torch.zeros((rows, d), dtype=torch.bfloat16, device=dev)
+        for _ in range(3):
+            dist.all_reduce(x)
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a0.record()
+        for _ in range(20):
+            dist.all_reduce(x)
+        a1.record()
+        torch.cuda.synchronize()
+        ar_ms += a0.elapsed_time(a1) / 20 * sizes.count(rows)
+    tot_ms, ar_ms = max_over_ranks([tot_ms, ar_ms], dist, dev)
+    if rank != 0:
+        return None
+    round_ms = tot_ms / n_t
+    return {"world": world, "batch": B, "value": tokens / (tot_ms / 1e3), "unit": UNIT, "rounds_timed": n_t,
+            "ms_per_round": round_ms, "allreduce_ms_per_round": ar_ms, "allreduce_share": ar_ms / round_ms,
+            "allreduces_per_round": len(sizes), "ranks_agree": len(set(digests)) == 1,
+            "what": "16 requests on all GPUs together (heads and FFN columns split, NCCL all-reduce after the "
+                    "attention output and FFN down projections); all-reduce time = torch's NCCL on the same "
+                    "sizes, timed apart"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -796,6 +890,7 @@ def main():
     ap.add_argument("--batch", type=int, default=0,
                     help="requests per GPU (0: the workload's); a smaller case for profiler captures")
     ap.add_argument("--skip-configs1", action="store_true", help="large workload: no configs[1] sub-line")
+    ap.add_argument("--no-tp", action="store_true", help="large workload on N > 1 GPUs: no tensor-parallel line")
     ap.add_argument("--profile", action="store_true",
                     help="timed steps only (no e2e, probes, CPU baseline or configs[1]): for profiler launch lists")
     args = ap.parse_args()
@@ -818,12 +913,20 @@ def main():
 
     torch.cuda.set_device(local)
     if world > 1:
+        # the tensor-parallel variant's NCCL traffic stays off NVLink
+        # multicast (NVLS), as its tests run it
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         from datetime import timedelta
         dist.init_process_group("nccl", init_method="env://", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     try:
         if large:
             line = run_session_bench(args, wl, rank, world, local, dist)
+            if world > 1 and not args.profile and not args.no_tp:
+                torch.cuda.empty_cache()
+                tp = run_tp_bench(args, wl, rank, world, local, dist)
+                if line is not None:
+                    line["tp"] = tp
             if not args.skip_configs1 and not args.profile:
                 torch.cuda.empty_cache()
                 sub_args = argparse.Namespace(**{**vars(args), "steps": 10, "warmup": 3})

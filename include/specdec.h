@@ -80,6 +80,11 @@ typedef struct specdec_config {
   int32_t max_lookahead;           /* largest k */
   int32_t max_prompt_len;          /* longest prompt */
   int32_t max_tree_nodes;          /* 0: no token trees; else the largest tree (<= 64 nodes) specdec_generate_tree accepts */
+  int32_t kv_pages;                /* paged KV cache: pages of 128 positions in each model's pool (the reference's
+                                      KVCache, include/nn/layer.hpp:212-230, grows one request's cache by copying);
+                                      0 -> max_batch x ceil(max_seq_len / 128).  A call takes the pages its requests
+                                      can reach (prompt + new tokens + one verify block) and returns SPECDEC_ERR_OOM
+                                      when the pool is too small */
 } specdec_config;
 
 /* The arguments of generate_speculative (include/nn/layer.hpp:318-323) plus

@@ -231,10 +231,13 @@ __global__ void __launch_bounds__(kAdThreads, 2) attn_dec_kernel(const __grid_co
         tma_load_2d(sq + qb * kAdQBytes, &a.tmq, it.h * kAdD, it.rq0, &q_full[qb]);
         tma_load_2d(sq + qb * kAdQBytes + kAdQBytes / 2, &a.tmq, it.h * kAdD + 64, it.rq0, &q_full[qb]);
         s_q_issued = ++qi;
-        const int base = (it.req * a.Hkv + it.h) * a.S_cap;
         bool stop = false;
         for (int t = 0; t < it.nt && !stop; ++t) {
-          const int y = base + (it.t0 + t) * kAdTile;
+          int y = kv_row(a.pg, a.Hkv, it.req, it.h, (it.t0 + t) * kAdTile);
+          if (y < 0) {  // no page: flagged, a valid row is read instead
+            if (a.err) atomicOr(a.err, kErrSeqLen);
+            y = 0;
+          }
           for (int kv = 0; kv < 2; ++kv) {
             const int s = idx % kAdSlots;
             if (!mbar_wait(&empty[s], ((idx / kAdSlots) & 1) ^ 1) || s_abort) {

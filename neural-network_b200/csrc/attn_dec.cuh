@@ -17,10 +17,11 @@ constexpr int kAdMaxSplit = 8;  // splits of one (group, head) over its cache
 
 struct alignas(64) AttnDecArgs {
   CUtensorMap tmq;       // [R][dq] bf16 query rows, box 64 x 16, 128-byte swizzle
-  CUtensorMap tmk, tmv;  // [slot * Hkv * S_cap + position][128] bf16 cache rows, box 64 x 128, 128-byte swizzle
+  CUtensorMap tmk, tmv;  // [cache row][128] bf16 page pools, box 64 x 128, 128-byte swizzle
+  KvPages pg;            // tile T of a request = positions [128 T, 128 T + 128) = one page
   RowsView rows;
   int R, Q;              // rows of the pass, rows per group (one request each)
-  int S_cap, H, Hkv;     // positions per (request, kv head); heads (H == Hkv)
+  int S_cap, H, Hkv;     // positions per request; heads (H == Hkv)
   int n_items;           // groups * H * nsplit
   int nsplit;            // splits of one (group, head)
   __nv_bfloat16 *out;    // [R][ldo]

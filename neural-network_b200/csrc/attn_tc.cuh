@@ -73,7 +73,8 @@ __device__ __forceinline__ uint64_t vis_word(int base, int qpos, int qtb, unsign
 
 struct alignas(64) AttnTcArgs {
   CUtensorMap tmq;       // [R][dq] bf16 query rows, box 64 x 128
-  CUtensorMap tmk, tmv;  // [slot * Hkv * S_cap + position][64] bf16, box 64 x 128 (the attention_kernel maps)
+  CUtensorMap tmk, tmv;  // [cache row][64] bf16 page pools, box 64 x 128 (the attention_kernel maps)
+  KvPages pg;
   RowsView rows;
   int R, Q;              // rows, queries per group
   int S_cap, H, Hkv;
@@ -144,16 +145,21 @@ __global__ void __launch_bounds__(kAtcThreads, 2) attn_tc_kernel(const __grid_co
   const int req = s_req, maxpos = s_maxpos;
   const bool work = req >= 0 && maxpos >= 0 && maxpos < a.S_cap;
   const int ntiles = work ? maxpos / kAtcTile + 1 : 0;
-  const int row0 = (req * a.Hkv + hk) * a.S_cap;
-
+  // tile t = positions [128 t, 128 t + 128): one page
+  auto tile_row = [&](int t) {
+    const int y = kv_row(a.pg, a.Hkv, req, hk, t * kAtcTile);
+    if (y >= 0) return y;
+    if (a.err) atomicOr(a.err, kErrSeqLen);  // no page: flagged, a valid row is read instead
+    return 0;
+  };
   auto issue_k = [&](int t) {  // thread 0
     const int s = t & 1;
     mbar_expect_tx(&bar_kv[s], kAtcKVBytes);
-    tma_load_2d(sk + s * kAtcKVBytes, &a.tmk, 0, row0 + t * kAtcTile, &bar_kv[s]);
+    tma_load_2d(sk + s * kAtcKVBytes, &a.tmk, 0, tile_row(t), &bar_kv[s]);
   };
   auto issue_v = [&](int t) {  // thread 0
     mbar_expect_tx(&bar_v, kAtcKVBytes);
-    tma_load_2d(sv, &a.tmv, 0, row0 + t * kAtcTile, &bar_v);
+    tma_load_2d(sv, &a.tmv, 0, tile_row(t), &bar_v);
   };
   if (threadIdx.x == 0 && ntiles > 0) {
     mbar_expect_tx(&bar_q, kAtcQBytes);

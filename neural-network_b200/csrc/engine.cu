@@ -240,8 +240,14 @@ struct specdec_handle {
   void *tk = nullptr, *tv = nullptr, *dk = nullptr, *dv = nullptr;
   float *tks = nullptr, *tvs = nullptr, *dks = nullptr, *dvs = nullptr;  // int8 cache: per-row scales
   float *KVN = nullptr;                                                  // int8 cache: staged K/V rows
-  size_t t_layer_stride = 0, d_layer_stride = 0, t_req_stride = 0, d_req_stride = 0;
-  int t_cap = 0, d_cap = 0;
+  size_t t_layer_stride = 0, d_layer_stride = 0;  // elements of one layer's page pool
+  int t_cap = 0, d_cap = 0;                        // positions per request (the models' max_seq_len)
+  // Paged KV cache: the pools hold kv_pages pages of kKvPage positions;
+  // request slot b's page table is d_pt[b * ppr .. b * ppr + ppr) (shared by
+  // the target and draft pools and by all layers).
+  int kv_pages = 0, ppr = 0;
+  int *d_pt = nullptr;
+  std::vector<int> h_pt;
   float2 *rope = nullptr;
   int rope_max = 0, rope_D = 0;
 
@@ -1147,7 +1153,8 @@ void launch_attention_d(specdec_handle *h, AttnArgs &a, int ngroups, const void 
     ns = std::min(std::min(kAttnMaxSplit, want), fit);
   }
   a.nsplit = ns;
-  a.chunk = (a.S_cap + ns - 1) / ns;
+  // whole tiles per split: a tile never straddles a page
+  a.chunk = ((a.S_cap + ns - 1) / ns + G::kTile - 1) / G::kTile * G::kTile;
   const size_t smem = static_cast<size_t>(G::smem_bytes(a.chunk > G::kTile ? 2 : 1));
   dim3 grid(ngroups * ngt, a.H, ns);
   dim3 block(kAttnThreads);
@@ -1171,12 +1178,13 @@ void launch_attention_t(specdec_handle *h, AttnArgs &a, int D, int ngroups, cons
 }
 
 // Attention over a row batch whose rows form groups of Q consecutive rows of
-// one request each.  kc/vc are one layer's caches of `layer_elems` elements
-// ([slot][kv head][S_cap][D]).
+// one request each.  kc/vc are one layer's page pools of `layer_elems`
+// elements ([page][kv head][kKvPage][D]), pg the requests' page tables.
 void attention(specdec_handle *h, const Dims &dm, RowsView rows, int R, int Q, const void *kc, const void *vc,
-               const float *ks, const float *vs, size_t layer_elems, int S_cap) {
+               const float *ks, const float *vs, size_t layer_elems, int S_cap, KvPages pg) {
   if (R <= 0) return;
   AttnArgs a{};
+  a.pg = pg;
   a.q = h->Q; a.ldq = dm.dq; a.rows = rows; a.R = R; a.Q = Q;
   a.S_cap = S_cap; a.H = dm.H; a.Hkv = dm.Hkv;
   a.k_scale = ks; a.v_scale = vs;
@@ -1191,7 +1199,7 @@ void attention(specdec_handle *h, const Dims &dm, RowsView rows, int R, int Q, c
     t.tmq = gemm_operand_map(h->Q, dm.dq, R, dm.dq, 128);
     t.tmk = kv_tensor_map<__nv_bfloat16, kAtcD>(kc, nrows);
     t.tmv = kv_tensor_map<__nv_bfloat16, kAtcD>(vc, nrows);
-    t.rows = rows; t.R = R; t.Q = Q; t.S_cap = S_cap; t.H = dm.H; t.Hkv = dm.Hkv;
+    t.rows = rows; t.R = R; t.Q = Q; t.S_cap = S_cap; t.H = dm.H; t.Hkv = dm.Hkv; t.pg = pg;
     t.out = static_cast<__nv_bfloat16 *>(h->ATT); t.ldo = dm.dq; t.err = h->st.err;
     launch_pdl(h, attn_tc_kernel, dim3(ngroups * ((Q + 127) / 128), dm.H), dim3(kAtcThreads),
                static_cast<size_t>(kAtcSmem), t);
@@ -1205,7 +1213,7 @@ void attention(specdec_handle *h, const Dims &dm, RowsView rows, int R, int Q, c
     d.tmq = gemm_operand_map(h->Q, dm.dq, R, dm.dq, kAdN);
     d.tmk = kv_tensor_map<__nv_bfloat16, kAdD>(kc, nrows);
     d.tmv = kv_tensor_map<__nv_bfloat16, kAdD>(vc, nrows);
-    d.rows = rows; d.R = R; d.Q = Q; d.S_cap = S_cap; d.H = dm.H; d.Hkv = dm.Hkv;
+    d.rows = rows; d.R = R; d.Q = Q; d.S_cap = S_cap; d.H = dm.H; d.Hkv = dm.Hkv; d.pg = pg;
     // splits while the (group, head) items would spread unevenly over the SMs
     const int base = ngroups * dm.H;
     const int tiles = (S_cap + kAdTile - 1) / kAdTile;
@@ -1316,7 +1324,7 @@ void forward_rows(specdec_handle *h, bool target, int off, int R, int Q, const i
   void *kc = target ? h->tk : h->dk;
   void *vc = target ? h->tv : h->dv;
   const size_t lstride = target ? h->t_layer_stride : h->d_layer_stride;
-  const size_t rstride = target ? h->t_req_stride : h->d_req_stride;
+  const KvPages pg{h->d_pt, h->ppr};
   const int S_cap = target ? h->t_cap : h->d_cap;
   const bool kv8 = h->cfg.kv_dtype == SPECDEC_INT8;
   const size_t kv_elt = kv8 ? 1 : h->cfg.kv_dtype == SPECDEC_BF16 ? 2 : 4;
@@ -1344,14 +1352,14 @@ void forward_rows(specdec_handle *h, bool target, int off, int R, int Q, const i
     } else {
       a.x = h->X; a.in_g = L.g1; a.in_b = L.b1;
     }
-    a.qkv = QKVArgs{dm.dq, dm.kvd, dm.D, h->rope, h->rope_max, kcl, vcl, rstride, S_cap,
+    a.qkv = QKVArgs{dm.dq, dm.kvd, dm.D, h->rope, h->rope_max, kcl, vcl, pg, S_cap,
                     kv8 ? 2 : h->cfg.kv_dtype == SPECDEC_BF16 ? 1 : 0, h->KVN, h->st.err};
     launch_linear<kEpiQKV>(h, a);
     float *ksl = kv8 ? ksc + l * lrows : nullptr, *vsl = kv8 ? vsc + l * lrows : nullptr;
     if (kv8)
       launch(h, kv_quant_kernel, dim3(R), dim3(256), 0, rows, R, static_cast<const float *>(h->KVN), dm.kvd, dm.D,
-             dm.Hkv, S_cap, static_cast<int8_t *>(kcl), static_cast<int8_t *>(vcl), ksl, vsl);
-    attention(h, dm, rows, R, Q, kcl, vcl, ksl, vsl, lstride, S_cap);
+             dm.Hkv, S_cap, pg, static_cast<int8_t *>(kcl), static_cast<int8_t *>(vcl), ksl, vsl);
+    attention(h, dm, rows, R, Q, kcl, vcl, ksl, vsl, lstride, S_cap, pg);
     // With tensor parallelism each rank multiplies its heads' slice; one rank
     // adds bias and residual, and the all-reduce sums the partial rows.
     const bool lead = h->tp_rank == 0;
@@ -1394,6 +1402,31 @@ void forward_rows(specdec_handle *h, bool target, int off, int R, int Q, const i
 namespace {
 
 void sync_check(specdec_handle *h) { CK(cudaStreamSynchronize(h->stream)); }
+
+// Gives request slots 0 .. B-1 the pages for positions [0, need) (at most
+// max_seq_len).  Every generation, session and forward starts with empty
+// caches, so the whole pool is free again: slot b's i-th page is the
+// (i * B + b)-th page of the pool, so a request's pages are not adjacent.
+// Slots past B and pages past need stay -1; a kernel that meets one flags
+// SPECDEC_ERR_SEQ_LEN.  The table goes up on the library's stream, ahead of
+// the launches that read it.
+void assign_pages(specdec_handle *h, int B, int need) {
+  const int per = std::min(h->ppr, (std::max(1, need) + kKvPage - 1) / kKvPage);
+  if (static_cast<int64_t>(B) * per > h->kv_pages)
+    fail(SPECDEC_ERR_OOM, "the KV page pool holds " + std::to_string(h->kv_pages) + " pages of " +
+                              std::to_string(kKvPage) + " positions; " + std::to_string(B) + " requests of " +
+                              std::to_string(need) + " positions need " + std::to_string(B * per));
+  h->h_pt.assign(static_cast<size_t>(h->cfg.max_batch) * h->ppr, -1);
+  for (int i = 0; i < per; ++i)
+    for (int b = 0; b < B; ++b) h->h_pt[static_cast<size_t>(b) * h->ppr + i] = i * B + b;
+  CK(cudaMemcpyAsync(h->d_pt, h->h_pt.data(), h->h_pt.size() * sizeof(int), cudaMemcpyHostToDevice, h->stream));
+}
+
+// Cache positions a generation can write: the prompt, the new tokens, and a
+// verify block (k + 1 rows, or a tree's nodes) past them.
+int positions_needed(const specdec_gen_params *p, int S, const TreeCfg *tree, bool ar) {
+  return S + std::max(0, p->max_new_tokens) + (ar ? 1 : tree ? tree->N + 1 : std::max(1, p->lookahead) + 1);
+}
 
 void validate_gen(specdec_handle *h, const specdec_gen_params *p, int B, int S, const TreeCfg *tree, bool ar) {
   if (!p) fail(SPECDEC_ERR_INVALID, "null params");
@@ -1487,7 +1520,7 @@ CacheView cache_view(specdec_handle *h, bool target) {
   c.ks = target ? h->tks : h->dks;
   c.vs = target ? h->tvs : h->dvs;
   c.layer_elems = target ? h->t_layer_stride : h->d_layer_stride;
-  c.req_stride = target ? h->t_req_stride : h->d_req_stride;
+  c.pg = KvPages{h->d_pt, h->ppr};
   c.S_cap = target ? h->t_cap : h->d_cap;
   c.Hkv = m.dm.Hkv;
   c.D = m.dm.D;
@@ -1707,6 +1740,7 @@ int generate_impl(specdec_handle *h, const specdec_gen_params *p, const int32_t 
   validate_gen(h, p, B, S, tree, ar);
   SpecState &st = h->st;
   h->step_open = false;  // a generation reuses the speculative state of a step session
+  assign_pages(h, B, positions_needed(p, S, tree, ar));
   if (ar && p->max_new_tokens == 0) {  // generate_advanced returns the prompt
     CK(cudaMemcpyAsync(d_out, d_prompts, static_cast<size_t>(B) * S * sizeof(int), cudaMemcpyDeviceToDevice, h->stream));
     if (d_stats_out) CK(cudaMemsetAsync(d_stats_out, 0, static_cast<size_t>(B) * 4 * sizeof(int64_t), h->stream));
@@ -1788,6 +1822,7 @@ void ensure_uniform_table(specdec_handle *h, size_t n) {
 void prefill_impl(specdec_handle *h, const specdec_gen_params *p, const int32_t *d_prompts, int B, int S) {
   validate_gen(h, p, B, S, nullptr, false);
   h->step_open = false;
+  assign_pages(h, B, positions_needed(p, S, nullptr, false));
   SpecState &st = h->st;
   setup_state(h, p, B, S, nullptr, false);
   if (d_prompts != h->d_prompts)
@@ -1995,13 +2030,19 @@ int create_impl(const specdec_config *cfg, int device, int rank, int world, cons
     const int B = cfg->max_batch, k = cfg->max_lookahead;
     const bool kv8 = cfg->kv_dtype == SPECDEC_INT8;
     const size_t kv_elt = kv8 ? 1 : cfg->kv_dtype == SPECDEC_BF16 ? 2 : 4;
-    // KV caches: [layer][B][Hkv][cap][D]
+    // KV caches: per layer a pool of kv_pages pages, [page][Hkv][kKvPage][D]
+    // (by default enough pages for every slot to reach max_seq_len)
     h->t_cap = td.max_seq;
     h->d_cap = dd.max_seq;
-    h->t_req_stride = static_cast<size_t>(td.Hkv) * h->t_cap * td.D;
-    h->d_req_stride = static_cast<size_t>(dd.Hkv) * h->d_cap * dd.D;
-    h->t_layer_stride = h->t_req_stride * B;
-    h->d_layer_stride = h->d_req_stride * B;
+    h->ppr = (std::max(h->t_cap, h->d_cap) + kKvPage - 1) / kKvPage;
+    if (cfg->kv_pages < 0) fail(SPECDEC_ERR_INVALID, "kv_pages < 0");
+    h->kv_pages = cfg->kv_pages > 0 ? cfg->kv_pages : B * h->ppr;
+    if (static_cast<int64_t>(h->kv_pages) * std::max(td.Hkv, dd.Hkv) * kKvPage > INT32_MAX)
+      fail(SPECDEC_ERR_INVALID, "kv_pages x kv heads x 128 cache rows exceed 2^31");
+    h->t_layer_stride = static_cast<size_t>(h->kv_pages) * td.Hkv * kKvPage * td.D;
+    h->d_layer_stride = static_cast<size_t>(h->kv_pages) * dd.Hkv * kKvPage * dd.D;
+    h->d_pt = static_cast<int *>(h->dalloc(static_cast<size_t>(B) * h->ppr * sizeof(int)));
+    CK(cudaMemset(h->d_pt, 0xff, static_cast<size_t>(B) * h->ppr * sizeof(int)));  // -1: no page
     h->tk = h->dalloc(h->t_layer_stride * td.L * kv_elt);
     h->tv = h->dalloc(h->t_layer_stride * td.L * kv_elt);
     h->dk = h->dalloc(h->d_layer_stride * dd.L * kv_elt);
@@ -2200,7 +2241,8 @@ int specdec_time_linear(specdec_handle *h, int role, int layer, int which, int r
       case SPECDEC_LIN_QKV:
         a.x = h->H; a.W = L.wqkv; a.scale = L.sqkv; a.bias = L.bqkv; a.N = dm.dq + 2 * dm.kvd; a.out = h->Q;
         a.ldo = dm.dq; a.in_g = L.g1; a.in_b = L.b1;
-        a.qkv = QKVArgs{dm.dq, dm.kvd, dm.D, h->rope, h->rope_max, h->tk, h->tv, 0, 1, 0, nullptr, nullptr};
+        a.qkv = QKVArgs{dm.dq, dm.kvd, dm.D, h->rope, h->rope_max, h->tk, h->tv, KvPages{h->d_pt, h->ppr}, 1, 0,
+                        nullptr, nullptr};
         epi = kEpiQKV; out_w = dm.dq + 2 * dm.kvd;
         break;
       case SPECDEC_LIN_OPROJ:
@@ -2299,7 +2341,8 @@ int specdec_time_attention(specdec_handle *h, int role, int layer, int q_per_req
     for (int i = 0; i < reps; ++i) {
       if (flush && flush_bytes) CK(cudaMemsetAsync(flush, i & 0xff, flush_bytes, h->stream));
       CK(cudaEventRecord(e0, h->stream));
-      attention(h, dm, rows, R, q_per_req, kcl, vcl, ksl, vsl, lstride, target ? h->t_cap : h->d_cap);
+      attention(h, dm, rows, R, q_per_req, kcl, vcl, ksl, vsl, lstride, target ? h->t_cap : h->d_cap,
+                KvPages{h->d_pt, h->ppr});
       CK(cudaEventRecord(e1, h->stream));
       CK(cudaEventSynchronize(e1));
       float ms = 0.f;
@@ -2625,6 +2668,9 @@ int specdec_forward_logits(specdec_handle *h, int role, const int32_t *tokens, i
       fail(SPECDEC_ERR_INVALID, "sequence length out of range");
     const Dims &dm = m.dm;
     h->launches = 0;
+    // the forward's K/V go to request slot 0's cache: an open session ends
+    h->step_open = false;
+    assign_pages(h, 1, S);
     CK(cudaMemsetAsync(h->st.err, 0, sizeof(int), h->stream));
     CK(cudaMemcpyAsync(h->d_prompts, tokens, S * sizeof(int), cudaMemcpyHostToDevice, h->stream));
     launch(h, plan_prefill_kernel, dim3((S + 255) / 256), dim3(256), 0, static_cast<const int *>(h->d_prompts), 1, S, 0,
@@ -2731,6 +2777,11 @@ cudaError_t noalloc_base(int device, unsigned char **out) {
 }
 
 // Copies the scratch array's error word to the caller's status word.
+// Page table of one request whose pages are 0 .. n-1 of its pool.
+__global__ void page_iota_kernel(int *pt, int n) {
+  for (int i = threadIdx.x; i < n; i += blockDim.x) pt[i] = i;
+}
+
 __global__ void copy_status_kernel(const int *err, int32_t *status) { *status = *err; }
 
 struct ArenaCarver {
@@ -2754,21 +2805,22 @@ extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const
     float *tks, *tvs, *dks, *dvs, *KVN;
     int *err;
     RowPool pool;
-    size_t tls, dls, trs, drs;
-    int tcap, dcap, R_max;
+    size_t tls, dls;
+    int *pt;
+    int ppr, tcap, dcap, R_max;
     cudaStream_t stream;
     float *gemm_ws, *ad_part, *w8_ws;
   };
   Saved sv{h->X, h->H, h->X1, h->A, h->Q, h->ATT, h->tk, h->tv, h->dk, h->dv, h->tks, h->tvs, h->dks, h->dvs, h->KVN,
            h->st.err, h->pool,
-           h->t_layer_stride, h->d_layer_stride, h->t_req_stride, h->d_req_stride, h->t_cap, h->d_cap, h->R_max,
+           h->t_layer_stride, h->d_layer_stride, h->d_pt, h->ppr, h->t_cap, h->d_cap, h->R_max,
            h->stream, h->gemm_ws, h->ad_part, h->w8_ws};
   auto restore = [&] {
     h->X = sv.X; h->H = sv.H; h->X1 = sv.X1; h->A = sv.A; h->Q = sv.Q; h->ATT = sv.ATT;
     h->tk = sv.tk; h->tv = sv.tv; h->dk = sv.dk; h->dv = sv.dv;
     h->tks = sv.tks; h->tvs = sv.tvs; h->dks = sv.dks; h->dvs = sv.dvs; h->KVN = sv.KVN;
     h->st.err = sv.err; h->pool = sv.pool;
-    h->t_layer_stride = sv.tls; h->d_layer_stride = sv.dls; h->t_req_stride = sv.trs; h->d_req_stride = sv.drs;
+    h->t_layer_stride = sv.tls; h->d_layer_stride = sv.dls; h->d_pt = sv.pt; h->ppr = sv.ppr;
     h->t_cap = sv.tcap; h->d_cap = sv.dcap; h->R_max = sv.R_max; h->stream = sv.stream;
     h->gemm_ws = sv.gemm_ws; h->ad_part = sv.ad_part; h->w8_ws = sv.w8_ws;
   };
@@ -2789,6 +2841,7 @@ extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const
     const size_t act = h->act_elt;
     const bool kv8 = h->cfg.kv_dtype == SPECDEC_INT8;
     const size_t kv_elt = kv8 ? 1 : h->cfg.kv_dtype == SPECDEC_BF16 ? 2 : 4;
+    const int np = (S + kKvPage - 1) / kKvPage;
     auto layout = [&](ArenaCarver &c, void **ptrs) {
       const size_t rows_d = static_cast<size_t>(S) * dm.d * act;
       ptrs[0] = c.take(rows_d);                                // X
@@ -2797,19 +2850,21 @@ extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const
       ptrs[3] = c.take(static_cast<size_t>(S) * dm.F * act);   // A
       ptrs[4] = c.take(rows_d);                                // Q
       ptrs[5] = c.take(rows_d);                                // ATT
-      const size_t kv = static_cast<size_t>(std::max(1, dm.L)) * dm.Hkv * S * dm.D * kv_elt;
+      // one request's cache: pages 0 .. np-1 of a scratch pool
+      const size_t kv = static_cast<size_t>(std::max(1, dm.L)) * np * dm.Hkv * kKvPage * dm.D * kv_elt;
       ptrs[6] = c.take(kv);                                    // K cache
       ptrs[7] = c.take(kv);                                    // V cache
       ptrs[8] = c.take(S * sizeof(int));                       // row tokens
       ptrs[9] = c.take(S * sizeof(int));                       // row positions
       ptrs[10] = c.take(S * sizeof(int));                      // row requests
       ptrs[11] = c.take(sizeof(int));                          // error word
-      const size_t nsc = kv8 ? static_cast<size_t>(std::max(1, dm.L)) * dm.Hkv * S : 0;
+      const size_t nsc = kv8 ? static_cast<size_t>(std::max(1, dm.L)) * np * dm.Hkv * kKvPage : 0;
       ptrs[12] = c.take(nsc * sizeof(float));                  // int8 cache: K scales
       ptrs[13] = c.take(nsc * sizeof(float));                  // int8 cache: V scales
       ptrs[14] = c.take(kv8 ? static_cast<size_t>(S) * 2 * dm.kvd * sizeof(float) : 0);  // int8 cache: staged rows
+      ptrs[15] = c.take(np * sizeof(int));                     // page table of slot 0
     };
-    void *ptrs[15];
+    void *ptrs[16];
     ArenaCarver sizing{nullptr};
     layout(sizing, ptrs);
     if (sizing.used > SPECDEC_NOALLOC_SCRATCH_BYTES)
@@ -2830,9 +2885,11 @@ extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const
     h->pool.pos = static_cast<int *>(ptrs[9]);
     h->pool.req = static_cast<int *>(ptrs[10]);
     h->st.err = static_cast<int *>(ptrs[11]);
-    const size_t req_stride = static_cast<size_t>(dm.Hkv) * S * dm.D;
-    if (target) { h->t_req_stride = req_stride; h->t_layer_stride = req_stride; h->t_cap = S; }
-    else { h->d_req_stride = req_stride; h->d_layer_stride = req_stride; h->d_cap = S; }
+    const size_t layer_elems = static_cast<size_t>(np) * dm.Hkv * kKvPage * dm.D;
+    if (target) { h->t_layer_stride = layer_elems; h->t_cap = S; }
+    else { h->d_layer_stride = layer_elems; h->d_cap = S; }
+    h->d_pt = static_cast<int *>(ptrs[15]);
+    h->ppr = np;
     h->R_max = S;
     h->stream = st;
     // the handle's split-K workspace and decode-attention partials belong to
@@ -2841,6 +2898,15 @@ extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const
     h->ad_part = nullptr;
     h->w8_ws = nullptr;
     CK(cudaMemsetAsync(h->st.err, 0, sizeof(int), st));
+    // The tensor-core attention multiplies whole 128-position tiles, the
+    // rows past S with probability 0: they must hold finite values, and the
+    // scratch array holds whatever an earlier call left there.
+    {
+      const size_t kv = static_cast<size_t>(std::max(1, dm.L)) * np * dm.Hkv * kKvPage * dm.D * kv_elt;
+      CK(cudaMemsetAsync(ptrs[6], 0, kv, st));
+      CK(cudaMemsetAsync(ptrs[7], 0, kv, st));
+    }
+    launch(h, page_iota_kernel, dim3(1), dim3(128), 0, h->d_pt, np);
     launch(h, plan_prefill_kernel, dim3((S + 255) / 256), dim3(256), 0, d_tokens, 1, S, 0, S, dm.V, h->pool.tok,
            h->pool.pos, h->pool.req, static_cast<int *>(nullptr));
     forward_rows(h, target, 0, S, S, nullptr, S, d_logits);

@@ -44,6 +44,28 @@ struct RowsView {
 };
 __device__ __forceinline__ int row_slot(const RowsView &rv, int r) { return rv.slot ? rv.slot[r] : rv.pos[r]; }
 
+// Paged KV cache.  A layer's K (or V) cache is a pool of pages; a page holds
+// kKvPage consecutive positions of one request for all its kv heads,
+// [Hkv][kKvPage][D].  Request q's position p lives in page
+// pt[q * ppr + p / kKvPage] (-1: no page), at cache row
+// (page * Hkv + head) * kKvPage + p % kKvPage -- the y coordinate of the
+// attention kernels' TMA views and the index of the int8 scale planes.  The
+// attention tiles (64 or 128 positions, starting at multiples of their size)
+// never straddle a page, so a tile is one TMA box of one page.
+constexpr int kKvPage = 128;
+struct KvPages {
+  const int *pt;  // [slot][ppr] page ids
+  int ppr;        // pages per slot
+};
+__device__ __forceinline__ int kv_page(const KvPages &pg, int req, int pos) {
+  return __ldg(pg.pt + static_cast<size_t>(req) * pg.ppr + pos / kKvPage);
+}
+// Cache row of (request, kv head, position); -1 when the position has no page.
+__device__ __forceinline__ int kv_row(const KvPages &pg, int Hkv, int req, int h, int pos) {
+  const int page = kv_page(pg, req, pos);
+  return page < 0 ? -1 : (page * Hkv + h) * kKvPage + pos % kKvPage;
+}
+
 // ---------------------------------------------------------------------------
 // Embedding gather (Embedding::forward -> CpuBackend::embedding,
 // src/backend/cpu_backend.cpp:998-1033: an out-of-range id reads row 0).  The
@@ -94,9 +116,9 @@ struct QKVArgs {
   int d, kvd, D;             // q width, k/v width, head dim
   const float2 *rope;        // [max_pos][D/2] (cos, sin)
   int rope_max_pos;
-  void *kc, *vc;             // this layer's caches
-  size_t kv_req_stride;      // elements per request slot
-  int S_cap;                 // positions per (request, head)
+  void *kc, *vc;             // this layer's page pools
+  KvPages pg;                // the requests' page tables
+  int S_cap;                 // positions per request
   int kv_mode;               // cache element type: 0 fp32, 1 bf16, 2 int8 (rows staged for kv_quant_kernel)
   float *stage;              // kv_mode 2: [R][2 * kvd] fp32 K and V of this pass's rows
   int *err;
@@ -319,7 +341,12 @@ __device__ __forceinline__ void linear_epilogue(const LinearArgs &a, int r, int 
       const bool is_k = n < q.d + q.kvd;
       const int nn = is_k ? n - q.d : n - q.d - q.kvd;
       const int h = nn / q.D, e = nn % q.D;
-      const size_t off = static_cast<size_t>(p.req) * q.kv_req_stride + (static_cast<size_t>(h) * q.S_cap + slot) * q.D + e;
+      const int row = kv_row(q.pg, q.kvd / q.D, p.req, h, slot);
+      if (row < 0) {
+        if (q.err) atomicOr(q.err, kErrSeqLen);
+        return;
+      }
+      const size_t off = static_cast<size_t>(row) * q.D + e;
       if (q.kv_mode == 2) {
         float *st = q.stage + static_cast<size_t>(r) * 2 * q.kvd + (is_k ? 0 : q.kvd) + nn;
         st[0] = v0;
@@ -529,8 +556,8 @@ __global__ void __launch_bounds__(32 * kLinWarps, 2) linear_kernel(LinearArgs a)
 // QKV pass staged, per (row, kv head): s = absmax / 127 (0 -> 1), q =
 // round(x * (1 / s)) clamped to +-127.  One warp per (row, head, K|V).
 static __global__ void kv_quant_kernel(RowsView rows, int R, const float *__restrict__ stage, int kvd, int D, int Hkv,
-                                int S_cap, int8_t *__restrict__ kc, int8_t *__restrict__ vc, float *__restrict__ ks,
-                                float *__restrict__ vs) {
+                                int S_cap, KvPages pg, int8_t *__restrict__ kc, int8_t *__restrict__ vc,
+                                float *__restrict__ ks, float *__restrict__ vs) {
   const int r = blockIdx.x;
   if (r >= R) return;
   const int req = rows.req[r], pos = row_slot(rows, r);
@@ -546,7 +573,9 @@ static __global__ void kv_quant_kernel(RowsView rows, int R, const float *__rest
     float sc = __fdiv_rn(mx, 127.0f);
     if (sc == 0.0f) sc = 1.0f;
     const float inv = __fdiv_rn(1.0f, sc);
-    const size_t row = (static_cast<size_t>(req) * Hkv + h) * S_cap + pos;
+    const int prow = kv_row(pg, Hkv, req, h, pos);
+    if (prow < 0) continue;  // the QKV pass flagged the missing page
+    const size_t row = static_cast<size_t>(prow);
     int8_t *dst = (is_v ? vc : kc) + row * D;
     for (int e = lane; e < D; e += 32) {
       const float qv = fminf(127.0f, fmaxf(-127.0f, roundf(__fmul_rn(src[e], inv))));
@@ -618,7 +647,8 @@ struct AttnGeom {
 };
 
 struct alignas(64) AttnArgs {
-  CUtensorMap tmk, tmv;  // 2-D views [slot * Hkv * S_cap + position][D] of this layer's K and V cache
+  CUtensorMap tmk, tmv;  // 2-D views [cache row][D] of this layer's K and V page pools
+  KvPages pg;
   const void *q;
   int ldq;
   RowsView rows;
@@ -771,17 +801,22 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
   // The splits share the positions the group's queries see (0 .. maxpos), so
   // every split has work while the cache is shorter than its capacity; a
   // split never exceeds a.chunk positions (the staging the host sized).
+  // Splits start at multiples of the tile, so no tile straddles a page.
   auto span = [&](int maxpos, int &j0, int &j1) {
-    const int ch = min(a.chunk, (maxpos + a.nsplit) / a.nsplit);
+    const int ch = min(a.chunk, ((maxpos + a.nsplit) / a.nsplit + kTile - 1) / kTile * kTile);
     j0 = split * ch;
     j1 = min(maxpos + 1, j0 + ch);
     return (j1 > j0) ? (j1 - j0 + kTile - 1) / kTile : 0;
   };
-  auto issue = [&](int t, int row0, int j0) {  // thread 0 only
+  auto issue = [&](int t, int req, int j0) {  // thread 0 only
     const int s = t & 1;
     unsigned char *kdst = tiles + s * G::kStageBytes;
     unsigned char *vdst = kdst + kTile * G::kRowBytes;
-    const int y = row0 + j0 + t * kTile;
+    int y = kv_row(a.pg, a.Hkv, req, hk, j0 + t * kTile);
+    if (y < 0) {  // a position without a page: flagged, and a valid row is read instead
+      if (a.err) atomicOr(a.err, kErrSeqLen);
+      y = 0;
+    }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&bars[s])),
                  "r"(G::kStageBytes)
@@ -820,7 +855,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     if (req >= 0 && maxpos < a.S_cap) {
       int j0, j1;
-      if (span(maxpos, j0, j1) > 0) issue(0, (req * a.Hkv + hk) * a.S_cap, j0);
+      if (span(maxpos, j0, j1) > 0) issue(0, req, j0);
     }
   }
   constexpr int kQIter = (QT * D + kAttnThreads - 1) / kAttnThreads;
@@ -839,7 +874,6 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
   if (req < 0 || maxpos >= a.S_cap) return;
   int j0, j1;
   const int ntiles = span(maxpos, j0, j1);
-  const int row0 = (req * a.Hkv + hk) * a.S_cap;
 
   float m[QT], l[QT], acc[QT][EPL];
   int qpos[QT], qtb[QT];
@@ -863,7 +897,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
   for (; t < ntiles; ++t) {
     const int t0 = j0 + t * kTile;
     const int nt = min(kTile, j1 - t0);
-    if (threadIdx.x == 0 && t + 1 < ntiles) issue(t + 1, row0, j0);  // the other stage was released at the end of t-1
+    if (threadIdx.x == 0 && t + 1 < ntiles) issue(t + 1, req, j0);  // the other stage was released at the end of t-1
     ok = __syncthreads_and(mbar_wait(&bars[t & 1], (t >> 1) & 1) ? 1 : 0) != 0;
     if (!ok) break;
     const unsigned char *kt = tiles + (t & 1) * G::kStageBytes;
@@ -874,9 +908,10 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
     const int pos = t0 + r;
     float ksc = 1.f, vsc = 1.f;
     if constexpr (kI8) {
-      if (r < nt) {
-        ksc = __ldg(a.k_scale + row0 + pos);
-        vsc = __ldg(a.v_scale + row0 + pos);
+      const int yb = kv_row(a.pg, a.Hkv, req, hk, t0);  // the tile's first cache row (one page)
+      if (r < nt && yb >= 0) {
+        ksc = __ldg(a.k_scale + yb + r);
+        vsc = __ldg(a.v_scale + yb + r);
       }
     }
     float sc[QT];

@@ -292,7 +292,12 @@ __device__ __forceinline__ void chunk_store(const LinearArgs &a, int row, int n,
       const bool is_k = n < q.d + q.kvd;
       const int nn = is_k ? n - q.d : n - q.d - q.kvd;
       const int h = nn / q.D, e = nn % q.D;
-      const size_t off = static_cast<size_t>(req) * q.kv_req_stride + (static_cast<size_t>(h) * q.S_cap + slot) * q.D + e;
+      const int crow = kv_row(q.pg, q.kvd / q.D, req, h, slot);
+      if (crow < 0) {
+        if (q.err) atomicOr(q.err, kErrSeqLen);
+        return;
+      }
+      const size_t off = static_cast<size_t>(crow) * q.D + e;
       if (q.kv_mode == 2) {
         float4 *st = reinterpret_cast<float4 *>(q.stage + static_cast<size_t>(row) * 2 * q.kvd + (is_k ? 0 : q.kvd) + nn);
 #pragma unroll

@@ -102,7 +102,12 @@ __device__ __forceinline__ void w8_epilogue(const LinearArgs &a, int r, int f, b
       const bool is_k = f < q.d + q.kvd;
       const int nn = is_k ? f - q.d : f - q.d - q.kvd;
       const int h = nn / q.D, e = nn % q.D;
-      const size_t off = static_cast<size_t>(req) * q.kv_req_stride + (static_cast<size_t>(h) * q.S_cap + slot) * q.D + e;
+      const int crow = kv_row(q.pg, q.kvd / q.D, req, h, slot);
+      if (crow < 0) {
+        if (q.err) atomicOr(q.err, kErrSeqLen);
+        return;
+      }
+      const size_t off = static_cast<size_t>(crow) * q.D + e;
       if (q.kv_mode == 2) q.stage[static_cast<size_t>(r) * 2 * q.kvd + (is_k ? 0 : q.kvd) + nn] = v;
       else if (q.kv_mode == 1) static_cast<AT *>(is_k ? q.kc : q.vc)[off] = __float2bfloat16_rn(v);
       else static_cast<float *>(is_k ? q.kc : q.vc)[off] = v;

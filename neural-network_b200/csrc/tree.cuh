@@ -184,10 +184,10 @@ __global__ void __launch_bounds__(kSampThreads) tree_accept_kernel(SpecState st,
 
 // One model's KV cache as the compaction kernel sees it.
 struct CacheView {
-  void *k, *v;        // [layer][slot][kv head][S_cap][D]
-  float *ks, *vs;     // int8 cache: [layer][slot][kv head][S_cap] scales, else null
+  void *k, *v;        // [layer][cache row][D] page pools
+  float *ks, *vs;     // int8 cache: [layer][cache row] scales, else null
   size_t layer_elems;
-  size_t req_stride;  // elements per request slot
+  KvPages pg;         // the requests' page tables
   int S_cap, Hkv, D, L, elt;
 };
 
@@ -206,15 +206,17 @@ __global__ void tree_compact_kernel(SpecState st, CacheView tc, CacheView dc) {
   const int cnt = tgt ? n : st.cp_dn[b];
   const int root = tgt ? st.cp_t0[b] : st.cp_d0[b];
   const int *path = st.cp_path + b * kTreeMaxDepth;
-  const size_t base = layer * c.layer_elems + static_cast<size_t>(b) * c.req_stride;
+  const size_t base = layer * c.layer_elems;
   const int per = c.Hkv * c.D;
   for (int x = threadIdx.x; x < per; x += blockDim.x) {
     const int h = x / c.D, e = x % c.D;
     for (int j = 0; j < cnt; ++j) {
       const int src = root + 1 + path[j], dst = root + 1 + j;
       if (src == dst) continue;
-      const size_t so = base + (static_cast<size_t>(h) * c.S_cap + src) * c.D + e;
-      const size_t dof = base + (static_cast<size_t>(h) * c.S_cap + dst) * c.D + e;
+      const int rs = kv_row(c.pg, c.Hkv, b, h, src), rd = kv_row(c.pg, c.Hkv, b, h, dst);
+      if (rs < 0 || rd < 0) continue;  // the verify pass flagged positions without pages
+      const size_t so = base + static_cast<size_t>(rs) * c.D + e;
+      const size_t dof = base + static_cast<size_t>(rd) * c.D + e;
       if (c.elt == 4) {
         static_cast<float *>(c.k)[dof] = static_cast<const float *>(c.k)[so];
         static_cast<float *>(c.v)[dof] = static_cast<const float *>(c.v)[so];
@@ -225,9 +227,9 @@ __global__ void tree_compact_kernel(SpecState st, CacheView tc, CacheView dc) {
         static_cast<int8_t *>(c.k)[dof] = static_cast<const int8_t *>(c.k)[so];
         static_cast<int8_t *>(c.v)[dof] = static_cast<const int8_t *>(c.v)[so];
         if (e == 0) {
-          const size_t sb = (base / c.D) + static_cast<size_t>(h) * c.S_cap;
-          c.ks[sb + dst] = c.ks[sb + src];
-          c.vs[sb + dst] = c.vs[sb + src];
+          const size_t sb = base / c.D;
+          c.ks[sb + rd] = c.ks[sb + rs];
+          c.vs[sb + rd] = c.vs[sb + rs];
         }
       }
     }

@@ -60,7 +60,7 @@ class _Config(C.Structure):
     _fields_ = [("target", _ModelConfig), ("draft", _ModelConfig), ("draft_shares_target", C.c_int32),
                 ("weight_dtype", C.c_int32), ("act_dtype", C.c_int32), ("kv_dtype", C.c_int32),
                 ("max_batch", C.c_int32), ("max_lookahead", C.c_int32), ("max_prompt_len", C.c_int32),
-                ("max_tree_nodes", C.c_int32)]
+                ("max_tree_nodes", C.c_int32), ("kv_pages", C.c_int32)]
 
 
 class _Tree(C.Structure):
@@ -156,14 +156,14 @@ class Engine:
     def __init__(self, target: ModelShape, draft_layers: Optional[int] = None, draft: Optional[ModelShape] = None,
                  weight_dtype: int = F32, act_dtype: int = F32, kv_dtype: int = F32, max_batch: int = 1,
                  max_lookahead: int = 4, max_prompt_len: int = 128, device: int = 0, max_tree_nodes: int = 0,
-                 tp_rank: int = 0, tp_world: int = 1, tp_id: Optional[bytes] = None):
+                 tp_rank: int = 0, tp_world: int = 1, tp_id: Optional[bytes] = None, kv_pages: int = 0):
         lib = load_library()
         shares = draft is None
         if shares and draft_layers is None:
             raise ValueError("give draft_layers (shared draft) or a draft shape")
         dshape = target.with_layers(draft_layers) if shares else draft
         cfg = _Config(_mcfg(target), _mcfg(dshape), 1 if shares else 0, weight_dtype, act_dtype, kv_dtype,
-                      max_batch, max_lookahead, max_prompt_len, max_tree_nodes)
+                      max_batch, max_lookahead, max_prompt_len, max_tree_nodes, kv_pages)
         h = C.c_void_p()
         if tp_world > 1:
             uid = C.create_string_buffer(bytes(tp_id), 128)

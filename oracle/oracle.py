@@ -118,7 +118,7 @@ class _SpecModelCfg(C.Structure):  # specdec_model_config (include/specdec.h)
 class _SpecCfg(C.Structure):  # specdec_config (include/specdec.h)
     _fields_ = [("target", _SpecModelCfg), ("draft", _SpecModelCfg)] + [
         (n, C.c_int32) for n in ("draft_shares_target", "weight_dtype", "act_dtype", "kv_dtype", "max_batch",
-                                 "max_lookahead", "max_prompt_len", "max_tree_nodes")]
+                                 "max_lookahead", "max_prompt_len", "max_tree_nodes", "kv_pages")]
 
 
 class CudaSpecBackendRef:

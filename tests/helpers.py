@@ -40,14 +40,14 @@ class Pair:
 def make_pair(shape: ModelShape, draft_layers: int, seed: int = 0, int8: bool = False, act_bf16: bool = False,
               kv_mode: int = 0, max_batch: int = 4, max_lookahead: int = 4, max_prompt_len: int = 64,
               bias_std: float = 0.02, ln_jitter: float = 0.05, head_std: Optional[float] = None,
-              max_tree_nodes: int = 0) -> Pair:
+              max_tree_nodes: int = 0, kv_pages: int = 0) -> Pair:
     P = make_params(shape, seed=seed, bias_std=bias_std, ln_jitter=ln_jitter, head_std=head_std)
     DP = draft_params(shape, P, draft_layers)
     eng = sd.Engine(shape, draft_layers=draft_layers, weight_dtype=sd.INT8 if int8 else sd.F32,
                     act_dtype=sd.BF16 if act_bf16 else sd.F32,
                     kv_dtype={0: sd.F32, 1: sd.BF16, 2: sd.INT8}[kv_mode],
                     max_batch=max_batch, max_lookahead=max_lookahead, max_prompt_len=max_prompt_len,
-                    max_tree_nodes=max_tree_nodes)
+                    max_tree_nodes=max_tree_nodes, kv_pages=kv_pages)
     eng.load_params(sd.TARGET, P)
     t = oracle.Oracle(shape, P, int8=int8)
     d = oracle.Oracle(shape.with_layers(draft_layers), DP, int8=int8)

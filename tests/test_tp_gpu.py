@@ -23,6 +23,17 @@ def _gpus():
         return 0
 
 
+def cfg_uid2(rank, idq):
+    """A second NCCL id for a second communicator, passed like the first."""
+    import specdec_b200 as sd
+    if rank == 0:
+        uid = sd.tp_unique_id()
+        for _ in range(WORLD - 1):
+            idq.put(uid)
+        return uid
+    return idq.get(timeout=120)
+
+
 def _worker(rank, idq, cfg, q):
     try:
         os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -51,8 +62,25 @@ def _worker(rank, idq, cfg, q):
         uni = sd.philox_uniforms(77, 3, 26, 9)
         ts, _ = eng.generate_speculative(prompts, 24, 4, 1.0, seed=77, uniforms=uni)
         eng.close()
+        # the round-level session on a handle loaded from device arrays (each
+        # rank slices and quantises its part on its GPU): the same tokens
+        import torch
+        eng = sd.Engine(shape, draft_layers=1, weight_dtype=cfg["wdt"], act_dtype=cfg["adt"], kv_dtype=cfg["kvdt"],
+                        max_batch=3, max_lookahead=4, max_prompt_len=cfg["S"], device=rank,
+                        tp_rank=rank, tp_world=WORLD, tp_id=cfg_uid2(rank, idq))
+        eng.load_params_device(sd.TARGET, [torch.from_numpy(np.ascontiguousarray(p, np.float32)).to(f"cuda:{rank}")
+                                           for p in P])
+        eng.prefill(prompts, 24, 4, 1.0, seed=77, uniforms=uni)
+        got = np.zeros(3, np.int64)
+        for _ in range(24):
+            _, cnt = eng.step(1)
+            got += cnt
+            if np.all(got >= 23):  # the first of the 24 new tokens came from the prefill
+                break
+        full, _ = eng.session_tokens()
+        eng.close()
         if rank == 0:
-            q.put(("ok", lg, tg, ts))
+            q.put(("ok", lg, tg, ts, full))
     except Exception as e:  # report instead of hanging the parent
         q.put(("err", f"rank {rank}: {e!r}"))
 
@@ -87,7 +115,8 @@ def test_tensor_parallel_matches_oracle(oracle_built, mode):
     bf = mode != "fp32"
     cfg = {"shape": shp, "seed": 3, "S": 80 if bf else 33, "wdt": sd.INT8 if bf else sd.F32,
            "adt": sd.BF16 if bf else sd.F32, "kvdt": sd.BF16 if bf else sd.F32}
-    lg, tg, ts = _run(cfg)
+    lg, tg, ts, session = _run(cfg)
+    assert np.array_equal(session, ts)
     shape = ModelShape(**shp)
     P = make_params(shape, seed=3, bias_std=0.02, ln_jitter=0.05)
     t = oracle.Oracle(shape, P, int8=bf)
