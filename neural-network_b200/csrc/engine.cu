@@ -44,6 +44,7 @@
 #include "kern_table.cuh"
 #include "attn_dec.cuh"
 #include "gemm_w8.cuh"
+#include "gemm_sk.cuh"
 
 using namespace specdec;
 
@@ -307,9 +308,17 @@ struct specdec_handle {
   // (opt-in: measured slower than the bf16-image GEMM on the large config)
   bool gemm_w8 = false;
   int w8_clusters[kW8MaxSplit + 1] = {};  // its split-K clusters of ks CTAs resident at once
-  bool w8_bf16_image = false;  // that GEMM streams the codes' bf16 image instead (no conversion)
   float *w8_ws = nullptr;  // its split-K partials: up to kW8WsTiles CTAs of kW8MaxRows x 128 fp32
   static constexpr int kW8WsTiles = 2 * 148;
+  // persistent stream-K GEMM for row batches of at most kSkMaxRows whose
+  // layers have at least sk_min_tiles 256-column tiles (QKV, gate/up, lm_head
+  // of the large config); narrower layers keep the cluster split-K.  Opt-in:
+  // measured slower than the tile GEMM on the large config
+  bool gemm_sk = false;
+  int sk_min_tiles = 40;
+  int sk_max_ctas = 0;       // persistent CTAs of a launch (0: one per SM)
+  float *sk_ws = nullptr;    // its partial tiles: two per CTA, 256 x 256 fp32
+  int *sk_ticket = nullptr;  // its per-tile counters
   int gemm_min_rows = kGemmMinRows;
   int gemm_wide_rows = 16;
   long long gemm_wide_elems = 2ll << 20;  // measured: the medium model's FFN down-projection (2.4M) at 32 rows
@@ -575,11 +584,13 @@ void upload_stacked(specdec_handle *h, int role, const std::vector<DenseSrc> &sr
     CK(cudaMemcpy(ds, scale.data(), Ntot * sizeof(float), cudaMemcpyHostToDevice));
   }
   if (i8 && act_bf16(h)) {
-    // exact bf16 image of the codes for the tensor-core GEMM (large row batches)
-    const size_t n = static_cast<size_t>(Ntot) * K;
+    // exact bf16 image of the codes for the tensor-core GEMM (large row
+    // batches), in the GEMM's tile order
+    const int nkb = (K + kBK - 1) / kBK;
+    const size_t n = static_cast<size_t>((Ntot + kBN - 1) / kBN) * nkb * kBN * kBK;
     void *dw16 = h->dalloc(n * 2, &own);
-    i8_to_bf16_kernel<<<static_cast<unsigned>(std::min<size_t>((n + 255) / 256, 4096)), 256, 0, h->stream>>>(
-        static_cast<const int8_t *>(dw), static_cast<__nv_bfloat16 *>(dw16), n);
+    i8_to_bf16_tiles_kernel<<<static_cast<unsigned>(std::min<size_t>((n + 255) / 256, 8192)), 256, 0, h->stream>>>(
+        static_cast<const int8_t *>(dw), static_cast<__nv_bfloat16 *>(dw16), Ntot, K, nkb, n);
     CK(cudaGetLastError());
     CK(cudaStreamSynchronize(h->stream));
     h->w_bf16[dw] = dw16;
@@ -881,6 +892,23 @@ CUtensorMap gemm_operand_map(const void *base, int K, int rows, int ld, int box_
   return m;
 }
 
+// 2-D TMA view of a bf16 weight image in tile order: rows of 64 elements
+// (128 bytes), block (t, kb) = rows (t nkb + kb) 256 .. + 255; box 64 x 256.
+CUtensorMap weight_tiles_map(const void *base, int K, int N) {
+  const int nkb = (K + kBK - 1) / kBK, nt = (N + kBN - 1) / kBN;
+  CUtensorMap m;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(kBK), static_cast<cuuint64_t>(nt) * nkb * kBN};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(kBK) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(kBN)};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = tensor_map_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims,
+                                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) fail(SPECDEC_ERR_CUDA, "cuTensorMapEncodeTiled failed with " + std::to_string(static_cast<int>(r)));
+  return m;
+}
+
 // LayerNorm of a's input rows (bf16) into contiguous rows at dst.
 bool ln_rows_ok(const LinearArgs &a) {
   return a.K % 8 == 0 && a.ldx % 8 == 0 && a.K <= 4096 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
@@ -924,16 +952,33 @@ bool try_launch_gemm(specdec_handle *h, LinearArgs a) {
   }
   GemmArgs g{};
   g.tma_a = gemm_operand_map(A, a.K, a.R, lda, kBM);
-  g.tma_b = gemm_operand_map(it->second, a.K, a.N, a.K, kBN);
+  g.tma_b = weight_tiles_map(it->second, a.K, a.N);
   a.in_g = a.in_b = nullptr;
   a.in_rows = nullptr;
   a.norm_out = nullptr;
   g.lin = a;
   g.err = h->st.err;
-  // split-K while the tiles leave most SMs idle: a power of two up to the
-  // largest cluster the device schedules, each split keeping one k-block at least
   const int gx = (a.N + kBN - 1) / kBN, gy = (a.R + kBM - 1) / kBM;
   const int nk = (a.K + kBK - 1) / kBK;
+  if (h->gemm_sk && h->sk_ws && a.R <= kSkMaxRows && gx >= h->sk_min_tiles && gx <= kSkMaxTiles) {
+    // row batches of a round over wide layers: the persistent stream-K GEMM
+    GemmSkArgs s{};
+    s.tma_a = g.tma_a;
+    s.tma_b = g.tma_b;
+    s.lin = a;
+    s.mt = gy;
+    s.nt = gx;
+    s.nk = nk;
+    s.ctas = std::min(h->sk_max_ctas > 0 ? std::min(h->sk_max_ctas, h->num_sms) : h->num_sms, gx * nk);
+    s.ws = h->sk_ws;
+    s.ticket = h->sk_ticket;
+    s.err = h->st.err;
+    CK(gemm_sk_launch(EPI, s, h->stream));
+    ++h->launches;
+    return true;
+  }
+  // split-K while the tiles leave most SMs idle: a power of two up to the
+  // largest cluster the device schedules, each split keeping one k-block at least
   int ks = 1;
   while (h->gemm_ws && 2 * ks <= h->gemm_max_split && gx * gy * 2 * ks <= h->num_sms && 2 * ks <= nk &&
          gx * gy <= h->gemm_clusters[2 * ks])  // all clusters in one wave
@@ -988,11 +1033,10 @@ bool try_launch_gemm_w8(specdec_handle *h, LinearArgs a) {
   }
   GemmW8Args g{};
   g.np = (a.R + 15) / 16 * 16;
-  auto img = h->w_bf16.find(a.W);
-  g.w_bf16 = (h->w8_bf16_image && img != h->w_bf16.end()) ? 1 : 0;
+  g.w_bf16 = 0;  // the codes themselves (the bf16 image is in the other GEMM's tile order)
   gemm_w8_rings(g.np, g.w_bf16, &g.stages_w, &g.stages_x);
   g.tma_x = gemm_operand_map(A, a.K, a.R, lda, g.np);
-  g.tma_w = g.w_bf16 ? gemm_operand_map(img->second, a.K, a.N, a.K, kW8Feat) : w8_operand_map(a.W, a.K, a.N);
+  g.tma_w = w8_operand_map(a.W, a.K, a.N);
   a.in_g = a.in_b = nullptr;
   a.in_rows = nullptr;
   a.norm_out = nullptr;
@@ -2006,7 +2050,10 @@ int create_impl(const specdec_config *cfg, int device, int rank, int world, cons
     CK(cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAtcSmem));
     CK(attn_dec_set_attrs());
     CK(gemm_w8_set_attrs(h->w8_clusters));
-    if (const char *e = std::getenv("SPECDEC_W8_BF16_IMAGE")) h->w8_bf16_image = std::atoi(e) != 0;
+    CK(gemm_sk_set_attrs());
+    if (const char *e = std::getenv("SPECDEC_GEMM_SK")) h->gemm_sk = std::atoi(e) != 0;  // 1: the stream-K GEMM
+    if (const char *e = std::getenv("SPECDEC_SK_MIN_TILES")) h->sk_min_tiles = std::max(1, std::atoi(e));
+    if (const char *e = std::getenv("SPECDEC_SK_CTAS")) h->sk_max_ctas = std::max(0, std::atoi(e));
     if (const char *e = std::getenv("SPECDEC_GEMM_W8")) h->gemm_w8 = std::atoi(e) != 0;  // 1: the int8-code GEMM
     if (const char *e = std::getenv("SPECDEC_ATTN_DEC")) h->attn_dec = std::atoi(e) != 0;  // 0: not the decode kernel
     // GEMV / GEMM routing thresholds, for tuning measurements
@@ -2111,6 +2158,9 @@ int create_impl(const specdec_config *cfg, int device, int rank, int world, cons
     if (cfg->act_dtype == SPECDEC_BF16 && cfg->weight_dtype == SPECDEC_INT8) {
       h->w8_ws = static_cast<float *>(
           h->dalloc(static_cast<size_t>(specdec_handle::kW8WsTiles) * kW8MaxRows * kW8Feat * sizeof(float)));
+      h->sk_ws = static_cast<float *>(h->dalloc(static_cast<size_t>(h->num_sms) * 2 * 256 * 256 * sizeof(float)));
+      h->sk_ticket = static_cast<int *>(h->dalloc(kSkMaxTiles * sizeof(int)));
+      CK(cudaMemset(h->sk_ticket, 0, kSkMaxTiles * sizeof(int)));
     }
     h->tree_base =
         h->R_max + 2 * B + (k - 1) * B + B * (k + 1);
@@ -2809,12 +2859,12 @@ extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const
     int *pt;
     int ppr, tcap, dcap, R_max;
     cudaStream_t stream;
-    float *gemm_ws, *ad_part, *w8_ws;
+    float *gemm_ws, *ad_part, *w8_ws, *sk_ws;
   };
   Saved sv{h->X, h->H, h->X1, h->A, h->Q, h->ATT, h->tk, h->tv, h->dk, h->dv, h->tks, h->tvs, h->dks, h->dvs, h->KVN,
            h->st.err, h->pool,
            h->t_layer_stride, h->d_layer_stride, h->d_pt, h->ppr, h->t_cap, h->d_cap, h->R_max,
-           h->stream, h->gemm_ws, h->ad_part, h->w8_ws};
+           h->stream, h->gemm_ws, h->ad_part, h->w8_ws, h->sk_ws};
   auto restore = [&] {
     h->X = sv.X; h->H = sv.H; h->X1 = sv.X1; h->A = sv.A; h->Q = sv.Q; h->ATT = sv.ATT;
     h->tk = sv.tk; h->tv = sv.tv; h->dk = sv.dk; h->dv = sv.dv;
@@ -2822,7 +2872,7 @@ extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const
     h->st.err = sv.err; h->pool = sv.pool;
     h->t_layer_stride = sv.tls; h->d_layer_stride = sv.dls; h->d_pt = sv.pt; h->ppr = sv.ppr;
     h->t_cap = sv.tcap; h->d_cap = sv.dcap; h->R_max = sv.R_max; h->stream = sv.stream;
-    h->gemm_ws = sv.gemm_ws; h->ad_part = sv.ad_part; h->w8_ws = sv.w8_ws;
+    h->gemm_ws = sv.gemm_ws; h->ad_part = sv.ad_part; h->w8_ws = sv.w8_ws; h->sk_ws = sv.sk_ws;
   };
   try {
     CK(cudaSetDevice(h->device));
@@ -2897,6 +2947,7 @@ extern "C" int specdec_forward_logits_noalloc(specdec_handle *h, int role, const
     h->gemm_ws = nullptr;
     h->ad_part = nullptr;
     h->w8_ws = nullptr;
+    h->sk_ws = nullptr;
     CK(cudaMemsetAsync(h->st.err, 0, sizeof(int), st));
     // The tensor-core attention multiplies whole 128-position tiles, the
     // rows past S with probability 0: they must hold finite values, and the

@@ -51,7 +51,7 @@ constexpr int kGemmMaxSplit = 8;                        // portable cluster size
 
 struct alignas(64) GemmArgs {
   CUtensorMap tma_a;  // [R][K] bf16 rows, box kBK x kBM, 128-byte swizzle
-  CUtensorMap tma_b;  // [N][K] bf16 weights, box kBK x kBN, 128-byte swizzle
+  CUtensorMap tma_b;  // bf16 weight image in tile order ([tile][k-block][256][64]), box kBK x kBN, 128-byte swizzle
   LinearArgs lin;     // epilogue operands (out, scale, bias, resid, rows, qkv), R, N, K
   int *err;
   int ksplit;         // CTAs per tile along z (a cluster), 1, 2, 4 or 8
@@ -373,7 +373,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
       unsigned char *sb = sa + kGemmABytes;
       mbar_expect_tx(&full[s], kGemmStageBytes);
       tma_load_2d(sa, &g.tma_a, (kb0 + kb) * kBK, m0, &full[s]);
-      tma_load_2d(sb, &g.tma_b, (kb0 + kb) * kBK, n0, &full[s]);
+      tma_load_2d(sb, &g.tma_b, 0, (blockIdx.x * nk_all + kb0 + kb) * kBN, &full[s]);
     }
   } else if (threadIdx.x == 32) {
     // MMA issuer
@@ -631,10 +631,23 @@ __global__ void ln_rows_kernel(const __nv_bfloat16 *__restrict__ x, int ldx, con
 }
 
 // int8 weight codes -> their exact bf16 values.
-static __global__ void i8_to_bf16_kernel(const int8_t *__restrict__ q, __nv_bfloat16 *__restrict__ out, size_t n) {
-  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
-       i += static_cast<size_t>(gridDim.x) * blockDim.x)
-    out[i] = __float2bfloat16_rn(static_cast<float>(q[i]));
+// The exact bf16 image of int8 codes [N][K] in the tensor-core GEMM's tile
+// order: block (t, kb) = weight rows 256 t .. 256 t + 255, columns
+// 64 kb .. 64 kb + 63, stored as 32 contiguous KB ([256][64], zeros past N
+// and K) at block index t * nkb + kb.  One TMA box of the GEMM is then one
+// contiguous read; in the row-major [N][K] layout it was 256 segments of
+// 128 bytes, K * 2 bytes apart.
+static __global__ void i8_to_bf16_tiles_kernel(const int8_t *__restrict__ q, __nv_bfloat16 *__restrict__ out, int N,
+                                               int K, int nkb, size_t total) {
+  for (size_t o = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; o < total;
+       o += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t blk = o / (kBN * kBK);
+    const int within = static_cast<int>(o % (kBN * kBK));
+    const int r = within / kBK, c = within % kBK;
+    const int t = static_cast<int>(blk / nkb), kb = static_cast<int>(blk % nkb);
+    const int n = t * kBN + r, k = kb * kBK + c;
+    out[o] = __float2bfloat16_rn((n < N && k < K) ? static_cast<float>(q[static_cast<size_t>(n) * K + k]) : 0.f);
+  }
 }
 
 }  // namespace specdec

@@ -1,0 +1,402 @@
+// Linear layer y = x . W + b on tcgen05 for the row batches of a speculative
+// round -- draft steps (32 or 64 rows on the large configuration) and verify
+// blocks (k + 1 rows per request: 160) -- as a persistent stream-K GEMM
+// (Dense / QuantizedDense forward, src/nn/layer.cpp:162-171,
+// src/nn/quantization.cpp:7-147: y = x . (q * s) + b, the scale applied per
+// output column in the epilogue, as the GEMV does).
+//
+// Why.  With 128 x 256 tiles a 32-row draft launch of the SwiGLU gate/up
+// projection (22016 x 4096) is 86 tiles: 62 of the 148 SMs idle while the
+// others stream 2 MB of weights each.  A 160-row verify launch is 172 tiles
+// (two row tiles per weight tile), 1.16 waves, and reads every weight tile
+// twice.  Here:
+//   * one CTA per SM (g.ctas of them) walks an equal share of the units
+//     (256-column tile, 64-wide k-block): CTA c takes units
+//     [c U / ctas, (c + 1) U / ctas), U = tiles x k-blocks, so every SM
+//     streams the same number of weight bytes;
+//   * a unit covers all the launch's rows: up to two 128-row accumulators
+//     (TMEM columns 0-255 and 256-511) take their MMAs from the same weight
+//     tile, so each weight byte crosses HBM once per launch;
+//   * a tile that one CTA covers whole gets its epilogue straight from
+//     TMEM; the pieces of a tile shared by several CTAs are stored as fp32
+//     partial tiles in an L2-resident workspace, and the CTA that stores the
+//     last piece (atomic ticket per tile) adds them in CTA order -- the same
+//     sum on every run, whichever CTA finishes last -- and runs the epilogue.
+//     No CTA ever waits for another.
+//   * With one row tile the two TMEM halves are a double buffer: the
+//     epilogue of one segment overlaps the MMAs of the next.
+//
+// Roles: warp 0 streams (A row tiles, B weight tile) stages with TMA
+// (128-byte swizzle, no multicast), warp 1 issues tcgen05.mma (M = 128,
+// N = 256, K = 16, both operands K-major from shared memory) and commits the
+// stages and accumulators, warps 2-5 read their 32 TMEM lanes (rows) with
+// tcgen05.ld and run the epilogue (the chunk functions of gemm.cuh: scale
+// and bias, residual, RoPE + paged cache append, SwiGLU, GELU, logits).
+// Every mbarrier wait is bounded; a wait that gives up raises kErrTimeout and
+// the CTA winds down (the host reports the error).
+#include <algorithm>
+
+#include "gemm.cuh"
+#include "gemm_sk.cuh"
+
+namespace specdec {
+
+namespace {
+
+constexpr int kSkThreads = 192;         // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int kSkRing = 192 * 1024;     // 4 stages of 48 KB (one row tile) or 3 of 64 KB (two)
+constexpr int kSkSmemBytes = kSkRing + 1024;
+constexpr int kSkTmemCols = 512;        // two 256-column fp32 accumulators
+constexpr int kSkMaxStages = 4;
+constexpr int kSkPiece = 256 * 256;     // floats of one partial tile: [256 columns][256 rows]
+
+__device__ __forceinline__ int sk_start(int c, int U, int P) {
+  return static_cast<int>(static_cast<long long>(c) * U / P);
+}
+// The CTA whose units include unit u: the largest c with sk_start(c) <= u.
+__device__ __forceinline__ int sk_owner(int u, int U, int P) {
+  return static_cast<int>((static_cast<long long>(u + 1) * P + U - 1) / U) - 1;
+}
+
+__device__ __forceinline__ bool bar_and_epi(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 1, 128, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v))
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void bar_epi() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Row metadata of the QKV epilogue (request, RoPE position, cache position).
+template <int EPI>
+__device__ __forceinline__ void sk_rowmeta(const LinearArgs &a, int row, bool ok, int &req, int &pos, int &slot) {
+  req = 0; pos = 0; slot = 0;
+  if constexpr (EPI == kEpiQKV) {
+    req = ok ? a.rows.req[row] : -1;
+    pos = ok ? a.rows.pos[row] : 0;
+    slot = ok ? row_slot(a.rows, row) : 0;
+  }
+}
+
+__device__ __forceinline__ int sk_ld_acquire(const int *p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// The epilogue of one row of one tile, 64 columns at a time.  The values
+// come from TMEM at tb (own < -1 ... see below), plus stored pieces:
+//   own == -1: the accumulators alone (a tile this CTA covers whole);
+//   own >= 0:  the pieces of CTAs cf .. cl in CTA order, CTA own's from TMEM;
+//   own == -2: the pieces of CTAs cf .. cl, all from the workspace.
+// tcgen05.ld is warp-collective: every lane runs the loads, rows past R
+// only skip the arithmetic and the stores.
+template <int EPI>
+__device__ __forceinline__ void sk_rows_epilogue(const LinearArgs &a, const GemmSkArgs &g, int row, uint32_t tb,
+                                                 int n0, int ncols, int own, int cf, int cl, int u0, int U, int P,
+                                                 const float *s_scale, const float *s_bias) {
+  const bool row_ok = row < a.R;
+  int req, pos, slot;
+  sk_rowmeta<EPI>(a, row, row_ok, req, pos, slot);
+  for (int g0 = 0; g0 < ncols; g0 += 64) {
+    // the group's row operands (residual or RoPE pairs) in flight first
+    ChunkOps op[4];
+    if (row_ok)
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (g0 + 16 * q < ncols) chunk_load<EPI>(a, row, n0 + g0 + 16 * q, req, pos, op[q]);
+    float v[64];
+    if (own == -1) {
+      tmem_ld64(tb + g0, v);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 64; ++e) v[e] = 0.f;
+      for (int q = cf; q <= cl; ++q) {
+        if (q == own) {  // warp-uniform
+          float mine[64];
+          tmem_ld64(tb + g0, mine);
+#pragma unroll
+          for (int e = 0; e < 64; ++e) v[e] += mine[e];
+          continue;
+        }
+        if (!row_ok) continue;
+        // CTA q's piece of this tile is its first segment when q starts
+        // inside the tile, else its last
+        const int w = sk_start(q, U, P) >= u0 ? 0 : 1;
+        const float4 *src =
+            reinterpret_cast<const float4 *>(g.ws + (static_cast<size_t>(q) * 2 + w) * kSkPiece +
+                                             static_cast<size_t>(row) * 256 + g0);
+        float4 x[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) x[e] = __ldcg(src + e);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          v[4 * e] += x[e].x;
+          v[4 * e + 1] += x[e].y;
+          v[4 * e + 2] += x[e].z;
+          v[4 * e + 3] += x[e].w;
+        }
+      }
+    }
+    if (!row_ok) continue;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int cc = g0 + 16 * q;
+      if (cc >= ncols) break;
+      float w16[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) w16[e] = v[16 * q + e];
+      chunk_store<EPI>(a, row, n0 + cc, w16, op[q], s_scale + cc, s_bias + cc, req, pos, slot);
+    }
+  }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kSkThreads, 1) gemm_sk_kernel(const __grid_constant__ GemmSkArgs g) {
+  extern __shared__ unsigned char sk_smem_raw[];
+  unsigned char *ring =
+      reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(sk_smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full[kSkMaxStages], empty[kSkMaxStages], acc_full[2], acc_empty[2], fin;
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_fail, s_last;
+  __shared__ __align__(16) float s_scale[kBN], s_bias[kBN];
+
+  const LinearArgs &a = g.lin;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mt = g.mt, nk = g.nk, P = g.ctas, c = blockIdx.x;
+  const int U = g.nt * nk;
+  const int u_begin = sk_start(c, U, P), u_end = sk_start(c + 1, U, P);
+  const int a_bytes = kBM * kBK * 2, b_bytes = kBN * kBK * 2;
+  const int stage_bytes = mt * a_bytes + b_bytes;
+  const int S = kSkRing / stage_bytes;  // 4 (one row tile) or 3 (two)
+  const int nbuf = mt == 1 ? 2 : 1;     // accumulator buffers
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                 "r"(kSkTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (threadIdx.x == 32) {
+    for (int s = 0; s < kSkMaxStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
+    mbar_init(&fin, 1);
+    s_fail = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+
+  if (warp == 0) {
+    // ---- producer: the CTA's units in order, through the stage ring -------
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int u = u_begin; u < u_end && ok; ++u) {
+        const int t = u / nk, kb = u - t * nk;
+        const int s = it % S;
+        if (it >= S && !mbar_wait(&empty[s], ((it / S) - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        unsigned char *st = ring + s * stage_bytes;
+        mbar_expect_tx(&full[s], static_cast<uint32_t>(stage_bytes));
+        for (int i = 0; i < mt; ++i) tma_load_2d(st + i * a_bytes, &g.tma_a, kb * kBK, i * kBM, &full[s]);
+        tma_load_2d(st + mt * a_bytes, &g.tma_b, 0, u * kBN, &full[s]);  // block (t, kb) of the tile-order image
+        ++it;
+      }
+      if (!ok) {
+        s_fail = 1;
+        // the copies already issued land before the CTA can leave
+        for (int j = max(0, it - S); j < it; ++j) mbar_wait(&full[j % S], (j / S) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer: one segment (a run of units in one tile) at a time ---
+    if (lane == 0) {
+      int it = 0, seg = 0;
+      bool ok = true;
+      for (int u = u_begin; u < u_end && ok; ++seg) {
+        const int t = u / nk, kb0 = u - t * nk;
+        const int kb1 = min(nk, kb0 + (u_end - u));
+        const int buf = seg % nbuf;
+        // the epilogue has drained this accumulator buffer
+        if (seg >= nbuf && !mbar_wait(&acc_empty[buf], ((seg / nbuf) - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % S;
+          if (!mbar_wait(&full[s], (it / S) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(ring + s * stage_bytes);
+          const uint32_t sb = sa + mt * a_bytes;
+          for (int i = 0; i < mt; ++i) {
+            const uint32_t d = tmem + static_cast<uint32_t>((buf + i) * kBN);
+#pragma unroll
+            for (int k = 0; k < kBK / 16; ++k)
+              tc_mma(d, umma_desc_k128(sa + i * a_bytes + 32 * k), umma_desc_k128(sb + 32 * k), kGemmIdesc,
+                     (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit(&empty[s]);  // the stage is free once these MMAs have read it
+        }
+        if (!ok) break;
+        tc_commit(&acc_full[buf]);  // the segment's accumulators are complete
+        u += kb1 - kb0;
+      }
+      if (!ok) s_fail = 1;
+      tc_commit(&fin);
+      mbar_wait(&fin, 0);  // no MMA in flight when TMEM is released
+    }
+  } else {
+    // ---- epilogue: warps 2-5, TMEM lane group warp % 4 --------------------
+    const int lg = warp & 3;
+    const int lr = lg * 32 + lane;  // this thread's row within a row tile
+    const uint32_t tl = tmem + (static_cast<uint32_t>(lg * 32) << 16);
+    int seg = 0;
+    for (int u = u_begin; u < u_end; ++seg) {
+      const int t = u / nk, kb0 = u - t * nk;
+      const int kb1 = min(nk, kb0 + (u_end - u));
+      const bool first = u == u_begin;
+      u += kb1 - kb0;
+      const int buf = seg % nbuf;
+      const int n0 = t * kBN;
+      const int ncols = min(kBN, a.N - n0);
+      if (!bar_and_epi(mbar_wait(&acc_full[buf], (seg / nbuf) & 1))) {
+        s_fail = 1;
+        break;
+      }
+      tc_fence_after();
+      const bool whole = kb0 == 0 && kb1 == nk;
+      const int cf = sk_owner(t * nk, U, P), cl = sk_owner(t * nk + nk - 1, U, P);
+      // merge now (this CTA's piece is the only one missing), store a piece,
+      // or (whole tile) run the epilogue on the accumulators alone
+      int mode = 0;  // 0 whole, 1 merge from TMEM + stored pieces, 2 store
+      if (!whole) {
+        if (threadIdx.x == 64) s_last = sk_ld_acquire(g.ticket + t) == cl - cf ? 1 : 0;
+        bar_epi();
+        mode = s_last ? 1 : 2;
+      }
+      if (mode != 2) {
+        // the tile's per-column scale and bias; s_scale / s_bias are free:
+        // the previous epilogue finished before the barrier above (or the
+        // one in bar_and_epi)
+        for (int j = threadIdx.x - 64; j < kBN; j += 128) {
+          const int n = n0 + j;
+          s_scale[j] = (n < a.N && a.scale) ? __ldg(a.scale + n) : 1.f;
+          s_bias[j] = n < a.N ? __ldg(a.bias + n) : 0.f;
+        }
+        if (mode == 1) __threadfence();
+        bar_epi();
+        for (int i = 0; i < mt; ++i) {
+          const int row = i * kBM + lr;
+          const uint32_t tb = tl + static_cast<uint32_t>((buf + i) * kBN);
+          sk_rows_epilogue<EPI>(a, g, row, tb, n0, ncols, mode == 1 ? c : -1, cf, cl, t * nk, U, P, s_scale, s_bias);
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[buf]);
+        if (mode == 1 && threadIdx.x == 64) g.ticket[t] = 0;  // ready for the next launch
+        bar_epi();  // s_scale / s_bias are read by every thread before the next segment rewrites them
+        continue;
+      }
+      // store this CTA's piece (row-major [256 rows][256 columns] fp32) in
+      // its first or last slot
+      float *piece = g.ws + (static_cast<size_t>(c) * 2 + (first ? 0 : 1)) * kSkPiece;
+      for (int i = 0; i < mt; ++i) {
+        const int row = i * kBM + lr;
+        const uint32_t tb = tl + static_cast<uint32_t>((buf + i) * kBN);
+        for (int g0 = 0; g0 < ncols; g0 += 64) {
+          float v[64];
+          tmem_ld64(tb + g0, v);  // warp-collective
+          if (row < a.R) {
+            float4 *dst = reinterpret_cast<float4 *>(piece + static_cast<size_t>(row) * 256 + g0);
+#pragma unroll
+            for (int q = 0; q < 16; ++q) __stcg(dst + q, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);  // the MMAs may refill this buffer
+      __threadfence();
+      bar_epi();
+      if (threadIdx.x == 64) s_last = atomicAdd(g.ticket + t, 1) == cl - cf ? 1 : 0;
+      bar_epi();
+      if (!s_last) continue;
+      // the last piece arrived meanwhile: add the stored pieces (this CTA's
+      // too), then the epilogue
+      for (int j = threadIdx.x - 64; j < kBN; j += 128) {
+        const int n = n0 + j;
+        s_scale[j] = (n < a.N && a.scale) ? __ldg(a.scale + n) : 1.f;
+        s_bias[j] = n < a.N ? __ldg(a.bias + n) : 0.f;
+      }
+      __threadfence();
+      bar_epi();
+      for (int i = 0; i < mt; ++i) {
+        const int row = i * kBM + lr;
+        sk_rows_epilogue<EPI>(a, g, row, 0u, n0, ncols, -2, cf, cl, t * nk, U, P, s_scale, s_bias);
+      }
+      if (threadIdx.x == 64) g.ticket[t] = 0;
+      bar_epi();
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && s_fail && g.err) atomicOr(g.err, kErrTimeout);
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kSkTmemCols) : "memory");
+}
+
+template <int EPI>
+cudaError_t set_attr_epi() {
+  return cudaFuncSetAttribute(gemm_sk_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSkSmemBytes);
+}
+
+template <int EPI>
+cudaError_t launch_epi(const GemmSkArgs &g, cudaStream_t stream) {
+  gemm_sk_kernel<EPI><<<g.ctas, kSkThreads, kSkSmemBytes, stream>>>(g);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+int gemm_sk_smem() { return kSkSmemBytes; }
+
+cudaError_t gemm_sk_set_attrs() {
+  cudaError_t e = set_attr_epi<kEpiStore>();
+  if (e == cudaSuccess) e = set_attr_epi<kEpiResid>();
+  if (e == cudaSuccess) e = set_attr_epi<kEpiQKV>();
+  if (e == cudaSuccess) e = set_attr_epi<kEpiSwiGLU>();
+  if (e == cudaSuccess) e = set_attr_epi<kEpiGelu>();
+  return e;
+}
+
+cudaError_t gemm_sk_launch(int epi, const GemmSkArgs &g, cudaStream_t stream) {
+  switch (epi) {
+    case kEpiStore: return launch_epi<kEpiStore>(g, stream);
+    case kEpiResid: return launch_epi<kEpiResid>(g, stream);
+    case kEpiQKV: return launch_epi<kEpiQKV>(g, stream);
+    case kEpiSwiGLU: return launch_epi<kEpiSwiGLU>(g, stream);
+    case kEpiGelu: return launch_epi<kEpiGelu>(g, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace specdec
