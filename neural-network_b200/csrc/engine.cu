@@ -311,14 +311,15 @@ struct specdec_handle {
   float *w8_ws = nullptr;  // its split-K partials: up to kW8WsTiles CTAs of kW8MaxRows x 128 fp32
   static constexpr int kW8WsTiles = 2 * 148;
   // persistent stream-K GEMM for row batches of at most kSkMaxRows whose
-  // layers have at least sk_min_tiles 256-column tiles (QKV, gate/up, lm_head
-  // of the large config); narrower layers keep the cluster split-K.  Opt-in:
-  // measured slower than the tile GEMM on the large config
-  bool gemm_sk = false;
-  int sk_min_tiles = 40;
+  // layers have at least sk_min_tiles 256-column tiles: the gate/up
+  // projection (86 tiles) and lm_head (125) of the large config.  Measured
+  // there: faster than the tile GEMM from about 80 tiles (verify gate/up 81
+  // against 105 us, lm_head 105 against 122 us), slower on QKV (48 tiles:
+  // 64 against 56 us), which keeps the tile GEMM with its cluster split-K
+  bool gemm_sk = true;
+  int sk_min_tiles = 80;
   int sk_max_ctas = 0;       // persistent CTAs of a launch (0: one per SM)
   float *sk_ws = nullptr;    // its partial tiles: two per CTA, 256 x 256 fp32
-  int *sk_ticket = nullptr;  // its per-tile counters
   int gemm_min_rows = kGemmMinRows;
   int gemm_wide_rows = 16;
   long long gemm_wide_elems = 2ll << 20;  // measured: the medium model's FFN down-projection (2.4M) at 32 rows
@@ -971,10 +972,9 @@ bool try_launch_gemm(specdec_handle *h, LinearArgs a) {
     s.nk = nk;
     s.ctas = std::min(h->sk_max_ctas > 0 ? std::min(h->sk_max_ctas, h->num_sms) : h->num_sms, gx * nk);
     s.ws = h->sk_ws;
-    s.ticket = h->sk_ticket;
     s.err = h->st.err;
     CK(gemm_sk_launch(EPI, s, h->stream));
-    ++h->launches;
+    h->launches += 2;
     return true;
   }
   // split-K while the tiles leave most SMs idle: a power of two up to the
@@ -2051,7 +2051,7 @@ int create_impl(const specdec_config *cfg, int device, int rank, int world, cons
     CK(attn_dec_set_attrs());
     CK(gemm_w8_set_attrs(h->w8_clusters));
     CK(gemm_sk_set_attrs());
-    if (const char *e = std::getenv("SPECDEC_GEMM_SK")) h->gemm_sk = std::atoi(e) != 0;  // 1: the stream-K GEMM
+    if (const char *e = std::getenv("SPECDEC_GEMM_SK")) h->gemm_sk = std::atoi(e) != 0;  // 0: no stream-K GEMM
     if (const char *e = std::getenv("SPECDEC_SK_MIN_TILES")) h->sk_min_tiles = std::max(1, std::atoi(e));
     if (const char *e = std::getenv("SPECDEC_SK_CTAS")) h->sk_max_ctas = std::max(0, std::atoi(e));
     if (const char *e = std::getenv("SPECDEC_GEMM_W8")) h->gemm_w8 = std::atoi(e) != 0;  // 1: the int8-code GEMM
@@ -2159,8 +2159,6 @@ int create_impl(const specdec_config *cfg, int device, int rank, int world, cons
       h->w8_ws = static_cast<float *>(
           h->dalloc(static_cast<size_t>(specdec_handle::kW8WsTiles) * kW8MaxRows * kW8Feat * sizeof(float)));
       h->sk_ws = static_cast<float *>(h->dalloc(static_cast<size_t>(h->num_sms) * 2 * 256 * 256 * sizeof(float)));
-      h->sk_ticket = static_cast<int *>(h->dalloc(kSkMaxTiles * sizeof(int)));
-      CK(cudaMemset(h->sk_ticket, 0, kSkMaxTiles * sizeof(int)));
     }
     h->tree_base =
         h->R_max + 2 * B + (k - 1) * B + B * (k + 1);

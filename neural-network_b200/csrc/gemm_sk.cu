@@ -19,10 +19,10 @@
 //     tile, so each weight byte crosses HBM once per launch;
 //   * a tile that one CTA covers whole gets its epilogue straight from
 //     TMEM; the pieces of a tile shared by several CTAs are stored as fp32
-//     partial tiles in an L2-resident workspace, and the CTA that stores the
-//     last piece (atomic ticket per tile) adds them in CTA order -- the same
-//     sum on every run, whichever CTA finishes last -- and runs the epilogue.
-//     No CTA ever waits for another.
+//     partial tiles in an L2-resident workspace, and a second, wide launch
+//     (gemm_sk_fixup_kernel: one block per tile, row tile and 64 columns)
+//     adds them in CTA order -- the same sum on every run -- and runs the
+//     epilogue.  No CTA ever waits for another.
 //   * With one row tile the two TMEM halves are a double buffer: the
 //     epilogue of one segment overlaps the MMAs of the next.
 //
@@ -83,66 +83,24 @@ __device__ __forceinline__ void sk_rowmeta(const LinearArgs &a, int row, bool ok
   }
 }
 
-__device__ __forceinline__ int sk_ld_acquire(const int *p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-// The epilogue of one row of one tile, 64 columns at a time.  The values
-// come from TMEM at tb (own < -1 ... see below), plus stored pieces:
-//   own == -1: the accumulators alone (a tile this CTA covers whole);
-//   own >= 0:  the pieces of CTAs cf .. cl in CTA order, CTA own's from TMEM;
-//   own == -2: the pieces of CTAs cf .. cl, all from the workspace.
-// tcgen05.ld is warp-collective: every lane runs the loads, rows past R
-// only skip the arithmetic and the stores.
+// The epilogue of one row of a tile this CTA covers whole, from its TMEM
+// accumulators at tb, 64 columns at a time (the row operands of the group in
+// flight before the TMEM load).  tcgen05.ld is warp-collective: every lane
+// runs the loads, rows past R skip the arithmetic and the stores.
 template <int EPI>
-__device__ __forceinline__ void sk_rows_epilogue(const LinearArgs &a, const GemmSkArgs &g, int row, uint32_t tb,
-                                                 int n0, int ncols, int own, int cf, int cl, int u0, int U, int P,
+__device__ __forceinline__ void sk_rows_epilogue(const LinearArgs &a, int row, uint32_t tb, int n0, int ncols,
                                                  const float *s_scale, const float *s_bias) {
   const bool row_ok = row < a.R;
   int req, pos, slot;
   sk_rowmeta<EPI>(a, row, row_ok, req, pos, slot);
   for (int g0 = 0; g0 < ncols; g0 += 64) {
-    // the group's row operands (residual or RoPE pairs) in flight first
     ChunkOps op[4];
     if (row_ok)
 #pragma unroll
       for (int q = 0; q < 4; ++q)
         if (g0 + 16 * q < ncols) chunk_load<EPI>(a, row, n0 + g0 + 16 * q, req, pos, op[q]);
     float v[64];
-    if (own == -1) {
-      tmem_ld64(tb + g0, v);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 64; ++e) v[e] = 0.f;
-      for (int q = cf; q <= cl; ++q) {
-        if (q == own) {  // warp-uniform
-          float mine[64];
-          tmem_ld64(tb + g0, mine);
-#pragma unroll
-          for (int e = 0; e < 64; ++e) v[e] += mine[e];
-          continue;
-        }
-        if (!row_ok) continue;
-        // CTA q's piece of this tile is its first segment when q starts
-        // inside the tile, else its last
-        const int w = sk_start(q, U, P) >= u0 ? 0 : 1;
-        const float4 *src =
-            reinterpret_cast<const float4 *>(g.ws + (static_cast<size_t>(q) * 2 + w) * kSkPiece +
-                                             static_cast<size_t>(row) * 256 + g0);
-        float4 x[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) x[e] = __ldcg(src + e);
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          v[4 * e] += x[e].x;
-          v[4 * e + 1] += x[e].y;
-          v[4 * e + 2] += x[e].z;
-          v[4 * e + 3] += x[e].w;
-        }
-      }
-    }
+    tmem_ld64(tb + g0, v);
     if (!row_ok) continue;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -163,7 +121,7 @@ __global__ void __launch_bounds__(kSkThreads, 1) gemm_sk_kernel(const __grid_con
       reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(sk_smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t full[kSkMaxStages], empty[kSkMaxStages], acc_full[2], acc_empty[2], fin;
   __shared__ uint32_t s_tmem;
-  __shared__ int s_fail, s_last;
+  __shared__ int s_fail;
   __shared__ __align__(16) float s_scale[kBN], s_bias[kBN];
 
   const LinearArgs &a = g.lin;
@@ -285,39 +243,26 @@ __global__ void __launch_bounds__(kSkThreads, 1) gemm_sk_kernel(const __grid_con
       }
       tc_fence_after();
       const bool whole = kb0 == 0 && kb1 == nk;
-      const int cf = sk_owner(t * nk, U, P), cl = sk_owner(t * nk + nk - 1, U, P);
-      // merge now (this CTA's piece is the only one missing), store a piece,
-      // or (whole tile) run the epilogue on the accumulators alone
-      int mode = 0;  // 0 whole, 1 merge from TMEM + stored pieces, 2 store
-      if (!whole) {
-        if (threadIdx.x == 64) s_last = sk_ld_acquire(g.ticket + t) == cl - cf ? 1 : 0;
-        bar_epi();
-        mode = s_last ? 1 : 2;
-      }
-      if (mode != 2) {
-        // the tile's per-column scale and bias; s_scale / s_bias are free:
-        // the previous epilogue finished before the barrier above (or the
-        // one in bar_and_epi)
+      if (whole) {
+        // the tile's per-column scale and bias (s_scale / s_bias are free:
+        // the previous epilogue ended before the barrier in bar_and_epi)
         for (int j = threadIdx.x - 64; j < kBN; j += 128) {
           const int n = n0 + j;
           s_scale[j] = (n < a.N && a.scale) ? __ldg(a.scale + n) : 1.f;
           s_bias[j] = n < a.N ? __ldg(a.bias + n) : 0.f;
         }
-        if (mode == 1) __threadfence();
         bar_epi();
         for (int i = 0; i < mt; ++i) {
-          const int row = i * kBM + lr;
           const uint32_t tb = tl + static_cast<uint32_t>((buf + i) * kBN);
-          sk_rows_epilogue<EPI>(a, g, row, tb, n0, ncols, mode == 1 ? c : -1, cf, cl, t * nk, U, P, s_scale, s_bias);
+          sk_rows_epilogue<EPI>(a, i * kBM + lr, tb, n0, ncols, s_scale, s_bias);
         }
         tc_fence_before();
         mbar_arrive(&acc_empty[buf]);
-        if (mode == 1 && threadIdx.x == 64) g.ticket[t] = 0;  // ready for the next launch
-        bar_epi();  // s_scale / s_bias are read by every thread before the next segment rewrites them
         continue;
       }
-      // store this CTA's piece (row-major [256 rows][256 columns] fp32) in
-      // its first or last slot
+      // a piece of a shared tile: column-major [256 columns][256 rows] fp32
+      // (a warp's 32 rows of one column are one 128-byte line) in this CTA's
+      // first or last slot; gemm_sk_fixup_kernel adds the pieces
       float *piece = g.ws + (static_cast<size_t>(c) * 2 + (first ? 0 : 1)) * kSkPiece;
       for (int i = 0; i < mt; ++i) {
         const int row = i * kBM + lr;
@@ -325,35 +270,13 @@ __global__ void __launch_bounds__(kSkThreads, 1) gemm_sk_kernel(const __grid_con
         for (int g0 = 0; g0 < ncols; g0 += 64) {
           float v[64];
           tmem_ld64(tb + g0, v);  // warp-collective
-          if (row < a.R) {
-            float4 *dst = reinterpret_cast<float4 *>(piece + static_cast<size_t>(row) * 256 + g0);
+          if (row < a.R)
 #pragma unroll
-            for (int q = 0; q < 16; ++q) __stcg(dst + q, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
-          }
+            for (int e = 0; e < 64; ++e) __stcg(piece + static_cast<size_t>(g0 + e) * 256 + row, v[e]);
         }
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[buf]);  // the MMAs may refill this buffer
-      __threadfence();
-      bar_epi();
-      if (threadIdx.x == 64) s_last = atomicAdd(g.ticket + t, 1) == cl - cf ? 1 : 0;
-      bar_epi();
-      if (!s_last) continue;
-      // the last piece arrived meanwhile: add the stored pieces (this CTA's
-      // too), then the epilogue
-      for (int j = threadIdx.x - 64; j < kBN; j += 128) {
-        const int n = n0 + j;
-        s_scale[j] = (n < a.N && a.scale) ? __ldg(a.scale + n) : 1.f;
-        s_bias[j] = n < a.N ? __ldg(a.bias + n) : 0.f;
-      }
-      __threadfence();
-      bar_epi();
-      for (int i = 0; i < mt; ++i) {
-        const int row = i * kBM + lr;
-        sk_rows_epilogue<EPI>(a, g, row, 0u, n0, ncols, -2, cf, cl, t * nk, U, P, s_scale, s_bias);
-      }
-      if (threadIdx.x == 64) g.ticket[t] = 0;
-      bar_epi();
     }
   }
 
@@ -364,6 +287,62 @@ __global__ void __launch_bounds__(kSkThreads, 1) gemm_sk_kernel(const __grid_con
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kSkTmemCols) : "memory");
 }
 
+// The fix-up of the shared tiles: block (t, i, gq) = tile t, row tile i,
+// columns 64 gq .. 64 gq + 63, thread = row.  It adds the pieces of the tile's
+// CTAs cf .. cl in CTA order -- the same sum on every run -- and runs the
+// epilogue.  Blocks of whole tiles (one CTA, epilogue already done) return at
+// once.  Many small blocks spread the merge over every SM, where one CTA per
+// tile adding its pieces alone made the tail of the GEMM.
+template <int EPI>
+__global__ void __launch_bounds__(128) gemm_sk_fixup_kernel(const __grid_constant__ GemmSkArgs g) {
+  const LinearArgs &a = g.lin;
+  const int t = blockIdx.x, i = blockIdx.y, g0 = blockIdx.z * 64;
+  const int nk = g.nk, P = g.ctas, U = g.nt * nk;
+  const int u0 = t * nk;
+  const int cf = sk_owner(u0, U, P), cl = sk_owner(u0 + nk - 1, U, P);
+  const int n0 = t * kBN;
+  const int ncols = min(kBN, a.N - n0);
+  if (cf == cl || g0 >= ncols) return;  // uniform over the block
+  __shared__ __align__(16) float s_scale[64], s_bias[64];
+  if (threadIdx.x < 64) {
+    const int n = n0 + g0 + threadIdx.x;
+    s_scale[threadIdx.x] = (n < a.N && a.scale) ? __ldg(a.scale + n) : 1.f;
+    s_bias[threadIdx.x] = n < a.N ? __ldg(a.bias + n) : 0.f;
+  }
+  __syncthreads();
+  const int row = i * kBM + threadIdx.x;
+  if (row >= a.R) return;
+  int req, pos, slot;
+  sk_rowmeta<EPI>(a, row, true, req, pos, slot);
+  ChunkOps op[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    if (g0 + 16 * q < ncols) chunk_load<EPI>(a, row, n0 + g0 + 16 * q, req, pos, op[q]);
+  float v[64];
+#pragma unroll
+  for (int e = 0; e < 64; ++e) v[e] = 0.f;
+  for (int q = cf; q <= cl; ++q) {
+    // CTA q's piece of this tile is its first segment when q starts inside
+    // the tile, else its last
+    const int w = sk_start(q, U, P) >= u0 ? 0 : 1;
+    const float *src = g.ws + (static_cast<size_t>(q) * 2 + w) * kSkPiece + static_cast<size_t>(g0) * 256 + row;
+    float x[64];
+#pragma unroll
+    for (int e = 0; e < 64; ++e) x[e] = __ldcg(src + static_cast<size_t>(e) * 256);
+#pragma unroll
+    for (int e = 0; e < 64; ++e) v[e] += x[e];
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int cc = g0 + 16 * q;
+    if (cc >= ncols) break;
+    float w16[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) w16[e] = v[16 * q + e];
+    chunk_store<EPI>(a, row, n0 + cc, w16, op[q], s_scale + 16 * q, s_bias + 16 * q, req, pos, slot);
+  }
+}
+
 template <int EPI>
 cudaError_t set_attr_epi() {
   return cudaFuncSetAttribute(gemm_sk_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSkSmemBytes);
@@ -372,6 +351,9 @@ cudaError_t set_attr_epi() {
 template <int EPI>
 cudaError_t launch_epi(const GemmSkArgs &g, cudaStream_t stream) {
   gemm_sk_kernel<EPI><<<g.ctas, kSkThreads, kSkSmemBytes, stream>>>(g);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  gemm_sk_fixup_kernel<EPI><<<dim3(g.nt, g.mt, kBN / 64), 128, 0, stream>>>(g);
   return cudaGetLastError();
 }
 

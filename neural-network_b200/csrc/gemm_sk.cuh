@@ -11,7 +11,7 @@
 namespace specdec {
 
 constexpr int kSkMaxRows = 256;    // two 128-row accumulators share every weight tile
-constexpr int kSkMaxTiles = 1024;  // 256-column tiles of one launch (tickets per tile)
+constexpr int kSkMaxTiles = 4096;  // 256-column tiles of one launch (the fix-up grid's x)
 
 struct alignas(64) GemmSkArgs {
   CUtensorMap tma_a;  // [R][K] bf16 input rows, box 64 x 128, 128-byte swizzle
@@ -22,7 +22,6 @@ struct alignas(64) GemmSkArgs {
   int nk;             // 64-wide k-blocks
   int ctas;           // persistent CTAs (the grid): CTA c takes units [c U / ctas, (c + 1) U / ctas), U = nt nk
   float *ws;          // partial tiles: [cta][first | last][256 columns][256 rows] fp32
-  int *ticket;        // per tile: partial tiles stored so far (0 between launches)
   int *err;
 };
 
@@ -30,7 +29,8 @@ struct alignas(64) GemmSkArgs {
 int gemm_sk_smem();
 // Sets the kernels' shared-memory attribute (once per device).
 cudaError_t gemm_sk_set_attrs();
-// Launches the kernel of epilogue `epi` (an Epi) with g.ctas CTAs on `stream`.
+// Launches the kernel of epilogue `epi` (an Epi) with g.ctas CTAs on `stream`,
+// then the fix-up of its shared tiles (two launches).
 cudaError_t gemm_sk_launch(int epi, const GemmSkArgs &g, cudaStream_t stream);
 
 }  // namespace specdec
