@@ -157,6 +157,8 @@ __global__ void __launch_bounds__(kSkThreads, 1) gemm_sk_kernel(const __grid_con
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s_tmem;
+  // the fix-up launch may begin now: its blocks wait for this grid to finish
+  if (threadIdx.x == 0) pdl_launch();
 
   if (warp == 0) {
     // ---- producer: the CTA's units in order, through the stage ring -------
@@ -288,58 +290,76 @@ __global__ void __launch_bounds__(kSkThreads, 1) gemm_sk_kernel(const __grid_con
 }
 
 // The fix-up of the shared tiles: block (t, i, gq) = tile t, row tile i,
-// columns 64 gq .. 64 gq + 63, thread = row.  It adds the pieces of the tile's
-// CTAs cf .. cl in CTA order -- the same sum on every run -- and runs the
-// epilogue.  Blocks of whole tiles (one CTA, epilogue already done) return at
-// once.  Many small blocks spread the merge over every SM, where one CTA per
-// tile adding its pieces alone made the tail of the GEMM.
+// columns 32 gq .. 32 gq + 31, thread = row.  It adds the pieces of the
+// tile's CTAs cf .. cl in CTA order -- the same sum on every run -- and runs
+// the epilogue; blocks of whole tiles (one CTA, epilogue already done) return
+// at once.  It is launched as a programmatic dependent of the main kernel,
+// which allows it to launch at its start: the blocks are resident and wait in
+// griddepcontrol.wait (which returns once the main kernel has completed and
+// its stores are visible) instead of paying a launch after it.  The pieces
+// are loaded four at a time, all in flight together; the tile's scale and
+// bias go through shared memory.
 template <int EPI>
 __global__ void __launch_bounds__(128) gemm_sk_fixup_kernel(const __grid_constant__ GemmSkArgs g) {
+  // first of all, in every thread: the main kernel's pieces and every earlier
+  // kernel's outputs are complete and visible past this point, and this grid
+  // cannot complete before the main kernel (whatever its blocks skip), which
+  // the launches after it rely on
+  pdl_wait();
   const LinearArgs &a = g.lin;
-  const int t = blockIdx.x, i = blockIdx.y, g0 = blockIdx.z * 64;
+  const int t = blockIdx.x, i = blockIdx.y, g0 = blockIdx.z * 32;
   const int nk = g.nk, P = g.ctas, U = g.nt * nk;
   const int u0 = t * nk;
   const int cf = sk_owner(u0, U, P), cl = sk_owner(u0 + nk - 1, U, P);
   const int n0 = t * kBN;
   const int ncols = min(kBN, a.N - n0);
   if (cf == cl || g0 >= ncols) return;  // uniform over the block
-  __shared__ __align__(16) float s_scale[64], s_bias[64];
-  if (threadIdx.x < 64) {
+  __shared__ __align__(16) float ssc[32], sbi[32];
+  if (threadIdx.x < 32) {
     const int n = n0 + g0 + threadIdx.x;
-    s_scale[threadIdx.x] = (n < a.N && a.scale) ? __ldg(a.scale + n) : 1.f;
-    s_bias[threadIdx.x] = n < a.N ? __ldg(a.bias + n) : 0.f;
+    ssc[threadIdx.x] = (n < a.N && a.scale) ? __ldg(a.scale + n) : 1.f;
+    sbi[threadIdx.x] = n < a.N ? __ldg(a.bias + n) : 0.f;
   }
   __syncthreads();
   const int row = i * kBM + threadIdx.x;
   if (row >= a.R) return;
   int req, pos, slot;
   sk_rowmeta<EPI>(a, row, true, req, pos, slot);
-  ChunkOps op[4];
+  ChunkOps op[2];
 #pragma unroll
-  for (int q = 0; q < 4; ++q)
+  for (int q = 0; q < 2; ++q)
     if (g0 + 16 * q < ncols) chunk_load<EPI>(a, row, n0 + g0 + 16 * q, req, pos, op[q]);
-  float v[64];
+  float v[32];
 #pragma unroll
-  for (int e = 0; e < 64; ++e) v[e] = 0.f;
-  for (int q = cf; q <= cl; ++q) {
-    // CTA q's piece of this tile is its first segment when q starts inside
-    // the tile, else its last
-    const int w = sk_start(q, U, P) >= u0 ? 0 : 1;
-    const float *src = g.ws + (static_cast<size_t>(q) * 2 + w) * kSkPiece + static_cast<size_t>(g0) * 256 + row;
-    float x[64];
+  for (int e = 0; e < 32; ++e) v[e] = 0.f;
+  for (int q0 = cf; q0 <= cl; q0 += 4) {
+    float x[4][32];
 #pragma unroll
-    for (int e = 0; e < 64; ++e) x[e] = __ldcg(src + static_cast<size_t>(e) * 256);
+    for (int j = 0; j < 4; ++j) {
+      const int q = q0 + j;
+      if (q > cl) break;
+      // CTA q's piece of this tile is its first segment when q starts inside
+      // the tile, else its last
+      const int w = sk_start(q, U, P) >= u0 ? 0 : 1;
+      const float *src = g.ws + (static_cast<size_t>(q) * 2 + w) * kSkPiece + static_cast<size_t>(g0) * 256 + row;
 #pragma unroll
-    for (int e = 0; e < 64; ++e) v[e] += x[e];
+      for (int e = 0; e < 32; ++e) x[j][e] = __ldcg(src + static_cast<size_t>(e) * 256);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (q0 + j > cl) break;
+#pragma unroll
+      for (int e = 0; e < 32; ++e) v[e] += x[j][e];
+    }
   }
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
+  for (int q = 0; q < 2; ++q) {
     const int cc = g0 + 16 * q;
     if (cc >= ncols) break;
     float w16[16];
 #pragma unroll
     for (int e = 0; e < 16; ++e) w16[e] = v[16 * q + e];
-    chunk_store<EPI>(a, row, n0 + cc, w16, op[q], s_scale + 16 * q, s_bias + 16 * q, req, pos, slot);
+    chunk_store<EPI>(a, row, n0 + cc, w16, op[q], ssc + 16 * q, sbi + 16 * q, req, pos, slot);
   }
 }
 
@@ -353,8 +373,16 @@ cudaError_t launch_epi(const GemmSkArgs &g, cudaStream_t stream) {
   gemm_sk_kernel<EPI><<<g.ctas, kSkThreads, kSkSmemBytes, stream>>>(g);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  gemm_sk_fixup_kernel<EPI><<<dim3(g.nt, g.mt, kBN / 64), 128, 0, stream>>>(g);
-  return cudaGetLastError();
+  cudaLaunchConfig_t lc{};
+  lc.gridDim = dim3(g.nt, g.mt, kBN / 32);
+  lc.blockDim = dim3(128);
+  lc.stream = stream;
+  cudaLaunchAttribute at{};
+  at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at.val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = &at;
+  lc.numAttrs = 1;
+  return cudaLaunchKernelEx(&lc, gemm_sk_fixup_kernel<EPI>, g);
 }
 
 }  // namespace
