@@ -917,7 +917,7 @@ bool ln_rows_ok(const LinearArgs &a) {
 void launch_ln_rows(specdec_handle *h, const LinearArgs &a, void *dst) {
   if (!ln_rows_ok(a)) fail(SPECDEC_ERR_UNSUPPORTED, "LayerNorm rows must be a multiple of 8 wide and 16-byte aligned");
   auto ln = a.K <= 1024 ? ln_rows_kernel<4> : a.K <= 2048 ? ln_rows_kernel<8> : ln_rows_kernel<16>;
-  launch(h, ln, dim3((a.R + 7) / 8), dim3(256), 0, static_cast<const __nv_bfloat16 *>(a.x), a.ldx, a.in_rows, a.R,
+  launch_pdl(h, ln, dim3((a.R + 7) / 8), dim3(256), 0, static_cast<const __nv_bfloat16 *>(a.x), a.ldx, a.in_rows, a.R,
          a.K, a.in_g, a.in_b, static_cast<__nv_bfloat16 *>(dst), static_cast<__nv_bfloat16 *>(nullptr));
 }
 
@@ -973,7 +973,7 @@ bool try_launch_gemm(specdec_handle *h, LinearArgs a) {
     s.ctas = std::min(h->sk_max_ctas > 0 ? std::min(h->sk_max_ctas, h->num_sms) : h->num_sms, gx * nk);
     s.ws = h->sk_ws;
     s.err = h->st.err;
-    CK(gemm_sk_launch(EPI, s, h->stream));
+    CK(gemm_sk_launch(EPI, s, h->stream, h->use_pdl));
     h->launches += 2;
     return true;
   }
@@ -986,9 +986,9 @@ bool try_launch_gemm(specdec_handle *h, LinearArgs a) {
   g.ksplit = ks;
   g.ws = h->gemm_ws;
   if (ks == 1)
-    launch(h, gemm_kernel<EPI>, dim3(gx, gy), dim3(kGemmThreads), static_cast<size_t>(kGemmSmem), g);
+    launch_pdl(h, gemm_kernel<EPI>, dim3(gx, gy), dim3(kGemmThreads), static_cast<size_t>(kGemmSmem), g);
   else
-    launch_ex(h, false, gemm_kernel<EPI>, dim3(gx, gy, ks), dim3(kGemmThreads), static_cast<size_t>(kGemmSmem),
+    launch_ex(h, true, gemm_kernel<EPI>, dim3(gx, gy, ks), dim3(kGemmThreads), static_cast<size_t>(kGemmSmem),
               dim3(1, 1, ks), g);
   return true;
 }

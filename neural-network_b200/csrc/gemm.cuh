@@ -352,6 +352,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s_tmem;
+  // programmatic dependent launch: the successor may launch now and waits in
+  // griddepcontrol.wait for this grid; this grid's reads of its predecessors'
+  // outputs (input rows, residual, row tables) and all its writes come after
+  // its own wait, so the set-up above overlaps the predecessor's tail
+  pdl_launch();
+  pdl_wait();
 
   if (warp >= 2) {
     // the epilogue's per-column operands, while the main loop runs
@@ -573,6 +579,8 @@ template <int NV>
 __global__ void ln_rows_kernel(const __nv_bfloat16 *__restrict__ x, int ldx, const int *__restrict__ in_rows, int R,
                                int K, const float *__restrict__ g, const float *__restrict__ b,
                                __nv_bfloat16 *__restrict__ out, __nv_bfloat16 *__restrict__ norm_out) {
+  pdl_launch();
+  pdl_wait();  // the rows come from the predecessor
   const int lane = threadIdx.x & 31;
   const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (r >= R) return;

@@ -159,6 +159,9 @@ __global__ void __launch_bounds__(kSkThreads, 1) gemm_sk_kernel(const __grid_con
   const uint32_t tmem = s_tmem;
   // the fix-up launch may begin now: its blocks wait for this grid to finish
   if (threadIdx.x == 0) pdl_launch();
+  // launched as a programmatic dependent itself: the predecessors' outputs
+  // (input rows, residual, row tables) are read and every write made after
+  pdl_wait();
 
   if (warp == 0) {
     // ---- producer: the CTA's units in order, through the stage ring -------
@@ -369,17 +372,23 @@ cudaError_t set_attr_epi() {
 }
 
 template <int EPI>
-cudaError_t launch_epi(const GemmSkArgs &g, cudaStream_t stream) {
-  gemm_sk_kernel<EPI><<<g.ctas, kSkThreads, kSkSmemBytes, stream>>>(g);
-  cudaError_t e = cudaGetLastError();
+cudaError_t launch_epi(const GemmSkArgs &g, cudaStream_t stream, bool pdl) {
+  cudaLaunchAttribute at{};
+  at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at.val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t mc{};
+  mc.gridDim = dim3(g.ctas);
+  mc.blockDim = dim3(kSkThreads);
+  mc.dynamicSmemBytes = kSkSmemBytes;
+  mc.stream = stream;
+  mc.attrs = &at;
+  mc.numAttrs = pdl ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&mc, gemm_sk_kernel<EPI>, g);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t lc{};
   lc.gridDim = dim3(g.nt, g.mt, kBN / 32);
   lc.blockDim = dim3(128);
   lc.stream = stream;
-  cudaLaunchAttribute at{};
-  at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at.val.programmaticStreamSerializationAllowed = 1;
   lc.attrs = &at;
   lc.numAttrs = 1;
   return cudaLaunchKernelEx(&lc, gemm_sk_fixup_kernel<EPI>, g);
@@ -398,13 +407,13 @@ cudaError_t gemm_sk_set_attrs() {
   return e;
 }
 
-cudaError_t gemm_sk_launch(int epi, const GemmSkArgs &g, cudaStream_t stream) {
+cudaError_t gemm_sk_launch(int epi, const GemmSkArgs &g, cudaStream_t stream, bool pdl) {
   switch (epi) {
-    case kEpiStore: return launch_epi<kEpiStore>(g, stream);
-    case kEpiResid: return launch_epi<kEpiResid>(g, stream);
-    case kEpiQKV: return launch_epi<kEpiQKV>(g, stream);
-    case kEpiSwiGLU: return launch_epi<kEpiSwiGLU>(g, stream);
-    case kEpiGelu: return launch_epi<kEpiGelu>(g, stream);
+    case kEpiStore: return launch_epi<kEpiStore>(g, stream, pdl);
+    case kEpiResid: return launch_epi<kEpiResid>(g, stream, pdl);
+    case kEpiQKV: return launch_epi<kEpiQKV>(g, stream, pdl);
+    case kEpiSwiGLU: return launch_epi<kEpiSwiGLU>(g, stream, pdl);
+    case kEpiGelu: return launch_epi<kEpiGelu>(g, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -29,8 +29,9 @@ struct alignas(64) GemmSkArgs {
 int gemm_sk_smem();
 // Sets the kernels' shared-memory attribute (once per device).
 cudaError_t gemm_sk_set_attrs();
-// Launches the kernel of epilogue `epi` (an Epi) with g.ctas CTAs on `stream`,
-// then the fix-up of its shared tiles (two launches).
-cudaError_t gemm_sk_launch(int epi, const GemmSkArgs &g, cudaStream_t stream);
+// Launches the kernel of epilogue `epi` (an Epi) with g.ctas CTAs on `stream`
+// (a programmatic dependent of the previous launch when `pdl`), then the
+// fix-up of its shared tiles (two launches).
+cudaError_t gemm_sk_launch(int epi, const GemmSkArgs &g, cudaStream_t stream, bool pdl);
 
 }  // namespace specdec
