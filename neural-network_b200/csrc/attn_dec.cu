@@ -22,9 +22,12 @@
 //                  64-dim atoms 16 KB apart), B = P^T; TMEM lane = dim
 //   o = o * alpha + O_t in registers (thread = dim), one tile behind, so the
 //   fold overlaps the next tile's products.
-// Warp 0 streams K and V tiles through a six-slot TMA ring (32 KB per slot,
-// 192 KB in flight per SM), warp 1 issues the MMAs, warps 2-5 do the softmax
-// and the output.  CTAs are persistent (one per SM) and walk work items
+// Warp 0 streams K and V tiles through a three-slot TMA ring per CTA (32 KB
+// per slot; two CTAs per SM, 192 KB in flight per SM), warp 1 issues the
+// MMAs, and one or two warpgroups do the softmax and the output: for groups of
+// up to 2 queries one warpgroup carries every query column, for the 8- and
+// 16-column variants (verify blocks) two warpgroups split the columns, which
+// halves the per-thread softmax chain of a tile.  CTAs are persistent and walk work items
 // (group, head, split) in a fixed order, so the ring never drains between
 // items.  A (group, head) whose cache is split writes unnormalised partials;
 // the last of its splits to finish (an arrival counter) merges them with the
@@ -43,7 +46,10 @@ constexpr int kAdHalf = kAdTile * kAdD * 2;      // 32 KB: 128 positions x 128 b
 constexpr int kAdBox = kAdTile * 64 * 2;         // 16 KB: one 64-dim atom of a half tile
 constexpr int kAdQBytes = kAdN * kAdD * 2;       // 4 KB: 16 query rows, two 2 KB atoms
 constexpr int kAdPBytes = kAdN * kAdTile * 2;    // 4 KB: 16 query rows x 128 positions, two atoms
-constexpr int kAdThreads = 192;
+// warp 0 TMA, warp 1 MMA, then the softmax warpgroups: one for up to two query
+// columns, two (four columns each, or eight) for the 8- and 16-column groups
+constexpr int ad_qgroups(int nq) { return nq >= 8 ? 2 : 1; }
+constexpr int ad_threads(int nq) { return 64 + 128 * ad_qgroups(nq); }
 // three ring slots, two query buffers, one P buffer: 111 KB, two CTAs per SM
 constexpr int kAdSmem = kAdSlots * kAdHalf + 2 * kAdQBytes + kAdPBytes + 1024;
 constexpr int kAdTmemCols = 64;                  // S0 S1 O0 O1, 16 columns each
@@ -71,26 +77,38 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Named barrier of the four softmax warps that also ANDs a predicate over
+// Named barrier of the N softmax threads that also ANDs a predicate over
 // them, so a decision to stop is taken by all of them at the same point.
+template <int N>
 __device__ __forceinline__ bool bar_and_softmax(bool v) {
   uint32_t r;
   asm volatile(
-      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 1, 128, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 1, %2, p;\n selp.u32 %0, 1, 0, q;\n}\n"
       : "=r"(r)
-      : "r"(static_cast<uint32_t>(v))
+      : "r"(static_cast<uint32_t>(v)), "n"(N)
       : "memory");
   return r != 0;
 }
-__device__ __forceinline__ void bar_softmax() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bar_softmax() {
+  asm volatile("bar.sync 1, %0;" ::"n"(N) : "memory");
+}
 
-// NC accumulator columns of the warp's 32 TMEM lanes (NC = 8 or 16), waited for.
+// NC accumulator columns of the warp's 32 TMEM lanes (NC = 4, 8 or 16), waited for.
 template <int NC>
 __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&v)[NC]) {
   if constexpr (NC == 16) {
     tmem_ld16(taddr, v);
+  } else if constexpr (NC == 4) {
+    uint32_t r[4];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = __uint_as_float(r[i]);
   } else {
-    static_assert(NC == 8, "8 or 16 columns");
+    static_assert(NC == 8, "4, 8 or 16 columns");
     uint32_t r[8];
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
@@ -165,8 +183,11 @@ __device__ __forceinline__ AdItem ad_item(const AttnDecArgs &a, int item) {
 // NQ: the group's queries rounded up to 1, 2, 8 or 16 (the columns the
 // softmax threads carry; the MMAs always have 16).
 template <int NQ>
-__global__ void __launch_bounds__(kAdThreads, 2) attn_dec_kernel(const __grid_constant__ AttnDecArgs a) {
-  constexpr int NC = NQ <= 8 ? 8 : 16;  // TMEM columns read per product
+__global__ void __launch_bounds__(ad_threads(NQ), 2) attn_dec_kernel(const __grid_constant__ AttnDecArgs a) {
+  constexpr int QH = ad_qgroups(NQ);      // softmax warpgroups, each carrying NL query columns
+  constexpr int NL = NQ / QH;
+  constexpr int kSm = 128 * QH;           // softmax threads
+  constexpr int NC = QH == 1 ? (NQ <= 8 ? 8 : 16) : NL;  // TMEM columns a softmax thread reads per product
   pdl_wait();
   extern __shared__ unsigned char ad_smem_raw[];
   unsigned char *ring =
@@ -197,10 +218,10 @@ __global__ void __launch_bounds__(kAdThreads, 2) attn_dec_kernel(const __grid_co
       mbar_init(&q_full[i], 1);
       mbar_init(&q_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 4);
-      mbar_init(&p_full[i], 4);
+      mbar_init(&s_free[i], 4 * QH);
+      mbar_init(&p_full[i], 4 * QH);
       mbar_init(&o_full[i], 1);
-      mbar_init(&o_free[i], 4);
+      mbar_init(&o_free[i], 4 * QH);
     }
     mbar_init(&mma_done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -346,47 +367,53 @@ __global__ void __launch_bounds__(kAdThreads, 2) attn_dec_kernel(const __grid_co
     }
   } else {
     // ---- softmax and output: thread = position of a tile, and = dim of O ---
+    // QH warpgroups of four warps: warpgroup h carries query columns
+    // h NL .. h NL + NL - 1 of every position (its warps cover the four TMEM
+    // lane quadrants), so a thread's softmax chain per tile is NL columns long
     const int qd = warp & 3;  // TMEM lane quadrant of this warp
+    const int h = (warp - 2) >> 2;
+    const int q0 = h * NL;
     const int p = 32 * qd + lane;
-    const int own = lane / (32 / NQ);  // the query this lane holds after a reduce-scatter
-    const bool owner = (lane % (32 / NQ)) == 0;
+    const int own = lane / (32 / NL);  // the query (q0 + own) this lane holds after a reduce-scatter
+    const bool owner = (lane % (32 / NL)) == 0;
     const uint32_t tl = tmem + (static_cast<uint32_t>(32 * qd) << 16);
     int T = 0, ni = 0;
     // ok: the last barrier's verdict (the same in every softmax thread); lok:
     // this thread's own waits so far, folded into ok at the next barrier, so
-    // the four warps always stop at the same point
+    // the softmax warps always stop at the same point
     bool ok = true, lok = true;
     for (int item = blockIdx.x; item < a.n_items; item += gridDim.x, ++ni) {
       const AdItem it = ad_item(a, item);
-      int qpos[NQ], qtb[NQ];
-      unsigned long long qmask[NQ];
+      int qpos[NL], qtb[NL];
+      unsigned long long qmask[NL];
 #pragma unroll
-      for (int q = 0; q < NQ; ++q) {
+      for (int j = 0; j < NL; ++j) {
+        const int q = q0 + j;
         const int r = it.rq0 + q;
         const bool v = q < it.nq && a.rows.req[r] >= 0;
-        qpos[q] = v ? row_slot(a.rows, r) : -1;
-        qtb[q] = (v && a.rows.tb) ? a.rows.tb[r] : 0x7fffffff;
-        qmask[q] = (v && a.rows.mask) ? a.rows.mask[r] : 0ull;
+        qpos[j] = v ? row_slot(a.rows, r) : -1;
+        qtb[j] = (v && a.rows.tb) ? a.rows.tb[r] : 0x7fffffff;
+        qmask[j] = (v && a.rows.mask) ? a.rows.mask[r] : 0ull;
       }
-      float m[NQ], l[NQ], o[NQ], al_prev[NQ];
+      float m[NL], l[NL], o[NL], al_prev[NL];
 #pragma unroll
-      for (int q = 0; q < NQ; ++q) {
-        m[q] = -INFINITY;
-        l[q] = 0.f;
-        o[q] = 0.f;
-        al_prev[q] = 0.f;
+      for (int j = 0; j < NL; ++j) {
+        m[j] = -INFINITY;
+        l[j] = 0.f;
+        o[j] = 0.f;
+        al_prev[j] = 0.f;
       }
       auto fold = [&](int Tp) -> bool {  // o = o * alpha + O_{Tp}
         const int ob = Tp & 1;
         const bool w = mbar_wait(&o_full[ob], (Tp >> 1) & 1);
         tc_fence_after();
         float ov[NC];
-        tmem_ld_cols<NC>(tl + 32 + 16 * ob, ov);
+        tmem_ld_cols<NC>(tl + 32 + 16 * ob + q0, ov);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&o_free[ob]);
 #pragma unroll
-        for (int q = 0; q < NQ; ++q) o[q] = o[q] * al_prev[q] + ov[q];
+        for (int j = 0; j < NL; ++j) o[j] = o[j] * al_prev[j] + ov[j];
         return w;
       };
       for (int t = 0; t < it.nt; ++t, ++T) {
@@ -394,41 +421,42 @@ __global__ void __launch_bounds__(kAdThreads, 2) attn_dec_kernel(const __grid_co
         lok = mbar_wait(&s_full[sb], (T >> 1) & 1) && lok;
         tc_fence_after();
         float sc[NC];
-        tmem_ld_cols<NC>(tl + 16 * sb, sc);
+        tmem_ld_cols<NC>(tl + 16 * sb + q0, sc);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_free[sb]);
         const int pos = (it.t0 + t) * kAdTile + p;
-        float s[NQ];
+        float s[NL];
 #pragma unroll
-        for (int q = 0; q < NQ; ++q) {
+        for (int j = 0; j < NL; ++j) {
           // causal, and inside a token tree only the prefix, the ancestors and itself
-          const bool vis = pos <= qpos[q] &&
-                           (pos < qtb[q] || (pos - qtb[q] < 64 && ((qmask[q] >> (pos - qtb[q])) & 1ull)));
-          s[q] = vis ? sc[q] * kAdScale : -INFINITY;
+          const bool vis = pos <= qpos[j] &&
+                           (pos < qtb[j] || (pos - qtb[j] < 64 && ((qmask[j] >> (pos - qtb[j])) & 1ull)));
+          s[j] = vis ? sc[j] * kAdScale : -INFINITY;
         }
         {
-          const float wm = warp_reduce_scatter<NQ, true>(s, lane);
-          if (owner) red[sb][own][qd] = wm;
+          const float wm = warp_reduce_scatter<NL, true>(s, lane);
+          if (owner) red[sb][q0 + own][qd] = wm;
         }
-        ok = bar_and_softmax(lok && !s_abort);
+        ok = bar_and_softmax<kSm>(lok && !s_abort);
         if (!ok) break;
-        float al[NQ], pr[NQ];
+        float al[NL], pr[NL];
 #pragma unroll
-        for (int q = 0; q < NQ; ++q) {
-          al[q] = 1.f;
-          pr[q] = 0.f;
+        for (int j = 0; j < NL; ++j) {
+          const int q = q0 + j;
+          al[j] = 1.f;
+          pr[j] = 0.f;
           if (q < it.nq) {  // uniform over the CTA: columns past the group's queries do no work
             const float4 r4 = *reinterpret_cast<const float4 *>(&red[sb][q][0]);
-            const float mn = fmaxf(m[q], fmaxf(fmaxf(r4.x, r4.y), fmaxf(r4.z, r4.w)));
+            const float mn = fmaxf(m[j], fmaxf(fmaxf(r4.x, r4.y), fmaxf(r4.z, r4.w)));
             // the running maximum is the same in every thread: when the tile
             // leaves it unchanged the rescale is 1 without an exponential
-            if (mn != m[q]) al[q] = (m[q] == -INFINITY) ? 0.f : __expf(m[q] - mn);
+            if (mn != m[j]) al[j] = (m[j] == -INFINITY) ? 0.f : __expf(m[j] - mn);
             // P is rounded to bf16 for the product: the fast exponential's
             // error (a few ulp of fp32) is far below that rounding
-            pr[q] = (s[q] == -INFINITY) ? 0.f : __expf(s[q] - mn);
-            l[q] = l[q] * al[q] + pr[q];
-            m[q] = mn;
+            pr[j] = (s[j] == -INFINITY) ? 0.f : __expf(s[j] - mn);
+            l[j] = l[j] * al[j] + pr[j];
+            m[j] = mn;
           }
         }
         // O_{T-1} into the registers: then its product has read P, which
@@ -442,65 +470,69 @@ __global__ void __launch_bounds__(kAdThreads, 2) attn_dec_kernel(const __grid_co
           unsigned char *pt = sp + (p >> 6) * (kAdPBytes / 2);
           const int chunk = (p & 63) >> 3, byte = (p & 7) * 2;
 #pragma unroll
-          for (int q = 0; q < NQ; ++q)
+          for (int j = 0; j < NL; ++j) {
+            const int q = q0 + j;
             if (q < it.nq)
               *reinterpret_cast<__nv_bfloat16 *>(pt + q * 128 + ((chunk ^ (q & 7)) << 4) + byte) =
-                  __float2bfloat16_rn(pr[q]);
+                  __float2bfloat16_rn(pr[j]);
+          }
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[sb]);
 #pragma unroll
-        for (int q = 0; q < NQ; ++q) al_prev[q] = al[q];
+        for (int j = 0; j < NL; ++j) al_prev[j] = al[j];
       }
       if (ok && it.nt > 0) lok = fold(T - 1) && lok;
       // the row sums over the 128 positions
       const int lb = ni & 1;
       {
-        const float ws = warp_reduce_scatter<NQ, false>(l, lane);
-        if (owner) lred[lb][own][qd] = ws;
+        const float ws = warp_reduce_scatter<NL, false>(l, lane);
+        if (owner) lred[lb][q0 + own][qd] = ws;
       }
-      ok = bar_and_softmax(ok && lok && !s_abort);
+      ok = bar_and_softmax<kSm>(ok && lok && !s_abort);
       if (!ok) break;
-      float L[NQ];
+      float L[NL];
 #pragma unroll
-      for (int q = 0; q < NQ; ++q) {
-        const float4 r4 = *reinterpret_cast<const float4 *>(&lred[lb][q][0]);
-        L[q] = (r4.x + r4.y) + (r4.z + r4.w);
+      for (int j = 0; j < NL; ++j) {
+        const float4 r4 = *reinterpret_cast<const float4 *>(&lred[lb][q0 + j][0]);
+        L[j] = (r4.x + r4.y) + (r4.z + r4.w);
       }
       if (a.nsplit == 1) {
 #pragma unroll
-        for (int q = 0; q < NQ; ++q)
-          if (qpos[q] >= 0 && qpos[q] < a.S_cap)
-            a.out[static_cast<size_t>(it.rq0 + q) * a.ldo + it.h * kAdD + p] =
-                __float2bfloat16_rn(L[q] > 0.f ? __fdiv_rn(o[q], L[q]) : 0.f);
+        for (int j = 0; j < NL; ++j)
+          if (qpos[j] >= 0 && qpos[j] < a.S_cap)
+            a.out[static_cast<size_t>(it.rq0 + q0 + j) * a.ldo + it.h * kAdD + p] =
+                __float2bfloat16_rn(L[j] > 0.f ? __fdiv_rn(o[j], L[j]) : 0.f);
         continue;
       }
       // split: this item's partial, then the last split of (group, head) merges
+      // (whether any query of the group is valid is the same for every split,
+      // and for both warpgroups: they read the same rows)
       bool any = false;
-#pragma unroll
-      for (int q = 0; q < NQ; ++q) any |= qpos[q] >= 0;
-      if (!any) continue;  // the same for every split of the group
+      for (int q = 0; q < it.nq; ++q) any |= a.rows.req[it.rq0 + q] >= 0;
+      if (!any) continue;
       float *pp = a.part + static_cast<size_t>(item) * kAdPartFloats;
 #pragma unroll
-      for (int q = 0; q < NQ; ++q) pp[q * kAdD + p] = o[q];
+      for (int j = 0; j < NL; ++j) pp[(q0 + j) * kAdD + p] = o[j];
 #pragma unroll
-      for (int q = 0; q < NQ; ++q)
-        if (p == q) {
-          pp[kAdN * kAdD + q] = m[q];
-          pp[kAdN * kAdD + kAdN + q] = L[q];
+      for (int j = 0; j < NL; ++j)
+        if (p == q0 + j) {
+          pp[kAdN * kAdD + q0 + j] = m[j];
+          pp[kAdN * kAdD + kAdN + q0 + j] = L[j];
         }
       __threadfence();
-      bar_softmax();
+      bar_softmax<kSm>();
       const int gh = item / a.nsplit;
-      if (p == 0) s_last = (atomicAdd(a.ticket + gh, 1) == a.nsplit - 1) ? 1 : 0;
-      bar_softmax();
+      if (p == 0 && h == 0) s_last = (atomicAdd(a.ticket + gh, 1) == a.nsplit - 1) ? 1 : 0;
+      bar_softmax<kSm>();
       if (s_last) {
         __threadfence();
         const float *p0 = a.part + static_cast<size_t>(gh) * a.nsplit * kAdPartFloats;
 #pragma unroll 1
-        for (int q = 0; q < NQ; ++q) {
-          if (qpos[q] < 0 || qpos[q] >= a.S_cap) continue;
+        for (int j = 0; j < NL; ++j) {
+          const int q = q0 + j;
+          if (qpos[j] < 0 || qpos[j] >= a.S_cap) continue;
           float M = -INFINITY;
           for (int s2 = 0; s2 < a.nsplit; ++s2) {
             const float *ps = p0 + static_cast<size_t>(s2) * kAdPartFloats;
@@ -519,9 +551,9 @@ __global__ void __launch_bounds__(kAdThreads, 2) attn_dec_kernel(const __grid_co
           a.out[static_cast<size_t>(it.rq0 + q) * a.ldo + it.h * kAdD + p] =
               __float2bfloat16_rn(den > 0.f ? __fdiv_rn(num, den) : 0.f);
         }
-        if (p == 0) a.ticket[gh] = 0;
+        if (p == 0 && h == 0) a.ticket[gh] = 0;
       }
-      bar_softmax();  // s_last is rewritten by the next item
+      bar_softmax<kSm>();  // s_last is rewritten by the next item
     }
     if (!ok) give_up();
   }
@@ -552,7 +584,7 @@ template <int NQ>
 cudaError_t launch_one(const AttnDecArgs &a, int grid, cudaStream_t stream, bool pdl) {
   cudaLaunchConfig_t lc{};
   lc.gridDim = dim3(grid);
-  lc.blockDim = dim3(kAdThreads);
+  lc.blockDim = dim3(ad_threads(NQ));
   lc.dynamicSmemBytes = kAdSmem;
   lc.stream = stream;
   cudaLaunchAttribute at[1];
