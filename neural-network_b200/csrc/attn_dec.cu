@@ -180,6 +180,18 @@ __device__ __forceinline__ AdItem ad_item(const AttnDecArgs &a, int item) {
   return it;
 }
 
+// Column j QH + h of a thread's NC loaded accumulator columns (h < QH, not a
+// compile-time constant: a select, not an indexed register array).
+template <int QH, int NC>
+__device__ __forceinline__ float pick(const float (&v)[NC], int j, int h) {
+  if constexpr (QH == 1) {
+    return v[j];
+  } else {
+    static_assert(QH == 2, "one or two softmax warpgroups");
+    return h ? v[2 * j + 1] : v[2 * j];
+  }
+}
+
 // NQ: the group's queries rounded up to 1, 2, 8 or 16 (the columns the
 // softmax threads carry; the MMAs always have 16).
 template <int NQ>
@@ -187,7 +199,7 @@ __global__ void __launch_bounds__(ad_threads(NQ), 2) attn_dec_kernel(const __gri
   constexpr int QH = ad_qgroups(NQ);      // softmax warpgroups, each carrying NL query columns
   constexpr int NL = NQ / QH;
   constexpr int kSm = 128 * QH;           // softmax threads
-  constexpr int NC = QH == 1 ? (NQ <= 8 ? 8 : 16) : NL;  // TMEM columns a softmax thread reads per product
+  constexpr int NC = NQ <= 8 ? 8 : 16;  // TMEM columns read per product
   pdl_wait();
   extern __shared__ unsigned char ad_smem_raw[];
   unsigned char *ring =
@@ -368,13 +380,13 @@ __global__ void __launch_bounds__(ad_threads(NQ), 2) attn_dec_kernel(const __gri
   } else {
     // ---- softmax and output: thread = position of a tile, and = dim of O ---
     // QH warpgroups of four warps: warpgroup h carries query columns
-    // h NL .. h NL + NL - 1 of every position (its warps cover the four TMEM
-    // lane quadrants), so a thread's softmax chain per tile is NL columns long
+    // h, h + QH, h + 2 QH, ... of every position (its warps cover the four
+    // TMEM lane quadrants), so a thread's softmax chain per tile is NL columns
+    // long, and the real columns of a group (5 of 8 for k = 4) spread 3 + 2
     const int qd = warp & 3;  // TMEM lane quadrant of this warp
     const int h = (warp - 2) >> 2;
-    const int q0 = h * NL;
     const int p = 32 * qd + lane;
-    const int own = lane / (32 / NL);  // the query (q0 + own) this lane holds after a reduce-scatter
+    const int own = lane / (32 / NL);  // the query (own QH + h) this lane holds after a reduce-scatter
     const bool owner = (lane % (32 / NL)) == 0;
     const uint32_t tl = tmem + (static_cast<uint32_t>(32 * qd) << 16);
     int T = 0, ni = 0;
@@ -388,7 +400,7 @@ __global__ void __launch_bounds__(ad_threads(NQ), 2) attn_dec_kernel(const __gri
       unsigned long long qmask[NL];
 #pragma unroll
       for (int j = 0; j < NL; ++j) {
-        const int q = q0 + j;
+        const int q = j * QH + h;
         const int r = it.rq0 + q;
         const bool v = q < it.nq && a.rows.req[r] >= 0;
         qpos[j] = v ? row_slot(a.rows, r) : -1;
@@ -408,12 +420,12 @@ __global__ void __launch_bounds__(ad_threads(NQ), 2) attn_dec_kernel(const __gri
         const bool w = mbar_wait(&o_full[ob], (Tp >> 1) & 1);
         tc_fence_after();
         float ov[NC];
-        tmem_ld_cols<NC>(tl + 32 + 16 * ob + q0, ov);
+        tmem_ld_cols<NC>(tl + 32 + 16 * ob, ov);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&o_free[ob]);
 #pragma unroll
-        for (int j = 0; j < NL; ++j) o[j] = o[j] * al_prev[j] + ov[j];
+        for (int j = 0; j < NL; ++j) o[j] = o[j] * al_prev[j] + pick<QH>(ov, j, h);
         return w;
       };
       for (int t = 0; t < it.nt; ++t, ++T) {
@@ -421,7 +433,7 @@ __global__ void __launch_bounds__(ad_threads(NQ), 2) attn_dec_kernel(const __gri
         lok = mbar_wait(&s_full[sb], (T >> 1) & 1) && lok;
         tc_fence_after();
         float sc[NC];
-        tmem_ld_cols<NC>(tl + 16 * sb + q0, sc);
+        tmem_ld_cols<NC>(tl + 16 * sb, sc);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_free[sb]);
@@ -432,18 +444,18 @@ __global__ void __launch_bounds__(ad_threads(NQ), 2) attn_dec_kernel(const __gri
           // causal, and inside a token tree only the prefix, the ancestors and itself
           const bool vis = pos <= qpos[j] &&
                            (pos < qtb[j] || (pos - qtb[j] < 64 && ((qmask[j] >> (pos - qtb[j])) & 1ull)));
-          s[j] = vis ? sc[j] * kAdScale : -INFINITY;
+          s[j] = vis ? pick<QH>(sc, j, h) * kAdScale : -INFINITY;
         }
         {
           const float wm = warp_reduce_scatter<NL, true>(s, lane);
-          if (owner) red[sb][q0 + own][qd] = wm;
+          if (owner) red[sb][own * QH + h][qd] = wm;
         }
         ok = bar_and_softmax<kSm>(lok && !s_abort);
         if (!ok) break;
         float al[NL], pr[NL];
 #pragma unroll
         for (int j = 0; j < NL; ++j) {
-          const int q = q0 + j;
+          const int q = j * QH + h;
           al[j] = 1.f;
           pr[j] = 0.f;
           if (q < it.nq) {  // uniform over the CTA: columns past the group's queries do no work
@@ -471,7 +483,7 @@ __global__ void __launch_bounds__(ad_threads(NQ), 2) attn_dec_kernel(const __gri
           const int chunk = (p & 63) >> 3, byte = (p & 7) * 2;
 #pragma unroll
           for (int j = 0; j < NL; ++j) {
-            const int q = q0 + j;
+            const int q = j * QH + h;
             if (q < it.nq)
               *reinterpret_cast<__nv_bfloat16 *>(pt + q * 128 + ((chunk ^ (q & 7)) << 4) + byte) =
                   __float2bfloat16_rn(pr[j]);
@@ -488,21 +500,21 @@ __global__ void __launch_bounds__(ad_threads(NQ), 2) attn_dec_kernel(const __gri
       const int lb = ni & 1;
       {
         const float ws = warp_reduce_scatter<NL, false>(l, lane);
-        if (owner) lred[lb][q0 + own][qd] = ws;
+        if (owner) lred[lb][own * QH + h][qd] = ws;
       }
       ok = bar_and_softmax<kSm>(ok && lok && !s_abort);
       if (!ok) break;
       float L[NL];
 #pragma unroll
       for (int j = 0; j < NL; ++j) {
-        const float4 r4 = *reinterpret_cast<const float4 *>(&lred[lb][q0 + j][0]);
+        const float4 r4 = *reinterpret_cast<const float4 *>(&lred[lb][j * QH + h][0]);
         L[j] = (r4.x + r4.y) + (r4.z + r4.w);
       }
       if (a.nsplit == 1) {
 #pragma unroll
         for (int j = 0; j < NL; ++j)
           if (qpos[j] >= 0 && qpos[j] < a.S_cap)
-            a.out[static_cast<size_t>(it.rq0 + q0 + j) * a.ldo + it.h * kAdD + p] =
+            a.out[static_cast<size_t>(it.rq0 + j * QH + h) * a.ldo + it.h * kAdD + p] =
                 __float2bfloat16_rn(L[j] > 0.f ? __fdiv_rn(o[j], L[j]) : 0.f);
         continue;
       }
@@ -514,12 +526,12 @@ __global__ void __launch_bounds__(ad_threads(NQ), 2) attn_dec_kernel(const __gri
       if (!any) continue;
       float *pp = a.part + static_cast<size_t>(item) * kAdPartFloats;
 #pragma unroll
-      for (int j = 0; j < NL; ++j) pp[(q0 + j) * kAdD + p] = o[j];
+      for (int j = 0; j < NL; ++j) pp[(j * QH + h) * kAdD + p] = o[j];
 #pragma unroll
       for (int j = 0; j < NL; ++j)
-        if (p == q0 + j) {
-          pp[kAdN * kAdD + q0 + j] = m[j];
-          pp[kAdN * kAdD + kAdN + q0 + j] = L[j];
+        if (p == j * QH + h) {
+          pp[kAdN * kAdD + p] = m[j];
+          pp[kAdN * kAdD + kAdN + p] = L[j];
         }
       __threadfence();
       bar_softmax<kSm>();
@@ -531,7 +543,7 @@ __global__ void __launch_bounds__(ad_threads(NQ), 2) attn_dec_kernel(const __gri
         const float *p0 = a.part + static_cast<size_t>(gh) * a.nsplit * kAdPartFloats;
 #pragma unroll 1
         for (int j = 0; j < NL; ++j) {
-          const int q = q0 + j;
+          const int q = j * QH + h;
           if (qpos[j] < 0 || qpos[j] >= a.S_cap) continue;
           float M = -INFINITY;
           for (int s2 = 0; s2 < a.nsplit; ++s2) {
