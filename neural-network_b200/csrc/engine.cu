@@ -917,7 +917,7 @@ bool ln_rows_ok(const LinearArgs &a) {
 void launch_ln_rows(specdec_handle *h, const LinearArgs &a, void *dst) {
   if (!ln_rows_ok(a)) fail(SPECDEC_ERR_UNSUPPORTED, "LayerNorm rows must be a multiple of 8 wide and 16-byte aligned");
   auto ln = a.K <= 1024 ? ln_rows_kernel<4> : a.K <= 2048 ? ln_rows_kernel<8> : ln_rows_kernel<16>;
-  launch_pdl(h, ln, dim3((a.R + 7) / 8), dim3(256), 0, static_cast<const __nv_bfloat16 *>(a.x), a.ldx, a.in_rows, a.R,
+  launch_pdl(h, ln, dim3((a.R + 1) / 2), dim3(64), 0, static_cast<const __nv_bfloat16 *>(a.x), a.ldx, a.in_rows, a.R,
          a.K, a.in_g, a.in_b, static_cast<__nv_bfloat16 *>(dst), static_cast<__nv_bfloat16 *>(nullptr));
 }
 
