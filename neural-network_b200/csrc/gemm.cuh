@@ -466,24 +466,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     // order (the same sum on every run) and runs the epilogue on it.
     const size_t tile = static_cast<size_t>(blockIdx.x) + static_cast<size_t>(gridDim.x) * blockIdx.y;
     float *mine = g.ws + (tile * ks + z) * (kBN * kBM) + lr;
+    // (rows past R -- 96 of the 128 in a 32-row draft step -- are neither
+    // stored nor read: the exchange moves only the launch's real rows)
     for (int c0 = 0; c0 < ncols; c0 += 64) {
       float v[64];
-      tmem_ld64(tbase + c0, v);
+      tmem_ld64(tbase + c0, v);  // warp-collective
+      if (row_ok)
 #pragma unroll
-      for (int i = 0; i < 64; ++i)
-        if (c0 + i < ncols) mine[(c0 + i) * kBM] = ok ? v[i] : 0.f;
+        for (int i = 0; i < 64; ++i)
+          if (c0 + i < ncols) mine[(c0 + i) * kBM] = ok ? v[i] : 0.f;
     }
     __threadfence();
     cluster_sync_all();
     const float *part = g.ws + tile * ks * (kBN * kBM) + static_cast<size_t>(ec0) * kBM + lr;
     for (int c = 0; c < ecols; c += 16) {
+      if (!(row_ok && ok)) break;
       float v[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) v[i] = 0.f;
       for (int zz = 0; zz < ks; ++zz)
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] += __ldcg(part + static_cast<size_t>(zz) * (kBN * kBM) + (c + i) * kBM);
-      if (row_ok && ok) {
+      {
         const int n = n0 + ec0 + c;
         ChunkOps op;
         if constexpr (EPI == kEpiResid) resid_chunk(c, op);
