@@ -370,13 +370,16 @@ def config_dict(wl, args):
                    if wl.name == "large" else "flushed between timed steps (256 MiB write)"),
             **({"requests": f"{wl.batch} per GPU: configs[4]'s 256 requests split over 8 GPUs",
                 "kv_pages": f"{kv_pages_needed(wl)} pages of 128 positions per model "
-                            f"(the call's prompt + new tokens + one verify block, not max_seq_len)"}
+                            f"(prompt + new tokens + one verify block + the draft's catch-up drift)"}
                if wl.name == "large" else {})}
 
 
 def kv_pages_needed(wl):
-    """Pages of the paged KV cache the large workload's requests reach."""
-    return wl.batch * -(-(wl.prompt_len + wl.max_new + wl.lookahead + 1) // 128)
+    """Pages of the paged KV cache a generation of the workload reserves:
+    prompt + new tokens + one verify block, plus the reference catch-up's
+    drift of the draft cache (one position per rejected round, at most
+    max_new)."""
+    return wl.batch * -(-(wl.prompt_len + 2 * wl.max_new + wl.lookahead + 1) // 128)
 
 
 def cpu_baseline_sample(wl):
@@ -811,7 +814,7 @@ def run_tp_bench(args, wl, rank, world, local, dist):
     eng = sd.Engine(wl.target, draft_layers=wl.draft_layers, weight_dtype=sd.INT8, act_dtype=sd.BF16,
                     kv_dtype=sd.BF16, max_batch=B, max_lookahead=k, max_prompt_len=S, device=local,
                     tp_rank=rank, tp_world=world, tp_id=obj[0],
-                    kv_pages=B * -(-(S + wl.max_new + k + 1) // 128))
+                    kv_pages=B * -(-(S + 2 * wl.max_new + k + 1) // 128))
     P = device_param_tensors(wl.target, 0, dev)
     eng.load_params_device(sd.TARGET, P)
     del P

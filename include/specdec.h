@@ -83,7 +83,8 @@ typedef struct specdec_config {
   int32_t kv_pages;                /* paged KV cache: pages of 128 positions in each model's pool (the reference's
                                       KVCache, include/nn/layer.hpp:212-230, grows one request's cache by copying);
                                       0 -> max_batch x ceil(max_seq_len / 128).  A call takes the pages its requests
-                                      can reach (prompt + new tokens + one verify block) and returns SPECDEC_ERR_OOM
+                                      can reach (prompt + new tokens + one verify block, plus max_new
+                                      for the draft's drift under SPECDEC_CATCHUP_REF) and returns SPECDEC_ERR_OOM
                                       when the pool is too small */
 } specdec_config;
 

@@ -1467,9 +1467,17 @@ void assign_pages(specdec_handle *h, int B, int need) {
 }
 
 // Cache positions a generation can write: the prompt, the new tokens, and a
-// verify block (k + 1 rows, or a tree's nodes) past them.
+// verify block (k + 1 rows, or a tree's nodes) past them.  With the
+// reference's catch-up (SPECDEC_CATCHUP_REF) the draft is fed one extra
+// position per rejected round (src/nn/layer.cpp:1632-1642, then 1542), so
+// its cache can run up to max_new positions ahead of the target's; the page
+// table is shared, so the reservation covers that drift.
 int positions_needed(const specdec_gen_params *p, int S, const TreeCfg *tree, bool ar) {
-  return S + std::max(0, p->max_new_tokens) + (ar ? 1 : tree ? tree->N + 1 : std::max(1, p->lookahead) + 1);
+  const int n = std::max(0, p->max_new_tokens);
+  if (ar) return S + n + 1;
+  if (tree) return S + n + tree->N + 1;
+  const int drift = p->draft_catchup == SPECDEC_CATCHUP_REF ? n : 0;
+  return S + n + drift + std::max(1, p->lookahead) + 1;
 }
 
 void validate_gen(specdec_handle *h, const specdec_gen_params *p, int B, int S, const TreeCfg *tree, bool ar) {

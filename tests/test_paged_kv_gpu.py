@@ -4,7 +4,9 @@ The reference's KVCache (include/nn/layer.hpp:212-230) holds one contiguous
 tensor per layer and grows it by copying (src/nn/layer.cpp:667-809); here
 each model's cache is a pool of 128-position pages and every request has a
 page table.  A call takes the pages its requests can reach (prompt + new
-tokens + one verify block): request b's i-th page is the pool's (i*B + b)-th,
+tokens + one verify block, and up to new positions more: under the reference
+catch-up the draft is fed one extra position per rejected round, so its cache
+runs ahead of the target's): request b's i-th page is the pool's (i*B + b)-th,
 so a request's pages are never adjacent once B > 1, and every multi-request
 test of the suite runs on scattered pages.  These cases add pools sized to
 the call (not to max_seq_len), caches that cross several pages, the three
@@ -25,7 +27,9 @@ D128 = ModelShape(vocab=2048, d_model=512, n_heads=4, d_ff=1024, n_layers=2, max
 
 
 def pages_for(B, S, new, k):
-    return B * -(-(S + new + k + 1) // PAGE)
+    # prompt + new tokens + a verify block, and the draft cache's drift under
+    # the reference catch-up (one position per rejected round, at most new)
+    return B * -(-(S + 2 * new + k + 1) // PAGE)
 
 
 # (shape, int8 weights, bf16 activations, kv mode): fp32 cache with the
@@ -80,6 +84,25 @@ def test_session_on_call_sized_pool(gpu_lib, oracle_built):
     got, _ = pair.engine.session_tokens()
     assert np.array_equal(got, want)
     pair.engine.close()
+
+
+def test_draft_drift_within_pages(gpu_lib, oracle_built):
+    """A long generation with a draft that is rarely accepted: under the
+    reference catch-up the draft cache drifts ahead of the target's by one
+    position per rejected round (here well past one page), and the call's
+    pages still cover it; tokens match the default pool and the oracle."""
+    B, S, new, k = 2, 100, 200, 4
+    small = make_pair(D64, 1, seed=53, int8=True, max_batch=B, max_prompt_len=S, kv_pages=pages_for(B, S, new, k))
+    full = make_pair(D64, 1, seed=53, int8=True, max_batch=B, max_prompt_len=S)
+    prompts = make_prompts(B, S, D64.vocab, seed=12)
+    ts, ss = small.engine.generate_speculative(prompts, new, k, 0.0)
+    tf, sf = full.engine.generate_speculative(prompts, new, k, 0.0)
+    assert np.array_equal(ts, tf) and np.array_equal(ss, sf)
+    to, _, mg = oracle.oracle_generate_speculative(small.target, small.draft, prompts, new, k, 0.0,
+                                                   cache_cap=D64.max_seq_len)
+    compare_tokens(ts, to, mg, S, greedy=True)
+    small.engine.close()
+    full.engine.close()
 
 
 def test_pool_exhausted(gpu_lib):
