@@ -24,10 +24,10 @@
 //   fold overlaps the next tile's products.
 // Warp 0 streams K and V tiles through a three-slot TMA ring per CTA (32 KB
 // per slot; two CTAs per SM, 192 KB in flight per SM), warp 1 issues the
-// MMAs, and one or two warpgroups do the softmax and the output: for groups of
-// up to 2 queries one warpgroup carries every query column, for the 8- and
-// 16-column variants (verify blocks) two warpgroups split the columns, which
-// halves the per-thread softmax chain of a tile.  CTAs are persistent and walk work items
+// MMAs, and one or two warpgroups do the softmax and the output: for a single
+// query one warpgroup, for the 2-, 8- and 16-column variants (draft step 0,
+// verify blocks) two warpgroups split the columns, which halves the
+// per-thread softmax chain of a tile.  CTAs are persistent and walk work items
 // (group, head, split) in a fixed order, so the ring never drains between
 // items.  A (group, head) whose cache is split writes unnormalised partials;
 // the last of its splits to finish (an arrival counter) merges them with the
@@ -46,9 +46,10 @@ constexpr int kAdHalf = kAdTile * kAdD * 2;      // 32 KB: 128 positions x 128 b
 constexpr int kAdBox = kAdTile * 64 * 2;         // 16 KB: one 64-dim atom of a half tile
 constexpr int kAdQBytes = kAdN * kAdD * 2;       // 4 KB: 16 query rows, two 2 KB atoms
 constexpr int kAdPBytes = kAdN * kAdTile * 2;    // 4 KB: 16 query rows x 128 positions, two atoms
-// warp 0 TMA, warp 1 MMA, then the softmax warpgroups: one for up to two query
-// columns, two (four columns each, or eight) for the 8- and 16-column groups
-constexpr int ad_qgroups(int nq) { return nq >= 8 ? 2 : 1; }
+// warp 0 TMA, warp 1 MMA, then the softmax warpgroups: one for a single query
+// column, two (one, four or eight columns each) for the 2-, 8- and 16-column
+// groups
+constexpr int ad_qgroups(int nq) { return nq >= 2 ? 2 : 1; }
 constexpr int ad_threads(int nq) { return 64 + 128 * ad_qgroups(nq); }
 // three ring slots, two query buffers, one P buffer: 111 KB, two CTAs per SM
 constexpr int kAdSmem = kAdSlots * kAdHalf + 2 * kAdQBytes + kAdPBytes + 1024;
