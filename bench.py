@@ -152,10 +152,18 @@ class ClockSampler:
         try:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                          "--format=csv,noheader,nounits", "-lms", "50"], stdout=self.f,
                                          stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+        # nvidia-smi takes a while to start: wait (up to 3 s, before the
+        # timed region) for its first sample, so the samples cover the region
+        t0 = time.perf_counter()
+        while self.proc is not None and time.perf_counter() - t0 < 3.0:
+            self.f.flush()
+            if os.path.getsize(self.path) > 0 or self.proc.poll() is not None:
+                break
+            time.sleep(0.02)
         return self
 
     def __exit__(self, *a):
