@@ -938,7 +938,11 @@ def main():
             line = run_session_bench(args, wl, rank, world, local, dist)
             if world > 1 and not args.profile and not args.no_tp:
                 torch.cuda.empty_cache()
-                tp = run_tp_bench(args, wl, rank, world, local, dist)
+                try:
+                    tp = run_tp_bench(args, wl, rank, world, local, dist)
+                except Exception as e:  # the same on every rank (shapes, memory): the main line stands
+                    tp = {"world": world, "error": f"{type(e).__name__}: {e}"[:300]}
+                torch.cuda.empty_cache()
                 if line is not None:
                     line["tp"] = tp
             if not args.skip_configs1 and not args.profile:
