@@ -2,8 +2,8 @@
 against the cluster split-K GEMM.
 
 The engine sends row batches of at most 256 rows over layers of at least
-SPECDEC_SK_MIN_TILES 256-column tiles to it (40 by default: the large
-config's QKV, gate/up and lm_head).  With the threshold at 1 every GEMM
+SPECDEC_SK_MIN_TILES 256-column tiles to it (80 by default: the large
+config's gate/up and lm_head).  With the threshold at 1 every GEMM
 launch of this small model takes it, so each tile is shared by several CTAs
 (8-16 k-blocks per tile, one or two per CTA) and every output goes through the
 fix-up of partial tiles; 129-256 rows use both 128-row accumulators.
