@@ -23,7 +23,10 @@
 //   o = o * alpha + O_t in registers (thread = dim), one tile behind, so the
 //   fold overlaps the next tile's products.
 // Warp 0 streams K and V tiles through a three-slot TMA ring per CTA (32 KB
-// per slot; two CTAs per SM, 192 KB in flight per SM), warp 1 issues the
+// per slot; two CTAs per SM, 192 KB in flight per SM), K one tile ahead of V
+// (K_0 K_1 V_0 K_2 V_1 ...: the ring releases slots in the order the MMAs
+// read them, so no slot sits loaded while a V tile waits for its softmax
+// and the next K queues behind it), warp 1 issues the
 // MMAs, and one or two warpgroups do the softmax and the output: for a single
 // query one warpgroup, for the 2-, 8- and 16-column variants (draft step 0,
 // verify blocks) two warpgroups split the columns, which halves the
@@ -254,46 +257,61 @@ __global__ void __launch_bounds__(ad_threads(NQ), 2) attn_dec_kernel(const __gri
 
   if (warp == 0) {
     // ---- producer: query rows per item, then K and V half tiles ----------
+    // Load order K_0 K_1 V_0 K_2 V_1 ... K_last V_last-1 V_last over the
+    // CTA's tiles (T counts them across items): a K slot frees as soon as its
+    // scores are on the tensor cores, so K of T + 1 is in flight while V of T
+    // waits for its softmax.  Ring index of K_T: 2T - 1 (0 for T = 0); of V_T:
+    // 2T + 2 (2T + 1 for the CTA's last tile).
     if (lane == 0) {
       int idx = 0, qi = 0;
-      for (int item = blockIdx.x; item < a.n_items && !s_abort; item += gridDim.x) {
+      auto load = [&](const CUtensorMap *m, int y) -> bool {
+        const int s = idx % kAdSlots;
+        if (!mbar_wait(&empty[s], ((idx / kAdSlots) & 1) ^ 1) || s_abort) {
+          give_up();
+          return false;
+        }
+        mbar_expect_tx(&full[s], kAdHalf);
+        tma_load_2d(ring + s * kAdHalf, m, 0, y, &full[s]);
+        tma_load_2d(ring + s * kAdHalf + kAdBox, m, 64, y, &full[s]);
+        s_issued = ++idx;
+        return true;
+      };
+      bool stop = false, pend = false;
+      int pend_y = 0;  // the cache row of the tile whose V is still to load
+      for (int item = blockIdx.x; item < a.n_items && !s_abort && !stop; item += gridDim.x) {
         const AdItem it = ad_item(a, item);
         if (it.nt == 0) continue;
         const int qb = qi & 1;
-        if (!mbar_wait(&q_empty[qb], ((qi >> 1) & 1) ^ 1)) { give_up(); break; }
+        if (!mbar_wait(&q_empty[qb], ((qi >> 1) & 1) ^ 1)) {
+          give_up();
+          break;
+        }
         mbar_expect_tx(&q_full[qb], kAdQBytes);
         tma_load_2d(sq + qb * kAdQBytes, &a.tmq, it.h * kAdD, it.rq0, &q_full[qb]);
         tma_load_2d(sq + qb * kAdQBytes + kAdQBytes / 2, &a.tmq, it.h * kAdD + 64, it.rq0, &q_full[qb]);
         s_q_issued = ++qi;
-        bool stop = false;
-        for (int t = 0; t < it.nt && !stop; ++t) {
+        for (int t = 0; t < it.nt; ++t) {
           int y = kv_row(a.pg, a.Hkv, it.req, it.h, (it.t0 + t) * kAdTile);
           if (y < 0) {  // no page: flagged, a valid row is read instead
             if (a.err) atomicOr(a.err, kErrSeqLen);
             y = 0;
           }
-          for (int kv = 0; kv < 2; ++kv) {
-            const int s = idx % kAdSlots;
-            if (!mbar_wait(&empty[s], ((idx / kAdSlots) & 1) ^ 1) || s_abort) {
-              give_up();
-              stop = true;
-              break;
-            }
-            mbar_expect_tx(&full[s], kAdHalf);
-            const CUtensorMap *m = kv ? &a.tmv : &a.tmk;
-            tma_load_2d(ring + s * kAdHalf, m, 0, y, &full[s]);
-            tma_load_2d(ring + s * kAdHalf + kAdBox, m, 64, y, &full[s]);
-            s_issued = ++idx;
+          if (!load(&a.tmk, y) || (pend && !load(&a.tmv, pend_y))) {
+            stop = true;
+            break;
           }
+          pend = true;
+          pend_y = y;
         }
-        if (stop) break;
       }
+      if (!stop && !s_abort && pend) load(&a.tmv, pend_y);
     }
   } else if (warp == 1) {
     // ---- MMA issuer --------------------------------------------------------
     // Order S_0, S_1, O_0, S_2, O_1, ...: the scores of tile T + 1 are on the
-    // tensor cores while the softmax of tile T runs.  K of tile T sits in
-    // ring slot 2T, V in slot 2T + 1 (the producer's order).
+    // tensor cores while the softmax of tile T runs.  K of tile T has ring
+    // index 2T - 1 (0 for T = 0), V has 2T + 2, or 2T + 1 on the last tile
+    // (the producer's order).
     if (lane == 0) {
       struct Cur {
         int item, t, qb;
@@ -307,7 +325,7 @@ __global__ void __launch_bounds__(ad_threads(NQ), 2) attn_dec_kernel(const __gri
         return a.n_items;
       };
       auto issue_s = [&](int T, const Cur &c) -> bool {
-        const int idx = 2 * T, sk = idx % kAdSlots, sb = T & 1;
+        const int idx = T ? 2 * T - 1 : 0, sk = idx % kAdSlots, sb = T & 1;
         if (!mbar_wait(&full[sk], (idx / kAdSlots) & 1) || !mbar_wait(&s_free[sb], ((T >> 1) & 1) ^ 1) || s_abort)
           return false;
         tc_fence_after();
@@ -320,8 +338,8 @@ __global__ void __launch_bounds__(ad_threads(NQ), 2) attn_dec_kernel(const __gri
         tc_commit(&s_full[sb]);
         return true;
       };
-      auto issue_o = [&](int T) -> bool {
-        const int idx = 2 * T + 1, sv = idx % kAdSlots, sb = T & 1;
+      auto issue_o = [&](int T, bool last) -> bool {
+        const int idx = last ? 2 * T + 1 : 2 * T + 2, sv = idx % kAdSlots, sb = T & 1;
         const uint32_t ph = (T >> 1) & 1;
         if (!mbar_wait(&full[sv], (idx / kAdSlots) & 1) || !mbar_wait(&p_full[sb], ph) ||
             !mbar_wait(&o_free[sb], ph ^ 1) || s_abort)
@@ -347,7 +365,7 @@ __global__ void __launch_bounds__(ad_threads(NQ), 2) attn_dec_kernel(const __gri
         ok = mbar_wait(&q_full[0], 0);
         s_q_consumed = qcount = 1;
         if (ok) ok = issue_s(0, c);
-        if (ok) s_consumed = 1;  // the lowest ring slot not yet taken: V of tile 0
+        if (ok) s_consumed = 1;  // the lowest ring index not yet taken
       }
       for (int T = 0; work && ok; ++T) {
         Cur n = c;
@@ -366,8 +384,8 @@ __global__ void __launch_bounds__(ad_threads(NQ), 2) attn_dec_kernel(const __gri
         }
         if (ok && more) ok = issue_s(T + 1, n);
         if (ok) {
-          ok = issue_o(T);
-          if (ok) s_consumed = 2 * T + 3;
+          ok = issue_o(T, !more);
+          if (ok) s_consumed = more ? 2 * T + 3 : 2 * T + 2;
         }
         if (ok && c.t + 1 == c.it.nt) tc_commit(&q_empty[c.qb]);
         if (!more) break;
