@@ -87,8 +87,8 @@ LARGE_REQUESTS_PER_GPU = 32
 TRAFFIC_BYTES = {
     "int8": 503808,
     # attn_dec_kernel<8>, verify pass, 32 requests x ~2,060 positions: the
-    # one-layer capture of the same launch (1,145.4 MB read + 20.2 MB written)
-    "large": 1165595160,
+    # one-layer capture of the same launch (1,145.9 MB read + 19.7 MB written)
+    "large": 1145909000 + 19673088,
 }
 
 
